@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Benchmark of the INT4 streaming matvec (llm.vhdl subsystem A) on B200.
+
+Workload (streamed): a stack of G = 64 distinct
+4096 x 4096 matrices in the benchmark format (signed INT4 uniform in [-8,7],
+fp16 scale per 128 columns in [0.002, 0.02], x fp16 ~ N(0,1), y fp16, fp32
+accumulation), seeded splitmix64 synthetic data (seed 0 + matrix index, one
+disjoint range per rank).  One step = one launch of the 64-job list, i.e. 64
+config-0 matvecs; 555 MB of weights per step is larger than the 126 MB L2, so
+no flush is needed between steps.
+
+Printed JSON line (rank 0):
+  value      HBM GB/s of algorithmic bytes (8,667,136 B per matvec), whole job
+  e2e        the same metric through mv4i_g128_matvec_host with pinned HOST
+             x / y, copies inside the timed region
+  roofline   the g128 kernel: achieved GB/s vs the measured copy bandwidth
+  cpu_baseline  the reference's mv4i_matvec (compiled from its C source) on the
+             box's cores, golden mode, config 0 (bounded sample)
+  golden     the same stack in the reference's bit-exact golden format
+             (uint15 scale per 32 columns, int16 BFP x, BFP output)
+  single     one 4096x4096 matvec per launch, rotating over the 64 matrices
+
+`--impl reference` times the reference's CPU mv4i_matvec instead (rank 0 only).
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = K = 4096
+G128_BYTES = M * K // 2 + M * (K // 128) * 2 + K * 2 + M * 2        # 8,667,136
+GOLDEN_BYTES = M * K // 2 + M * (K // 32) * 2 + K * 2 + M * 2       # 9,453,568
+METRIC = "INT4 matvec HBM GB/s (% of peak) and decode tokens/s at 1/2/4/8 B200"
+FALLBACK_HBM = 6650.0
+
+
+def load_pkg():
+    import importlib.util
+    if "llmvhdl_b200" in sys.modules:
+        return sys.modules["llmvhdl_b200"]
+    d = os.path.join(ROOT, "llm.vhdl_b200")
+    spec = importlib.util.spec_from_file_location(
+        "llmvhdl_b200", os.path.join(d, "__init__.py"), submodule_search_locations=[d])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["llmvhdl_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM, "fallback"
+
+
+def profiled_traffic(name):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.startswith("traffic_bytes_per_launch:"):
+            return float(ln.split(":")[1])
+    return None
+
+
+class Clocks:
+    """Samples SM clock and clock-event reasons through NVML every 2 ms on a
+    thread while the timed region runs (read-only)."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, torch_dev):
+        self.samples, self.reasons, self.ok = [], 0, False
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            bus = torch_dev_bus(torch_dev)
+            self.h = N.nvmlDeviceGetHandleByPciBusId(bus) if bus else N.nvmlDeviceGetHandleByIndex(0)
+            self.N = N
+            self.max = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.err = str(e)
+
+    def _run(self):
+        N = self.N
+        while not self.stop:
+            try:
+                self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+                self.reasons |= N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        self.stop = False
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop = True
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": getattr(self, "max", None), "reasons": [],
+                    "note": getattr(self, "err", "no samples")}
+        rs = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max, "reasons": rs,
+                "samples": len(self.samples)}
+
+
+def torch_dev_bus(dev):
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return "%08X:%02X:%02X.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def cpu_baseline(budget_s=3.0):
+    from oracle import cpu_baseline as CB
+    steps, kind, P = CB.run(budget_s=budget_s)
+    t = steps[0]
+    return {"value": round(CB.GOLDEN_BYTES / t / 1e9, 4), "unit": "GB/s", "cores": P,
+            "kind": kind, "ms_per_matvec": round(t * 1e3, 3),
+            "sample": "config-0 golden-mode mv4i_matvec (BFP out), %d processes x row shards, "
+                      "~%.0f s each" % (P, budget_s)}
+
+
+# --------------------------------------------------------------------- ours
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    pkg = load_pkg()
+    L = pkg.lib()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    G = args.stack
+    seed = rank * G
+    stream = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def vp(t):
+        return C.c_void_p(t.data_ptr())
+
+    wq = torch.empty((G, M, K // 2), dtype=torch.uint8, device=dev)
+    sc = torch.empty((G, M, K // 128), dtype=torch.float16, device=dev)
+    x = torch.empty((G, K), dtype=torch.float16, device=dev)
+    y16 = torch.empty((G, M), dtype=torch.float16, device=dev)
+    assert L.mv4i_synth_g128(seed, G, M, K, vp(wq), vp(sc), vp(x), sp) == 0
+    mats = (pkg.DMat * G)()
+    jobs = (pkg.Job * G)()
+    for i in range(G):
+        assert L.mv4i_dmat_wrap_g128(vp(wq[i]), K // 2, vp(sc[i]), K // 128, M, K, local_rank,
+                                     C.byref(mats[i])) == 0
+        j = jobs[i]
+        j.w = C.pointer(mats[i]); j.x = x[i].data_ptr(); j.n_rows = M; j.n_cols = K; j.nvec = 1
+        j.y_f16 = y16[i].data_ptr()
+
+    def launch(js=jobs, n=G, scratch=None):
+        rc = L.mv4i_launch(js, n, scratch, sp)
+        if rc:
+            raise RuntimeError("mv4i_launch failed: %d (cuda %d)" % (rc, L.mv4i_last_cuda_error()))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def timed(fn, steps):
+        """Run fn() `steps` times between events on `stream`; max over ranks."""
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        barrier()
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # --- headline: the g128 stack
+    for _ in range(args.warmup):
+        launch()
+    clk = Clocks(local_rank)
+    with clk:
+        ms = timed(launch, args.steps)
+    ms_step = ms / args.steps
+    value = world * G * G128_BYTES / (ms_step * 1e-3) / 1e9
+
+    # --- golden-mode stack: same nibbles, uint15 scales per 32 columns, BFP x
+    gsc = torch.repeat_interleave((sc.float() * 2.0 ** 20).round().to(torch.int16), 4, dim=2).contiguous()
+    xm = torch.empty((G, K), dtype=torch.int16, device=dev)
+    xe = torch.empty(G, dtype=torch.int32, device=dev)
+    assert L.mv4i_bfp_pack(vp(x), 0, K, G, K, vp(xm), vp(xe), sp) == 0
+    cb = (C.c_int8 * 16)(*[i if i < 8 else i - 16 for i in range(16)])
+    gmats = (pkg.DMat * G)()
+    gjobs = (pkg.Job * G)()
+    yd = torch.empty((G, M), dtype=torch.int32, device=dev)
+    ym = torch.empty((G, M), dtype=torch.int16, device=dev)
+    st = torch.zeros((G, 8), dtype=torch.int32, device=dev)
+    scratch = torch.zeros(L.mv4i_scratch_bytes(), dtype=torch.uint8, device=dev)
+    for i in range(G):
+        assert L.mv4i_dmat_wrap_golden(vp(wq[i]), K // 2, vp(gsc[i]), K // 32, M, K, 5, 3, cb,
+                                       local_rank, C.byref(gmats[i])) == 0
+        j = gjobs[i]
+        j.w = C.pointer(gmats[i]); j.x = xm[i].data_ptr(); j.d_x_exp = xe[i].data_ptr()
+        j.n_rows = M; j.n_cols = K; j.mode = 0; j.nvec = 1
+        j.y_data = yd[i].data_ptr(); j.y_mant = ym[i].data_ptr(); j.status = st[i].data_ptr()
+    gscr = vp(scratch)
+    for _ in range(args.warmup):
+        launch(gjobs, G, gscr)
+    gsteps = max(10, args.steps // 2)
+    gms = timed(lambda: launch(gjobs, G, gscr), gsteps) / gsteps
+    gvalue = world * G * GOLDEN_BYTES / (gms * 1e-3) / 1e9
+    assert int(st[:, 4].abs().sum().item()) == 0
+
+    # --- one matvec per launch, rotating over the stack (cold L2 each time)
+    single = [0]
+
+    def one():
+        i = single[0] % G
+        single[0] += 1
+        rc = L.mv4i_launch(C.byref(jobs[i]), 1, None, sp)
+        if rc:
+            raise RuntimeError("single launch failed %d" % rc)
+    for _ in range(G):
+        one()
+    nsingle = max(G, args.steps)
+    sms = timed(one, nsingle) / nsingle
+
+    # --- end to end through the host-buffer entry point
+    hx = torch.empty((G, K), dtype=torch.float16).pin_memory()
+    hx.copy_(x.cpu())
+    hy = torch.empty((G, M), dtype=torch.float16).pin_memory()
+
+    def e2e_call():
+        rc = L.mv4i_g128_matvec_host(mats, G, C.c_void_p(hx.data_ptr()), C.c_void_p(hy.data_ptr()), sp)
+        if rc:
+            raise RuntimeError("mv4i_g128_matvec_host failed %d" % rc)
+    for _ in range(3):
+        e2e_call()
+    esteps = max(10, args.steps // 4)
+    ems = timed(e2e_call, esteps) / esteps
+    e2e_value = world * G * G128_BYTES / (ems * 1e-3) / 1e9
+    assert torch.equal(hy.to(dev), y16), "host-buffer result differs from the device launch"
+
+    peak, peak_kind = peaks()
+    achieved = G * G128_BYTES / (ms_step * 1e-3) / 1e9
+    traffic = profiled_traffic("mv4i_g128_stack64.txt")
+    out = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 x fp16 (fp32 accumulate)",
+        "data": "synthetic (splitmix64 seeds, config-0 distributions)",
+        "config": {"workload": "config 0: 64 x [4096x4096 INT4 g128 fp16-scale matvec, batch 1] per step",
+                   "stack": G, "M": M, "K": K, "group": 128, "parallelism": "replica%d" % world,
+                   "l2": "inputs 555 MB/step per GPU > 126 MB L2 (no flush)"},
+        "percent_of_peak": round(100.0 * achieved / peak, 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind + " copy bandwidth",
+                     "traffic": traffic,
+                     "kernel": "mv4i_kernel<G128>", "bytes_per_launch": G * G128_BYTES},
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": G * K * 2, "d2h_bytes_per_step": G * M * 2,
+                "call": "mv4i_g128_matvec_host (pinned host x/y)", "ms_per_step": round(ems, 4)},
+        "golden": {"value": round(gvalue, 1), "unit": "GB/s", "ms_per_step": round(gms, 5),
+                   "bytes_per_matvec": GOLDEN_BYTES, "frac": round(gvalue / world / peak, 4),
+                   "mode": "BFP out, linear codebook, bit-exact with ref/matvec_int4.c"},
+        "single": {"us_per_matvec": round(sms * 1e3, 2),
+                   "GBps": round(G128_BYTES / (sms * 1e-3) / 1e9, 1)},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--stack", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import cpu_baseline as CB
+        steps, kind, P = CB.run(n_iter=args.warmup + args.steps, lockstep=True)
+        t = statistics.mean(steps[args.warmup:]) if len(steps) > args.warmup else statistics.mean(steps)
+        v = CB.GOLDEN_BYTES / t / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 x int16 (integer, bit-exact golden model)",
+            "data": "synthetic (splitmix64 seed 0, config-0 distributions)",
+            "config": {"workload": "config 0: 4096x4096 INT4 matvec, batch 1, golden-mode image",
+                       "M": M, "K": K, "parallelism": "%d processes x row shards" % P},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": P, "kind": kind,
+                             "sample": "%d lockstep steps of one config-0 mv4i_matvec split over %d "
+                                       "processes" % (args.warmup + args.steps, P)},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}))
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()          # spawn-started workers, before any CUDA work
+    out = run_ours(args, rank, world, local_rank)
+    out["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

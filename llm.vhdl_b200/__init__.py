@@ -1,0 +1,180 @@
+"""Python view of the llm.vhdl B200 hot-path library (ctypes over the C ABI).
+
+The product is the C ABI in include/mv4i_b200.h, implemented by
+lib/libmv4i_b200.so (CUDA sm_100a + C host code).  This module only binds it
+for the tests and bench.py; it has no compute of its own and no fallback:
+``lib()`` raises if the shared library is missing.
+
+Because the directory name contains a dot it is loaded by path:
+``load_package()`` in tests/conftest.py and bench.py registers it as the
+module ``llmvhdl_b200``.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIBDIR = os.path.join(HERE, "lib")
+LIBPATH = os.path.join(LIBDIR, "libmv4i_b200.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+SOURCES = ["csrc/mv4i_kernels.cu", "csrc/mv4i_host.c"]
+
+MODE_BFP, MODE_RAW, MODE_PARTIAL = 0, 1, 2
+KIND_GOLDEN, KIND_G128 = 0, 1
+MAX_JOBS = 64
+
+
+def build(verbose=False):
+    """Compile the CUDA + C sources into lib/libmv4i_b200.so for sm_100a."""
+    os.makedirs(LIBDIR, exist_ok=True)
+    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
+           "-shared", "-o", LIBPATH, *[os.path.join(HERE, s) for s in SOURCES],
+           "-lpthread"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
+    if verbose:
+        print(r.stdout + r.stderr)
+    return LIBPATH
+
+
+# ----------------------------------------------------------------- structs
+
+class Hdr(C.Structure):
+    _fields_ = [("magic", C.c_uint32), ("M", C.c_uint32), ("K", C.c_uint32),
+                ("scale_offset", C.c_uint32), ("n_scale_sub", C.c_uint32),
+                ("version", C.c_uint16), ("flags", C.c_uint16), ("rows_if", C.c_uint16),
+                ("nports_w", C.c_uint16), ("block", C.c_uint16), ("axi_dw", C.c_uint16),
+                ("w_exp", C.c_int32), ("out_shift", C.c_int32), ("codebook", C.c_int8 * 16),
+                ("w_sub_offset", C.c_uint64 * 64), ("s_sub_offset", C.c_uint64 * 64)]
+
+
+class File(C.Structure):
+    _fields_ = [("h", Hdr), ("base", C.c_void_p), ("nb", C.c_int), ("port_b", C.c_int),
+                ("grp", C.c_int)]
+
+
+class Result(C.Structure):
+    _fields_ = [("y_data", C.c_void_p), ("y_acc", C.c_void_p), ("y_mant", C.c_void_p),
+                ("y_exp", C.c_int), ("sat_event", C.c_int), ("sat_count", C.c_uint64),
+                ("ns", C.c_int)]
+
+
+class DMat(C.Structure):
+    _fields_ = [("wq", C.c_void_p), ("sc", C.c_void_p), ("w_pitch", C.c_int64),
+                ("s_pitch", C.c_int64), ("M", C.c_int32), ("K", C.c_int32),
+                ("w_exp", C.c_int32), ("out_shift", C.c_int32), ("codebook", C.c_int8 * 16),
+                ("kind", C.c_int32), ("device", C.c_int32), ("owned", C.c_void_p)]
+
+
+class Status(C.Structure):
+    _fields_ = [("y_exp", C.c_int32), ("ns", C.c_int32), ("sat_event", C.c_int32),
+                ("sat_count", C.c_uint32), ("err", C.c_int32), ("pad", C.c_int32 * 3)]
+
+
+class Job(C.Structure):
+    _fields_ = [("w", C.POINTER(DMat)), ("x", C.c_void_p), ("d_x_exp", C.c_void_p),
+                ("x_exp", C.c_int32), ("n_rows", C.c_int32), ("n_cols", C.c_int32),
+                ("mode", C.c_int32), ("nvec", C.c_int32), ("x_stride", C.c_int64),
+                ("y_stride", C.c_int64), ("y_data", C.c_void_p), ("y_mant", C.c_void_p),
+                ("y_acc", C.c_void_p), ("y_f16", C.c_void_p), ("y_f32", C.c_void_p),
+                ("status", C.c_void_p)]
+
+
+EXPORTS = {
+    "mv4i_parse": (C.c_int, [C.POINTER(File), C.c_void_p, C.c_size_t]),
+    "mv4i_matvec": (C.c_int, [C.POINTER(File), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                              C.POINTER(Result)]),
+    "mv4i_forget": (C.c_int, [C.POINTER(File)]),
+    "mv4i_get_widx": (C.c_int, [C.POINTER(File), C.c_int, C.c_int]),
+    "mv4i_get_scale": (C.c_uint16, [C.POINTER(File), C.c_int, C.c_int]),
+    "mv4i_dmat_upload": (C.c_int, [C.POINTER(File), C.c_int, C.POINTER(DMat)]),
+    "mv4i_dmat_wrap_g128": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int,
+                                      C.c_int, C.c_int, C.POINTER(DMat)]),
+    "mv4i_dmat_wrap_golden": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int,
+                                        C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                        C.POINTER(DMat)]),
+    "mv4i_dmat_free": (C.c_int, [C.POINTER(DMat)]),
+    "mv4i_bfp_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int64, C.c_void_p,
+                                C.c_void_p, C.c_void_p]),
+    "mv4i_scratch_bytes": (C.c_size_t, []),
+    "mv4i_launch": (C.c_int, [C.POINTER(Job), C.c_int, C.c_void_p, C.c_void_p]),
+    "mv4i_tp_reduce": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mv4i_synth_g128": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                  C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mv4i_g128_matvec_host": (C.c_int, [C.POINTER(DMat), C.c_int, C.c_void_p, C.c_void_p,
+                                        C.c_void_p]),
+    "mv4i_last_cuda_error": (C.c_int, []),
+    "mv4i_version": (C.c_char_p, []),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded C-ABI library.  Raises when it has not been built: there is
+    no other implementation to fall back to."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIBPATH):
+            raise RuntimeError("libmv4i_b200.so is not built (run __graft_entry__.build())")
+        L = C.CDLL(LIBPATH)
+        for name, (res, args) in EXPORTS.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def header_symbols(path=None):
+    """Function names declared in include/mv4i_b200.h (and other include/*.h)."""
+    import glob
+    import re
+    names = set()
+    paths = [path] if path else glob.glob(os.path.join(ROOT, "include", "*.h"))
+    for p in paths:
+        src = open(p).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b([a-z][a-z0-9_]*)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return sorted(n for n in names if not n.startswith("sizeof"))
+
+
+# ------------------------------------------------------------ host drop-in
+
+def ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class ParsedImage:
+    """A parsed .mv4i image; keeps the bytes alive (the file borrows them)."""
+
+    def __init__(self, img):
+        self.buf = np.frombuffer(bytes(img), dtype=np.uint8).copy()
+        self.f = File()
+        self.rc = lib().mv4i_parse(C.byref(self.f), ptr(self.buf), self.buf.size)
+
+    @property
+    def M(self):
+        return self.f.h.M
+
+    @property
+    def K(self):
+        return self.f.h.K
+
+
+def matvec(pi, x_mant, x_exp, n_rows, n_cols, mode):
+    """mv4i_matvec through the drop-in C entry point (host buffers)."""
+    x = np.ascontiguousarray(x_mant, dtype=np.int16)
+    yd = np.zeros(max(n_rows, 1), np.int32)
+    ya = np.zeros(max(n_rows, 1), np.int64)
+    ym = np.zeros(max(n_rows, 1), np.int16)
+    r = Result(yd.ctypes.data, ya.ctypes.data, ym.ctypes.data, 0, 0, 0, 0)
+    rc = lib().mv4i_matvec(C.byref(pi.f), ptr(x), x_exp, n_rows, n_cols, mode, C.byref(r))
+    return rc, dict(y_data=yd[:n_rows], y_acc=ya[:n_rows], y_mant=ym[:n_rows], y_exp=r.y_exp,
+                    sat_event=r.sat_event, sat_count=r.sat_count, ns=r.ns)

