@@ -91,10 +91,11 @@ int mv4i_parse(mv4i_file *f, const uint8_t *img, size_t len);
  * of `out` filled exactly as the reference fills them (y_data in RAW and BFP
  * modes, y_mant in BFP, y_acc in PARTIAL; y_exp, sat_event, sat_count, ns).
  * Runs on the current CUDA device.  The first call for an image uploads its
- * stream relayout to HBM and caches it keyed by (f->base, header); later calls
- * reuse it, so only x and y cross PCIe.  If the caller rewrites the image bytes
- * behind the same pointer it must call mv4i_forget(f) first.  Thread-safe;
- * calls are serialised on an internal stream. */
+ * stream relayout to HBM and caches it keyed by (f->base, header, a sampled
+ * content fingerprint); later calls reuse it, so only x and y cross PCIe.
+ * A caller that frees an image, or rewrites its bytes in place, calls
+ * mv4i_forget(f) first: the fingerprint samples the image and cannot see
+ * every edit.  Thread-safe; calls are serialised on an internal stream. */
 int mv4i_matvec(const mv4i_file *f, const int16_t *x_mant, int x_exp,
                 int n_rows, int n_cols, int out_mode, mv4i_result *out);
 

@@ -159,6 +159,17 @@ class ParsedImage:
         self.f = File()
         self.rc = lib().mv4i_parse(C.byref(self.f), ptr(self.buf), self.buf.size)
 
+    def forget(self):
+        """Drop the library's cached device copy of this image."""
+        if self.rc == 0 and _lib is not None:
+            _lib.mv4i_forget(C.byref(self.f))
+
+    def __del__(self):
+        try:
+            self.forget()
+        except Exception:  # noqa: BLE001  (interpreter shutdown)
+            pass
+
     @property
     def M(self):
         return self.f.h.M

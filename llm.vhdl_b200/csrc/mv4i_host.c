@@ -227,6 +227,7 @@ int mv4i_dmat_free(mv4i_dmat *m)
 typedef struct {
     const uint8_t *base;
     mv4i_hdr       h;
+    uint64_t       fp;          /* sampled content fingerprint */
     int            device;
     mv4i_dmat      m;
     uint64_t       stamp;
@@ -248,13 +249,50 @@ static dev_ctx g_ctx[16];
 
 static int hdr_same(const mv4i_hdr *a, const mv4i_hdr *b) { return memcmp(a, b, sizeof *a) == 0; }
 
+static uint64_t fnv1a(uint64_t h, const uint8_t *p, size_t n)
+{
+    for (size_t i = 0; i < n; i++) { h ^= p[i]; h *= 0x100000001B3ull; }
+    return h;
+}
+
+/* Fingerprint of an image: the 4 KB header plus 128 evenly spaced 32-byte
+ * windows of every weight and scale sub-region (~20 KB hashed per call).
+ * It catches the usual way a pointer-keyed cache goes stale -- an image freed
+ * and another of the same geometry allocated at the same address -- but not
+ * an edit of a few bytes between samples; that case needs mv4i_forget. */
+static uint64_t image_fp(const mv4i_file *f)
+{
+    uint64_t h = fnv1a(0xCBF29CE484222325ull, f->base, MV4I_HDR_BYTES);
+    const int ri = f->h.rows_if;
+    const uint64_t tiles = (f->h.M + (uint64_t)ri - 1) / ri;
+    const uint64_t wlen = tiles * (uint64_t)f->nb * (uint64_t)f->port_b;
+    const uint64_t slen = ((tiles * (uint64_t)f->nb + (uint64_t)f->grp - 1) / (uint64_t)f->grp) * (uint64_t)f->port_b;
+    for (int pass = 0; pass < 2; pass++) {
+        const int nsub = pass ? (int)f->h.n_scale_sub : (int)f->h.nports_w;
+        const uint64_t len = pass ? slen : wlen;
+        for (int s = 0; s < nsub; s++) {
+            const uint8_t *base = f->base + (pass ? f->h.s_sub_offset[s] : f->h.w_sub_offset[s]);
+            if (len <= 4096) { h = fnv1a(h, base, len); continue; }
+            for (int i = 0; i < 128; i++) {
+                const uint64_t off = (len - 32) * (uint64_t)i / 127u;
+                h = fnv1a(h, base + off, 32);
+            }
+        }
+    }
+    return h;
+}
+
 static int cache_get(const mv4i_file *f, int device, const mv4i_dmat **out)
 {
     int free_i = -1, lru = 0;
+    const uint64_t fp = image_fp(f);
     for (int i = 0; i < CACHE_N; i++) {
         cache_ent *c = &g_cache[i];
-        if (c->base == f->base && c->device == device && hdr_same(&c->h, &f->h)) {
+        if (c->base == f->base && c->device == device && c->fp == fp && hdr_same(&c->h, &f->h)) {
             c->stamp = ++g_stamp; *out = &c->m; return 0;
+        }
+        if (c->base == f->base && c->device == device) {     /* same address, new content */
+            mv4i_dmat_free(&c->m); memset(c, 0, sizeof *c);
         }
         if (!c->base && free_i < 0) free_i = i;
         if (c->stamp < g_cache[lru].stamp) lru = i;
@@ -264,7 +302,7 @@ static int cache_get(const mv4i_file *f, int device, const mv4i_dmat **out)
     if (c->base) { mv4i_dmat_free(&c->m); memset(c, 0, sizeof *c); }
     int rc = mv4i_dmat_upload(f, device, &c->m);
     if (rc) return rc;
-    c->base = f->base; c->h = f->h; c->device = device; c->stamp = ++g_stamp;
+    c->base = f->base; c->h = f->h; c->fp = fp; c->device = device; c->stamp = ++g_stamp;
     *out = &c->m;
     return 0;
 }

@@ -113,21 +113,24 @@ def test_dropin_argument_errors_and_contract(cuda, pkg, golden):
     assert rc == 0 and np.array_equal(r["y_data"].astype(np.int64), golden["lin1_y"])
 
 
-def test_dropin_cache_forget(cuda, pkg, golden):
-    """A rewritten image behind the same pointer is picked up after mv4i_forget."""
+def test_dropin_cache_rewrite_and_forget(cuda, pkg, golden):
+    """The device copy follows the image: an in-place rewrite inside the
+    fingerprinted region is picked up on the next call, and mv4i_forget
+    drops the copy outright."""
     pi = pkg.ParsedImage(_img(golden, "lin1"))
     m = [int(v) for v in golden["lin1_meta"]]
     x = golden["lin1_x"]
     rc, r0 = pkg.matvec(pi, x, m[4], m[5], m[6], 1)
+    assert rc == 0
     soff = int.from_bytes(bytes(pi.buf[0x30:0x34]), "little")
-    pi.buf[soff + 1] ^= 0x40
+    pi.buf[soff + 1] ^= 0x40                 # the scale region is hashed whole
     rc, r1 = pkg.matvec(pi, x, m[4], m[5], m[6], 1)
-    assert np.array_equal(r0["y_data"], r1["y_data"])        # still the cached copy
-    pkg.lib().mv4i_forget(C.byref(pi.f))
-    rc, r2 = pkg.matvec(pi, x, m[4], m[5], m[6], 1)
     o = O.matvec(pi.buf.tobytes(), x, m[4], m[5], m[6], 1)[1]
-    assert np.array_equal(r2["y_data"], o["y_data"])
-    assert not np.array_equal(r2["y_data"], r0["y_data"])
+    assert rc == 0 and np.array_equal(r1["y_data"], o["y_data"])
+    assert not np.array_equal(r1["y_data"], r0["y_data"])
+    assert pkg.lib().mv4i_forget(C.byref(pi.f)) == 0
+    rc, r2 = pkg.matvec(pi, x, m[4], m[5], m[6], 1)
+    assert rc == 0 and np.array_equal(r2["y_data"], o["y_data"])
 
 
 # ------------------------------------------------------------ device layer
