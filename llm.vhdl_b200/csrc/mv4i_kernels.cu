@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include "../../include/mv4i_b200.h"
 
 #define MV_WARPS 8
@@ -58,6 +59,7 @@ struct DevJob {
 struct LaunchParams {
     int32_t njobs;
     int32_t rows_per_cta;
+    int32_t total_tiles;
     uint32_t *scratch;          // 4 words per job
     DevJob jobs[MV4I_MAX_JOBS];
 };
@@ -201,76 +203,67 @@ __device__ __forceinline__ int32_t block_dot(uint4 wv, const uint4 *planes, cons
 
 // ------------------------------------------------------------ the kernel
 
-template <int KIND, int RW>
-__global__ void __launch_bounds__(MV_THREADS)
-mv4i_kernel(const __grid_constant__ LaunchParams P)
+// Stage the activation of job J into shared memory (all threads; caller syncs).
+template <int KIND>
+__device__ __forceinline__ void stage_x(const DevJob &J, uint4 *planes, int32_t *sums, float *gfac,
+                                        float *bam, int nb, int nbp)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ int s_job, s_last;
-    __shared__ uint32_t s_amax, s_sat;
-    __shared__ int32_t s_err;
-
-    // ---- which job, which rows
-    int jid = 0;
-    for (int j = 1; j < P.njobs; j++) if ((int)blockIdx.x >= P.jobs[j].tile0) jid = j;
-    const DevJob &J = P.jobs[jid];
-    const int tile = blockIdx.x - J.tile0;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = tile * P.rows_per_cta + warp * RW;
-    const int nb = J.nb;
-    const int nbp = (nb + 3) & ~3;           // plane pitch in blocks
-
-    if (threadIdx.x == 0) { s_amax = 0; s_sat = 0; s_err = 0; }
-
-    // ---- prologue: issue the first chunk of weight loads before staging x
-    uint4 wv[RW][MV_U];
-#pragma unroll
-    for (int r = 0; r < RW; r++)
-#pragma unroll
-        for (int u = 0; u < MV_U; u++) {
-            const int b = lane + 32 * u;
-            const int row = row0 + r;
-            wv[r][u] = (row < J.n_rows && b < nb)
-                     ? ld_stream16(J.wq + (int64_t)row * J.w_pitch + 16 * (int64_t)b)
-                     : make_uint4(0, 0, 0, 0);
-        }
-
-    // ---- stage x
-    uint4 *planes = reinterpret_cast<uint4 *>(smem);
-    int32_t *sums = reinterpret_cast<int32_t *>(planes + 4 * nbp);
-    float *gfac = reinterpret_cast<float *>(sums + nbp);
     if (KIND == KIND_G128) {
         // fp16 x -> int16 on a per-128-column exponent e_g:
-        // xi = sat16(rint(x * 2^e_g)), e_g = 14 - floor(log2 amax_g); factor 2^-e_g.
-        int16_t *xi = reinterpret_cast<int16_t *>(gfac + ((nbp / 4) + 4));
+        //   xi = sat16(rint(x * 2^e_g)), e_g = 15 - ceil-exponent of the group max,
+        //   so |x * 2^e_g| < 2^15; the factor 2^-e_g goes with the group's scale.
+        // pass 1: max |x| of each 32-column block; pass 2: convert per group.
         const __half *xh = reinterpret_cast<const __half *>(J.x);
-        const int ng = (nb + 3) / 4;
-        for (int g = warp; g < ng; g += MV_WARPS) {
-            float v[4], am = 0.f;
+        const bool vec = ((((uintptr_t)xh) & 15) == 0);
+        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+            float am = 0.f;
+            if (vec && 32 * (b + 1) <= J.n_cols) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
 #pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const int k = g * 128 + lane * 4 + t;
-                v[t] = k < J.n_cols ? __half2float(xh[k]) : 0.f;
-                am = fmaxf(am, fabsf(v[t]));
+                for (int i = 0; i < 4; i++) {
+                    uint4 t = src[i];
+                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&tw[h]));
+                        am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
+                    }
+                }
+            } else {
+                for (int j = 0; j < 32; j++)
+                    if (32 * b + j < J.n_cols) am = fmaxf(am, fabsf(__half2float(xh[32 * b + j])));
             }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-            int e = 0;
-            if (am > 0.f) { int ex; frexpf(am, &ex); e = 15 - ex; }   // am in [2^(ex-1), 2^ex)
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                float s = rintf(ldexpf(v[t], e));
-                s = fminf(fmaxf(s, -32768.f), 32767.f);
-                xi[g * 128 + lane * 4 + t] = (int16_t)s;
-            }
-            if (lane == 0) gfac[g] = ldexpf(1.0f, -e);
+            bam[b] = am;
         }
         __syncthreads();
         for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+            const int g = b >> 2;
+            const float am = fmaxf(fmaxf(bam[4 * g], bam[4 * g + 1]), fmaxf(bam[4 * g + 2], bam[4 * g + 3]));
+            int e = 0;
+            if (am > 0.f) { int ex; frexpf(am, &ex); e = 15 - ex; }   // am in [2^(ex-1), 2^ex)
             int16_t v[32];
+            if (vec && 32 * (b + 1) <= J.n_cols) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = xi[32 * b + j];
+                for (int i = 0; i < 4; i++) {
+                    uint4 t = src[i];
+                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&tw[h]));
+                        v[8 * i + 2 * h]     = (int16_t)fminf(fmaxf(rintf(ldexpf(f.x, e)), -32768.f), 32767.f);
+                        v[8 * i + 2 * h + 1] = (int16_t)fminf(fmaxf(rintf(ldexpf(f.y, e)), -32768.f), 32767.f);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const float f = (32 * b + j < J.n_cols) ? __half2float(xh[32 * b + j]) : 0.f;
+                    v[j] = (int16_t)fminf(fmaxf(rintf(ldexpf(f, e)), -32768.f), 32767.f);
+                }
+            }
             stage_block<KIND_LIN>(planes, sums, nbp, b, v);
+            if ((b & 3) == 0) gfac[g] = ldexpf(1.0f, -e);
         }
     } else {
         const int16_t *xg = reinterpret_cast<const int16_t *>(J.x);
@@ -295,143 +288,195 @@ mv4i_kernel(const __grid_constant__ LaunchParams P)
             stage_block<KIND>(planes, sums, nbp, b, v);
         }
     }
-    __syncthreads();
+}
 
-    // ---- main loop
-    int64_t acc[RW];
-    float facc[RW];
-#pragma unroll
-    for (int r = 0; r < RW; r++) { acc[r] = 0; facc[r] = 0.f; }
-    bool bad = false;
+// Persistent CTAs: the flattened list of row tiles (RPC = 8 warps x RW rows
+// each, job after job) is cut into gridDim.x contiguous ranges.  A CTA stages
+// x once per job it touches, then streams its tiles; each warp owns RW rows of
+// a tile across the whole K.  Golden jobs count finished tiles per job in the
+// scratch block; the CTA that completes a job finalises it (BFP pack, status).
+template <int KIND, int RW>
+__global__ void __launch_bounds__(MV_THREADS, RW == 4 ? 2 : (RW == 2 ? 3 : 4))
+mv4i_kernel(const __grid_constant__ LaunchParams P)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ int s_last;
+    __shared__ uint32_t s_amax, s_sat;
+    __shared__ int32_t s_err;
 
-    for (int b0 = 0; b0 < nb; b0 += 32 * MV_U) {
-        if (b0 > 0) {
-#pragma unroll
-            for (int r = 0; r < RW; r++)
-#pragma unroll
-                for (int u = 0; u < MV_U; u++) {
-                    const int b = b0 + lane + 32 * u;
-                    const int row = row0 + r;
-                    wv[r][u] = (row < J.n_rows && b < nb)
-                             ? ld_stream16(J.wq + (int64_t)row * J.w_pitch + 16 * (int64_t)b)
-                             : make_uint4(0, 0, 0, 0);
-                }
-        }
-        uint16_t sv[RW][MV_U];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T = P.total_tiles;
+    const int t_end = (int)((int64_t)(blockIdx.x + 1) * T / gridDim.x);
+    int t = (int)((int64_t)blockIdx.x * T / gridDim.x);
+
+    while (t < t_end) {
+        int jid = 0;
+        for (int j = 1; j < P.njobs; j++) if (t >= P.jobs[j].tile0) jid = j;
+        const DevJob &J = P.jobs[jid];
+        const int tj_end = min(t_end, J.tile0 + J.ntiles);
+        const int nb = J.nb;
+        const int nbp = (nb + 3) & ~3;                // plane pitch in blocks
+        uint4 *planes = reinterpret_cast<uint4 *>(smem);
+        int32_t *sums = reinterpret_cast<int32_t *>(planes + 4 * nbp);
+        float *gfac = reinterpret_cast<float *>(sums + nbp);
+        float *bam = gfac + (nbp / 4 + 4);
+
+        // first tile's weights in flight while x is staged
+        int row0 = (t - J.tile0) * P.rows_per_cta + warp * RW;
+        uint4 wv[RW][MV_U];
 #pragma unroll
         for (int r = 0; r < RW; r++)
 #pragma unroll
             for (int u = 0; u < MV_U; u++) {
-                const int b = b0 + lane + 32 * u;
-                const int row = row0 + r;
-                const int col = (KIND == KIND_G128) ? (b >> 2) : b;
-                sv[r][u] = (row < J.n_rows && b < nb)
-                         ? ld_nc_u16(reinterpret_cast<const uint16_t *>(J.sc) + (int64_t)row * J.s_pitch + col)
-                         : (uint16_t)0;
+                const int b = lane + 32 * u, row = row0 + r;
+                wv[r][u] = (row < J.n_rows && b < nb)
+                         ? ld_stream16(J.wq + (int64_t)row * J.w_pitch + 16 * (int64_t)b)
+                         : make_uint4(0, 0, 0, 0);
             }
+        __syncthreads();                 // smem of the previous job is free
+        if (threadIdx.x == 0) { s_amax = 0; s_sat = 0; s_err = 0; }
+        stage_x<KIND>(J, planes, sums, gfac, bam, nb, nbp);
+        __syncthreads();
+
+        uint32_t amax = 0, nsat = 0;
+        bool bad = false;
+        for (int tile = t; tile < tj_end; tile++) {
+            row0 = (tile - J.tile0) * P.rows_per_cta + warp * RW;
+            int64_t acc[RW];
+            float facc[RW];
 #pragma unroll
-        for (int u = 0; u < MV_U; u++) {
-            const int b = b0 + lane + 32 * u;
-            if (b < nb) {
+            for (int r = 0; r < RW; r++) { acc[r] = 0; facc[r] = 0.f; }
+            for (int b0 = 0; b0 < nb; b0 += 32 * MV_U) {
+                if (b0 > 0 || tile > t) {
 #pragma unroll
-                for (int r = 0; r < RW; r++) {
-                    const int32_t part = block_dot<KIND == KIND_G128 ? KIND_LIN : KIND>(
-                        wv[r][u], planes, sums, nbp, b, J.cb);
-                    if (KIND == KIND_G128) {
-                        const float s = __half2float(__ushort_as_half(sv[r][u])) * gfac[b >> 2];
-                        facc[r] = fmaf((float)part, s, facc[r]);
-                    } else {
-                        const uint32_t sc = sv[r][u];
-                        bad |= (part >= (1 << 27) || part <= -(1 << 27) || sc > 32767u);
-                        const int64_t contrib = floor_shr((int64_t)part * (int64_t)sc, 15);
-                        acc[r] += contrib;
+                    for (int r = 0; r < RW; r++)
+#pragma unroll
+                        for (int u = 0; u < MV_U; u++) {
+                            const int b = b0 + lane + 32 * u, row = row0 + r;
+                            wv[r][u] = (row < J.n_rows && b < nb)
+                                     ? ld_stream16(J.wq + (int64_t)row * J.w_pitch + 16 * (int64_t)b)
+                                     : make_uint4(0, 0, 0, 0);
+                        }
+                }
+                uint16_t sv[RW][MV_U];
+#pragma unroll
+                for (int r = 0; r < RW; r++)
+#pragma unroll
+                    for (int u = 0; u < MV_U; u++) {
+                        const int b = b0 + lane + 32 * u, row = row0 + r;
+                        const int col = (KIND == KIND_G128) ? (b >> 2) : b;
+                        sv[r][u] = (row < J.n_rows && b < nb)
+                                 ? ld_nc_u16(reinterpret_cast<const uint16_t *>(J.sc) + (int64_t)row * J.s_pitch + col)
+                                 : (uint16_t)0;
+                    }
+#pragma unroll
+                for (int u = 0; u < MV_U; u++) {
+                    const int b = b0 + lane + 32 * u;
+                    if (b < nb) {
+#pragma unroll
+                        for (int r = 0; r < RW; r++) {
+                            const int32_t part = block_dot<KIND == KIND_G128 ? KIND_LIN : KIND>(
+                                wv[r][u], planes, sums, nbp, b, J.cb);
+                            if (KIND == KIND_G128) {
+                                const float s = __half2float(__ushort_as_half(sv[r][u])) * gfac[b >> 2];
+                                facc[r] = fmaf((float)part, s, facc[r]);
+                            } else {
+                                const uint32_t sc = sv[r][u];
+                                bad |= (part >= (1 << 27) || part <= -(1 << 27) || sc > 32767u);
+                                acc[r] += floor_shr((int64_t)part * (int64_t)sc, 15);
+                            }
+                        }
+                    }
+                }
+            }
+            // reduce across lanes, epilogue per row
+#pragma unroll
+            for (int r = 0; r < RW; r++) {
+                const int row = row0 + r;
+                if (KIND == KIND_G128) {
+                    float v = facc[r];
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0 && row < J.n_rows) {
+                        if (J.y_f32) J.y_f32[row] = v;
+                        if (J.y_f16) J.y_f16[row] = __half_as_ushort(__float2half_rn(v));
+                    }
+                } else {
+                    int64_t v = acc[r];
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0 && row < J.n_rows) {
+                        bad |= !(v < ((int64_t)1 << 47) && v > -((int64_t)1 << 47));
+                        if (J.mode == MV4I_MODE_PARTIAL) {
+                            J.y_acc[row] = v;
+                        } else {
+                            const int64_t rs = round_shift(v, J.out_shift);
+                            int32_t y;
+                            if (rs > 2147483647LL) { y = 2147483647; nsat++; }
+                            else if (rs < -2147483648LL) { y = (int32_t)0x80000000u; nsat++; }
+                            else y = (int32_t)rs;
+                            J.y_data[row] = y;
+                            const uint32_t a = y < 0 ? (uint32_t)0 - (uint32_t)y : (uint32_t)y;
+                            amax = a > amax ? a : amax;
+                        }
                     }
                 }
             }
         }
-    }
 
-    // ---- reduce across lanes, epilogue per row
-    uint32_t amax = 0, nsat = 0;
-#pragma unroll
-    for (int r = 0; r < RW; r++) {
-        const int row = row0 + r;
-        if (KIND == KIND_G128) {
-            float v = facc[r];
-#pragma unroll
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && row < J.n_rows) {
-                if (J.y_f32) J.y_f32[row] = v;
-                if (J.y_f16) J.y_f16[row] = __half_as_ushort(__float2half_rn(v));
+        if (KIND != KIND_G128) {
+            // ---- per-job completion: the CTA that finishes the job's last
+            // tile finalises BFP and the status
+            bad = __any_sync(0xffffffffu, bad);
+            if (lane == 0) {
+                if (amax) atomicMax(&s_amax, amax);
+                if (nsat) atomicAdd(&s_sat, nsat);
+                if (bad) atomicOr(reinterpret_cast<unsigned *>(&s_err), 1u);
             }
-        } else {
-            int64_t v = acc[r];
-#pragma unroll
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && row < J.n_rows) {
-                bad |= !(v < ((int64_t)1 << 47) && v > -((int64_t)1 << 47));
-                if (J.mode == MV4I_MODE_PARTIAL) {
-                    J.y_acc[row] = v;
-                } else {
-                    const int64_t rs = round_shift(v, J.out_shift);
-                    int32_t y;
-                    if (rs > 2147483647LL) { y = 2147483647; nsat++; }
-                    else if (rs < -2147483648LL) { y = (int32_t)0x80000000u; nsat++; }
-                    else y = (int32_t)rs;
-                    J.y_data[row] = y;
-                    const uint32_t a = y < 0 ? (uint32_t)0 - (uint32_t)y : (uint32_t)y;
-                    amax = a > amax ? a : amax;
+            __threadfence();
+            __syncthreads();
+            uint32_t *cnt = P.scratch + 4 * jid;     // [0] amax, [1] done, [2] sat, [3] err
+            if (threadIdx.x == 0) {
+                if (s_amax) atomicMax(&cnt[0], s_amax);
+                if (s_sat) atomicAdd(&cnt[2], s_sat);
+                if (s_err) atomicOr(&cnt[3], 1u);
+                __threadfence();
+                const uint32_t mine = (uint32_t)(tj_end - t);
+                const uint32_t done = atomicAdd(&cnt[1], mine);
+                s_last = (done + mine == (uint32_t)J.ntiles);
+            }
+            __syncthreads();
+            if (s_last) {
+                __threadfence();
+                const uint32_t gmax = atomicAdd(&cnt[0], 0u);
+                const uint32_t gsat = atomicAdd(&cnt[2], 0u);
+                const uint32_t gerr = atomicAdd(&cnt[3], 0u);
+                const int x_exp = J.d_x_exp ? *J.d_x_exp : J.x_exp;
+                int ns = 0;
+                if (J.mode == MV4I_MODE_BFP) {
+                    ns = msb_pos(gmax) - 14;
+                    if (ns < 0) ns = 0;
+                    for (int r = threadIdx.x; r < J.n_rows; r += MV_THREADS)
+                        J.y_mant[r] = sat16(round_shift((int64_t)__ldcg(J.y_data + r), ns));
+                }
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    if (J.status) {
+                        mv4i_status st;
+                        st.y_exp = J.mode == MV4I_MODE_PARTIAL ? J.w_exp + x_exp
+                                 : J.w_exp + x_exp - J.out_shift - ns;
+                        st.ns = ns;
+                        st.sat_event = gsat ? 1 : 0;
+                        st.sat_count = gsat;
+                        st.err = gerr ? -10 : 0;
+                        st.pad[0] = st.pad[1] = st.pad[2] = 0;
+                        *J.status = st;
+                    }
+                    cnt[0] = 0; cnt[1] = 0; cnt[2] = 0; cnt[3] = 0;     // leave scratch zeroed
                 }
             }
         }
-    }
-    if (KIND == KIND_G128) return;
-
-    // ---- per-job completion: the last CTA finalises BFP and the status
-    bad = __any_sync(0xffffffffu, bad);
-    if (lane == 0) {
-        if (amax) atomicMax(&s_amax, amax);
-        if (nsat) atomicAdd(&s_sat, nsat);
-        if (bad) atomicOr(reinterpret_cast<unsigned *>(&s_err), 1u);
-    }
-    __threadfence();
-    __syncthreads();
-    uint32_t *cnt = P.scratch + 4 * jid;     // [0] amax, [1] done, [2] sat, [3] err
-    if (threadIdx.x == 0) {
-        if (s_amax) atomicMax(&cnt[0], s_amax);
-        if (s_sat) atomicAdd(&cnt[2], s_sat);
-        if (s_err) atomicOr(&cnt[3], 1u);
-        __threadfence();
-        const uint32_t done = atomicAdd(&cnt[1], 1u);
-        s_last = (done == (uint32_t)J.ntiles - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const uint32_t gmax = atomicAdd(&cnt[0], 0u);
-    const uint32_t gsat = atomicAdd(&cnt[2], 0u);
-    const uint32_t gerr = atomicAdd(&cnt[3], 0u);
-    const int x_exp = J.d_x_exp ? *J.d_x_exp : J.x_exp;
-    int ns = 0;
-    if (J.mode == MV4I_MODE_BFP) {
-        ns = msb_pos(gmax) - 14;
-        if (ns < 0) ns = 0;
-        for (int r = threadIdx.x; r < J.n_rows; r += MV_THREADS)
-            J.y_mant[r] = sat16(round_shift((int64_t)__ldcg(J.y_data + r), ns));
-    }
-    if (threadIdx.x == 0) {
-        if (J.status) {
-            mv4i_status st;
-            st.y_exp = J.mode == MV4I_MODE_PARTIAL ? J.w_exp + x_exp
-                     : J.w_exp + x_exp - J.out_shift - ns;
-            st.ns = ns;
-            st.sat_event = gsat ? 1 : 0;
-            st.sat_count = gsat;
-            st.err = gerr ? -10 : 0;
-            st.pad[0] = st.pad[1] = st.pad[2] = 0;
-            *J.status = st;
-        }
-        cnt[0] = 0; cnt[1] = 0; cnt[2] = 0; cnt[3] = 0;     // leave scratch zeroed
+        t = tj_end;
     }
 }
 
@@ -448,28 +493,48 @@ extern "C" size_t mv4i_scratch_bytes(void) { return sizeof(uint32_t) * 4 * MV4I_
 
 static size_t smem_bytes(int kind, int nb)
 {
-    const int nbp = (nb + 3) & ~3;
-    size_t s = (size_t)nbp * 64 + (size_t)nbp * 4;
-    if (kind == KIND_G128) s += ((size_t)nbp / 4 + 4) * 4 + (size_t)nbp * 64;
-    return s;
+    (void)kind;
+    const size_t nbp = (size_t)((nb + 3) & ~3);
+    return nbp * 64 + nbp * 4 + (nbp / 4 + 4) * 4 + nbp * 4;   // planes, sums, gfac, bam
 }
 
+// Resident CTAs per SM for one instantiation at a given shared-memory size,
+// cached per device.
+struct OccEntry { int dev, kind, rw; size_t smem; int ctas; };
+static OccEntry g_occ[64];
+static int g_nocc = 0;
+static int g_sms[64];
+
 template <int KIND, int RW>
-static cudaError_t launch_one(const LaunchParams &P, int grid, size_t smem, cudaStream_t st)
+static cudaError_t launch_one(const LaunchParams &P, int tiles, size_t smem, cudaStream_t st)
 {
-    // opt in to more than 48 KB of dynamic shared memory once per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64) return cudaErrorInvalidDevice;
     static unsigned long long attr_set = 0;
-    if (smem > 48 * 1024) {
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
+    if (!(attr_set >> dev & 1ull)) {
+        e = cudaFuncSetAttribute(mv4i_kernel<KIND, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024);
         if (e != cudaSuccess) return e;
-        if (dev < 64 && !(attr_set >> dev & 1ull)) {
-            e = cudaFuncSetAttribute(mv4i_kernel<KIND, RW>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            if (e != cudaSuccess) return e;
-            attr_set |= 1ull << dev;
-        }
+        attr_set |= 1ull << dev;
     }
+    if (!g_sms[dev]) {
+        e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    int ctas = 0;
+    for (int i = 0; i < g_nocc; i++)
+        if (g_occ[i].dev == dev && g_occ[i].kind == KIND && g_occ[i].rw == RW && g_occ[i].smem == smem)
+            ctas = g_occ[i].ctas;
+    if (!ctas) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, mv4i_kernel<KIND, RW>, MV_THREADS, smem);
+        if (e != cudaSuccess) return e;
+        if (ctas < 1) ctas = 1;
+        if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{dev, KIND, RW, smem, ctas};
+    }
+    int grid = g_sms[dev] * ctas;
+    if (grid > tiles) grid = tiles;
     mv4i_kernel<KIND, RW><<<grid, MV_THREADS, smem, st>>>(P);
     return cudaGetLastError();
 }
@@ -478,6 +543,17 @@ static int is_linear_cb(const int8_t cb[16])
 {
     for (int i = 0; i < 16; i++) if (cb[i] != (i < 8 ? i : i - 16)) return 0;
     return 1;
+}
+
+static int env_rw()
+{
+    static int v = -1;
+    if (v < 0) {
+        const char *s = getenv("MV4I_RW");
+        v = s ? atoi(s) : 0;
+        if (v != 1 && v != 2 && v != 4) v = 0;
+    }
+    return v;
 }
 
 extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, void *stream)
@@ -490,7 +566,8 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
     P.njobs = njobs;
     P.scratch = reinterpret_cast<uint32_t *>(d_scratch);
     int kind = kind0 == MV4I_KIND_G128 ? KIND_G128 : KIND_LIN;
-    int min_rows = 1 << 30, max_nb = 0;
+    int max_nb = 0;
+    long long total_rows = 0;
     for (int i = 0; i < njobs; i++) {
         const mv4i_job &a = jobs[i];
         if (!a.w || a.w->kind != kind0 || !a.x) return -11;
@@ -498,24 +575,25 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
         if (a.n_cols > a.w->K) return -2;
         if (a.n_rows > a.w->M) return -3;
         if (a.nvec != 0 && a.nvec != 1) return -11;
-        if (a.n_cols > 65536) return -11;
+        if (a.n_cols > (kind0 == MV4I_KIND_G128 ? 32768 : 65536)) return -11;
         if (kind0 == MV4I_KIND_GOLDEN) {
             if (a.mode == MV4I_MODE_PARTIAL ? !a.y_acc : !a.y_data) return -11;
             if (a.mode == MV4I_MODE_BFP && !a.y_mant) return -11;
             if (a.mode < 0 || a.mode > 2) return -11;
+            // a non-linear codebook anywhere sends the whole list through the
+            // table path (exact for the linear codebook too)
             if (!is_linear_cb(a.w->codebook)) kind = KIND_TAB;
         } else if (!a.y_f16 && !a.y_f32) return -11;
         if ((a.w->w_pitch & 15) || (((uintptr_t)a.w->wq) & 15)) return -11;
-        if (a.n_rows < min_rows) min_rows = a.n_rows;
+        total_rows += a.n_rows;
     }
-    // a codebook that is not the linear one anywhere in the list sends every
-    // job through the table path (it is exact for the linear codebook too)
-    int tiles = 0;
-    // rows per warp: enough CTAs to cover the SMs for small jobs
-    int rw = min_rows >= 8 * 148 * 4 ? 4 : (min_rows >= 8 * 148 * 2 ? 2 : 1);
-    if (kind == KIND_G128 || kind == KIND_LIN || kind == KIND_TAB) { /* all kinds honour rw */ }
+    // rows per warp: 2 keeps three 256-thread CTAs resident per SM; small
+    // lists drop to 1 so that the tiles still cover every SM
+    int rw = env_rw();
+    if (!rw) rw = total_rows >= 148LL * 8 * 2 * 4 ? 2 : 1;
     const int rpc = MV_WARPS * rw;
     P.rows_per_cta = rpc;
+    int tiles = 0;
     for (int i = 0; i < njobs; i++) {
         const mv4i_job &a = jobs[i];
         DevJob &d = P.jobs[i];
@@ -535,6 +613,7 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
         tiles += d.ntiles;
         if (d.nb > max_nb) max_nb = d.nb;
     }
+    P.total_tiles = tiles;
     const size_t smem = smem_bytes(kind, max_nb);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e;
