@@ -114,15 +114,16 @@ uint16_t mv4i_get_scale(const mv4i_file *f, int r, int b)
 
 /* -------------------------------------------------------------- relayout */
 
-/* Stream layout: row r, block b = 16 bytes at r*pitch + 16*b (pitch = 16*nb),
- * scale (r, b) at sc[r*nb + b].  Row r of tile t sits in the tile word at byte
- * rr*16, so for each (tile, block) beat the word's bytes are scattered to their
- * rows; the sub-region slicing (6.5a) only decides which beat holds which byte. */
-static void relayout(const mv4i_file *f, uint8_t *wq, uint16_t *sc)
+/* Stream layout: row r, block b = 16 bytes at r*pitch + 16*b, scale (r, b) at
+ * sc[r*spitch + b]; rows are padded with zeros to whole 128-column groups
+ * (pitch = 64*ceil(nb/4), spitch = 4*ceil(nb/4)) so every row starts 64-byte
+ * aligned.  Row r of tile t sits in the tile word at byte rr*16, so for each
+ * (tile, block) beat the word's bytes are scattered to their rows; the
+ * sub-region slicing (6.5a) only decides which beat holds which byte. */
+static void relayout(const mv4i_file *f, uint8_t *wq, uint16_t *sc, size_t pitch, size_t spitch)
 {
     const int M = (int)f->h.M, nb = f->nb, ri = f->h.rows_if, pb = f->port_b;
     const int tiles = (M + ri - 1) / ri;
-    const size_t pitch = (size_t)nb * 16;
     const int word_b = ri * 16;
     for (int t = 0; t < tiles; t++)
         for (int b = 0; b < nb; b++) {
@@ -136,7 +137,7 @@ static void relayout(const mv4i_file *f, uint8_t *wq, uint16_t *sc)
             }
         }
     for (int r = 0; r < M; r++)
-        for (int b = 0; b < nb; b++) sc[(size_t)r * nb + b] = mv4i_get_scale(f, r, b);
+        for (int b = 0; b < nb; b++) sc[(size_t)r * spitch + b] = mv4i_get_scale(f, r, b);
 }
 
 int mv4i_dmat_upload(const mv4i_file *f, int device, mv4i_dmat *out)
@@ -145,11 +146,13 @@ int mv4i_dmat_upload(const mv4i_file *f, int device, mv4i_dmat *out)
     memset(out, 0, sizeof *out);
     const int M = (int)f->h.M, nb = f->nb;
     if (M <= 0 || nb <= 0) return -11;
-    const size_t wbytes = (size_t)M * nb * 16, sbytes = (size_t)M * nb * 2;
+    const size_t ngr = (size_t)(nb + 3) / 4;
+    const size_t pitch = ngr * 64, spitch = ngr * 4;
+    const size_t wbytes = (size_t)M * pitch, sbytes = (size_t)M * spitch * 2;
     const size_t soff = (wbytes + 255) & ~(size_t)255;
-    uint8_t *host = (uint8_t *)malloc(soff + sbytes);
+    uint8_t *host = (uint8_t *)calloc(1, soff + sbytes);
     if (!host) return -11;
-    relayout(f, host, (uint16_t *)(host + soff));
+    relayout(f, host, (uint16_t *)(host + soff), pitch, spitch);
     int prev = 0;
     cudaError_t e = cudaGetDevice(&prev);
     if (e == cudaSuccess) e = cudaSetDevice(device);
@@ -161,8 +164,8 @@ int mv4i_dmat_upload(const mv4i_file *f, int device, mv4i_dmat *out)
     if (e != cudaSuccess) { if (d) cudaFree(d); return fail_cuda(e); }
     out->wq = (const uint8_t *)d;
     out->sc = (const uint8_t *)d + soff;
-    out->w_pitch = (int64_t)nb * 16;
-    out->s_pitch = nb;
+    out->w_pitch = (int64_t)pitch;
+    out->s_pitch = (int64_t)spitch;
     out->M = M; out->K = (int32_t)f->h.K;
     out->w_exp = f->h.w_exp; out->out_shift = f->h.out_shift;
     memcpy(out->codebook, f->h.codebook, 16);

@@ -30,6 +30,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <string.h>
 #include "../../include/mv4i_b200.h"
 
 #define MV_WARPS 8
@@ -54,6 +55,8 @@ struct DevJob {
     int32_t        mode, x_exp, w_exp, out_shift;
     uint32_t       cb[4];
     int32_t        tile0, ntiles;
+    int32_t        lpr;                    // v3: lanes per row
+    int32_t        sc_vec;                 // v3: golden scales as one 8-byte load per group
 };
 
 struct LaunchParams {
@@ -204,10 +207,16 @@ __device__ __forceinline__ int32_t block_dot(uint4 wv, const uint4 *planes, cons
 // ------------------------------------------------------------ the kernel
 
 // Stage the activation of job J into shared memory (all threads; caller syncs).
-template <int KIND>
+__device__ __forceinline__ void named_sync(int id, int n)
+{ asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory"); }
+
+// NTHR threads with index tid stage x; NAMED selects barrier 1 over NTHR
+// threads (producer/consumer kernel) instead of __syncthreads.
+template <int KIND, int NTHR = MV_THREADS, bool NAMED = false>
 __device__ __forceinline__ void stage_x(const DevJob &J, uint4 *planes, int32_t *sums, float *gfac,
-                                        float *bam, int nb, int nbp)
+                                        float *bam, int nb, int nbp, int tid = -1)
 {
+    if (tid < 0) tid = threadIdx.x;
     if (KIND == KIND_G128) {
         // fp16 x -> int16 on a per-128-column exponent e_g:
         //   xi = sat16(rint(x * 2^e_g)), e_g = 15 - ceil-exponent of the group max,
@@ -215,7 +224,7 @@ __device__ __forceinline__ void stage_x(const DevJob &J, uint4 *planes, int32_t 
         // pass 1: max |x| of each 32-column block; pass 2: convert per group.
         const __half *xh = reinterpret_cast<const __half *>(J.x);
         const bool vec = ((((uintptr_t)xh) & 15) == 0);
-        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+        for (int b = tid; b < nb; b += NTHR) {
             float am = 0.f;
             if (vec && 32 * (b + 1) <= J.n_cols) {
                 const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
@@ -235,8 +244,8 @@ __device__ __forceinline__ void stage_x(const DevJob &J, uint4 *planes, int32_t 
             }
             bam[b] = am;
         }
-        __syncthreads();
-        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+        if (NAMED) named_sync(1, NTHR); else __syncthreads();
+        for (int b = tid; b < nb; b += NTHR) {
             const int g = b >> 2;
             const float am = fmaxf(fmaxf(bam[4 * g], bam[4 * g + 1]), fmaxf(bam[4 * g + 2], bam[4 * g + 3]));
             int e = 0;
@@ -267,7 +276,7 @@ __device__ __forceinline__ void stage_x(const DevJob &J, uint4 *planes, int32_t 
         }
     } else {
         const int16_t *xg = reinterpret_cast<const int16_t *>(J.x);
-        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+        for (int b = tid; b < nb; b += NTHR) {
             int16_t v[32];
             if (32 * (b + 1) <= J.n_cols && (((uintptr_t)(xg + 32 * b)) & 15) == 0) {
                 const uint4 *src = reinterpret_cast<const uint4 *>(xg + 32 * b);
@@ -299,7 +308,7 @@ template <int KIND, int RW>
 __global__ void __launch_bounds__(MV_THREADS, RW == 4 ? 2 : (RW == 2 ? 3 : 4))
 mv4i_kernel(const __grid_constant__ LaunchParams P)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_last;
     __shared__ uint32_t s_amax, s_sat;
     __shared__ int32_t s_err;
@@ -480,6 +489,429 @@ mv4i_kernel(const __grid_constant__ LaunchParams P)
     }
 }
 
+// ------------------------------------------------------- v3 kernel (default)
+
+// 256-bit streaming load (sm_100): 32 bytes = 64 nibbles = two 32-blocks.
+__device__ __forceinline__ void ld_stream32(const void *p, uint32_t (&w)[8])
+{
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]),
+                   "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7]) : "l"(p));
+}
+__device__ __forceinline__ uint2 ld_nc_u64(const void *p)
+{
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+// Shared layout for v3: plane c of block i (0..3) of group g (128 columns)
+// at planes[(c*4 + i)*ngp + g]; block sums as int4 per group.
+template <int KIND>
+__device__ __forceinline__ void stage_block_v3(uint4 *planes, int4 *sums4, int ngp, int b, const int16_t v[32])
+{
+    uint32_t w[4][4];
+    int32_t s = 0;
+    if (KIND == KIND_TAB) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const uint32_t u = (uint16_t)v[4 * q + t];
+                lo |= (u & 0xFFu) << (8 * t);
+                hi |= (u >> 8) << (8 * t);
+            }
+            w[q >> 2][q & 3] = lo;
+            w[2 + (q >> 2)][q & 3] = hi;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t le = 0, lo = 0, he = 0, ho = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const uint32_t ue = (uint16_t)v[8 * q + 2 * t], uo = (uint16_t)v[8 * q + 2 * t + 1];
+                le |= (ue & 0xFFu) << (8 * t);
+                lo |= (uo & 0xFFu) << (8 * t);
+                he |= (ue >> 8) << (8 * t);
+                ho |= (uo >> 8) << (8 * t);
+            }
+            w[0][q] = le; w[1][q] = lo; w[2][q] = he; w[3][q] = ho;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) s += v[j];
+    }
+    const int g = b >> 2, i = b & 3;
+#pragma unroll
+    for (int c = 0; c < 4; c++) planes[(c * 4 + i) * ngp + g] = make_uint4(w[c][0], w[c][1], w[c][2], w[c][3]);
+    reinterpret_cast<int32_t *>(sums4 + g)[i] = s;
+}
+
+template <int KIND>
+__device__ __forceinline__ void stage_x_v3(const DevJob &J, uint4 *planes, int4 *sums4, float *gfac,
+                                           float *bam, int nb, int ngp)
+{
+    const int ngr = (nb + 3) >> 2;                 // groups covering nb
+    if (KIND == KIND_G128) {
+        const __half *xh = reinterpret_cast<const __half *>(J.x);
+        const bool vec = ((((uintptr_t)xh) & 15) == 0);
+        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+            float am = 0.f;
+            if (vec && 32 * (b + 1) <= J.n_cols) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const uint4 t = src[q];
+                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&tw[h]));
+                        am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
+                    }
+                }
+            } else {
+                for (int j = 0; j < 32; j++)
+                    if (32 * b + j < J.n_cols) am = fmaxf(am, fabsf(__half2float(xh[32 * b + j])));
+            }
+            bam[b] = am;
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
+            const int g = b >> 2;
+            const float am = fmaxf(fmaxf(bam[4 * g], bam[4 * g + 1]), fmaxf(bam[4 * g + 2], bam[4 * g + 3]));
+            int e = 0;
+            if (am > 0.f) { int ex; frexpf(am, &ex); e = 15 - ex; }   // am in [2^(ex-1), 2^ex)
+            int16_t v[32];
+            if (vec && 32 * (b + 1) <= J.n_cols) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const uint4 t = src[q];
+                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&tw[h]));
+                        v[8 * q + 2 * h]     = (int16_t)fminf(fmaxf(rintf(ldexpf(f.x, e)), -32768.f), 32767.f);
+                        v[8 * q + 2 * h + 1] = (int16_t)fminf(fmaxf(rintf(ldexpf(f.y, e)), -32768.f), 32767.f);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const float f = (32 * b + j < J.n_cols) ? __half2float(xh[32 * b + j]) : 0.f;
+                    v[j] = (int16_t)fminf(fmaxf(rintf(ldexpf(f, e)), -32768.f), 32767.f);
+                }
+            }
+            stage_block_v3<KIND_LIN>(planes, sums4, ngp, b, v);
+            if ((b & 3) == 0) gfac[g] = ldexpf(1.0f, -e);
+        }
+    } else {
+        const int16_t *xg = reinterpret_cast<const int16_t *>(J.x);
+        for (int b = threadIdx.x; b < 4 * ngr; b += MV_THREADS) {
+            int16_t v[32];
+            if (32 * (b + 1) <= J.n_cols && (((uintptr_t)(xg + 32 * b)) & 15) == 0) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(xg + 32 * b);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const uint4 t = src[q];
+                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        v[8 * q + 2 * h] = (int16_t)(tw[h] & 0xFFFFu);
+                        v[8 * q + 2 * h + 1] = (int16_t)(tw[h] >> 16);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = (32 * b + j < J.n_cols) ? xg[32 * b + j] : (int16_t)0;
+            }
+            stage_block_v3<KIND>(planes, sums4, ngp, b, v);
+        }
+    }
+}
+
+// One 32-block for RW rows: the 4 x planes of the block are loaded once.
+// ws[r][0..3] are the block's 4 weight words of row r.  Linear codebook:
+// accumulates the 4 per-row partial sums; table codebook: 2.
+template <int KIND, int RW>
+__device__ __forceinline__ void block_dot_v3(const uint32_t (&ws)[RW][4], const uint4 p0, const uint4 p1,
+                                             const uint4 p2, const uint4 p3, const uint32_t cbt[4],
+                                             int (&a)[RW][4])
+{
+    if (KIND == KIND_TAB) {
+        const uint32_t xl[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const uint32_t xh[8] = {p2.x, p2.y, p2.z, p2.w, p3.x, p3.y, p3.z, p3.w};
+#pragma unroll
+        for (int r = 0; r < RW; r++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t w = ws[r][q];
+                const uint32_t sl = w & 0x7777u, sh = (w >> 16) & 0x7777u;
+                const uint32_t w4 = w << 4;
+                const uint32_t m0 = prmt(w4, w, 0xD9C8u), m1 = prmt(w4, w, 0xFBEAu);
+                const uint32_t c0 = (prmt(cbt[0], cbt[1], sl) & ~m0) | (prmt(cbt[2], cbt[3], sl) & m0);
+                const uint32_t c1 = (prmt(cbt[0], cbt[1], sh) & ~m1) | (prmt(cbt[2], cbt[3], sh) & m1);
+                a[r][0] = dp4a_su(c0, xl[2 * q], a[r][0]);
+                a[r][1] = dp4a_su(c1, xl[2 * q + 1], a[r][1]);
+                a[r][2] = dp4a_ss(c0, xh[2 * q], a[r][2]);
+                a[r][3] = dp4a_ss(c1, xh[2 * q + 1], a[r][3]);
+            }
+    } else {
+        const uint32_t xle[4] = {p0.x, p0.y, p0.z, p0.w}, xlo[4] = {p1.x, p1.y, p1.z, p1.w};
+        const uint32_t xhe[4] = {p2.x, p2.y, p2.z, p2.w}, xho[4] = {p3.x, p3.y, p3.z, p3.w};
+#pragma unroll
+        for (int r = 0; r < RW; r++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t w = ws[r][q];
+                const uint32_t e = (w & 0x0F0F0F0Fu) ^ 0x08080808u;     // (idx^8) of even j
+                const uint32_t o = (w & 0xF0F0F0F0u) ^ 0x80808080u;     // 16*(idx^8) of odd j
+                a[r][0] = dp4a_uu(e, xle[q], a[r][0]);
+                a[r][1] = dp4a_uu(o, xlo[q], a[r][1]);
+                a[r][2] = dp4a_us(e, xhe[q], a[r][2]);
+                a[r][3] = dp4a_us(o, xho[q], a[r][3]);
+            }
+    }
+}
+
+// exact sum_j cb*x of the accumulated blocks; sx = sum of x over them
+template <int KIND>
+__device__ __forceinline__ int32_t combine_v3(const int (&a)[4], int32_t sx)
+{
+    if (KIND == KIND_TAB) return a[0] + a[1] + (a[2] + a[3]) * 256;
+    return a[0] + (a[1] >> 4) + (a[2] + (a[3] >> 4)) * 256 - 8 * sx;   // a[1], a[3]: multiples of 16
+}
+
+// Work split: a job's rows are processed LPR lanes per row (LPR = largest
+// power of two <= 32 dividing the job's group count), so 32/LPR rows share a
+// warp and every lane owns whole 128-column groups (GPL of them); RW rows per
+// lane segment share each x-plane load.  Tiles of 8 warps x (32/LPR) x RW
+// rows are flattened over the job list and cut into contiguous per-CTA ranges.
+template <int KIND, int RW>
+__global__ void __launch_bounds__(MV_THREADS, RW == 4 ? 2 : 3)
+mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_last;
+    __shared__ uint32_t s_amax, s_sat;
+    __shared__ int32_t s_err;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T = P.total_tiles;
+    const int t_end = (int)((int64_t)(blockIdx.x + 1) * T / gridDim.x);
+    int t = (int)((int64_t)blockIdx.x * T / gridDim.x);
+
+    while (t < t_end) {
+        int jid = 0;
+        for (int j = 1; j < P.njobs; j++) if (t >= P.jobs[j].tile0) jid = j;
+        const DevJob &J = P.jobs[jid];
+        // job fields in registers for the whole segment
+        const uint8_t *const wq = J.wq;
+        const uint16_t *const scp = reinterpret_cast<const uint16_t *>(J.sc);
+        const int64_t w_pitch = J.w_pitch, s_pitch = J.s_pitch;
+        const int n_rows = J.n_rows, nb = J.nb, lpr = J.lpr, mode = J.mode, out_shift = J.out_shift;
+        const bool sc_vec = J.sc_vec;
+        const int tile0 = J.tile0;
+        const int tj_end = min(t_end, tile0 + J.ntiles);
+        const int ngr = (nb + 3) >> 2;             // groups covering the job
+        const int ngp = (ngr + 3) & ~3;
+        const int rpw = (32 / lpr) * RW;           // rows per warp per tile
+        const int rpt = MV_WARPS * rpw;            // rows per tile
+        uint4 *planes = reinterpret_cast<uint4 *>(smem);
+        int4 *sums4 = reinterpret_cast<int4 *>(planes + 16 * ngp);
+        float *gfac = reinterpret_cast<float *>(sums4 + ngp);
+        float *bam = gfac + ngp;
+        uint32_t cbt[4] = {J.cb[0], J.cb[1], J.cb[2], J.cb[3]};
+
+        __syncthreads();                            // previous job's smem is free
+        if (threadIdx.x == 0) { s_amax = 0; s_sat = 0; s_err = 0; }
+        stage_x_v3<KIND>(J, planes, sums4, gfac, bam, nb, ngp);
+        __syncthreads();
+
+        const int seg = lane / lpr, sl = lane % lpr;   // row segment, lane in segment
+        uint32_t amax = 0, nsat = 0;
+        bool bad = false;
+        for (int tile = t; tile < tj_end; tile++) {
+            const int rbase = (tile - tile0) * rpt + warp * rpw + seg * RW;
+            bool rv[RW];
+            const uint8_t *wrow[RW];
+#pragma unroll
+            for (int r = 0; r < RW; r++) {
+                rv[r] = rbase + r < n_rows;
+                wrow[r] = wq + (int64_t)(rv[r] ? rbase + r : 0) * w_pitch;
+            }
+            int64_t acc[RW];
+            float facc[RW];
+#pragma unroll
+            for (int r = 0; r < RW; r++) { acc[r] = 0; facc[r] = 0.f; }
+            for (int g = sl; g < ngr; g += lpr) {
+                // weights: 64 bytes (4 blocks) per row
+                uint32_t wv[RW][16];
+#pragma unroll
+                for (int r = 0; r < RW; r++) {
+                    if (rv[r]) {
+                        uint32_t h0[8], h1[8];
+                        ld_stream32(wrow[r] + 64 * (int64_t)g, h0);
+                        ld_stream32(wrow[r] + 64 * (int64_t)g + 32, h1);
+#pragma unroll
+                        for (int k = 0; k < 8; k++) { wv[r][k] = h0[k]; wv[r][8 + k] = h1[k]; }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 16; k++) wv[r][k] = 0;
+                    }
+                }
+                // scales
+                uint16_t sv[RW][4];
+#pragma unroll
+                for (int r = 0; r < RW; r++) {
+                    const uint16_t *srow = scp + (int64_t)(rv[r] ? rbase + r : 0) * s_pitch;
+                    if (KIND == KIND_G128) {
+                        sv[r][0] = rv[r] ? ld_nc_u16(srow + g) : (uint16_t)0;
+                    } else if (sc_vec) {
+                        const uint2 s4 = rv[r] ? ld_nc_u64(srow + 4 * g) : make_uint2(0, 0);
+                        sv[r][0] = (uint16_t)s4.x; sv[r][1] = (uint16_t)(s4.x >> 16);
+                        sv[r][2] = (uint16_t)s4.y; sv[r][3] = (uint16_t)(s4.y >> 16);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            sv[r][i] = (rv[r] && 4 * g + i < nb) ? ld_nc_u16(srow + 4 * g + i) : (uint16_t)0;
+                    }
+                }
+                const int4 sx4 = sums4[g];
+                const int32_t sxv[4] = {sx4.x, sx4.y, sx4.z, sx4.w};
+                if (KIND == KIND_G128) {
+                    int a[RW][4];
+#pragma unroll
+                    for (int r = 0; r < RW; r++) a[r][0] = a[r][1] = a[r][2] = a[r][3] = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        uint32_t ws[RW][4];
+#pragma unroll
+                        for (int r = 0; r < RW; r++)
+#pragma unroll
+                            for (int q = 0; q < 4; q++) ws[r][q] = wv[r][4 * i + q];
+                        block_dot_v3<KIND_LIN, RW>(ws, planes[(0 * 4 + i) * ngp + g], planes[(1 * 4 + i) * ngp + g],
+                                                   planes[(2 * 4 + i) * ngp + g], planes[(3 * 4 + i) * ngp + g], cbt, a);
+                    }
+                    const int32_t sxg = sxv[0] + sxv[1] + sxv[2] + sxv[3];
+                    const float gf = gfac[g];
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        const int32_t part = combine_v3<KIND_LIN>(a[r], sxg);
+                        const float s = __half2float(__ushort_as_half(sv[r][0])) * gf;
+                        facc[r] = fmaf((float)part, s, facc[r]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        int a[RW][4];
+#pragma unroll
+                        for (int r = 0; r < RW; r++) a[r][0] = a[r][1] = a[r][2] = a[r][3] = 0;
+                        uint32_t ws[RW][4];
+#pragma unroll
+                        for (int r = 0; r < RW; r++)
+#pragma unroll
+                            for (int q = 0; q < 4; q++) ws[r][q] = wv[r][4 * i + q];
+                        block_dot_v3<KIND, RW>(ws, planes[(0 * 4 + i) * ngp + g], planes[(1 * 4 + i) * ngp + g],
+                                               planes[(2 * 4 + i) * ngp + g], planes[(3 * 4 + i) * ngp + g], cbt, a);
+#pragma unroll
+                        for (int r = 0; r < RW; r++) {
+                            const int32_t part = combine_v3<KIND>(a[r], sxv[i]);
+                            const uint32_t sc = sv[r][i];
+                            bad |= (part >= (1 << 27) || part <= -(1 << 27) || sc > 32767u);
+                            acc[r] += floor_shr((int64_t)part * (int64_t)sc, 15);
+                        }
+                    }
+                }
+            }
+            // reduce across the lpr lanes of the segment, epilogue per row
+#pragma unroll
+            for (int r = 0; r < RW; r++) {
+                const int row = rbase + r;
+                if (KIND == KIND_G128) {
+                    float v = facc[r];
+                    for (int o = lpr >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (sl == 0 && row < n_rows) {
+                        if (J.y_f32) J.y_f32[row] = v;
+                        if (J.y_f16) J.y_f16[row] = __half_as_ushort(__float2half_rn(v));
+                    }
+                } else {
+                    int64_t v = acc[r];
+                    for (int o = lpr >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (sl == 0 && row < n_rows) {
+                        bad |= !(v < ((int64_t)1 << 47) && v > -((int64_t)1 << 47));
+                        if (mode == MV4I_MODE_PARTIAL) {
+                            J.y_acc[row] = v;
+                        } else {
+                            const int64_t rs = round_shift(v, out_shift);
+                            int32_t y;
+                            if (rs > 2147483647LL) { y = 2147483647; nsat++; }
+                            else if (rs < -2147483648LL) { y = (int32_t)0x80000000u; nsat++; }
+                            else y = (int32_t)rs;
+                            J.y_data[row] = y;
+                            const uint32_t av = y < 0 ? (uint32_t)0 - (uint32_t)y : (uint32_t)y;
+                            amax = av > amax ? av : amax;
+                        }
+                    }
+                }
+            }
+        }
+
+        if (KIND != KIND_G128) {
+            bad = __any_sync(0xffffffffu, bad);
+            if (lane == 0) {
+                if (bad) atomicOr(reinterpret_cast<unsigned *>(&s_err), 1u);
+            }
+            if (amax) atomicMax(&s_amax, amax);
+            if (nsat) atomicAdd(&s_sat, nsat);
+            __threadfence();
+            __syncthreads();
+            uint32_t *cnt = P.scratch + 4 * jid;     // [0] amax, [1] done, [2] sat, [3] err
+            if (threadIdx.x == 0) {
+                if (s_amax) atomicMax(&cnt[0], s_amax);
+                if (s_sat) atomicAdd(&cnt[2], s_sat);
+                if (s_err) atomicOr(&cnt[3], 1u);
+                __threadfence();
+                const uint32_t mine = (uint32_t)(tj_end - t);
+                const uint32_t done = atomicAdd(&cnt[1], mine);
+                s_last = (done + mine == (uint32_t)J.ntiles);
+            }
+            __syncthreads();
+            if (s_last) {
+                __threadfence();
+                const uint32_t gmax = atomicAdd(&cnt[0], 0u);
+                const uint32_t gsat = atomicAdd(&cnt[2], 0u);
+                const uint32_t gerr = atomicAdd(&cnt[3], 0u);
+                const int x_exp = J.d_x_exp ? *J.d_x_exp : J.x_exp;
+                int ns = 0;
+                if (mode == MV4I_MODE_BFP) {
+                    ns = msb_pos(gmax) - 14;
+                    if (ns < 0) ns = 0;
+                    for (int r = threadIdx.x; r < n_rows; r += MV_THREADS)
+                        J.y_mant[r] = sat16(round_shift((int64_t)__ldcg(J.y_data + r), ns));
+                }
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    if (J.status) {
+                        mv4i_status st;
+                        st.y_exp = mode == MV4I_MODE_PARTIAL ? J.w_exp + x_exp
+                                 : J.w_exp + x_exp - out_shift - ns;
+                        st.ns = ns;
+                        st.sat_event = gsat ? 1 : 0;
+                        st.sat_count = gsat;
+                        st.err = gerr ? -10 : 0;
+                        st.pad[0] = st.pad[1] = st.pad[2] = 0;
+                        *J.status = st;
+                    }
+                    cnt[0] = 0; cnt[1] = 0; cnt[2] = 0; cnt[3] = 0;     // leave scratch zeroed
+                }
+            }
+        }
+        t = tj_end;
+    }
+}
+
 // ---------------------------------------------------------------- launch
 
 // last CUDA error seen by any entry point (shared with mv4i_host.c)
@@ -539,6 +971,47 @@ static cudaError_t launch_one(const LaunchParams &P, int tiles, size_t smem, cud
     return cudaGetLastError();
 }
 
+template <int KIND, int RW>
+static cudaError_t launch_v3(const LaunchParams &P, int tiles, size_t smem, cudaStream_t st)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64) return cudaErrorInvalidDevice;
+    static unsigned long long attr_set = 0;
+    if (!(attr_set >> dev & 1ull)) {
+        e = cudaFuncSetAttribute(mv4i_v3_kernel<KIND, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set |= 1ull << dev;
+    }
+    if (!g_sms[dev]) {
+        e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    int ctas = 0;
+    for (int i = 0; i < g_nocc; i++)
+        if (g_occ[i].dev == dev && g_occ[i].kind == 16 + KIND && g_occ[i].rw == RW && g_occ[i].smem == smem)
+            ctas = g_occ[i].ctas;
+    if (!ctas) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, mv4i_v3_kernel<KIND, RW>, MV_THREADS, smem);
+        if (e != cudaSuccess) return e;
+        if (ctas < 1) ctas = 1;
+        if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{dev, 16 + KIND, RW, smem, ctas};
+    }
+    int grid = g_sms[dev] * ctas;
+    if (grid > tiles) grid = tiles;
+    mv4i_v3_kernel<KIND, RW><<<grid, MV_THREADS, smem, st>>>(P);
+    return cudaGetLastError();
+}
+
+static int env_path()
+{
+    static int v = -1;
+    if (v < 0) { const char *s = getenv("MV4I_PATH"); v = (s && !strcmp(s, "v1")) ? 1 : 0; }
+    return v;
+}
+
 static int is_linear_cb(const int8_t cb[16])
 {
     for (int i = 0; i < 16; i++) if (cb[i] != (i < 8 ? i : i - 16)) return 0;
@@ -587,12 +1060,25 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
         if ((a.w->w_pitch & 15) || (((uintptr_t)a.w->wq) & 15)) return -11;
         total_rows += a.n_rows;
     }
-    // rows per warp: 2 keeps three 256-thread CTAs resident per SM; small
-    // lists drop to 1 so that the tiles still cover every SM
+    // v3 (default) streams 64-byte groups with 256-bit loads; it needs every
+    // row 32-byte aligned and rows padded to whole 128-column groups.  Other
+    // layouts take the 128-bit load kernel (v1).
+    bool v3 = !env_path();
+    for (int i = 0; i < njobs && v3; i++) {
+        const mv4i_dmat *w = jobs[i].w;
+        const int ngr = ((kind0 == MV4I_KIND_G128 ? ((jobs[i].n_cols + 127) / 128) * 4
+                                                  : (jobs[i].n_cols + 31) / 32) + 3) / 4;
+        if ((((uintptr_t)w->wq) & 31) || (w->w_pitch & 31) || w->w_pitch < 64LL * ngr) v3 = false;
+    }
     int rw = env_rw();
-    if (!rw) rw = total_rows >= 148LL * 8 * 2 * 4 ? 2 : 1;
-    const int rpc = MV_WARPS * rw;
-    P.rows_per_cta = rpc;
+    if (v3) {
+        if (!rw || rw == 1) rw = 2;
+    } else if (!rw) {
+        // 2 keeps three 256-thread CTAs resident per SM; small lists drop to 1
+        // so that the tiles still cover every SM
+        rw = total_rows >= 148LL * 8 * 2 * 4 ? 2 : 1;
+    }
+    P.rows_per_cta = MV_WARPS * rw;
     int tiles = 0;
     for (int i = 0; i < njobs; i++) {
         const mv4i_job &a = jobs[i];
@@ -608,15 +1094,35 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
         for (int q = 0; q < 4; q++)
             d.cb[q] = (uint32_t)(uint8_t)a.w->codebook[4 * q] | ((uint32_t)(uint8_t)a.w->codebook[4 * q + 1] << 8)
                     | ((uint32_t)(uint8_t)a.w->codebook[4 * q + 2] << 16) | ((uint32_t)(uint8_t)a.w->codebook[4 * q + 3] << 24);
-        d.ntiles = (a.n_rows + rpc - 1) / rpc;
+        const int ngr = (d.nb + 3) / 4;
+        int lpr = 32;
+        while (lpr > 1 && (ngr % lpr)) lpr >>= 1;
+        d.lpr = lpr;
+        d.sc_vec = (kind0 == MV4I_KIND_GOLDEN) && !(d.nb & 3) && !(d.s_pitch & 3) && !(((uintptr_t)d.sc) & 7);
+        const int rpt = v3 ? MV_WARPS * (32 / lpr) * rw : MV_WARPS * rw;
+        d.ntiles = (a.n_rows + rpt - 1) / rpt;
         d.tile0 = tiles;
         tiles += d.ntiles;
         if (d.nb > max_nb) max_nb = d.nb;
     }
     P.total_tiles = tiles;
-    const size_t smem = smem_bytes(kind, max_nb);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e;
+    if (v3) {
+        const size_t ngp = (size_t)((((max_nb + 3) / 4) + 3) & ~3);
+        const size_t smem = ngp * (256 + 16 + 4 + 16);
+        switch (kind * 4 + rw) {
+        case KIND_LIN * 4 + 2:  e = launch_v3<KIND_LIN, 2>(P, tiles, smem, st); break;
+        case KIND_LIN * 4 + 4:  e = launch_v3<KIND_LIN, 4>(P, tiles, smem, st); break;
+        case KIND_TAB * 4 + 2:  e = launch_v3<KIND_TAB, 2>(P, tiles, smem, st); break;
+        case KIND_TAB * 4 + 4:  e = launch_v3<KIND_TAB, 4>(P, tiles, smem, st); break;
+        case KIND_G128 * 4 + 2: e = launch_v3<KIND_G128, 2>(P, tiles, smem, st); break;
+        case KIND_G128 * 4 + 4: e = launch_v3<KIND_G128, 4>(P, tiles, smem, st); break;
+        default: return -11;
+        }
+        return e == cudaSuccess ? 0 : cuda_fail(e);
+    }
+    const size_t smem = smem_bytes(kind, max_nb);
     switch (kind * 4 + rw) {
     case KIND_LIN * 4 + 1:  e = launch_one<KIND_LIN, 1>(P, tiles, smem, st); break;
     case KIND_LIN * 4 + 2:  e = launch_one<KIND_LIN, 2>(P, tiles, smem, st); break;
