@@ -505,47 +505,93 @@ __device__ __forceinline__ uint2 ld_nc_u64(const void *p)
     return v;
 }
 
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c)
+{ int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+
 // Shared layout for v3: plane c of block i (0..3) of group g (128 columns)
-// at planes[(c*4 + i)*ngp + g]; block sums as int4 per group.
+// at planes[(c*4 + i)*ngp + g]; block sums as int4 per group.  xw holds the
+// block's 32 int16 values as 16 packed pairs (x[2h] low half, x[2h+1] high).
 template <int KIND>
-__device__ __forceinline__ void stage_block_v3(uint4 *planes, int4 *sums4, int ngp, int b, const int16_t v[32])
+__device__ __forceinline__ void stage_block_v3(uint4 *planes, int4 *sums4, int ngp, int b, const uint32_t (&xw)[16])
 {
     uint32_t w[4][4];
-    int32_t s = 0;
     if (KIND == KIND_TAB) {
+        // natural order: low bytes of x[4q..4q+3], high bytes likewise
 #pragma unroll
         for (int q = 0; q < 8; q++) {
-            uint32_t lo = 0, hi = 0;
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const uint32_t u = (uint16_t)v[4 * q + t];
-                lo |= (u & 0xFFu) << (8 * t);
-                hi |= (u >> 8) << (8 * t);
-            }
-            w[q >> 2][q & 3] = lo;
-            w[2 + (q >> 2)][q & 3] = hi;
+            w[q >> 2][q & 3]       = prmt(xw[2 * q], xw[2 * q + 1], 0x6420u);
+            w[2 + (q >> 2)][q & 3] = prmt(xw[2 * q], xw[2 * q + 1], 0x7531u);
         }
     } else {
+        // word q: even j = 8q + {0,2,4,6} and odd j = 8q + {1,3,5,7}
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-            uint32_t le = 0, lo = 0, he = 0, ho = 0;
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const uint32_t ue = (uint16_t)v[8 * q + 2 * t], uo = (uint16_t)v[8 * q + 2 * t + 1];
-                le |= (ue & 0xFFu) << (8 * t);
-                lo |= (uo & 0xFFu) << (8 * t);
-                he |= (ue >> 8) << (8 * t);
-                ho |= (uo >> 8) << (8 * t);
-            }
-            w[0][q] = le; w[1][q] = lo; w[2][q] = he; w[3][q] = ho;
+            const uint32_t alo = prmt(xw[4 * q], xw[4 * q + 1], 0x6420u);       // lo bytes j 8q..8q+3
+            const uint32_t blo = prmt(xw[4 * q + 2], xw[4 * q + 3], 0x6420u);   // lo bytes j 8q+4..8q+7
+            const uint32_t ahi = prmt(xw[4 * q], xw[4 * q + 1], 0x7531u);
+            const uint32_t bhi = prmt(xw[4 * q + 2], xw[4 * q + 3], 0x7531u);
+            w[0][q] = prmt(alo, blo, 0x6420u);
+            w[1][q] = prmt(alo, blo, 0x7531u);
+            w[2][q] = prmt(ahi, bhi, 0x6420u);
+            w[3][q] = prmt(ahi, bhi, 0x7531u);
         }
+    }
+    int32_t s = 0;
+    if (KIND != KIND_TAB) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) s += v[j];
+        for (int h = 0; h < 16; h++) s = dp2a_lo(xw[h], 0x0101u, s);    // x[2h] + x[2h+1]
     }
     const int g = b >> 2, i = b & 3;
 #pragma unroll
     for (int c = 0; c < 4; c++) planes[(c * 4 + i) * ngp + g] = make_uint4(w[c][0], w[c][1], w[c][2], w[c][3]);
     reinterpret_cast<int32_t *>(sums4 + g)[i] = s;
+}
+
+// x block b as 16 packed int16 pairs, zero past n_cols.
+__device__ __forceinline__ void load_x16(const int16_t *xg, int n_cols, int b, uint32_t (&xw)[16])
+{
+    if (32 * (b + 1) <= n_cols && (((uintptr_t)(xg + 32 * b)) & 15) == 0) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xg + 32 * b);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint4 t = src[q];
+            xw[4 * q] = t.x; xw[4 * q + 1] = t.y; xw[4 * q + 2] = t.z; xw[4 * q + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 16; h++) {
+            const int k = 32 * b + 2 * h;
+            const uint32_t lo = k < n_cols ? (uint16_t)xg[k] : 0u;
+            const uint32_t hi = k + 1 < n_cols ? (uint16_t)xg[k + 1] : 0u;
+            xw[h] = lo | (hi << 16);
+        }
+    }
+}
+
+// x block b of fp16 values as 16 packed half2, zero past n_cols.
+__device__ __forceinline__ void load_h16(const __half *xh, int n_cols, int b, uint32_t (&hw)[16])
+{
+    if (32 * (b + 1) <= n_cols && (((uintptr_t)(xh + 32 * b)) & 15) == 0) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint4 t = src[q];
+            hw[4 * q] = t.x; hw[4 * q + 1] = t.y; hw[4 * q + 2] = t.z; hw[4 * q + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 16; h++) {
+            const int k = 32 * b + 2 * h;
+            const uint32_t lo = k < n_cols ? __half_as_ushort(xh[k]) : 0u;
+            const uint32_t hi = k + 1 < n_cols ? __half_as_ushort(xh[k + 1]) : 0u;
+            hw[h] = lo | (hi << 16);
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t to_i16(float f, int e)
+{
+    return (uint32_t)(uint16_t)(int16_t)fminf(fmaxf(rintf(ldexpf(f, e)), -32768.f), 32767.f);
 }
 
 template <int KIND>
@@ -554,27 +600,17 @@ __device__ __forceinline__ void stage_x_v3(const DevJob &J, uint4 *planes, int4 
 {
     const int ngr = (nb + 3) >> 2;                 // groups covering nb
     if (KIND == KIND_G128) {
+        // fp16 x -> int16 on a per-128-column exponent e_g: xi = sat16(rint(x * 2^e_g))
+        // with |x * 2^e_g| < 2^15; the factor 2^-e_g goes with the group's scale.
+        // Pass 1: max |x| per 32-block; pass 2: convert per group (re-read, L1/L2).
         const __half *xh = reinterpret_cast<const __half *>(J.x);
-        const bool vec = ((((uintptr_t)xh) & 15) == 0);
         for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
-            float am = 0.f;
-            if (vec && 32 * (b + 1) <= J.n_cols) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
+            uint32_t hw[16];
+            load_h16(xh, J.n_cols, b, hw);
+            uint32_t m = 0;
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const uint4 t = src[q];
-                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&tw[h]));
-                        am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
-                    }
-                }
-            } else {
-                for (int j = 0; j < 32; j++)
-                    if (32 * b + j < J.n_cols) am = fmaxf(am, fabsf(__half2float(xh[32 * b + j])));
-            }
-            bam[b] = am;
+            for (int h = 0; h < 16; h++) m = max(m, max(hw[h] & 0x7FFFu, (hw[h] >> 16) & 0x7FFFu));
+            bam[b] = __half2float(__ushort_as_half((uint16_t)m));   // |fp16| orders like its bits
         }
         __syncthreads();
         for (int b = threadIdx.x; b < nb; b += MV_THREADS) {
@@ -582,51 +618,22 @@ __device__ __forceinline__ void stage_x_v3(const DevJob &J, uint4 *planes, int4 
             const float am = fmaxf(fmaxf(bam[4 * g], bam[4 * g + 1]), fmaxf(bam[4 * g + 2], bam[4 * g + 3]));
             int e = 0;
             if (am > 0.f) { int ex; frexpf(am, &ex); e = 15 - ex; }   // am in [2^(ex-1), 2^ex)
-            int16_t v[32];
-            if (vec && 32 * (b + 1) <= J.n_cols) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(xh + 32 * b);
+            uint32_t hw[16], xw[16];
+            load_h16(xh, J.n_cols, b, hw);
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const uint4 t = src[q];
-                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&tw[h]));
-                        v[8 * q + 2 * h]     = (int16_t)fminf(fmaxf(rintf(ldexpf(f.x, e)), -32768.f), 32767.f);
-                        v[8 * q + 2 * h + 1] = (int16_t)fminf(fmaxf(rintf(ldexpf(f.y, e)), -32768.f), 32767.f);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const float f = (32 * b + j < J.n_cols) ? __half2float(xh[32 * b + j]) : 0.f;
-                    v[j] = (int16_t)fminf(fmaxf(rintf(ldexpf(f, e)), -32768.f), 32767.f);
-                }
+            for (int h = 0; h < 16; h++) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hw[h]));
+                xw[h] = to_i16(f.x, e) | (to_i16(f.y, e) << 16);
             }
-            stage_block_v3<KIND_LIN>(planes, sums4, ngp, b, v);
+            stage_block_v3<KIND_LIN>(planes, sums4, ngp, b, xw);
             if ((b & 3) == 0) gfac[g] = ldexpf(1.0f, -e);
         }
     } else {
         const int16_t *xg = reinterpret_cast<const int16_t *>(J.x);
         for (int b = threadIdx.x; b < 4 * ngr; b += MV_THREADS) {
-            int16_t v[32];
-            if (32 * (b + 1) <= J.n_cols && (((uintptr_t)(xg + 32 * b)) & 15) == 0) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(xg + 32 * b);
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const uint4 t = src[q];
-                    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        v[8 * q + 2 * h] = (int16_t)(tw[h] & 0xFFFFu);
-                        v[8 * q + 2 * h + 1] = (int16_t)(tw[h] >> 16);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = (32 * b + j < J.n_cols) ? xg[32 * b + j] : (int16_t)0;
-            }
-            stage_block_v3<KIND>(planes, sums4, ngp, b, v);
+            uint32_t xw[16];
+            load_x16(xg, J.n_cols, b, xw);
+            stage_block_v3<KIND>(planes, sums4, ngp, b, xw);
         }
     }
 }
@@ -724,12 +731,13 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
         float *bam = gfac + ngp;
         uint32_t cbt[4] = {J.cb[0], J.cb[1], J.cb[2], J.cb[3]};
 
+        const int seg = lane / lpr, sl = lane % lpr;   // row segment, lane in segment
+
         __syncthreads();                            // previous job's smem is free
         if (threadIdx.x == 0) { s_amax = 0; s_sat = 0; s_err = 0; }
         stage_x_v3<KIND>(J, planes, sums4, gfac, bam, nb, ngp);
         __syncthreads();
 
-        const int seg = lane / lpr, sl = lane % lpr;   // row segment, lane in segment
         uint32_t amax = 0, nsat = 0;
         bool bad = false;
         for (int tile = t; tile < tj_end; tile++) {
@@ -745,12 +753,13 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
             float facc[RW];
 #pragma unroll
             for (int r = 0; r < RW; r++) { acc[r] = 0; facc[r] = 0.f; }
+            const bool full = rbase + RW <= n_rows;      // no row of this slot is past the end
             for (int g = sl; g < ngr; g += lpr) {
                 // weights: 64 bytes (4 blocks) per row
                 uint32_t wv[RW][16];
 #pragma unroll
                 for (int r = 0; r < RW; r++) {
-                    if (rv[r]) {
+                    if (full || rv[r]) {
                         uint32_t h0[8], h1[8];
                         ld_stream32(wrow[r] + 64 * (int64_t)g, h0);
                         ld_stream32(wrow[r] + 64 * (int64_t)g + 32, h1);
@@ -761,21 +770,25 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
                         for (int k = 0; k < 16; k++) wv[r][k] = 0;
                     }
                 }
-                // scales
-                uint16_t sv[RW][4];
+                // scales: packed pairs, block 2p in the low half of sv[r][p]
+                uint32_t sv[RW][2];
 #pragma unroll
                 for (int r = 0; r < RW; r++) {
                     const uint16_t *srow = scp + (int64_t)(rv[r] ? rbase + r : 0) * s_pitch;
                     if (KIND == KIND_G128) {
-                        sv[r][0] = rv[r] ? ld_nc_u16(srow + g) : (uint16_t)0;
+                        sv[r][0] = rv[r] ? ld_nc_u16(srow + g) : 0u;
+                        sv[r][1] = 0;
                     } else if (sc_vec) {
                         const uint2 s4 = rv[r] ? ld_nc_u64(srow + 4 * g) : make_uint2(0, 0);
-                        sv[r][0] = (uint16_t)s4.x; sv[r][1] = (uint16_t)(s4.x >> 16);
-                        sv[r][2] = (uint16_t)s4.y; sv[r][3] = (uint16_t)(s4.y >> 16);
+                        sv[r][0] = s4.x; sv[r][1] = s4.y;
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            sv[r][i] = (rv[r] && 4 * g + i < nb) ? ld_nc_u16(srow + 4 * g + i) : (uint16_t)0;
+                        for (int p2 = 0; p2 < 2; p2++) {
+                            const int b = 4 * g + 2 * p2;
+                            const uint32_t lo = (rv[r] && b < nb) ? ld_nc_u16(srow + b) : 0u;
+                            const uint32_t hi = (rv[r] && b + 1 < nb) ? ld_nc_u16(srow + b + 1) : 0u;
+                            sv[r][p2] = lo | (hi << 16);
+                        }
                     }
                 }
                 const int4 sx4 = sums4[g];
@@ -799,10 +812,19 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
 #pragma unroll
                     for (int r = 0; r < RW; r++) {
                         const int32_t part = combine_v3<KIND_LIN>(a[r], sxg);
-                        const float s = __half2float(__ushort_as_half(sv[r][0])) * gf;
+                        const float s = __half2float(__ushort_as_half((uint16_t)sv[r][0])) * gf;
                         facc[r] = fmaf((float)part, s, facc[r]);
                     }
                 } else {
+                    // |partial| <= 32*127*32768 < 2^27 holds for every codebook
+                    // without -128 (refused at parse and wrap), so the s28/s29
+                    // bounds of the contract need no check; the uint15 scale does.
+                    int32_t gsum[RW];
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        gsum[r] = 0;
+                        bad |= ((sv[r][0] | sv[r][1]) & 0x80008000u) != 0;
+                    }
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         int a[RW][4];
@@ -818,11 +840,14 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
 #pragma unroll
                         for (int r = 0; r < RW; r++) {
                             const int32_t part = combine_v3<KIND>(a[r], sxv[i]);
-                            const uint32_t sc = sv[r][i];
-                            bad |= (part >= (1 << 27) || part <= -(1 << 27) || sc > 32767u);
-                            acc[r] += floor_shr((int64_t)part * (int64_t)sc, 15);
+                            // site 1: floor(part*sc / 2^15); |result| < 2^27, so the
+                            // low word of the arithmetic 64-bit shift is the value
+                            const uint32_t sc = (sv[r][i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+                            gsum[r] += (int32_t)((int64_t)part * (int64_t)sc >> 15);
                         }
                     }
+#pragma unroll
+                    for (int r = 0; r < RW; r++) acc[r] += gsum[r];     // 4 contribs < 2^29
                 }
             }
             // reduce across the lpr lanes of the segment, epilogue per row
