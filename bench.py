@@ -62,14 +62,15 @@ def peaks():
     return FALLBACK_HBM, "fallback"
 
 
-def profiled_traffic(name):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
+def profiled_traffic(name, key):
+    """dram read+write bytes per launch recorded from an ncu capture summary
+    in profiles/<name> (line '<key>: <bytes> ...')."""
     p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
     for ln in open(p):
-        if ln.startswith("traffic_bytes_per_launch:"):
-            return float(ln.split(":")[1])
+        if ln.startswith(key + ":"):
+            return float(ln.split(":")[1].split()[0])
     return None
 
 
@@ -277,7 +278,7 @@ def run_ours(args, rank, world, local_rank):
 
     peak, peak_kind = peaks()
     achieved = G * G128_BYTES / (ms_step * 1e-3) / 1e9
-    traffic = profiled_traffic("mv4i_g128_stack64.txt")
+    traffic = profiled_traffic("mv4i_g128_stack16.txt", "traffic_bytes_per_launch_stack64") if G == 64 else None
     out = {
         "metric": METRIC,
         "value": round(value, 1),
