@@ -28,6 +28,7 @@
  *   -11      bad argument (NULL pointer, job count, geometry)
  *   -12      tensor-parallel reduction refused: y_exp spread > 17
  *   -13      tensor-parallel reduction refused: out_shift differs between shards
+ *   -14      mv4i_launch_noalloc: more jobs than its fixed counter array holds
  *   -20      CUDA runtime error (mv4i_last_cuda_error() has the code)
  *
  * Streams are passed as void* (a cudaStream_t; NULL = legacy default stream)
@@ -194,6 +195,31 @@ size_t mv4i_scratch_bytes(void);
  * of one launch must have the same kind.  Returns after enqueueing; errors in
  * the data (contract violations) land in each job's status->err. */
 int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, void *stream);
+
+/* Allocation-free form of mv4i_launch: the same jobs, the same results, but
+ * the per-job completion counters (the only device scratch a launch needs)
+ * live in a fixed array compiled into the library -- 16 bytes for each of
+ * MV4I_NOALLOC_MAX_JOBS jobs, 1 KiB on every GPU that loads the library,
+ * held until the process exits -- instead of in caller-provided memory.
+ *
+ * It exists for callers that cannot call cudaMalloc on their decode path: a
+ * serving runtime that has already divided all of HBM between weights, KV
+ * cache and recurrent state (and must not fail or fragment mid-stream), a
+ * loop that cannot afford the device-wide synchronisation cudaMalloc may
+ * imply while other streams are in flight, or a host in another language
+ * that reaches this library through a bare C FFI and owns no device
+ * allocator.  It calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * The first call on a device looks up the array's device address with that
+ * device current (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  Each call clears the counters it uses on `stream`
+ * (cudaMemsetAsync) before its kernel.  All calls on one device share the
+ * array and it keeps the last call's contents, so calls that overlap on the
+ * GPU (other streams, other host threads) race.  More than
+ * MV4I_NOALLOC_MAX_JOBS jobs is refused with -14.  No counterpart in the
+ * reference, whose golden model allocates nothing on the device. */
+#define MV4I_NOALLOC_MAX_JOBS 64
+int mv4i_launch_noalloc(const mv4i_job *jobs, int njobs, void *stream);
 
 /* Host-buffer form of a g128 launch, the end-to-end call: copies count
  * activation vectors h_x[count][K] (fp16) in, runs count jobs over the

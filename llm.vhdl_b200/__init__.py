@@ -103,6 +103,7 @@ EXPORTS = {
                                 C.c_void_p, C.c_void_p]),
     "mv4i_scratch_bytes": (C.c_size_t, []),
     "mv4i_launch": (C.c_int, [C.POINTER(Job), C.c_int, C.c_void_p, C.c_void_p]),
+    "mv4i_launch_noalloc": (C.c_int, [C.POINTER(Job), C.c_int, C.c_void_p]),
     "mv4i_tp_reduce": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mv4i_synth_g128": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_void_p,

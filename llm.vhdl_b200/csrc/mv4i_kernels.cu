@@ -1163,6 +1163,35 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
     return e == cudaSuccess ? 0 : cuda_fail(e);
 }
 
+// --------------------------------------------------- allocation-free launch
+
+// Completion counters for mv4i_launch_noalloc: four 32-bit words per job,
+// zero-initialised at module load, cleared again by every call.  In host
+// code `g_noalloc_scratch` names a host-side stand-in, not device memory; the
+// device address comes from cudaGetSymbolAddress, looked up once per device.
+static __device__ __align__(256) uint32_t g_noalloc_scratch[4 * MV4I_NOALLOC_MAX_JOBS];
+static void *g_noalloc_addr[64];
+
+extern "C" int mv4i_launch_noalloc(const mv4i_job *jobs, int njobs, void *stream)
+{
+    if (!jobs || njobs <= 0) return -11;
+    if (njobs > MV4I_NOALLOC_MAX_JOBS) return -14;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= 64) return -11;
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+        g_noalloc_addr[dev] = p;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    e = cudaMemsetAsync(g_noalloc_addr[dev], 0, sizeof(uint32_t) * 4 * (size_t)njobs, st);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return mv4i_launch(jobs, njobs, g_noalloc_addr[dev], stream);
+}
+
 // ------------------------------------------------ tensor-parallel reduction
 
 // One CTA: n_rows is a hidden size (<= a few 10^4), so a single pass with a
