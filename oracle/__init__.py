@@ -178,3 +178,114 @@ def tp_reduce(parts, y_exps, out_shifts):
     rc = orc().orc_tp_reduce(N, n, arr, _p(ye), _p(os_), _p(out), C.byref(oe), _p(y32),
                              C.byref(sat))
     return rc, out, oe.value, y32, sat.value
+
+
+# ------------------------------------------------------------ DeltaNet (B)
+
+def _gdn_sig():
+    L = orc()
+    if getattr(L, "_gdn_bound", False):
+        return L
+    i32p = C.POINTER(C.c_int)
+    sig = {
+        "orc_fx_init": (None, []),
+        "orc_fx_tables": (None, [C.c_void_p, C.c_void_p, C.c_void_p]),
+        "orc_gdn_scalar": (None, [C.c_int32, C.c_int, C.c_int32, C.c_int, C.c_int32, C.c_int,
+                                  C.c_int32, C.c_int, i32p, i32p, i32p]),
+        "orc_gdn_col_fixed": (C.c_int, [C.c_int, C.c_void_p, i32p, C.c_void_p, C.c_void_p, C.c_int32,
+                                        C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, i32p]),
+        "orc_gdn_step_fixed": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                         C.c_int, C.c_void_p, C.c_void_p]),
+        "orc_gdn_head_emit": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+        "orc_gdn_cfg1_f64": (None, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                    C.c_double, C.c_void_p]),
+        "orc_gdn_cfg1_f32": (None, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                    C.c_float, C.c_void_p, C.c_int]),
+    }
+    for n, (res, args) in sig.items():
+        f = getattr(L, n)
+        f.restype, f.argtypes = res, args
+    L._gdn_bound = True
+    return L
+
+
+def gdn_scalar(al_m, al_e, dt_m, dt_e, a_m, a_e, b_m, b_e):
+    L = _gdn_sig()
+    eg, be, err = C.c_int(0), C.c_int(0), C.c_int(0)
+    L.orc_gdn_scalar(al_m, al_e, dt_m, dt_e, a_m, a_e, b_m, b_e, C.byref(eg), C.byref(be), C.byref(err))
+    return eg.value, be.value, err.value
+
+
+def gdn_col_fixed(smant, se_j, kn, qs, v, e_v, eg, beta, tk0):
+    """One column of the fixed recurrence; returns (snew, se_new, o_acc, e_o, err)."""
+    L = _gdn_sig()
+    s = np.ascontiguousarray(smant, np.int16).copy()
+    kn = np.ascontiguousarray(kn, np.int16)
+    qs = np.ascontiguousarray(qs, np.int16)
+    se = C.c_int(int(se_j))
+    oacc = np.zeros(1, np.int64)
+    eo = C.c_int(0)
+    err = L.orc_gdn_col_fixed(s.size, _p(s), C.byref(se), _p(kn), _p(qs), int(v), int(e_v), int(eg),
+                              int(beta), int(tk0), _p(oacc), C.byref(eo))
+    return s, se.value, int(oacc[0]), eo.value, err
+
+
+def gdn_step_fixed(smem, se, kn, qs, v, e_v, eg, beta, tk0):
+    """All heads; smem [H][D][D] int16 and se [H][D] int32 are updated in place."""
+    L = _gdn_sig()
+    H, D = smem.shape[0], smem.shape[2]
+    KH = kn.shape[0]
+    o = np.zeros((H, D), np.int64)
+    eo = np.zeros((H, D), np.int32)
+    eg = np.ascontiguousarray(eg, np.int32)
+    beta = np.ascontiguousarray(beta, np.int32)
+    v = np.ascontiguousarray(v, np.int32)
+    err = L.orc_gdn_step_fixed(H, KH, D, _p(smem), _p(se), _p(np.ascontiguousarray(kn, np.int16)),
+                               _p(np.ascontiguousarray(qs, np.int16)), _p(v), int(e_v), _p(eg), _p(beta),
+                               int(tk0), _p(o), _p(eo))
+    return o, eo, err
+
+
+def gdn_head_emit(o_acc, e_o):
+    L = _gdn_sig()
+    o_acc = np.ascontiguousarray(o_acc, np.int64)
+    e_o = np.ascontiguousarray(e_o, np.int32)
+    out = np.zeros(o_acc.size, np.int16)
+    e = L.orc_gdn_head_emit(o_acc.size, _p(o_acc), _p(e_o), _p(out))
+    return out, e
+
+
+def gdn_cfg1_f64(S, q, k, v, a, b, g, l2=True, q_scale=1.0):
+    """Config-1 steps in double.  S [H][D][D] (float64, updated in place);
+    q, k, v, g [T][H][D]; a, b [T][H].  Returns out [T][H][D]."""
+    L = _gdn_sig()
+    T, H, D = q.shape
+    arrs = [np.ascontiguousarray(x, np.float64) for x in (q, k, v, a, b, g)]
+    out = np.zeros((T, H, D), np.float64)
+    L.orc_gdn_cfg1_f64(T, H, D, _p(S), *[_p(x) for x in arrs], int(l2), float(q_scale), _p(out))
+    return out
+
+
+def gdn_cfg1_f32(S, q, k, v, a, b, g, l2=True, q_scale=1.0, threads=1):
+    L = _gdn_sig()
+    T, H, D = q.shape
+    arrs = [np.ascontiguousarray(x, np.float32) for x in (q, k, v, a, b, g)]
+    out = np.zeros((T, H, D), np.float32)
+    L.orc_gdn_cfg1_f32(T, H, D, _p(S), *[_p(x) for x in arrs], int(l2), float(q_scale), _p(out), int(threads))
+    return out
+
+
+def have_gdn_ref():
+    return os.path.exists(os.path.join(HERE, "_ref", "libref_gdn.so"))
+
+
+def ref_gdn():
+    L = C.CDLL(os.path.join(HERE, "_ref", "libref_gdn.so"))
+    i32p = C.POINTER(C.c_int)
+    L.ref_gdn_scalar.argtypes = [C.c_int32, C.c_int, C.c_int32, C.c_int, C.c_int32, C.c_int,
+                                 C.c_int32, C.c_int, i32p, i32p, i32p]
+    L.ref_fx_tables.argtypes = [C.c_void_p] * 3
+    return L
