@@ -21,7 +21,7 @@ LIBDIR = os.path.join(HERE, "lib")
 LIBPATH = os.path.join(LIBDIR, "libmv4i_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["csrc/mv4i_kernels.cu", "csrc/mv4i_host.c"]
+SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]
 
 MODE_BFP, MODE_RAW, MODE_PARTIAL = 0, 1, 2
 KIND_GOLDEN, KIND_G128 = 0, 1
@@ -76,6 +76,21 @@ class Status(C.Structure):
                 ("sat_count", C.c_uint32), ("err", C.c_int32), ("pad", C.c_int32 * 3)]
 
 
+class GdnFixed(C.Structure):
+    _fields_ = [("H", C.c_int32), ("KH", C.c_int32), ("D", C.c_int32), ("smem", C.c_void_p),
+                ("semem", C.c_void_p), ("kn", C.c_void_p), ("qs", C.c_void_p), ("v", C.c_void_p),
+                ("e_v", C.c_int32), ("eg", C.c_void_p), ("beta", C.c_void_p), ("tk0", C.c_int32),
+                ("o_acc", C.c_void_p), ("e_o", C.c_void_p), ("o_head", C.c_void_p),
+                ("e_head", C.c_void_p), ("err", C.c_void_p)]
+
+
+class GdnF32(C.Structure):
+    _fields_ = [("T", C.c_int32), ("H", C.c_int32), ("KH", C.c_int32), ("D", C.c_int32),
+                ("S", C.c_void_p), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
+                ("g", C.c_void_p), ("a", C.c_void_p), ("b", C.c_void_p), ("l2norm", C.c_int32),
+                ("q_scale", C.c_float), ("out_f32", C.c_void_p), ("out_f16", C.c_void_p)]
+
+
 class Job(C.Structure):
     _fields_ = [("w", C.POINTER(DMat)), ("x", C.c_void_p), ("d_x_exp", C.c_void_p),
                 ("x_exp", C.c_int32), ("n_rows", C.c_int32), ("n_cols", C.c_int32),
@@ -110,6 +125,9 @@ EXPORTS = {
                                   C.c_void_p, C.c_void_p, C.c_void_p]),
     "mv4i_g128_matvec_host": (C.c_int, [C.POINTER(DMat), C.c_int, C.c_void_p, C.c_void_p,
                                         C.c_void_p]),
+    "gdn_scalar_dev": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "gdn_step_fixed": (C.c_int, [C.POINTER(GdnFixed), C.c_void_p]),
+    "gdn_run_f32": (C.c_int, [C.POINTER(GdnF32), C.c_void_p]),
     "mv4i_last_cuda_error": (C.c_int, []),
     "mv4i_version": (C.c_char_p, []),
 }

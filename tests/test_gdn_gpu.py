@@ -1,0 +1,194 @@
+"""GPU parity of the Gated DeltaNet step (subsystem B) through the C ABI.
+
+Fixed point (scalar path, recurrence, head emit): BIT-EXACT against the
+reference's vector files (tests/golden/gdn_golden.npz) and against the oracle
+restatement over whole multi-step runs.  Binary32 (config 1): against the
+double oracle with the tolerance written in each test.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+D = 128
+
+
+@pytest.fixture(scope="module")
+def gg():
+    return np.load(os.path.join(os.path.dirname(__file__), "golden", "gdn_golden.npz"))
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+@pytest.mark.parametrize("which", ["sim", "regen"])
+def test_scalar_path_vectors(cuda, pkg, gg, which):
+    torch = cuda
+    ins = torch.from_numpy(gg["gsc_%s_in" % which].copy()).cuda()
+    H = ins.shape[0]
+    eg = torch.zeros(H, dtype=torch.int32, device="cuda")
+    be = torch.zeros(H, dtype=torch.int32, device="cuda")
+    er = torch.zeros(H, dtype=torch.int32, device="cuda")
+    assert pkg.lib().gdn_scalar_dev(H, _p(ins), _p(eg), _p(be), _p(er), None) == 0
+    got = torch.stack([eg, be, er], 1).cpu().numpy()
+    assert np.array_equal(got, gg["gsc_%s_out" % which])
+
+
+def _fixed_run(torch, pkg, smem, se, kn, qs, v, e_v, eg, beta, tk0):
+    H, KH = smem.shape[0], kn.shape[0]
+    t = {n: torch.from_numpy(np.ascontiguousarray(a)).cuda() for n, a in
+         dict(smem=smem, se=se.astype(np.int32), kn=kn, qs=qs, v=v.astype(np.int32),
+              eg=np.asarray(eg, np.int32), beta=np.asarray(beta, np.int32)).items()}
+    oacc = torch.zeros((H, D), dtype=torch.int64, device="cuda")
+    eo = torch.zeros((H, D), dtype=torch.int32, device="cuda")
+    oh = torch.zeros((H, D), dtype=torch.int16, device="cuda")
+    eh = torch.zeros(H, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = pkg.GdnFixed(H, KH, D, t["smem"].data_ptr(), t["se"].data_ptr(), t["kn"].data_ptr(),
+                     t["qs"].data_ptr(), t["v"].data_ptr(), int(e_v), t["eg"].data_ptr(),
+                     t["beta"].data_ptr(), int(tk0), oacc.data_ptr(), eo.data_ptr(), oh.data_ptr(),
+                     eh.data_ptr(), err.data_ptr())
+    assert pkg.lib().gdn_step_fixed(C.byref(a), None) == 0
+    torch.cuda.synchronize()
+    return (t["smem"].cpu().numpy(), t["se"].cpu().numpy(), oacc.cpu().numpy(), eo.cpu().numpy(),
+            oh.cpu().numpy(), eh.cpu().numpy(), int(err.item()))
+
+
+@pytest.mark.parametrize("which", ["sim", "regen"])
+def test_recurrence_vectors(cuda, pkg, gg, which):
+    """Every column of the reference's vector file (each its own head, its
+    state replicated over the head's 128 columns)."""
+    torch = cuda
+    p = "grc_%s_" % which
+    meta = gg[p + "meta"]
+    for c in range(meta.shape[0]):
+        phys, tk0, se_j, e_v, eg, beta, v_j, gid = [int(x) for x in meta[c]]
+        smem = np.broadcast_to(gg[p + "smant"][c], (1, D, D)).copy()
+        se = np.full((1, D), se_j, np.int32)
+        v = np.full((1, D), v_j, np.int32)
+        s2, se2, oacc, eo, oh, eh, err = _fixed_run(torch, pkg, smem, se, gg[p + "kn"][c][None],
+                                                    gg[p + "qs"][c][None], v, e_v, [eg], [beta], tk0)
+        want = gg[p + "out"][c]
+        assert np.array_equal(s2[0, 0], gg[p + "snew"][c]), (which, c)
+        assert (int(se2[0, 0]), int(oacc[0, 0]), int(eo[0, 0]), err) == tuple(int(x) for x in want), (which, c)
+
+
+@pytest.mark.parametrize("H,KH", [(16, 16), (32, 16), (8, 4)])
+def test_fixed_multistep_vs_oracle(cuda, pkg, H, KH):
+    """Eight sequential tokens (the first with tk0), random per-token eg/beta
+    through the scalar path, state carried on the device; recurrence outputs,
+    state, head emit bit-exact against the oracle."""
+    torch = cuda
+    rng = np.random.default_rng(H * 10 + KH)
+    smem = rng.integers(-20000, 20000, (H, D, D)).astype(np.int16)
+    se = rng.integers(-10, 10, (H, D)).astype(np.int32)
+    smem_o, se_o = smem.copy(), se.copy()
+    dsm = torch.from_numpy(smem).cuda()
+    dse = torch.from_numpy(se).cuda()
+    L = pkg.lib()
+    for tok in range(8):
+        kd = rng.normal(size=(KH, D)); kd /= np.linalg.norm(kd, axis=1, keepdims=True)
+        qd = rng.normal(size=(KH, D)); qd /= np.linalg.norm(qd, axis=1, keepdims=True) * np.sqrt(D)
+        kn = np.clip(np.rint(kd * 32768), -32768, 32767).astype(np.int16)
+        qs = np.clip(np.rint(qd * 262144), -32768, 32767).astype(np.int16)
+        v = rng.integers(-32768, 32767, (H, D)).astype(np.int32)
+        e_v = int(rng.integers(-5, 20))
+        sc = np.stack([rng.integers(-1000, 1000, H), np.full(H, 14), -rng.integers(2000, 30000, H),
+                       np.full(H, 12), -rng.integers(1, 3000, H), np.full(H, 16),
+                       rng.integers(-30000, 30000, H), np.full(H, 12)], 1).astype(np.int32)
+        egs = [O.gdn_scalar(*[int(x) for x in row]) for row in sc]
+        eg = np.array([e[0] for e in egs], np.int32)
+        be = np.array([e[1] for e in egs], np.int32)
+        dsc = torch.from_numpy(sc).cuda()
+        deg = torch.zeros(H, dtype=torch.int32, device="cuda")
+        dbe = torch.zeros(H, dtype=torch.int32, device="cuda")
+        assert L.gdn_scalar_dev(H, _p(dsc), _p(deg), _p(dbe), None, None) == 0
+        assert np.array_equal(deg.cpu().numpy(), eg) and np.array_equal(dbe.cpu().numpy(), be)
+        tk0 = int(tok == 0)
+        oacc_o, eo_o, err_o = O.gdn_step_fixed(smem_o, se_o, kn, qs, v, e_v, eg, be, tk0)
+        t = {n: torch.from_numpy(np.ascontiguousarray(a)).cuda() for n, a in dict(kn=kn, qs=qs, v=v).items()}
+        oacc = torch.zeros((H, D), dtype=torch.int64, device="cuda")
+        eo = torch.zeros((H, D), dtype=torch.int32, device="cuda")
+        oh = torch.zeros((H, D), dtype=torch.int16, device="cuda")
+        eh = torch.zeros(H, dtype=torch.int32, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        a = pkg.GdnFixed(H, KH, D, dsm.data_ptr(), dse.data_ptr(), t["kn"].data_ptr(), t["qs"].data_ptr(),
+                         t["v"].data_ptr(), e_v, deg.data_ptr(), dbe.data_ptr(), tk0, oacc.data_ptr(),
+                         eo.data_ptr(), oh.data_ptr(), eh.data_ptr(), err.data_ptr())
+        assert L.gdn_step_fixed(C.byref(a), None) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(dsm.cpu().numpy(), smem_o), tok
+        assert np.array_equal(dse.cpu().numpy(), se_o), tok
+        assert np.array_equal(oacc.cpu().numpy(), oacc_o), tok
+        assert np.array_equal(eo.cpu().numpy(), eo_o), tok
+        assert int(err.item()) == err_o
+        for h in range(H):
+            o_head, e_head = O.gdn_head_emit(oacc_o[h], eo_o[h])
+            assert np.array_equal(oh[h].cpu().numpy(), o_head) and int(eh[h].item()) == e_head, (tok, h)
+
+
+def _cfg1_inputs(rng, T, H, D=128):
+    q = rng.normal(size=(T, H, D)).astype(np.float16)
+    k = rng.normal(size=(T, H, D)).astype(np.float16)
+    v = rng.normal(size=(T, H, D)).astype(np.float16)
+    g = rng.normal(size=(T, H, D)).astype(np.float16)
+    a = rng.normal(size=(T, H)).astype(np.float32)
+    b = rng.normal(size=(T, H)).astype(np.float32)
+    S0 = rng.normal(0, 0.02, (H, D, D)).astype(np.float32)
+    return S0, q, k, v, g, a, b
+
+
+def _run_f32(torch, pkg, S, q, k, v, g, a, b, l2=1, q_scale=1.0):
+    T, H, _ = q.shape
+    t = {n: torch.from_numpy(np.ascontiguousarray(x)).cuda() for n, x in
+         dict(q=q, k=k, v=v, g=g, a=a, b=b).items()}
+    out = torch.zeros((T, H, D), dtype=torch.float32, device="cuda")
+    out16 = torch.zeros((T, H, D), dtype=torch.float16, device="cuda")
+    args = pkg.GdnF32(T, H, H, D, S.data_ptr(), t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(),
+                      t["g"].data_ptr(), t["a"].data_ptr(), t["b"].data_ptr(), l2, q_scale,
+                      out.data_ptr(), out16.data_ptr())
+    assert pkg.lib().gdn_run_f32(C.byref(args), None) == 0
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), out16.cpu().numpy()
+
+
+def test_f32_config1_256_steps_vs_double(cuda, pkg):
+    """Config 1: 16 heads, d 128, 256 steps from seed 1, state fp32 N(0, 0.02).
+    Tolerance: per step max|out - ref| <= 1e-4 * max|ref| (fp32 state);
+    fp16 output within 1e-3 * max|ref|; final state within 1e-4 * max|S|."""
+    torch = cuda
+    rng = np.random.default_rng(1)
+    T, H = 256, 16
+    S0, q, k, v, g, a, b = _cfg1_inputs(rng, T, H)
+    S = torch.from_numpy(S0.copy()).cuda()
+    out, out16 = _run_f32(torch, pkg, S, q, k, v, g, a, b)
+    S64 = S0.astype(np.float64)
+    ref = O.gdn_cfg1_f64(S64, q.astype(np.float64), k.astype(np.float64), v.astype(np.float64),
+                         a.astype(np.float64), b.astype(np.float64), g.astype(np.float64))
+    for t in range(T):
+        m = np.abs(ref[t]).max()
+        assert np.abs(out[t] - ref[t]).max() <= 1e-4 * m, t
+        assert np.abs(out16[t].astype(np.float64) - ref[t]).max() <= 1e-3 * m, t
+    Sd = S.cpu().numpy()
+    assert np.abs(Sd - S64).max() <= 1e-4 * np.abs(S64).max()
+
+
+def test_f32_single_steps_equal_one_run(cuda, pkg):
+    """T launches of one step (state through HBM) give exactly the state and
+    outputs of one T-step launch."""
+    torch = cuda
+    rng = np.random.default_rng(3)
+    T, H = 16, 8
+    S0, q, k, v, g, a, b = _cfg1_inputs(rng, T, H)
+    S1 = torch.from_numpy(S0.copy()).cuda()
+    run, _ = _run_f32(torch, pkg, S1, q, k, v, g, a, b)
+    S2 = torch.from_numpy(S0.copy()).cuda()
+    for t in range(T):
+        o, _ = _run_f32(torch, pkg, S2, q[t:t + 1], k[t:t + 1], v[t:t + 1], g[t:t + 1], a[t:t + 1], b[t:t + 1])
+        assert np.array_equal(o[0], run[t]), t
+    assert torch.equal(S1, S2)
