@@ -276,6 +276,8 @@ def run_ours(args, rank, world, local_rank):
     e2e_value = world * G * G128_BYTES / (ems * 1e-3) / 1e9
     assert torch.equal(hy.to(dev), y16), "host-buffer result differs from the device launch"
 
+    gdn = run_gdn(args, pkg, L, torch, dev, stream, sp, timed)
+
     peak, peak_kind = peaks()
     achieved = G * G128_BYTES / (ms_step * 1e-3) / 1e9
     traffic = profiled_traffic("mv4i_g128_stack16.txt", "traffic_bytes_per_launch_stack64") if G == 64 else None
@@ -309,10 +311,113 @@ def run_ours(args, rank, world, local_rank):
         "single": {"us_per_matvec": round(sms * 1e3, 2),
                    "GBps": round(G128_BYTES / (sms * 1e-3) / 1e9, 1),
                    "how": "64 one-job launches in a CUDA graph, rotating over the stack"},
+        "gdn": gdn,
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
     return out
+
+
+# ------------------------------------------------------------ config 1
+
+GDN_H, GDN_D, GDN_T = 16, 128, 256
+# per step, state in HBM: S read + written (2 x 1 MiB fp32), q, k, v (fp16),
+# a, b (fp32), gate (fp16), out (fp16)
+GDN_STEP_BYTES = 2 * GDN_H * GDN_D * GDN_D * 4 + 3 * GDN_H * GDN_D * 2 + 2 * GDN_H * 4 \
+    + GDN_H * GDN_D * 2 + GDN_H * GDN_D * 2
+
+
+def gdn_inputs(seed=1):
+    """Config 1: q, k, v, g fp16 ~ N(0,1); a, b ~ N(0,1); S0 ~ N(0, 0.02)."""
+    import numpy as np
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("synth", os.path.join(ROOT, "llm.vhdl_b200", "synth.py"))
+    S = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(S)
+    n = GDN_T * GDN_H * GDN_D
+    key = 3 * seed
+    q = S.normal_f16(key + 100, n).reshape(GDN_T, GDN_H, GDN_D)
+    k = S.normal_f16(key + 101, n).reshape(GDN_T, GDN_H, GDN_D)
+    v = S.normal_f16(key + 102, n).reshape(GDN_T, GDN_H, GDN_D)
+    g = S.normal_f16(key + 103, n).reshape(GDN_T, GDN_H, GDN_D)
+    a = S.normal_f16(key + 104, GDN_T * GDN_H).astype(np.float32).reshape(GDN_T, GDN_H)
+    b = S.normal_f16(key + 105, GDN_T * GDN_H).astype(np.float32).reshape(GDN_T, GDN_H)
+    s0 = (S.normal_f16(key + 106, GDN_H * GDN_D * GDN_D).astype(np.float32) * 0.02).reshape(GDN_H, GDN_D, GDN_D)
+    return s0, q, k, v, g, a, b
+
+
+def run_gdn(args, pkg, L, torch, dev, stream, sp, timed):
+    """Config 1 two ways: (1) one launch of all 256 steps with the state on
+    chip; (2) one launch per step, the state read and written through HBM
+    each step, 256 launches captured in a CUDA graph (a decode loop)."""
+    s0, q, k, v, g, a, b = gdn_inputs(1)
+    t = {n: torch.from_numpy(x.copy()).to(dev) for n, x in dict(q=q, k=k, v=v, g=g, a=a, b=b).items()}
+    S = torch.from_numpy(s0.copy()).to(dev)
+    out = torch.empty((GDN_T, GDN_H, GDN_D), dtype=torch.float16, device=dev)
+    full = pkg.GdnF32(GDN_T, GDN_H, GDN_H, GDN_D, S.data_ptr(), t["q"].data_ptr(), t["k"].data_ptr(),
+                      t["v"].data_ptr(), t["g"].data_ptr(), t["a"].data_ptr(), t["b"].data_ptr(), 1, 1.0,
+                      None, out.data_ptr())
+
+    def run_all():
+        if L.gdn_run_f32(C.byref(full), sp):
+            raise RuntimeError("gdn_run_f32 failed")
+    for _ in range(3):
+        run_all()
+    nrep = max(3, args.steps // 50)
+    ms_all = timed(run_all, nrep) / nrep
+
+    steps = []
+    for i in range(GDN_T):
+        steps.append(pkg.GdnF32(1, GDN_H, GDN_H, GDN_D, S.data_ptr(), t["q"][i].data_ptr(),
+                                t["k"][i].data_ptr(), t["v"][i].data_ptr(), t["g"][i].data_ptr(),
+                                t["a"][i].data_ptr(), t["b"][i].data_ptr(), 1, 1.0, None,
+                                out[i].data_ptr()))
+
+    def run_steps():
+        for st in steps:
+            if L.gdn_run_f32(C.byref(st), sp):
+                raise RuntimeError("gdn_run_f32 failed")
+    run_steps()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        run_steps()
+    for _ in range(3):
+        graph.replay()
+    ms_steps = timed(graph.replay, nrep) / nrep
+    del graph
+    us_step = ms_steps * 1e3 / GDN_T
+    return {
+        "workload": "config 1: 16 heads x 128 x 128 fp32 state, 256 sequential steps, seed 1",
+        "persistent_us_per_step": round(ms_all * 1e3 / GDN_T, 3),
+        "persistent_ms_per_256": round(ms_all, 4),
+        "per_step_us": round(us_step, 3),
+        "per_step_GBps": round(GDN_STEP_BYTES / (us_step * 1e-6) / 1e9, 1),
+        "per_step_bytes": GDN_STEP_BYTES,
+        "per_step_how": "one launch per step, state through HBM, 256 launches in a CUDA graph",
+        "kernel": "gdn_f32_kernel",
+    }
+
+
+def gdn_cpu_baseline(budget_s=3.0):
+    """The reference's binary32 recurrence (restated in oracle/gdn_oracle.c,
+    heads over pthreads as ref/gdn_err.c:447-449 does with OpenMP)."""
+    import numpy as np
+    import oracle as O
+    from oracle import cpu_baseline as CB
+    s0, q, k, v, g, a, b = gdn_inputs(1)
+    P = CB.cores()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        S = s0.copy()
+        O.gdn_cfg1_f32(S, q, k, v, a, b, g.astype(np.float32), threads=P)
+        n += 1
+        el = time.perf_counter() - t0
+        if el > budget_s and n >= 1:
+            break
+    us = el / n / GDN_T * 1e6
+    return {"us_per_step": round(us, 2), "cores": min(P, GDN_H), "kind": "port",
+            "sample": "%d runs of the 256 config-1 steps, heads over %d threads" % (n, min(P, GDN_H))}
 
 
 def main():
@@ -359,11 +464,14 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    cpu = None
+    cpu = gcpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()          # spawn-started workers, before any CUDA work
+        gcpu = gdn_cpu_baseline()
     out = run_ours(args, rank, world, local_rank)
     out["cpu_baseline"] = cpu
+    if gcpu:
+        out["gdn"]["cpu_baseline"] = gcpu
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
