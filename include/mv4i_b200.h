@@ -159,6 +159,13 @@ int mv4i_dmat_wrap_golden(const uint8_t *d_wq, int64_t w_pitch, const uint16_t *
 
 int mv4i_dmat_free(mv4i_dmat *m);
 
+/* A view of rows [row0, row0+n) of a resident matrix (nothing is copied or
+ * allocated; the view does not own memory).  A BFP job on the view is the
+ * reference's row-window A job, ref/run9b.c:455-490 (RAW over the rows, then
+ * the BFP scan over the window only): rows are independent, so computing only
+ * the window's rows gives the same RAW values and the window's own ns. */
+int mv4i_dmat_rows(const mv4i_dmat *m, int row0, int n, mv4i_dmat *view);
+
 /* One matvec job.
  *   golden: x = int16 mantissas (x_exp, or *d_x_exp when non-NULL);
  *           y_data int32 (RAW, BFP), y_mant int16 (BFP), y_acc int64 (PARTIAL)
@@ -254,6 +261,14 @@ int mv4i_tp_reduce(int N, int n_rows, const int64_t *d_parts, const int32_t *d_y
  * with the double-precision rule for fp16 and fp32 inputs. */
 int mv4i_bfp_pack(const void *d_v, int dtype, int n, int count, int64_t stride,
                   int16_t *d_mant, int32_t *d_exp, void *stream);
+
+/* ------------------------------------------------------------- argmax */
+
+/* Replaces argmax_first (ref/run9b.c:399-405): index of the largest of n
+ * values, the FIRST one on ties.  dtype 0 = int32 (golden RAW logits on one
+ * grid), 1 = fp32, 2 = fp16.  d_work is 8 bytes of device scratch; *d_idx
+ * receives the index.  Two kernels on `stream`. */
+int mv4i_argmax(const void *d_v, int dtype, int n, uint64_t *d_work, int32_t *d_idx, void *stream);
 
 /* ----------------------------------------------------------- utilities */
 

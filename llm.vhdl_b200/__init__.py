@@ -114,6 +114,8 @@ EXPORTS = {
                                         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
                                         C.POINTER(DMat)]),
     "mv4i_dmat_free": (C.c_int, [C.POINTER(DMat)]),
+    "mv4i_dmat_rows": (C.c_int, [C.POINTER(DMat), C.c_int, C.c_int, C.POINTER(DMat)]),
+    "mv4i_argmax": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mv4i_bfp_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int64, C.c_void_p,
                                 C.c_void_p, C.c_void_p]),
     "mv4i_scratch_bytes": (C.c_size_t, []),

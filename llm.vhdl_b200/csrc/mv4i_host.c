@@ -208,6 +208,17 @@ int mv4i_dmat_wrap_golden(const uint8_t *d_wq, int64_t w_pitch, const uint16_t *
     return 0;
 }
 
+int mv4i_dmat_rows(const mv4i_dmat *m, int row0, int n, mv4i_dmat *view)
+{
+    if (!m || !view || row0 < 0 || n <= 0 || row0 + n > m->M) return -11;
+    *view = *m;
+    view->wq = m->wq + (int64_t)row0 * m->w_pitch;
+    view->sc = (const uint8_t *)m->sc + (int64_t)row0 * m->s_pitch * 2;
+    view->M = n;
+    view->owned = NULL;
+    return 0;
+}
+
 int mv4i_dmat_free(mv4i_dmat *m)
 {
     if (!m) return -11;

@@ -1313,6 +1313,58 @@ extern "C" int mv4i_bfp_pack(const void *d_v, int dtype, int n, int count, int64
     return e == cudaSuccess ? 0 : cuda_fail(e);
 }
 
+// --------------------------------------------------------------- argmax
+
+// Order-preserving 32-bit key of a value; the index goes in the low word,
+// complemented, so that the 64-bit maximum picks the first index on ties.
+__device__ __forceinline__ uint32_t okey_i32(int32_t v) { return (uint32_t)v ^ 0x80000000u; }
+__device__ __forceinline__ uint32_t okey_f32(float f)
+{
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(512)
+argmax_kernel(const void *v, int n, unsigned long long *work)
+{
+    unsigned long long best = 0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        uint32_t k;
+        if (DT == 0) k = okey_i32(reinterpret_cast<const int32_t *>(v)[i]);
+        else if (DT == 1) k = okey_f32(reinterpret_cast<const float *>(v)[i]);
+        else k = okey_f32(__half2float(reinterpret_cast<const __half *>(v)[i]));
+        const unsigned long long key = ((unsigned long long)k << 32) | (0xFFFFFFFFull - (uint32_t)i);
+        best = key > best ? key : best;
+    }
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long w = __shfl_xor_sync(0xffffffffu, best, o);
+        best = w > best ? w : best;
+    }
+    if ((threadIdx.x & 31) == 0) atomicMax(work, best);
+}
+
+__global__ void argmax_finish(const unsigned long long *work, int32_t *idx)
+{
+    *idx = (int32_t)(0xFFFFFFFFull - (*work & 0xFFFFFFFFull));
+}
+
+extern "C" int mv4i_argmax(const void *d_v, int dtype, int n, uint64_t *d_work, int32_t *d_idx, void *stream)
+{
+    if (!d_v || !d_work || !d_idx || n <= 0 || dtype < 0 || dtype > 2) return -11;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(d_work, 0, 8, st);
+    if (e != cudaSuccess) return cuda_fail(e);
+    const int grid = min(296, (n + 511) / 512);
+    unsigned long long *w = reinterpret_cast<unsigned long long *>(d_work);
+    if (dtype == 0) argmax_kernel<0><<<grid, 512, 0, st>>>(d_v, n, w);
+    else if (dtype == 1) argmax_kernel<1><<<grid, 512, 0, st>>>(d_v, n, w);
+    else argmax_kernel<2><<<grid, 512, 0, st>>>(d_v, n, w);
+    argmax_finish<<<1, 1, 0, st>>>(w, d_idx);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}
+
 // ------------------------------------------------------- synthetic inputs
 
 __device__ __forceinline__ uint64_t mix64(uint64_t z)

@@ -289,3 +289,26 @@ def ref_gdn():
                                  C.c_int32, C.c_int, i32p, i32p, i32p]
     L.ref_fx_tables.argtypes = [C.c_void_p] * 3
     return L
+
+
+def a_job(img, x, x_exp, K, row0, n):
+    """ref/run9b.c:455-490 restated: (y_mant[n], y_exp)."""
+    L = orc()
+    if not getattr(L, "_ajob", False):
+        L.orc_a_job.restype = C.c_int
+        L.orc_a_job.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                C.c_void_p, C.POINTER(C.c_int)]
+        L._ajob = True
+    buf = np.frombuffer(img, np.uint8).copy()
+    x = np.ascontiguousarray(x, np.int16)
+    y = np.zeros(n, np.int16)
+    e = C.c_int(0)
+    rc = L.orc_a_job(_p(buf), buf.size, _p(x), x_exp, K, row0, n, _p(y), C.byref(e))
+    assert rc == 0, rc
+    return y, e.value
+
+
+def argmax_first(v):
+    """ref/run9b.c:399-405: the first maximum wins."""
+    v = np.asarray(v)
+    return int(np.flatnonzero(v == v.max())[0])
