@@ -69,8 +69,9 @@ def main():
                                             list(osh.cpu().numpy()))
     assert prc == 0 and int(status[4].item()) == 0
     assert np.array_equal(out.cpu().numpy(), oout) and int(status[0].item()) == oexp
-    allo = [torch.empty_like(out) for _ in range(world)]
-    dist.all_gather(allo, out)
+    out32 = out.to(torch.int32)                     # NCCL has no int16
+    allo = [torch.empty_like(out32) for _ in range(world)]
+    dist.all_gather(allo, out32)
     assert all(torch.equal(allo[0], a) for a in allo)
 
     # ---- g128 row-parallel: fp32 partials + all-reduce
