@@ -1,0 +1,98 @@
+/* include/dec_b200.h -- C ABI of the decode loop built on the hot path: a
+ * Qwen3.5-style hybrid decoder (Gated DeltaNet and gated-attention layers,
+ * SwiGLU MLP, INT4 g128 linears, LM head + first-max argmax) stepping one
+ * token per call, on one GPU or tensor-parallel over several (one process per
+ * GPU, NCCL).  It composes the matvec (mv4i_b200.h) and DeltaNet step
+ * (gdn_b200.h) kernels the way ref/run9b.c composes mv4i_matvec and its
+ * delta rule: layer_gdn (ref/run9b.c:602-756), layer_attn (:758-900),
+ * lm_head + argmax_first (:399-405, :522-540).  The arithmetic is the
+ * benchmark's floating-point mode (fp16 activations into INT4 g128
+ * projections, fp32 residual stream, recurrent state and accumulation); the
+ * bit-exact integer mode of the golden model is the matvec library's.
+ *
+ * The position and the current token live in device memory, so one step can
+ * be captured in a CUDA graph and replayed for every token.
+ */
+#ifndef DEC_B200_H
+#define DEC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int32_t hidden;          /* residual width                                */
+    int32_t n_layers;
+    int32_t attn_every;      /* layer il is attention when (il+1) % attn_every == 0
+                                (ref/run9b.c is_attn)                          */
+    int32_t vocab;
+    int32_t ffn;             /* SwiGLU intermediate                           */
+    int32_t gdn_kh, gdn_vh, gdn_hd;      /* DeltaNet key heads, value heads, dim */
+    int32_t att_qh, att_kvh, att_hd;     /* attention heads and dim             */
+    int32_t n_rot;           /* rotary dims per head (NeoX pairing i, i+n_rot/2) */
+    float   rope_theta;
+    float   rms_eps;
+    int32_t max_ctx;         /* KV-cache capacity in positions               */
+} dec_config;
+
+typedef struct dec_model dec_model;
+
+/* Random-init weights of the configured architecture (seeded splitmix64,
+ * INT4 g128 linears as in the benchmark's config 0), on `device`; tp_world
+ * ranks each hold their shard (tp_world = 1: everything).  Shards: heads for
+ * DeltaNet and attention, rows for column-parallel projections (qkv, z, a/b,
+ * q|gate, k|v, gate, up) and the LM head's vocabulary, columns for the
+ * row-parallel ones (DeltaNet out, attention O, FFN down).  Every rank draws
+ * its shard from the same global matrices (draws are keyed by global row and
+ * column), so any tp_world computes the same model. */
+int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, int tp_world,
+               dec_model **out);
+int dec_destroy(dec_model *m);
+
+/* NCCL for tp_world > 1: rank 0 calls dec_nccl_unique_id, the caller ships
+ * the 128 bytes to every rank (any transport), and every rank calls
+ * dec_tp_init before its first step. */
+int dec_nccl_unique_id(uint8_t id[128]);
+int dec_tp_init(dec_model *m, const uint8_t id[128]);
+
+/* Fills the first `len` positions of every attention layer's KV cache with
+ * N(0,1) fp16 (the benchmark's pre-filled context), the DeltaNet states with
+ * N(0, 0.02) and the conv states with N(0, 0.5), and sets the position to len. */
+int dec_prefill_random(dec_model *m, int len, uint64_t seed);
+
+/* Sets the position and the current input token (host values). */
+int dec_set(dec_model *m, int pos, int token);
+
+/* One decode step on `stream`: embeds the current token, runs every layer,
+ * the LM head and argmax; the argmax becomes the current token and is stored
+ * in the token history at the current position; the position advances.  No
+ * host synchronisation. */
+int dec_step(dec_model *m, void *stream);
+
+/* Device pointers for inspection: the fp32 logits of the last step (this
+ * rank's vocabulary shard), the token history [max_ctx], the fp32 residual
+ * [hidden], the position. */
+int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residual, int32_t **pos,
+                 int32_t *vocab0, int32_t *vocab_n);
+
+/* Weight arrays of one linear, for the oracle: d_wq [rows][cols/2] packed
+ * INT4, d_sc [rows][cols/128] fp16.  Names: "qkv", "z", "ab", "out", "qg",
+ * "kv", "o", "gate", "up", "down" (per layer) and "lm_head" (layer -1). */
+int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, const uint16_t **d_sc,
+               int32_t *rows, int32_t *cols);
+
+/* Parameter and state vectors: "attn_norm", "post_norm", "conv_w"
+ * ([conv_dim][4]), "ssm_a", "dt_bias", "ssm_norm", "q_norm", "k_norm",
+ * "conv_state", "rec_state", "kcache", "vcache" (per layer), "final_norm" and
+ * the fp16 "embed" [vocab][hidden] (layer -1). */
+int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count);
+
+/* Bytes of weights, KV cache and state one step reads on this rank. */
+int64_t dec_step_bytes(dec_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DEC_B200_H */

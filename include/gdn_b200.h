@@ -70,6 +70,10 @@ typedef struct {
     float           q_scale;
     float          *out_f32;
     uint16_t       *out_f16;
+    const float    *eg, *beta;      /* optional [T][H]: the decay and beta
+                                       already activated (the model's
+                                       exp(ssm_a*softplus(.)) and sigmoid);
+                                       when set, a and b are not read      */
 } gdn_f32_args;
 
 int gdn_run_f32(const gdn_f32_args *a, void *stream);

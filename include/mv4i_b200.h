@@ -189,6 +189,9 @@ typedef struct {
     uint16_t        *y_f16;
     float           *y_f32;
     mv4i_status     *status;          /* device; may be NULL for g128        */
+    int32_t          accum;           /* g128: y_f32[row] += result (residual
+                                         add fused into the projection)     */
+    int32_t          pad_;
 } mv4i_job;
 
 #define MV4I_MAX_JOBS 64

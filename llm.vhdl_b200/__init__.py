@@ -22,6 +22,8 @@ LIBPATH = os.path.join(LIBDIR, "libmv4i_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]
+DEC_LIBPATH = os.path.join(LIBDIR, "libdec_b200.so")
+DEC_SOURCES = ["csrc/dec_kernels.cu", "csrc/dec_model.c"]
 
 MODE_BFP, MODE_RAW, MODE_PARTIAL = 0, 1, 2
 KIND_GOLDEN, KIND_G128 = 0, 1
@@ -29,16 +31,23 @@ MAX_JOBS = 64
 
 
 def build(verbose=False):
-    """Compile the CUDA + C sources into lib/libmv4i_b200.so for sm_100a."""
+    """Compile the CUDA + C sources for sm_100a: lib/libmv4i_b200.so (matvec,
+    DeltaNet, drop-in host API) and lib/libdec_b200.so (the decode step,
+    linked against the first and NCCL)."""
     os.makedirs(LIBDIR, exist_ok=True)
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
-           "-shared", "-o", LIBPATH, *[os.path.join(HERE, s) for s in SOURCES],
-           "-lpthread"]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
-    if verbose:
-        print(r.stdout + r.stderr)
+    cmds = [
+        [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
+         "-shared", "-o", LIBPATH, *[os.path.join(HERE, s) for s in SOURCES], "-lpthread"],
+        [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
+         "-shared", "-o", DEC_LIBPATH, *[os.path.join(HERE, s) for s in DEC_SOURCES],
+         "-L" + LIBDIR, "-lmv4i_b200", "-lnccl", "-Xlinker", "-rpath=$ORIGIN"],
+    ]
+    for cmd in cmds:
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
+        if verbose:
+            print(r.stdout + r.stderr)
     return LIBPATH
 
 
@@ -88,7 +97,8 @@ class GdnF32(C.Structure):
     _fields_ = [("T", C.c_int32), ("H", C.c_int32), ("KH", C.c_int32), ("D", C.c_int32),
                 ("S", C.c_void_p), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
                 ("g", C.c_void_p), ("a", C.c_void_p), ("b", C.c_void_p), ("l2norm", C.c_int32),
-                ("q_scale", C.c_float), ("out_f32", C.c_void_p), ("out_f16", C.c_void_p)]
+                ("q_scale", C.c_float), ("out_f32", C.c_void_p), ("out_f16", C.c_void_p),
+                ("eg", C.c_void_p), ("beta", C.c_void_p)]
 
 
 class Job(C.Structure):
@@ -97,7 +107,7 @@ class Job(C.Structure):
                 ("mode", C.c_int32), ("nvec", C.c_int32), ("x_stride", C.c_int64),
                 ("y_stride", C.c_int64), ("y_data", C.c_void_p), ("y_mant", C.c_void_p),
                 ("y_acc", C.c_void_p), ("y_f16", C.c_void_p), ("y_f32", C.c_void_p),
-                ("status", C.c_void_p)]
+                ("status", C.c_void_p), ("accum", C.c_int32), ("pad_", C.c_int32)]
 
 
 EXPORTS = {
@@ -150,6 +160,52 @@ def lib():
             fn.restype, fn.argtypes = res, args
         _lib = L
     return _lib
+
+
+class DecConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("n_layers", C.c_int32), ("attn_every", C.c_int32),
+                ("vocab", C.c_int32), ("ffn", C.c_int32), ("gdn_kh", C.c_int32),
+                ("gdn_vh", C.c_int32), ("gdn_hd", C.c_int32), ("att_qh", C.c_int32),
+                ("att_kvh", C.c_int32), ("att_hd", C.c_int32), ("n_rot", C.c_int32),
+                ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("max_ctx", C.c_int32)]
+
+
+DEC_EXPORTS = {
+    "dec_create": (C.c_int, [C.POINTER(DecConfig), C.c_uint64, C.c_int, C.c_int, C.c_int,
+                             C.POINTER(C.c_void_p)]),
+    "dec_destroy": (C.c_int, [C.c_void_p]),
+    "dec_nccl_unique_id": (C.c_int, [C.c_void_p]),
+    "dec_tp_init": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "dec_prefill_random": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64]),
+    "dec_set": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "dec_step": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "dec_pointers": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                               C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                               C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "dec_linear": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_void_p),
+                             C.POINTER(C.c_void_p), C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "dec_param": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_void_p),
+                            C.POINTER(C.c_int32)]),
+    "dec_step_bytes": (C.c_int64, [C.c_void_p]),
+}
+
+_declib = None
+
+
+def declib():
+    """The decode-step library (include/dec_b200.h).  Raises when it has not
+    been built."""
+    global _declib
+    if _declib is None:
+        lib()
+        if not os.path.exists(DEC_LIBPATH):
+            raise RuntimeError("libdec_b200.so is not built (run __graft_entry__.build())")
+        L = C.CDLL(DEC_LIBPATH)
+        for name, (res, args) in DEC_EXPORTS.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _declib = L
+    return _declib
 
 
 def header_symbols(path=None):

@@ -1,0 +1,486 @@
+/* llm.vhdl_b200/csrc/dec_model.c -- the decode step built on the hot path.
+ *
+ * One token through a Qwen3.5-style hybrid decoder, composed the way
+ * ref/run9b.c composes its A jobs and its delta rule (layer_gdn :602-756,
+ * layer_attn :758-900, lm_head :522-540, argmax_first :399-405), in the
+ * floating-point mode: fp16 activations into INT4 g128 projections
+ * (mv4i_launch job lists), fp32 residual stream, DeltaNet state and
+ * accumulation, fp16 KV cache.  Projections that read the same activation go
+ * in one launch; the residual add of a single-GPU run is fused into the output
+ * projection (accumulate flag).  Tensor parallel: heads and rows are sharded,
+ * the row-parallel outputs are summed with one NCCL all-reduce each, and the
+ * vocabulary-sharded argmax keys are all-gathered.
+ */
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <math.h>
+#include <cuda_runtime_api.h>
+#include <nccl.h>
+#include "../../include/mv4i_b200.h"
+#include "../../include/gdn_b200.h"
+#include "../../include/dec_b200.h"
+
+extern int mv4i_g_cuda_err;
+
+/* kernels in dec_kernels.cu */
+int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s);
+int dec_k_rmsnorm(const float *x, const float *w, int n, float eps, uint16_t *y, void *s);
+int dec_k_gdn_pre(const float *qkv, int conv_dim, const float *conv_w, float *conv_state, uint16_t *qkv16,
+                  const float *ab, int vh, const float *ssm_a, const float *dt_bias, float *eg, float *beta, void *s);
+int dec_k_gated_norm(const float *o, const float *z, const float *w, int heads, int hd, float eps, uint16_t *y, void *s);
+int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
+                   const float *qn_w, const float *kn_w, const int32_t *d_pos, float *q_out, float *gate_out,
+                   uint16_t *kcache, uint16_t *vcache, void *s);
+int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int qh, int kvh, int hd, int ch,
+                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s);
+int dec_k_swiglu(const float *g, const float *u, int n, uint16_t *h, void *s);
+int dec_k_add(float *x, const float *t, int n, void *s);
+int dec_k_argmax(const float *v, int n, int idx0, unsigned long long *key, void *s);
+int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
+                  int32_t *pos, int max_ctx, void *s);
+int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
+                       uint8_t *wq, uint16_t *sc, void *s);
+int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, float mean, float std,
+                    float *f32, uint16_t *f16, void *s);
+
+#define ATT_CHUNK 64
+#define HD 128
+#define MAX_ALLOCS 8192
+#define CK(x) do { int rc_ = (x); if (rc_) return rc_; } while (0)
+
+typedef struct {
+    mv4i_dmat w;
+    uint8_t  *wq;
+    uint16_t *sc;
+    int32_t   rows, cols;
+} linear_t;
+
+typedef struct {
+    int       attn;
+    linear_t  qkv, z, ab, out;            /* DeltaNet */
+    linear_t  qg, kv, o;                  /* attention */
+    linear_t  gate, up, down;
+    float    *attn_norm, *post_norm;
+    float    *conv_w, *ssm_a, *dt_bias, *ssm_norm, *conv_state, *rec_state;
+    float    *q_norm, *k_norm;
+    uint16_t *kcache, *vcache;
+} layer_t;
+
+struct dec_model {
+    dec_config c;
+    int device, rank, world;
+    /* local shard sizes */
+    int kh, vh, v0, qh, q0, kvh, kv0, ffn, f0, vocab, voc0, conv_dim, nchunks;
+    layer_t  *L;
+    linear_t  lm;
+    float    *final_norm;
+    uint16_t *embed;
+    /* activations */
+    float    *x, *t, *qkv_f, *z_f, *ab_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *gate_f, *part, *g_f, *u_f, *logits;
+    uint16_t *h16, *qkv16, *y16, *ya16, *hf16;
+    unsigned long long *key, *keys;
+    int32_t  *tok, *pos, *hist;
+    ncclComm_t comm;
+    int       comm_ok;
+    int64_t   weight_bytes;
+    void     *allocs[MAX_ALLOCS];
+    int       nalloc;
+};
+
+static int fail(cudaError_t e) { mv4i_g_cuda_err = (int)e; return -20; }
+
+static int dalloc(dec_model *m, void **p, size_t bytes)
+{
+    if (m->nalloc >= MAX_ALLOCS) return -11;
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return fail(e);
+    e = cudaMemset(*p, 0, bytes ? bytes : 16);
+    if (e != cudaSuccess) return fail(e);
+    m->allocs[m->nalloc++] = *p;
+    return 0;
+}
+
+static uint64_t mkey(uint64_t seed, int layer, int id)
+{ return seed * 1000003ull + (uint64_t)(layer + 2) * 131ull + (uint64_t)id * 7919ull; }
+
+static int to_device_i32(dec_model *m, int32_t **d, const int32_t *h, size_t n)
+{
+    CK(dalloc(m, (void **)d, sizeof(int32_t) * n));
+    cudaError_t e = cudaMemcpy(*d, h, sizeof(int32_t) * n, cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? 0 : fail(e);
+}
+
+/* A local g128 shard: rows (map or row0..) of a global [*, Kg] matrix,
+ * columns [k0, k0+kn). */
+static int make_linear(dec_model *m, linear_t *l, uint64_t key, const int32_t *h_rows, int row0, int nrows,
+                       int k0, int kn, int Kg)
+{
+    l->rows = nrows; l->cols = kn;
+    CK(dalloc(m, (void **)&l->wq, (size_t)nrows * kn / 2));
+    CK(dalloc(m, (void **)&l->sc, (size_t)nrows * (kn / 128) * 2));
+    int32_t *d_rows = NULL;
+    if (h_rows) CK(to_device_i32(m, &d_rows, h_rows, (size_t)nrows));
+    CK(dec_k_synth_linear(key, d_rows, row0, nrows, k0, kn, Kg, l->wq, l->sc, NULL));
+    CK(mv4i_dmat_wrap_g128(l->wq, kn / 2, l->sc, kn / 128, nrows, kn, m->device, &l->w));
+    m->weight_bytes += (int64_t)nrows * kn / 2 + (int64_t)nrows * (kn / 128) * 2;
+    return 0;
+}
+
+static int make_vec(dec_model *m, float **p, uint64_t key, const int32_t *h_idx, int64_t idx0, int64_t n,
+                    float mean, float std)
+{
+    CK(dalloc(m, (void **)p, sizeof(float) * (size_t)n));
+    int32_t *d_idx = NULL;
+    if (h_idx) CK(to_device_i32(m, &d_idx, h_idx, (size_t)n));
+    return dec_k_synth_vec(key, d_idx, idx0, n, mean, std, *p, NULL, NULL);
+}
+
+static int is_attn(const dec_config *c, int il) { return ((il + 1) % c->attn_every) == 0; }
+
+int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, int tp_world, dec_model **out)
+{
+    if (!cfg || !out || tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world) return -11;
+    const dec_config *c = cfg;
+    if (c->gdn_hd != HD || c->att_hd != HD || c->hidden % 128 || c->hidden > 16384 || c->ffn % (128 * tp_world)
+        || c->gdn_vh % tp_world || c->att_qh % tp_world || c->att_kvh % tp_world || c->att_kvh <= 0
+        || (c->att_qh / c->att_kvh) > 32 || c->att_qh % c->att_kvh || c->attn_every < 1
+        || c->n_rot > HD || (c->n_rot & 1) || c->max_ctx <= 0 || c->vocab < tp_world)
+        return -11;
+    dec_model *m = (dec_model *)calloc(1, sizeof *m);
+    if (!m) return -11;
+    m->c = *c; m->device = device; m->rank = tp_rank; m->world = tp_world;
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) { free(m); return fail(e); }
+    const int W = tp_world, R = tp_rank;
+    m->vh = c->gdn_vh / W; m->v0 = R * m->vh;
+    m->kh = c->gdn_kh < m->vh ? c->gdn_kh : m->vh;
+    m->qh = c->att_qh / W; m->q0 = R * m->qh;
+    m->kvh = c->att_kvh / W; m->kv0 = R * m->kvh;
+    m->ffn = c->ffn / W; m->f0 = R * m->ffn;
+    m->vocab = c->vocab / W + (R < c->vocab % W ? 1 : 0);
+    m->voc0 = R * (c->vocab / W) + (R < c->vocab % W ? R : c->vocab % W);
+    m->conv_dim = 2 * m->kh * HD + m->vh * HD;
+    m->nchunks = (c->max_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
+    m->L = (layer_t *)calloc((size_t)c->n_layers, sizeof(layer_t));
+    const int H = c->hidden, KHg = c->gdn_kh, VHg = c->gdn_vh;
+    const int conv_g = 2 * KHg * HD + VHg * HD;
+    int rc = 0;
+    int32_t *rows = (int32_t *)malloc(sizeof(int32_t) * (size_t)(2 * c->att_qh * HD + conv_g + 2 * VHg + 8));
+    int32_t *cidx = (int32_t *)malloc(sizeof(int32_t) * (size_t)conv_g * 4);
+#define TRY(x) do { rc = (x); if (rc) goto bad; } while (0)
+    for (int il = 0; il < c->n_layers; il++) {
+        layer_t *l = &m->L[il];
+        l->attn = is_attn(c, il);
+        TRY(make_vec(m, &l->attn_norm, mkey(seed, il, 1), NULL, 0, H, 1.0f, 0.1f));
+        TRY(make_vec(m, &l->post_norm, mkey(seed, il, 2), NULL, 0, H, 1.0f, 0.1f));
+        if (!l->attn) {
+            int n = 0;
+            for (int i = 0; i < m->kh; i++) {            /* local key head i = global (v0 + i) % KH */
+                const int g = (m->v0 + i) % KHg;
+                for (int d = 0; d < HD; d++) rows[n++] = g * HD + d;
+            }
+            for (int i = 0; i < m->kh; i++) {
+                const int g = (m->v0 + i) % KHg;
+                for (int d = 0; d < HD; d++) rows[n++] = KHg * HD + g * HD + d;
+            }
+            for (int i = 0; i < m->vh; i++)
+                for (int d = 0; d < HD; d++) rows[n++] = 2 * KHg * HD + (m->v0 + i) * HD + d;
+            TRY(make_linear(m, &l->qkv, mkey(seed, il, 10), rows, 0, n, 0, H, H));
+            for (int i = 0; i < n; i++) for (int t = 0; t < 4; t++) cidx[4 * i + t] = rows[i] * 4 + t;
+            TRY(make_vec(m, &l->conv_w, mkey(seed, il, 3), cidx, 0, (int64_t)n * 4, 0.0f, 0.5f));
+            TRY(make_linear(m, &l->z, mkey(seed, il, 11), NULL, m->v0 * HD, m->vh * HD, 0, H, H));
+            n = 0;
+            for (int i = 0; i < m->vh; i++) rows[n++] = m->v0 + i;
+            for (int i = 0; i < m->vh; i++) rows[n++] = VHg + m->v0 + i;
+            TRY(make_linear(m, &l->ab, mkey(seed, il, 12), rows, 0, n, 0, H, H));
+            TRY(make_linear(m, &l->out, mkey(seed, il, 13), NULL, 0, H, m->v0 * HD, m->vh * HD, VHg * HD));
+            TRY(make_vec(m, &l->ssm_a, mkey(seed, il, 4), NULL, m->v0, m->vh, -1.0f, 0.2f));
+            TRY(make_vec(m, &l->dt_bias, mkey(seed, il, 5), NULL, m->v0, m->vh, 0.0f, 0.5f));
+            TRY(make_vec(m, &l->ssm_norm, mkey(seed, il, 6), NULL, 0, HD, 1.0f, 0.1f));
+            TRY(dalloc(m, (void **)&l->conv_state, sizeof(float) * 3 * (size_t)m->conv_dim));
+            TRY(dalloc(m, (void **)&l->rec_state, sizeof(float) * (size_t)m->vh * HD * HD));
+        } else {
+            int n = 0;
+            for (int i = 0; i < m->qh; i++)
+                for (int j = 0; j < 2 * HD; j++) rows[n++] = (m->q0 + i) * 2 * HD + j;
+            TRY(make_linear(m, &l->qg, mkey(seed, il, 20), rows, 0, n, 0, H, H));
+            n = 0;
+            for (int i = 0; i < m->kvh; i++) for (int d = 0; d < HD; d++) rows[n++] = (m->kv0 + i) * HD + d;
+            for (int i = 0; i < m->kvh; i++)
+                for (int d = 0; d < HD; d++) rows[n++] = c->att_kvh * HD + (m->kv0 + i) * HD + d;
+            TRY(make_linear(m, &l->kv, mkey(seed, il, 21), rows, 0, n, 0, H, H));
+            TRY(make_linear(m, &l->o, mkey(seed, il, 22), NULL, 0, H, m->q0 * HD, m->qh * HD, c->att_qh * HD));
+            TRY(make_vec(m, &l->q_norm, mkey(seed, il, 7), NULL, 0, HD, 1.0f, 0.1f));
+            TRY(make_vec(m, &l->k_norm, mkey(seed, il, 8), NULL, 0, HD, 1.0f, 0.1f));
+            TRY(dalloc(m, (void **)&l->kcache, 2 * (size_t)c->max_ctx * m->kvh * HD));
+            TRY(dalloc(m, (void **)&l->vcache, 2 * (size_t)c->max_ctx * m->kvh * HD));
+        }
+        TRY(make_linear(m, &l->gate, mkey(seed, il, 30), NULL, m->f0, m->ffn, 0, H, H));
+        TRY(make_linear(m, &l->up, mkey(seed, il, 31), NULL, m->f0, m->ffn, 0, H, H));
+        TRY(make_linear(m, &l->down, mkey(seed, il, 32), NULL, 0, H, m->f0, m->ffn, c->ffn));
+    }
+    TRY(make_linear(m, &m->lm, mkey(seed, -1, 40), NULL, m->voc0, m->vocab, 0, H, H));
+    TRY(make_vec(m, &m->final_norm, mkey(seed, -1, 9), NULL, 0, H, 1.0f, 0.1f));
+    TRY(dalloc(m, (void **)&m->embed, 2 * (size_t)c->vocab * H));
+    TRY(dec_k_synth_vec(mkey(seed, -1, 41), NULL, 0, (int64_t)c->vocab * H, 0.0f, 1.0f, NULL, m->embed, NULL));
+    /* activations */
+    const int mx = H > m->ffn ? H : m->ffn;
+    TRY(dalloc(m, (void **)&m->x, 4 * (size_t)H));
+    TRY(dalloc(m, (void **)&m->t, 4 * (size_t)H));
+    TRY(dalloc(m, (void **)&m->h16, 2 * (size_t)mx));
+    TRY(dalloc(m, (void **)&m->qkv_f, 4 * (size_t)m->conv_dim));
+    TRY(dalloc(m, (void **)&m->qkv16, 2 * (size_t)m->conv_dim));
+    TRY(dalloc(m, (void **)&m->z_f, 4 * (size_t)m->vh * HD));
+    TRY(dalloc(m, (void **)&m->ab_f, 4 * 2 * (size_t)m->vh));
+    TRY(dalloc(m, (void **)&m->eg, 4 * (size_t)m->vh));
+    TRY(dalloc(m, (void **)&m->beta, 4 * (size_t)m->vh));
+    TRY(dalloc(m, (void **)&m->o_f, 4 * (size_t)m->vh * HD));
+    TRY(dalloc(m, (void **)&m->y16, 2 * (size_t)m->vh * HD));
+    TRY(dalloc(m, (void **)&m->qg_f, 4 * 2 * (size_t)m->qh * HD));
+    TRY(dalloc(m, (void **)&m->kv_f, 4 * 2 * (size_t)m->kvh * HD));
+    TRY(dalloc(m, (void **)&m->q_f, 4 * (size_t)m->qh * HD));
+    TRY(dalloc(m, (void **)&m->gate_f, 4 * (size_t)m->qh * HD));
+    TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 2)));
+    TRY(dalloc(m, (void **)&m->ya16, 2 * (size_t)m->qh * HD));
+    TRY(dalloc(m, (void **)&m->g_f, 4 * (size_t)m->ffn));
+    TRY(dalloc(m, (void **)&m->u_f, 4 * (size_t)m->ffn));
+    TRY(dalloc(m, (void **)&m->hf16, 2 * (size_t)m->ffn));
+    TRY(dalloc(m, (void **)&m->logits, 4 * (size_t)m->vocab));
+    TRY(dalloc(m, (void **)&m->key, 8));
+    TRY(dalloc(m, (void **)&m->keys, 8 * (size_t)W));
+    TRY(dalloc(m, (void **)&m->tok, 4));
+    TRY(dalloc(m, (void **)&m->pos, 4));
+    TRY(dalloc(m, (void **)&m->hist, 4 * (size_t)c->max_ctx));
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { rc = fail(e); goto bad; }
+    free(rows); free(cidx);
+    *out = m;
+    return 0;
+bad:
+    free(rows); free(cidx);
+    dec_destroy(m);
+    return rc;
+#undef TRY
+}
+
+int dec_destroy(dec_model *m)
+{
+    if (!m) return -11;
+    cudaSetDevice(m->device);
+    if (m->comm_ok) ncclCommDestroy(m->comm);
+    for (int i = 0; i < m->nalloc; i++) cudaFree(m->allocs[i]);
+    free(m->L);
+    free(m);
+    return 0;
+}
+
+int dec_nccl_unique_id(uint8_t id[128])
+{
+    ncclUniqueId u;
+    if (ncclGetUniqueId(&u) != ncclSuccess) return -20;
+    memcpy(id, &u, 128);
+    return 0;
+}
+
+int dec_tp_init(dec_model *m, const uint8_t id[128])
+{
+    if (!m) return -11;
+    if (m->world == 1) return 0;
+    ncclUniqueId u;
+    memcpy(&u, id, 128);
+    cudaSetDevice(m->device);
+    if (ncclCommInitRank(&m->comm, m->world, u, m->rank) != ncclSuccess) return -20;
+    m->comm_ok = 1;
+    return 0;
+}
+
+int dec_prefill_random(dec_model *m, int len, uint64_t seed)
+{
+    if (!m || len < 0 || len >= m->c.max_ctx) return -11;
+    cudaSetDevice(m->device);
+    for (int il = 0; il < m->c.n_layers; il++) {
+        layer_t *l = &m->L[il];
+        if (l->attn) {
+            /* cache [pos][kvh][hd]: draws indexed by (pos, global kv head, d) */
+            const int64_t n = (int64_t)len * m->kvh * HD;
+            if (n == 0) continue;
+            int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
+            for (int64_t i = 0; i < n; i++) {
+                const int64_t p = i / (m->kvh * HD), r = i % (m->kvh * HD);
+                idx[i] = (int32_t)((p * m->c.att_kvh + m->kv0 + r / HD) * HD + r % HD);
+            }
+            int32_t *d_idx = NULL;
+            cudaError_t e = cudaMalloc((void **)&d_idx, sizeof(int32_t) * (size_t)n);
+            if (e == cudaSuccess) e = cudaMemcpy(d_idx, idx, sizeof(int32_t) * (size_t)n, cudaMemcpyHostToDevice);
+            free(idx);
+            if (e != cudaSuccess) { if (d_idx) cudaFree(d_idx); return fail(e); }
+            int rc = dec_k_synth_vec(mkey(seed, il, 50), d_idx, 0, n, 0.f, 1.f, NULL, l->kcache, NULL);
+            if (!rc) rc = dec_k_synth_vec(mkey(seed, il, 51), d_idx, 0, n, 0.f, 1.f, NULL, l->vcache, NULL);
+            e = cudaDeviceSynchronize();
+            cudaFree(d_idx);
+            if (rc) return rc;
+            if (e != cudaSuccess) return fail(e);
+        } else {
+            const int64_t ns = (int64_t)m->vh * HD * HD;
+            CK(dec_k_synth_vec(mkey(seed, il, 52), NULL, (int64_t)m->v0 * HD * HD, ns, 0.f, 0.02f, l->rec_state, NULL, NULL));
+            CK(dec_k_synth_vec(mkey(seed, il, 53), NULL, 0, 3 * (int64_t)m->conv_dim, 0.f, 0.5f, l->conv_state, NULL, NULL));
+        }
+    }
+    cudaError_t e = cudaMemcpy(m->pos, &len, 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? 0 : fail(e);
+}
+
+int dec_set(dec_model *m, int pos, int token)
+{
+    if (!m || pos < 0 || pos >= m->c.max_ctx || token < 0 || token >= m->c.vocab) return -11;
+    cudaError_t e = cudaMemcpy(m->pos, &pos, 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(m->tok, &token, 4, cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? 0 : fail(e);
+}
+
+static void job(mv4i_job *j, const linear_t *l, const void *x, float *y, int accum)
+{
+    memset(j, 0, sizeof *j);
+    j->w = &l->w; j->x = x; j->n_rows = l->rows; j->n_cols = l->cols; j->nvec = 1;
+    j->y_f32 = y; j->accum = accum;
+}
+
+/* row-parallel block: a single GPU adds into x directly; TP sums partials */
+static int row_parallel(dec_model *m, const linear_t *l, const void *x16, void *s)
+{
+    mv4i_job j;
+    if (m->world == 1) {
+        job(&j, l, x16, m->x, 1);
+        return mv4i_launch(&j, 1, NULL, s);
+    }
+    job(&j, l, x16, m->t, 0);
+    CK(mv4i_launch(&j, 1, NULL, s));
+    if (ncclAllReduce(m->t, m->t, (size_t)m->c.hidden, ncclFloat32, ncclSum, m->comm, (cudaStream_t)s)
+        != ncclSuccess) return -20;
+    return dec_k_add(m->x, m->t, m->c.hidden, s);
+}
+
+int dec_step(dec_model *m, void *s)
+{
+    if (!m) return -11;
+    if (m->world > 1 && !m->comm_ok) return -11;
+    const dec_config *c = &m->c;
+    const int H = c->hidden;
+    mv4i_job jobs[4];
+    CK(dec_k_embed(m->embed, H, m->tok, m->x, s));
+    for (int il = 0; il < c->n_layers; il++) {
+        layer_t *l = &m->L[il];
+        CK(dec_k_rmsnorm(m->x, l->attn_norm, H, c->rms_eps, m->h16, s));
+        if (!l->attn) {
+            job(&jobs[0], &l->qkv, m->h16, m->qkv_f, 0);
+            job(&jobs[1], &l->z, m->h16, m->z_f, 0);
+            job(&jobs[2], &l->ab, m->h16, m->ab_f, 0);
+            CK(mv4i_launch(jobs, 3, NULL, s));
+            CK(dec_k_gdn_pre(m->qkv_f, m->conv_dim, l->conv_w, l->conv_state, m->qkv16, m->ab_f, m->vh,
+                             l->ssm_a, l->dt_bias, m->eg, m->beta, s));
+            gdn_f32_args g;
+            memset(&g, 0, sizeof g);
+            g.T = 1; g.H = m->vh; g.KH = m->kh; g.D = HD; g.S = l->rec_state;
+            g.q = m->qkv16; g.k = m->qkv16 + (size_t)m->kh * HD; g.v = m->qkv16 + (size_t)2 * m->kh * HD;
+            g.g = NULL; g.eg = m->eg; g.beta = m->beta; g.l2norm = 1; g.q_scale = 1.0f / sqrtf((float)HD);
+            g.out_f32 = m->o_f;
+            CK(gdn_run_f32(&g, s));
+            CK(dec_k_gated_norm(m->o_f, m->z_f, l->ssm_norm, m->vh, HD, c->rms_eps, m->y16, s));
+            CK(row_parallel(m, &l->out, m->y16, s));
+        } else {
+            job(&jobs[0], &l->qg, m->h16, m->qg_f, 0);
+            job(&jobs[1], &l->kv, m->h16, m->kv_f, 0);
+            CK(mv4i_launch(jobs, 2, NULL, s));
+            CK(dec_k_attn_pre(m->qg_f, m->kv_f, m->qh, m->kvh, HD, c->n_rot, c->rope_theta, c->rms_eps,
+                              l->q_norm, l->k_norm, m->pos, m->q_f, m->gate_f, l->kcache, l->vcache, s));
+            CK(dec_k_attention(m->q_f, l->kcache, l->vcache, m->qh, m->kvh, HD, ATT_CHUNK, c->max_ctx, m->pos,
+                               m->part, m->gate_f, m->ya16, s));
+            CK(row_parallel(m, &l->o, m->ya16, s));
+        }
+        CK(dec_k_rmsnorm(m->x, l->post_norm, H, c->rms_eps, m->h16, s));
+        job(&jobs[0], &l->gate, m->h16, m->g_f, 0);
+        job(&jobs[1], &l->up, m->h16, m->u_f, 0);
+        CK(mv4i_launch(jobs, 2, NULL, s));
+        CK(dec_k_swiglu(m->g_f, m->u_f, m->ffn, m->hf16, s));
+        CK(row_parallel(m, &l->down, m->hf16, s));
+    }
+    CK(dec_k_rmsnorm(m->x, m->final_norm, H, c->rms_eps, m->h16, s));
+    job(&jobs[0], &m->lm, m->h16, m->logits, 0);
+    CK(mv4i_launch(jobs, 1, NULL, s));
+    CK(dec_k_argmax(m->logits, m->vocab, m->voc0, m->key, s));
+    if (m->world > 1) {
+        if (ncclAllGather(m->key, m->keys, 1, ncclUint64, m->comm, (cudaStream_t)s) != ncclSuccess) return -20;
+        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, s);
+    }
+    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, s);
+}
+
+int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residual, int32_t **pos,
+                 int32_t *vocab0, int32_t *vocab_n)
+{
+    if (!m) return -11;
+    if (logits) *logits = m->logits;
+    if (history) *history = m->hist;
+    if (residual) *residual = m->x;
+    if (pos) *pos = m->pos;
+    if (vocab0) *vocab0 = m->voc0;
+    if (vocab_n) *vocab_n = m->vocab;
+    return 0;
+}
+
+int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, const uint16_t **d_sc,
+               int32_t *rows, int32_t *cols)
+{
+    if (!m || !name) return -11;
+    const linear_t *l = NULL;
+    if (layer < 0) { if (!strcmp(name, "lm_head")) l = &m->lm; }
+    else if (layer < m->c.n_layers) {
+        layer_t *L = &m->L[layer];
+        const struct { const char *n; linear_t *l; } tab[] = {
+            {"qkv", &L->qkv}, {"z", &L->z}, {"ab", &L->ab}, {"out", &L->out}, {"qg", &L->qg},
+            {"kv", &L->kv}, {"o", &L->o}, {"gate", &L->gate}, {"up", &L->up}, {"down", &L->down}};
+        for (unsigned i = 0; i < sizeof tab / sizeof tab[0]; i++)
+            if (!strcmp(name, tab[i].n) && tab[i].l->wq) l = tab[i].l;
+    }
+    if (!l) return -11;
+    *d_wq = l->wq; *d_sc = l->sc; *rows = l->rows; *cols = l->cols;
+    return 0;
+}
+
+int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count)
+{
+    if (!m || !name) return -11;
+    if (layer < 0) {
+        if (!strcmp(name, "final_norm")) { *d_ptr = m->final_norm; *count = m->c.hidden; return 0; }
+        if (!strcmp(name, "embed")) { *d_ptr = m->embed; *count = m->c.vocab * m->c.hidden; return 0; }
+        return -11;
+    }
+    if (layer >= m->c.n_layers) return -11;
+    layer_t *L = &m->L[layer];
+    const struct { const char *n; const void *p; int32_t c; } tab[] = {
+        {"attn_norm", L->attn_norm, m->c.hidden}, {"post_norm", L->post_norm, m->c.hidden},
+        {"conv_w", L->conv_w, 4 * m->conv_dim}, {"ssm_a", L->ssm_a, m->vh}, {"dt_bias", L->dt_bias, m->vh},
+        {"ssm_norm", L->ssm_norm, HD}, {"q_norm", L->q_norm, HD}, {"k_norm", L->k_norm, HD},
+        {"conv_state", L->conv_state, 3 * m->conv_dim}, {"rec_state", L->rec_state, m->vh * HD * HD},
+        {"kcache", L->kcache, m->c.max_ctx * m->kvh * HD}, {"vcache", L->vcache, m->c.max_ctx * m->kvh * HD}};
+    for (unsigned i = 0; i < sizeof tab / sizeof tab[0]; i++)
+        if (!strcmp(name, tab[i].n) && tab[i].p) { *d_ptr = tab[i].p; *count = tab[i].c; return 0; }
+    return -11;
+}
+
+int64_t dec_step_bytes(dec_model *m)
+{
+    if (!m) return -11;
+    int pos = 0;
+    cudaSetDevice(m->device);
+    cudaMemcpy(&pos, m->pos, 4, cudaMemcpyDeviceToHost);
+    int64_t b = m->weight_bytes;
+    for (int il = 0; il < m->c.n_layers; il++) {
+        if (m->L[il].attn) b += (int64_t)2 * (pos + 1) * m->kvh * HD * 2;
+        else b += (int64_t)2 * m->vh * HD * HD * 4 + (int64_t)2 * 3 * m->conv_dim * 4;
+    }
+    b += (int64_t)m->c.hidden * 2;              /* the embedding row */
+    return b;
+}

@@ -354,8 +354,8 @@ __device__ __forceinline__ void load_step(const gdn_f32_args &A, int t, int h, i
     const size_t vj = ((size_t)t * A.H + h) * 128 + j;
     s.v = __ldg(A.v + vj);
     s.g = A.g ? __ldg(A.g + vj) : (uint16_t)0;
-    s.a = __ldg(A.a + (size_t)t * A.H + h);
-    s.b = __ldg(A.b + (size_t)t * A.H + h);
+    s.a = A.eg ? __ldg(A.eg + (size_t)t * A.H + h) : __ldg(A.a + (size_t)t * A.H + h);
+    s.b = A.beta ? __ldg(A.beta + (size_t)t * A.H + h) : __ldg(A.b + (size_t)t * A.H + h);
 }
 
 // grid: H x 8 CTAs of 4 warps; CTA (h, c) owns columns 16c .. 16c+15 of head h.
@@ -398,9 +398,13 @@ gdn_f32_kernel(const gdn_f32_args A)
 #pragma unroll
             for (int i = 0; i < 16; i++) qf[i] *= A.q_scale;
         }
-        const float sp = cur.a > 30.f ? cur.a : log1pf(expf(cur.a));
-        const float alpha = expf(-sp);
-        const float beta = 1.0f / (1.0f + expf(-cur.b));
+        float alpha, beta;
+        if (A.eg) { alpha = cur.a; beta = cur.b; }
+        else {
+            const float sp = cur.a > 30.f ? cur.a : log1pf(expf(cur.a));
+            alpha = expf(-sp);
+            beta = 1.0f / (1.0f + expf(-cur.b));
+        }
         float sk0 = 0.f, sk1 = 0.f;
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
@@ -432,7 +436,7 @@ gdn_f32_kernel(const gdn_f32_args A)
 extern "C" int gdn_run_f32(const gdn_f32_args *a, void *stream)
 {
     if (!a || a->D != 128 || a->T <= 0 || a->H <= 0 || a->KH <= 0 || !a->S || !a->q || !a->k || !a->v
-        || !a->a || !a->b || (!a->out_f32 && !a->out_f16)) return -11;
+        || (!a->eg && !a->a) || (!a->beta && !a->b) || (!a->out_f32 && !a->out_f16)) return -11;
     if ((((uintptr_t)a->S) | ((uintptr_t)a->q) | ((uintptr_t)a->k)) & 15) return -11;
     gdn_f32_kernel<<<a->H * 8, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*a);
     cudaError_t e = cudaGetLastError();

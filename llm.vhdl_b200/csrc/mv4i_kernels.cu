@@ -57,6 +57,7 @@ struct DevJob {
     int32_t        tile0, ntiles;
     int32_t        lpr;                    // v3: lanes per row
     int32_t        sc_vec;                 // v3: golden scales as one 8-byte load per group
+    int32_t        accum;                  // g128: add into y_f32
 };
 
 struct LaunchParams {
@@ -407,6 +408,7 @@ mv4i_kernel(const __grid_constant__ LaunchParams P)
 #pragma unroll
                     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                     if (lane == 0 && row < J.n_rows) {
+                        if (J.accum) v += J.y_f32[row];
                         if (J.y_f32) J.y_f32[row] = v;
                         if (J.y_f16) J.y_f16[row] = __half_as_ushort(__float2half_rn(v));
                     }
@@ -858,6 +860,7 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
                     float v = facc[r];
                     for (int o = lpr >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                     if (sl == 0 && row < n_rows) {
+                        if (J.accum) v += J.y_f32[row];
                         if (J.y_f32) J.y_f32[row] = v;
                         if (J.y_f16) J.y_f16[row] = __half_as_ushort(__float2half_rn(v));
                     }
@@ -1111,6 +1114,8 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
         d.wq = a.w->wq; d.sc = a.w->sc; d.x = a.x; d.d_x_exp = a.d_x_exp;
         d.y_data = a.y_data; d.y_mant = a.y_mant; d.y_acc = a.y_acc;
         d.y_f16 = a.y_f16; d.y_f32 = a.y_f32; d.status = a.status;
+        d.accum = (kind0 == MV4I_KIND_G128) && a.accum;
+        if (d.accum && !a.y_f32) return -11;
         d.w_pitch = a.w->w_pitch; d.s_pitch = a.w->s_pitch;
         d.n_rows = a.n_rows; d.n_cols = a.n_cols;
         d.nb = kind0 == MV4I_KIND_G128 ? ((a.n_cols + 127) / 128) * 4 : (a.n_cols + 31) / 32;

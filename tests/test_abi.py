@@ -10,11 +10,21 @@ import oracle as O
 
 
 def test_library_exports_every_declared_symbol(pkg):
+    import glob
+    import os
     L = pkg.lib()
+    D = pkg.declib()
+    inc = os.path.join(pkg.ROOT, "include")
+    for h in glob.glob(os.path.join(inc, "*.h")):
+        names = pkg.header_symbols(h)
+        assert names, h
+        lb = D if os.path.basename(h) == "dec_b200.h" else L
+        missing = [n for n in names if not hasattr(lb, n)]
+        assert not missing, (h, missing)
     names = pkg.header_symbols()
     assert "mv4i_parse" in names and "mv4i_matvec" in names and "mv4i_launch" in names
-    missing = [n for n in names if not hasattr(L, n)]
-    assert not missing, missing
+    assert "dec_step" in names and "gdn_run_f32" in names
+    assert set(pkg.DEC_EXPORTS) == set(pkg.header_symbols(os.path.join(inc, "dec_b200.h")))
     assert b"sm_100a" in L.mv4i_version()
 
 
