@@ -59,3 +59,28 @@ def cuda():
         pytest.fail("GPU test collected without a CUDA device")
     torch.cuda.init()
     return torch
+
+
+class _DevArray:
+    """A raw device allocation seen through __cuda_array_interface__."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2, "strides": None}
+
+
+_SIGNED = {np.dtype(np.uint16): np.int16, np.dtype(np.uint32): np.int32, np.dtype(np.uint64): np.int64}
+
+
+def device_view(torch, ptr, shape, dtype):
+    """A torch tensor aliasing `shape` elements of `dtype` at device address ptr
+    (unsigned 16/32/64-bit are viewed as the signed type of the same width)."""
+    dt = np.dtype(dtype)
+    dt = np.dtype(_SIGNED.get(dt, dt))
+    return torch.as_tensor(_DevArray(ptr, shape, dt.str), device="cuda")
+
+
+def device_read(torch, ptr, shape, dtype):
+    """Copy device memory at ptr into a new numpy array of `dtype`."""
+    torch.cuda.synchronize()
+    return device_view(torch, ptr, shape, dtype).cpu().numpy().view(np.dtype(dtype)).copy()

@@ -83,3 +83,18 @@ def test_parse_refusals_match_reference(pkg):
         assert pi.rc == rr, (name, pi.rc, rr)
         seen.add(rr)
     assert {0, -1, -2, -3, -4, -5, -6, -7, -9}.issubset(seen) or len(seen) >= 8
+
+
+def test_decode_bad_configs_are_refused_before_any_cuda_call(pkg):
+    """dec_create validates the configuration on the host (-11) first."""
+    cfg0 = dict(hidden=256, n_layers=8, attn_every=4, vocab=1000, ffn=512, gdn_kh=2, gdn_vh=4, gdn_hd=128,
+                att_qh=8, att_kvh=4, att_hd=128, n_rot=32, rope_theta=1.0e6, rms_eps=1e-6, max_ctx=256)
+    L = pkg.declib()
+    h = C.c_void_p()
+    for k, v in [("gdn_hd", 64), ("hidden", 200), ("att_kvh", 3), ("n_rot", 33), ("max_ctx", 0),
+                 ("ffn", 320), ("attn_every", 0)]:
+        cfg = dict(cfg0)
+        cfg[k] = v
+        assert L.dec_create(C.byref(pkg.DecConfig(**cfg)), 1, 0, 0, 1, C.byref(h)) == -11, k
+    assert L.dec_create(C.byref(pkg.DecConfig(**cfg0)), 1, 0, 2, 2, C.byref(h)) == -11
+    assert L.dec_create(C.byref(pkg.DecConfig(**cfg0)), 1, 0, 0, 8, C.byref(h)) == -11   # 4 kv heads
