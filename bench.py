@@ -277,6 +277,7 @@ def run_ours(args, rank, world, local_rank):
     assert torch.equal(hy.to(dev), y16), "host-buffer result differs from the device launch"
 
     gdn = run_gdn(args, pkg, L, torch, dev, stream, sp, timed)
+    dec = run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank)
 
     peak, peak_kind = peaks()
     achieved = G * G128_BYTES / (ms_step * 1e-3) / 1e9
@@ -312,6 +313,7 @@ def run_ours(args, rank, world, local_rank):
                    "GBps": round(G128_BYTES / (sms * 1e-3) / 1e9, 1),
                    "how": "64 one-job launches in a CUDA graph, rotating over the stack"},
         "gdn": gdn,
+        "decode": dec,
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
@@ -397,6 +399,151 @@ def run_gdn(args, pkg, L, torch, dev, stream, sp, timed):
         "per_step_how": "one launch per step, state through HBM, 256 launches in a CUDA graph",
         "kernel": "gdn_f32_kernel",
     }
+
+
+# ------------------------------------------------------------ decode (configs 3, 4)
+
+DEC_C3 = dict(hidden=2048, n_layers=24, attn_every=4, vocab=151936, ffn=6144, gdn_kh=16, gdn_vh=16, gdn_hd=128,
+              att_qh=16, att_kvh=2, att_hd=128, n_rot=32, rope_theta=1.0e6, rms_eps=1e-6, max_ctx=1024)
+DEC_C4 = dict(hidden=5120, n_layers=48, attn_every=4, vocab=151936, ffn=17408, gdn_kh=32, gdn_vh=32, gdn_hd=128,
+              att_qh=40, att_kvh=8, att_hd=128, n_rot=32, rope_theta=1.0e6, rms_eps=1e-6, max_ctx=8192 + 512)
+
+
+class _DevArray:
+    def __init__(self, ptr, n, typestr):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 2, "strides": None}
+
+
+def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank):
+    """Decode tokens/s through include/dec_b200.h, one step per CUDA-graph
+    replay.  Config 3 (1 GPU): 512-token random-id prompt fed through the
+    decode step, then 256 greedy tokens, batch 1.  Config 4: tensor parallel
+    over the `world` ranks (NCCL all-reduce per row-parallel block), KV
+    context pre-filled to 8192 with N(0,1), batch 1."""
+    import numpy as np
+    D = pkg.declib()
+    out = {}
+
+    def create(cfg, seed, R, W):
+        h = C.c_void_p()
+        rc = D.dec_create(C.byref(pkg.DecConfig(**cfg)), seed, local_rank, R, W, C.byref(h))
+        if rc:
+            raise RuntimeError("dec_create failed %d (cuda %d)" % (rc, pkg.lib().mv4i_last_cuda_error()))
+        return h
+
+    def step_fn(h):
+        def f():
+            rc = D.dec_step(h, sp)
+            if rc:
+                raise RuntimeError("dec_step failed %d" % rc)
+        return f
+
+    def capture(h):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step_fn(h)()
+        return g
+
+    if world == 1:
+        cfg = DEC_C3
+        h = create(cfg, 2, 0, 1)
+        prompt = np.random.default_rng(2).integers(0, cfg["vocab"], 512).astype(np.int32)
+        pa = C.cast((C.c_int32 * 512)(*prompt.tolist()), C.c_void_p)
+        assert D.dec_set_prompt(h, pa, 512, sp) == 0
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step_fn(h)()
+        torch.cuda.synchronize(dev)
+        g = capture(h)
+        for _ in range(args.warmup):
+            g.replay()
+        assert D.dec_set_prompt(h, pa, 512, sp) == 0
+        ms_prompt = timed(g.replay, 511)
+        gen = 256
+        ms_gen = timed(g.replay, gen)
+        torch.cuda.synchronize(dev)
+        hp = C.c_void_p()
+        assert D.dec_pointers(h, None, C.byref(hp), None, None, None, None) == 0
+        hist = torch.as_tensor(_DevArray(hp.value, cfg["max_ctx"], "<i4"), device=dev)
+        toks = hist[511:511 + gen].cpu().numpy()
+        # end to end: the prompt from pinned host memory, and each generated
+        # token read back to pinned host memory as it is produced
+        hprompt = torch.from_numpy(prompt).pin_memory()
+        htok = torch.empty(1, dtype=torch.int32).pin_memory()
+
+        def e2e_run():
+            assert D.dec_set_prompt(h, C.c_void_p(hprompt.data_ptr()), 512, sp) == 0
+            with torch.cuda.stream(stream):
+                for _ in range(511):
+                    g.replay()
+                for i in range(gen):
+                    g.replay()
+                    htok.copy_(hist[511 + i:512 + i], non_blocking=True)
+                    stream.synchronize()
+        e2e_ms = timed(e2e_run, 1)
+        sbytes = D.dec_step_bytes(h)
+        del g
+        D.dec_destroy(h)
+        peak, _ = peaks()
+        us = ms_gen * 1e3 / gen
+        out["config3"] = {
+            "workload": "config 3: 24-layer hybrid (18 DeltaNet + 6 gated attention), hidden 2048, vocab 151936, "
+                        "INT4 g128, seed 2; 512-token random-id prompt, 256 greedy tokens, batch 1",
+            "tokens_per_s": round(gen / (ms_gen * 1e-3), 1),
+            "us_per_token": round(us, 2),
+            "prompt_tokens_per_s": round(511 / (ms_prompt * 1e-3), 1),
+            "bytes_per_step": sbytes,
+            "GBps": round(sbytes / (us * 1e-6) / 1e9, 1),
+            "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
+            "first_tokens": [int(t) for t in toks[:8]],
+            "e2e": {"tokens_per_s": round((511 + gen) / (e2e_ms * 1e-3), 1),
+                    "how": "prompt H2D from pinned host, 767 graph replays, each generated token D2H "
+                           "(pinned) and synchronised as produced",
+                    "h2d_bytes": 512 * 4, "d2h_bytes_per_token": 4},
+            "batch8": None,
+        }
+
+    # config 4, tensor parallel over all ranks
+    cfg = DEC_C4
+    h = create(cfg, 4, rank, world)
+    uid = (C.c_uint8 * 128)()
+    if world > 1:
+        import torch.distributed as dist
+        if rank == 0:
+            assert D.dec_nccl_unique_id(uid) == 0
+        t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device=dev)
+        dist.broadcast(t, 0)
+        uid = (C.c_uint8 * 128)(*t.cpu().tolist())
+    assert D.dec_tp_init(h, uid) == 0
+    assert D.dec_prefill_random(h, 8192, 5) == 0
+    assert D.dec_set(h, 8192, 1) == 0
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step_fn(h)()
+    torch.cuda.synchronize(dev)
+    g = capture(h)
+    for _ in range(args.warmup):
+        g.replay()
+    n = 64
+    ms = timed(g.replay, n)
+    sbytes = D.dec_step_bytes(h)
+    del g
+    D.dec_destroy(h)
+    peak, _ = peaks()
+    us = ms * 1e3 / n
+    out["config4"] = {
+        "workload": "config 4: 48-layer hybrid (36 DeltaNet + 12 gated attention), hidden 5120, 40/8 heads, "
+                    "32 DeltaNet heads, FFN 17408, vocab 151936, INT4 g128; KV context 8192, batch 1",
+        "tp": world,
+        "tokens_per_s": round(n / (ms * 1e-3), 1),
+        "us_per_token": round(us, 2),
+        "bytes_per_step_per_rank": sbytes,
+        "GBps_per_rank": round(sbytes / (us * 1e-6) / 1e9, 1),
+        "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
+        "collectives_per_step": (2 * cfg["n_layers"] + 1) if world > 1 else 0,
+    }
+    return out
 
 
 def gdn_cpu_baseline(budget_s=3.0):

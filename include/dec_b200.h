@@ -62,13 +62,25 @@ int dec_tp_init(dec_model *m, const uint8_t id[128]);
  * N(0, 0.02) and the conv states with N(0, 0.5), and sets the position to len. */
 int dec_prefill_random(dec_model *m, int len, uint64_t seed);
 
-/* Sets the position and the current input token (host values). */
+/* Sets the position and the current input token (host values); clears any
+ * prompt. */
 int dec_set(dec_model *m, int pos, int token);
+
+/* Starts a sequence from position 0 (DeltaNet and conv states zeroed) with a
+ * prompt of n tokens (host array):
+ * steps 0 .. n-2 take the prompt's next token as their next input (teacher
+ * forcing, ref/run9b.c's --tokens loop), later steps their own argmax.  The
+ * prediction of every step is recorded in the history at its position, so
+ * history[n-1 ..] is the generated continuation.  The copies are ordered on
+ * `stream` and complete before the call returns. */
+int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream);
 
 /* One decode step on `stream`: embeds the current token, runs every layer,
  * the LM head and argmax; the argmax becomes the current token and is stored
  * in the token history at the current position; the position advances.  No
- * host synchronisation. */
+ * host synchronisation.  Returns -11 once the position reaches max_ctx (a
+ * host-side count); replays of a captured step are bounded on the device
+ * instead: past max_ctx nothing more is written to the KV cache or history. */
 int dec_step(dec_model *m, void *stream);
 
 /* Device pointers for inspection: the fp32 logits of the last step (this
@@ -86,7 +98,11 @@ int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, 
 /* Parameter and state vectors: "attn_norm", "post_norm", "conv_w"
  * ([conv_dim][4]), "ssm_a", "dt_bias", "ssm_norm", "q_norm", "k_norm",
  * "conv_state", "rec_state", "kcache", "vcache" (per layer), "final_norm" and
- * the fp16 "embed" [vocab][hidden] (layer -1). */
+ * the fp16 "embed" [vocab][hidden] (layer -1).  Layer -1 also names the
+ * activation seams of the last step, as the last layer to write each left
+ * them (the reference's seam records): fp32 "x" (residual), "qkv", "z", "ab",
+ * "eg", "beta", "o", "qg", "kv", "q", "gate", "g", "u", "logits"; fp16 "h16"
+ * (the last norm output), "qkv16", "y16", "ya16", "hf16". */
 int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count);
 
 /* Bytes of weights, KV cache and state one step reads on this rank. */

@@ -178,6 +178,7 @@ DEC_EXPORTS = {
     "dec_tp_init": (C.c_int, [C.c_void_p, C.c_void_p]),
     "dec_prefill_random": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64]),
     "dec_set": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "dec_set_prompt": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "dec_step": (C.c_int, [C.c_void_p, C.c_void_p]),
     "dec_pointers": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),

@@ -99,7 +99,7 @@ __global__ void dec_gated_norm_kernel(const float *o, const float *z, const floa
 // position.  One CTA per q head, then one per k head; hd threads.
 __global__ void dec_attn_pre_kernel(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot,
                                     float theta, float eps, const float *qn_w, const float *kn_w,
-                                    const int32_t *d_pos, float *q_out, float *gate_out,
+                                    const int32_t *d_pos, int max_ctx, float *q_out, float *gate_out,
                                     uint16_t *kcache, uint16_t *vcache)
 {
     __shared__ float red[32];
@@ -128,7 +128,7 @@ __global__ void dec_attn_pre_kernel(const float *qg, const float *kv, int qh, in
         if (isq) {
             q_out[(size_t)h * hd + i] = r;
             gate_out[(size_t)h * hd + i] = qg[(size_t)h * 2 * hd + hd + i];
-        } else {
+        } else if (pos < max_ctx) {          // a full cache takes no more entries
             const size_t off = ((size_t)pos * kvh + h) * hd + i;
             kcache[off] = __half_as_ushort(__float2half_rn(r));
             vcache[off] = __half_as_ushort(__float2half_rn(kv[(size_t)(kvh + h) * hd + i]));
@@ -139,16 +139,17 @@ __global__ void dec_attn_pre_kernel(const float *qg, const float *kv, int qh, in
 // Flash-decoding, part 1: CTA (chunk c of `ch` positions, kv head g), one warp
 // per q head of the group (q head h uses kv head h / (qh/kvh),
 // ref/run9b.c:859); lane l holds dims 4l..4l+3 (hd = 128).  Writes the
-// chunk's running max, sum and unnormalised output per q head.
+// chunk's running max, sum and unnormalised output per q head into a record
+// of hd + 4 floats (max, sum, 2 unused, then hd sums: 16-byte aligned).
 __global__ void dec_attn_decode_kernel(const float *q, const uint16_t *kcache, const uint16_t *vcache,
-                                       int qh, int kvh, int hd, int ch, const int32_t *d_pos, int nchunks,
-                                       float *part)
+                                       int qh, int kvh, int hd, int ch, const int32_t *d_pos, int max_ctx,
+                                       int nchunks, float *part)
 {
     const int c = blockIdx.x, g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = qh / kvh, h = g * grp + warp;
-    const int len = *d_pos + 1;
+    const int len = min(*d_pos + 1, max_ctx);
     const int p0 = c * ch;
-    float *pp = part + ((size_t)h * nchunks + c) * (hd + 2);
+    float *pp = part + ((size_t)h * nchunks + c) * (hd + 4);
     if (p0 >= len) {
         if (lane == 0) { pp[0] = -INFINITY; pp[1] = 0.f; }
         return;
@@ -177,7 +178,7 @@ __global__ void dec_attn_decode_kernel(const float *q, const uint16_t *kcache, c
         m = mn;
     }
     if (lane == 0) { pp[0] = m; pp[1] = l; }
-    reinterpret_cast<float4 *>(pp + 2)[lane] = make_float4(a0, a1, a2, a3);
+    reinterpret_cast<float4 *>(pp + 4)[lane] = make_float4(a0, a1, a2, a3);
 }
 
 // Flash-decoding, part 2: combine the chunks of each q head, apply the
@@ -188,13 +189,13 @@ __global__ void dec_attn_combine_kernel(const float *part, const float *gate, in
     const int h = blockIdx.x, lane = threadIdx.x;     // 32 threads, 4 dims each
     const int used = min(nchunks, (*d_pos + 1 + ch - 1) / ch);
     float M = -INFINITY;
-    for (int c = 0; c < used; c++) M = fmaxf(M, part[((size_t)h * nchunks + c) * (hd + 2)]);
+    for (int c = 0; c < used; c++) M = fmaxf(M, part[((size_t)h * nchunks + c) * (hd + 4)]);
     float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     for (int c = 0; c < used; c++) {
-        const float *pp = part + ((size_t)h * nchunks + c) * (hd + 2);
+        const float *pp = part + ((size_t)h * nchunks + c) * (hd + 4);
         const float w = expf(pp[0] - M);
         L += pp[1] * w;
-        const float4 a = reinterpret_cast<const float4 *>(pp + 2)[lane];
+        const float4 a = reinterpret_cast<const float4 *>(pp + 4)[lane];
         a0 += a.x * w; a1 += a.y * w; a2 += a.z * w; a3 += a.w * w;
     }
     const float inv = 1.0f / L;
@@ -236,17 +237,20 @@ __global__ void __launch_bounds__(512) dec_argmax_kernel(const float *v, int n, 
     if ((threadIdx.x & 31) == 0) atomicMax(key, best);
 }
 
-// Pick the largest of `n` keys (one per rank), make it the current token,
-// record it at the current position, advance the position, clear `key`.
+// Pick the largest of `n` keys (one per rank), record it as the prediction
+// at the current position, advance the position, clear `key`.  The next
+// input token is the prompt's while the prompt lasts (prompt[0] holds its
+// length, prompt[1 + i] its tokens), else the prediction.
 __global__ void dec_advance_kernel(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok,
-                                   int32_t *history, int32_t *pos, int max_ctx)
+                                   int32_t *history, int32_t *pos, int max_ctx, const int32_t *prompt)
 {
     unsigned long long best = 0;
     for (int i = 0; i < n; i++) best = keys[i] > best ? keys[i] : best;
     const int32_t t = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
-    *tok = t;
     const int p = *pos;
     if (p < max_ctx) history[p] = t;
+    const int plen = prompt ? prompt[0] : 0;
+    *tok = (p + 1 < plen) ? prompt[1 + p + 1] : t;
     *pos = p + 1;
     *key = 0;
 }
@@ -327,11 +331,12 @@ int dec_k_gated_norm(const float *o, const float *z, const float *w, int heads, 
 { dec_gated_norm_kernel<<<heads, 128, 0, ST(s)>>>(o, z, w, hd, eps, y); return dk(cudaGetLastError()); }
 
 int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
-                   const float *qn_w, const float *kn_w, const int32_t *d_pos, float *q_out, float *gate_out,
-                   uint16_t *kcache, uint16_t *vcache, void *s)
+                   const float *qn_w, const float *kn_w, const int32_t *d_pos, int max_ctx, float *q_out,
+                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s)
 {
     dec_attn_pre_kernel<<<qh + kvh, ((hd + 31) / 32) * 32, 0, ST(s)>>>(qg, kv, qh, kvh, hd, n_rot, theta, eps, qn_w,
-                                                                      kn_w, d_pos, q_out, gate_out, kcache, vcache);
+                                                                      kn_w, d_pos, max_ctx, q_out, gate_out, kcache,
+                                                                      vcache);
     return dk(cudaGetLastError());
 }
 
@@ -340,7 +345,7 @@ int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int 
 {
     const int nchunks = (max_ctx + ch - 1) / ch;
     dec_attn_decode_kernel<<<dim3(nchunks, kvh), 32 * (qh / kvh), 0, ST(s)>>>(q, kc, vc, qh, kvh, hd, ch, d_pos,
-                                                                              nchunks, part);
+                                                                              max_ctx, nchunks, part);
     dec_attn_combine_kernel<<<qh, 32, 0, ST(s)>>>(part, gate, hd, nchunks, d_pos, ch, y);
     return dk(cudaGetLastError());
 }
@@ -358,8 +363,11 @@ int dec_k_argmax(const float *v, int n, int idx0, unsigned long long *key, void 
 }
 
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
-                  int32_t *pos, int max_ctx, void *s)
-{ dec_advance_kernel<<<1, 1, 0, ST(s)>>>(keys, n, key, tok, hist, pos, max_ctx); return dk(cudaGetLastError()); }
+                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s)
+{
+    dec_advance_kernel<<<1, 1, 0, ST(s)>>>(keys, n, key, tok, hist, pos, max_ctx, prompt);
+    return dk(cudaGetLastError());
+}
 
 int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
                        uint8_t *wq, uint16_t *sc, void *s)

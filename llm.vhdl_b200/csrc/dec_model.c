@@ -30,15 +30,15 @@ int dec_k_gdn_pre(const float *qkv, int conv_dim, const float *conv_w, float *co
                   const float *ab, int vh, const float *ssm_a, const float *dt_bias, float *eg, float *beta, void *s);
 int dec_k_gated_norm(const float *o, const float *z, const float *w, int heads, int hd, float eps, uint16_t *y, void *s);
 int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
-                   const float *qn_w, const float *kn_w, const int32_t *d_pos, float *q_out, float *gate_out,
-                   uint16_t *kcache, uint16_t *vcache, void *s);
+                   const float *qn_w, const float *kn_w, const int32_t *d_pos, int max_ctx, float *q_out,
+                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s);
 int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int qh, int kvh, int hd, int ch,
                     int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s);
 int dec_k_swiglu(const float *g, const float *u, int n, uint16_t *h, void *s);
 int dec_k_add(float *x, const float *t, int n, void *s);
 int dec_k_argmax(const float *v, int n, int idx0, unsigned long long *key, void *s);
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
-                  int32_t *pos, int max_ctx, void *s);
+                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s);
 int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
                        uint8_t *wq, uint16_t *sc, void *s);
 int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, float mean, float std,
@@ -81,6 +81,8 @@ struct dec_model {
     uint16_t *h16, *qkv16, *y16, *ya16, *hf16;
     unsigned long long *key, *keys;
     int32_t  *tok, *pos, *hist;
+    int32_t  *prompt;                    /* [0] = length, [1..] = tokens     */
+    int       hpos;                      /* host mirror of *pos for direct calls */
     ncclComm_t comm;
     int       comm_ok;
     int64_t   weight_bytes;
@@ -241,7 +243,7 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->kv_f, 4 * 2 * (size_t)m->kvh * HD));
     TRY(dalloc(m, (void **)&m->q_f, 4 * (size_t)m->qh * HD));
     TRY(dalloc(m, (void **)&m->gate_f, 4 * (size_t)m->qh * HD));
-    TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 2)));
+    TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 4)));
     TRY(dalloc(m, (void **)&m->ya16, 2 * (size_t)m->qh * HD));
     TRY(dalloc(m, (void **)&m->g_f, 4 * (size_t)m->ffn));
     TRY(dalloc(m, (void **)&m->u_f, 4 * (size_t)m->ffn));
@@ -252,6 +254,7 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->tok, 4));
     TRY(dalloc(m, (void **)&m->pos, 4));
     TRY(dalloc(m, (void **)&m->hist, 4 * (size_t)c->max_ctx));
+    TRY(dalloc(m, (void **)&m->prompt, 4 * ((size_t)c->max_ctx + 1)));
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { rc = fail(e); goto bad; }
     free(rows); free(cidx);
@@ -329,15 +332,44 @@ int dec_prefill_random(dec_model *m, int len, uint64_t seed)
     }
     cudaError_t e = cudaMemcpy(m->pos, &len, 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    return e == cudaSuccess ? 0 : fail(e);
+    if (e != cudaSuccess) return fail(e);
+    m->hpos = len;
+    return 0;
 }
 
 int dec_set(dec_model *m, int pos, int token)
 {
     if (!m || pos < 0 || pos >= m->c.max_ctx || token < 0 || token >= m->c.vocab) return -11;
+    const int32_t zero = 0;
     cudaError_t e = cudaMemcpy(m->pos, &pos, 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(m->tok, &token, 4, cudaMemcpyHostToDevice);
-    return e == cudaSuccess ? 0 : fail(e);
+    if (e == cudaSuccess) e = cudaMemcpy(m->prompt, &zero, 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail(e);
+    m->hpos = pos;
+    return 0;
+}
+
+int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream)
+{
+    if (!m || !tokens || n < 1 || n > m->c.max_ctx) return -11;
+    for (int i = 0; i < n; i++) if (tokens[i] < 0 || tokens[i] >= m->c.vocab) return -11;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int32_t zero = 0;
+    cudaError_t e = cudaSuccess;
+    for (int il = 0; il < m->c.n_layers && e == cudaSuccess; il++) {     /* a new sequence */
+        layer_t *l = &m->L[il];
+        if (l->attn) continue;
+        e = cudaMemsetAsync(l->conv_state, 0, sizeof(float) * 3 * (size_t)m->conv_dim, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(l->rec_state, 0, sizeof(float) * (size_t)m->vh * HD * HD, s);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->prompt, &n, 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->prompt + 1, tokens, 4 * (size_t)n, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->tok, tokens, 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, &zero, 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(e);
+    m->hpos = 0;
+    return 0;
 }
 
 static void job(mv4i_job *j, const linear_t *l, const void *x, float *y, int accum)
@@ -366,6 +398,8 @@ int dec_step(dec_model *m, void *s)
 {
     if (!m) return -11;
     if (m->world > 1 && !m->comm_ok) return -11;
+    if (m->hpos >= m->c.max_ctx) return -11;   /* the KV cache is full */
+    m->hpos++;
     const dec_config *c = &m->c;
     const int H = c->hidden;
     mv4i_job jobs[4];
@@ -394,7 +428,7 @@ int dec_step(dec_model *m, void *s)
             job(&jobs[1], &l->kv, m->h16, m->kv_f, 0);
             CK(mv4i_launch(jobs, 2, NULL, s));
             CK(dec_k_attn_pre(m->qg_f, m->kv_f, m->qh, m->kvh, HD, c->n_rot, c->rope_theta, c->rms_eps,
-                              l->q_norm, l->k_norm, m->pos, m->q_f, m->gate_f, l->kcache, l->vcache, s));
+                              l->q_norm, l->k_norm, m->pos, c->max_ctx, m->q_f, m->gate_f, l->kcache, l->vcache, s));
             CK(dec_k_attention(m->q_f, l->kcache, l->vcache, m->qh, m->kvh, HD, ATT_CHUNK, c->max_ctx, m->pos,
                                m->part, m->gate_f, m->ya16, s));
             CK(row_parallel(m, &l->o, m->ya16, s));
@@ -412,9 +446,9 @@ int dec_step(dec_model *m, void *s)
     CK(dec_k_argmax(m->logits, m->vocab, m->voc0, m->key, s));
     if (m->world > 1) {
         if (ncclAllGather(m->key, m->keys, 1, ncclUint64, m->comm, (cudaStream_t)s) != ncclSuccess) return -20;
-        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, s);
+        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s);
     }
-    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, s);
+    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s);
 }
 
 int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residual, int32_t **pos,
@@ -453,8 +487,19 @@ int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int
 {
     if (!m || !name) return -11;
     if (layer < 0) {
-        if (!strcmp(name, "final_norm")) { *d_ptr = m->final_norm; *count = m->c.hidden; return 0; }
-        if (!strcmp(name, "embed")) { *d_ptr = m->embed; *count = m->c.vocab * m->c.hidden; return 0; }
+        const int H = m->c.hidden;
+        const struct { const char *n; const void *p; int32_t c; } act[] = {
+            {"final_norm", m->final_norm, H}, {"embed", m->embed, m->c.vocab * H},
+            /* activation seams of the last step (the last layer that wrote them) */
+            {"x", m->x, H}, {"h16", m->h16, H}, {"qkv", m->qkv_f, m->conv_dim},
+            {"qkv16", m->qkv16, m->conv_dim}, {"z", m->z_f, m->vh * HD}, {"ab", m->ab_f, 2 * m->vh},
+            {"eg", m->eg, m->vh}, {"beta", m->beta, m->vh}, {"o", m->o_f, m->vh * HD},
+            {"y16", m->y16, m->vh * HD}, {"qg", m->qg_f, 2 * m->qh * HD}, {"kv", m->kv_f, 2 * m->kvh * HD},
+            {"q", m->q_f, m->qh * HD}, {"gate", m->gate_f, m->qh * HD}, {"ya16", m->ya16, m->qh * HD},
+            {"g", m->g_f, m->ffn}, {"u", m->u_f, m->ffn}, {"hf16", m->hf16, m->ffn},
+            {"logits", m->logits, m->vocab}};
+        for (unsigned i = 0; i < sizeof act / sizeof act[0]; i++)
+            if (!strcmp(name, act[i].n)) { *d_ptr = act[i].p; *count = act[i].c; return 0; }
         return -11;
     }
     if (layer >= m->c.n_layers) return -11;

@@ -27,7 +27,9 @@ projection, the conv output and the KV cache as fp16 instead.  The oracle rounds
 to fp16 at exactly those points (``f16``) and computes everything else in
 float64, so a difference against the GPU is fp32-versus-float64 arithmetic
 only.  Weights are the INT4 g128 images the library holds (signed nibbles
-times the fp16 group scale, the w_deq rule of ref/run9b.c:437-443).
+times the fp16 group scale, the w_deq rule of ref/run9b.c:437-443), and every
+projection sees its activation through the g128 kernel's int16 staging
+(``stage_g128``), the one approximation of that kernel besides fp32 summation.
 
 A non-zero ``mutant`` plants one of the reference's own documented mistakes
 (ref/run9b.c:180-192, the REF9B_MUT list) so the tests can show that the
@@ -49,6 +51,26 @@ def dequant_g128(wq, sc):
     q = np.where(q >= 8, q - 16, q)
     s = np.asarray(sc, np.uint16).view(np.float16).astype(np.float64)
     return q.astype(np.float64) * np.repeat(s, 128, axis=1)
+
+
+def stage_g128(x):
+    """The g128 matvec's activation staging (the numeric contract of
+    mv4i_kernels.cu stage_x for KIND_G128): per 128-column group, e = 15 -
+    (exponent of the group's max |x|, frexp convention), x_i ->
+    sat16(rint(x_i * 2^e)) * 2^-e, round half to even.  Finer than the
+    reference's own BFP registers (one exponent per whole vector, reg_put at
+    ref/run9b.c:343-359), coarser than fp16 for elements below max/16."""
+    x = np.asarray(x, np.float64)
+    n = x.size
+    G = (n + 127) // 128
+    g = np.zeros(G * 128)
+    g[:n] = x
+    g = g.reshape(G, 128)
+    am = np.max(np.abs(g), axis=1)
+    ex = np.frexp(am)[1]
+    e = np.where(am > 0, 15 - ex, 0)[:, None]
+    q = np.clip(np.rint(np.ldexp(g, e)), -32768, 32767)
+    return np.ldexp(q, -e).reshape(-1)[:n]
 
 
 def rmsnorm(x, w, eps, mutant=0):
@@ -84,10 +106,17 @@ class Model:
     [VH][j][i] with value column j over key i, kcache/vcache [ctx][KVH][att_hd]
     fp16 values)."""
 
-    def __init__(self, cfg, W, P, S, mutant=0, fp16=True):
+    def __init__(self, cfg, W, P, S, mutant=0, fp16=True, stage=None):
         self.c, self.W, self.P, self.S, self.mut = cfg, W, P, S, mutant
         # fp16=False: no storage rounding at all (the reference's --acts f32)
         self.r = f16 if fp16 else (lambda a: np.asarray(a, np.float64))
+        # stage: the g128 kernel's int16 activation staging before every
+        # projection (default: with fp16 storage)
+        self.stage = fp16 if stage is None else stage
+        self.seams = {}          # (layer, name) -> value, as the reference's seam()
+
+    def mv(self, w, x):
+        return w @ (stage_g128(x) if self.stage else x)
 
     def is_attn(self, il):
         return ((il + 1) % self.c["attn_every"]) == 0
@@ -96,14 +125,15 @@ class Model:
         c, W, P, S, mut, f16 = self.c, self.W, self.P, self.S, self.mut, self.r
         eps, KH, VH, HD = c["rms_eps"], c["gdn_kh"], c["gdn_vh"], c["gdn_hd"]
         h = f16(rmsnorm(x, P[il, "attn_norm"], eps, mut))
-        mixed = W[il, "qkv"] @ h
-        z = W[il, "z"] @ h
-        ab = W[il, "ab"] @ h
+        mixed = self.mv(W[il, "qkv"], h)
+        z = self.mv(W[il, "z"], h)
+        ab = self.mv(W[il, "ab"], h)
         cw = P[il, "conv_w"].reshape(-1, 4)
         cs = S[il, "conv_state"]
         acc = cs[0] * cw[:, 0] + cs[1] * cw[:, 1] + cs[2] * cw[:, 2] + mixed * cw[:, 3]
         S[il, "conv_state"] = np.stack([cs[1], cs[2], mixed])
         conv = f16(silu(acc))
+        self.seams.update({(il, "qkv"): mixed, (il, "z"): z, (il, "ab"): ab, (il, "qkv16"): conv, (il, "h16"): h})
         kd = KH * HD
         qc, kc, vc = conv[:kd].reshape(KH, HD), conv[kd:2 * kd].reshape(KH, HD), conv[2 * kd:].reshape(VH, HD)
         qc = np.stack([l2norm(r, eps, mut) for r in qc])
@@ -120,18 +150,20 @@ class Model:
             st[hh] = Sh
             out[hh] = (Sh @ qc[ki]) / np.sqrt(HD)
         zz = z.reshape(VH, HD)
+        self.seams[il, "o"] = out.reshape(-1)
         if mut == 5:
             y = np.stack([rmsnorm(out[i] * silu(zz[i]), P[il, "ssm_norm"], eps, mut) for i in range(VH)])
         else:
             y = np.stack([rmsnorm(out[i], P[il, "ssm_norm"], eps, mut) * silu(zz[i]) for i in range(VH)])
-        return x + W[il, "out"] @ f16(y.reshape(-1))
+        self.seams[il, "y16"] = f16(y.reshape(-1))
+        return x + self.mv(W[il, "out"], f16(y.reshape(-1)))
 
     def attn(self, il, x, pos):
         c, W, P, S, mut, f16 = self.c, self.W, self.P, self.S, self.mut, self.r
         eps, QH, KVH, nrot, HD = c["rms_eps"], c["att_qh"], c["att_kvh"], c["n_rot"], c["att_hd"]
         h = f16(rmsnorm(x, P[il, "attn_norm"], eps, mut))
-        qg = W[il, "qg"] @ h
-        kv = W[il, "kv"] @ h
+        qg = self.mv(W[il, "qg"], h)
+        kv = self.mv(W[il, "kv"], h)
         if mut == 1:
             q, g = qg[:QH * HD].reshape(QH, HD), qg[QH * HD:].reshape(QH, HD)
         else:
@@ -157,13 +189,14 @@ class Model:
             e = np.exp(sc - sc.max())
             t[hh] = (e @ vc[:, g_kv]) / e.sum()
         t = t * sigmoid(g)
-        return x + W[il, "o"] @ f16(t.reshape(-1))
+        return x + self.mv(W[il, "o"], f16(t.reshape(-1)))
 
     def ffn(self, il, x):
         eps, f16 = self.c["rms_eps"], self.r
         h = f16(rmsnorm(x, self.P[il, "post_norm"], eps, self.mut))
-        hh = f16(silu(self.W[il, "gate"] @ h) * (self.W[il, "up"] @ h))
-        return x + self.W[il, "down"] @ hh
+        hh = f16(silu(self.mv(self.W[il, "gate"], h)) * self.mv(self.W[il, "up"], h))
+        self.seams.update({(il, "xmid"): x, (il, "post16"): h, (il, "hf16"): hh})
+        return x + self.mv(self.W[il, "down"], hh)
 
     def step(self, tok, pos):
         """One token: returns (float64 logits, argmax_first token)."""
@@ -171,6 +204,7 @@ class Model:
         for il in range(self.c["n_layers"]):
             x = self.attn(il, x, pos) if self.is_attn(il) else self.gdn(il, x)
             x = self.ffn(il, x)
+        self.last_x = x
         h = self.r(rmsnorm(x, self.P[-1, "final_norm"], self.c["rms_eps"], self.mut))
-        logits = self.W[-1, "lm_head"] @ h
+        logits = self.mv(self.W[-1, "lm_head"], h)
         return logits, int(np.argmax(logits))                 # numpy: first maximum

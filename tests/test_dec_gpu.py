@@ -4,7 +4,10 @@ A small hybrid stack (DeltaNet layers and gated-attention layers in the 3:1
 pattern, INT4 g128 linears, fp16 KV cache pre-filled past one attention chunk)
 is stepped on the GPU through the C ABI; every weight, parameter and state is
 read back from the device into oracle/dec_oracle.py, which steps the same
-tokens in float64 with fp16 rounding at the same storage points.
+tokens in float64 with fp16 rounding at the same storage points.  Before each
+step the oracle takes the GPU's states, so every step is compared from the same
+inputs: a value that lands on the other side of an fp16 rounding boundary
+(fp32 versus float64 arithmetic) then cannot compound over steps.
 
 Tolerance (floating-point mode of the benchmark): logits within 1e-3 of the
 largest |logit|, states within 1e-3 of their largest magnitude, and the same
@@ -32,8 +35,8 @@ TOL = 1e-3
 LINEARS = {"gdn": ["qkv", "z", "ab", "out"], "attn": ["qg", "kv", "o"], "ffn": ["gate", "up", "down"]}
 
 
-def is_attn(il, cfg=CFG):
-    return ((il + 1) % cfg["attn_every"]) == 0
+def is_attn(il, cfg=None):
+    return ((il + 1) % (cfg or CFG)["attn_every"]) == 0
 
 
 class Dec:
@@ -81,14 +84,14 @@ def oracle_from(dec, torch, O, mutant=0):
     KH, VH, KVH = cfg["gdn_kh"], cfg["gdn_vh"], cfg["att_kvh"]
     conv_dim = 2 * KH * HD + VH * HD
     for il in range(cfg["n_layers"]):
-        names = LINEARS["attn" if is_attn(il) else "gdn"] + LINEARS["ffn"]
+        names = LINEARS["attn" if is_attn(il, cfg) else "gdn"] + LINEARS["ffn"]
         for n in names:
             W[il, n] = O.dequant_g128(*dec.linear(torch, il, n))
-        pn = ["attn_norm", "post_norm"] + (["q_norm", "k_norm"] if is_attn(il)
+        pn = ["attn_norm", "post_norm"] + (["q_norm", "k_norm"] if is_attn(il, cfg)
                                            else ["conv_w", "ssm_a", "dt_bias", "ssm_norm"])
         for n in pn:
             P[il, n] = dec.param(torch, il, n).astype(np.float64)
-        if is_attn(il):
+        if is_attn(il, cfg):
             for n in ("kcache", "vcache"):
                 S[il, n] = dec.param(torch, il, n, np.float16).astype(np.float64).reshape(-1, KVH, HD)
         else:
@@ -98,6 +101,20 @@ def oracle_from(dec, torch, O, mutant=0):
     P[-1, "final_norm"] = dec.param(torch, -1, "final_norm").astype(np.float64)
     P[-1, "embed"] = dec.param(torch, -1, "embed", np.float16).astype(np.float64).reshape(cfg["vocab"], -1)
     return O.Model(cfg, W, P, S, mutant)
+
+
+def sync_states(dec, torch, M):
+    """Load the GPU's current recurrent, conv and KV states into the oracle, so
+    each step is compared from identical inputs (fp16 storage flips do not
+    carry over from one step to the next)."""
+    cfg = dec.cfg
+    for il in range(cfg["n_layers"]):
+        if is_attn(il, cfg):
+            for n in ("kcache", "vcache"):
+                M.S[il, n] = dec.param(torch, il, n, np.float16).astype(np.float64).reshape(M.S[il, n].shape)
+        else:
+            for n in ("conv_state", "rec_state"):
+                M.S[il, n] = dec.param(torch, il, n).astype(np.float64).reshape(M.S[il, n].shape)
 
 
 def rel(a, b):
@@ -122,6 +139,7 @@ def test_decode_steps_match_oracle(pkg, cuda, O, prefill):
         ptrs = d.pointers()
         pos = prefill
         for s in range(4):
+            sync_states(d, torch, M)
             d.step(torch)
             lg = device_read(torch, ptrs["logits"], (CFG["vocab"],), np.float32).astype(np.float64)
             ref, rtok = M.step(tok, pos)
@@ -143,6 +161,35 @@ def test_decode_steps_match_oracle(pkg, cuda, O, prefill):
                 assert rel(st, M.S[il, "rec_state"]) <= TOL, il
                 cs = d.param(torch, il, "conv_state").astype(np.float64).reshape(3, -1)
                 assert rel(cs, M.S[il, "conv_state"]) <= TOL, il
+    finally:
+        d.close()
+
+
+def test_prompt_then_greedy_generation(pkg, cuda, O):
+    """dec_set_prompt: a new sequence (zero states) fed the prompt's tokens,
+    then its own argmax; every step's prediction lands in the history."""
+    torch = cuda
+    d = Dec(pkg)
+    try:
+        prompt = [5, 900, 17, 17, 333]
+        arr = C.cast((C.c_int32 * len(prompt))(*prompt), C.c_void_p)
+        assert d.L.dec_set_prompt(d.h, arr, len(prompt), None) == 0
+        M = oracle_from(d, torch, O)
+        assert not any(np.any(M.S[k]) for k in M.S if k[1] in ("conv_state", "rec_state"))
+        ptrs = d.pointers()
+        tok = prompt[0]
+        for pos in range(len(prompt) + 3):
+            sync_states(d, torch, M)
+            d.step(torch)
+            lg = device_read(torch, ptrs["logits"], (CFG["vocab"],), np.float32).astype(np.float64)
+            ref, rtok = M.step(tok, pos)
+            assert rel(lg, ref) <= TOL, (pos, rel(lg, ref))
+            hist = device_read(torch, ptrs["hist"], (CFG["max_ctx"],), np.int32)
+            assert hist[pos] == int(np.argmax(lg))
+            tok = prompt[pos + 1] if pos + 1 < len(prompt) else int(hist[pos])
+        assert d.L.dec_set_prompt(d.h, arr, 0, None) == -11
+        bad = C.cast((C.c_int32 * 1)(CFG["vocab"]), C.c_void_p)
+        assert d.L.dec_set_prompt(d.h, bad, 1, None) == -11
     finally:
         d.close()
 

@@ -245,6 +245,32 @@ def test_g128_vs_double_oracle(cuda, pkg, shape):
     assert np.all(e16 <= 2.0 ** -11 * np.abs(ref) + 1e-4 * amax)
 
 
+@pytest.mark.parametrize("shape", [(2048, 2048), (512, 6144), (37, 384)])
+def test_g128_staging_contract(cuda, pkg, shape):
+    """The g128 kernel's only approximation besides fp32 summation is its
+    activation staging (int16 on a per-128-column exponent, oracle/dec_oracle.py
+    stage_g128): against the double product of the STAGED x the fp32 output
+    agrees to 2e-6 of max|y|, with x spanning many octaves inside each group
+    (where staging and fp16 differ most)."""
+    from oracle import dec_oracle as D
+    torch = cuda
+    M, K = shape
+    wq, sc, _ = _g128_operands(torch, pkg, 1, M, K)
+    g = torch.Generator().manual_seed(M)
+    xs = (torch.randn(K, generator=g) * torch.exp2(torch.randint(-14, 3, (K,), generator=g).float())).half()
+    xs[:5] = 0
+    x = xs.cuda().reshape(1, K)
+    _, y32 = _g128_run(torch, pkg, wq, sc, x, M, K)
+    w = O.matvec_g128_f64
+    xh = xs.numpy()
+    ref_staged = D.dequant_g128(wq[0].cpu().numpy(), sc[0].cpu().numpy().view(np.uint16)) @ \
+        D.stage_g128(xh.astype(np.float64))
+    ref_exact = w(wq[0].cpu().numpy(), sc[0].cpu().numpy(), xh, K)
+    amax = np.max(np.abs(ref_exact))
+    assert np.max(np.abs(y32[0] - ref_staged)) <= 2e-6 * amax
+    assert np.max(np.abs(y32[0] - ref_exact)) <= 1e-4 * amax
+
+
 def test_g128_stack_equals_single(cuda, pkg):
     """A stack of matrices in one launch gives the per-matrix results."""
     torch = cuda
