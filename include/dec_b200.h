@@ -90,19 +90,21 @@ int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residu
                  int32_t *vocab0, int32_t *vocab_n);
 
 /* Weight arrays of one linear, for the oracle: d_wq [rows][cols/2] packed
- * INT4, d_sc [rows][cols/128] fp16.  Names: "qkv", "z", "ab", "out", "qg",
- * "kv", "o", "gate", "up", "down" (per layer) and "lm_head" (layer -1). */
+ * INT4, d_sc [rows][s_pitch] fp16 (cols/128 used; the pitch keeps every row
+ * 16-byte aligned).  Names: "qkv", "z", "ab", "out", "qg", "kv", "o", "gate",
+ * "up", "down" (per layer) and "lm_head" (layer -1). */
 int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, const uint16_t **d_sc,
-               int32_t *rows, int32_t *cols);
+               int32_t *rows, int32_t *cols, int32_t *s_pitch);
 
 /* Parameter and state vectors: "attn_norm", "post_norm", "conv_w"
  * ([conv_dim][4]), "ssm_a", "dt_bias", "ssm_norm", "q_norm", "k_norm",
  * "conv_state", "rec_state", "kcache", "vcache" (per layer), "final_norm" and
  * the fp16 "embed" [vocab][hidden] (layer -1).  Layer -1 also names the
  * activation seams of the last step, as the last layer to write each left
- * them (the reference's seam records): fp32 "x" (residual), "qkv", "z", "ab",
- * "eg", "beta", "o", "qg", "kv", "q", "gate", "g", "u", "logits"; fp16 "h16"
- * (the last norm output), "qkv16", "y16", "ya16", "hf16". */
+ * them (the reference's seam records): fp32 "x" (residual), "qkv" (the raw
+ * projection), "z", "eg", "beta", "o", "qg", "kv", "q", "gate", "logits"; fp16
+ * "h16" (the last RMSNorm output), "qkv16" (after conv + SiLU), "y16" (DeltaNet
+ * output after norm and gate), "ya16" (attention output), "hf16" (SwiGLU). */
 int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count);
 
 /* Bytes of weights, KV cache and state one step reads on this rank. */

@@ -74,6 +74,9 @@ typedef struct {
                                        already activated (the model's
                                        exp(ssm_a*softplus(.)) and sigmoid);
                                        when set, a and b are not read      */
+    int32_t         pdl;            /* launch as a programmatic dependent of
+                                       the previous kernel in the stream    */
+    int32_t         pad_;
 } gdn_f32_args;
 
 int gdn_run_f32(const gdn_f32_args *a, void *stream);

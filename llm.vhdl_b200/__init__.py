@@ -23,7 +23,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]
 DEC_LIBPATH = os.path.join(LIBDIR, "libdec_b200.so")
-DEC_SOURCES = ["csrc/dec_kernels.cu", "csrc/dec_model.c"]
+DEC_SOURCES = ["csrc/dec_kernels.cu", "csrc/dec_matvec.cu", "csrc/dec_model.c"]
 
 MODE_BFP, MODE_RAW, MODE_PARTIAL = 0, 1, 2
 KIND_GOLDEN, KIND_G128 = 0, 1
@@ -98,7 +98,7 @@ class GdnF32(C.Structure):
                 ("S", C.c_void_p), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
                 ("g", C.c_void_p), ("a", C.c_void_p), ("b", C.c_void_p), ("l2norm", C.c_int32),
                 ("q_scale", C.c_float), ("out_f32", C.c_void_p), ("out_f16", C.c_void_p),
-                ("eg", C.c_void_p), ("beta", C.c_void_p)]
+                ("eg", C.c_void_p), ("beta", C.c_void_p), ("pdl", C.c_int32), ("pad_", C.c_int32)]
 
 
 class Job(C.Structure):
@@ -184,7 +184,8 @@ DEC_EXPORTS = {
                                C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "dec_linear": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_void_p),
-                             C.POINTER(C.c_void_p), C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+                             C.POINTER(C.c_void_p), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                             C.POINTER(C.c_int32)]),
     "dec_param": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_void_p),
                             C.POINTER(C.c_int32)]),
     "dec_step_bytes": (C.c_int64, [C.c_void_p]),

@@ -1,10 +1,11 @@
-// llm.vhdl_b200/csrc/dec_kernels.cu -- the small kernels between projections
-// in a decode step (the vector ops of ref/run9b.c's layer_gdn / layer_attn):
-// embedding gather, RMSNorm to fp16, the DeltaNet conv + SiLU + gate
-// activations, the gated output norm, attention pre-processing (q/k norm,
-// RoPE, KV-cache write), flash-decoding attention with its combine, SwiGLU,
-// residual add, the argmax key and the step advance.  Every kernel reads the
-// position from device memory so a step can be replayed from a CUDA graph.
+// llm.vhdl_b200/csrc/dec_kernels.cu -- the kernels of a decode step that are
+// not projections (the rest are folded into dec_matvec.cu): embedding gather,
+// attention pre-processing (q/k norm, RoPE, KV-cache write), flash-decoding
+// attention with its combine, the tensor-parallel residual add and the step
+// advance; plus the seeded synthetic weights.  Every kernel reads the position
+// from device memory so a step can be replayed from a CUDA graph, and every
+// one may be launched as a programmatic dependent of the kernel before it
+// (it lets the next one launch, then waits for its inputs).
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -13,8 +14,10 @@
 
 extern "C" int mv4i_g_cuda_err;
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float sigm_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#define PDL_ENTER() do { pdl_trigger(); pdl_wait(); } while (0)
 
 // block-wide sum (blockDim.x a multiple of 32, <= 1024); every thread calls it
 __device__ __forceinline__ float block_sum(float v, float *red)
@@ -33,64 +36,10 @@ __device__ __forceinline__ float block_sum(float v, float *red)
 
 __global__ void dec_embed_kernel(const uint16_t *emb, int hidden, const int32_t *tok, float *x)
 {
+    PDL_ENTER();
     const int64_t base = (int64_t)(*tok) * hidden;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x)
         x[i] = __half2float(__ushort_as_half(emb[base + i]));
-}
-
-// y = x * (1/sqrt(mean(x^2) + eps)) * w, ref/run9b.c:557-569, to fp16
-__global__ void __launch_bounds__(1024) dec_rmsnorm_kernel(const float *x, const float *w, int n, float eps, uint16_t *y)
-{
-    __shared__ float red[32];
-    float s = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s = fmaf(x[i], x[i], s);
-    s = block_sum(s, red);
-    const float inv = rsqrtf(s / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
-        y[i] = __half_as_ushort(__float2half_rn(x[i] * inv * w[i]));
-}
-
-// DeltaNet pre-step (ref/run9b.c:634-672): 4-tap causal depthwise conv over
-// the [q | k | v] projection with the rolling state (taps 0..2 on the stored
-// inputs, oldest first, tap 3 on the current one), SiLU, to fp16; per value
-// head beta = sigmoid(b), eg = exp(ssm_a * softplus(a + dt_bias)) (softplus
-// returns x above 20).
-__global__ void dec_gdn_pre_kernel(const float *qkv, int conv_dim, const float *conv_w, float *conv_state,
-                                   uint16_t *qkv16, const float *ab, int vh, const float *ssm_a,
-                                   const float *dt_bias, float *eg, float *beta)
-{
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c < conv_dim) {
-        const float x = qkv[c];
-        const float s0 = conv_state[c], s1 = conv_state[conv_dim + c], s2 = conv_state[2 * conv_dim + c];
-        const float4 w = reinterpret_cast<const float4 *>(conv_w)[c];
-        const float acc = s0 * w.x + s1 * w.y + s2 * w.z + x * w.w;
-        conv_state[c] = s1;
-        conv_state[conv_dim + c] = s2;
-        conv_state[2 * conv_dim + c] = x;
-        qkv16[c] = __half_as_ushort(__float2half_rn(silu_f(acc)));
-    }
-    if (c < vh) {
-        const float av = ab[c] + dt_bias[c], bv = ab[vh + c];
-        const float sp = av > 20.f ? av : log1pf(expf(av));
-        eg[c] = expf(ssm_a[c] * sp);
-        beta[c] = sigm_f(bv);
-    }
-}
-
-// Output norm then gate (ref/run9b.c:708-728): per head rmsnorm(o) * silu(z).
-__global__ void dec_gated_norm_kernel(const float *o, const float *z, const float *w, int hd, float eps,
-                                      uint16_t *y)
-{
-    __shared__ float red[32];
-    const int h = blockIdx.x;
-    const float *oh = o + (size_t)h * hd;
-    float s = 0.f;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) s = fmaf(oh[i], oh[i], s);
-    s = block_sum(s, red);
-    const float inv = rsqrtf(s / (float)hd + eps);
-    for (int i = threadIdx.x; i < hd; i += blockDim.x)
-        y[(size_t)h * hd + i] = __half_as_ushort(__float2half_rn(oh[i] * inv * w[i] * silu_f(z[(size_t)h * hd + i])));
 }
 
 // Attention pre-processing (ref/run9b.c:786-843): q|gate interleaved per
@@ -104,6 +53,7 @@ __global__ void dec_attn_pre_kernel(const float *qg, const float *kv, int qh, in
 {
     __shared__ float red[32];
     __shared__ float buf[512];
+    PDL_ENTER();
     const int hb = blockIdx.x, i = threadIdx.x;
     const int pos = *d_pos;
     const bool isq = hb < qh;
@@ -145,6 +95,7 @@ __global__ void dec_attn_decode_kernel(const float *q, const uint16_t *kcache, c
                                        int qh, int kvh, int hd, int ch, const int32_t *d_pos, int max_ctx,
                                        int nchunks, float *part)
 {
+    PDL_ENTER();
     const int c = blockIdx.x, g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = qh / kvh, h = g * grp + warp;
     const int len = min(*d_pos + 1, max_ctx);
@@ -186,6 +137,7 @@ __global__ void dec_attn_decode_kernel(const float *q, const uint16_t *kcache, c
 __global__ void dec_attn_combine_kernel(const float *part, const float *gate, int hd, int nchunks,
                                         const int32_t *d_pos, int ch, uint16_t *y)
 {
+    PDL_ENTER();
     const int h = blockIdx.x, lane = threadIdx.x;     // 32 threads, 4 dims each
     const int used = min(nchunks, (*d_pos + 1 + ch - 1) / ch);
     float M = -INFINITY;
@@ -207,34 +159,10 @@ __global__ void dec_attn_combine_kernel(const float *part, const float *gate, in
     yo[3] = __half_as_ushort(__float2half_rn(a3 * inv * sigm_f(gv.w)));
 }
 
-// SwiGLU (ref/run9b.c:744): h = silu(gate) * up, to fp16.
-__global__ void dec_swiglu_kernel(const float *g, const float *u, int n, uint16_t *h)
-{
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
-        h[i] = __half_as_ushort(__float2half_rn(silu_f(g[i]) * u[i]));
-}
-
 __global__ void dec_add_kernel(float *x, const float *t, int n)
 {
+    PDL_ENTER();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] += t[i];
-}
-
-// Argmax key of this rank's logits: order-preserving value in the high
-// word, the complemented GLOBAL index in the low word (first max wins).
-__global__ void __launch_bounds__(512) dec_argmax_kernel(const float *v, int n, int idx0, unsigned long long *key)
-{
-    unsigned long long best = 0;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const uint32_t u = __float_as_uint(v[i]);
-        const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-        const unsigned long long kk = ((unsigned long long)k << 32) | (0xFFFFFFFFull - (uint32_t)(idx0 + i));
-        best = kk > best ? kk : best;
-    }
-    for (int o = 16; o; o >>= 1) {
-        const unsigned long long w = __shfl_xor_sync(0xffffffffu, best, o);
-        best = w > best ? w : best;
-    }
-    if ((threadIdx.x & 31) == 0) atomicMax(key, best);
 }
 
 // Pick the largest of `n` keys (one per rank), record it as the prediction
@@ -244,6 +172,7 @@ __global__ void __launch_bounds__(512) dec_argmax_kernel(const float *v, int n, 
 __global__ void dec_advance_kernel(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok,
                                    int32_t *history, int32_t *pos, int max_ctx, const int32_t *prompt)
 {
+    PDL_ENTER();
     unsigned long long best = 0;
     for (int i = 0; i < n; i++) best = keys[i] > best ? keys[i] : best;
     const int32_t t = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
@@ -268,9 +197,10 @@ __device__ __forceinline__ uint64_t d_draw(uint64_t key, uint64_t i)
 
 // INT4 g128 shard: local row r is global row rows[r] (or row0 + r when rows is
 // NULL); local columns [0, kn) are global columns [k0, k0+kn) of a Kg-column
-// matrix.  Same draws as mv4i_synth_g128 for the same key and global index.
+// matrix; scales at row pitch s_pitch.  Same draws as mv4i_synth_g128 for the
+// same key and global index.
 __global__ void dec_synth_linear_kernel(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn,
-                                        int Kg, uint8_t *wq, uint16_t *sc)
+                                        int Kg, uint8_t *wq, uint16_t *sc, int s_pitch)
 {
     const int64_t nb = (int64_t)nrows * (kn / 2);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nb; i += (int64_t)gridDim.x * blockDim.x) {
@@ -286,7 +216,7 @@ __global__ void dec_synth_linear_kernel(uint64_t key, const int32_t *rows, int r
         const int64_t r = i / ng, g = i % ng;
         const int64_t gr = rows ? rows[r] : row0 + r;
         const double u = (double)(d_draw(3 * key + 1, (uint64_t)gr * ngg + k0 / 128 + g) >> 11) * 0x1.0p-53;
-        sc[i] = __half_as_ushort(__float2half_rn((float)(0.002 + 0.018 * u)));
+        sc[r * s_pitch + g] = __half_as_ushort(__float2half_rn((float)(0.002 + 0.018 * u)));
     }
 }
 
@@ -307,80 +237,63 @@ __global__ void dec_synth_vec_kernel(uint64_t key, const int32_t *idx, int64_t i
 
 // ------------------------------------------------------------ launchers
 
-extern "C" {
-
 static int dk(cudaError_t e) { if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; } return 0; }
-#define ST(s) reinterpret_cast<cudaStream_t>(s)
 
-int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s)
-{ dec_embed_kernel<<<(hidden + 255) / 256, 256, 0, ST(s)>>>(emb, hidden, tok, x); return dk(cudaGetLastError()); }
-
-int dec_k_rmsnorm(const float *x, const float *w, int n, float eps, uint16_t *y, void *s)
-{ dec_rmsnorm_kernel<<<1, 1024, 0, ST(s)>>>(x, w, n, eps, y); return dk(cudaGetLastError()); }
-
-int dec_k_gdn_pre(const float *qkv, int conv_dim, const float *conv_w, float *conv_state, uint16_t *qkv16,
-                  const float *ab, int vh, const float *ssm_a, const float *dt_bias, float *eg, float *beta, void *s)
+// launch on `s`, as a programmatic dependent of the previous kernel when pdl
+template <typename... KArgs, typename... Args>
+static int launch(void (*k)(KArgs...), dim3 g, dim3 b, void *s, int pdl, Args... args)
 {
-    const int n = conv_dim > vh ? conv_dim : vh;
-    dec_gdn_pre_kernel<<<(n + 255) / 256, 256, 0, ST(s)>>>(qkv, conv_dim, conv_w, conv_state, qkv16, ab, vh,
-                                                           ssm_a, dt_bias, eg, beta);
-    return dk(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = g;
+    cfg.blockDim = b;
+    cfg.stream = reinterpret_cast<cudaStream_t>(s);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return dk(cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...));
 }
 
-int dec_k_gated_norm(const float *o, const float *z, const float *w, int heads, int hd, float eps, uint16_t *y, void *s)
-{ dec_gated_norm_kernel<<<heads, 128, 0, ST(s)>>>(o, z, w, hd, eps, y); return dk(cudaGetLastError()); }
+extern "C" {
+
+int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s, int pdl)
+{ return launch(dec_embed_kernel, dim3((hidden + 255) / 256), dim3(256), s, pdl, emb, hidden, tok, x); }
 
 int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
                    const float *qn_w, const float *kn_w, const int32_t *d_pos, int max_ctx, float *q_out,
-                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s)
+                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s, int pdl)
 {
-    dec_attn_pre_kernel<<<qh + kvh, ((hd + 31) / 32) * 32, 0, ST(s)>>>(qg, kv, qh, kvh, hd, n_rot, theta, eps, qn_w,
-                                                                      kn_w, d_pos, max_ctx, q_out, gate_out, kcache,
-                                                                      vcache);
-    return dk(cudaGetLastError());
+    return launch(dec_attn_pre_kernel, dim3(qh + kvh), dim3(((hd + 31) / 32) * 32), s, pdl, qg, kv, qh, kvh, hd,
+                  n_rot, theta, eps, qn_w, kn_w, d_pos, max_ctx, q_out, gate_out, kcache, vcache);
 }
 
 int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int qh, int kvh, int hd, int ch,
-                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s)
+                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s, int pdl)
 {
     const int nchunks = (max_ctx + ch - 1) / ch;
-    dec_attn_decode_kernel<<<dim3(nchunks, kvh), 32 * (qh / kvh), 0, ST(s)>>>(q, kc, vc, qh, kvh, hd, ch, d_pos,
-                                                                              max_ctx, nchunks, part);
-    dec_attn_combine_kernel<<<qh, 32, 0, ST(s)>>>(part, gate, hd, nchunks, d_pos, ch, y);
-    return dk(cudaGetLastError());
+    int rc = launch(dec_attn_decode_kernel, dim3(nchunks, kvh), dim3(32 * (qh / kvh)), s, pdl, q, kc, vc, qh, kvh,
+                    hd, ch, d_pos, max_ctx, nchunks, part);
+    if (rc) return rc;
+    return launch(dec_attn_combine_kernel, dim3(qh), dim3(32), s, pdl, part, gate, hd, nchunks, d_pos, ch, y);
 }
 
-int dec_k_swiglu(const float *g, const float *u, int n, uint16_t *h, void *s)
-{ dec_swiglu_kernel<<<(n + 255) / 256, 256, 0, ST(s)>>>(g, u, n, h); return dk(cudaGetLastError()); }
-
-int dec_k_add(float *x, const float *t, int n, void *s)
-{ dec_add_kernel<<<(n + 255) / 256, 256, 0, ST(s)>>>(x, t, n); return dk(cudaGetLastError()); }
-
-int dec_k_argmax(const float *v, int n, int idx0, unsigned long long *key, void *s)
-{
-    dec_argmax_kernel<<<min(296, (n + 511) / 512), 512, 0, ST(s)>>>(v, n, idx0, key);
-    return dk(cudaGetLastError());
-}
+int dec_k_add(float *x, const float *t, int n, void *s, int pdl)
+{ return launch(dec_add_kernel, dim3((n + 255) / 256), dim3(256), s, pdl, x, t, n); }
 
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
-                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s)
-{
-    dec_advance_kernel<<<1, 1, 0, ST(s)>>>(keys, n, key, tok, hist, pos, max_ctx, prompt);
-    return dk(cudaGetLastError());
-}
+                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s, int pdl)
+{ return launch(dec_advance_kernel, dim3(1), dim3(1), s, pdl, keys, n, key, tok, hist, pos, max_ctx, prompt); }
 
 int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
-                       uint8_t *wq, uint16_t *sc, void *s)
+                       uint8_t *wq, uint16_t *sc, int s_pitch, void *s)
 {
-    dec_synth_linear_kernel<<<148 * 8, 256, 0, ST(s)>>>(key, rows, row0, nrows, k0, kn, Kg, wq, sc);
-    return dk(cudaGetLastError());
+    return launch(dec_synth_linear_kernel, dim3(148 * 8), dim3(256), s, 0, key, rows, row0, nrows, k0, kn, Kg, wq,
+                  sc, s_pitch);
 }
 
 int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, float mean, float std,
                     float *f32, uint16_t *f16, void *s)
-{
-    dec_synth_vec_kernel<<<148 * 4, 256, 0, ST(s)>>>(key, idx, idx0, n, mean, std, f32, f16);
-    return dk(cudaGetLastError());
-}
+{ return launch(dec_synth_vec_kernel, dim3(148 * 4), dim3(256), s, 0, key, idx, idx0, n, mean, std, f32, f16); }
 
 }  // extern "C"

@@ -1,0 +1,530 @@
+// llm.vhdl_b200/csrc/dec_matvec.cu -- the INT4 g128 matvec of the decode step.
+//
+// One launch computes up to four projections of the same input vector (the A
+// jobs of ref/run9b.c's layer_gdn / layer_attn, :602-900) with the vector ops
+// around them folded in:
+//   prologue  each CTA builds the fp16 input itself: plain fp16, RMSNorm of the
+//             fp32 residual (ref/run9b.c:557-569), or the DeltaNet output norm
+//             and z gate per 128-wide head (:708-728); then stages it as int16
+//             on a per-128-column exponent (the g128 contract of
+//             mv4i_kernels.cu) in shared memory.
+//   epilogue  per output row: fp32 / fp16 store, residual accumulate, SwiGLU of
+//             paired gate/up rows (:744), the DeltaNet 4-tap conv + SiLU with its
+//             rolling state (:634-672), the decay/beta gates (:674-683), or the
+//             LM head's first-max argmax key (:399-405).
+// Work split: tiles of 8 rows (one warp per row, or per gate/up row pair),
+// contiguous tile ranges per CTA, a grid of at most one wave; a warp streams
+// up to 4 rows at a time, lanes over 64-column pairs, one batch of loads
+// ahead.  Launched as a programmatic dependent of the previous kernel: the
+// first weights are requested before waiting for it (they do not depend on
+// it), and the next kernel may launch at once.
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <math.h>
+#include "dec_internal.h"
+
+extern "C" int mv4i_g_cuda_err;
+
+#define DMV_THREADS 256
+#define DMV_WARPS 8
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+
+// 32 bytes of streamed weights (read once: no L1 allocation)
+__device__ __forceinline__ void ld_w32(const uint8_t *p, uint32_t (&w)[8])
+{
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+        : "l"(p));
+}
+
+// a 16-bit scale, issued in program order with the weight loads
+__device__ __forceinline__ float ld_scale(const uint16_t *p)
+{
+    unsigned short v;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return __half2float(__ushort_as_half(v));
+}
+
+__device__ __forceinline__ int dp_uu(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm volatile("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp_us(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm volatile("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float block_sum(float v, float *red)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    v = l < DMV_WARPS ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ int to_i16(float f, int e)
+{
+    return (int)fminf(fmaxf(rintf(ldexpf(f, e)), -32768.f), 32767.f);
+}
+
+// Shared memory (K columns, np = K/64 pairs of 32-column blocks, ng = K/128):
+//   planes  uint4 [4 planes][2 block parities][np]: the int16 x split into
+//           low bytes (unsigned) and high bytes (signed) of even / odd
+//           columns; word q of a block holds columns 8q + {0,2,4,6} (+1)
+//   psum    int   [np]  sum of the staged int16 x over the pair
+//   gfac    float [ng]  2^-e of each group
+struct Sm {
+    uint4 *planes; int *psum; float *gfac;
+};
+
+__host__ __device__ __forceinline__ size_t r16(size_t n) { return (n + 15) & ~(size_t)15; }
+
+__device__ __forceinline__ Sm sm_layout(uint8_t *sm, int K)
+{
+    const size_t np = K >> 6;
+    Sm s;
+    s.planes = reinterpret_cast<uint4 *>(sm);
+    s.psum = reinterpret_cast<int *>(sm + 128 * np);
+    s.gfac = reinterpret_cast<float *>(sm + 128 * np + r16(4 * np));
+    return s;
+}
+
+__host__ __device__ __forceinline__ size_t dmv_smem_x_bytes(int K)
+{
+    const size_t np = K >> 6, ng = K >> 7;
+    return 128 * np + r16(4 * np) + r16(4 * ng);
+}
+
+// the 8 fp32 inputs of unit u (columns 8u .. 8u+7): x (fp16 / fp32
+// residual / DeltaNet o) and, for the gated prologue, z
+__device__ __forceinline__ void unit_load(const dmv_params &P, int u, bool ok, float (&v)[8], float (&z)[8])
+{
+    if (!ok) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) { v[k] = 0.f; z[k] = 0.f; }
+        return;
+    }
+    if (P.op == DMV_OP_F16) {
+        const uint4 r = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(P.x) + 8 * u);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[k]));
+            v[2 * k] = f.x; v[2 * k + 1] = f.y;
+        }
+    } else {
+        const float4 *x = reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) + 8 * u);
+        const float4 a = x[0], b = x[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        if (P.op == DMV_OP_GATED) {
+            const float4 *zp = reinterpret_cast<const float4 *>(P.x2 + 8 * u);
+            const float4 c = zp[0], d = zp[1];
+            z[0] = c.x; z[1] = c.y; z[2] = c.z; z[3] = c.w; z[4] = d.x; z[5] = d.y; z[6] = d.z; z[7] = d.w;
+        }
+    }
+}
+
+// Stage x: unit u = 8 columns per thread, so a 128-column group is 16
+// consecutive lanes (a half warp) and a 64-column pair 8 lanes: group max,
+// pair sums and per-head norms are shuffle reductions.
+__device__ void dmv_stage(const dmv_params &P, const Sm &s)
+{
+    __shared__ float red[32];
+    const int K = P.K, np = K >> 6, nu = K >> 3, tid = threadIdx.x;
+    float inv = 0.f;
+    if (P.op == DMV_OP_RMSNORM) {
+        const float *x = static_cast<const float *>(P.x);
+        float a = 0.f;
+        for (int i = 4 * tid; i < K; i += 4 * DMV_THREADS) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + i);
+            a = fmaf(v.x, v.x, a); a = fmaf(v.y, v.y, a); a = fmaf(v.z, v.z, a); a = fmaf(v.w, v.w, a);
+        }
+        a = block_sum(a, red);
+        inv = rsqrtf(a / (float)K + P.eps);
+    }
+    uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
+    for (int u0 = 0; u0 < nu; u0 += DMV_THREADS) {        // uniform trip count: shuffles below
+        const int u = u0 + tid;
+        const bool ok = u < nu;                             // whole half warps (nu % 16 == 0)
+        float v[8], z[8];
+        unit_load(P, u, ok, v, z);
+        if (P.op == DMV_OP_RMSNORM) {
+            if (ok) {
+                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + 8 * u);
+                const float4 a = wp[0], b = wp[1];
+                const float w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[k] = v[k] * inv * w[k];
+            }
+        } else if (P.op == DMV_OP_GATED) {
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float ginv = rsqrtf(ss / 128.f + P.eps);
+            if (ok) {
+                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + ((8 * u) & 127));
+                const float4 a = wp[0], b = wp[1];
+                const float w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[k] = v[k] * ginv * w[k] * silu_f(z[k]);
+            }
+        }
+        // fp16 rounding (the storage contract), then the group exponent
+        uint32_t hw[4];
+        float m = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+            hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
+            const float2 f = __half22float2(h2);
+            v[2 * k] = f.x; v[2 * k + 1] = f.y;
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        int e = 0;
+        if (m > 0.f) { int ex; frexpf(m, &ex); e = 15 - ex; }    // m in [2^(ex-1), 2^ex)
+        int xi[8], ssum = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], e); ssum += xi[k]; }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+        if (ok) {
+            uint32_t le = 0, lo = 0, he = 0, ho = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                le |= (uint32_t)(xi[2 * t] & 0xFF) << (8 * t);
+                he |= (uint32_t)((xi[2 * t] >> 8) & 0xFF) << (8 * t);
+                lo |= (uint32_t)(xi[2 * t + 1] & 0xFF) << (8 * t);
+                ho |= (uint32_t)((xi[2 * t + 1] >> 8) & 0xFF) << (8 * t);
+            }
+            const int b = u >> 2, q = u & 3, p = b >> 1, par = b & 1;
+            pw[4 * ((0 + par) * np + p) + q] = le;
+            pw[4 * ((2 + par) * np + p) + q] = lo;
+            pw[4 * ((4 + par) * np + p) + q] = he;
+            pw[4 * ((6 + par) * np + p) + q] = ho;
+            if (!(u & 7)) s.psum[u >> 3] = ssum;
+            if (!(u & 15)) s.gfac[u >> 4] = ldexpf(1.0f, -e);
+            if (blockIdx.x == 0 && P.seam)
+                *reinterpret_cast<uint4 *>(P.seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+    }
+    __syncthreads();
+}
+
+// sum_j cb_j * x_j over the 64 columns of pair p; w[0..3] block 2p, w[4..7]
+// block 2p+1; cb = (nibble ^ 8) - 8, x = 256 * hi + lo.
+__device__ __forceinline__ void pair_dot4(const uint32_t (&w)[8], const uint4 (&xp)[8], int (&a)[4])
+{
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint4 xle = xp[0 + half], xlo = xp[2 + half], xhe = xp[4 + half], xho = xp[6 + half];
+        const uint32_t le[4] = {xle.x, xle.y, xle.z, xle.w}, lo[4] = {xlo.x, xlo.y, xlo.z, xlo.w};
+        const uint32_t he[4] = {xhe.x, xhe.y, xhe.z, xhe.w}, ho[4] = {xho.x, xho.y, xho.z, xho.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint32_t wv = w[4 * half + q];
+            const uint32_t e = (wv & 0x0F0F0F0Fu) ^ 0x08080808u;     // idx^8 of even columns
+            const uint32_t o = (wv & 0xF0F0F0F0u) ^ 0x80808080u;     // 16*(idx^8) of odd columns
+            a[0] = dp_uu(e, le[q], a[0]);
+            a[1] = dp_uu(o, lo[q], a[1]);
+            a[2] = dp_us(e, he[q], a[2]);
+            a[3] = dp_us(o, ho[q], a[3]);
+        }
+    }
+}
+
+// the job descriptors live in shared memory (kernel parameters indexed at
+// run time would be read through memory loads in the inner loop)
+__device__ __forceinline__ int dmv_job_of(const dmv_params &P, const dmv_job *JS, int t)
+{
+    int j = 0;
+    for (int i = 1; i < P.njobs; i++) if (t >= JS[i].tile0) j = i;
+    return j;
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx)
+{
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)k << 32) | (0xFFFFFFFFull - (uint32_t)idx);
+}
+
+// per-row epilogue (lane 0); v2 is the paired row's value
+__device__ __forceinline__ void dmv_epilogue(const dmv_params &P, const dmv_job &J, int row, float v, float v2,
+                                             unsigned long long &best)
+{
+    switch (J.epi) {
+    case DMV_EPI_F32: J.out_f32[row] = v; break;
+    case DMV_EPI_ACC: J.out_f32[row] += v; break;
+    case DMV_EPI_F16:
+        J.out_f16[row] = __half_as_ushort(__float2half_rn(v));
+        if (J.out_f32) J.out_f32[row] = v;
+        break;
+    case DMV_EPI_SWIGLU:
+        J.out_f16[row] = __half_as_ushort(__float2half_rn(silu_f(v) * v2));
+        break;
+    case DMV_EPI_CONV: {
+        // taps 0..2 on the stored inputs (oldest first), tap 3 on this one
+        float *st = J.st;
+        const int S = J.st_stride;
+        const float s0 = st[row], s1 = st[S + row], s2 = st[2 * S + row];
+        const float4 cw = reinterpret_cast<const float4 *>(J.p0)[row];
+        const float a = s0 * cw.x + s1 * cw.y + s2 * cw.z + v * cw.w;
+        st[row] = s1; st[S + row] = s2; st[2 * S + row] = v;
+        J.out_f16[row] = __half_as_ushort(__float2half_rn(silu_f(a)));
+        if (J.out_f32) J.out_f32[row] = v;
+        break;
+    }
+    case DMV_EPI_GATES:
+        if (row < J.n1) {
+            const float av = v + J.p1[row];
+            const float sp = av > 20.f ? av : log1pf(expf(av));
+            J.out_f32[row] = expf(J.p0[row] * sp);
+        } else {
+            J.out2_f32[row - J.n1] = 1.0f / (1.0f + expf(-v));
+        }
+        break;
+    case DMV_EPI_ARGMAX: {
+        J.out_f32[row] = v;
+        const unsigned long long k = argmax_key(v, P.idx0 + row);
+        best = k > best ? k : best;
+        break;
+    }
+    default: break;
+    }
+}
+
+// ------------------------------------------------------------ the stream
+//
+// A CTA owns a contiguous range of tiles; within each job it meets, warp w
+// takes row w of every tile, G rows at a time (G = 4, or 2 gate/up pairs),
+// and each lane one 64-column pair of each row per batch (a 32-byte load; a
+// warp reads 1 KB per row and batch).  The x planes of a pair are read once
+// for the G rows.  The first weights are requested (into L2) before the
+// kernel waits for its predecessor: they do not depend on it.
+
+template <int NR>
+__device__ __forceinline__ void dmv_loads(const uint8_t *const (&wr)[NR], const uint16_t *const (&sr)[NR], int p,
+                                          bool on, uint32_t (&w)[NR][8], float (&sc)[NR])
+{
+#pragma unroll
+    for (int k = 0; k < NR; k++) {
+        if (on) {
+            ld_w32(wr[k] + 32 * (size_t)p, w[k]);
+            sc[k] = ld_scale(sr[k] + (p >> 1));
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; q++) w[k][q] = 0;
+            sc[k] = 0.f;
+        }
+    }
+}
+
+template <int NR>
+__device__ __forceinline__ void dmv_dots(const Sm &s, int np, int p, const uint32_t (&w)[NR][8],
+                                         const float (&sc)[NR], float (&acc)[NR])
+{
+    uint4 xp[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) xp[k] = s.planes[k * np + p];
+    const int sx = s.psum[p];
+    const float gf = s.gfac[p >> 1];
+#pragma unroll
+    for (int k = 0; k < NR; k++) {
+        int a[4] = {0, 0, 0, 0};
+        pair_dot4(w[k], xp, a);
+        const int part = a[0] + (a[1] >> 4) + (a[2] + (a[3] >> 4)) * 256 - 8 * sx;   // a1, a3: x16
+        acc[k] = fmaf((float)part, sc[k] * gf, acc[k]);
+    }
+}
+
+// rows of job J in tiles [ta, tb) for this warp; NR dot products per group:
+// 4 rows, or (PAIRED) 2 rows of gate and up
+template <bool PAIRED>
+__device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &J, const Sm &s, int ta, int tb,
+                                            int warp, int lane, int np, size_t wpitch, unsigned long long &best)
+{
+    constexpr int G = PAIRED ? 2 : 4;
+    constexpr int NR = 4;
+    for (int t = ta; t < tb; t += G) {
+        const int g = min(G, tb - t);
+        const uint8_t *wr[NR];
+        const uint16_t *sr[NR];
+        int rows[G];
+#pragma unroll
+        for (int i = 0; i < G; i++) {
+            rows[i] = (t + min(i, g - 1) - J.tile0) * DMV_WARPS + warp;
+            const int rr = min(rows[i], J.rows - 1);            // past the end: a valid row, discarded
+            if (PAIRED) {
+                wr[2 * i] = J.wq + (size_t)rr * wpitch;  sr[2 * i] = J.sc + (size_t)rr * J.s_pitch;
+                wr[2 * i + 1] = J.wq2 + (size_t)rr * wpitch; sr[2 * i + 1] = J.sc2 + (size_t)rr * J.s_pitch;
+            } else {
+                wr[i] = J.wq + (size_t)rr * wpitch; sr[i] = J.sc + (size_t)rr * J.s_pitch;
+            }
+        }
+        float acc[NR] = {0.f, 0.f, 0.f, 0.f};
+        for (int pb = 0; pb < np; pb += 32) {
+            const int p = pb + lane;
+            uint32_t w[NR][8];
+            float sc[NR];
+            dmv_loads<NR>(wr, sr, p, p < np, w, sc);
+            if (p < np) dmv_dots<NR>(s, np, p, w, sc, acc);
+        }
+#pragma unroll
+        for (int k = 0; k < NR; k++)
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < G; i++)
+                if (i < g && rows[i] < J.rows)
+                    dmv_epilogue(P, J, rows[i], PAIRED ? acc[2 * i] : acc[i], PAIRED ? acc[2 * i + 1] : 0.f, best);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(DMV_THREADS, 2) dmv_kernel(const __grid_constant__ dmv_params P)
+{
+    extern __shared__ __align__(128) uint8_t dmv_sm[];
+    __shared__ dmv_job JS[DMV_MAXJ];
+    if (threadIdx.x < P.njobs) JS[threadIdx.x] = P.jobs[threadIdx.x];
+    __syncthreads();
+    const int T = P.total_tiles;
+    const int t0 = (int)((int64_t)blockIdx.x * T / gridDim.x);
+    const int t1 = (int)((int64_t)(blockIdx.x + 1) * T / gridDim.x);
+    const int K = P.K, np = K >> 6;
+    const size_t wpitch = (size_t)K >> 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int j0 = dmv_job_of(P, JS, min(t0, T - 1));
+    // weights do not depend on the previous kernel: ask L2 for the first
+    // ones now
+    if (threadIdx.x == 0 && P.pf_bytes > 0) {
+        int64_t budget = P.pf_bytes;
+        for (int t = t0; t < t1 && budget > 0;) {
+            const dmv_job &J = JS[dmv_job_of(P, JS, t)];
+            const int te = min(t1, J.tile0 + J.ntiles);
+            const int r0 = (t - J.tile0) * DMV_WARPS;
+            const int r1 = min(J.rows, (te - J.tile0) * DMV_WARPS);
+            int64_t bytes = (int64_t)(r1 - r0) * (int64_t)wpitch;
+            if (bytes > budget) bytes = budget & ~(int64_t)15;
+            for (int m = 0; m < (J.wq2 ? 2 : 1); m++) {
+                const uint8_t *base = (m ? J.wq2 : J.wq) + (size_t)r0 * wpitch;
+                for (int64_t off = 0; off < bytes; off += 65536)
+                    prefetch_l2(base + off, (uint32_t)min((int64_t)65536, bytes - off));
+            }
+            budget -= bytes * (J.wq2 ? 2 : 1);
+            t = te;
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
+
+    const Sm s = sm_layout(dmv_sm, K);
+    dmv_stage(P, s);
+
+    unsigned long long best = 0;
+    for (int j = j0; j < P.njobs && t0 < t1; j++) {
+        const dmv_job &J = JS[j];
+        const int ta = max(t0, J.tile0), tb = min(t1, J.tile0 + J.ntiles);
+        if (ta >= tb) continue;
+        if (J.wq2) dmv_segment<true>(P, J, s, ta, tb, warp, lane, np, wpitch, best);
+        else dmv_segment<false>(P, J, s, ta, tb, warp, lane, np, wpitch, best);
+    }
+    if (best) atomicMax(P.key, best);
+}
+
+extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
+{
+    if (!p || p->njobs < 1 || p->njobs > DMV_MAXJ || p->K < 128 || (p->K & 127) || p->K > 32768 || !p->x)
+        return -11;
+    if (p->op == DMV_OP_RMSNORM && !p->nw) return -11;
+    if (p->op == DMV_OP_GATED && (!p->nw || !p->x2)) return -11;
+    if (p->op < DMV_OP_F16 || p->op > DMV_OP_GATED) return -11;
+    dmv_params P = *p;
+    int tiles = 0;
+    for (int j = 0; j < P.njobs; j++) {
+        dmv_job &J = P.jobs[j];
+        if (!J.wq || !J.sc || J.rows <= 0) return -11;
+        if ((((uintptr_t)J.wq) & 15) || (J.wq2 && (((uintptr_t)J.wq2) & 15))) return -11;
+        if ((((uintptr_t)J.sc) & 15) || (J.sc2 && (((uintptr_t)J.sc2) & 15))) return -11;
+        if ((J.s_pitch & 7) || J.s_pitch < ((P.K / 128 + 7) & ~7)) return -11;
+        switch (J.epi) {
+        case DMV_EPI_F32: case DMV_EPI_ACC: if (!J.out_f32) return -11; break;
+        case DMV_EPI_F16: if (!J.out_f16) return -11; break;
+        case DMV_EPI_SWIGLU: if (!J.out_f16 || !J.wq2 || !J.sc2) return -11; break;
+        case DMV_EPI_CONV: if (!J.out_f16 || !J.st || !J.p0 || J.st_stride < J.rows) return -11; break;
+        case DMV_EPI_GATES: if (!J.out_f32 || !J.out2_f32 || !J.p0 || !J.p1 || J.n1 <= 0 || J.n1 > J.rows)
+                                return -11;
+                            break;
+        case DMV_EPI_ARGMAX: if (!J.out_f32 || !P.key) return -11; break;
+        default: return -11;
+        }
+        if (J.epi != DMV_EPI_SWIGLU && J.wq2) return -11;
+        J.tile0 = tiles;
+        J.ntiles = (J.rows + DMV_WARPS - 1) / DMV_WARPS;
+        tiles += J.ntiles;
+    }
+    P.total_tiles = tiles;
+    const size_t smem = dmv_smem_x_bytes(P.K);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+    static int s_sms[64], s_occ[64][4], s_attr[64];
+    static size_t s_occ_smem[64][4];
+    if (dev < 0 || dev >= 64) return -11;
+    if (!s_attr[dev]) {
+        e = cudaFuncSetAttribute(dmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+        s_attr[dev] = 1;
+    }
+    int occ = 0;
+    for (int i = 0; i < 4; i++) if (s_occ[dev][i] && s_occ_smem[dev][i] == smem) occ = s_occ[dev][i];
+    if (!occ) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dmv_kernel, DMV_THREADS, smem);
+        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+        if (occ < 1) occ = 1;
+        for (int i = 0; i < 4; i++)
+            if (!s_occ[dev][i]) { s_occ[dev][i] = occ; s_occ_smem[dev][i] = smem; break; }
+    }
+    int grid = s_sms[dev] * occ;
+    if (grid > tiles) grid = tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(DMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, dmv_kernel, P);
+    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+    return 0;
+}

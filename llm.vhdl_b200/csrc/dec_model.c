@@ -20,27 +20,23 @@
 #include "../../include/mv4i_b200.h"
 #include "../../include/gdn_b200.h"
 #include "../../include/dec_b200.h"
+#include "dec_internal.h"
 
 extern int mv4i_g_cuda_err;
 
-/* kernels in dec_kernels.cu */
-int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s);
-int dec_k_rmsnorm(const float *x, const float *w, int n, float eps, uint16_t *y, void *s);
-int dec_k_gdn_pre(const float *qkv, int conv_dim, const float *conv_w, float *conv_state, uint16_t *qkv16,
-                  const float *ab, int vh, const float *ssm_a, const float *dt_bias, float *eg, float *beta, void *s);
-int dec_k_gated_norm(const float *o, const float *z, const float *w, int heads, int hd, float eps, uint16_t *y, void *s);
+/* kernels in dec_kernels.cu (pdl: launch as a programmatic dependent) */
+int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s, int pdl);
 int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
                    const float *qn_w, const float *kn_w, const int32_t *d_pos, int max_ctx, float *q_out,
-                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s);
+                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s, int pdl);
 int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int qh, int kvh, int hd, int ch,
-                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s);
-int dec_k_swiglu(const float *g, const float *u, int n, uint16_t *h, void *s);
-int dec_k_add(float *x, const float *t, int n, void *s);
-int dec_k_argmax(const float *v, int n, int idx0, unsigned long long *key, void *s);
+                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s,
+                    int pdl);
+int dec_k_add(float *x, const float *t, int n, void *s, int pdl);
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
-                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s);
+                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s, int pdl);
 int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
-                       uint8_t *wq, uint16_t *sc, void *s);
+                       uint8_t *wq, uint16_t *sc, int s_pitch, void *s);
 int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, float mean, float std,
                     float *f32, uint16_t *f16, void *s);
 
@@ -53,7 +49,7 @@ typedef struct {
     mv4i_dmat w;
     uint8_t  *wq;
     uint16_t *sc;
-    int32_t   rows, cols;
+    int32_t   rows, cols, s_pitch;   /* scales [rows][s_pitch], 16-byte rows */
 } linear_t;
 
 typedef struct {
@@ -77,8 +73,9 @@ struct dec_model {
     float    *final_norm;
     uint16_t *embed;
     /* activations */
-    float    *x, *t, *qkv_f, *z_f, *ab_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *gate_f, *part, *g_f, *u_f, *logits;
+    float    *x, *t, *qkv_f, *z_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *gate_f, *part, *logits;
     uint16_t *h16, *qkv16, *y16, *ya16, *hf16;
+    int       pdl;                       /* programmatic dependent launches     */
     unsigned long long *key, *keys;
     int32_t  *tok, *pos, *hist;
     int32_t  *prompt;                    /* [0] = length, [1..] = tokens     */
@@ -118,14 +115,14 @@ static int to_device_i32(dec_model *m, int32_t **d, const int32_t *h, size_t n)
 static int make_linear(dec_model *m, linear_t *l, uint64_t key, const int32_t *h_rows, int row0, int nrows,
                        int k0, int kn, int Kg)
 {
-    l->rows = nrows; l->cols = kn;
+    l->rows = nrows; l->cols = kn; l->s_pitch = ((kn / 128) + 7) & ~7;
     CK(dalloc(m, (void **)&l->wq, (size_t)nrows * kn / 2));
-    CK(dalloc(m, (void **)&l->sc, (size_t)nrows * (kn / 128) * 2));
+    CK(dalloc(m, (void **)&l->sc, (size_t)nrows * l->s_pitch * 2));
     int32_t *d_rows = NULL;
     if (h_rows) CK(to_device_i32(m, &d_rows, h_rows, (size_t)nrows));
-    CK(dec_k_synth_linear(key, d_rows, row0, nrows, k0, kn, Kg, l->wq, l->sc, NULL));
-    CK(mv4i_dmat_wrap_g128(l->wq, kn / 2, l->sc, kn / 128, nrows, kn, m->device, &l->w));
-    m->weight_bytes += (int64_t)nrows * kn / 2 + (int64_t)nrows * (kn / 128) * 2;
+    CK(dec_k_synth_linear(key, d_rows, row0, nrows, k0, kn, Kg, l->wq, l->sc, l->s_pitch, NULL));
+    CK(mv4i_dmat_wrap_g128(l->wq, kn / 2, l->sc, l->s_pitch, nrows, kn, m->device, &l->w));
+    m->weight_bytes += (int64_t)nrows * kn / 2 + (int64_t)nrows * (kn / 128) * 2;   /* bytes read */
     return 0;
 }
 
@@ -152,6 +149,7 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     dec_model *m = (dec_model *)calloc(1, sizeof *m);
     if (!m) return -11;
     m->c = *c; m->device = device; m->rank = tp_rank; m->world = tp_world;
+    { const char *e = getenv("DEC_PDL"); m->pdl = !(e && e[0] == '0'); }
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) { free(m); return fail(e); }
     const int W = tp_world, R = tp_rank;
@@ -234,7 +232,6 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->qkv_f, 4 * (size_t)m->conv_dim));
     TRY(dalloc(m, (void **)&m->qkv16, 2 * (size_t)m->conv_dim));
     TRY(dalloc(m, (void **)&m->z_f, 4 * (size_t)m->vh * HD));
-    TRY(dalloc(m, (void **)&m->ab_f, 4 * 2 * (size_t)m->vh));
     TRY(dalloc(m, (void **)&m->eg, 4 * (size_t)m->vh));
     TRY(dalloc(m, (void **)&m->beta, 4 * (size_t)m->vh));
     TRY(dalloc(m, (void **)&m->o_f, 4 * (size_t)m->vh * HD));
@@ -245,8 +242,6 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->gate_f, 4 * (size_t)m->qh * HD));
     TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 4)));
     TRY(dalloc(m, (void **)&m->ya16, 2 * (size_t)m->qh * HD));
-    TRY(dalloc(m, (void **)&m->g_f, 4 * (size_t)m->ffn));
-    TRY(dalloc(m, (void **)&m->u_f, 4 * (size_t)m->ffn));
     TRY(dalloc(m, (void **)&m->hf16, 2 * (size_t)m->ffn));
     TRY(dalloc(m, (void **)&m->logits, 4 * (size_t)m->vocab));
     TRY(dalloc(m, (void **)&m->key, 8));
@@ -372,26 +367,32 @@ int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream)
     return 0;
 }
 
-static void job(mv4i_job *j, const linear_t *l, const void *x, float *y, int accum)
+#define PF_BYTES (48 * 1024)
+
+static void mvjob(dmv_job *J, const linear_t *l, int epi)
 {
-    memset(j, 0, sizeof *j);
-    j->w = &l->w; j->x = x; j->n_rows = l->rows; j->n_cols = l->cols; j->nvec = 1;
-    j->y_f32 = y; j->accum = accum;
+    memset(J, 0, sizeof *J);
+    J->wq = l->wq; J->sc = l->sc; J->rows = l->rows; J->epi = epi; J->s_pitch = l->s_pitch;
 }
 
-/* row-parallel block: a single GPU adds into x directly; TP sums partials */
-static int row_parallel(dec_model *m, const linear_t *l, const void *x16, void *s)
+static void mvparams(dmv_params *P, int K, int op, const void *x, const float *nw, float eps, uint16_t *seam)
 {
-    mv4i_job j;
-    if (m->world == 1) {
-        job(&j, l, x16, m->x, 1);
-        return mv4i_launch(&j, 1, NULL, s);
-    }
-    job(&j, l, x16, m->t, 0);
-    CK(mv4i_launch(&j, 1, NULL, s));
+    memset(P, 0, sizeof *P);
+    P->K = K; P->op = op; P->x = x; P->nw = nw; P->eps = eps; P->seam = seam; P->pf_bytes = PF_BYTES;
+}
+
+/* row-parallel block: a single GPU adds into the residual in the matvec
+ * epilogue; tensor parallel sums the partials with one NCCL all-reduce */
+static int row_parallel(dec_model *m, dmv_params *P, const linear_t *l, void *s)
+{
+    mvjob(&P->jobs[0], l, m->world == 1 ? DMV_EPI_ACC : DMV_EPI_F32);
+    P->jobs[0].out_f32 = m->world == 1 ? m->x : m->t;
+    P->njobs = 1;
+    CK(dec_k_matvec(P, s, m->pdl));
+    if (m->world == 1) return 0;
     if (ncclAllReduce(m->t, m->t, (size_t)m->c.hidden, ncclFloat32, ncclSum, m->comm, (cudaStream_t)s)
         != ncclSuccess) return -20;
-    return dec_k_add(m->x, m->t, m->c.hidden, s);
+    return dec_k_add(m->x, m->t, m->c.hidden, s, m->pdl);
 }
 
 int dec_step(dec_model *m, void *s)
@@ -401,54 +402,70 @@ int dec_step(dec_model *m, void *s)
     if (m->hpos >= m->c.max_ctx) return -11;   /* the KV cache is full */
     m->hpos++;
     const dec_config *c = &m->c;
-    const int H = c->hidden;
-    mv4i_job jobs[4];
-    CK(dec_k_embed(m->embed, H, m->tok, m->x, s));
+    const int H = c->hidden, pdl = m->pdl && s != NULL;   /* not on the legacy default stream */
+    dmv_params P;
+    CK(dec_k_embed(m->embed, H, m->tok, m->x, s, pdl));
     for (int il = 0; il < c->n_layers; il++) {
         layer_t *l = &m->L[il];
-        CK(dec_k_rmsnorm(m->x, l->attn_norm, H, c->rms_eps, m->h16, s));
+        mvparams(&P, H, DMV_OP_RMSNORM, m->x, l->attn_norm, c->rms_eps, m->h16);
         if (!l->attn) {
-            job(&jobs[0], &l->qkv, m->h16, m->qkv_f, 0);
-            job(&jobs[1], &l->z, m->h16, m->z_f, 0);
-            job(&jobs[2], &l->ab, m->h16, m->ab_f, 0);
-            CK(mv4i_launch(jobs, 3, NULL, s));
-            CK(dec_k_gdn_pre(m->qkv_f, m->conv_dim, l->conv_w, l->conv_state, m->qkv16, m->ab_f, m->vh,
-                             l->ssm_a, l->dt_bias, m->eg, m->beta, s));
+            /* q|k|v with the conv + SiLU epilogue, z, and a|b with the gates */
+            mvjob(&P.jobs[0], &l->qkv, DMV_EPI_CONV);
+            P.jobs[0].out_f16 = m->qkv16; P.jobs[0].out_f32 = m->qkv_f;
+            P.jobs[0].p0 = l->conv_w; P.jobs[0].st = l->conv_state; P.jobs[0].st_stride = m->conv_dim;
+            mvjob(&P.jobs[1], &l->z, DMV_EPI_F32);
+            P.jobs[1].out_f32 = m->z_f;
+            mvjob(&P.jobs[2], &l->ab, DMV_EPI_GATES);
+            P.jobs[2].out_f32 = m->eg; P.jobs[2].out2_f32 = m->beta;
+            P.jobs[2].p0 = l->ssm_a; P.jobs[2].p1 = l->dt_bias; P.jobs[2].n1 = m->vh;
+            P.njobs = 3;
+            CK(dec_k_matvec(&P, s, pdl));
             gdn_f32_args g;
             memset(&g, 0, sizeof g);
             g.T = 1; g.H = m->vh; g.KH = m->kh; g.D = HD; g.S = l->rec_state;
             g.q = m->qkv16; g.k = m->qkv16 + (size_t)m->kh * HD; g.v = m->qkv16 + (size_t)2 * m->kh * HD;
             g.g = NULL; g.eg = m->eg; g.beta = m->beta; g.l2norm = 1; g.q_scale = 1.0f / sqrtf((float)HD);
-            g.out_f32 = m->o_f;
+            g.out_f32 = m->o_f; g.pdl = pdl;
             CK(gdn_run_f32(&g, s));
-            CK(dec_k_gated_norm(m->o_f, m->z_f, l->ssm_norm, m->vh, HD, c->rms_eps, m->y16, s));
-            CK(row_parallel(m, &l->out, m->y16, s));
+            /* output norm and z gate folded into the out projection */
+            mvparams(&P, m->vh * HD, DMV_OP_GATED, m->o_f, l->ssm_norm, c->rms_eps, m->y16);
+            P.x2 = m->z_f;
+            CK(row_parallel(m, &P, &l->out, s));
         } else {
-            job(&jobs[0], &l->qg, m->h16, m->qg_f, 0);
-            job(&jobs[1], &l->kv, m->h16, m->kv_f, 0);
-            CK(mv4i_launch(jobs, 2, NULL, s));
+            mvjob(&P.jobs[0], &l->qg, DMV_EPI_F32);
+            P.jobs[0].out_f32 = m->qg_f;
+            mvjob(&P.jobs[1], &l->kv, DMV_EPI_F32);
+            P.jobs[1].out_f32 = m->kv_f;
+            P.njobs = 2;
+            CK(dec_k_matvec(&P, s, pdl));
             CK(dec_k_attn_pre(m->qg_f, m->kv_f, m->qh, m->kvh, HD, c->n_rot, c->rope_theta, c->rms_eps,
-                              l->q_norm, l->k_norm, m->pos, c->max_ctx, m->q_f, m->gate_f, l->kcache, l->vcache, s));
+                              l->q_norm, l->k_norm, m->pos, c->max_ctx, m->q_f, m->gate_f, l->kcache, l->vcache,
+                              s, pdl));
             CK(dec_k_attention(m->q_f, l->kcache, l->vcache, m->qh, m->kvh, HD, ATT_CHUNK, c->max_ctx, m->pos,
-                               m->part, m->gate_f, m->ya16, s));
-            CK(row_parallel(m, &l->o, m->ya16, s));
+                               m->part, m->gate_f, m->ya16, s, pdl));
+            mvparams(&P, m->qh * HD, DMV_OP_F16, m->ya16, NULL, 0.f, NULL);
+            CK(row_parallel(m, &P, &l->o, s));
         }
-        CK(dec_k_rmsnorm(m->x, l->post_norm, H, c->rms_eps, m->h16, s));
-        job(&jobs[0], &l->gate, m->h16, m->g_f, 0);
-        job(&jobs[1], &l->up, m->h16, m->u_f, 0);
-        CK(mv4i_launch(jobs, 2, NULL, s));
-        CK(dec_k_swiglu(m->g_f, m->u_f, m->ffn, m->hf16, s));
-        CK(row_parallel(m, &l->down, m->hf16, s));
+        /* SwiGLU: gate and up rows paired in one warp, silu(g)*u in the epilogue */
+        mvparams(&P, H, DMV_OP_RMSNORM, m->x, l->post_norm, c->rms_eps, m->h16);
+        mvjob(&P.jobs[0], &l->gate, DMV_EPI_SWIGLU);
+        P.jobs[0].wq2 = l->up.wq; P.jobs[0].sc2 = l->up.sc; P.jobs[0].out_f16 = m->hf16;
+        P.njobs = 1;
+        CK(dec_k_matvec(&P, s, pdl));
+        mvparams(&P, m->ffn, DMV_OP_F16, m->hf16, NULL, 0.f, NULL);
+        CK(row_parallel(m, &P, &l->down, s));
     }
-    CK(dec_k_rmsnorm(m->x, m->final_norm, H, c->rms_eps, m->h16, s));
-    job(&jobs[0], &m->lm, m->h16, m->logits, 0);
-    CK(mv4i_launch(jobs, 1, NULL, s));
-    CK(dec_k_argmax(m->logits, m->vocab, m->voc0, m->key, s));
+    /* LM head with the first-max argmax key in its epilogue */
+    mvparams(&P, H, DMV_OP_RMSNORM, m->x, m->final_norm, c->rms_eps, m->h16);
+    mvjob(&P.jobs[0], &m->lm, DMV_EPI_ARGMAX);
+    P.jobs[0].out_f32 = m->logits;
+    P.key = m->key; P.idx0 = m->voc0; P.njobs = 1;
+    CK(dec_k_matvec(&P, s, pdl));
     if (m->world > 1) {
         if (ncclAllGather(m->key, m->keys, 1, ncclUint64, m->comm, (cudaStream_t)s) != ncclSuccess) return -20;
-        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s);
+        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);
     }
-    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s);
+    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);
 }
 
 int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residual, int32_t **pos,
@@ -465,7 +482,7 @@ int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residu
 }
 
 int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, const uint16_t **d_sc,
-               int32_t *rows, int32_t *cols)
+               int32_t *rows, int32_t *cols, int32_t *s_pitch)
 {
     if (!m || !name) return -11;
     const linear_t *l = NULL;
@@ -480,6 +497,7 @@ int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, 
     }
     if (!l) return -11;
     *d_wq = l->wq; *d_sc = l->sc; *rows = l->rows; *cols = l->cols;
+    if (s_pitch) *s_pitch = l->s_pitch;
     return 0;
 }
 
@@ -492,12 +510,11 @@ int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int
             {"final_norm", m->final_norm, H}, {"embed", m->embed, m->c.vocab * H},
             /* activation seams of the last step (the last layer that wrote them) */
             {"x", m->x, H}, {"h16", m->h16, H}, {"qkv", m->qkv_f, m->conv_dim},
-            {"qkv16", m->qkv16, m->conv_dim}, {"z", m->z_f, m->vh * HD}, {"ab", m->ab_f, 2 * m->vh},
+            {"qkv16", m->qkv16, m->conv_dim}, {"z", m->z_f, m->vh * HD},
             {"eg", m->eg, m->vh}, {"beta", m->beta, m->vh}, {"o", m->o_f, m->vh * HD},
             {"y16", m->y16, m->vh * HD}, {"qg", m->qg_f, 2 * m->qh * HD}, {"kv", m->kv_f, 2 * m->kvh * HD},
             {"q", m->q_f, m->qh * HD}, {"gate", m->gate_f, m->qh * HD}, {"ya16", m->ya16, m->qh * HD},
-            {"g", m->g_f, m->ffn}, {"u", m->u_f, m->ffn}, {"hf16", m->hf16, m->ffn},
-            {"logits", m->logits, m->vocab}};
+            {"hf16", m->hf16, m->ffn}, {"logits", m->logits, m->vocab}};
         for (unsigned i = 0; i < sizeof act / sizeof act[0]; i++)
             if (!strcmp(name, act[i].n)) { *d_ptr = act[i].p; *count = act[i].c; return 0; }
         return -11;

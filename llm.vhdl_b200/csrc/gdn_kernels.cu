@@ -367,6 +367,10 @@ gdn_f32_kernel(const gdn_f32_args A)
     const int j = (blockIdx.x & 7) * 16 + warp * 4 + (lane >> 3);
     const int sl = lane & 7, i0 = 16 * sl;
     const int hk = h % A.KH;
+    // a programmatic dependent of the previous kernel: let the next one
+    // launch, then wait for this one's inputs (no-ops otherwise)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float *scol = A.S + ((size_t)h * 128 + j) * 128 + i0;
     float s[16];
 #pragma unroll
@@ -438,7 +442,15 @@ extern "C" int gdn_run_f32(const gdn_f32_args *a, void *stream)
     if (!a || a->D != 128 || a->T <= 0 || a->H <= 0 || a->KH <= 0 || !a->S || !a->q || !a->k || !a->v
         || (!a->eg && !a->a) || (!a->beta && !a->b) || (!a->out_f32 && !a->out_f16)) return -11;
     if ((((uintptr_t)a->S) | ((uintptr_t)a->q) | ((uintptr_t)a->k)) & 15) return -11;
-    gdn_f32_kernel<<<a->H * 8, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*a);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a->H * 8);
+    cfg.blockDim = dim3(128);
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a->pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_f32_kernel, *a);
     return e == cudaSuccess ? 0 : gdn_fail(e);
 }

@@ -53,12 +53,14 @@ class Dec:
             self.h = C.c_void_p()
 
     def linear(self, torch, layer, name):
-        wq, sc, r, k = C.c_void_p(), C.c_void_p(), C.c_int32(), C.c_int32()
-        rc = self.L.dec_linear(self.h, layer, name.encode(), C.byref(wq), C.byref(sc), C.byref(r), C.byref(k))
+        wq, sc, r, k, sp = C.c_void_p(), C.c_void_p(), C.c_int32(), C.c_int32(), C.c_int32()
+        rc = self.L.dec_linear(self.h, layer, name.encode(), C.byref(wq), C.byref(sc), C.byref(r), C.byref(k),
+                               C.byref(sp))
         assert rc == 0, (layer, name)
-        r, k = r.value, k.value
+        r, k, sp = r.value, k.value, sp.value
+        assert sp % 8 == 0 and sp >= k // 128
         return (device_read(torch, wq.value, (r, k // 2), np.uint8),
-                device_read(torch, sc.value, (r, k // 128), np.uint16))
+                device_read(torch, sc.value, (r, sp), np.uint16)[:, :k // 128].copy())
 
     def param(self, torch, layer, name, dtype=np.float32):
         p, n = C.c_void_p(), C.c_int32()

@@ -1,8 +1,10 @@
-"""Seam tests: each vector kernel of the decode step on identical inputs
-against the oracle's restatement of the same ref/run9b.c stage
-(oracle/dec_oracle.py), within 1e-3 of the largest magnitude (fp32 arithmetic,
-fp16 outputs) -- bit-exact for the argmax.  The kernels are the library's
-internal launchers (exported from libdec_b200.so, not part of the header)."""
+"""Seam tests: the attention kernels and the step advance of the decode step
+on identical inputs against the oracle's restatement of the same ref/run9b.c
+stage (oracle/dec_oracle.py), within 1e-3 of the largest magnitude (fp32
+arithmetic, fp16 outputs); the advance bit-exact.  The kernels are the
+library's internal launchers (exported from libdec_b200.so, not part of the
+header).  The projections and the vector ops folded into them are covered by
+tests/test_dec_matvec_gpu.py."""
 import ctypes as C
 
 import numpy as np
@@ -18,14 +20,9 @@ def K(pkg):
     L = pkg.declib()
     P, I, F, U64 = C.c_void_p, C.c_int, C.c_float, C.c_uint64
     sig = {
-        "dec_k_rmsnorm": [P, P, I, F, P, P],
-        "dec_k_gdn_pre": [P, I, P, P, P, P, I, P, P, P, P, P],
-        "dec_k_gated_norm": [P, P, P, I, I, F, P, P],
-        "dec_k_attn_pre": [P, P, I, I, I, I, F, F, P, P, P, I, P, P, P, P, P],
-        "dec_k_attention": [P, P, P, I, I, I, I, I, P, P, P, P, P],
-        "dec_k_swiglu": [P, P, I, P, P],
-        "dec_k_argmax": [P, I, I, P, P],
-        "dec_k_advance": [P, I, P, P, P, P, I, P, P],
+        "dec_k_attn_pre": [P, P, I, I, I, I, F, F, P, P, P, I, P, P, P, P, P, I],
+        "dec_k_attention": [P, P, P, I, I, I, I, I, P, P, P, P, P, I],
+        "dec_k_advance": [P, I, P, P, P, P, I, P, P, I],
     }
     for n, a in sig.items():
         getattr(L, n).argtypes = a
@@ -51,63 +48,6 @@ def O():
     return dec_oracle
 
 
-def test_rmsnorm_and_swiglu(cuda, K, O):
-    torch = cuda
-    g = torch.Generator().manual_seed(1)
-    for n in (256, 2048, 5120, 16384):
-        x = torch.randn(n, generator=g, dtype=torch.float64) * 3
-        w = 1 + 0.1 * torch.randn(n, generator=g, dtype=torch.float64)
-        y = torch.zeros(n, dtype=torch.int16, device="cuda")
-        xd, wd = x.float().cuda(), w.float().cuda()
-        assert K.dec_k_rmsnorm(ptr(xd), ptr(wd), n, 1e-6, ptr(y), None) == 0
-        ref = O.rmsnorm(xd.double().cpu().numpy(), wd.double().cpu().numpy(), 1e-6)
-        assert rel(h16(y), ref) <= TOL, n
-        u = torch.randn(n, generator=g).cuda()
-        assert K.dec_k_swiglu(ptr(xd), ptr(u), n, ptr(y), None) == 0
-        ref = O.silu(xd.double().cpu().numpy()) * u.double().cpu().numpy()
-        assert rel(h16(y), ref) <= TOL, n
-
-
-def test_gdn_pre_conv_and_gates(cuda, K, O):
-    torch = cuda
-    g = torch.Generator().manual_seed(2)
-    kh, vh = 2, 6
-    cd = 2 * kh * HD + vh * HD
-    qkv = torch.randn(cd, generator=g)
-    cw = 0.5 * torch.randn(cd * 4, generator=g)
-    cs = 0.5 * torch.randn(3, cd, generator=g)
-    ab = torch.randn(2 * vh, generator=g) * 4
-    ab[0] = 30.0                                               # softplus passthrough branch
-    a = -1 + 0.2 * torch.randn(vh, generator=g)
-    dt = 0.5 * torch.randn(vh, generator=g)
-    d = {k: v.cuda() for k, v in dict(qkv=qkv, cw=cw, cs=cs, ab=ab, a=a, dt=dt).items()}
-    q16 = torch.zeros(cd, dtype=torch.int16, device="cuda")
-    eg, beta = torch.zeros(vh, device="cuda"), torch.zeros(vh, device="cuda")
-    assert K.dec_k_gdn_pre(ptr(d["qkv"]), cd, ptr(d["cw"]), ptr(d["cs"]), ptr(q16), ptr(d["ab"]), vh,
-                           ptr(d["a"]), ptr(d["dt"]), ptr(eg), ptr(beta), None) == 0
-    n = {k: v.double().numpy() for k, v in dict(qkv=qkv, cw=cw, cs=cs, ab=ab, a=a, dt=dt).items()}
-    w = n["cw"].reshape(cd, 4)
-    acc = n["cs"][0] * w[:, 0] + n["cs"][1] * w[:, 1] + n["cs"][2] * w[:, 2] + n["qkv"] * w[:, 3]
-    assert rel(h16(q16), O.silu(acc)) <= TOL
-    assert np.array_equal(d["cs"].cpu().numpy(), np.stack([cs[1].numpy(), cs[2].numpy(), qkv.numpy()]))
-    e_ref = np.exp(O.softplus(n["ab"][:vh] + n["dt"]) * n["a"])
-    assert rel(eg.double().cpu().numpy(), e_ref) <= TOL
-    assert rel(beta.double().cpu().numpy(), O.sigmoid(n["ab"][vh:])) <= TOL
-
-
-def test_gated_norm(cuda, K, O):
-    torch = cuda
-    g = torch.Generator().manual_seed(3)
-    H = 5
-    o, z = torch.randn(H * HD, generator=g), 2 * torch.randn(H * HD, generator=g)
-    w = 1 + 0.1 * torch.randn(HD, generator=g)
-    y = torch.zeros(H * HD, dtype=torch.int16, device="cuda")
-    assert K.dec_k_gated_norm(ptr(o.cuda()), ptr(z.cuda()), ptr(w.cuda()), H, HD, 1e-6, ptr(y), None) == 0
-    on, zn, wn = o.double().numpy().reshape(H, HD), z.double().numpy().reshape(H, HD), w.double().numpy()
-    ref = np.stack([O.rmsnorm(on[i], wn, 1e-6) * O.silu(zn[i]) for i in range(H)]).reshape(-1)
-    assert rel(h16(y), ref) <= TOL
-
-
 @pytest.mark.parametrize("pos", [0, 1, 77, 4095])
 def test_attn_pre_norm_rope_and_cache_write(cuda, K, O, pos):
     torch = cuda
@@ -120,7 +60,7 @@ def test_attn_pre_norm_rope_and_cache_write(cuda, K, O, pos):
     kc = torch.zeros(ctx * kvh * HD, dtype=torch.int16, device="cuda")
     vc = torch.zeros_like(kc)
     assert K.dec_k_attn_pre(ptr(qg.cuda()), ptr(kv.cuda()), qh, kvh, HD, nrot, theta, 1e-6, ptr(qn.cuda()),
-                            ptr(kn.cuda()), ptr(dpos), ctx, ptr(qo), ptr(go), ptr(kc), ptr(vc), None) == 0
+                            ptr(kn.cuda()), ptr(dpos), ctx, ptr(qo), ptr(go), ptr(kc), ptr(vc), None, 0) == 0
 
     def rope(r):
         r = r.copy()
@@ -160,7 +100,7 @@ def test_flash_decoding_attention(cuda, K, O, qh, kvh, pos, ctx):
     dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
     kcd, vcd = kc.cuda(), vc.cuda()
     assert K.dec_k_attention(ptr(q.cuda()), ptr(kcd), ptr(vcd), qh, kvh, HD, ch, ctx, ptr(dpos), ptr(part),
-                             ptr(gate.cuda()), ptr(y), None) == 0
+                             ptr(gate.cuda()), ptr(y), None, 0) == 0
     qn = q.double().numpy().reshape(qh, HD)
     kn, vn = kc.double().numpy()[:pos + 1], vc.double().numpy()[:pos + 1]
     ref = np.empty((qh, HD))
@@ -188,36 +128,28 @@ def test_attention_past_capacity_reads_only_the_cache(cuda, K):
     for p, y in ((ctx - 1, ya), (ctx + 50, yb)):
         dpos = torch.tensor([p], dtype=torch.int32, device="cuda")
         assert K.dec_k_attention(ptr(q), ptr(kc), ptr(vc), qh, kvh, HD, 64, ctx, ptr(dpos), ptr(part), ptr(gate),
-                                 ptr(y), None) == 0
+                                 ptr(y), None, 0) == 0
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
 
 
-def test_argmax_first_max_across_shards(cuda, K):
-    """First maximum wins (ref/run9b.c:399-405), also across vocabulary shards
-    whose keys are combined by dec_k_advance."""
+def test_advance_picks_first_max_key_and_follows_the_prompt(cuda, K):
+    """The largest key wins (keys of equal value: the lower global index,
+    ref/run9b.c:399-405); while a prompt lasts its next token is the input."""
     torch = cuda
-    V, W = 151936, 4
-    v = torch.randn(V, generator=torch.Generator().manual_seed(9))
-    v[1000] = v[120000] = v[77777] = 9.0                      # a three-way tie
-    v[5] = -1e30
-    vd = v.cuda()
-    n = V // W
-    keys = torch.zeros(W, dtype=torch.int64, device="cuda")
-    for r in range(W):
-        key = torch.zeros(1, dtype=torch.int64, device="cuda")
-        assert K.dec_k_argmax(C.c_void_p(vd.data_ptr() + 4 * r * n), n, r * n, ptr(key), None) == 0
-        keys[r] = key[0]
+    keys = torch.tensor([5 << 32 | 0xFFFFFFFF - 900, 7 << 32 | 0xFFFFFFFF - 1200, 7 << 32 | 0xFFFFFFFF - 40],
+                        dtype=torch.int64, device="cuda")
     tok = torch.zeros(1, dtype=torch.int32, device="cuda")
     hist = torch.zeros(8, dtype=torch.int32, device="cuda")
     pos = torch.tensor([3], dtype=torch.int32, device="cuda")
-    key = torch.zeros(1, dtype=torch.int64, device="cuda")
-    assert K.dec_k_advance(ptr(keys), W, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, None, None) == 0
+    key = torch.ones(1, dtype=torch.int64, device="cuda")
+    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, None, None, 0) == 0
     torch.cuda.synchronize()
-    assert int(tok.item()) == 1000 and int(hist[3].item()) == 1000 and int(pos.item()) == 4
-    vn = -torch.arange(V, dtype=torch.float32)                # all negative: max at index 0
-    key = torch.zeros(1, dtype=torch.int64, device="cuda")
-    assert K.dec_k_argmax(ptr(vn.cuda()), V, 0, ptr(key), None) == 0
-    assert K.dec_k_advance(ptr(key), 1, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, None, None) == 0
+    assert int(tok.item()) == 40 and int(hist[3].item()) == 40 and int(pos.item()) == 4 and int(key.item()) == 0
+    prompt = torch.tensor([6, 11, 12, 13, 14, 15, 16], dtype=torch.int32, device="cuda")   # length 6
+    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), None, 0) == 0
     torch.cuda.synchronize()
-    assert int(tok.item()) == 0
+    assert int(hist[4].item()) == 40 and int(tok.item()) == 16 and int(pos.item()) == 5     # prompt[1 + 5]
+    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), None, 0) == 0
+    torch.cuda.synchronize()
+    assert int(tok.item()) == 40 and int(pos.item()) == 6                                    # prompt over

@@ -1,0 +1,323 @@
+"""The decode-step matvec (llm.vhdl_b200/csrc/dec_matvec.cu) against the oracle.
+
+Each prologue (fp16 input, RMSNorm of the residual, DeltaNet output norm x
+silu(z) per head) and each epilogue (fp32 / fp16 store, residual accumulate,
+paired SwiGLU, conv + SiLU with its rolling state, decay / beta gates, LM-head
+argmax key) is compared with oracle/dec_oracle.py on identical inputs:
+
+* the staged product is exact up to fp32 summation: against the double
+  product of the g128-staged fp16 input (oracle stage_g128) the output agrees to
+  2e-6 of its largest magnitude;
+* the fp16 input a prologue builds (read back through the seam pointer) equals
+  the oracle's fp16 rounding of the same expression except for values within
+  fp32 rounding of an fp16 boundary (at most 1 ulp, at most 1% of them);
+* epilogue nonlinearities within 1e-3 of the largest magnitude, argmax exact.
+
+Launches are also chained as programmatic dependents (PDL) with each consuming
+the previous one's output, which must give the same answer as plain launches.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+P_ = C.c_void_p
+EPI = dict(F32=0, ACC=1, F16=2, SWIGLU=3, CONV=4, GATES=5, ARGMAX=6)
+OP = dict(F16=0, RMSNORM=1, GATED=2)
+
+
+class Job(C.Structure):
+    _fields_ = [("wq", P_), ("wq2", P_), ("sc", P_), ("sc2", P_), ("out_f32", P_), ("out2_f32", P_),
+                ("out_f16", P_), ("p0", P_), ("p1", P_), ("st", P_), ("st_stride", C.c_int32),
+                ("n1", C.c_int32), ("rows", C.c_int32), ("epi", C.c_int32), ("tile0", C.c_int32),
+                ("ntiles", C.c_int32), ("s_pitch", C.c_int32), ("pad_", C.c_int32)]
+
+
+class Params(C.Structure):
+    _fields_ = [("jobs", Job * 4), ("njobs", C.c_int32), ("total_tiles", C.c_int32), ("K", C.c_int32),
+                ("op", C.c_int32), ("x", P_), ("x2", P_), ("nw", P_), ("eps", C.c_float), ("seam", P_),
+                ("key", P_), ("idx0", C.c_int32), ("pf_bytes", C.c_int32)]
+
+
+@pytest.fixture(scope="module")
+def L(pkg):
+    D = pkg.declib()
+    D.dec_k_matvec.argtypes = [C.POINTER(Params), P_, C.c_int]
+    D.dec_k_matvec.restype = C.c_int
+    return D
+
+
+@pytest.fixture(scope="module")
+def O():
+    from oracle import dec_oracle
+    return dec_oracle
+
+
+def dp(t):
+    return t.data_ptr() if t is not None else None
+
+
+def spitch(K):
+    return (K // 128 + 7) & ~7
+
+
+class Scales:
+    """fp16 scales [rows][K/128] stored at a 16-byte row pitch (the kernel's
+    layout); .t is the padded device tensor, .v the [rows][K/128] view."""
+
+    def __init__(self, v):
+        rows, ng = v.shape
+        self.t = torch_mod().zeros(rows, spitch(128 * ng), dtype=v.dtype, device=v.device)
+        self.t[:, :ng] = v
+        self.v = self.t[:, :ng]
+
+    def data_ptr(self):
+        return self.t.data_ptr()
+
+    def __getitem__(self, i):
+        return self.v[i]
+
+    def __setitem__(self, i, val):
+        self.v[i] = val
+
+
+def torch_mod():
+    import torch
+    return torch
+
+
+def weights(torch, rows, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    wq = torch.randint(0, 256, (rows, K // 2), generator=g, dtype=torch.uint8)
+    sc = (0.002 + 0.018 * torch.rand(rows, K // 128, generator=g)).half()
+    return wq.cuda(), Scales(sc.cuda())
+
+
+def deq(O, wq, sc):
+    return O.dequant_g128(wq.cpu().numpy(), sc.v.cpu().numpy().view(np.uint16))
+
+
+def run(L, torch, p, pdl=0):
+    rc = L.dec_k_matvec(C.byref(p), None, pdl)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+
+
+def rel(a, b):
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def seam_ok(got16, want):
+    """fp16 seam vs the oracle's fp16 of the same fp64 expression."""
+    w16 = want.astype(np.float16)
+    g = got16.astype(np.float16)
+    diff = g != w16
+    if np.any(diff):
+        ulp = np.abs(np.spacing(w16[diff]).astype(np.float64))
+        assert np.all(np.abs(g[diff].astype(np.float64) - w16[diff].astype(np.float64)) <= ulp * 1.01)
+    assert np.mean(diff) <= 0.01, np.mean(diff)
+
+
+@pytest.mark.parametrize("K,rows", [(128, 1), (2048, 7), (2048, 2048), (5120, 33), (17408, 64), (6144, 300)])
+def test_f16_input_staged_product(cuda, L, O, K, rows):
+    torch = cuda
+    wq, sc = weights(torch, rows, K, K + rows)
+    g = torch.Generator().manual_seed(K)
+    x = (torch.randn(K, generator=g) * torch.exp2(torch.randint(-10, 3, (K,), generator=g).float())).half().cuda()
+    y32 = torch.zeros(rows, device="cuda")
+    y16 = torch.zeros(rows, dtype=torch.int16, device="cuda")
+    acc = torch.randn(rows, generator=g).cuda()
+    acc0 = acc.clone()
+    p = Params(K=K, op=OP["F16"], x=dp(x), njobs=3, pf_bytes=65536)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F32"], out_f32=dp(y32))
+    p.jobs[1] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F16"], out_f16=dp(y16))
+    p.jobs[2] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["ACC"], out_f32=dp(acc))
+    run(L, torch, p)
+    W = deq(O, wq, sc)
+    xs = O.stage_g128(x.cpu().numpy().astype(np.float64))
+    ref = W @ xs
+    got = y32.cpu().numpy().astype(np.float64)
+    assert rel(got, ref) <= 2e-6
+    assert rel(W @ x.cpu().numpy().astype(np.float64), got) <= 1e-4      # the staging's own cost
+    assert np.array_equal(y16.cpu().numpy().view(np.float16), got.astype(np.float32).astype(np.float16))
+    assert np.allclose((acc - acc0).cpu().numpy(), got, rtol=0, atol=1e-6 * np.max(np.abs(got)))
+
+
+@pytest.mark.parametrize("K", [256, 2048, 5120])
+def test_rmsnorm_prologue_and_seam(cuda, L, O, K):
+    torch = cuda
+    rows = 300
+    wq, sc = weights(torch, rows, K, 7 + K)
+    g = torch.Generator().manual_seed(K + 1)
+    res = (torch.randn(K, generator=g) * 3).cuda()
+    w = (1 + 0.1 * torch.randn(K, generator=g)).cuda()
+    seam = torch.zeros(K, dtype=torch.int16, device="cuda")
+    y = torch.zeros(rows, device="cuda")
+    p = Params(K=K, op=OP["RMSNORM"], x=dp(res), nw=dp(w), eps=1e-6, seam=dp(seam), njobs=1)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F32"], out_f32=dp(y))
+    run(L, torch, p)
+    h16 = seam.cpu().numpy().view(np.float16)
+    seam_ok(h16, O.rmsnorm(res.double().cpu().numpy(), w.double().cpu().numpy(), 1e-6))
+    ref = deq(O, wq, sc) @ O.stage_g128(h16.astype(np.float64))
+    assert rel(y.cpu().numpy().astype(np.float64), ref) <= 2e-6
+
+
+def test_gated_prologue(cuda, L, O):
+    torch = cuda
+    H, rows = 6, 256
+    K = H * 128
+    wq, sc = weights(torch, rows, K, 11)
+    g = torch.Generator().manual_seed(12)
+    o = torch.randn(K, generator=g) * torch.exp2(torch.randint(-6, 2, (H, 1), generator=g).float()).repeat(1, 128).reshape(-1)
+    z = 2 * torch.randn(K, generator=g)
+    w = 1 + 0.1 * torch.randn(128, generator=g)
+    seam = torch.zeros(K, dtype=torch.int16, device="cuda")
+    y = torch.zeros(rows, device="cuda")
+    od, zd, wd = o.cuda(), z.cuda(), w.cuda()
+    p = Params(K=K, op=OP["GATED"], x=dp(od), x2=dp(zd), nw=dp(wd), eps=1e-6, seam=dp(seam), njobs=1)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F32"], out_f32=dp(y))
+    run(L, torch, p)
+    on, zn, wn = o.double().numpy().reshape(H, 128), z.double().numpy().reshape(H, 128), w.double().numpy()
+    want = np.stack([O.rmsnorm(on[i], wn, 1e-6) * O.silu(zn[i]) for i in range(H)]).reshape(-1)
+    y16 = seam.cpu().numpy().view(np.float16)
+    seam_ok(y16, want)
+    ref = deq(O, wq, sc) @ O.stage_g128(y16.astype(np.float64))
+    assert rel(y.cpu().numpy().astype(np.float64), ref) <= 2e-6
+
+
+def test_paired_swiglu_epilogue(cuda, L, O):
+    torch = cuda
+    K, F = 2048, 640
+    wg, sg = weights(torch, F, K, 21)
+    wu, su = weights(torch, F, K, 22)
+    x = torch.randn(K, generator=torch.Generator().manual_seed(23)).half().cuda()
+    h = torch.zeros(F, dtype=torch.int16, device="cuda")
+    p = Params(K=K, op=OP["F16"], x=dp(x), njobs=1)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wg), wq2=dp(wu), sc=dp(sg), sc2=dp(su), rows=F, epi=EPI["SWIGLU"], out_f16=dp(h))
+    run(L, torch, p)
+    xs = O.stage_g128(x.cpu().numpy().astype(np.float64))
+    want = O.silu(deq(O, wg, sg) @ xs) * (deq(O, wu, su) @ xs)
+    got = h.cpu().numpy().view(np.float16).astype(np.float64)
+    assert np.all(np.abs(got - want) <= 2.0 ** -10 * np.abs(want) + 1e-6 * np.max(np.abs(want)))
+
+
+def test_conv_and_gate_epilogues(cuda, L, O):
+    """q|k|v channels: 4-tap conv over the rolling state + SiLU to fp16 and
+    the state shifted; a|b rows: decay exp(ssm_a * softplus(a + dt_bias))
+    (softplus passes x through above 20) and sigmoid beta."""
+    torch = cuda
+    K, cd, vh = 1024, 768, 6
+    g = torch.Generator().manual_seed(31)
+    wc, scc = weights(torch, cd, K, 32)
+    wa, sa = weights(torch, 2 * vh, K, 33)
+    x = torch.randn(K, generator=g).half().cuda()
+    cw = (0.5 * torch.randn(cd * 4, generator=g)).cuda()
+    st = (0.5 * torch.randn(3 * (cd + 16), generator=g)).cuda()        # stride cd + 16
+    st0 = st.clone()
+    ssm_a = (-1 + 0.2 * torch.randn(vh, generator=g)).cuda()
+    dt = (0.5 * torch.randn(vh, generator=g)).cuda()
+    dt[0] = 40.0                                                        # the passthrough branch
+    q16 = torch.zeros(cd, dtype=torch.int16, device="cuda")
+    raw = torch.zeros(cd, device="cuda")
+    eg, beta = torch.zeros(vh, device="cuda"), torch.zeros(vh, device="cuda")
+    p = Params(K=K, op=OP["F16"], x=dp(x), njobs=2)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wc), sc=dp(scc), rows=cd, epi=EPI["CONV"], out_f16=dp(q16), out_f32=dp(raw),
+                    p0=dp(cw), st=dp(st), st_stride=cd + 16)
+    p.jobs[1] = Job(s_pitch=spitch(K), wq=dp(wa), sc=dp(sa), rows=2 * vh, epi=EPI["GATES"], out_f32=dp(eg), out2_f32=dp(beta),
+                    p0=dp(ssm_a), p1=dp(dt), n1=vh)
+    run(L, torch, p)
+    xs = O.stage_g128(x.cpu().numpy().astype(np.float64))
+    proj = deq(O, wc, scc) @ xs
+    assert rel(raw.cpu().numpy().astype(np.float64), proj) <= 2e-6
+    S = st0.cpu().numpy().astype(np.float64).reshape(3, cd + 16)[:, :cd]
+    w4 = cw.cpu().numpy().astype(np.float64).reshape(cd, 4)
+    r = raw.cpu().numpy().astype(np.float64)
+    acc = S[0] * w4[:, 0] + S[1] * w4[:, 1] + S[2] * w4[:, 2] + r * w4[:, 3]
+    seam_ok(q16.cpu().numpy().view(np.float16), O.silu(acc))
+    S1 = st.cpu().numpy().reshape(3, cd + 16)
+    S0 = st0.cpu().numpy().reshape(3, cd + 16)
+    assert np.array_equal(S1[0, :cd], S0[1, :cd]) and np.array_equal(S1[1, :cd], S0[2, :cd])
+    assert np.array_equal(S1[2, :cd], raw.cpu().numpy())
+    assert np.array_equal(S1[:, cd:], S0[:, cd:])                       # padding untouched
+    ab = deq(O, wa, sa) @ xs
+    e_ref = np.exp(ssm_a.double().cpu().numpy() * O.softplus(ab[:vh] + dt.double().cpu().numpy()))
+    assert rel(eg.double().cpu().numpy(), e_ref) <= 1e-5
+    assert rel(beta.double().cpu().numpy(), O.sigmoid(ab[vh:])) <= 1e-5
+
+
+def test_argmax_epilogue_first_max(cuda, L, O):
+    """Logits and the first-max key; duplicated rows tie exactly and the lower
+    global index must win (ref/run9b.c:399-405)."""
+    torch = cuda
+    K, V = 2048, 20000
+    wq, sc = weights(torch, V, K, 41)
+    x = torch.randn(K, generator=torch.Generator().manual_seed(42)).half().cuda()
+    xs = O.stage_g128(x.cpu().numpy().astype(np.float64))
+    top = int(np.argmax(deq(O, wq, sc) @ xs))
+    wq[17000] = wq[top]                                  # a later row with the same weights ties
+    sc[17000] = sc[top]
+    wq[3] = wq[top]                                      # an earlier one wins the tie
+    sc[3] = sc[top]
+    logits = torch.zeros(V, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    p = Params(K=K, op=OP["F16"], x=dp(x), njobs=1, key=dp(key), idx0=5000)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=V, epi=EPI["ARGMAX"], out_f32=dp(logits))
+    run(L, torch, p)
+    lg = logits.cpu().numpy()
+    assert lg[3] == lg[top] == lg[17000]
+    k = int(key.item()) & 0xFFFFFFFF
+    assert 0xFFFFFFFF - k == 5000 + min(3, top)
+    assert rel(lg.astype(np.float64), deq(O, wq, sc) @ xs) <= 2e-6
+
+
+def test_programmatic_dependent_chain(cuda, L, O):
+    """Four launches, each reading the previous one's fp16 output, as
+    programmatic dependents: same result as plain launches."""
+    torch = cuda
+    K = 2048
+    mats = [weights(torch, K, K, 50 + i) for i in range(4)]
+    x0 = torch.randn(K, generator=torch.Generator().manual_seed(51)).half().cuda()
+    outs = {}
+    s = torch.cuda.Stream()
+    for pdl in (0, 1):
+        bufs = [x0] + [torch.zeros(K, dtype=torch.float16, device="cuda") for _ in range(4)]
+        torch.cuda.synchronize()
+        for i, (wq, sc) in enumerate(mats):
+            p = Params(K=K, op=OP["F16"], x=dp(bufs[i]), njobs=1, pf_bytes=65536)
+            p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=K, epi=EPI["F16"], out_f16=dp(bufs[i + 1]))
+            assert L.dec_k_matvec(C.byref(p), C.c_void_p(s.cuda_stream), pdl) == 0
+        torch.cuda.synchronize()
+        outs[pdl] = bufs[4].cpu().numpy()
+    assert np.array_equal(outs[0], outs[1])
+    y = x0.cpu().numpy().astype(np.float64)
+    for wq, sc in mats:
+        y = (deq(O, wq, sc) @ O.stage_g128(y)).astype(np.float16).astype(np.float64)
+    assert rel(outs[1].astype(np.float64), y) <= 1e-2     # four fp16 roundings of chained random products
+
+
+def test_refusals(cuda, L):
+    torch = cuda
+    wq, sc = weights(torch, 8, 256, 60)
+    x = torch.zeros(256, dtype=torch.float16, device="cuda")
+    y = torch.zeros(8, device="cuda")
+
+    def p(**kw):
+        q = Params(K=kw.pop("K", 256), op=kw.pop("op", 0), x=dp(x), njobs=kw.pop("njobs", 1))
+        q.jobs[0] = Job(s_pitch=spitch(256), wq=dp(wq), sc=dp(sc), rows=8, epi=EPI["F32"], out_f32=dp(y))
+        for k, v in kw.items():
+            setattr(q.jobs[0], k, v)
+        return q
+    assert L.dec_k_matvec(C.byref(p(K=200)), None, 0) == -11
+    assert L.dec_k_matvec(C.byref(p(K=65536)), None, 0) == -11
+    assert L.dec_k_matvec(C.byref(p(njobs=0)), None, 0) == -11
+    assert L.dec_k_matvec(C.byref(p(njobs=5)), None, 0) == -11
+    assert L.dec_k_matvec(C.byref(p(op=1)), None, 0) == -11                   # RMSNORM without weights
+    assert L.dec_k_matvec(C.byref(p(out_f32=None)), None, 0) == -11
+    assert L.dec_k_matvec(C.byref(p(wq=dp(wq) + 8)), None, 0) == -11          # 16-byte alignment
+    assert L.dec_k_matvec(C.byref(p(s_pitch=2)), None, 0) == -11              # scale rows not 16 bytes
+    assert L.dec_k_matvec(C.byref(p(epi=EPI["SWIGLU"])), None, 0) == -11      # unpaired SwiGLU
+    assert L.dec_k_matvec(C.byref(p(epi=9)), None, 0) == -11
+    assert L.dec_k_matvec(C.byref(p()), None, 0) == 0
+    torch.cuda.synchronize()
