@@ -50,6 +50,8 @@ typedef struct {
     unsigned long long *key;       /* ARGMAX key (first max, global index)         */
     int32_t      idx0;             /* ARGMAX: global index of row 0                */
     int32_t      pf_bytes;         /* weight bytes each CTA prefetches to L2 early */
+    int32_t      ksplit;           /* set by the launcher: warps per row       */
+    int32_t      pad_;
 } dmv_params;
 
 #ifdef __cplusplus

@@ -29,6 +29,12 @@ extern "C" int mv4i_g_cuda_err;
 
 #define DMV_THREADS 256
 #define DMV_WARPS 8
+#ifndef DMV_G
+#define DMV_G 4                    // rows a warp streams together (2 gate/up pairs)
+#endif
+#ifndef DMV_MINB
+#define DMV_MINB 2                 // resident CTAs per SM the registers are sized for
+#endif
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -83,10 +89,15 @@ __device__ __forceinline__ float block_sum(float v, float *red)
     return v;
 }
 
-__device__ __forceinline__ int to_i16(float f, int e)
+// sat16(rint(f * 2^e)), round half to even; scale = 2^e exactly.  |f * 2^e| <
+// 2^15 by the choice of e, so only +32768 (from rounding) needs the clamp.
+__device__ __forceinline__ int to_i16(float f, float scale)
 {
-    return (int)fminf(fmaxf(rintf(ldexpf(f, e)), -32768.f), 32767.f);
+    return min(__float2int_rn(f * scale), 32767);
 }
+
+// 2^n for n in [-126, 127]
+__device__ __forceinline__ float exp2i(int n) { return __int_as_float((127 + n) << 23); }
 
 // Shared memory (K columns, np = K/64 pairs of 32-column blocks, ng = K/128):
 //   planes  uint4 [4 planes][2 block parities][np]: the int16 x split into
@@ -206,10 +217,12 @@ __device__ void dmv_stage(const dmv_params &P, const Sm &s)
 #pragma unroll
         for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         int e = 0;
-        if (m > 0.f) { int ex; frexpf(m, &ex); e = 15 - ex; }    // m in [2^(ex-1), 2^ex)
+        // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
+        if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
+        const float scale = exp2i(e);
         int xi[8], ssum = 0;
 #pragma unroll
-        for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], e); ssum += xi[k]; }
+        for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
 #pragma unroll
         for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
         if (ok) {
@@ -227,7 +240,7 @@ __device__ void dmv_stage(const dmv_params &P, const Sm &s)
             pw[4 * ((4 + par) * np + p) + q] = he;
             pw[4 * ((6 + par) * np + p) + q] = ho;
             if (!(u & 7)) s.psum[u >> 3] = ssum;
-            if (!(u & 15)) s.gfac[u >> 4] = ldexpf(1.0f, -e);
+            if (!(u & 15)) s.gfac[u >> 4] = exp2i(-e);
             if (blockIdx.x == 0 && P.seam)
                 *reinterpret_cast<uint4 *>(P.seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         }
@@ -348,28 +361,55 @@ template <int NR>
 __device__ __forceinline__ void dmv_dots(const Sm &s, int np, int p, const uint32_t (&w)[NR][8],
                                          const float (&sc)[NR], float (&acc)[NR])
 {
-    uint4 xp[8];
+    int a[NR][4];
 #pragma unroll
-    for (int k = 0; k < 8; k++) xp[k] = s.planes[k * np + p];
+    for (int k = 0; k < NR; k++) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0;
+    // one block parity at a time: 4 x-plane vectors live, shared by the NR rows
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint4 xle = s.planes[(0 + half) * np + p], xlo = s.planes[(2 + half) * np + p];
+        const uint4 xhe = s.planes[(4 + half) * np + p], xho = s.planes[(6 + half) * np + p];
+        const uint32_t le[4] = {xle.x, xle.y, xle.z, xle.w}, lo[4] = {xlo.x, xlo.y, xlo.z, xlo.w};
+        const uint32_t he[4] = {xhe.x, xhe.y, xhe.z, xhe.w}, ho[4] = {xho.x, xho.y, xho.z, xho.w};
+#pragma unroll
+        for (int k = 0; k < NR; k++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t wv = w[k][4 * half + q];
+                const uint32_t e = (wv & 0x0F0F0F0Fu) ^ 0x08080808u;     // idx^8 of even columns
+                const uint32_t o = (wv & 0xF0F0F0F0u) ^ 0x80808080u;     // 16*(idx^8) of odd columns
+                a[k][0] = dp_uu(e, le[q], a[k][0]);
+                a[k][1] = dp_uu(o, lo[q], a[k][1]);
+                a[k][2] = dp_us(e, he[q], a[k][2]);
+                a[k][3] = dp_us(o, ho[q], a[k][3]);
+            }
+    }
     const int sx = s.psum[p];
     const float gf = s.gfac[p >> 1];
 #pragma unroll
     for (int k = 0; k < NR; k++) {
-        int a[4] = {0, 0, 0, 0};
-        pair_dot4(w[k], xp, a);
-        const int part = a[0] + (a[1] >> 4) + (a[2] + (a[3] >> 4)) * 256 - 8 * sx;   // a1, a3: x16
+        const int part = a[k][0] + (a[k][1] >> 4) + (a[k][2] + (a[k][3] >> 4)) * 256 - 8 * sx;   // a1, a3: x16
         acc[k] = fmaf((float)part, sc[k] * gf, acc[k]);
     }
 }
 
 // rows of job J in tiles [ta, tb) for this warp; NR dot products per group:
 // 4 rows, or (PAIRED) 2 rows of gate and up
+// rows of job J in tiles [ta, tb) for this warp; NR dot products per group:
+// G rows, or (PAIRED) G/2 rows of gate and up.  The CTA's warps are split
+// into rt = 8/ks row slots x ks column slices: a tile is rt rows, warp w takes
+// row slot w / ks over column slice w % ks, and the ks partial sums of a row
+// meet in shared memory (uniform control flow: every warp walks the same
+// groups and the same number of batches).
 template <bool PAIRED>
-__device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &J, const Sm &s, int ta, int tb,
-                                            int warp, int lane, int np, size_t wpitch, unsigned long long &best)
+__device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &J, const Sm &s, float *red,
+                                            int ta, int tb, int warp, int lane, int np, size_t wpitch,
+                                            unsigned long long &best)
 {
-    constexpr int G = PAIRED ? 2 : 4;
-    constexpr int NR = 4;
+    constexpr int G = PAIRED ? DMV_G / 2 : DMV_G;
+    constexpr int NR = DMV_G;
+    const int ks = P.ksplit, rt = DMV_WARPS / ks, rs = warp / ks, kq = warp % ks;
+    const int npk = np / ks, p0 = kq * npk, p1 = p0 + npk;
     for (int t = ta; t < tb; t += G) {
         const int g = min(G, tb - t);
         const uint8_t *wr[NR];
@@ -377,7 +417,7 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
         int rows[G];
 #pragma unroll
         for (int i = 0; i < G; i++) {
-            rows[i] = (t + min(i, g - 1) - J.tile0) * DMV_WARPS + warp;
+            rows[i] = (t + min(i, g - 1) - J.tile0) * rt + rs;
             const int rr = min(rows[i], J.rows - 1);            // past the end: a valid row, discarded
             if (PAIRED) {
                 wr[2 * i] = J.wq + (size_t)rr * wpitch;  sr[2 * i] = J.sc + (size_t)rr * J.s_pitch;
@@ -386,19 +426,37 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
                 wr[i] = J.wq + (size_t)rr * wpitch; sr[i] = J.sc + (size_t)rr * J.s_pitch;
             }
         }
-        float acc[NR] = {0.f, 0.f, 0.f, 0.f};
-        for (int pb = 0; pb < np; pb += 32) {
+        float acc[NR];
+#pragma unroll
+        for (int k = 0; k < NR; k++) acc[k] = 0.f;
+        for (int pb = p0; pb < p1; pb += 32) {
             const int p = pb + lane;
             uint32_t w[NR][8];
             float sc[NR];
-            dmv_loads<NR>(wr, sr, p, p < np, w, sc);
-            if (p < np) dmv_dots<NR>(s, np, p, w, sc, acc);
+            dmv_loads<NR>(wr, sr, p, p < p1, w, sc);
+            if (p < p1) dmv_dots<NR>(s, np, p, w, sc, acc);
         }
 #pragma unroll
         for (int k = 0; k < NR; k++)
 #pragma unroll
             for (int o = 16; o; o >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
-        if (lane == 0) {
+        if (ks > 1) {
+            if (lane == 0) {
+#pragma unroll
+                for (int k = 0; k < NR; k++) red[(rs * NR + k) * DMV_WARPS + kq] = acc[k];
+            }
+            __syncthreads();
+            if (kq == 0 && lane == 0) {
+#pragma unroll
+                for (int k = 0; k < NR; k++) {
+                    float v = 0.f;
+                    for (int q = 0; q < ks; q++) v += red[(rs * NR + k) * DMV_WARPS + q];
+                    acc[k] = v;
+                }
+            }
+            __syncthreads();
+        }
+        if (lane == 0 && kq == 0) {
 #pragma unroll
             for (int i = 0; i < G; i++)
                 if (i < g && rows[i] < J.rows)
@@ -407,10 +465,11 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
     }
 }
 
-__global__ void __launch_bounds__(DMV_THREADS, 2) dmv_kernel(const __grid_constant__ dmv_params P)
+__global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid_constant__ dmv_params P)
 {
     extern __shared__ __align__(128) uint8_t dmv_sm[];
     __shared__ dmv_job JS[DMV_MAXJ];
+    __shared__ float red[DMV_WARPS * DMV_G * DMV_WARPS];
     if (threadIdx.x < P.njobs) JS[threadIdx.x] = P.jobs[threadIdx.x];
     __syncthreads();
     const int T = P.total_tiles;
@@ -428,8 +487,8 @@ __global__ void __launch_bounds__(DMV_THREADS, 2) dmv_kernel(const __grid_consta
         for (int t = t0; t < t1 && budget > 0;) {
             const dmv_job &J = JS[dmv_job_of(P, JS, t)];
             const int te = min(t1, J.tile0 + J.ntiles);
-            const int r0 = (t - J.tile0) * DMV_WARPS;
-            const int r1 = min(J.rows, (te - J.tile0) * DMV_WARPS);
+            const int r0 = (t - J.tile0) * (DMV_WARPS / P.ksplit);
+            const int r1 = min(J.rows, (te - J.tile0) * (DMV_WARPS / P.ksplit));
             int64_t bytes = (int64_t)(r1 - r0) * (int64_t)wpitch;
             if (bytes > budget) bytes = budget & ~(int64_t)15;
             for (int m = 0; m < (J.wq2 ? 2 : 1); m++) {
@@ -452,8 +511,8 @@ __global__ void __launch_bounds__(DMV_THREADS, 2) dmv_kernel(const __grid_consta
         const dmv_job &J = JS[j];
         const int ta = max(t0, J.tile0), tb = min(t1, J.tile0 + J.ntiles);
         if (ta >= tb) continue;
-        if (J.wq2) dmv_segment<true>(P, J, s, ta, tb, warp, lane, np, wpitch, best);
-        else dmv_segment<false>(P, J, s, ta, tb, warp, lane, np, wpitch, best);
+        if (J.wq2) dmv_segment<true>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
+        else dmv_segment<false>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
     }
     if (best) atomicMax(P.key, best);
 }
@@ -466,6 +525,40 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
     if (p->op == DMV_OP_GATED && (!p->nw || !p->x2)) return -11;
     if (p->op < DMV_OP_F16 || p->op > DMV_OP_GATED) return -11;
     dmv_params P = *p;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+    if (dev < 0 || dev >= 64) return -11;
+    static int s_sms[64], s_occ[64][4], s_attr[64];
+    static size_t s_occ_smem[64][4];
+    if (!s_attr[dev]) {
+        e = cudaFuncSetAttribute(dmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+        s_attr[dev] = 1;
+    }
+    const size_t smem = dmv_smem_x_bytes(P.K);
+    int occ = 0;
+    for (int i = 0; i < 4; i++) if (s_occ[dev][i] && s_occ_smem[dev][i] == smem) occ = s_occ[dev][i];
+    if (!occ) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dmv_kernel, DMV_THREADS, smem);
+        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+        if (occ < 1) occ = 1;
+        for (int i = 0; i < 4; i++)
+            if (!s_occ[dev][i]) { s_occ[dev][i] = occ; s_occ_smem[dev][i] = smem; break; }
+    }
+    const int slots = s_sms[dev] * occ;
+    // Rows are short of warps when a CTA would get fewer than 16: then split
+    // each row's columns over up to all 8 warps of the CTA (at most 32 pairs,
+    // one batch, per warp where the pair count allows).
+    long long all_rows = 0;
+    for (int j = 0; j < P.njobs; j++) all_rows += P.jobs[j].rows > 0 ? P.jobs[j].rows : 0;
+    const int np = P.K / 64;
+    int ks = 1;
+    if (all_rows < 16LL * slots)
+        while (ks < DMV_WARPS && np / ks > 32 && (np % (2 * ks)) == 0) ks *= 2;
+    P.ksplit = ks;
+    const int rt = DMV_WARPS / ks;
     int tiles = 0;
     for (int j = 0; j < P.njobs; j++) {
         dmv_job &J = P.jobs[j];
@@ -486,33 +579,11 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
         }
         if (J.epi != DMV_EPI_SWIGLU && J.wq2) return -11;
         J.tile0 = tiles;
-        J.ntiles = (J.rows + DMV_WARPS - 1) / DMV_WARPS;
+        J.ntiles = (J.rows + rt - 1) / rt;
         tiles += J.ntiles;
     }
     P.total_tiles = tiles;
-    const size_t smem = dmv_smem_x_bytes(P.K);
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-    static int s_sms[64], s_occ[64][4], s_attr[64];
-    static size_t s_occ_smem[64][4];
-    if (dev < 0 || dev >= 64) return -11;
-    if (!s_attr[dev]) {
-        e = cudaFuncSetAttribute(dmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-        s_attr[dev] = 1;
-    }
-    int occ = 0;
-    for (int i = 0; i < 4; i++) if (s_occ[dev][i] && s_occ_smem[dev][i] == smem) occ = s_occ[dev][i];
-    if (!occ) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dmv_kernel, DMV_THREADS, smem);
-        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-        if (occ < 1) occ = 1;
-        for (int i = 0; i < 4; i++)
-            if (!s_occ[dev][i]) { s_occ[dev][i] = occ; s_occ_smem[dev][i] = smem; break; }
-    }
-    int grid = s_sms[dev] * occ;
+    int grid = slots;
     if (grid > tiles) grid = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

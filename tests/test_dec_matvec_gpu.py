@@ -38,7 +38,8 @@ class Job(C.Structure):
 class Params(C.Structure):
     _fields_ = [("jobs", Job * 4), ("njobs", C.c_int32), ("total_tiles", C.c_int32), ("K", C.c_int32),
                 ("op", C.c_int32), ("x", P_), ("x2", P_), ("nw", P_), ("eps", C.c_float), ("seam", P_),
-                ("key", P_), ("idx0", C.c_int32), ("pf_bytes", C.c_int32)]
+                ("key", P_), ("idx0", C.c_int32), ("pf_bytes", C.c_int32), ("ksplit", C.c_int32),
+                ("pad_", C.c_int32)]
 
 
 @pytest.fixture(scope="module")
