@@ -102,7 +102,7 @@ int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, 
  * the fp16 "embed" [vocab][hidden] (layer -1).  Layer -1 also names the
  * activation seams of the last step, as the last layer to write each left
  * them (the reference's seam records): fp32 "x" (residual), "qkv" (the raw
- * projection), "z", "eg", "beta", "o", "qg", "kv", "q", "gate", "logits"; fp16
+ * projection), "z", "eg", "beta", "o", "qg", "kv", "q" (after norm and RoPE), "logits"; fp16
  * "h16" (the last RMSNorm output), "qkv16" (after conv + SiLU), "y16" (DeltaNet
  * output after norm and gate), "ya16" (attention output), "hf16" (SwiGLU). */
 int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count);

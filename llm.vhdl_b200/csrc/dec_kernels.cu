@@ -42,91 +42,158 @@ __global__ void dec_embed_kernel(const uint16_t *emb, int hidden, const int32_t 
         x[i] = __half2float(__ushort_as_half(emb[base + i]));
 }
 
-// Attention pre-processing (ref/run9b.c:786-843): q|gate interleaved per
-// head, q and k RMSNorm over the head dim, NeoX RoPE on the first n_rot
-// dims (pairs i, i + n_rot/2), k and v into the fp16 cache at the current
-// position.  One CTA per q head, then one per k head; hd threads.
-__global__ void dec_attn_pre_kernel(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot,
-                                    float theta, float eps, const float *qn_w, const float *kn_w,
-                                    const int32_t *d_pos, int max_ctx, float *q_out, float *gate_out,
-                                    uint16_t *kcache, uint16_t *vcache)
+// One decode step of gated attention, flash-decoding part 1 with the
+// pre-processing folded in (ref/run9b.c:786-869).  Grid (chunks of `ch`
+// positions, kv heads); one warp per q head of the GQA group (q head h reads
+// kv head h / (qh/kvh), ref/run9b.c:859).  Each CTA builds its group's q from
+// the raw projection (q|gate interleaved per head): RMSNorm over the head dim
+// with q_norm, NeoX RoPE on the first n_rot dims (pairs i, i + n_rot/2) at the
+// current position.  The CTA whose chunk holds the current position builds k
+// (k_norm, RoPE) and v the same way, stores both in the fp16 cache and uses
+// them.  Then the chunk's scores (scale 1/sqrt(128)), running max, sum and
+// unnormalised output per q head go to a record of 132 floats [max, sum, -,
+// -, o[128]].  Head dim 128.
+#define ATT_HD 128
+#define ATT_KS (ATT_HD + 8)          // padded k row in shared memory (272 bytes)
+
+// RMSNorm + RoPE of one 128-dim head held by a warp (lane: dims 4l..4l+3);
+// buf is the warp's 128-float scratch
+__device__ __forceinline__ void att_norm_rope(const float4 r, const float *w, float eps, int n_rot, float theta,
+                                              int pos, float *buf, int lane, float (&out)[4])
 {
-    __shared__ float red[32];
-    __shared__ float buf[512];
-    PDL_ENTER();
-    const int hb = blockIdx.x, i = threadIdx.x;
-    const int pos = *d_pos;
-    const bool isq = hb < qh;
-    const int h = isq ? hb : hb - qh;
-    const float *src = isq ? qg + (size_t)h * 2 * hd : kv + (size_t)h * hd;
-    const float v = i < hd ? src[i] : 0.f;
-    const float s = block_sum(v * v, red);
-    const float inv = rsqrtf(s / (float)hd + eps);
-    if (i < hd) buf[i] = v * inv * (isq ? qn_w[i] : kn_w[i]);
-    __syncthreads();
-    float r = i < hd ? buf[i] : 0.f;
+    float ss = r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)ATT_HD + eps);
+    const float4 w4 = reinterpret_cast<const float4 *>(w)[lane];
+    const float v[4] = {r.x * inv * w4.x, r.y * inv * w4.y, r.z * inv * w4.z, r.w * inv * w4.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) buf[4 * lane + i] = v[i];
+    __syncwarp();
     const int half = n_rot / 2;
-    if (i < n_rot) {
-        const int k = i < half ? i : i - half;
-        const double th = (double)pos * exp2(-2.0 * (double)k / (double)n_rot * log2((double)theta));
-        double sn, cs;
-        sincos(th, &sn, &cs);
-        const float a = buf[k], b = buf[k + half];
-        r = i < half ? (float)(a * cs - b * sn) : (float)(a * sn + b * cs);
-    }
-    if (i < hd) {
-        if (isq) {
-            q_out[(size_t)h * hd + i] = r;
-            gate_out[(size_t)h * hd + i] = qg[(size_t)h * 2 * hd + hd + i];
-        } else if (pos < max_ctx) {          // a full cache takes no more entries
-            const size_t off = ((size_t)pos * kvh + h) * hd + i;
-            kcache[off] = __half_as_ushort(__float2half_rn(r));
-            vcache[off] = __half_as_ushort(__float2half_rn(kv[(size_t)(kvh + h) * hd + i]));
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int d = 4 * lane + i;
+        if (d < n_rot) {
+            const int k = d < half ? d : d - half;
+            const double th = (double)pos * exp2(-2.0 * (double)k / (double)n_rot * log2((double)theta));
+            double sn, cs;
+            sincos(th, &sn, &cs);
+            const float a = buf[k], b = buf[k + half];
+            out[i] = d < half ? (float)(a * cs - b * sn) : (float)(a * sn + b * cs);
+        } else {
+            out[i] = v[i];
         }
     }
+    __syncwarp();
 }
 
-// Flash-decoding, part 1: CTA (chunk c of `ch` positions, kv head g), one warp
-// per q head of the group (q head h uses kv head h / (qh/kvh),
-// ref/run9b.c:859); lane l holds dims 4l..4l+3 (hd = 128).  Writes the
-// chunk's running max, sum and unnormalised output per q head into a record
-// of hd + 4 floats (max, sum, 2 unused, then hd sums: 16-byte aligned).
-__global__ void dec_attn_decode_kernel(const float *q, const uint16_t *kcache, const uint16_t *vcache,
-                                       int qh, int kvh, int hd, int ch, const int32_t *d_pos, int max_ctx,
-                                       int nchunks, float *part)
+__global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const float *kv, const float *qn_w,
+                                                        const float *kn_w, int qh, int kvh, int n_rot, float theta,
+                                                        float eps, const int32_t *d_pos, int max_ctx, int ch,
+                                                        int nchunks, uint16_t *kcache, uint16_t *vcache,
+                                                        float *q_seam, float *part)
 {
+    extern __shared__ __align__(16) uint8_t att_sm[];
     PDL_ENTER();
+    const int grp = qh / kvh;
     const int c = blockIdx.x, g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int grp = qh / kvh, h = g * grp + warp;
-    const int len = min(*d_pos + 1, max_ctx);
-    const int p0 = c * ch;
-    float *pp = part + ((size_t)h * nchunks + c) * (hd + 4);
-    if (p0 >= len) {
+    const int h = g * grp + warp;
+    const int pos = *d_pos, len = min(pos + 1, max_ctx), p0 = c * ch;
+    float *pp = part + ((size_t)h * nchunks + c) * (ATT_HD + 4);
+    if (p0 >= len) {                                   // the whole CTA leaves: no barrier below
         if (lane == 0) { pp[0] = -INFINITY; pp[1] = 0.f; }
         return;
     }
-    const float scale = rsqrtf((float)hd);
-    const float4 qv = reinterpret_cast<const float4 *>(q + (size_t)h * hd)[lane];
-    float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    const int p1 = min(len, p0 + ch);
-    for (int p = p0; p < p1; p++) {
-        const size_t off = ((size_t)p * kvh + g) * hd + 4 * lane;
-        const uint2 kr = *reinterpret_cast<const uint2 *>(kcache + off);
-        const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
-        const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
-        float s = qv.x * k01.x + qv.y * k01.y + qv.z * k23.x + qv.w * k23.y;
+    const int n = min(ch, len - p0);
+    float *qs = reinterpret_cast<float *>(att_sm);                  // [grp][128]
+    float *ps = qs + grp * ATT_HD;                                  // [grp][ch]
+    __half *ks = reinterpret_cast<__half *>(ps + grp * ch);         // [ch][ATT_KS]
+    __half *vs = ks + ch * ATT_KS;                                  // [ch][128]
+    float *kb = reinterpret_cast<float *>(vs + ch * ATT_HD);        // [128] scratch for the new k
+
+    // q of head h
+    {
+        float q[4];
+        const float4 r = reinterpret_cast<const float4 *>(qg + (size_t)h * 2 * ATT_HD)[lane];
+        att_norm_rope(r, qn_w, eps, n_rot, theta, pos, qs + warp * ATT_HD, lane, q);
 #pragma unroll
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        s *= scale;
-        const float mn = fmaxf(m, s);
-        const float corr = expf(m - mn), e = expf(s - mn);
-        const uint2 vr = *reinterpret_cast<const uint2 *>(vcache + off);
+        for (int i = 0; i < 4; i++) qs[warp * ATT_HD + 4 * lane + i] = q[i];
+        if (c == 0 && q_seam)
+            reinterpret_cast<float4 *>(q_seam + (size_t)h * ATT_HD)[lane] = make_float4(q[0], q[1], q[2], q[3]);
+    }
+    // the chunk's cached k and v rows (16-byte pieces; the current position's
+    // row is replaced below)
+    for (int i = threadIdx.x; i < n * 32; i += blockDim.x) {
+        const int r = i >> 5, piece = i & 15;
+        const size_t off = ((size_t)(p0 + r) * kvh + g) * ATT_HD + 8 * piece;
+        if (i & 16) *reinterpret_cast<uint4 *>(vs + r * ATT_HD + 8 * piece) = *reinterpret_cast<const uint4 *>(vcache + off);
+        else *reinterpret_cast<uint4 *>(ks + r * ATT_KS + 8 * piece) = *reinterpret_cast<const uint4 *>(kcache + off);
+    }
+    __syncthreads();
+    // the current position: new k and v of kv head g
+    if (warp == 0 && pos >= p0 && pos < p0 + n) {
+        float k[4];
+        const float4 r = reinterpret_cast<const float4 *>(kv + (size_t)g * ATT_HD)[lane];
+        att_norm_rope(r, kn_w, eps, n_rot, theta, pos, kb, lane, k);
+        const float4 vr = reinterpret_cast<const float4 *>(kv + (size_t)(kvh + g) * ATT_HD)[lane];
+        const __half2 k01 = __floats2half2_rn(k[0], k[1]), k23 = __floats2half2_rn(k[2], k[3]);
+        const __half2 v01 = __floats2half2_rn(vr.x, vr.y), v23 = __floats2half2_rn(vr.z, vr.w);
+        uint2 kw, vw;
+        kw.x = *reinterpret_cast<const uint32_t *>(&k01); kw.y = *reinterpret_cast<const uint32_t *>(&k23);
+        vw.x = *reinterpret_cast<const uint32_t *>(&v01); vw.y = *reinterpret_cast<const uint32_t *>(&v23);
+        const int r0 = pos - p0;
+        *reinterpret_cast<uint2 *>(ks + r0 * ATT_KS + 4 * lane) = kw;
+        *reinterpret_cast<uint2 *>(vs + r0 * ATT_HD + 4 * lane) = vw;
+        const size_t off = ((size_t)pos * kvh + g) * ATT_HD + 4 * lane;
+        *reinterpret_cast<uint2 *>(kcache + off) = kw;
+        *reinterpret_cast<uint2 *>(vcache + off) = vw;
+    }
+    __syncthreads();
+    // scores: lanes over positions, q broadcast from shared memory
+    const float scale = rsqrtf((float)ATT_HD);
+    const float *qw = qs + warp * ATT_HD;
+    float *pw = ps + warp * ch;
+    float m = -INFINITY;
+    for (int j0 = 0; j0 < n; j0 += 32) {
+        const int j = j0 + lane;
+        if (j < n) {
+            float sc = 0.f;
+#pragma unroll 4
+            for (int d = 0; d < ATT_HD; d += 8) {
+                const uint4 kr = *reinterpret_cast<const uint4 *>(ks + j * ATT_KS + d);
+                const uint32_t kw[4] = {kr.x, kr.y, kr.z, kr.w};
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&kw[t]));
+                    sc = fmaf(qw[d + 2 * t], kf.x, sc);
+                    sc = fmaf(qw[d + 2 * t + 1], kf.y, sc);
+                }
+            }
+            sc *= scale;
+            pw[j] = sc;
+            m = fmaxf(m, sc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int j = lane; j < n; j += 32) {
+        const float e = expf(pw[j] - m);
+        pw[j] = e;
+        l += e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    __syncwarp();
+    // unnormalised output: lane holds dims 4l..4l+3
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int j = 0; j < n; j++) {
+        const float e = pw[j];
+        const uint2 vr = *reinterpret_cast<const uint2 *>(vs + j * ATT_HD + 4 * lane);
         const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
         const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
-        a0 = a0 * corr + e * v01.x; a1 = a1 * corr + e * v01.y;
-        a2 = a2 * corr + e * v23.x; a3 = a3 * corr + e * v23.y;
-        l = l * corr + e;
-        m = mn;
+        a0 = fmaf(e, v01.x, a0); a1 = fmaf(e, v01.y, a1); a2 = fmaf(e, v23.x, a2); a3 = fmaf(e, v23.y, a3);
     }
     if (lane == 0) { pp[0] = m; pp[1] = l; }
     reinterpret_cast<float4 *>(pp + 4)[lane] = make_float4(a0, a1, a2, a3);
@@ -134,7 +201,7 @@ __global__ void dec_attn_decode_kernel(const float *q, const uint16_t *kcache, c
 
 // Flash-decoding, part 2: combine the chunks of each q head, apply the
 // sigmoid output gate (the raw projection, ref/run9b.c:871-872), to fp16.
-__global__ void dec_attn_combine_kernel(const float *part, const float *gate, int hd, int nchunks,
+__global__ void dec_attn_combine_kernel(const float *part, const float *gate, int gate_stride, int hd, int nchunks,
                                         const int32_t *d_pos, int ch, uint16_t *y)
 {
     PDL_ENTER();
@@ -151,7 +218,7 @@ __global__ void dec_attn_combine_kernel(const float *part, const float *gate, in
         a0 += a.x * w; a1 += a.y * w; a2 += a.z * w; a3 += a.w * w;
     }
     const float inv = 1.0f / L;
-    const float4 gv = reinterpret_cast<const float4 *>(gate + (size_t)h * hd)[lane];
+    const float4 gv = reinterpret_cast<const float4 *>(gate + (size_t)h * gate_stride)[lane];
     uint16_t *yo = y + (size_t)h * hd + 4 * lane;
     yo[0] = __half_as_ushort(__float2half_rn(a0 * inv * sigm_f(gv.x)));
     yo[1] = __half_as_ushort(__float2half_rn(a1 * inv * sigm_f(gv.y)));
@@ -260,22 +327,43 @@ extern "C" {
 int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s, int pdl)
 { return launch(dec_embed_kernel, dim3((hidden + 255) / 256), dim3(256), s, pdl, emb, hidden, tok, x); }
 
-int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
-                   const float *qn_w, const float *kn_w, const int32_t *d_pos, int max_ctx, float *q_out,
-                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s, int pdl)
+size_t dec_attention_smem(int qh, int kvh, int ch)
 {
-    return launch(dec_attn_pre_kernel, dim3(qh + kvh), dim3(((hd + 31) / 32) * 32), s, pdl, qg, kv, qh, kvh, hd,
-                  n_rot, theta, eps, qn_w, kn_w, d_pos, max_ctx, q_out, gate_out, kcache, vcache);
+    const int grp = qh / kvh;
+    return (size_t)(grp * ATT_HD + grp * ch) * 4 + (size_t)ch * ATT_KS * 2 + (size_t)ch * ATT_HD * 2 + ATT_HD * 4;
 }
 
-int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int qh, int kvh, int hd, int ch,
-                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s, int pdl)
+int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const float *kn_w, int qh, int kvh,
+                    int n_rot, float theta, float eps, const int32_t *d_pos, int max_ctx, int ch, float *part,
+                    float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, void *s, int pdl)
 {
+    if (kvh <= 0 || qh % kvh || qh / kvh > 32 || ch <= 0 || ch > 64 || (n_rot & 1) || n_rot > ATT_HD) return -11;
     const int nchunks = (max_ctx + ch - 1) / ch;
-    int rc = launch(dec_attn_decode_kernel, dim3(nchunks, kvh), dim3(32 * (qh / kvh)), s, pdl, q, kc, vc, qh, kvh,
-                    hd, ch, d_pos, max_ctx, nchunks, part);
+    const size_t smem = dec_attention_smem(qh, kvh, ch);
+    static int attr_set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -11;
+    if (!attr_set[dev]) {
+        const int rc = dk(cudaFuncSetAttribute(dec_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        if (rc) return rc;
+        attr_set[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nchunks, kvh);
+    cfg.blockDim = dim3(32 * (qh / kvh));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = reinterpret_cast<cudaStream_t>(s);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const int rc = dk(cudaLaunchKernelEx(&cfg, dec_attn_kernel, qg, kv, qn_w, kn_w, qh, kvh, n_rot, theta, eps,
+                                         d_pos, max_ctx, ch, nchunks, kcache, vcache, q_seam, part));
     if (rc) return rc;
-    return launch(dec_attn_combine_kernel, dim3(qh), dim3(32), s, pdl, part, gate, hd, nchunks, d_pos, ch, y);
+    // the gate is the raw projection: second half of each head's q|gate row
+    return launch(dec_attn_combine_kernel, dim3(qh), dim3(32), s, pdl, part, qg + ATT_HD, 2 * ATT_HD, ATT_HD,
+                  nchunks, d_pos, ch, y);
 }
 
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl)

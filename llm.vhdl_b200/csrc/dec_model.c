@@ -26,12 +26,9 @@ extern int mv4i_g_cuda_err;
 
 /* kernels in dec_kernels.cu (pdl: launch as a programmatic dependent) */
 int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s, int pdl);
-int dec_k_attn_pre(const float *qg, const float *kv, int qh, int kvh, int hd, int n_rot, float theta, float eps,
-                   const float *qn_w, const float *kn_w, const int32_t *d_pos, int max_ctx, float *q_out,
-                   float *gate_out, uint16_t *kcache, uint16_t *vcache, void *s, int pdl);
-int dec_k_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int qh, int kvh, int hd, int ch,
-                    int max_ctx, const int32_t *d_pos, float *part, const float *gate, uint16_t *y, void *s,
-                    int pdl);
+int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const float *kn_w, int qh, int kvh,
+                    int n_rot, float theta, float eps, const int32_t *d_pos, int max_ctx, int ch, float *part,
+                    float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, void *s, int pdl);
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl);
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
                   int32_t *pos, int max_ctx, const int32_t *prompt, void *s, int pdl);
@@ -40,7 +37,6 @@ int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, i
 int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, float mean, float std,
                     float *f32, uint16_t *f16, void *s);
 
-#define ATT_CHUNK 64
 #define HD 128
 #define MAX_ALLOCS 8192
 #define CK(x) do { int rc_ = (x); if (rc_) return rc_; } while (0)
@@ -67,13 +63,13 @@ struct dec_model {
     dec_config c;
     int device, rank, world;
     /* local shard sizes */
-    int kh, vh, v0, qh, q0, kvh, kv0, ffn, f0, vocab, voc0, conv_dim, nchunks;
+    int kh, vh, v0, qh, q0, kvh, kv0, ffn, f0, vocab, voc0, conv_dim, att_ch, nchunks;
     layer_t  *L;
     linear_t  lm;
     float    *final_norm;
     uint16_t *embed;
     /* activations */
-    float    *x, *t, *qkv_f, *z_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *gate_f, *part, *logits;
+    float    *x, *t, *qkv_f, *z_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *part, *logits;
     uint16_t *h16, *qkv16, *y16, *ya16, *hf16;
     int       pdl;                       /* programmatic dependent launches     */
     unsigned long long *key, *keys;
@@ -161,7 +157,8 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     m->vocab = c->vocab / W + (R < c->vocab % W ? 1 : 0);
     m->voc0 = R * (c->vocab / W) + (R < c->vocab % W ? R : c->vocab % W);
     m->conv_dim = 2 * m->kh * HD + m->vh * HD;
-    m->nchunks = (c->max_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
+    m->att_ch = c->max_ctx <= 4096 ? 32 : 64;       /* positions per attention CTA */
+    m->nchunks = (c->max_ctx + m->att_ch - 1) / m->att_ch;
     m->L = (layer_t *)calloc((size_t)c->n_layers, sizeof(layer_t));
     const int H = c->hidden, KHg = c->gdn_kh, VHg = c->gdn_vh;
     const int conv_g = 2 * KHg * HD + VHg * HD;
@@ -239,7 +236,6 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->qg_f, 4 * 2 * (size_t)m->qh * HD));
     TRY(dalloc(m, (void **)&m->kv_f, 4 * 2 * (size_t)m->kvh * HD));
     TRY(dalloc(m, (void **)&m->q_f, 4 * (size_t)m->qh * HD));
-    TRY(dalloc(m, (void **)&m->gate_f, 4 * (size_t)m->qh * HD));
     TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 4)));
     TRY(dalloc(m, (void **)&m->ya16, 2 * (size_t)m->qh * HD));
     TRY(dalloc(m, (void **)&m->hf16, 2 * (size_t)m->ffn));
@@ -438,11 +434,10 @@ int dec_step(dec_model *m, void *s)
             P.jobs[1].out_f32 = m->kv_f;
             P.njobs = 2;
             CK(dec_k_matvec(&P, s, pdl));
-            CK(dec_k_attn_pre(m->qg_f, m->kv_f, m->qh, m->kvh, HD, c->n_rot, c->rope_theta, c->rms_eps,
-                              l->q_norm, l->k_norm, m->pos, c->max_ctx, m->q_f, m->gate_f, l->kcache, l->vcache,
-                              s, pdl));
-            CK(dec_k_attention(m->q_f, l->kcache, l->vcache, m->qh, m->kvh, HD, ATT_CHUNK, c->max_ctx, m->pos,
-                               m->part, m->gate_f, m->ya16, s, pdl));
+            /* q/k norm, RoPE and the cache write folded into flash decoding */
+            CK(dec_k_attention(m->qg_f, m->kv_f, l->q_norm, l->k_norm, m->qh, m->kvh, c->n_rot, c->rope_theta,
+                               c->rms_eps, m->pos, c->max_ctx, m->att_ch, m->part, m->q_f, l->kcache, l->vcache,
+                               m->ya16, s, pdl));
             mvparams(&P, m->qh * HD, DMV_OP_F16, m->ya16, NULL, 0.f, NULL);
             CK(row_parallel(m, &P, &l->o, s));
         }
@@ -513,7 +508,7 @@ int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int
             {"qkv16", m->qkv16, m->conv_dim}, {"z", m->z_f, m->vh * HD},
             {"eg", m->eg, m->vh}, {"beta", m->beta, m->vh}, {"o", m->o_f, m->vh * HD},
             {"y16", m->y16, m->vh * HD}, {"qg", m->qg_f, 2 * m->qh * HD}, {"kv", m->kv_f, 2 * m->kvh * HD},
-            {"q", m->q_f, m->qh * HD}, {"gate", m->gate_f, m->qh * HD}, {"ya16", m->ya16, m->qh * HD},
+            {"q", m->q_f, m->qh * HD}, {"ya16", m->ya16, m->qh * HD},
             {"hf16", m->hf16, m->ffn}, {"logits", m->logits, m->vocab}};
         for (unsigned i = 0; i < sizeof act / sizeof act[0]; i++)
             if (!strcmp(name, act[i].n)) { *d_ptr = act[i].p; *count = act[i].c; return 0; }

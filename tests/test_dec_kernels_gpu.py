@@ -1,4 +1,4 @@
-"""Seam tests: the attention kernels and the step advance of the decode step
+"""Seam tests: the attention kernel and the step advance of the decode step
 on identical inputs against the oracle's restatement of the same ref/run9b.c
 stage (oracle/dec_oracle.py), within 1e-3 of the largest magnitude (fp32
 arithmetic, fp16 outputs); the advance bit-exact.  The kernels are the
@@ -20,8 +20,7 @@ def K(pkg):
     L = pkg.declib()
     P, I, F, U64 = C.c_void_p, C.c_int, C.c_float, C.c_uint64
     sig = {
-        "dec_k_attn_pre": [P, P, I, I, I, I, F, F, P, P, P, I, P, P, P, P, P, I],
-        "dec_k_attention": [P, P, P, I, I, I, I, I, P, P, P, P, P, I],
+        "dec_k_attention": [P, P, P, P, I, I, I, F, F, P, I, I, P, P, P, P, P, P, I],
         "dec_k_advance": [P, I, P, P, P, P, I, P, P, I],
     }
     for n, a in sig.items():
@@ -48,89 +47,99 @@ def O():
     return dec_oracle
 
 
-@pytest.mark.parametrize("pos", [0, 1, 77, 4095])
-def test_attn_pre_norm_rope_and_cache_write(cuda, K, O, pos):
-    torch = cuda
-    g = torch.Generator().manual_seed(4 + pos)
-    qh, kvh, nrot, theta, ctx = 8, 2, 32, 1e6, 4096
-    qg, kv = torch.randn(qh * 2 * HD, generator=g) * 2, torch.randn(2 * kvh * HD, generator=g) * 2
-    qn, kn = 1 + 0.1 * torch.randn(HD, generator=g), 1 + 0.1 * torch.randn(HD, generator=g)
-    dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
-    qo, go = torch.zeros(qh * HD, device="cuda"), torch.zeros(qh * HD, device="cuda")
-    kc = torch.zeros(ctx * kvh * HD, dtype=torch.int16, device="cuda")
-    vc = torch.zeros_like(kc)
-    assert K.dec_k_attn_pre(ptr(qg.cuda()), ptr(kv.cuda()), qh, kvh, HD, nrot, theta, 1e-6, ptr(qn.cuda()),
-                            ptr(kn.cuda()), ptr(dpos), ctx, ptr(qo), ptr(go), ptr(kc), ptr(vc), None, 0) == 0
-
-    def rope(r):
-        r = r.copy()
-        half = nrot // 2
-        for i in range(half):
-            th = pos * theta ** (-2.0 * i / nrot)
-            a, b = r[i], r[i + half]
-            r[i], r[i + half] = a * np.cos(th) - b * np.sin(th), a * np.sin(th) + b * np.cos(th)
-        return r
-
-    qgn = qg.double().numpy().reshape(qh, 2, HD)
-    qref = np.stack([rope(O.rmsnorm(qgn[h, 0], qn.double().numpy(), 1e-6)) for h in range(qh)])
-    assert rel(qo.double().cpu().numpy(), qref.reshape(-1)) <= TOL
-    assert np.array_equal(go.cpu().numpy(), qgn[:, 1].reshape(-1).astype(np.float32))
-    kvn = kv.double().numpy().reshape(2, kvh, HD)
-    kref = np.stack([rope(O.rmsnorm(kvn[0, h], kn.double().numpy(), 1e-6)) for h in range(kvh)])
-    kcn = h16(kc).reshape(ctx, kvh, HD)
-    assert rel(kcn[pos], kref) <= TOL
-    assert np.array_equal(h16(vc).reshape(ctx, kvh, HD)[pos], O.f16(kvn[1]))
-    others = np.delete(kcn, pos, axis=0)
-    assert not np.any(others)
-
-
-@pytest.mark.parametrize("qh,kvh,pos,ctx", [(8, 2, 0, 256), (8, 2, 63, 256), (8, 2, 64, 256), (16, 2, 200, 256),
-                                            (4, 4, 255, 256), (32, 1, 130, 4096), (40, 8, 1000, 8192)])
-def test_flash_decoding_attention(cuda, K, O, qh, kvh, pos, ctx):
-    torch = cuda
-    g = torch.Generator().manual_seed(qh * 1000 + pos)
-    ch = 64
+def _attention_case(torch, O, qh, kvh, pos, ctx, ch, seed):
+    """Random q|gate, k|v projections, norms and a random fp16 cache; returns
+    the device tensors, the kernel's outputs and the oracle's."""
+    g = torch.Generator().manual_seed(seed)
+    nrot, theta = 32, 1e6
     nchunks = (ctx + ch - 1) // ch
-    q = torch.randn(qh * HD, generator=g)
-    kc = (torch.randn(ctx, kvh, HD, generator=g)).half()
-    vc = (torch.randn(ctx, kvh, HD, generator=g)).half()
-    gate = torch.randn(qh * HD, generator=g)
+    qg = torch.randn(qh * 2 * HD, generator=g) * 2
+    kv = torch.randn(2 * kvh * HD, generator=g) * 2
+    qn, kn = 1 + 0.1 * torch.randn(HD, generator=g), 1 + 0.1 * torch.randn(HD, generator=g)
+    kc = torch.randn(ctx, kvh, HD, generator=g).half()
+    vc = torch.randn(ctx, kvh, HD, generator=g).half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    d = {k: v.cuda() for k, v in dict(qg=qg, kv=kv, qn=qn, kn=kn, kc=kc, vc=vc).items()}
     part = torch.zeros(qh * nchunks * (HD + 4), device="cuda")
+    qseam = torch.zeros(qh * HD, device="cuda")
     y = torch.zeros(qh * HD, dtype=torch.int16, device="cuda")
     dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
-    kcd, vcd = kc.cuda(), vc.cuda()
-    assert K.dec_k_attention(ptr(q.cuda()), ptr(kcd), ptr(vcd), qh, kvh, HD, ch, ctx, ptr(dpos), ptr(part),
-                             ptr(gate.cuda()), ptr(y), None, 0) == 0
-    qn = q.double().numpy().reshape(qh, HD)
-    kn, vn = kc.double().numpy()[:pos + 1], vc.double().numpy()[:pos + 1]
+    return dict(d=d, part=part, qseam=qseam, y=y, dpos=dpos, nrot=nrot, theta=theta, kc0=kc0, vc0=vc0,
+                qg=qg.double().numpy(), kv=kv.double().numpy(), qn=qn.double().numpy(), kn=kn.double().numpy())
+
+
+def _rope(r, pos, nrot, theta):
+    r = r.copy()
+    half = nrot // 2
+    for i in range(half):
+        th = pos * theta ** (-2.0 * i / nrot)
+        a, b = r[i], r[i + half]
+        r[i], r[i + half] = a * np.cos(th) - b * np.sin(th), a * np.sin(th) + b * np.cos(th)
+    return r
+
+
+def _run_attention(K, torch, c, qh, kvh, pos, ctx, ch):
+    d = c["d"]
+    rc = K.dec_k_attention(ptr(d["qg"]), ptr(d["kv"]), ptr(d["qn"]), ptr(d["kn"]), qh, kvh, c["nrot"], c["theta"], 1e-6,
+                           ptr(c["dpos"]), ctx, ch, ptr(c["part"]), ptr(c["qseam"]), ptr(d["kc"]), ptr(d["vc"]),
+                           ptr(c["y"]), None, 0)
+    assert rc == 0
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("qh,kvh,pos,ctx,ch", [(8, 2, 0, 256, 32), (8, 2, 31, 256, 32), (8, 2, 32, 256, 32),
+                                               (16, 2, 200, 1024, 32), (4, 4, 255, 256, 32), (32, 1, 130, 4096, 32),
+                                               (40, 8, 1000, 8192, 64), (5, 1, 8191, 8192, 64)])
+def test_attention_step_against_oracle(cuda, K, O, qh, kvh, pos, ctx, ch):
+    """q and the new k: RMSNorm + NeoX RoPE (ref/run9b.c:800-826); k, v into
+    the fp16 cache at pos, nothing else written; GQA softmax attention over
+    positions 0..pos with the sigmoid gate of the raw projection
+    (ref/run9b.c:846-872), fp16 output."""
+    torch = cuda
+    c = _attention_case(torch, O, qh, kvh, pos, ctx, ch, qh * 1000 + pos)
+    _run_attention(K, torch, c, qh, kvh, pos, ctx, ch)
+    qgn = c["qg"].reshape(qh, 2, HD)
+    q = np.stack([_rope(O.rmsnorm(qgn[h, 0], c["qn"], 1e-6), pos, c["nrot"], c["theta"]) for h in range(qh)])
+    assert rel(c["qseam"].double().cpu().numpy().reshape(qh, HD), q) <= 1e-5
+    kvn = c["kv"].reshape(2, kvh, HD)
+    knew = np.stack([_rope(O.rmsnorm(kvn[0, g], c["kn"], 1e-6), pos, c["nrot"], c["theta"]) for g in range(kvh)])
+    kc = c["d"]["kc"].cpu().double().numpy()
+    vc = c["d"]["vc"].cpu().double().numpy()
+    assert rel(kc[pos], knew) <= 1e-3
+    assert np.array_equal(vc[pos], O.f16(kvn[1]))
+    others = np.ones(ctx, bool)
+    others[pos] = False
+    assert np.array_equal(kc[others], c["kc0"].double().numpy()[others])
+    assert np.array_equal(vc[others], c["vc0"].double().numpy()[others])
     ref = np.empty((qh, HD))
     for h in range(qh):
         gk = h // (qh // kvh)
-        sc = kn[:, gk] @ qn[h] / np.sqrt(HD)
+        sc = kc[:pos + 1, gk] @ q[h] / np.sqrt(HD)
         e = np.exp(sc - sc.max())
-        ref[h] = (e @ vn[:, gk]) / e.sum()
-    ref *= O.sigmoid(gate.double().numpy().reshape(qh, HD))
-    assert rel(h16(y), ref.reshape(-1)) <= TOL
+        ref[h] = (e @ vc[:pos + 1, gk]) / e.sum()
+    ref *= O.sigmoid(qgn[:, 1])
+    assert rel(h16(c["y"]), ref.reshape(-1)) <= TOL
 
 
-def test_attention_past_capacity_reads_only_the_cache(cuda, K):
+def test_attention_past_capacity_reads_only_the_cache(cuda, K, O):
     """A position at or past max_ctx (a replayed graph that ran past the end)
-    attends over the max_ctx cached entries and writes nothing out of range."""
+    writes nothing and attends over the max_ctx cached entries."""
     torch = cuda
-    qh, kvh, ctx = 8, 2, 128
-    q = torch.randn(qh * HD, device="cuda")
-    kc = torch.randn(ctx, kvh, HD, device="cuda").half()
-    vc = torch.randn(ctx, kvh, HD, device="cuda").half()
-    gate = torch.randn(qh * HD, device="cuda")
-    part = torch.zeros(qh * 2 * (HD + 4), device="cuda")
-    ya = torch.zeros(qh * HD, dtype=torch.int16, device="cuda")
-    yb = torch.zeros_like(ya)
-    for p, y in ((ctx - 1, ya), (ctx + 50, yb)):
-        dpos = torch.tensor([p], dtype=torch.int32, device="cuda")
-        assert K.dec_k_attention(ptr(q), ptr(kc), ptr(vc), qh, kvh, HD, 64, ctx, ptr(dpos), ptr(part), ptr(gate),
-                                 ptr(y), None, 0) == 0
-    torch.cuda.synchronize()
-    assert torch.equal(ya, yb)
+    qh, kvh, ctx, ch, pos = 8, 2, 128, 32, 128 + 50
+    c = _attention_case(torch, O, qh, kvh, pos, ctx, ch, 7)
+    _run_attention(K, torch, c, qh, kvh, pos, ctx, ch)
+    assert torch.equal(c["d"]["kc"].cpu(), c["kc0"]) and torch.equal(c["d"]["vc"].cpu(), c["vc0"])
+    qgn = c["qg"].reshape(qh, 2, HD)
+    q = np.stack([_rope(O.rmsnorm(qgn[h, 0], c["qn"], 1e-6), pos, c["nrot"], c["theta"]) for h in range(qh)])
+    kc, vc = c["kc0"].double().numpy(), c["vc0"].double().numpy()
+    ref = np.empty((qh, HD))
+    for h in range(qh):
+        gk = h // (qh // kvh)
+        sc = kc[:, gk] @ q[h] / np.sqrt(HD)
+        e = np.exp(sc - sc.max())
+        ref[h] = (e @ vc[:, gk]) / e.sum()
+    ref *= O.sigmoid(qgn[:, 1])
+    assert rel(h16(c["y"]), ref.reshape(-1)) <= TOL
 
 
 def test_advance_picks_first_max_key_and_follows_the_prompt(cuda, K):
