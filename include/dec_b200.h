@@ -34,7 +34,7 @@ typedef struct {
     int32_t n_rot;           /* rotary dims per head (NeoX pairing i, i+n_rot/2) */
     float   rope_theta;
     float   rms_eps;
-    int32_t max_ctx;         /* KV-cache capacity in positions               */
+    int32_t max_ctx;         /* KV-cache capacity in positions (<= 65536)    */
 } dec_config;
 
 typedef struct dec_model dec_model;

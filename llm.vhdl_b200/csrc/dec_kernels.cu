@@ -201,29 +201,42 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
 
 // Flash-decoding, part 2: combine the chunks of each q head, apply the
 // sigmoid output gate (the raw projection, ref/run9b.c:871-872), to fp16.
-__global__ void dec_attn_combine_kernel(const float *part, const float *gate, int gate_stride, int hd, int nchunks,
-                                        const int32_t *d_pos, int ch, uint16_t *y)
+// One CTA of 128 threads per q head: chunk weights exp(m_c - M) in shared
+// memory, then thread d sums dimension d over the chunks.
+__global__ void __launch_bounds__(128) dec_attn_combine_kernel(const float *part, const float *gate, int gate_stride,
+                                                               int hd, int nchunks, const int32_t *d_pos, int ch,
+                                                               uint16_t *y)
 {
+    __shared__ float wc[1024];
+    __shared__ float red[32];
     PDL_ENTER();
-    const int h = blockIdx.x, lane = threadIdx.x;     // 32 threads, 4 dims each
+    const int h = blockIdx.x, t = threadIdx.x;
     const int used = min(nchunks, (*d_pos + 1 + ch - 1) / ch);
+    const float *ph = part + (size_t)h * nchunks * (hd + 4);
     float M = -INFINITY;
-    for (int c = 0; c < used; c++) M = fmaxf(M, part[((size_t)h * nchunks + c) * (hd + 4)]);
-    float L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int c = 0; c < used; c++) {
-        const float *pp = part + ((size_t)h * nchunks + c) * (hd + 4);
-        const float w = expf(pp[0] - M);
-        L += pp[1] * w;
-        const float4 a = reinterpret_cast<const float4 *>(pp + 4)[lane];
-        a0 += a.x * w; a1 += a.y * w; a2 += a.z * w; a3 += a.w * w;
+    for (int c = t; c < used; c += 128) M = fmaxf(M, ph[(size_t)c * (hd + 4)]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((t & 31) == 0) red[t >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float L = 0.f;
+    for (int c = t; c < used; c += 128) {
+        const float w = expf(ph[(size_t)c * (hd + 4)] - M);
+        wc[c] = w;
+        L += ph[(size_t)c * (hd + 4) + 1] * w;
     }
-    const float inv = 1.0f / L;
-    const float4 gv = reinterpret_cast<const float4 *>(gate + (size_t)h * gate_stride)[lane];
-    uint16_t *yo = y + (size_t)h * hd + 4 * lane;
-    yo[0] = __half_as_ushort(__float2half_rn(a0 * inv * sigm_f(gv.x)));
-    yo[1] = __half_as_ushort(__float2half_rn(a1 * inv * sigm_f(gv.y)));
-    yo[2] = __half_as_ushort(__float2half_rn(a2 * inv * sigm_f(gv.z)));
-    yo[3] = __half_as_ushort(__float2half_rn(a3 * inv * sigm_f(gv.w)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    __syncthreads();
+    if ((t & 31) == 0) red[8 + (t >> 5)] = L;
+    __syncthreads();
+    L = red[8] + red[9] + red[10] + red[11];
+    float a = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < used; c++) a = fmaf(wc[c], ph[(size_t)c * (hd + 4) + 4 + t], a);
+    const float gv = gate[(size_t)h * gate_stride + t];
+    y[(size_t)h * hd + t] = __half_as_ushort(__float2half_rn(a / L * sigm_f(gv)));
 }
 
 __global__ void dec_add_kernel(float *x, const float *t, int n)
@@ -339,6 +352,7 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
 {
     if (kvh <= 0 || qh % kvh || qh / kvh > 32 || ch <= 0 || ch > 64 || (n_rot & 1) || n_rot > ATT_HD) return -11;
     const int nchunks = (max_ctx + ch - 1) / ch;
+    if (nchunks > 1024) return -11;                   // the combine's weight table
     const size_t smem = dec_attention_smem(qh, kvh, ch);
     static int attr_set[64];
     int dev = 0;
@@ -362,7 +376,7 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
                                          d_pos, max_ctx, ch, nchunks, kcache, vcache, q_seam, part));
     if (rc) return rc;
     // the gate is the raw projection: second half of each head's q|gate row
-    return launch(dec_attn_combine_kernel, dim3(qh), dim3(32), s, pdl, part, qg + ATT_HD, 2 * ATT_HD, ATT_HD,
+    return launch(dec_attn_combine_kernel, dim3(qh), dim3(ATT_HD), s, pdl, part, qg + ATT_HD, 2 * ATT_HD, ATT_HD,
                   nchunks, d_pos, ch, y);
 }
 

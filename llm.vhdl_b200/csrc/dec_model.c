@@ -63,7 +63,8 @@ struct dec_model {
     dec_config c;
     int device, rank, world;
     /* local shard sizes */
-    int kh, vh, v0, qh, q0, kvh, kv0, ffn, f0, vocab, voc0, conv_dim, att_ch, nchunks;
+    int kh, vh, v0, qh, q0, kvh, kv0, ffn, f0, vocab, voc0, conv_dim, conv_g, att_ch, nchunks;
+    int32_t  *chan;                      /* host: global conv channel of each local one */
     layer_t  *L;
     linear_t  lm;
     float    *final_norm;
@@ -140,7 +141,7 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     if (c->gdn_hd != HD || c->att_hd != HD || c->hidden % 128 || c->hidden > 16384 || c->ffn % (128 * tp_world)
         || c->gdn_vh % tp_world || c->att_qh % tp_world || c->att_kvh % tp_world || c->att_kvh <= 0
         || (c->att_qh / c->att_kvh) > 32 || c->att_qh % c->att_kvh || c->attn_every < 1
-        || c->n_rot > HD || (c->n_rot & 1) || c->max_ctx <= 0 || c->vocab < tp_world)
+        || c->n_rot > HD || (c->n_rot & 1) || c->max_ctx <= 0 || c->max_ctx > 65536 || c->vocab < tp_world)
         return -11;
     dec_model *m = (dec_model *)calloc(1, sizeof *m);
     if (!m) return -11;
@@ -162,6 +163,7 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     m->L = (layer_t *)calloc((size_t)c->n_layers, sizeof(layer_t));
     const int H = c->hidden, KHg = c->gdn_kh, VHg = c->gdn_vh;
     const int conv_g = 2 * KHg * HD + VHg * HD;
+    m->conv_g = conv_g;
     int rc = 0;
     int32_t *rows = (int32_t *)malloc(sizeof(int32_t) * (size_t)(2 * c->att_qh * HD + conv_g + 2 * VHg + 8));
     int32_t *cidx = (int32_t *)malloc(sizeof(int32_t) * (size_t)conv_g * 4);
@@ -184,6 +186,11 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
             for (int i = 0; i < m->vh; i++)
                 for (int d = 0; d < HD; d++) rows[n++] = 2 * KHg * HD + (m->v0 + i) * HD + d;
             TRY(make_linear(m, &l->qkv, mkey(seed, il, 10), rows, 0, n, 0, H, H));
+            if (!m->chan) {
+                m->chan = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
+                if (!m->chan) { rc = -11; goto bad; }
+                memcpy(m->chan, rows, sizeof(int32_t) * (size_t)n);
+            }
             for (int i = 0; i < n; i++) for (int t = 0; t < 4; t++) cidx[4 * i + t] = rows[i] * 4 + t;
             TRY(make_vec(m, &l->conv_w, mkey(seed, il, 3), cidx, 0, (int64_t)n * 4, 0.0f, 0.5f));
             TRY(make_linear(m, &l->z, mkey(seed, il, 11), NULL, m->v0 * HD, m->vh * HD, 0, H, H));
@@ -264,6 +271,7 @@ int dec_destroy(dec_model *m)
     cudaSetDevice(m->device);
     if (m->comm_ok) ncclCommDestroy(m->comm);
     for (int i = 0; i < m->nalloc; i++) cudaFree(m->allocs[i]);
+    free(m->chan);
     free(m->L);
     free(m);
     return 0;
@@ -318,7 +326,22 @@ int dec_prefill_random(dec_model *m, int len, uint64_t seed)
         } else {
             const int64_t ns = (int64_t)m->vh * HD * HD;
             CK(dec_k_synth_vec(mkey(seed, il, 52), NULL, (int64_t)m->v0 * HD * HD, ns, 0.f, 0.02f, l->rec_state, NULL, NULL));
-            CK(dec_k_synth_vec(mkey(seed, il, 53), NULL, 0, 3 * (int64_t)m->conv_dim, 0.f, 0.5f, l->conv_state, NULL, NULL));
+            /* conv state [3][conv_dim]: draws keyed by (tap, global channel) */
+            const int64_t nc = 3 * (int64_t)m->conv_dim;
+            int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * (size_t)nc);
+            if (!idx) return -11;
+            for (int64_t i = 0; i < nc; i++)
+                idx[i] = (int32_t)((i / m->conv_dim) * m->conv_g + m->chan[i % m->conv_dim]);
+            int32_t *d_idx = NULL;
+            cudaError_t e = cudaMalloc((void **)&d_idx, sizeof(int32_t) * (size_t)nc);
+            if (e == cudaSuccess) e = cudaMemcpy(d_idx, idx, sizeof(int32_t) * (size_t)nc, cudaMemcpyHostToDevice);
+            free(idx);
+            if (e != cudaSuccess) { if (d_idx) cudaFree(d_idx); return fail(e); }
+            int rc = dec_k_synth_vec(mkey(seed, il, 53), d_idx, 0, nc, 0.f, 0.5f, l->conv_state, NULL, NULL);
+            e = cudaDeviceSynchronize();
+            cudaFree(d_idx);
+            if (rc) return rc;
+            if (e != cudaSuccess) return fail(e);
         }
     }
     cudaError_t e = cudaMemcpy(m->pos, &len, 4, cudaMemcpyHostToDevice);

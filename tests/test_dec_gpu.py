@@ -275,6 +275,25 @@ def test_tensor_parallel_shards_are_slices_of_the_whole(pkg, cuda, O, world):
         for R, p in enumerate(parts):
             vh = CFG["gdn_vh"] // world
             assert np.array_equal(p.param(torch, 0, "ssm_a"), a[R * vh:(R + 1) * vh])
+        # the synthetic prefill draws every state entry by its global index
+        for d in [full] + parts:
+            assert d.L.dec_prefill_random(d.h, 40, 9) == 0
+        KH, VH, KVH = CFG["gdn_kh"], CFG["gdn_vh"], CFG["att_kvh"]
+        cg = 2 * KH * HD + VH * HD
+        cs = full.param(torch, 0, "conv_state").reshape(3, cg)
+        st = full.param(torch, 0, "rec_state").reshape(VH, HD, HD)
+        kc = full.param(torch, 3, "kcache", np.float16).reshape(-1, KVH, HD)
+        for R, p in enumerate(parts):
+            vh, kvh = VH // world, KVH // world
+            kh = min(KH, vh)
+            ks = [(R * vh + i) % KH for i in range(kh)]
+            hd = np.arange(HD)
+            chan = np.concatenate([g * HD + hd for g in ks] + [KH * HD + g * HD + hd for g in ks]
+                                  + [2 * KH * HD + (R * vh + i) * HD + hd for i in range(vh)])
+            assert np.array_equal(p.param(torch, 0, "conv_state").reshape(3, -1), cs[:, chan])
+            assert np.array_equal(p.param(torch, 0, "rec_state").reshape(vh, HD, HD), st[R * vh:(R + 1) * vh])
+            pk = p.param(torch, 3, "kcache", np.float16).reshape(-1, kvh, HD)
+            assert np.array_equal(pk[:40], kc[:40, R * kvh:(R + 1) * kvh])
     finally:
         full.close()
         for p in parts:
