@@ -516,6 +516,17 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         dist.broadcast(t, 0)
         uid = (C.c_uint8 * 128)(*t.cpu().tolist())
     assert D.dec_tp_init(h, uid) == 0
+    exchange = "none"
+    if world > 1:
+        # row-parallel sums and argmax keys through peer memory (NVLink stores),
+        # not NCCL: each rank's 64-byte IPC handle goes to every rank
+        import torch.distributed as dist
+        hnd = (C.c_uint8 * 64)()
+        assert D.dec_p2p_handle(h, hnd) == 0
+        allh = [None] * world
+        dist.all_gather_object(allh, bytes(hnd))
+        assert D.dec_p2p_open(h, (C.c_uint8 * (64 * world))(*b"".join(allh)), 0) == 0
+        exchange = "peer memory (one-shot NVLink stores, bounded waits)"
     assert D.dec_prefill_random(h, 8192, 5) == 0
     assert D.dec_set(h, 8192, 1) == 0
     with torch.cuda.stream(stream):
@@ -528,6 +539,8 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
     n = 64
     ms = timed(g.replay, n)
     sbytes = D.dec_step_bytes(h)
+    fl = C.c_int32(0)
+    assert D.dec_status(h, C.byref(fl)) == 0 and fl.value == 0, "peer exchange timed out"
     del g
     D.dec_destroy(h)
     peak, _ = peaks()
@@ -542,6 +555,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         "GBps_per_rank": round(sbytes / (us * 1e-6) / 1e9, 1),
         "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
         "collectives_per_step": (2 * cfg["n_layers"] + 1) if world > 1 else 0,
+        "exchange": exchange,
     }
     return out
 

@@ -57,6 +57,20 @@ int dec_destroy(dec_model *m);
 int dec_nccl_unique_id(uint8_t id[128]);
 int dec_tp_init(dec_model *m, const uint8_t id[128]);
 
+/* Peer-memory exchange for tensor parallel: replaces the NCCL all-reduce of
+ * every row-parallel block and the all-gather of the argmax keys with one-shot
+ * stores into the peers' memory over NVLink (one small kernel each, no NCCL
+ * on the data path).  Every rank calls dec_p2p_handle (it allocates this
+ * rank's exchange region), the host all-gathers the 64-byte handles in rank
+ * order (any transport), and every rank calls dec_p2p_open with all of them.
+ * Waits on peers are bounded by spin_limit polls (<= 0: about a second); a
+ * wait that runs out records a flag and the step goes on, so a rank that never
+ * joins cannot hang the others: dec_status returns the flags (1 all-reduce, 2
+ * key exchange) and clears them. */
+int dec_p2p_handle(dec_model *m, uint8_t handle[64]);
+int dec_p2p_open(dec_model *m, const uint8_t *handles, int spin_limit);
+int dec_status(dec_model *m, int32_t *flags);
+
 /* Fills the first `len` positions of every attention layer's KV cache with
  * N(0,1) fp16 (the benchmark's pre-filled context), the DeltaNet states with
  * N(0, 0.02) and the conv states with N(0, 0.5), and sets the position to len. */

@@ -176,6 +176,9 @@ DEC_EXPORTS = {
     "dec_destroy": (C.c_int, [C.c_void_p]),
     "dec_nccl_unique_id": (C.c_int, [C.c_void_p]),
     "dec_tp_init": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "dec_p2p_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "dec_p2p_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "dec_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "dec_prefill_random": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64]),
     "dec_set": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "dec_set_prompt": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),

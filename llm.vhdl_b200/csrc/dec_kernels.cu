@@ -399,3 +399,172 @@ int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, f
 { return launch(dec_synth_vec_kernel, dim3(148 * 4), dim3(256), s, 0, key, idx, idx0, n, mean, std, f32, f16); }
 
 }  // extern "C"
+
+// ------------------------------------------------- peer-memory exchange
+//
+// Tensor-parallel all-reduce of the row-parallel partial sums and all-gather
+// of the argmax keys over NVLink with plain peer stores (no NCCL, no
+// multicast).  Every rank owns one exchange region, mapped by every peer:
+//   xbuf  float [2][world][hidden]   partial sums, by epoch parity and sender
+//   keys  u64   [2][world]           argmax keys
+//   xflag u32   [2][world][nslices]  epoch stamps, one per (sender, slice)
+//   kflag u32   [2][world]
+// An exchange with epoch E (a per-rank device counter, identical on all
+// ranks because every rank runs the same sequence) writes buffer E & 1; a
+// rank can reach epoch E + 2 only after every peer has stamped epoch E + 1,
+// which each peer does after it finished reading its epoch-E buffer, so two
+// buffers suffice.  Waits are bounded: after `spin_limit` polls the kernel
+// records the failure in `err` and carries on (the step's output is then
+// garbage; the host reads `err`).
+#define X_SLICE 512                      // floats per CTA of the all-reduce
+
+struct PeerRegion {
+    float *xbuf[8];                      // each rank's region, as mapped here
+    unsigned long long *keys[8];
+    uint32_t *xflag[8], *kflag[8];
+};
+
+__device__ __forceinline__ void st_release(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// x[slice] += sum over ranks of their partial t[slice]; one CTA per slice of
+// X_SLICE floats, X_SLICE/4 threads
+__global__ void __launch_bounds__(X_SLICE / 4) dec_ar_kernel(const __grid_constant__ PeerRegion R, int rank,
+                                                             int world, int hidden, const float *t, float *x,
+                                                             uint32_t *epoch, uint32_t *done, int *err,
+                                                             int spin_limit)
+{
+    PDL_ENTER();
+    const int i = blockIdx.x, tid = threadIdx.x, ns = gridDim.x;
+    const uint32_t E = *(volatile uint32_t *)epoch + 1u;
+    const int par = E & 1;
+    const int base = i * X_SLICE + 4 * tid;
+    const bool on = base < hidden;
+    float4 mine = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (on) mine = *reinterpret_cast<const float4 *>(t + base);
+    for (int r = 0; r < world; r++)
+        if (on) *reinterpret_cast<float4 *>(R.xbuf[r] + ((size_t)par * world + rank) * hidden + base) = mine;
+    __threadfence_system();
+    __syncthreads();
+    if (tid < world) st_release(R.xflag[tid] + ((size_t)par * world + rank) * ns + i, E);
+    if (tid < world) {
+        const uint32_t *f = R.xflag[rank] + ((size_t)par * world + tid) * ns + i;
+        int n = 0;
+        while (ld_acquire(f) != E) {
+            if (++n > spin_limit) { atomicOr(err, 1); break; }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    if (on) {
+        float4 a = *reinterpret_cast<const float4 *>(x + base);
+        for (int r = 0; r < world; r++) {
+            const float4 p = __ldcv(reinterpret_cast<const float4 *>(R.xbuf[rank] + ((size_t)par * world + r) * hidden + base));
+            a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+        }
+        *reinterpret_cast<float4 *>(x + base) = a;
+    }
+    __syncthreads();
+    if (tid == 0 && atomicAdd(done, 1u) == (uint32_t)ns - 1) { *done = 0; *epoch = E; }
+}
+
+// the step advance with the argmax keys exchanged through peer memory
+__global__ void dec_advance_p2p_kernel(const __grid_constant__ PeerRegion R, int rank, int world,
+                                       unsigned long long *key, int32_t *tok, int32_t *history, int32_t *pos,
+                                       int max_ctx, const int32_t *prompt, uint32_t *epoch, int *err,
+                                       int spin_limit)
+{
+    PDL_ENTER();
+    const uint32_t E = *epoch + 1u;
+    const int par = E & 1;
+    const unsigned long long mine = *key;
+    for (int r = 0; r < world; r++) R.keys[r][par * world + rank] = mine;
+    __threadfence_system();
+    for (int r = 0; r < world; r++) st_release(R.kflag[r] + par * world + rank, E);
+    unsigned long long best = 0;
+    for (int r = 0; r < world; r++) {
+        const uint32_t *f = R.kflag[rank] + par * world + r;
+        int n = 0;
+        while (ld_acquire(f) != E) {
+            if (++n > spin_limit) { atomicOr(err, 2); break; }
+            __nanosleep(64);
+        }
+        const unsigned long long k = *(volatile unsigned long long *)(R.keys[rank] + par * world + r);
+        best = k > best ? k : best;
+    }
+    *epoch = E;
+    const int32_t tk = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
+    const int p = *pos;
+    if (p < max_ctx) history[p] = tk;
+    const int plen = prompt ? prompt[0] : 0;
+    *tok = (p + 1 < plen) ? prompt[1 + p + 1] : tk;
+    *pos = p + 1;
+    *key = 0;
+}
+
+extern "C" {
+
+// bytes of one exchange region and the offsets of its parts
+size_t dec_p2p_region(int world, int hidden, size_t *off_keys, size_t *off_xflag, size_t *off_kflag)
+{
+    const int ns = (hidden + X_SLICE - 1) / X_SLICE;
+    size_t o = (size_t)2 * world * hidden * 4;
+    o = (o + 127) & ~(size_t)127;
+    if (off_keys) *off_keys = o;
+    o += (size_t)2 * world * 8;
+    o = (o + 127) & ~(size_t)127;
+    if (off_xflag) *off_xflag = o;
+    o += (size_t)2 * world * ns * 4;
+    o = (o + 127) & ~(size_t)127;
+    if (off_kflag) *off_kflag = o;
+    o += (size_t)2 * world * 4;
+    return (o + 127) & ~(size_t)127;
+}
+
+int dec_k_allreduce_p2p(void *const *regions, int rank, int world, int hidden, const float *t, float *x,
+                        uint32_t *epoch, uint32_t *done, int *err, int spin_limit, void *s, int pdl)
+{
+    if (world < 1 || world > 8 || (hidden & 3)) return -11;
+    size_t ok, oxf, okf;
+    dec_p2p_region(world, hidden, &ok, &oxf, &okf);
+    PeerRegion R = {};
+    for (int r = 0; r < world; r++) {
+        uint8_t *b = (uint8_t *)regions[r];
+        R.xbuf[r] = (float *)b;
+        R.keys[r] = (unsigned long long *)(b + ok);
+        R.xflag[r] = (uint32_t *)(b + oxf);
+        R.kflag[r] = (uint32_t *)(b + okf);
+    }
+    const int ns = (hidden + X_SLICE - 1) / X_SLICE;
+    return launch(dec_ar_kernel, dim3(ns), dim3(X_SLICE / 4), s, pdl, R, rank, world, hidden, t, x, epoch, done,
+                  err, spin_limit);
+}
+
+int dec_k_advance_p2p(void *const *regions, int rank, int world, int hidden, unsigned long long *key,
+                      int32_t *tok, int32_t *hist, int32_t *pos, int max_ctx, const int32_t *prompt,
+                      uint32_t *epoch, int *err, int spin_limit, void *s, int pdl)
+{
+    if (world < 1 || world > 8) return -11;
+    size_t ok, oxf, okf;
+    dec_p2p_region(world, hidden, &ok, &oxf, &okf);
+    PeerRegion R = {};
+    for (int r = 0; r < world; r++) {
+        uint8_t *b = (uint8_t *)regions[r];
+        R.xbuf[r] = (float *)b;
+        R.keys[r] = (unsigned long long *)(b + ok);
+        R.xflag[r] = (uint32_t *)(b + oxf);
+        R.kflag[r] = (uint32_t *)(b + okf);
+    }
+    return launch(dec_advance_p2p_kernel, dim3(1), dim3(1), s, pdl, R, rank, world, key, tok, hist, pos, max_ctx,
+                  prompt, epoch, err, spin_limit);
+}
+
+}  // extern "C"

@@ -32,6 +32,12 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl);
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
                   int32_t *pos, int max_ctx, const int32_t *prompt, void *s, int pdl);
+size_t dec_p2p_region(int world, int hidden, size_t *off_keys, size_t *off_xflag, size_t *off_kflag);
+int dec_k_allreduce_p2p(void *const *regions, int rank, int world, int hidden, const float *t, float *x,
+                        uint32_t *epoch, uint32_t *done, int *err, int spin_limit, void *s, int pdl);
+int dec_k_advance_p2p(void *const *regions, int rank, int world, int hidden, unsigned long long *key,
+                      int32_t *tok, int32_t *hist, int32_t *pos, int max_ctx, const int32_t *prompt,
+                      uint32_t *epoch, int *err, int spin_limit, void *s, int pdl);
 int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
                        uint8_t *wq, uint16_t *sc, int s_pitch, void *s);
 int dec_k_synth_vec(uint64_t key, const int32_t *idx, int64_t idx0, int64_t n, float mean, float std,
@@ -79,6 +85,11 @@ struct dec_model {
     int       hpos;                      /* host mirror of *pos for direct calls */
     ncclComm_t comm;
     int       comm_ok;
+    /* peer-memory exchange (tensor parallel without NCCL on the data path) */
+    void     *p2p_region, *p2p_peer[8];
+    int       p2p_ok, p2p_open[8], spin_limit;
+    uint32_t *ar_epoch, *ar_done, *ak_epoch;
+    int      *err;
     int64_t   weight_bytes;
     void     *allocs[MAX_ALLOCS];
     int       nalloc;
@@ -252,6 +263,10 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->tok, 4));
     TRY(dalloc(m, (void **)&m->pos, 4));
     TRY(dalloc(m, (void **)&m->hist, 4 * (size_t)c->max_ctx));
+    TRY(dalloc(m, (void **)&m->ar_epoch, 16));
+    TRY(dalloc(m, (void **)&m->ar_done, 16));
+    TRY(dalloc(m, (void **)&m->ak_epoch, 16));
+    TRY(dalloc(m, (void **)&m->err, 16));
     TRY(dalloc(m, (void **)&m->prompt, 4 * ((size_t)c->max_ctx + 1)));
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { rc = fail(e); goto bad; }
@@ -270,6 +285,7 @@ int dec_destroy(dec_model *m)
     if (!m) return -11;
     cudaSetDevice(m->device);
     if (m->comm_ok) ncclCommDestroy(m->comm);
+    for (int r = 0; r < 8; r++) if (m->p2p_open[r]) cudaIpcCloseMemHandle(m->p2p_peer[r]);
     for (int i = 0; i < m->nalloc; i++) cudaFree(m->allocs[i]);
     free(m->chan);
     free(m->L);
@@ -294,6 +310,53 @@ int dec_tp_init(dec_model *m, const uint8_t id[128])
     cudaSetDevice(m->device);
     if (ncclCommInitRank(&m->comm, m->world, u, m->rank) != ncclSuccess) return -20;
     m->comm_ok = 1;
+    return 0;
+}
+
+int dec_p2p_handle(dec_model *m, uint8_t handle[64])
+{
+    if (!m || !handle || m->world < 2 || m->world > 8) return -11;
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e != cudaSuccess) return fail(e);
+    if (!m->p2p_region) {
+        const size_t bytes = dec_p2p_region(m->world, m->c.hidden, NULL, NULL, NULL);
+        CK(dalloc(m, &m->p2p_region, bytes));
+    }
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, m->p2p_region);
+    if (e != cudaSuccess) return fail(e);
+    memcpy(handle, &h, 64);
+    return 0;
+}
+
+int dec_p2p_open(dec_model *m, const uint8_t *handles, int spin_limit)
+{
+    if (!m || !handles || !m->p2p_region) return -11;
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e != cudaSuccess) return fail(e);
+    for (int r = 0; r < m->world; r++) {
+        if (r == m->rank) { m->p2p_peer[r] = m->p2p_region; continue; }
+        if (m->p2p_open[r]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + 64 * (size_t)r, 64);
+        e = cudaIpcOpenMemHandle(&m->p2p_peer[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return fail(e);
+        m->p2p_open[r] = 1;
+    }
+    m->spin_limit = spin_limit > 0 ? spin_limit : (1 << 22);
+    m->p2p_ok = 1;
+    return 0;
+}
+
+int dec_status(dec_model *m, int32_t *flags)
+{
+    if (!m || !flags) return -11;
+    int v = 0;
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e == cudaSuccess) e = cudaMemcpy(&v, m->err, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(m->err, 0, 4);
+    if (e != cudaSuccess) return fail(e);
+    *flags = v;
     return 0;
 }
 
@@ -409,15 +472,18 @@ static int row_parallel(dec_model *m, dmv_params *P, const linear_t *l, void *s)
     P->njobs = 1;
     CK(dec_k_matvec(P, s, m->pdl));
     if (m->world == 1) return 0;
+    if (m->p2p_ok)
+        return dec_k_allreduce_p2p(m->p2p_peer, m->rank, m->world, m->c.hidden, m->t, m->x, m->ar_epoch,
+                                   m->ar_done, m->err, m->spin_limit, s, m->pdl && s != NULL);
     if (ncclAllReduce(m->t, m->t, (size_t)m->c.hidden, ncclFloat32, ncclSum, m->comm, (cudaStream_t)s)
         != ncclSuccess) return -20;
-    return dec_k_add(m->x, m->t, m->c.hidden, s, m->pdl);
+    return dec_k_add(m->x, m->t, m->c.hidden, s, m->pdl && s != NULL);
 }
 
 int dec_step(dec_model *m, void *s)
 {
     if (!m) return -11;
-    if (m->world > 1 && !m->comm_ok) return -11;
+    if (m->world > 1 && !m->comm_ok && !m->p2p_ok) return -11;
     if (m->hpos >= m->c.max_ctx) return -11;   /* the KV cache is full */
     m->hpos++;
     const dec_config *c = &m->c;
@@ -479,6 +545,9 @@ int dec_step(dec_model *m, void *s)
     P.jobs[0].out_f32 = m->logits;
     P.key = m->key; P.idx0 = m->voc0; P.njobs = 1;
     CK(dec_k_matvec(&P, s, pdl));
+    if (m->world > 1 && m->p2p_ok)
+        return dec_k_advance_p2p(m->p2p_peer, m->rank, m->world, H, m->key, m->tok, m->hist, m->pos, c->max_ctx,
+                                 m->prompt, m->ak_epoch, m->err, m->spin_limit, s, pdl);
     if (m->world > 1) {
         if (ncclAllGather(m->key, m->keys, 1, ncclUint64, m->comm, (cudaStream_t)s) != ncclSuccess) return -20;
         return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);

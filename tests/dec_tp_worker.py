@@ -3,8 +3,11 @@
 Tensor-parallel decode: every rank builds its shard of the same model
 (dec_create with tp_rank / tp_world), rank 0's NCCL id reaches the others over
 a gloo group, and all ranks step the same tokens; the row-parallel blocks sum
-over NCCL inside dec_step and the vocabulary-sharded argmax keys are
-all-gathered.  Rank 0 also runs the unsharded model on its GPU and checks that
+inside dec_step -- over NCCL (DEC_TP_MODE=nccl) or through peer memory
+(DEC_TP_MODE=p2p, handles all-gathered over gloo) -- and the
+vocabulary-sharded argmax keys are all-gathered.  DEC_TP_MODE=p2p_missing:
+rank 1 never steps, and rank 0's bounded waits must run out and be reported
+by dec_status (the failure is made on the host; no GPU hangs or faults).  Rank 0 also runs the unsharded model on its GPU and checks that
 the gathered logits agree within 1e-3 of the largest |logit| and that the
 tokens agree wherever the top-2 margin exceeds that.  Exits 0 on success.
 """
@@ -59,6 +62,35 @@ def main():
     uid = (C.c_uint8 * 128)(*t.tolist())
     d = Dec(pkg, device=rank, rank=rank, world=world)
     assert L.dec_tp_init(d.h, uid) == 0
+    mode = os.environ.get("DEC_TP_MODE", "nccl")
+    if mode.startswith("p2p"):
+        hnd = (C.c_uint8 * 64)()
+        assert L.dec_p2p_handle(d.h, hnd) == 0
+        allh = [None] * world
+        dist.all_gather_object(allh, bytes(hnd))
+        buf = (C.c_uint8 * (64 * world))(*b"".join(allh))
+        assert L.dec_p2p_open(d.h, buf, 20000 if mode == "p2p_missing" else 0) == 0
+    if mode == "p2p_missing":
+        # rank 1 never steps: rank 0's bounded waits run out and say so
+        ok = True
+        if rank == 0:
+            assert L.dec_prefill_random(d.h, PREFILL, 5) == 0
+            assert L.dec_set(d.h, PREFILL, 7) == 0
+            d.step(torch)
+            torch.cuda.synchronize()
+            fl = C.c_int32(0)
+            assert L.dec_status(d.h, C.byref(fl)) == 0
+            print("flags", fl.value)
+            ok = fl.value == 3
+            assert L.dec_status(d.h, C.byref(fl)) == 0 and fl.value == 0          # cleared
+        dist.barrier()                          # rank 1 keeps its memory mapped until rank 0 is done
+        d.close()
+        flag = torch.tensor([1 if ok else 0])
+        dist.broadcast(flag, 0)
+        dist.destroy_process_group()
+        if rank == 0 and ok:
+            print("DEC_TP_OK")
+        sys.exit(0 if int(flag.item()) else 1)
     assert L.dec_prefill_random(d.h, PREFILL, 5) == 0
     assert L.dec_set(d.h, PREFILL, 7) == 0
     logits, hist, v0 = run(pkg, torch, d, STEPS)
@@ -85,6 +117,10 @@ def main():
                     ok = False
                 break                       # the inputs diverge from here on
         full.close()
+    if mode == "p2p":
+        fl = C.c_int32(0)
+        assert L.dec_status(d.h, C.byref(fl)) == 0
+        ok = ok and fl.value == 0
     d.close()
     flag = torch.tensor([1 if ok else 0])
     dist.broadcast(flag, 0)

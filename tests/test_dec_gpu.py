@@ -335,15 +335,15 @@ def test_decode_step_replays_from_a_cuda_graph(pkg, cuda, O):
         b.close()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_tensor_parallel_decode_over_nccl(cuda, world):
+@pytest.mark.parametrize("world,mode", [(2, "nccl"), (4, "nccl"), (2, "p2p"), (4, "p2p"), (2, "p2p_missing")])
+def test_tensor_parallel_decode(cuda, world, mode):
     torch = cuda
     n = torch.cuda.device_count()
     if n < world:
         pytest.skip("needs %d GPUs" % world)
     ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     s = socket.socket(); s.bind(("127.0.0.1", 0)); port = s.getsockname()[1]; s.close()
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DEC_TP_MODE=mode)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(port),
            os.path.join(ROOT, "tests", "dec_tp_worker.py")]
