@@ -29,9 +29,7 @@ extern "C" int mv4i_g_cuda_err;
 
 #define DMV_THREADS 256
 #define DMV_WARPS 8
-#ifndef DMV_G
 #define DMV_G 4                    // rows a warp streams together (2 gate/up pairs)
-#endif
 #ifndef DMV_MINB
 #define DMV_MINB 2                 // resident CTAs per SM the registers are sized for
 #endif
@@ -436,31 +434,50 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
             dmv_loads<NR>(wr, sr, p, p < p1, w, sc);
             if (p < p1) dmv_dots<NR>(s, np, p, w, sc, acc);
         }
+        // warp totals by a transposing butterfly: 6 shuffles for 4 values
+        // (10 for 2 gate/up pairs) instead of 20; lane L ends with value
+        // (L >> 3) & 3 (unpaired) or the pair (L >> 4) (paired)
+        const bool hi = lane & 16;
+        float k0 = hi ? acc[2] : acc[0], k1 = hi ? acc[3] : acc[1];
+        k0 += __shfl_xor_sync(0xffffffffu, hi ? acc[0] : acc[2], 16);
+        k1 += __shfl_xor_sync(0xffffffffu, hi ? acc[1] : acc[3], 16);
+        float v0, v1;
+        int vi;
+        bool holder;
+        if (PAIRED) {
 #pragma unroll
-        for (int k = 0; k < NR; k++)
+            for (int o = 8; o; o >>= 1) {
+                k0 += __shfl_xor_sync(0xffffffffu, k0, o);
+                k1 += __shfl_xor_sync(0xffffffffu, k1, o);
+            }
+            v0 = k0; v1 = k1; vi = lane >> 4; holder = (lane & 15) == 0;
+        } else {
+            const bool b3 = lane & 8;
+            float k = b3 ? k1 : k0;
+            k += __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
 #pragma unroll
-            for (int o = 16; o; o >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
+            for (int o = 4; o; o >>= 1) k += __shfl_xor_sync(0xffffffffu, k, o);
+            v0 = k; v1 = 0.f; vi = (lane >> 3) & 3; holder = (lane & 7) == 0;
+        }
         if (ks > 1) {
-            if (lane == 0) {
-#pragma unroll
-                for (int k = 0; k < NR; k++) red[(rs * NR + k) * DMV_WARPS + kq] = acc[k];
+            if (holder) {
+                red[((rs * 4 + vi) * 2 + 0) * DMV_WARPS + kq] = v0;
+                red[((rs * 4 + vi) * 2 + 1) * DMV_WARPS + kq] = v1;
             }
             __syncthreads();
-            if (kq == 0 && lane == 0) {
-#pragma unroll
-                for (int k = 0; k < NR; k++) {
-                    float v = 0.f;
-                    for (int q = 0; q < ks; q++) v += red[(rs * NR + k) * DMV_WARPS + q];
-                    acc[k] = v;
+            if (kq == 0 && holder) {
+                float a = 0.f, b2 = 0.f;
+                for (int q = 0; q < ks; q++) {
+                    a += red[((rs * 4 + vi) * 2 + 0) * DMV_WARPS + q];
+                    b2 += red[((rs * 4 + vi) * 2 + 1) * DMV_WARPS + q];
                 }
+                v0 = a; v1 = b2;
             }
             __syncthreads();
         }
-        if (lane == 0 && kq == 0) {
-#pragma unroll
-            for (int i = 0; i < G; i++)
-                if (i < g && rows[i] < J.rows)
-                    dmv_epilogue(P, J, rows[i], PAIRED ? acc[2 * i] : acc[i], PAIRED ? acc[2 * i + 1] : 0.f, best);
+        if (kq == 0 && holder && vi < g) {
+            const int row = (t + vi - J.tile0) * rt + rs;
+            if (row < J.rows) dmv_epilogue(P, J, row, v0, v1, best);
         }
     }
 }
@@ -469,7 +486,7 @@ __global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid
 {
     extern __shared__ __align__(128) uint8_t dmv_sm[];
     __shared__ dmv_job JS[DMV_MAXJ];
-    __shared__ float red[DMV_WARPS * DMV_G * DMV_WARPS];
+    __shared__ float red[DMV_WARPS * 4 * 2 * DMV_WARPS];
     if (threadIdx.x < P.njobs) JS[threadIdx.x] = P.jobs[threadIdx.x];
     __syncthreads();
     const int T = P.total_tiles;
