@@ -439,6 +439,39 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
                 raise RuntimeError("dec_step failed %d" % rc)
         return f
 
+    def layer_profile(h, cfg):
+        """One direct step with an event after every layer: per-layer time and
+        the fraction of the HBM peak its bytes reach (DeltaNet / attention
+        layers and the LM head, averaged by kind).  Events between kernels
+        stop programmatic launches from overlapping layer boundaries, so these
+        fractions are a little below the graph-replay rate."""
+        peak, _ = peaks()
+        nl = cfg["n_layers"]
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(nl + 2)]
+        arr = (C.c_void_p * nl)(*[C.c_void_p(e.cuda_event) for e in evs[1:nl + 1]])
+        assert D.dec_set_layer_events(h, arr, nl) == 0
+        lb = [D.dec_layer_bytes(h, il) for il in range(nl)] + [D.dec_layer_bytes(h, -1)]
+        with torch.cuda.stream(stream):
+            evs[0].record(stream)
+            step_fn(h)()
+            evs[nl + 1].record(stream)
+        torch.cuda.synchronize(dev)
+        assert D.dec_set_layer_events(h, None, 0) == 0
+        kinds = {"deltanet": [], "attention": [], "lm_head": []}
+        for il in range(nl + 1):
+            us = evs[il].elapsed_time(evs[il + 1]) * 1e3
+            kind = "lm_head" if il == nl else ("attention" if (il + 1) % cfg["attn_every"] == 0 else "deltanet")
+            kinds[kind].append((us, lb[il]))
+        out = {}
+        for k, v in kinds.items():
+            if not v:
+                continue
+            us = sum(x[0] for x in v) / len(v)
+            b = sum(x[1] for x in v) / len(v)
+            out[k] = {"layers": len(v), "us": round(us, 2), "bytes": int(b),
+                      "frac_hbm": round(b / (us * 1e-6) / 1e9 / peak, 4)}
+        return out
+
     def capture(h):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -483,6 +516,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
                     stream.synchronize()
         e2e_ms = timed(e2e_run, 1)
         sbytes = D.dec_step_bytes(h)
+        per_layer = layer_profile(h, cfg)
         del g
         D.dec_destroy(h)
         peak, _ = peaks()
@@ -497,6 +531,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
             "GBps": round(sbytes / (us * 1e-6) / 1e9, 1),
             "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
             "first_tokens": [int(t) for t in toks[:8]],
+            "per_layer": per_layer,
             "e2e": {"tokens_per_s": round((511 + gen) / (e2e_ms * 1e-3), 1),
                     "how": "prompt H2D from pinned host, 767 graph replays, each generated token D2H "
                            "(pinned) and synchronised as produced",
@@ -539,6 +574,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
     n = 64
     ms = timed(g.replay, n)
     sbytes = D.dec_step_bytes(h)
+    per_layer = layer_profile(h, cfg)
     fl = C.c_int32(0)
     assert D.dec_status(h, C.byref(fl)) == 0 and fl.value == 0, "peer exchange timed out"
     del g
@@ -554,10 +590,38 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         "bytes_per_step_per_rank": sbytes,
         "GBps_per_rank": round(sbytes / (us * 1e-6) / 1e9, 1),
         "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
+        "per_layer_rank0": per_layer,
         "collectives_per_step": (2 * cfg["n_layers"] + 1) if world > 1 else 0,
         "exchange": exchange,
     }
     return out
+
+
+def profile_decode(args):
+    """`--only decode3|decode4`: a short run for profilers -- one model, the
+    KV context pre-filled (512 or 8192 positions), `--warmup` then `--steps`
+    direct steps on a stream (programmatic dependent launches on)."""
+    import torch
+    pkg = load_pkg()
+    D = pkg.declib()
+    cfg, pre = (DEC_C3, 512) if args.only == "decode3" else (DEC_C4, 8192)
+    h = C.c_void_p()
+    assert D.dec_create(C.byref(pkg.DecConfig(**cfg)), 2, 0, 0, 1, C.byref(h)) == 0
+    assert D.dec_prefill_random(h, pre, 3) == 0
+    assert D.dec_set(h, pre, 1) == 0
+    s = torch.cuda.Stream()
+    sp = C.c_void_p(s.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            assert D.dec_step(h, sp) == 0
+        e0.record(s)
+        for _ in range(args.steps):
+            assert D.dec_step(h, sp) == 0
+        e1.record(s)
+    torch.cuda.synchronize()
+    print(json.dumps({"only": args.only, "steps": args.steps, "ms_per_step": e0.elapsed_time(e1) / args.steps}))
+    D.dec_destroy(h)
 
 
 def gdn_cpu_baseline(budget_s=3.0):
@@ -589,6 +653,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--stack", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["decode3", "decode4"], default=None,
+                    help="profiling aid: build one decode model, run --steps direct steps, print ms/step")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -615,6 +681,10 @@ def main():
                                        "processes" % (args.warmup + args.steps, P)},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}))
+        return
+
+    if args.only:
+        profile_decode(args)
         return
 
     if world > 1:

@@ -124,6 +124,14 @@ int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int
 /* Bytes of weights, KV cache and state one step reads on this rank. */
 int64_t dec_step_bytes(dec_model *m);
 
+/* Per-layer accounting: dec_layer_bytes is what layer `layer` reads in one
+ * step on this rank (layer -1: LM head and embedding row); with
+ * dec_set_layer_events (n cudaEvent_t handles, NULL/0 to stop) dec_step
+ * records events[il] on its stream after layer il, so the host can time each
+ * layer (record a start event before the step). */
+int64_t dec_layer_bytes(dec_model *m, int layer);
+int dec_set_layer_events(dec_model *m, void **events, int n);
+
 #ifdef __cplusplus
 }
 #endif

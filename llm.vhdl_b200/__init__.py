@@ -192,6 +192,8 @@ DEC_EXPORTS = {
     "dec_param": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_void_p),
                             C.POINTER(C.c_int32)]),
     "dec_step_bytes": (C.c_int64, [C.c_void_p]),
+    "dec_layer_bytes": (C.c_int64, [C.c_void_p, C.c_int]),
+    "dec_set_layer_events": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
 }
 
 _declib = None

@@ -79,6 +79,8 @@ struct dec_model {
     float    *x, *t, *qkv_f, *z_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *part, *logits;
     uint16_t *h16, *qkv16, *y16, *ya16, *hf16;
     int       pdl;                       /* programmatic dependent launches     */
+    void    **lev;                       /* optional: event after each layer    */
+    int       nlev;
     unsigned long long *key, *keys;
     int32_t  *tok, *pos, *hist;
     int32_t  *prompt;                    /* [0] = length, [1..] = tokens     */
@@ -538,6 +540,8 @@ int dec_step(dec_model *m, void *s)
         CK(dec_k_matvec(&P, s, pdl));
         mvparams(&P, m->ffn, DMV_OP_F16, m->hf16, NULL, 0.f, NULL);
         CK(row_parallel(m, &P, &l->down, s));
+        if (m->lev && il < m->nlev && cudaEventRecord((cudaEvent_t)m->lev[il], (cudaStream_t)s) != cudaSuccess)
+            return -20;
     }
     /* LM head with the first-max argmax key in its epilogue */
     mvparams(&P, H, DMV_OP_RMSNORM, m->x, m->final_norm, c->rms_eps, m->h16);
@@ -553,6 +557,42 @@ int dec_step(dec_model *m, void *s)
         return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);
     }
     return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);
+}
+
+int dec_set_layer_events(dec_model *m, void **events, int n)
+{
+    if (!m || n < 0 || (n && !events)) return -11;
+    m->lev = n ? events : NULL;
+    m->nlev = n;
+    return 0;
+}
+
+int64_t dec_layer_bytes(dec_model *m, int layer)
+{
+    if (!m || layer < -1 || layer >= m->c.n_layers) return -11;
+    const linear_t *ls[8];
+    int n = 0;
+    int64_t b = 0;
+    if (layer < 0) {
+        ls[n++] = &m->lm;
+        b += (int64_t)m->c.hidden * 2;                 /* the embedding row */
+    } else {
+        const layer_t *l = &m->L[layer];
+        if (l->attn) {
+            ls[n++] = &l->qg; ls[n++] = &l->kv; ls[n++] = &l->o;
+            int pos = 0;
+            cudaSetDevice(m->device);
+            cudaMemcpy(&pos, m->pos, 4, cudaMemcpyDeviceToHost);
+            b += (int64_t)2 * (pos + 1) * m->kvh * HD * 2;            /* K and V up to the position */
+        } else {
+            ls[n++] = &l->qkv; ls[n++] = &l->z; ls[n++] = &l->ab; ls[n++] = &l->out;
+            b += (int64_t)2 * m->vh * HD * HD * 4 + (int64_t)2 * 3 * m->conv_dim * 4;   /* states r+w */
+        }
+        ls[n++] = &l->gate; ls[n++] = &l->up; ls[n++] = &l->down;
+    }
+    for (int i = 0; i < n; i++)
+        b += (int64_t)ls[i]->rows * ls[i]->cols / 2 + (int64_t)ls[i]->rows * (ls[i]->cols / 128) * 2;
+    return b;
 }
 
 int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residual, int32_t **pos,

@@ -121,7 +121,9 @@ def seam_ok(got16, want):
     assert np.mean(diff) <= 0.01, np.mean(diff)
 
 
-@pytest.mark.parametrize("K,rows", [(128, 1), (2048, 7), (2048, 2048), (5120, 33), (17408, 64), (6144, 300)])
+# tall and short K, few and many rows per warp, the column split over warps
+@pytest.mark.parametrize("K,rows", [(128, 1), (2048, 7), (2048, 2048), (5120, 33), (17408, 64), (6144, 300),
+                                    (4096, 5120), (17408, 5120), (2048, 20000)])
 def test_f16_input_staged_product(cuda, L, O, K, rows):
     torch = cuda
     wq, sc = weights(torch, rows, K, K + rows)
@@ -188,9 +190,9 @@ def test_gated_prologue(cuda, L, O):
     assert rel(y.cpu().numpy().astype(np.float64), ref) <= 2e-6
 
 
-def test_paired_swiglu_epilogue(cuda, L, O):
+@pytest.mark.parametrize("K,F", [(2048, 640), (5120, 5120)])
+def test_paired_swiglu_epilogue(cuda, L, O, K, F):
     torch = cuda
-    K, F = 2048, 640
     wg, sg = weights(torch, F, K, 21)
     wu, su = weights(torch, F, K, 22)
     x = torch.randn(K, generator=torch.Generator().manual_seed(23)).half().cuda()
