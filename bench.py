@@ -448,6 +448,9 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         peak, _ = peaks()
         nl = cfg["n_layers"]
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(nl + 2)]
+        for e in evs:                       # torch creates the CUDA event on first record
+            e.record(stream)
+        torch.cuda.synchronize(dev)
         arr = (C.c_void_p * nl)(*[C.c_void_p(e.cuda_event) for e in evs[1:nl + 1]])
         assert D.dec_set_layer_events(h, arr, nl) == 0
         lb = [D.dec_layer_bytes(h, il) for il in range(nl)] + [D.dec_layer_bytes(h, -1)]
