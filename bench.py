@@ -418,7 +418,7 @@ class _DevArray:
 def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank):
     """Decode tokens/s through include/dec_b200.h, one step per CUDA-graph
     replay.  Config 3 (1 GPU): 512-token random-id prompt fed through the
-    decode step, then 256 greedy tokens, batch 1.  Config 4: tensor parallel
+    decode step, then 256 greedy tokens, at batch 1 and batch 8.  Config 4: tensor parallel
     over the `world` ranks (NCCL all-reduce per row-parallel block), KV
     context pre-filled to 8192 with N(0,1), batch 1."""
     import numpy as np
@@ -481,11 +481,16 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
             step_fn(h)()
         return g
 
-    if world == 1:
-        cfg = DEC_C3
+    def run_c3(nb):
+        """Config 3 at batch nb: nb random-id prompts of 512 tokens (sequence
+        0's is the batch-1 prompt), fed through the decode step, then 256
+        greedy tokens per sequence; tokens/s counts every sequence."""
+        cfg = dict(DEC_C3, batch=nb)
         h = create(cfg, 2, 0, 1)
-        prompt = np.random.default_rng(2).integers(0, cfg["vocab"], 512).astype(np.int32)
-        pa = C.cast((C.c_int32 * 512)(*prompt.tolist()), C.c_void_p)
+        prompt = np.stack([np.random.default_rng(2 + 1000 * b).integers(0, cfg["vocab"], 512)
+                           for b in range(nb)]).astype(np.int32)
+        hprompt = torch.from_numpy(prompt).pin_memory()
+        pa = C.c_void_p(hprompt.data_ptr())
         assert D.dec_set_prompt(h, pa, 512, sp) == 0
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -501,21 +506,20 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         torch.cuda.synchronize(dev)
         hp = C.c_void_p()
         assert D.dec_pointers(h, None, C.byref(hp), None, None, None, None) == 0
-        hist = torch.as_tensor(_DevArray(hp.value, cfg["max_ctx"], "<i4"), device=dev)
-        toks = hist[511:511 + gen].cpu().numpy()
-        # end to end: the prompt from pinned host memory, and each generated
-        # token read back to pinned host memory as it is produced
-        hprompt = torch.from_numpy(prompt).pin_memory()
-        htok = torch.empty(1, dtype=torch.int32).pin_memory()
+        hist = torch.as_tensor(_DevArray(hp.value, nb * cfg["max_ctx"], "<i4"), device=dev).view(nb, -1)
+        toks = hist[:, 511:511 + gen].cpu().numpy()
+        # end to end: the prompts from pinned host memory, and each step's
+        # generated tokens read back to pinned host memory as they are produced
+        htok = torch.empty(nb, dtype=torch.int32).pin_memory()
 
         def e2e_run():
-            assert D.dec_set_prompt(h, C.c_void_p(hprompt.data_ptr()), 512, sp) == 0
+            assert D.dec_set_prompt(h, pa, 512, sp) == 0
             with torch.cuda.stream(stream):
                 for _ in range(511):
                     g.replay()
                 for i in range(gen):
                     g.replay()
-                    htok.copy_(hist[511 + i:512 + i], non_blocking=True)
+                    htok.copy_(hist[:, 511 + i], non_blocking=True)
                     stream.synchronize()
         e2e_ms = timed(e2e_run, 1)
         sbytes = D.dec_step_bytes(h)
@@ -524,23 +528,27 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         D.dec_destroy(h)
         peak, _ = peaks()
         us = ms_gen * 1e3 / gen
-        out["config3"] = {
+        return {
             "workload": "config 3: 24-layer hybrid (18 DeltaNet + 6 gated attention), hidden 2048, vocab 151936, "
-                        "INT4 g128, seed 2; 512-token random-id prompt, 256 greedy tokens, batch 1",
-            "tokens_per_s": round(gen / (ms_gen * 1e-3), 1),
-            "us_per_token": round(us, 2),
-            "prompt_tokens_per_s": round(511 / (ms_prompt * 1e-3), 1),
+                        "INT4 g128, seed 2; 512-token random-id prompt, 256 greedy tokens, batch %d" % nb,
+            "batch": nb,
+            "tokens_per_s": round(nb * gen / (ms_gen * 1e-3), 1),
+            "us_per_step": round(us, 2),
+            "prompt_tokens_per_s": round(nb * 511 / (ms_prompt * 1e-3), 1),
             "bytes_per_step": sbytes,
             "GBps": round(sbytes / (us * 1e-6) / 1e9, 1),
             "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
-            "first_tokens": [int(t) for t in toks[:8]],
+            "first_tokens": [int(t) for t in toks[0, :8]],
             "per_layer": per_layer,
-            "e2e": {"tokens_per_s": round((511 + gen) / (e2e_ms * 1e-3), 1),
-                    "how": "prompt H2D from pinned host, 767 graph replays, each generated token D2H "
+            "e2e": {"tokens_per_s": round(nb * (511 + gen) / (e2e_ms * 1e-3), 1),
+                    "how": "prompts H2D from pinned host, 767 graph replays, each step's generated tokens D2H "
                            "(pinned) and synchronised as produced",
-                    "h2d_bytes": 512 * 4, "d2h_bytes_per_token": 4},
-            "batch8": None,
+                    "h2d_bytes": nb * 512 * 4, "d2h_bytes_per_step": nb * 4},
         }
+
+    if world == 1:
+        out["config3"] = run_c3(1)
+        out["config3"]["batch8"] = run_c3(8)
 
     # config 4, tensor parallel over all ranks
     cfg = DEC_C4
@@ -601,13 +609,15 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
 
 
 def profile_decode(args):
-    """`--only decode3|decode4`: a short run for profilers -- one model, the
-    KV context pre-filled (512 or 8192 positions), `--warmup` then `--steps`
-    direct steps on a stream (programmatic dependent launches on)."""
+    """`--only decode3|decode4`: a short run for profilers -- one model
+    (`--batch` sequences), the KV context pre-filled (512 or 8192 positions),
+    `--warmup` then `--steps` direct steps on a stream (programmatic
+    dependent launches on)."""
     import torch
     pkg = load_pkg()
     D = pkg.declib()
     cfg, pre = (DEC_C3, 512) if args.only == "decode3" else (DEC_C4, 8192)
+    cfg = dict(cfg, batch=args.batch)
     h = C.c_void_p()
     assert D.dec_create(C.byref(pkg.DecConfig(**cfg)), 2, 0, 0, 1, C.byref(h)) == 0
     assert D.dec_prefill_random(h, pre, 3) == 0
@@ -623,7 +633,8 @@ def profile_decode(args):
             assert D.dec_step(h, sp) == 0
         e1.record(s)
     torch.cuda.synchronize()
-    print(json.dumps({"only": args.only, "steps": args.steps, "ms_per_step": e0.elapsed_time(e1) / args.steps}))
+    print(json.dumps({"only": args.only, "batch": args.batch, "steps": args.steps,
+                      "ms_per_step": e0.elapsed_time(e1) / args.steps}))
     D.dec_destroy(h)
 
 
@@ -658,6 +669,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["decode3", "decode4"], default=None,
                     help="profiling aid: build one decode model, run --steps direct steps, print ms/step")
+    ap.add_argument("--batch", type=int, default=1, help="sequences of the --only decode model")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

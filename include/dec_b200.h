@@ -35,6 +35,11 @@ typedef struct {
     float   rope_theta;
     float   rms_eps;
     int32_t max_ctx;         /* KV-cache capacity in positions (<= 65536)    */
+    int32_t batch;           /* independent sequences decoded together, 1..8
+                                (0 means 1; more than 1 only with tp_world 1).
+                                They share every weight read of a step and
+                                the position; each has its own token, KV
+                                cache, DeltaNet and conv states and history */
 } dec_config;
 
 typedef struct dec_model dec_model;
@@ -73,15 +78,16 @@ int dec_status(dec_model *m, int32_t *flags);
 
 /* Fills the first `len` positions of every attention layer's KV cache with
  * N(0,1) fp16 (the benchmark's pre-filled context), the DeltaNet states with
- * N(0, 0.02) and the conv states with N(0, 0.5), and sets the position to len. */
+ * N(0, 0.02) and the conv states with N(0, 0.5), and sets the position to len.
+ * Sequence b of a batch draws from seed ^ (b * 0x9E3779B97F4A7C15). */
 int dec_prefill_random(dec_model *m, int len, uint64_t seed);
 
-/* Sets the position and the current input token (host values); clears any
- * prompt. */
+/* Sets the position and the current input token of every sequence (host
+ * values); clears any prompt. */
 int dec_set(dec_model *m, int pos, int token);
 
-/* Starts a sequence from position 0 (DeltaNet and conv states zeroed) with a
- * prompt of n tokens (host array):
+/* Starts the batch's sequences from position 0 (DeltaNet and conv states
+ * zeroed) with prompts of n tokens each (host array [batch][n]):
  * steps 0 .. n-2 take the prompt's next token as their next input (teacher
  * forcing, ref/run9b.c's --tokens loop), later steps their own argmax.  The
  * prediction of every step is recorded in the history at its position, so
@@ -98,8 +104,8 @@ int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream);
 int dec_step(dec_model *m, void *stream);
 
 /* Device pointers for inspection: the fp32 logits of the last step (this
- * rank's vocabulary shard), the token history [max_ctx], the fp32 residual
- * [hidden], the position. */
+ * rank's vocabulary shard, [batch][vocab_n]), the token history
+ * [batch][max_ctx], the fp32 residual [batch][hidden], the position. */
 int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residual, int32_t **pos,
                  int32_t *vocab0, int32_t *vocab_n);
 
@@ -112,16 +118,19 @@ int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, 
 
 /* Parameter and state vectors: "attn_norm", "post_norm", "conv_w"
  * ([conv_dim][4]), "ssm_a", "dt_bias", "ssm_norm", "q_norm", "k_norm",
- * "conv_state", "rec_state", "kcache", "vcache" (per layer), "final_norm" and
+ * "conv_state", "rec_state", "kcache", "vcache" (per layer; the states and
+ * caches [batch][...]), "final_norm" and
  * the fp16 "embed" [vocab][hidden] (layer -1).  Layer -1 also names the
  * activation seams of the last step, as the last layer to write each left
  * them (the reference's seam records): fp32 "x" (residual), "qkv" (the raw
  * projection), "z", "eg", "beta", "o", "qg", "kv", "q" (after norm and RoPE), "logits"; fp16
  * "h16" (the last RMSNorm output), "qkv16" (after conv + SiLU), "y16" (DeltaNet
- * output after norm and gate), "ya16" (attention output), "hf16" (SwiGLU). */
+ * output after norm and gate), "ya16" (attention output), "hf16" (SwiGLU), each
+ * [batch][...]. */
 int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count);
 
-/* Bytes of weights, KV cache and state one step reads on this rank. */
+/* Bytes of weights, KV cache and state one step (of every sequence of the
+ * batch) reads on this rank. */
 int64_t dec_step_bytes(dec_model *m);
 
 /* Per-layer accounting: dec_layer_bytes is what layer `layer` reads in one
@@ -131,6 +140,13 @@ int64_t dec_step_bytes(dec_model *m);
  * layer (record a start event before the step). */
 int64_t dec_layer_bytes(dec_model *m, int layer);
 int dec_set_layer_events(dec_model *m, void **events, int n);
+
+/* Residual seams (the reference's per-layer seam records, for parity
+ * checks): with a device buffer of n slots of [batch][hidden] fp32 (n <=
+ * n_layers + 1; NULL/0 to stop), dec_step copies the residual stream into
+ * slot il as layer il starts, and into slot n_layers after the last layer
+ * (the LM head's input).  Copies on the step's stream. */
+int dec_set_residual_seams(dec_model *m, float *buf, int n);
 
 #ifdef __cplusplus
 }

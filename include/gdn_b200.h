@@ -60,7 +60,8 @@ int gdn_step_fixed(const gdn_fixed_args *a, void *stream);
  *   out   = (S q) * sigmoid(g)  when g != NULL, else S q
  * S [H][D][D] fp32 (value column j of head h contiguous over key i);
  * q, k [T][KH][D], v [T][H][D], g [T][H][D] fp16; a, b [T][H] fp32;
- * out [T][H][D] fp32 and/or fp16.  T = 1 is one decode step. */
+ * out [T][H][D] fp32 and/or fp16.  T = 1 is one decode step (of nseq
+ * sequences at once when nseq > 1). */
 typedef struct {
     int32_t         T, H, KH, D;    /* D must be 128                            */
     float          *S;
@@ -76,6 +77,13 @@ typedef struct {
                                        when set, a and b are not read      */
     int32_t         pdl;            /* launch as a programmatic dependent of
                                        the previous kernel in the stream    */
+    int32_t         nseq;           /* independent sequences stepped in one
+                                       launch (0 or 1: one).  With nseq > 1,
+                                       T must be 1; sequence n reads q, k, v
+                                       at +n*seq_in elements, a, b, eg, beta
+                                       at +n*H, g and writes out at +n*H*D,
+                                       and owns the state S + n*H*D*D      */
+    int32_t         seq_in;
     int32_t         pad_;
 } gdn_f32_args;
 

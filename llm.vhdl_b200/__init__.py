@@ -98,7 +98,8 @@ class GdnF32(C.Structure):
                 ("S", C.c_void_p), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
                 ("g", C.c_void_p), ("a", C.c_void_p), ("b", C.c_void_p), ("l2norm", C.c_int32),
                 ("q_scale", C.c_float), ("out_f32", C.c_void_p), ("out_f16", C.c_void_p),
-                ("eg", C.c_void_p), ("beta", C.c_void_p), ("pdl", C.c_int32), ("pad_", C.c_int32)]
+                ("eg", C.c_void_p), ("beta", C.c_void_p), ("pdl", C.c_int32), ("nseq", C.c_int32),
+                ("seq_in", C.c_int32), ("pad_", C.c_int32)]
 
 
 class Job(C.Structure):
@@ -167,7 +168,8 @@ class DecConfig(C.Structure):
                 ("vocab", C.c_int32), ("ffn", C.c_int32), ("gdn_kh", C.c_int32),
                 ("gdn_vh", C.c_int32), ("gdn_hd", C.c_int32), ("att_qh", C.c_int32),
                 ("att_kvh", C.c_int32), ("att_hd", C.c_int32), ("n_rot", C.c_int32),
-                ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("max_ctx", C.c_int32)]
+                ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("max_ctx", C.c_int32),
+                ("batch", C.c_int32)]
 
 
 DEC_EXPORTS = {
@@ -194,6 +196,7 @@ DEC_EXPORTS = {
     "dec_step_bytes": (C.c_int64, [C.c_void_p]),
     "dec_layer_bytes": (C.c_int64, [C.c_void_p, C.c_int]),
     "dec_set_layer_events": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "dec_set_residual_seams": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
 }
 
 _declib = None

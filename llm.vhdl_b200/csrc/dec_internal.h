@@ -36,7 +36,9 @@ typedef struct {
     int32_t         rows, epi, tile0, ntiles;
     int32_t         s_pitch;       /* scale row pitch in fp16 elements: a
                                       multiple of 8, >= ceil8(K/128)           */
-    int32_t         pad_;
+    int32_t         ostride;       /* vector b's outputs (out_f32, out2_f32,
+                                      out_f16) at +b*ostride elements; its
+                                      CONV state at st + b*3*st_stride       */
 } dmv_job;
 
 typedef struct {
@@ -51,6 +53,11 @@ typedef struct {
     int32_t      idx0;             /* ARGMAX: global index of row 0                */
     int32_t      pf_bytes;         /* weight bytes each CTA prefetches to L2 early */
     int32_t      ksplit;           /* set by the launcher: warps per row       */
+    int32_t      nvec;             /* input vectors (sequences) 1..8, sharing
+                                      every weight load: vector b's x and x2
+                                      at +b*xs elements, its seam at +b*K, its
+                                      argmax key at key[b] (0 means 1)      */
+    int32_t      xs;
     int32_t      pad_;
 } dmv_params;
 

@@ -37,6 +37,8 @@ __device__ __forceinline__ float block_sum(float v, float *red)
 __global__ void dec_embed_kernel(const uint16_t *emb, int hidden, const int32_t *tok, float *x)
 {
     PDL_ENTER();
+    tok += blockIdx.y;                                   // sequence blockIdx.y of a batch
+    x += (size_t)blockIdx.y * hidden;
     const int64_t base = (int64_t)(*tok) * hidden;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x)
         x[i] = __half2float(__ushort_as_half(emb[base + i]));
@@ -99,6 +101,15 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
     const int grp = qh / kvh;
     const int c = blockIdx.x, g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = g * grp + warp;
+    if (blockIdx.z) {                                    // sequence blockIdx.z of a batch
+        const size_t b = blockIdx.z;
+        qg += b * 2 * qh * ATT_HD;
+        kv += b * 2 * kvh * ATT_HD;
+        kcache += b * max_ctx * kvh * ATT_HD;
+        vcache += b * max_ctx * kvh * ATT_HD;
+        if (q_seam) q_seam += b * qh * ATT_HD;
+        part += b * qh * nchunks * (ATT_HD + 4);
+    }
     const int pos = *d_pos, len = min(pos + 1, max_ctx), p0 = c * ch;
     float *pp = part + ((size_t)h * nchunks + c) * (ATT_HD + 4);
     if (p0 >= len) {                                   // the whole CTA leaves: no barrier below
@@ -211,6 +222,12 @@ __global__ void __launch_bounds__(128) dec_attn_combine_kernel(const float *part
     __shared__ float red[32];
     PDL_ENTER();
     const int h = blockIdx.x, t = threadIdx.x;
+    if (blockIdx.y) {                                    // sequence blockIdx.y of a batch
+        const size_t b = blockIdx.y, qh = gridDim.x;
+        part += b * qh * nchunks * (hd + 4);
+        gate += b * qh * gate_stride;
+        y += b * qh * hd;
+    }
     const int used = min(nchunks, (*d_pos + 1 + ch - 1) / ch);
     const float *ph = part + (size_t)h * nchunks * (hd + 4);
     float M = -INFINITY;
@@ -245,23 +262,27 @@ __global__ void dec_add_kernel(float *x, const float *t, int n)
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] += t[i];
 }
 
-// Pick the largest of `n` keys (one per rank), record it as the prediction
-// at the current position, advance the position, clear `key`.  The next
-// input token is the prompt's while the prompt lasts (prompt[0] holds its
-// length, prompt[1 + i] its tokens), else the prediction.
+// Thread b, for sequence b of the batch: pick the largest of its `n` keys
+// (one per rank, keys[r * nseq + b]), record it as the prediction at the
+// current position in history[b][max_ctx], clear key[b].  The next input
+// token is the prompt's while the prompt lasts (prompt[0] holds its length
+// len, prompt[1 + b * len + i] sequence b's tokens), else the prediction.
+// Then the shared position advances.
 __global__ void dec_advance_kernel(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok,
                                    int32_t *history, int32_t *pos, int max_ctx, const int32_t *prompt)
 {
     PDL_ENTER();
+    const int b = threadIdx.x, nseq = blockDim.x;
     unsigned long long best = 0;
-    for (int i = 0; i < n; i++) best = keys[i] > best ? keys[i] : best;
+    for (int i = 0; i < n; i++) best = keys[i * nseq + b] > best ? keys[i * nseq + b] : best;
     const int32_t t = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
     const int p = *pos;
-    if (p < max_ctx) history[p] = t;
+    if (p < max_ctx) history[(size_t)b * max_ctx + p] = t;
     const int plen = prompt ? prompt[0] : 0;
-    *tok = (p + 1 < plen) ? prompt[1 + p + 1] : t;
-    *pos = p + 1;
-    *key = 0;
+    tok[b] = (p + 1 < plen) ? prompt[1 + (size_t)b * plen + p + 1] : t;
+    key[b] = 0;
+    __syncthreads();
+    if (b == 0) *pos = p + 1;
 }
 
 // --------------------------------------------------- synthetic weights
@@ -337,8 +358,8 @@ static int launch(void (*k)(KArgs...), dim3 g, dim3 b, void *s, int pdl, Args...
 
 extern "C" {
 
-int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s, int pdl)
-{ return launch(dec_embed_kernel, dim3((hidden + 255) / 256), dim3(256), s, pdl, emb, hidden, tok, x); }
+int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, int nseq, void *s, int pdl)
+{ return launch(dec_embed_kernel, dim3((hidden + 255) / 256, nseq), dim3(256), s, pdl, emb, hidden, tok, x); }
 
 size_t dec_attention_smem(int qh, int kvh, int ch)
 {
@@ -348,9 +369,10 @@ size_t dec_attention_smem(int qh, int kvh, int ch)
 
 int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const float *kn_w, int qh, int kvh,
                     int n_rot, float theta, float eps, const int32_t *d_pos, int max_ctx, int ch, float *part,
-                    float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, void *s, int pdl)
+                    float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, int nseq, void *s, int pdl)
 {
-    if (kvh <= 0 || qh % kvh || qh / kvh > 32 || ch <= 0 || ch > 64 || (n_rot & 1) || n_rot > ATT_HD) return -11;
+    if (kvh <= 0 || qh % kvh || qh / kvh > 32 || ch <= 0 || ch > 64 || (n_rot & 1) || n_rot > ATT_HD
+        || nseq < 1 || nseq > 64) return -11;
     const int nchunks = (max_ctx + ch - 1) / ch;
     if (nchunks > 1024) return -11;                   // the combine's weight table
     const size_t smem = dec_attention_smem(qh, kvh, ch);
@@ -363,7 +385,7 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
         attr_set[dev] = 1;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nchunks, kvh);
+    cfg.gridDim = dim3(nchunks, kvh, nseq);
     cfg.blockDim = dim3(32 * (qh / kvh));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = reinterpret_cast<cudaStream_t>(s);
@@ -376,7 +398,7 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
                                          d_pos, max_ctx, ch, nchunks, kcache, vcache, q_seam, part));
     if (rc) return rc;
     // the gate is the raw projection: second half of each head's q|gate row
-    return launch(dec_attn_combine_kernel, dim3(qh), dim3(ATT_HD), s, pdl, part, qg + ATT_HD, 2 * ATT_HD, ATT_HD,
+    return launch(dec_attn_combine_kernel, dim3(qh, nseq), dim3(ATT_HD), s, pdl, part, qg + ATT_HD, 2 * ATT_HD, ATT_HD,
                   nchunks, d_pos, ch, y);
 }
 
@@ -384,8 +406,8 @@ int dec_k_add(float *x, const float *t, int n, void *s, int pdl)
 { return launch(dec_add_kernel, dim3((n + 255) / 256), dim3(256), s, pdl, x, t, n); }
 
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
-                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s, int pdl)
-{ return launch(dec_advance_kernel, dim3(1), dim3(1), s, pdl, keys, n, key, tok, hist, pos, max_ctx, prompt); }
+                  int32_t *pos, int max_ctx, const int32_t *prompt, int nseq, void *s, int pdl)
+{ return launch(dec_advance_kernel, dim3(1), dim3(nseq), s, pdl, keys, n, key, tok, hist, pos, max_ctx, prompt); }
 
 int dec_k_synth_linear(uint64_t key, const int32_t *rows, int row0, int nrows, int k0, int kn, int Kg,
                        uint8_t *wq, uint16_t *sc, int s_pitch, void *s)

@@ -127,7 +127,8 @@ __host__ __device__ __forceinline__ size_t dmv_smem_x_bytes(int K)
 
 // the 8 fp32 inputs of unit u (columns 8u .. 8u+7): x (fp16 / fp32
 // residual / DeltaNet o) and, for the gated prologue, z
-__device__ __forceinline__ void unit_load(const dmv_params &P, int u, bool ok, float (&v)[8], float (&z)[8])
+__device__ __forceinline__ void unit_load(const dmv_params &P, const void *xv, const float *x2v, int u, bool ok,
+                                          float (&v)[8], float (&z)[8])
 {
     if (!ok) {
 #pragma unroll
@@ -135,7 +136,7 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, int u, bool ok, f
         return;
     }
     if (P.op == DMV_OP_F16) {
-        const uint4 r = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(P.x) + 8 * u);
+        const uint4 r = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(xv) + 8 * u);
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int k = 0; k < 4; k++) {
@@ -143,11 +144,11 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, int u, bool ok, f
             v[2 * k] = f.x; v[2 * k + 1] = f.y;
         }
     } else {
-        const float4 *x = reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) + 8 * u);
+        const float4 *x = reinterpret_cast<const float4 *>(static_cast<const float *>(xv) + 8 * u);
         const float4 a = x[0], b = x[1];
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         if (P.op == DMV_OP_GATED) {
-            const float4 *zp = reinterpret_cast<const float4 *>(P.x2 + 8 * u);
+            const float4 *zp = reinterpret_cast<const float4 *>(x2v + 8 * u);
             const float4 c = zp[0], d = zp[1];
             z[0] = c.x; z[1] = c.y; z[2] = c.z; z[3] = c.w; z[4] = d.x; z[5] = d.y; z[6] = d.z; z[7] = d.w;
         }
@@ -156,91 +157,119 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, int u, bool ok, f
 
 // Stage x: unit u = 8 columns per thread, so a 128-column group is 16
 // consecutive lanes (a half warp) and a 64-column pair 8 lanes: group max,
-// pair sums and per-head norms are shuffle reductions.
-__device__ void dmv_stage(const dmv_params &P, const Sm &s)
+// pair sums and per-head norms are shuffle reductions.  NV vectors (the
+// sequences of a batch; those past P.nvec are not staged and their results
+// are dropped), vector b into the shared-memory block at sm + b * xb.
+template <int NV>
+__device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb)
 {
-    __shared__ float red[32];
-    const int K = P.K, np = K >> 6, nu = K >> 3, tid = threadIdx.x;
-    float inv = 0.f;
+    __shared__ float red[DMV_WARPS * 8];
+    __shared__ float invs[8];
+    const int K = P.K, np = K >> 6, nu = K >> 3, tid = threadIdx.x, nv = P.nvec;
     if (P.op == DMV_OP_RMSNORM) {
-        const float *x = static_cast<const float *>(P.x);
-        float a = 0.f;
-        for (int i = 4 * tid; i < K; i += 4 * DMV_THREADS) {
-            const float4 v = *reinterpret_cast<const float4 *>(x + i);
-            a = fmaf(v.x, v.x, a); a = fmaf(v.y, v.y, a); a = fmaf(v.z, v.z, a); a = fmaf(v.w, v.w, a);
+        float a[NV];
+#pragma unroll
+        for (int b = 0; b < NV; b++) {
+            a[b] = 0.f;
+            if (b < nv) {
+                const float *x = static_cast<const float *>(P.x) + (size_t)b * P.xs;
+                for (int i = 4 * tid; i < K; i += 4 * DMV_THREADS) {
+                    const float4 v = *reinterpret_cast<const float4 *>(x + i);
+                    a[b] = fmaf(v.x, v.x, a[b]); a[b] = fmaf(v.y, v.y, a[b]);
+                    a[b] = fmaf(v.z, v.z, a[b]); a[b] = fmaf(v.w, v.w, a[b]);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) a[b] += __shfl_xor_sync(0xffffffffu, a[b], o);
+            if ((tid & 31) == 0) red[b * DMV_WARPS + (tid >> 5)] = a[b];
         }
-        a = block_sum(a, red);
-        inv = rsqrtf(a / (float)K + P.eps);
+        __syncthreads();
+        if (tid < NV) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < DMV_WARPS; w++) t += red[tid * DMV_WARPS + w];
+            invs[tid] = rsqrtf(t / (float)K + P.eps);
+        }
+        __syncthreads();
     }
-    uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
-    for (int u0 = 0; u0 < nu; u0 += DMV_THREADS) {        // uniform trip count: shuffles below
-        const int u = u0 + tid;
-        const bool ok = u < nu;                             // whole half warps (nu % 16 == 0)
-        float v[8], z[8];
-        unit_load(P, u, ok, v, z);
-        if (P.op == DMV_OP_RMSNORM) {
+#pragma unroll 1
+    for (int b = 0; b < NV && b < nv; b++) {
+        const Sm s = sm_layout(sm + b * xb, K);
+        const float inv = P.op == DMV_OP_RMSNORM ? invs[b] : 0.f;
+        const void *xv = P.op == DMV_OP_F16 ? static_cast<const void *>(static_cast<const uint16_t *>(P.x) + (size_t)b * P.xs)
+                                            : static_cast<const void *>(static_cast<const float *>(P.x) + (size_t)b * P.xs);
+        const float *x2v = P.x2 ? P.x2 + (size_t)b * P.xs : nullptr;
+        uint16_t *seam = P.seam ? P.seam + (size_t)b * K : nullptr;
+        uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
+        for (int u0 = 0; u0 < nu; u0 += DMV_THREADS) {        // uniform trip count: shuffles below
+            const int u = u0 + tid;
+            const bool ok = u < nu;                             // whole half warps (nu % 16 == 0)
+            float v[8], z[8];
+            unit_load(P, xv, x2v, u, ok, v, z);
+            if (P.op == DMV_OP_RMSNORM) {
+                if (ok) {
+                    const float4 *wp = reinterpret_cast<const float4 *>(P.nw + 8 * u);
+                    const float4 a = wp[0], c = wp[1];
+                    const float w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+                    for (int k = 0; k < 8; k++) v[k] = v[k] * inv * w[k];
+                }
+            } else if (P.op == DMV_OP_GATED) {
+                float ss = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                const float ginv = rsqrtf(ss / 128.f + P.eps);
+                if (ok) {
+                    const float4 *wp = reinterpret_cast<const float4 *>(P.nw + ((8 * u) & 127));
+                    const float4 a = wp[0], c = wp[1];
+                    const float w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+                    for (int k = 0; k < 8; k++) v[k] = v[k] * ginv * w[k] * silu_f(z[k]);
+                }
+            }
+            // fp16 rounding (the storage contract), then the group exponent
+            uint32_t hw[4];
+            float m = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+                hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
+                const float2 f = __half22float2(h2);
+                v[2 * k] = f.x; v[2 * k + 1] = f.y;
+                m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+            }
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            int e = 0;
+            // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
+            if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
+            const float scale = exp2i(e);
+            int xi[8], ssum = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
             if (ok) {
-                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + 8 * u);
-                const float4 a = wp[0], b = wp[1];
-                const float w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                uint32_t le = 0, lo = 0, he = 0, ho = 0;
 #pragma unroll
-                for (int k = 0; k < 8; k++) v[k] = v[k] * inv * w[k];
+                for (int t = 0; t < 4; t++) {
+                    le |= (uint32_t)(xi[2 * t] & 0xFF) << (8 * t);
+                    he |= (uint32_t)((xi[2 * t] >> 8) & 0xFF) << (8 * t);
+                    lo |= (uint32_t)(xi[2 * t + 1] & 0xFF) << (8 * t);
+                    ho |= (uint32_t)((xi[2 * t + 1] >> 8) & 0xFF) << (8 * t);
+                }
+                const int c = u >> 2, q = u & 3, p = c >> 1, par = c & 1;
+                pw[4 * ((0 + par) * np + p) + q] = le;
+                pw[4 * ((2 + par) * np + p) + q] = lo;
+                pw[4 * ((4 + par) * np + p) + q] = he;
+                pw[4 * ((6 + par) * np + p) + q] = ho;
+                if (!(u & 7)) s.psum[u >> 3] = ssum;
+                if (!(u & 15)) s.gfac[u >> 4] = exp2i(-e);
+                if (blockIdx.x == 0 && seam)
+                    *reinterpret_cast<uint4 *>(seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             }
-        } else if (P.op == DMV_OP_GATED) {
-            float ss = 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float ginv = rsqrtf(ss / 128.f + P.eps);
-            if (ok) {
-                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + ((8 * u) & 127));
-                const float4 a = wp[0], b = wp[1];
-                const float w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int k = 0; k < 8; k++) v[k] = v[k] * ginv * w[k] * silu_f(z[k]);
-            }
-        }
-        // fp16 rounding (the storage contract), then the group exponent
-        uint32_t hw[4];
-        float m = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-            hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
-            const float2 f = __half22float2(h2);
-            v[2 * k] = f.x; v[2 * k + 1] = f.y;
-            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        int e = 0;
-        // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
-        if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
-        const float scale = exp2i(e);
-        int xi[8], ssum = 0;
-#pragma unroll
-        for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-        if (ok) {
-            uint32_t le = 0, lo = 0, he = 0, ho = 0;
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                le |= (uint32_t)(xi[2 * t] & 0xFF) << (8 * t);
-                he |= (uint32_t)((xi[2 * t] >> 8) & 0xFF) << (8 * t);
-                lo |= (uint32_t)(xi[2 * t + 1] & 0xFF) << (8 * t);
-                ho |= (uint32_t)((xi[2 * t + 1] >> 8) & 0xFF) << (8 * t);
-            }
-            const int b = u >> 2, q = u & 3, p = b >> 1, par = b & 1;
-            pw[4 * ((0 + par) * np + p) + q] = le;
-            pw[4 * ((2 + par) * np + p) + q] = lo;
-            pw[4 * ((4 + par) * np + p) + q] = he;
-            pw[4 * ((6 + par) * np + p) + q] = ho;
-            if (!(u & 7)) s.psum[u >> 3] = ssum;
-            if (!(u & 15)) s.gfac[u >> 4] = exp2i(-e);
-            if (blockIdx.x == 0 && P.seam)
-                *reinterpret_cast<uint4 *>(P.seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         }
     }
     __syncthreads();
@@ -284,43 +313,46 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx)
     return ((unsigned long long)k << 32) | (0xFFFFFFFFull - (uint32_t)idx);
 }
 
-// per-row epilogue (lane 0); v2 is the paired row's value
-__device__ __forceinline__ void dmv_epilogue(const dmv_params &P, const dmv_job &J, int row, float v, float v2,
-                                             unsigned long long &best)
+// per-row epilogue of vector b (one lane); v2 is the paired row's value.
+// Vector b's outputs sit b * ostride elements on, its conv state b * 3 *
+// st_stride.
+__device__ __forceinline__ void dmv_epilogue(const dmv_params &P, const dmv_job &J, int b, int row, float v,
+                                             float v2, unsigned long long &best)
 {
+    const size_t o = (size_t)b * J.ostride + row;
     switch (J.epi) {
-    case DMV_EPI_F32: J.out_f32[row] = v; break;
-    case DMV_EPI_ACC: J.out_f32[row] += v; break;
+    case DMV_EPI_F32: J.out_f32[o] = v; break;
+    case DMV_EPI_ACC: J.out_f32[o] += v; break;
     case DMV_EPI_F16:
-        J.out_f16[row] = __half_as_ushort(__float2half_rn(v));
-        if (J.out_f32) J.out_f32[row] = v;
+        J.out_f16[o] = __half_as_ushort(__float2half_rn(v));
+        if (J.out_f32) J.out_f32[o] = v;
         break;
     case DMV_EPI_SWIGLU:
-        J.out_f16[row] = __half_as_ushort(__float2half_rn(silu_f(v) * v2));
+        J.out_f16[o] = __half_as_ushort(__float2half_rn(silu_f(v) * v2));
         break;
     case DMV_EPI_CONV: {
         // taps 0..2 on the stored inputs (oldest first), tap 3 on this one
-        float *st = J.st;
         const int S = J.st_stride;
+        float *st = J.st + (size_t)b * 3 * S;
         const float s0 = st[row], s1 = st[S + row], s2 = st[2 * S + row];
         const float4 cw = reinterpret_cast<const float4 *>(J.p0)[row];
         const float a = s0 * cw.x + s1 * cw.y + s2 * cw.z + v * cw.w;
         st[row] = s1; st[S + row] = s2; st[2 * S + row] = v;
-        J.out_f16[row] = __half_as_ushort(__float2half_rn(silu_f(a)));
-        if (J.out_f32) J.out_f32[row] = v;
+        J.out_f16[o] = __half_as_ushort(__float2half_rn(silu_f(a)));
+        if (J.out_f32) J.out_f32[o] = v;
         break;
     }
     case DMV_EPI_GATES:
         if (row < J.n1) {
             const float av = v + J.p1[row];
             const float sp = av > 20.f ? av : log1pf(expf(av));
-            J.out_f32[row] = expf(J.p0[row] * sp);
+            J.out_f32[o] = expf(J.p0[row] * sp);
         } else {
-            J.out2_f32[row - J.n1] = 1.0f / (1.0f + expf(-v));
+            J.out2_f32[o - J.n1] = 1.0f / (1.0f + expf(-v));
         }
         break;
     case DMV_EPI_ARGMAX: {
-        J.out_f32[row] = v;
+        J.out_f32[o] = v;
         const unsigned long long k = argmax_key(v, P.idx0 + row);
         best = k > best ? k : best;
         break;
@@ -477,12 +509,141 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
         }
         if (kq == 0 && holder && vi < g) {
             const int row = (t + vi - J.tile0) * rt + rs;
-            if (row < J.rows) dmv_epilogue(P, J, row, v0, v1, best);
+            if (row < J.rows) dmv_epilogue(P, J, 0, row, v0, v1, best);
         }
     }
 }
 
-__global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid_constant__ dmv_params P)
+// Several vectors (NV = 2, 4, 8): the same walk over rows and pairs, each
+// weight load and its decode shared by the NV dot products.  Per pair, the
+// x planes of one vector at a time are read from shared memory (reused by
+// the 4 row slots), so the live registers are the 4 rows' weights, 4 x NV
+// fp32 accumulators and one vector's planes.
+template <int V>
+__device__ __forceinline__ float tbfly(float (&v)[V], int lane)
+{
+    // transposing butterfly: V values per lane in, lane L ends with the warp
+    // total of value L >> (5 - log2 V) (V - 1 shuffles, then plain ones)
+    constexpr int LV = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : 1;
+#pragma unroll
+    for (int st = 0; st < LV; st++) {
+        const int o = 16 >> st, n = V >> (st + 1);
+        const bool up = lane & o;
+#pragma unroll
+        for (int i = 0; i < n; i++) {
+            const float keep = up ? v[i + n] : v[i], send = up ? v[i] : v[i + n];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int o = 16 >> LV; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
+
+template <int NV, bool PAIRED>
+__device__ __forceinline__ void dmv_segment_b(const dmv_params &P, const dmv_job &J, uint8_t *sm, size_t xb,
+                                              float *red, int ta, int tb, int warp, int lane, int np,
+                                              size_t wpitch, unsigned long long &best)
+{
+    constexpr int G = PAIRED ? DMV_G / 2 : DMV_G;
+    constexpr int NR = DMV_G;
+    constexpr int V = NR * NV;
+    constexpr int SH = V >= 32 ? 0 : V >= 16 ? 1 : 2;      // lane L holds value L >> SH
+    const int ks = P.ksplit, rt = DMV_WARPS / ks, rs = warp / ks, kq = warp % ks;
+    const int npk = np / ks, p0 = kq * npk, p1 = p0 + npk;
+    const int K = P.K;
+    for (int t = ta; t < tb; t += G) {
+        const int g = min(G, tb - t);
+        const uint8_t *wr[NR];
+        const uint16_t *sr[NR];
+#pragma unroll
+        for (int i = 0; i < G; i++) {
+            const int row = (t + min(i, g - 1) - J.tile0) * rt + rs;
+            const int rr = min(row, J.rows - 1);               // past the end: a valid row, discarded
+            if (PAIRED) {
+                wr[2 * i] = J.wq + (size_t)rr * wpitch;  sr[2 * i] = J.sc + (size_t)rr * J.s_pitch;
+                wr[2 * i + 1] = J.wq2 + (size_t)rr * wpitch; sr[2 * i + 1] = J.sc2 + (size_t)rr * J.s_pitch;
+            } else {
+                wr[i] = J.wq + (size_t)rr * wpitch; sr[i] = J.sc + (size_t)rr * J.s_pitch;
+            }
+        }
+        float acc[V];
+#pragma unroll
+        for (int k = 0; k < V; k++) acc[k] = 0.f;
+        for (int pb = p0; pb < p1; pb += 32) {
+            const int p = pb + lane;
+            uint32_t w[NR][8];
+            float sc[NR];
+            dmv_loads<NR>(wr, sr, p, p < p1, w, sc);
+            if (p < p1) {
+                // the weights as idx^8 nibbles (even columns) and 16*(idx^8) (odd)
+                uint32_t we[NR][8], wo[NR][8];
+#pragma unroll
+                for (int k = 0; k < NR; k++)
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        we[k][q] = (w[k][q] & 0x0F0F0F0Fu) ^ 0x08080808u;
+                        wo[k][q] = (w[k][q] & 0xF0F0F0F0u) ^ 0x80808080u;
+                    }
+#pragma unroll
+                for (int b = 0; b < NV; b++) {
+                    const Sm s = sm_layout(sm + b * xb, K);
+                    int a[NR][4];
+#pragma unroll
+                    for (int k = 0; k < NR; k++) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0;
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        const uint4 xle = s.planes[(0 + half) * np + p], xlo = s.planes[(2 + half) * np + p];
+                        const uint4 xhe = s.planes[(4 + half) * np + p], xho = s.planes[(6 + half) * np + p];
+                        const uint32_t le[4] = {xle.x, xle.y, xle.z, xle.w}, lo[4] = {xlo.x, xlo.y, xlo.z, xlo.w};
+                        const uint32_t he[4] = {xhe.x, xhe.y, xhe.z, xhe.w}, ho[4] = {xho.x, xho.y, xho.z, xho.w};
+#pragma unroll
+                        for (int k = 0; k < NR; k++)
+#pragma unroll
+                            for (int q = 0; q < 4; q++) {
+                                a[k][0] = dp_uu(we[k][4 * half + q], le[q], a[k][0]);
+                                a[k][1] = dp_uu(wo[k][4 * half + q], lo[q], a[k][1]);
+                                a[k][2] = dp_us(we[k][4 * half + q], he[q], a[k][2]);
+                                a[k][3] = dp_us(wo[k][4 * half + q], ho[q], a[k][3]);
+                            }
+                    }
+                    const int sx = s.psum[p];
+                    const float gf = s.gfac[p >> 1];
+#pragma unroll
+                    for (int k = 0; k < NR; k++) {
+                        const int part = a[k][0] + (a[k][1] >> 4) + (a[k][2] + (a[k][3] >> 4)) * 256 - 8 * sx;
+                        acc[k * NV + b] = fmaf((float)part, sc[k] * gf, acc[k * NV + b]);
+                    }
+                }
+            }
+        }
+        float v0 = tbfly<V>(acc, lane);
+        const int vi = lane >> SH, k = vi / NV, b = vi % NV;
+        // the up row of a gate/up pair sits NV values (NV << SH lanes) higher
+        float v1 = PAIRED ? __shfl_down_sync(0xffffffffu, v0, NV << SH) : 0.f;
+        const bool holder = (lane & ((1 << SH) - 1)) == 0 && (!PAIRED || !(k & 1));
+        if (ks > 1) {
+            red[warp * 64 + lane] = v0;
+            red[warp * 64 + 32 + lane] = v1;
+            __syncthreads();
+            if (kq == 0) {
+                float a = 0.f, c = 0.f;
+                for (int q = 0; q < ks; q++) { a += red[(warp + q) * 64 + lane]; c += red[(warp + q) * 64 + 32 + lane]; }
+                v0 = a; v1 = c;
+            }
+            __syncthreads();
+        }
+        const int i = PAIRED ? k >> 1 : k;
+        if (kq == 0 && holder && i < g && b < P.nvec) {
+            const int row = (t + i - J.tile0) * rt + rs;
+            if (row < J.rows) dmv_epilogue(P, J, b, row, v0, v1, best);
+        }
+    }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(DMV_THREADS, NV == 1 ? DMV_MINB : 1) dmv_kernel(const __grid_constant__ dmv_params P)
 {
     extern __shared__ __align__(128) uint8_t dmv_sm[];
     __shared__ dmv_job JS[DMV_MAXJ];
@@ -520,18 +681,28 @@ __global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid
     pdl_trigger();
     pdl_wait();
 
-    const Sm s = sm_layout(dmv_sm, K);
-    dmv_stage(P, s);
+    const size_t xb = dmv_smem_x_bytes(K);
+    dmv_stage<NV>(P, dmv_sm, xb);
 
     unsigned long long best = 0;
     for (int j = j0; j < P.njobs && t0 < t1; j++) {
         const dmv_job &J = JS[j];
         const int ta = max(t0, J.tile0), tb = min(t1, J.tile0 + J.ntiles);
         if (ta >= tb) continue;
-        if (J.wq2) dmv_segment<true>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
-        else dmv_segment<false>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
+        if (NV == 1) {
+            const Sm s = sm_layout(dmv_sm, K);
+            if (J.wq2) dmv_segment<true>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
+            else dmv_segment<false>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
+        } else {
+            if (J.wq2) dmv_segment_b<NV, true>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, np, wpitch, best);
+            else dmv_segment_b<NV, false>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, np, wpitch, best);
+        }
     }
-    if (best) atomicMax(P.key, best);
+    // the argmax keys: every holder lane keeps one vector's best
+    if (best) {
+        constexpr int SH = NV >= 8 ? 0 : NV >= 4 ? 1 : NV >= 2 ? 2 : 3;
+        atomicMax(P.key + (NV == 1 ? 0 : ((lane >> SH) % NV)), best);
+    }
 }
 
 extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
@@ -542,27 +713,36 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
     if (p->op == DMV_OP_GATED && (!p->nw || !p->x2)) return -11;
     if (p->op < DMV_OP_F16 || p->op > DMV_OP_GATED) return -11;
     dmv_params P = *p;
+    if (P.nvec <= 0) P.nvec = 1;
+    if (P.nvec > 8 || (P.nvec > 1 && P.xs < P.K) || (P.xs & 7)) return -11;
+    const int NV = P.nvec == 1 ? 1 : P.nvec == 2 ? 2 : P.nvec <= 4 ? 4 : 8;
+    const void *fn = NV == 1 ? (const void *)dmv_kernel<1> : NV == 2 ? (const void *)dmv_kernel<2>
+                   : NV == 4 ? (const void *)dmv_kernel<4> : (const void *)dmv_kernel<8>;
+    const int fi = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : 3;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
     if (dev < 0 || dev >= 64) return -11;
-    static int s_sms[64], s_occ[64][4], s_attr[64];
-    static size_t s_occ_smem[64][4];
-    if (!s_attr[dev]) {
-        e = cudaFuncSetAttribute(dmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    // per device and kernel instance: the SM count, and the occupancy of up
+    // to 8 shared-memory sizes (the decode step uses 3 or 4)
+    static int s_sms[64], s_occ[64][4][8], s_attr[64][4];
+    static size_t s_occ_smem[64][4][8];
+    const size_t smem = (size_t)NV * dmv_smem_x_bytes(P.K);
+    if (smem > 200 * 1024) return -11;
+    if (!s_attr[dev][fi]) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-        s_attr[dev] = 1;
+        s_attr[dev][fi] = 1;
     }
-    const size_t smem = dmv_smem_x_bytes(P.K);
     int occ = 0;
-    for (int i = 0; i < 4; i++) if (s_occ[dev][i] && s_occ_smem[dev][i] == smem) occ = s_occ[dev][i];
+    for (int i = 0; i < 8; i++) if (s_occ[dev][fi][i] && s_occ_smem[dev][fi][i] == smem) occ = s_occ[dev][fi][i];
     if (!occ) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dmv_kernel, DMV_THREADS, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DMV_THREADS, smem);
         if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
         if (occ < 1) occ = 1;
-        for (int i = 0; i < 4; i++)
-            if (!s_occ[dev][i]) { s_occ[dev][i] = occ; s_occ_smem[dev][i] = smem; break; }
+        for (int i = 0; i < 8; i++)
+            if (!s_occ[dev][fi][i]) { s_occ[dev][fi][i] = occ; s_occ_smem[dev][fi][i] = smem; break; }
     }
     const int slots = s_sms[dev] * occ;
     // Rows are short of warps when a CTA would get fewer than 16: then split
@@ -594,6 +774,8 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
         case DMV_EPI_ARGMAX: if (!J.out_f32 || !P.key) return -11; break;
         default: return -11;
         }
+        if (P.nvec > 1 && J.ostride < J.rows && J.epi != DMV_EPI_GATES) return -11;
+        if (P.nvec > 1 && J.epi == DMV_EPI_GATES && (J.ostride < J.n1 || J.ostride < J.rows - J.n1)) return -11;
         if (J.epi != DMV_EPI_SWIGLU && J.wq2) return -11;
         J.tile0 = tiles;
         J.ntiles = (J.rows + rt - 1) / rt;
@@ -612,7 +794,8 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, dmv_kernel, P);
+    void *args[] = {&P};
+    e = cudaLaunchKernelExC(&cfg, fn, args);
     if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
     return 0;
 }

@@ -25,13 +25,13 @@
 extern int mv4i_g_cuda_err;
 
 /* kernels in dec_kernels.cu (pdl: launch as a programmatic dependent) */
-int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, void *s, int pdl);
+int dec_k_embed(const uint16_t *emb, int hidden, const int32_t *tok, float *x, int nseq, void *s, int pdl);
 int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const float *kn_w, int qh, int kvh,
                     int n_rot, float theta, float eps, const int32_t *d_pos, int max_ctx, int ch, float *part,
-                    float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, void *s, int pdl);
+                    float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, int nseq, void *s, int pdl);
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl);
 int dec_k_advance(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok, int32_t *hist,
-                  int32_t *pos, int max_ctx, const int32_t *prompt, void *s, int pdl);
+                  int32_t *pos, int max_ctx, const int32_t *prompt, int nseq, void *s, int pdl);
 size_t dec_p2p_region(int world, int hidden, size_t *off_keys, size_t *off_xflag, size_t *off_kflag);
 int dec_k_allreduce_p2p(void *const *regions, int rank, int world, int hidden, const float *t, float *x,
                         uint32_t *epoch, uint32_t *done, int *err, int spin_limit, void *s, int pdl);
@@ -78,9 +78,12 @@ struct dec_model {
     /* activations */
     float    *x, *t, *qkv_f, *z_f, *eg, *beta, *o_f, *qg_f, *kv_f, *q_f, *part, *logits;
     uint16_t *h16, *qkv16, *y16, *ya16, *hf16;
+    int       B;                         /* sequences decoded together          */
     int       pdl;                       /* programmatic dependent launches     */
     void    **lev;                       /* optional: event after each layer    */
     int       nlev;
+    float    *rseam;                     /* optional: residual at each layer input */
+    int       nrseam;
     unsigned long long *key, *keys;
     int32_t  *tok, *pos, *hist;
     int32_t  *prompt;                    /* [0] = length, [1..] = tokens     */
@@ -154,11 +157,14 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     if (c->gdn_hd != HD || c->att_hd != HD || c->hidden % 128 || c->hidden > 16384 || c->ffn % (128 * tp_world)
         || c->gdn_vh % tp_world || c->att_qh % tp_world || c->att_kvh % tp_world || c->att_kvh <= 0
         || (c->att_qh / c->att_kvh) > 32 || c->att_qh % c->att_kvh || c->attn_every < 1
-        || c->n_rot > HD || (c->n_rot & 1) || c->max_ctx <= 0 || c->max_ctx > 65536 || c->vocab < tp_world)
+        || c->n_rot > HD || (c->n_rot & 1) || c->max_ctx <= 0 || c->max_ctx > 65536 || c->vocab < tp_world
+        || c->batch < 0 || c->batch > 8 || (c->batch > 1 && tp_world > 1))
         return -11;
     dec_model *m = (dec_model *)calloc(1, sizeof *m);
     if (!m) return -11;
     m->c = *c; m->device = device; m->rank = tp_rank; m->world = tp_world;
+    m->B = c->batch > 1 ? c->batch : 1;
+    m->c.batch = m->B;
     { const char *e = getenv("DEC_PDL"); m->pdl = !(e && e[0] == '0'); }
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) { free(m); return fail(e); }
@@ -215,8 +221,8 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
             TRY(make_vec(m, &l->ssm_a, mkey(seed, il, 4), NULL, m->v0, m->vh, -1.0f, 0.2f));
             TRY(make_vec(m, &l->dt_bias, mkey(seed, il, 5), NULL, m->v0, m->vh, 0.0f, 0.5f));
             TRY(make_vec(m, &l->ssm_norm, mkey(seed, il, 6), NULL, 0, HD, 1.0f, 0.1f));
-            TRY(dalloc(m, (void **)&l->conv_state, sizeof(float) * 3 * (size_t)m->conv_dim));
-            TRY(dalloc(m, (void **)&l->rec_state, sizeof(float) * (size_t)m->vh * HD * HD));
+            TRY(dalloc(m, (void **)&l->conv_state, sizeof(float) * 3 * (size_t)m->conv_dim * m->B));
+            TRY(dalloc(m, (void **)&l->rec_state, sizeof(float) * (size_t)m->vh * HD * HD * m->B));
         } else {
             int n = 0;
             for (int i = 0; i < m->qh; i++)
@@ -230,8 +236,8 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
             TRY(make_linear(m, &l->o, mkey(seed, il, 22), NULL, 0, H, m->q0 * HD, m->qh * HD, c->att_qh * HD));
             TRY(make_vec(m, &l->q_norm, mkey(seed, il, 7), NULL, 0, HD, 1.0f, 0.1f));
             TRY(make_vec(m, &l->k_norm, mkey(seed, il, 8), NULL, 0, HD, 1.0f, 0.1f));
-            TRY(dalloc(m, (void **)&l->kcache, 2 * (size_t)c->max_ctx * m->kvh * HD));
-            TRY(dalloc(m, (void **)&l->vcache, 2 * (size_t)c->max_ctx * m->kvh * HD));
+            TRY(dalloc(m, (void **)&l->kcache, 2 * (size_t)c->max_ctx * m->kvh * HD * m->B));
+            TRY(dalloc(m, (void **)&l->vcache, 2 * (size_t)c->max_ctx * m->kvh * HD * m->B));
         }
         TRY(make_linear(m, &l->gate, mkey(seed, il, 30), NULL, m->f0, m->ffn, 0, H, H));
         TRY(make_linear(m, &l->up, mkey(seed, il, 31), NULL, m->f0, m->ffn, 0, H, H));
@@ -241,35 +247,36 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(make_vec(m, &m->final_norm, mkey(seed, -1, 9), NULL, 0, H, 1.0f, 0.1f));
     TRY(dalloc(m, (void **)&m->embed, 2 * (size_t)c->vocab * H));
     TRY(dec_k_synth_vec(mkey(seed, -1, 41), NULL, 0, (int64_t)c->vocab * H, 0.0f, 1.0f, NULL, m->embed, NULL));
-    /* activations */
+    /* activations, [batch][...] */
     const int mx = H > m->ffn ? H : m->ffn;
-    TRY(dalloc(m, (void **)&m->x, 4 * (size_t)H));
-    TRY(dalloc(m, (void **)&m->t, 4 * (size_t)H));
-    TRY(dalloc(m, (void **)&m->h16, 2 * (size_t)mx));
-    TRY(dalloc(m, (void **)&m->qkv_f, 4 * (size_t)m->conv_dim));
-    TRY(dalloc(m, (void **)&m->qkv16, 2 * (size_t)m->conv_dim));
-    TRY(dalloc(m, (void **)&m->z_f, 4 * (size_t)m->vh * HD));
-    TRY(dalloc(m, (void **)&m->eg, 4 * (size_t)m->vh));
-    TRY(dalloc(m, (void **)&m->beta, 4 * (size_t)m->vh));
-    TRY(dalloc(m, (void **)&m->o_f, 4 * (size_t)m->vh * HD));
-    TRY(dalloc(m, (void **)&m->y16, 2 * (size_t)m->vh * HD));
-    TRY(dalloc(m, (void **)&m->qg_f, 4 * 2 * (size_t)m->qh * HD));
-    TRY(dalloc(m, (void **)&m->kv_f, 4 * 2 * (size_t)m->kvh * HD));
-    TRY(dalloc(m, (void **)&m->q_f, 4 * (size_t)m->qh * HD));
-    TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 4)));
-    TRY(dalloc(m, (void **)&m->ya16, 2 * (size_t)m->qh * HD));
-    TRY(dalloc(m, (void **)&m->hf16, 2 * (size_t)m->ffn));
-    TRY(dalloc(m, (void **)&m->logits, 4 * (size_t)m->vocab));
-    TRY(dalloc(m, (void **)&m->key, 8));
-    TRY(dalloc(m, (void **)&m->keys, 8 * (size_t)W));
-    TRY(dalloc(m, (void **)&m->tok, 4));
+    const size_t B = (size_t)m->B;
+    TRY(dalloc(m, (void **)&m->x, 4 * (size_t)H * B));
+    TRY(dalloc(m, (void **)&m->t, 4 * (size_t)H * B));
+    TRY(dalloc(m, (void **)&m->h16, 2 * (size_t)mx * B));
+    TRY(dalloc(m, (void **)&m->qkv_f, 4 * (size_t)m->conv_dim * B));
+    TRY(dalloc(m, (void **)&m->qkv16, 2 * (size_t)m->conv_dim * B));
+    TRY(dalloc(m, (void **)&m->z_f, 4 * (size_t)m->vh * HD * B));
+    TRY(dalloc(m, (void **)&m->eg, 4 * (size_t)m->vh * B));
+    TRY(dalloc(m, (void **)&m->beta, 4 * (size_t)m->vh * B));
+    TRY(dalloc(m, (void **)&m->o_f, 4 * (size_t)m->vh * HD * B));
+    TRY(dalloc(m, (void **)&m->y16, 2 * (size_t)m->vh * HD * B));
+    TRY(dalloc(m, (void **)&m->qg_f, 4 * 2 * (size_t)m->qh * HD * B));
+    TRY(dalloc(m, (void **)&m->kv_f, 4 * 2 * (size_t)m->kvh * HD * B));
+    TRY(dalloc(m, (void **)&m->q_f, 4 * (size_t)m->qh * HD * B));
+    TRY(dalloc(m, (void **)&m->part, 4 * (size_t)m->qh * m->nchunks * (HD + 4) * B));
+    TRY(dalloc(m, (void **)&m->ya16, 2 * (size_t)m->qh * HD * B));
+    TRY(dalloc(m, (void **)&m->hf16, 2 * (size_t)m->ffn * B));
+    TRY(dalloc(m, (void **)&m->logits, 4 * (size_t)m->vocab * B));
+    TRY(dalloc(m, (void **)&m->key, 8 * B));
+    TRY(dalloc(m, (void **)&m->keys, 8 * (size_t)W * B));
+    TRY(dalloc(m, (void **)&m->tok, 4 * B));
     TRY(dalloc(m, (void **)&m->pos, 4));
-    TRY(dalloc(m, (void **)&m->hist, 4 * (size_t)c->max_ctx));
+    TRY(dalloc(m, (void **)&m->hist, 4 * (size_t)c->max_ctx * B));
     TRY(dalloc(m, (void **)&m->ar_epoch, 16));
     TRY(dalloc(m, (void **)&m->ar_done, 16));
     TRY(dalloc(m, (void **)&m->ak_epoch, 16));
     TRY(dalloc(m, (void **)&m->err, 16));
-    TRY(dalloc(m, (void **)&m->prompt, 4 * ((size_t)c->max_ctx + 1)));
+    TRY(dalloc(m, (void **)&m->prompt, 4 * ((size_t)c->max_ctx * B + 1)));
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { rc = fail(e); goto bad; }
     free(rows); free(cidx);
@@ -362,55 +369,61 @@ int dec_status(dec_model *m, int32_t *flags)
     return 0;
 }
 
+/* Sequence b of a batch draws from seed ^ (b * golden ratio): sequence 0
+ * is the unbatched model's. */
+static uint64_t seq_seed(uint64_t seed, int b) { return seed ^ ((uint64_t)b * 0x9E3779B97F4A7C15ull); }
+
 int dec_prefill_random(dec_model *m, int len, uint64_t seed)
 {
     if (!m || len < 0 || len >= m->c.max_ctx) return -11;
     cudaSetDevice(m->device);
-    for (int il = 0; il < m->c.n_layers; il++) {
-        layer_t *l = &m->L[il];
-        if (l->attn) {
-            /* cache [pos][kvh][hd]: draws indexed by (pos, global kv head, d) */
-            const int64_t n = (int64_t)len * m->kvh * HD;
-            if (n == 0) continue;
-            int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
-            for (int64_t i = 0; i < n; i++) {
-                const int64_t p = i / (m->kvh * HD), r = i % (m->kvh * HD);
-                idx[i] = (int32_t)((p * m->c.att_kvh + m->kv0 + r / HD) * HD + r % HD);
+    const size_t cache_seq = (size_t)m->c.max_ctx * m->kvh * HD;
+    /* draw indices: cache [pos][kvh][hd] by (pos, global kv head, d); conv
+     * state [3][conv_dim] by (tap, global channel) */
+    const int64_t n_kv = (int64_t)len * m->kvh * HD, n_cv = 3 * (int64_t)m->conv_dim;
+    const int64_t n_idx = n_kv > n_cv ? n_kv : n_cv;
+    int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * (size_t)(n_idx > 0 ? n_idx : 1));
+    int32_t *d_kv = NULL, *d_cv = NULL;
+    int rc = idx ? 0 : -11;
+    cudaError_t e = cudaSuccess;
+    if (!rc && n_kv > 0) {
+        for (int64_t i = 0; i < n_kv; i++) {
+            const int64_t p = i / (m->kvh * HD), r = i % (m->kvh * HD);
+            idx[i] = (int32_t)((p * m->c.att_kvh + m->kv0 + r / HD) * HD + r % HD);
+        }
+        e = cudaMalloc((void **)&d_kv, sizeof(int32_t) * (size_t)n_kv);
+        if (e == cudaSuccess) e = cudaMemcpy(d_kv, idx, sizeof(int32_t) * (size_t)n_kv, cudaMemcpyHostToDevice);
+    }
+    if (!rc && e == cudaSuccess && m->chan) {
+        for (int64_t i = 0; i < n_cv; i++)
+            idx[i] = (int32_t)((i / m->conv_dim) * m->conv_g + m->chan[i % m->conv_dim]);
+        e = cudaMalloc((void **)&d_cv, sizeof(int32_t) * (size_t)n_cv);
+        if (e == cudaSuccess) e = cudaMemcpy(d_cv, idx, sizeof(int32_t) * (size_t)n_cv, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) rc = fail(e);
+    for (int b = 0; b < m->B && !rc; b++) {
+        const uint64_t sb = seq_seed(seed, b);
+        for (int il = 0; il < m->c.n_layers && !rc; il++) {
+            layer_t *l = &m->L[il];
+            if (l->attn) {
+                if (n_kv == 0) continue;
+                rc = dec_k_synth_vec(mkey(sb, il, 50), d_kv, 0, n_kv, 0.f, 1.f, NULL, l->kcache + b * cache_seq, NULL);
+                if (!rc) rc = dec_k_synth_vec(mkey(sb, il, 51), d_kv, 0, n_kv, 0.f, 1.f, NULL, l->vcache + b * cache_seq, NULL);
+            } else {
+                const int64_t ns = (int64_t)m->vh * HD * HD;
+                rc = dec_k_synth_vec(mkey(sb, il, 52), NULL, (int64_t)m->v0 * HD * HD, ns, 0.f, 0.02f,
+                                     l->rec_state + b * ns, NULL, NULL);
+                if (!rc) rc = dec_k_synth_vec(mkey(sb, il, 53), d_cv, 0, n_cv, 0.f, 0.5f, l->conv_state + b * n_cv,
+                                              NULL, NULL);
             }
-            int32_t *d_idx = NULL;
-            cudaError_t e = cudaMalloc((void **)&d_idx, sizeof(int32_t) * (size_t)n);
-            if (e == cudaSuccess) e = cudaMemcpy(d_idx, idx, sizeof(int32_t) * (size_t)n, cudaMemcpyHostToDevice);
-            free(idx);
-            if (e != cudaSuccess) { if (d_idx) cudaFree(d_idx); return fail(e); }
-            int rc = dec_k_synth_vec(mkey(seed, il, 50), d_idx, 0, n, 0.f, 1.f, NULL, l->kcache, NULL);
-            if (!rc) rc = dec_k_synth_vec(mkey(seed, il, 51), d_idx, 0, n, 0.f, 1.f, NULL, l->vcache, NULL);
-            e = cudaDeviceSynchronize();
-            cudaFree(d_idx);
-            if (rc) return rc;
-            if (e != cudaSuccess) return fail(e);
-        } else {
-            const int64_t ns = (int64_t)m->vh * HD * HD;
-            CK(dec_k_synth_vec(mkey(seed, il, 52), NULL, (int64_t)m->v0 * HD * HD, ns, 0.f, 0.02f, l->rec_state, NULL, NULL));
-            /* conv state [3][conv_dim]: draws keyed by (tap, global channel) */
-            const int64_t nc = 3 * (int64_t)m->conv_dim;
-            int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * (size_t)nc);
-            if (!idx) return -11;
-            for (int64_t i = 0; i < nc; i++)
-                idx[i] = (int32_t)((i / m->conv_dim) * m->conv_g + m->chan[i % m->conv_dim]);
-            int32_t *d_idx = NULL;
-            cudaError_t e = cudaMalloc((void **)&d_idx, sizeof(int32_t) * (size_t)nc);
-            if (e == cudaSuccess) e = cudaMemcpy(d_idx, idx, sizeof(int32_t) * (size_t)nc, cudaMemcpyHostToDevice);
-            free(idx);
-            if (e != cudaSuccess) { if (d_idx) cudaFree(d_idx); return fail(e); }
-            int rc = dec_k_synth_vec(mkey(seed, il, 53), d_idx, 0, nc, 0.f, 0.5f, l->conv_state, NULL, NULL);
-            e = cudaDeviceSynchronize();
-            cudaFree(d_idx);
-            if (rc) return rc;
-            if (e != cudaSuccess) return fail(e);
         }
     }
-    cudaError_t e = cudaMemcpy(m->pos, &len, 4, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    e = cudaDeviceSynchronize();
+    if (d_kv) cudaFree(d_kv);
+    if (d_cv) cudaFree(d_cv);
+    free(idx);
+    if (rc) return rc;
+    if (e == cudaSuccess) e = cudaMemcpy(m->pos, &len, 4, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return fail(e);
     m->hpos = len;
     return 0;
@@ -420,8 +433,10 @@ int dec_set(dec_model *m, int pos, int token)
 {
     if (!m || pos < 0 || pos >= m->c.max_ctx || token < 0 || token >= m->c.vocab) return -11;
     const int32_t zero = 0;
+    int32_t toks[8];
+    for (int b = 0; b < m->B; b++) toks[b] = token;
     cudaError_t e = cudaMemcpy(m->pos, &pos, 4, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(m->tok, &token, 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(m->tok, toks, 4 * (size_t)m->B, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(m->prompt, &zero, 4, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return fail(e);
     m->hpos = pos;
@@ -431,19 +446,23 @@ int dec_set(dec_model *m, int pos, int token)
 int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream)
 {
     if (!m || !tokens || n < 1 || n > m->c.max_ctx) return -11;
-    for (int i = 0; i < n; i++) if (tokens[i] < 0 || tokens[i] >= m->c.vocab) return -11;
+    for (int64_t i = 0; i < (int64_t)n * m->B; i++) if (tokens[i] < 0 || tokens[i] >= m->c.vocab) return -11;
     const cudaStream_t s = (cudaStream_t)stream;
     const int32_t zero = 0;
     cudaError_t e = cudaSuccess;
-    for (int il = 0; il < m->c.n_layers && e == cudaSuccess; il++) {     /* a new sequence */
+    for (int il = 0; il < m->c.n_layers && e == cudaSuccess; il++) {     /* new sequences */
         layer_t *l = &m->L[il];
         if (l->attn) continue;
-        e = cudaMemsetAsync(l->conv_state, 0, sizeof(float) * 3 * (size_t)m->conv_dim, s);
-        if (e == cudaSuccess) e = cudaMemsetAsync(l->rec_state, 0, sizeof(float) * (size_t)m->vh * HD * HD, s);
+        e = cudaMemsetAsync(l->conv_state, 0, sizeof(float) * 3 * (size_t)m->conv_dim * m->B, s);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(l->rec_state, 0, sizeof(float) * (size_t)m->vh * HD * HD * m->B, s);
     }
+    int32_t first[8];
+    for (int b = 0; b < m->B; b++) first[b] = tokens[(size_t)b * n];
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->prompt, &n, 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(m->prompt + 1, tokens, 4 * (size_t)n, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(m->tok, tokens, 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->prompt + 1, tokens, 4 * (size_t)n * m->B, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->tok, first, 4 * (size_t)m->B, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, &zero, 4, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return fail(e);
@@ -453,16 +472,21 @@ int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream)
 
 #define PF_BYTES (48 * 1024)
 
+/* outputs [batch][rows] */
 static void mvjob(dmv_job *J, const linear_t *l, int epi)
 {
     memset(J, 0, sizeof *J);
     J->wq = l->wq; J->sc = l->sc; J->rows = l->rows; J->epi = epi; J->s_pitch = l->s_pitch;
+    J->ostride = l->rows;
 }
 
-static void mvparams(dmv_params *P, int K, int op, const void *x, const float *nw, float eps, uint16_t *seam)
+/* inputs [batch][K] */
+static void mvparams(dec_model *m, dmv_params *P, int K, int op, const void *x, const float *nw, float eps,
+                     uint16_t *seam)
 {
     memset(P, 0, sizeof *P);
     P->K = K; P->op = op; P->x = x; P->nw = nw; P->eps = eps; P->seam = seam; P->pf_bytes = PF_BYTES;
+    P->nvec = m->B; P->xs = K;
 }
 
 /* row-parallel block: a single GPU adds into the residual in the matvec
@@ -471,6 +495,7 @@ static int row_parallel(dec_model *m, dmv_params *P, const linear_t *l, void *s)
 {
     mvjob(&P->jobs[0], l, m->world == 1 ? DMV_EPI_ACC : DMV_EPI_F32);
     P->jobs[0].out_f32 = m->world == 1 ? m->x : m->t;
+    P->jobs[0].ostride = m->c.hidden;
     P->njobs = 1;
     CK(dec_k_matvec(P, s, m->pdl));
     if (m->world == 1) return 0;
@@ -491,10 +516,14 @@ int dec_step(dec_model *m, void *s)
     const dec_config *c = &m->c;
     const int H = c->hidden, pdl = m->pdl && s != NULL;   /* not on the legacy default stream */
     dmv_params P;
-    CK(dec_k_embed(m->embed, H, m->tok, m->x, s, pdl));
+    CK(dec_k_embed(m->embed, H, m->tok, m->x, m->B, s, pdl));
+    const size_t xbytes = sizeof(float) * (size_t)H * m->B;
     for (int il = 0; il < c->n_layers; il++) {
         layer_t *l = &m->L[il];
-        mvparams(&P, H, DMV_OP_RMSNORM, m->x, l->attn_norm, c->rms_eps, m->h16);
+        if (m->rseam && il < m->nrseam
+            && cudaMemcpyAsync(m->rseam + il * (xbytes / 4), m->x, xbytes, cudaMemcpyDeviceToDevice,
+                               (cudaStream_t)s) != cudaSuccess) return -20;
+        mvparams(m, &P, H, DMV_OP_RMSNORM, m->x, l->attn_norm, c->rms_eps, m->h16);
         if (!l->attn) {
             /* q|k|v with the conv + SiLU epilogue, z, and a|b with the gates */
             mvjob(&P.jobs[0], &l->qkv, DMV_EPI_CONV);
@@ -504,7 +533,7 @@ int dec_step(dec_model *m, void *s)
             P.jobs[1].out_f32 = m->z_f;
             mvjob(&P.jobs[2], &l->ab, DMV_EPI_GATES);
             P.jobs[2].out_f32 = m->eg; P.jobs[2].out2_f32 = m->beta;
-            P.jobs[2].p0 = l->ssm_a; P.jobs[2].p1 = l->dt_bias; P.jobs[2].n1 = m->vh;
+            P.jobs[2].p0 = l->ssm_a; P.jobs[2].p1 = l->dt_bias; P.jobs[2].n1 = m->vh; P.jobs[2].ostride = m->vh;
             P.njobs = 3;
             CK(dec_k_matvec(&P, s, pdl));
             gdn_f32_args g;
@@ -513,9 +542,10 @@ int dec_step(dec_model *m, void *s)
             g.q = m->qkv16; g.k = m->qkv16 + (size_t)m->kh * HD; g.v = m->qkv16 + (size_t)2 * m->kh * HD;
             g.g = NULL; g.eg = m->eg; g.beta = m->beta; g.l2norm = 1; g.q_scale = 1.0f / sqrtf((float)HD);
             g.out_f32 = m->o_f; g.pdl = pdl;
+            g.nseq = m->B; g.seq_in = m->conv_dim;
             CK(gdn_run_f32(&g, s));
             /* output norm and z gate folded into the out projection */
-            mvparams(&P, m->vh * HD, DMV_OP_GATED, m->o_f, l->ssm_norm, c->rms_eps, m->y16);
+            mvparams(m, &P, m->vh * HD, DMV_OP_GATED, m->o_f, l->ssm_norm, c->rms_eps, m->y16);
             P.x2 = m->z_f;
             CK(row_parallel(m, &P, &l->out, s));
         } else {
@@ -528,23 +558,26 @@ int dec_step(dec_model *m, void *s)
             /* q/k norm, RoPE and the cache write folded into flash decoding */
             CK(dec_k_attention(m->qg_f, m->kv_f, l->q_norm, l->k_norm, m->qh, m->kvh, c->n_rot, c->rope_theta,
                                c->rms_eps, m->pos, c->max_ctx, m->att_ch, m->part, m->q_f, l->kcache, l->vcache,
-                               m->ya16, s, pdl));
-            mvparams(&P, m->qh * HD, DMV_OP_F16, m->ya16, NULL, 0.f, NULL);
+                               m->ya16, m->B, s, pdl));
+            mvparams(m, &P, m->qh * HD, DMV_OP_F16, m->ya16, NULL, 0.f, NULL);
             CK(row_parallel(m, &P, &l->o, s));
         }
         /* SwiGLU: gate and up rows paired in one warp, silu(g)*u in the epilogue */
-        mvparams(&P, H, DMV_OP_RMSNORM, m->x, l->post_norm, c->rms_eps, m->h16);
+        mvparams(m, &P, H, DMV_OP_RMSNORM, m->x, l->post_norm, c->rms_eps, m->h16);
         mvjob(&P.jobs[0], &l->gate, DMV_EPI_SWIGLU);
         P.jobs[0].wq2 = l->up.wq; P.jobs[0].sc2 = l->up.sc; P.jobs[0].out_f16 = m->hf16;
         P.njobs = 1;
         CK(dec_k_matvec(&P, s, pdl));
-        mvparams(&P, m->ffn, DMV_OP_F16, m->hf16, NULL, 0.f, NULL);
+        mvparams(m, &P, m->ffn, DMV_OP_F16, m->hf16, NULL, 0.f, NULL);
         CK(row_parallel(m, &P, &l->down, s));
         if (m->lev && il < m->nlev && cudaEventRecord((cudaEvent_t)m->lev[il], (cudaStream_t)s) != cudaSuccess)
             return -20;
     }
+    if (m->rseam && c->n_layers < m->nrseam
+        && cudaMemcpyAsync(m->rseam + c->n_layers * (xbytes / 4), m->x, xbytes, cudaMemcpyDeviceToDevice,
+                           (cudaStream_t)s) != cudaSuccess) return -20;
     /* LM head with the first-max argmax key in its epilogue */
-    mvparams(&P, H, DMV_OP_RMSNORM, m->x, m->final_norm, c->rms_eps, m->h16);
+    mvparams(m, &P, H, DMV_OP_RMSNORM, m->x, m->final_norm, c->rms_eps, m->h16);
     mvjob(&P.jobs[0], &m->lm, DMV_EPI_ARGMAX);
     P.jobs[0].out_f32 = m->logits;
     P.key = m->key; P.idx0 = m->voc0; P.njobs = 1;
@@ -554,9 +587,9 @@ int dec_step(dec_model *m, void *s)
                                  m->prompt, m->ak_epoch, m->err, m->spin_limit, s, pdl);
     if (m->world > 1) {
         if (ncclAllGather(m->key, m->keys, 1, ncclUint64, m->comm, (cudaStream_t)s) != ncclSuccess) return -20;
-        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);
+        return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, 1, s, pdl);
     }
-    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, s, pdl);
+    return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, m->B, s, pdl);
 }
 
 int dec_set_layer_events(dec_model *m, void **events, int n)
@@ -564,6 +597,14 @@ int dec_set_layer_events(dec_model *m, void **events, int n)
     if (!m || n < 0 || (n && !events)) return -11;
     m->lev = n ? events : NULL;
     m->nlev = n;
+    return 0;
+}
+
+int dec_set_residual_seams(dec_model *m, float *buf, int n)
+{
+    if (!m || n < 0 || n > m->c.n_layers + 1 || (n && !buf)) return -11;
+    m->rseam = n ? buf : NULL;
+    m->nrseam = n;
     return 0;
 }
 
@@ -575,7 +616,7 @@ int64_t dec_layer_bytes(dec_model *m, int layer)
     int64_t b = 0;
     if (layer < 0) {
         ls[n++] = &m->lm;
-        b += (int64_t)m->c.hidden * 2;                 /* the embedding row */
+        b += (int64_t)m->c.hidden * 2 * m->B;          /* the embedding rows */
     } else {
         const layer_t *l = &m->L[layer];
         if (l->attn) {
@@ -583,10 +624,10 @@ int64_t dec_layer_bytes(dec_model *m, int layer)
             int pos = 0;
             cudaSetDevice(m->device);
             cudaMemcpy(&pos, m->pos, 4, cudaMemcpyDeviceToHost);
-            b += (int64_t)2 * (pos + 1) * m->kvh * HD * 2;            /* K and V up to the position */
+            b += (int64_t)2 * (pos + 1) * m->kvh * HD * 2 * m->B;     /* K and V up to the position */
         } else {
             ls[n++] = &l->qkv; ls[n++] = &l->z; ls[n++] = &l->ab; ls[n++] = &l->out;
-            b += (int64_t)2 * m->vh * HD * HD * 4 + (int64_t)2 * 3 * m->conv_dim * 4;   /* states r+w */
+            b += ((int64_t)2 * m->vh * HD * HD * 4 + (int64_t)2 * 3 * m->conv_dim * 4) * m->B;   /* states r+w */
         }
         ls[n++] = &l->gate; ls[n++] = &l->up; ls[n++] = &l->down;
     }
@@ -631,17 +672,19 @@ int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, 
 int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count)
 {
     if (!m || !name) return -11;
+    const int B = m->B;
     if (layer < 0) {
         const int H = m->c.hidden;
         const struct { const char *n; const void *p; int32_t c; } act[] = {
             {"final_norm", m->final_norm, H}, {"embed", m->embed, m->c.vocab * H},
-            /* activation seams of the last step (the last layer that wrote them) */
-            {"x", m->x, H}, {"h16", m->h16, H}, {"qkv", m->qkv_f, m->conv_dim},
-            {"qkv16", m->qkv16, m->conv_dim}, {"z", m->z_f, m->vh * HD},
-            {"eg", m->eg, m->vh}, {"beta", m->beta, m->vh}, {"o", m->o_f, m->vh * HD},
-            {"y16", m->y16, m->vh * HD}, {"qg", m->qg_f, 2 * m->qh * HD}, {"kv", m->kv_f, 2 * m->kvh * HD},
-            {"q", m->q_f, m->qh * HD}, {"ya16", m->ya16, m->qh * HD},
-            {"hf16", m->hf16, m->ffn}, {"logits", m->logits, m->vocab}};
+            /* activation seams of the last step (the last layer that wrote
+             * them), [batch][...] */
+            {"x", m->x, H * B}, {"h16", m->h16, H * B}, {"qkv", m->qkv_f, m->conv_dim * B},
+            {"qkv16", m->qkv16, m->conv_dim * B}, {"z", m->z_f, m->vh * HD * B},
+            {"eg", m->eg, m->vh * B}, {"beta", m->beta, m->vh * B}, {"o", m->o_f, m->vh * HD * B},
+            {"y16", m->y16, m->vh * HD * B}, {"qg", m->qg_f, 2 * m->qh * HD * B},
+            {"kv", m->kv_f, 2 * m->kvh * HD * B}, {"q", m->q_f, m->qh * HD * B},
+            {"ya16", m->ya16, m->qh * HD * B}, {"hf16", m->hf16, m->ffn * B}, {"logits", m->logits, m->vocab * B}};
         for (unsigned i = 0; i < sizeof act / sizeof act[0]; i++)
             if (!strcmp(name, act[i].n)) { *d_ptr = act[i].p; *count = act[i].c; return 0; }
         return -11;
@@ -652,8 +695,9 @@ int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int
         {"attn_norm", L->attn_norm, m->c.hidden}, {"post_norm", L->post_norm, m->c.hidden},
         {"conv_w", L->conv_w, 4 * m->conv_dim}, {"ssm_a", L->ssm_a, m->vh}, {"dt_bias", L->dt_bias, m->vh},
         {"ssm_norm", L->ssm_norm, HD}, {"q_norm", L->q_norm, HD}, {"k_norm", L->k_norm, HD},
-        {"conv_state", L->conv_state, 3 * m->conv_dim}, {"rec_state", L->rec_state, m->vh * HD * HD},
-        {"kcache", L->kcache, m->c.max_ctx * m->kvh * HD}, {"vcache", L->vcache, m->c.max_ctx * m->kvh * HD}};
+        {"conv_state", L->conv_state, 3 * m->conv_dim * B}, {"rec_state", L->rec_state, m->vh * HD * HD * B},
+        {"kcache", L->kcache, m->c.max_ctx * m->kvh * HD * B},
+        {"vcache", L->vcache, m->c.max_ctx * m->kvh * HD * B}};
     for (unsigned i = 0; i < sizeof tab / sizeof tab[0]; i++)
         if (!strcmp(name, tab[i].n) && tab[i].p) { *d_ptr = tab[i].p; *count = tab[i].c; return 0; }
     return -11;
@@ -667,9 +711,9 @@ int64_t dec_step_bytes(dec_model *m)
     cudaMemcpy(&pos, m->pos, 4, cudaMemcpyDeviceToHost);
     int64_t b = m->weight_bytes;
     for (int il = 0; il < m->c.n_layers; il++) {
-        if (m->L[il].attn) b += (int64_t)2 * (pos + 1) * m->kvh * HD * 2;
-        else b += (int64_t)2 * m->vh * HD * HD * 4 + (int64_t)2 * 3 * m->conv_dim * 4;
+        if (m->L[il].attn) b += (int64_t)2 * (pos + 1) * m->kvh * HD * 2 * m->B;
+        else b += ((int64_t)2 * m->vh * HD * HD * 4 + (int64_t)2 * 3 * m->conv_dim * 4) * m->B;
     }
-    b += (int64_t)m->c.hidden * 2;              /* the embedding row */
+    b += (int64_t)m->c.hidden * 2 * m->B;       /* the embedding rows */
     return b;
 }

@@ -360,8 +360,22 @@ __device__ __forceinline__ void load_step(const gdn_f32_args &A, int t, int h, i
 
 // grid: H x 8 CTAs of 4 warps; CTA (h, c) owns columns 16c .. 16c+15 of head h.
 __global__ void __launch_bounds__(128)
-gdn_f32_kernel(const gdn_f32_args A)
+gdn_f32_kernel(const gdn_f32_args A0)
 {
+    // sequence blockIdx.y of a batched step: its inputs, outputs and state
+    gdn_f32_args A = A0;
+    if (blockIdx.y) {
+        const size_t n = blockIdx.y, hd = (size_t)A.H * 128;
+        A.q += n * A.seq_in; A.k += n * A.seq_in; A.v += n * A.seq_in;
+        if (A.g) A.g += n * hd;
+        if (A.a) A.a += n * A.H;
+        if (A.b) A.b += n * A.H;
+        if (A.eg) A.eg += n * A.H;
+        if (A.beta) A.beta += n * A.H;
+        if (A.out_f32) A.out_f32 += n * hd;
+        if (A.out_f16) A.out_f16 += n * hd;
+        A.S += n * hd * 128;
+    }
     const int h = blockIdx.x >> 3;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j = (blockIdx.x & 7) * 16 + warp * 4 + (lane >> 3);
@@ -442,8 +456,10 @@ extern "C" int gdn_run_f32(const gdn_f32_args *a, void *stream)
     if (!a || a->D != 128 || a->T <= 0 || a->H <= 0 || a->KH <= 0 || !a->S || !a->q || !a->k || !a->v
         || (!a->eg && !a->a) || (!a->beta && !a->b) || (!a->out_f32 && !a->out_f16)) return -11;
     if ((((uintptr_t)a->S) | ((uintptr_t)a->q) | ((uintptr_t)a->k)) & 15) return -11;
+    const int nseq = a->nseq > 1 ? a->nseq : 1;
+    if (nseq > 1 && (a->T != 1 || a->seq_in <= 0 || (a->seq_in & 7) || nseq > 65535)) return -11;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a->H * 8);
+    cfg.gridDim = dim3(a->H * 8, nseq);
     cfg.blockDim = dim3(128);
     cfg.stream = reinterpret_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];

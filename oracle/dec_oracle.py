@@ -198,12 +198,23 @@ class Model:
         self.seams.update({(il, "xmid"): x, (il, "post16"): h, (il, "hf16"): hh})
         return x + self.mv(self.W[il, "down"], hh)
 
-    def step(self, tok, pos):
-        """One token: returns (float64 logits, argmax_first token)."""
+    def step(self, tok, pos, x_in=None):
+        """One token: returns (float64 logits, argmax_first token).  x_in
+        (optional, [n_layers + 1][hidden]): the residual each layer starts
+        from and the LM head's input, taken from the implementation under test
+        (its residual seams) instead of this model's own, so each layer is
+        compared from identical inputs; self.layer_out[il] is layer il's output
+        from that input."""
         x = self.P[-1, "embed"][tok].astype(np.float64)
+        self.layer_out = []
         for il in range(self.c["n_layers"]):
+            if x_in is not None:
+                x = np.asarray(x_in[il], dtype=np.float64)
             x = self.attn(il, x, pos) if self.is_attn(il) else self.gdn(il, x)
             x = self.ffn(il, x)
+            self.layer_out.append(x)
+        if x_in is not None:
+            x = np.asarray(x_in[self.c["n_layers"]], dtype=np.float64)
         self.last_x = x
         h = self.r(rmsnorm(x, self.P[-1, "final_norm"], self.c["rms_eps"], self.mut))
         logits = self.mv(self.W[-1, "lm_head"], h)

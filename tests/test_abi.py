@@ -92,9 +92,11 @@ def test_decode_bad_configs_are_refused_before_any_cuda_call(pkg):
     L = pkg.declib()
     h = C.c_void_p()
     for k, v in [("gdn_hd", 64), ("hidden", 200), ("att_kvh", 3), ("n_rot", 33), ("max_ctx", 0),
-                 ("ffn", 320), ("attn_every", 0)]:
+                 ("ffn", 320), ("attn_every", 0), ("batch", 9), ("batch", -1)]:
         cfg = dict(cfg0)
         cfg[k] = v
         assert L.dec_create(C.byref(pkg.DecConfig(**cfg)), 1, 0, 0, 1, C.byref(h)) == -11, k
     assert L.dec_create(C.byref(pkg.DecConfig(**cfg0)), 1, 0, 2, 2, C.byref(h)) == -11
     assert L.dec_create(C.byref(pkg.DecConfig(**cfg0)), 1, 0, 0, 8, C.byref(h)) == -11   # 4 kv heads
+    # batches are single-GPU
+    assert L.dec_create(C.byref(pkg.DecConfig(**dict(cfg0, batch=2))), 1, 0, 0, 2, C.byref(h)) == -11

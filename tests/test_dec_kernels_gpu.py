@@ -20,8 +20,8 @@ def K(pkg):
     L = pkg.declib()
     P, I, F, U64 = C.c_void_p, C.c_int, C.c_float, C.c_uint64
     sig = {
-        "dec_k_attention": [P, P, P, P, I, I, I, F, F, P, I, I, P, P, P, P, P, P, I],
-        "dec_k_advance": [P, I, P, P, P, P, I, P, P, I],
+        "dec_k_attention": [P, P, P, P, I, I, I, F, F, P, I, I, P, P, P, P, P, I, P, I],
+        "dec_k_advance": [P, I, P, P, P, P, I, P, I, P, I],
     }
     for n, a in sig.items():
         getattr(L, n).argtypes = a
@@ -82,7 +82,7 @@ def _run_attention(K, torch, c, qh, kvh, pos, ctx, ch):
     d = c["d"]
     rc = K.dec_k_attention(ptr(d["qg"]), ptr(d["kv"]), ptr(d["qn"]), ptr(d["kn"]), qh, kvh, c["nrot"], c["theta"], 1e-6,
                            ptr(c["dpos"]), ctx, ch, ptr(c["part"]), ptr(c["qseam"]), ptr(d["kc"]), ptr(d["vc"]),
-                           ptr(c["y"]), None, 0)
+                           ptr(c["y"]), 1, None, 0)
     assert rc == 0
     torch.cuda.synchronize()
 
@@ -152,13 +152,73 @@ def test_advance_picks_first_max_key_and_follows_the_prompt(cuda, K):
     hist = torch.zeros(8, dtype=torch.int32, device="cuda")
     pos = torch.tensor([3], dtype=torch.int32, device="cuda")
     key = torch.ones(1, dtype=torch.int64, device="cuda")
-    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, None, None, 0) == 0
+    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, None, 1, None, 0) == 0
     torch.cuda.synchronize()
     assert int(tok.item()) == 40 and int(hist[3].item()) == 40 and int(pos.item()) == 4 and int(key.item()) == 0
     prompt = torch.tensor([6, 11, 12, 13, 14, 15, 16], dtype=torch.int32, device="cuda")   # length 6
-    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), None, 0) == 0
+    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), 1, None, 0) == 0
     torch.cuda.synchronize()
     assert int(hist[4].item()) == 40 and int(tok.item()) == 16 and int(pos.item()) == 5     # prompt[1 + 5]
-    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), None, 0) == 0
+    assert K.dec_k_advance(ptr(keys), 3, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), 1, None, 0) == 0
     torch.cuda.synchronize()
     assert int(tok.item()) == 40 and int(pos.item()) == 6                                    # prompt over
+
+
+def _attention_ref(O, c, qh, kvh, pos, kc, vc):
+    qgn = c["qg"].reshape(qh, 2, HD)
+    q = np.stack([_rope(O.rmsnorm(qgn[h, 0], c["qn"], 1e-6), pos, c["nrot"], c["theta"]) for h in range(qh)])
+    ref = np.empty((qh, HD))
+    for h in range(qh):
+        gk = h // (qh // kvh)
+        sc = kc[:pos + 1, gk] @ q[h] / np.sqrt(HD)
+        e = np.exp(sc - sc.max())
+        ref[h] = (e @ vc[:pos + 1, gk]) / e.sum()
+    return q, ref * O.sigmoid(qgn[:, 1])
+
+
+def test_attention_batch_of_sequences(cuda, K, O):
+    """Three sequences in one launch (grid z): each attends over its own
+    cache with its own projections at the shared position, and writes its
+    own cache row, q seam and output."""
+    torch = cuda
+    nseq, qh, kvh, ctx, ch, pos = 3, 16, 2, 512, 32, 300
+    cs = [_attention_case(torch, O, qh, kvh, pos, ctx, ch, 500 + b) for b in range(nseq)]
+    cat = lambda k: torch.stack([c["d"][k] for c in cs]).contiguous()
+    qg, kv, kc, vc = cat("qg"), cat("kv"), cat("kc"), cat("vc")
+    nchunks = (ctx + ch - 1) // ch
+    part = torch.zeros(nseq * qh * nchunks * (HD + 4), device="cuda")
+    qseam = torch.zeros(nseq, qh * HD, device="cuda")
+    y = torch.zeros(nseq, qh * HD, dtype=torch.int16, device="cuda")
+    c0 = cs[0]
+    rc = K.dec_k_attention(ptr(qg), ptr(kv), ptr(c0["d"]["qn"]), ptr(c0["d"]["kn"]), qh, kvh, c0["nrot"], c0["theta"],
+                           1e-6, ptr(c0["dpos"]), ctx, ch, ptr(part), ptr(qseam), ptr(kc), ptr(vc), ptr(y), nseq, None, 0)
+    assert rc == 0
+    torch.cuda.synchronize()
+    for b, c in enumerate(cs):
+        c["qn"], c["kn"] = c0["qn"], c0["kn"]                 # the norms are shared weights
+        kcb, vcb = kc[b].cpu().double().numpy(), vc[b].cpu().double().numpy()
+        others = np.ones(ctx, bool)
+        others[pos] = False
+        assert np.array_equal(kcb[others], c["kc0"].double().numpy()[others])
+        kvn = c["kv"].reshape(2, kvh, HD)
+        assert np.array_equal(vcb[pos], O.f16(kvn[1]))
+        q, ref = _attention_ref(O, c, qh, kvh, pos, kcb, vcb)
+        assert rel(qseam[b].double().cpu().numpy().reshape(qh, HD), q) <= 1e-5
+        assert rel(h16(y[b]), ref.reshape(-1)) <= TOL, b
+
+
+def test_advance_batch(cuda, K):
+    """Two sequences: each takes its own first max and its own prompt token;
+    the shared position advances once."""
+    torch = cuda
+    big = lambda v, i: v << 32 | 0xFFFFFFFF - i
+    keys = torch.tensor([big(5, 900), big(9, 4), big(7, 1200), big(9, 3)], dtype=torch.int64, device="cuda")  # [rank][seq]
+    tok = torch.zeros(2, dtype=torch.int32, device="cuda")
+    hist = torch.zeros(2, 8, dtype=torch.int32, device="cuda")
+    pos = torch.tensor([2], dtype=torch.int32, device="cuda")
+    key = torch.ones(2, dtype=torch.int64, device="cuda")
+    prompt = torch.tensor([5, 10, 11, 12, 13, 14, 20, 21, 22, 23, 24], dtype=torch.int32, device="cuda")
+    assert K.dec_k_advance(ptr(keys), 2, ptr(key), ptr(tok), ptr(hist), ptr(pos), 8, ptr(prompt), 2, None, 0) == 0
+    torch.cuda.synchronize()
+    assert hist[0, 2].item() == 1200 and hist[1, 2].item() == 3
+    assert tok.tolist() == [13, 23] and int(pos.item()) == 3 and key.tolist() == [0, 0]

@@ -15,6 +15,8 @@ argmax key) is compared with oracle/dec_oracle.py on identical inputs:
 
 Launches are also chained as programmatic dependents (PDL) with each consuming
 the previous one's output, which must give the same answer as plain launches.
+Batched launches (nvec input vectors sharing each weight load, the decode
+step's sequences) must give every vector the single-vector result.
 """
 import ctypes as C
 
@@ -32,14 +34,14 @@ class Job(C.Structure):
     _fields_ = [("wq", P_), ("wq2", P_), ("sc", P_), ("sc2", P_), ("out_f32", P_), ("out2_f32", P_),
                 ("out_f16", P_), ("p0", P_), ("p1", P_), ("st", P_), ("st_stride", C.c_int32),
                 ("n1", C.c_int32), ("rows", C.c_int32), ("epi", C.c_int32), ("tile0", C.c_int32),
-                ("ntiles", C.c_int32), ("s_pitch", C.c_int32), ("pad_", C.c_int32)]
+                ("ntiles", C.c_int32), ("s_pitch", C.c_int32), ("ostride", C.c_int32)]
 
 
 class Params(C.Structure):
     _fields_ = [("jobs", Job * 4), ("njobs", C.c_int32), ("total_tiles", C.c_int32), ("K", C.c_int32),
                 ("op", C.c_int32), ("x", P_), ("x2", P_), ("nw", P_), ("eps", C.c_float), ("seam", P_),
                 ("key", P_), ("idx0", C.c_int32), ("pf_bytes", C.c_int32), ("ksplit", C.c_int32),
-                ("pad_", C.c_int32)]
+                ("nvec", C.c_int32), ("xs", C.c_int32), ("pad_", C.c_int32)]
 
 
 @pytest.fixture(scope="module")
@@ -322,5 +324,169 @@ def test_refusals(cuda, L):
     assert L.dec_k_matvec(C.byref(p(s_pitch=2)), None, 0) == -11              # scale rows not 16 bytes
     assert L.dec_k_matvec(C.byref(p(epi=EPI["SWIGLU"])), None, 0) == -11      # unpaired SwiGLU
     assert L.dec_k_matvec(C.byref(p(epi=9)), None, 0) == -11
+    q = p()
+    q.nvec, q.xs = 9, 256                                                    # more than 8 vectors
+    assert L.dec_k_matvec(C.byref(q), None, 0) == -11
+    q.nvec, q.xs = 2, 128                                                    # inputs overlap
+    assert L.dec_k_matvec(C.byref(q), None, 0) == -11
+    q = p(ostride=4)
+    q.nvec, q.xs = 2, 256                                                    # outputs overlap
+    assert L.dec_k_matvec(C.byref(q), None, 0) == -11
     assert L.dec_k_matvec(C.byref(p()), None, 0) == 0
     torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------ batches
+
+def staged_ref(O, W, x16):
+    return W @ O.stage_g128(np.asarray(x16, dtype=np.float64))
+
+
+@pytest.mark.parametrize("nv", [2, 3, 4, 8])
+@pytest.mark.parametrize("K,rows", [(128, 5), (2048, 96), (2048, 2048), (6144, 2048), (2048, 20000)])
+def test_batch_f16_inputs(cuda, L, O, nv, K, rows):
+    """nv fp16 vectors at a padded stride: every vector's fp32, fp16 and
+    accumulate outputs equal its own staged product; few rows take the
+    column split over warps."""
+    torch = cuda
+    wq, sc = weights(torch, rows, K, 3 * K + rows + nv)
+    g = torch.Generator().manual_seed(K + nv)
+    xs_ = K + 64
+    xb = (torch.randn(nv, xs_, generator=g) * torch.exp2(torch.randint(-8, 3, (nv, xs_), generator=g).float())).half().cuda()
+    os_ = rows + 8
+    y32 = torch.full((nv, os_), 7.0, device="cuda")
+    y16 = torch.zeros(nv, os_, dtype=torch.int16, device="cuda")
+    acc = torch.randn(nv, os_, generator=g).cuda()
+    acc0 = acc.clone()
+    p = Params(K=K, op=OP["F16"], x=dp(xb), njobs=3, pf_bytes=65536, nvec=nv, xs=xs_)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F32"], out_f32=dp(y32), ostride=os_)
+    p.jobs[1] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F16"], out_f16=dp(y16), ostride=os_)
+    p.jobs[2] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["ACC"], out_f32=dp(acc), ostride=os_)
+    run(L, torch, p)
+    W = deq(O, wq, sc)
+    X = xb.cpu().numpy()[:, :K]
+    Y32, Y16 = y32.cpu().numpy(), y16.cpu().numpy().view(np.float16)
+    D = (acc - acc0).cpu().numpy()
+    for b in range(nv):
+        ref = staged_ref(O, W, X[b])
+        got = Y32[b, :rows].astype(np.float64)
+        assert rel(got, ref) <= 2e-6, b
+        assert np.array_equal(Y16[b, :rows], got.astype(np.float32).astype(np.float16))
+        assert np.allclose(D[b, :rows], got, rtol=0, atol=1e-6 * np.max(np.abs(got)))
+        assert np.all(Y32[b, rows:] == 7.0) and np.all(D[b, rows:] == 0)    # past the rows: untouched
+
+
+@pytest.mark.parametrize("nv", [2, 8])
+def test_batch_rmsnorm_and_seams(cuda, L, O, nv):
+    torch = cuda
+    K, rows = 2048, 700
+    wq, sc = weights(torch, rows, K, 70 + nv)
+    g = torch.Generator().manual_seed(71)
+    res = (torch.randn(nv, K, generator=g) * (1 + torch.arange(nv).float()[:, None])).cuda()
+    w = (1 + 0.1 * torch.randn(K, generator=g)).cuda()
+    seam = torch.zeros(nv, K, dtype=torch.int16, device="cuda")
+    y = torch.zeros(nv, rows, device="cuda")
+    p = Params(K=K, op=OP["RMSNORM"], x=dp(res), nw=dp(w), eps=1e-6, seam=dp(seam), njobs=1, nvec=nv, xs=K)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F32"], out_f32=dp(y), ostride=rows)
+    run(L, torch, p)
+    W = deq(O, wq, sc)
+    H16 = seam.cpu().numpy().view(np.float16)
+    R, wn, Y = res.double().cpu().numpy(), w.double().cpu().numpy(), y.cpu().numpy().astype(np.float64)
+    for b in range(nv):
+        seam_ok(H16[b], O.rmsnorm(R[b], wn, 1e-6))
+        assert rel(Y[b], staged_ref(O, W, H16[b])) <= 2e-6
+
+
+def test_batch_gated_conv_gates(cuda, L, O):
+    """DeltaNet shapes at batch 4: the gated prologue per vector, the conv
+    epilogue on each sequence's own rolling state, the gates per vector."""
+    torch = cuda
+    nv, H, cd, vh = 4, 4, 768, 6
+    K = H * 128
+    g = torch.Generator().manual_seed(81)
+    o = torch.randn(nv, K, generator=g).cuda()
+    z = (2 * torch.randn(nv, K, generator=g)).cuda()
+    w = (1 + 0.1 * torch.randn(128, generator=g)).cuda()
+    seam = torch.zeros(nv, K, dtype=torch.int16, device="cuda")
+    wc, scc = weights(torch, cd, K, 82)
+    wa, sa = weights(torch, 2 * vh, K, 83)
+    cw = (0.5 * torch.randn(cd * 4, generator=g)).cuda()
+    st = (0.5 * torch.randn(nv, 3, cd, generator=g)).cuda()
+    st0 = st.clone()
+    ssm_a = (-1 + 0.2 * torch.randn(vh, generator=g)).cuda()
+    dt = (0.5 * torch.randn(vh, generator=g)).cuda()
+    q16 = torch.zeros(nv, cd, dtype=torch.int16, device="cuda")
+    raw = torch.zeros(nv, cd, device="cuda")
+    eg, beta = torch.zeros(nv, vh, device="cuda"), torch.zeros(nv, vh, device="cuda")
+    p = Params(K=K, op=OP["GATED"], x=dp(o), x2=dp(z), nw=dp(w), eps=1e-6, seam=dp(seam), njobs=2, nvec=nv, xs=K)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wc), sc=dp(scc), rows=cd, epi=EPI["CONV"], out_f16=dp(q16),
+                    out_f32=dp(raw), p0=dp(cw), st=dp(st), st_stride=cd, ostride=cd)
+    p.jobs[1] = Job(s_pitch=spitch(K), wq=dp(wa), sc=dp(sa), rows=2 * vh, epi=EPI["GATES"], out_f32=dp(eg),
+                    out2_f32=dp(beta), p0=dp(ssm_a), p1=dp(dt), n1=vh, ostride=vh)
+    run(L, torch, p)
+    on, zn, wn = o.double().cpu().numpy(), z.double().cpu().numpy(), w.double().cpu().numpy()
+    Wc, Wa = deq(O, wc, scc), deq(O, wa, sa)
+    w4 = cw.cpu().numpy().astype(np.float64).reshape(cd, 4)
+    S0, S1 = st0.cpu().numpy().astype(np.float64), st.cpu().numpy()
+    for b in range(nv):
+        want = np.concatenate([O.rmsnorm(on[b, 128 * i:128 * (i + 1)], wn, 1e-6) * O.silu(zn[b, 128 * i:128 * (i + 1)])
+                               for i in range(H)])
+        y16 = seam.cpu().numpy().view(np.float16)[b]
+        seam_ok(y16, want)
+        proj = staged_ref(O, Wc, y16)
+        r = raw.cpu().numpy()[b].astype(np.float64)
+        assert rel(r, proj) <= 2e-6
+        a = S0[b, 0] * w4[:, 0] + S0[b, 1] * w4[:, 1] + S0[b, 2] * w4[:, 2] + r * w4[:, 3]
+        seam_ok(q16.cpu().numpy().view(np.float16)[b], O.silu(a))
+        assert np.array_equal(S1[b, 0], S0[b, 1].astype(np.float32)) and np.array_equal(S1[b, 2], raw.cpu().numpy()[b])
+        ab = staged_ref(O, Wa, y16)
+        e_ref = np.exp(ssm_a.double().cpu().numpy() * O.softplus(ab[:vh] + dt.double().cpu().numpy()))
+        assert rel(eg[b].double().cpu().numpy(), e_ref) <= 1e-5
+        assert rel(beta[b].double().cpu().numpy(), O.sigmoid(ab[vh:])) <= 1e-5
+
+
+@pytest.mark.parametrize("nv", [2, 8])
+def test_batch_paired_swiglu(cuda, L, O, nv):
+    torch = cuda
+    K, F = 2048, 6144
+    wg, sg = weights(torch, F, K, 91)
+    wu, su = weights(torch, F, K, 92)
+    x = torch.randn(nv, K, generator=torch.Generator().manual_seed(93)).half().cuda()
+    h = torch.zeros(nv, F, dtype=torch.int16, device="cuda")
+    p = Params(K=K, op=OP["F16"], x=dp(x), njobs=1, nvec=nv, xs=K)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wg), wq2=dp(wu), sc=dp(sg), sc2=dp(su), rows=F, epi=EPI["SWIGLU"],
+                    out_f16=dp(h), ostride=F)
+    run(L, torch, p)
+    Wg, Wu = deq(O, wg, sg), deq(O, wu, su)
+    for b in range(nv):
+        xs = O.stage_g128(x[b].cpu().numpy().astype(np.float64))
+        want = O.silu(Wg @ xs) * (Wu @ xs)
+        got = h[b].cpu().numpy().view(np.float16).astype(np.float64)
+        assert np.all(np.abs(got - want) <= 2.0 ** -10 * np.abs(want) + 1e-6 * np.max(np.abs(want))), b
+
+
+def test_batch_argmax_keys(cuda, L, O):
+    """One first-max key per vector; vector 1's winner is planted as a tie
+    with an earlier row."""
+    torch = cuda
+    nv, K, V = 8, 2048, 30000
+    wq, sc = weights(torch, V, K, 101)
+    x = torch.randn(nv, K, generator=torch.Generator().manual_seed(102)).half().cuda()
+    W = deq(O, wq, sc)
+    top1 = int(np.argmax(staged_ref(O, W, x[1].cpu().numpy())))
+    e = 11 if top1 != 11 else 12
+    wq[e] = wq[top1]
+    sc[e] = sc[top1]
+    W = deq(O, wq, sc)
+    logits = torch.zeros(nv, V, device="cuda")
+    key = torch.zeros(nv, dtype=torch.int64, device="cuda")
+    p = Params(K=K, op=OP["F16"], x=dp(x), njobs=1, key=dp(key), idx0=100, nvec=nv, xs=K)
+    p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=V, epi=EPI["ARGMAX"], out_f32=dp(logits), ostride=V)
+    run(L, torch, p)
+    lg = logits.cpu().numpy()
+    for b in range(nv):
+        ref = staged_ref(O, W, x[b].cpu().numpy())
+        assert rel(lg[b].astype(np.float64), ref) <= 2e-6
+        want = int(np.flatnonzero(lg[b] == lg[b].max())[0])
+        assert 0xFFFFFFFF - (int(key[b].item()) & 0xFFFFFFFF) == 100 + want, b
+    assert 0xFFFFFFFF - (int(key[1].item()) & 0xFFFFFFFF) == 100 + min(e, top1)
