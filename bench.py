@@ -440,29 +440,45 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         return f
 
     def layer_profile(h, cfg):
-        """One direct step with an event after every layer: per-layer time and
-        the fraction of the HBM peak its bytes reach (DeltaNet / attention
-        layers and the LM head, averaged by kind).  Events between kernels
-        stop programmatic launches from overlapping layer boundaries, so these
-        fractions are a little below the graph-replay rate."""
+        """One step timed layer by layer: per-layer time and the fraction of
+        the HBM peak its bytes reach (DeltaNet / attention layers and the LM
+        head, averaged by kind).  The persistent step stamps the GPU global
+        timer after every grid barrier (dec_set_clock); the launch-mode step
+        records an event after every layer (events between kernels stop
+        programmatic launches from overlapping layer boundaries, so those
+        fractions are a little below the graph-replay rate)."""
         peak, _ = peaks()
         nl = cfg["n_layers"]
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(nl + 2)]
-        for e in evs:                       # torch creates the CUDA event on first record
-            e.record(stream)
-        torch.cuda.synchronize(dev)
-        arr = (C.c_void_p * nl)(*[C.c_void_p(e.cuda_event) for e in evs[1:nl + 1]])
-        assert D.dec_set_layer_events(h, arr, nl) == 0
         lb = [D.dec_layer_bytes(h, il) for il in range(nl)] + [D.dec_layer_bytes(h, -1)]
-        with torch.cuda.stream(stream):
-            evs[0].record(stream)
-            step_fn(h)()
-            evs[nl + 1].record(stream)
-        torch.cuda.synchronize(dev)
-        assert D.dec_set_layer_events(h, None, 0) == 0
+        bounds = []
+        if D.dec_persistent(h) == 1:
+            slots = D.dec_clock_slots(h)
+            clk = torch.zeros(slots, dtype=torch.int64, device=dev)
+            assert D.dec_set_clock(h, C.c_void_p(clk.data_ptr())) == 0
+            with torch.cuda.stream(stream):
+                step_fn(h)()
+            torch.cuda.synchronize(dev)
+            assert D.dec_set_clock(h, None) == 0
+            t = clk.cpu().numpy()
+            idx = [D.dec_layer_clock(h, il) for il in range(-1, nl + 1)]
+            bounds = [(t[idx[il + 1]] - t[idx[il]]) / 1e3 for il in range(nl + 1)]
+        else:
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(nl + 2)]
+            for e in evs:                       # torch creates the CUDA event on first record
+                e.record(stream)
+            torch.cuda.synchronize(dev)
+            arr = (C.c_void_p * nl)(*[C.c_void_p(e.cuda_event) for e in evs[1:nl + 1]])
+            assert D.dec_set_layer_events(h, arr, nl) == 0
+            with torch.cuda.stream(stream):
+                evs[0].record(stream)
+                step_fn(h)()
+                evs[nl + 1].record(stream)
+            torch.cuda.synchronize(dev)
+            assert D.dec_set_layer_events(h, None, 0) == 0
+            bounds = [evs[il].elapsed_time(evs[il + 1]) * 1e3 for il in range(nl + 1)]
         kinds = {"deltanet": [], "attention": [], "lm_head": []}
         for il in range(nl + 1):
-            us = evs[il].elapsed_time(evs[il + 1]) * 1e3
+            us = float(bounds[il])
             kind = "lm_head" if il == nl else ("attention" if (il + 1) % cfg["attn_every"] == 0 else "deltanet")
             kinds[kind].append((us, lb[il]))
         out = {}
@@ -473,6 +489,8 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
             b = sum(x[1] for x in v) / len(v)
             out[k] = {"layers": len(v), "us": round(us, 2), "bytes": int(b),
                       "frac_hbm": round(b / (us * 1e-6) / 1e9 / peak, 4)}
+        out["timing"] = "global-timer stamps at the persistent kernel's barriers" if D.dec_persistent(h) == 1 \
+            else "CUDA events between layers"
         return out
 
     def capture(h):
@@ -524,6 +542,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         e2e_ms = timed(e2e_run, 1)
         sbytes = D.dec_step_bytes(h)
         per_layer = layer_profile(h, cfg)
+        mode = "persistent (1 launch per step)" if D.dec_persistent(h) == 1 else "one launch per stage"
         del g
         D.dec_destroy(h)
         peak, _ = peaks()
@@ -539,6 +558,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
             "GBps": round(sbytes / (us * 1e-6) / 1e9, 1),
             "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
             "first_tokens": [int(t) for t in toks[0, :8]],
+            "step": mode,
             "per_layer": per_layer,
             "e2e": {"tokens_per_s": round(nb * (511 + gen) / (e2e_ms * 1e-3), 1),
                     "how": "prompts H2D from pinned host, 767 graph replays, each step's generated tokens D2H "
@@ -586,6 +606,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
     ms = timed(g.replay, n)
     sbytes = D.dec_step_bytes(h)
     per_layer = layer_profile(h, cfg)
+    mode = "persistent (1 launch per step)" if D.dec_persistent(h) == 1 else "one launch per stage"
     fl = C.c_int32(0)
     assert D.dec_status(h, C.byref(fl)) == 0 and fl.value == 0, "peer exchange timed out"
     del g
@@ -601,6 +622,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
         "bytes_per_step_per_rank": sbytes,
         "GBps_per_rank": round(sbytes / (us * 1e-6) / 1e9, 1),
         "frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
+        "step": mode,
         "per_layer_rank0": per_layer,
         "collectives_per_step": (2 * cfg["n_layers"] + 1) if world > 1 else 0,
         "exchange": exchange,

@@ -141,6 +141,37 @@ int64_t dec_step_bytes(dec_model *m);
 int64_t dec_layer_bytes(dec_model *m, int layer);
 int dec_set_layer_events(dec_model *m, void **events, int n);
 
+/* The persistent step (single GPU; off by default, environment
+ * DEC_PERSISTENT=1 turns it on at creation): dec_step is then ONE launch of a
+ * kernel that
+ * walks the whole layer program -- the counterpart of the reference
+ * sequencer's per-token program (ref/run9b.c:1028-1170 issues the same A jobs
+ * and delta rule one by one) -- with a grid barrier between dependent stages
+ * and the next projection's weights prefetched into L2 during the current
+ * stage.  Barrier waits are bounded (about a second); a wait that runs out
+ * aborts the step and sets flag 4 of dec_status (which clears it).  Off, every
+ * stage is its own kernel launch (programmatic dependent launches).  On B200 a
+ * grid barrier costs about as much as a dependent launch (2-3 us), so the
+ * launch mode, whose next kernel starts its weight prefetch while the previous
+ * one finishes, is the faster default.
+ * Tensor-parallel models always step in launch mode.
+ * dec_set_persistent(m, on) switches (on: builds and uploads the program;
+ * synchronises the device), dec_persistent(m) tells which mode dec_step uses. */
+int dec_set_persistent(dec_model *m, int on);
+int dec_persistent(dec_model *m);
+/* Bound of each grid-barrier wait of the persistent step, in ns (0: the
+ * default, one second). */
+int dec_set_wait_limit(dec_model *m, int64_t ns);
+
+/* Stage clock of the persistent step: with a device buffer of
+ * dec_clock_slots(m) uint64 entries (NULL to stop), each step writes the GPU
+ * global timer (ns) at its start (entry 0) and after every grid barrier;
+ * dec_layer_clock(m, il) is the entry written at the end of layer il
+ * (il = -1: the embedding; il = n_layers: the LM head). */
+int dec_set_clock(dec_model *m, uint64_t *d_clock);
+int dec_clock_slots(dec_model *m);
+int dec_layer_clock(dec_model *m, int layer);
+
 /* Residual seams (the reference's per-layer seam records, for parity
  * checks): with a device buffer of n slots of [batch][hidden] fp32 (n <=
  * n_layers + 1; NULL/0 to stop), dec_step copies the residual stream into

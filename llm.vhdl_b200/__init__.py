@@ -23,7 +23,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]
 DEC_LIBPATH = os.path.join(LIBDIR, "libdec_b200.so")
-DEC_SOURCES = ["csrc/dec_kernels.cu", "csrc/dec_matvec.cu", "csrc/dec_model.c"]
+DEC_SOURCES = ["csrc/dec_step.cu", "csrc/dec_model.c"]   # dec_step.cu includes dec_kernels.cu, dec_matvec.cu
 
 MODE_BFP, MODE_RAW, MODE_PARTIAL = 0, 1, 2
 KIND_GOLDEN, KIND_G128 = 0, 1
@@ -197,6 +197,12 @@ DEC_EXPORTS = {
     "dec_layer_bytes": (C.c_int64, [C.c_void_p, C.c_int]),
     "dec_set_layer_events": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "dec_set_residual_seams": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "dec_set_persistent": (C.c_int, [C.c_void_p, C.c_int]),
+    "dec_persistent": (C.c_int, [C.c_void_p]),
+    "dec_set_clock": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "dec_set_wait_limit": (C.c_int, [C.c_void_p, C.c_int64]),
+    "dec_clock_slots": (C.c_int, [C.c_void_p]),
+    "dec_layer_clock": (C.c_int, [C.c_void_p, C.c_int]),
 }
 
 _declib = None

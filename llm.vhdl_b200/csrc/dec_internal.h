@@ -5,6 +5,7 @@
 #define DEC_INTERNAL_H
 
 #include <stdint.h>
+#include "../../include/gdn_b200.h"
 
 #define DMV_MAXJ 4
 
@@ -61,9 +62,87 @@ typedef struct {
     int32_t      pad_;
 } dmv_params;
 
+/* the gated-attention step (dec_kernels.cu): flash decoding over chunks of
+ * `ch` positions, then the combine with the sigmoid gate */
+typedef struct {
+    const float *qg, *kv;          /* raw projections: q|gate per head, k|v    */
+    const float *qn_w, *kn_w;      /* q / k RMSNorm weights [128]               */
+    int32_t      qh, kvh, n_rot;
+    float        theta, eps;
+    const int32_t *d_pos;          /* the position (device)                     */
+    int32_t      max_ctx, ch, nchunks;
+    uint16_t    *kcache, *vcache;  /* [nseq][max_ctx][kvh][128] fp16            */
+    float       *q_seam, *part;    /* optional q seam; chunk records            */
+    uint16_t    *y;                /* fp16 gated output [nseq][qh][128]         */
+    int32_t      nseq;
+} dec_attn_args;
+
+/* One stage of the persistent decode kernel's program (dec_step.cu): a piece
+ * of work every CTA takes its share of, then (sync != 0) a grid-wide barrier.
+ * The program of a step is the reference sequencer's per-token layer program
+ * in this form: embed, per layer the projection / delta-rule / attention
+ * stages, LM head, advance. */
+enum { MG_EMBED = 1, MG_MATVEC = 2, MG_GDN = 3, MG_ATTN = 4, MG_COMBINE = 5, MG_ADVANCE = 6, MG_COPY = 7 };
+
+typedef struct {
+    const uint16_t *emb; const int32_t *tok; float *x; int32_t hidden, nseq;
+} mg_embed_args;
+
+typedef struct {
+    unsigned long long *keys, *key; int32_t *tok, *hist, *pos; const int32_t *prompt;
+    int32_t n, nseq, max_ctx, pad_;
+} mg_advance_args;
+
+typedef struct {
+    float *dst; const float *src; int64_t n;
+} mg_copy_args;
+
+typedef struct {
+    int32_t op, sync;
+    int32_t pf;                    /* set on upload: the MATVEC stage whose
+                                      weights this stage prefetches, or -1 */
+    int32_t pad_;
+    union {
+        dmv_params      mv;
+        gdn_f32_args    gdn;
+        dec_attn_args   att;
+        mg_embed_args   emb;
+        mg_advance_args adv;
+        mg_copy_args    cp;
+        uint8_t         raw_[544];     /* the record is a whole number of
+                                          16-byte words (copied as such) */
+    } u;
+} mg_stage;
+typedef char mg_stage_size_check[(sizeof(mg_stage) % 16) == 0 && sizeof(dmv_params) <= 544 ? 1 : -1];
+
+/* the control block of the persistent kernel (device memory, zeroed) */
+typedef struct {
+    unsigned long long count;      /* grid-barrier arrivals, never reset        */
+    int32_t abort;                 /* a barrier timed out: every CTA leaves     */
+    int32_t err_stage;             /* the stage whose barrier timed out         */
+} mg_ctl;
+
+/* an uploaded program */
+typedef struct {
+    mg_stage *d_prog;
+    int32_t   n, nbar, grid, nv;
+    int64_t   smem;
+    mg_ctl   *ctl;
+    unsigned long long *clock;     /* optional [nbar + 1] globaltimer stamps */
+    int64_t   timeout_ns;
+    int32_t   pf_bytes, pad_;
+} mg_prog;
+
 #ifdef __cplusplus
 extern "C" {
 #endif
+/* Prepares and uploads a recorded program (host stages, n of them) for the
+ * persistent kernel of `nv` sequences on the current device: grid size,
+ * matvec tiling for that grid, prefetch plan, shared memory.  *P must hold a
+ * zeroed d_prog (first upload: allocated here) or a previous upload of the
+ * same length. */
+int dec_mega_upload(mg_stage *stages, int n, int nv, mg_prog *P);
+int dec_k_mega(const mg_prog *P, void *stream);
 /* Launches the decode matvec on `stream`; pdl != 0 launches it as a
  * programmatic dependent of the previous kernel in the stream. */
 int dec_k_matvec(const dmv_params *p, void *stream, int pdl);

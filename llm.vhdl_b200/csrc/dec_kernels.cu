@@ -11,12 +11,16 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <math.h>
+#include "dec_internal.h"
 
 extern "C" int mv4i_g_cuda_err;
 
 __device__ __forceinline__ float sigm_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+#ifndef DEC_PDL_HELPERS
+#define DEC_PDL_HELPERS
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#endif
 #define PDL_ENTER() do { pdl_trigger(); pdl_wait(); } while (0)
 
 // block-wide sum (blockDim.x a multiple of 32, <= 1024); every thread calls it
@@ -34,14 +38,23 @@ __device__ __forceinline__ float block_sum(float v, float *red)
     return v;
 }
 
+// x[b][i] = emb[tok[b]][i] for the flat indices i0, i0 + stride, ... of the
+// nseq x hidden residual
+__device__ __forceinline__ void dec_embed_range(const uint16_t *emb, int hidden, const int32_t *tok, float *x,
+                                                int nseq, int i0, int stride)
+{
+    for (int i = i0; i < nseq * hidden; i += stride) {
+        const int b = i / hidden, k = i - b * hidden;
+        x[i] = __half2float(__ushort_as_half(emb[(int64_t)tok[b] * hidden + k]));
+    }
+}
+
 __global__ void dec_embed_kernel(const uint16_t *emb, int hidden, const int32_t *tok, float *x)
 {
     PDL_ENTER();
     tok += blockIdx.y;                                   // sequence blockIdx.y of a batch
     x += (size_t)blockIdx.y * hidden;
-    const int64_t base = (int64_t)(*tok) * hidden;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x)
-        x[i] = __half2float(__ushort_as_half(emb[base + i]));
+    dec_embed_range(emb, hidden, tok, x, 1, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
 
 // One decode step of gated attention, flash-decoding part 1 with the
@@ -90,30 +103,32 @@ __device__ __forceinline__ void att_norm_rope(const float4 r, const float *w, fl
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const float *kv, const float *qn_w,
-                                                        const float *kn_w, int qh, int kvh, int n_rot, float theta,
-                                                        float eps, const int32_t *d_pos, int max_ctx, int ch,
-                                                        int nchunks, uint16_t *kcache, uint16_t *vcache,
-                                                        float *q_seam, float *part)
+// Piece (chunk c, kv head g, sequence b) of the attention step, by `nthr`
+// threads (tid < nthr; at least 32 * qh/kvh; warps past the GQA group only help
+// load the chunk).  Every thread reaches the same barriers.
+__device__ void dec_attn_cta(const dec_attn_args &A, int c, int g, int b, int tid, int nthr, uint8_t *att_sm)
 {
-    extern __shared__ __align__(16) uint8_t att_sm[];
-    PDL_ENTER();
+    const int qh = A.qh, kvh = A.kvh, max_ctx = A.max_ctx, ch = A.ch, nchunks = A.nchunks, n_rot = A.n_rot;
+    const float theta = A.theta, eps = A.eps;
+    const float *qg = A.qg, *kv = A.kv;
+    uint16_t *kcache = A.kcache, *vcache = A.vcache;
+    float *q_seam = A.q_seam, *part = A.part;
     const int grp = qh / kvh;
-    const int c = blockIdx.x, g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = g * grp + warp;
-    if (blockIdx.z) {                                    // sequence blockIdx.z of a batch
-        const size_t b = blockIdx.z;
-        qg += b * 2 * qh * ATT_HD;
-        kv += b * 2 * kvh * ATT_HD;
-        kcache += b * max_ctx * kvh * ATT_HD;
-        vcache += b * max_ctx * kvh * ATT_HD;
-        if (q_seam) q_seam += b * qh * ATT_HD;
-        part += b * qh * nchunks * (ATT_HD + 4);
+    const int warp = tid >> 5, lane = tid & 31;
+    const bool qw_on = warp < grp;
+    const int h = g * grp + (qw_on ? warp : 0);
+    if (b) {
+        qg += (size_t)b * 2 * qh * ATT_HD;
+        kv += (size_t)b * 2 * kvh * ATT_HD;
+        kcache += (size_t)b * max_ctx * kvh * ATT_HD;
+        vcache += (size_t)b * max_ctx * kvh * ATT_HD;
+        if (q_seam) q_seam += (size_t)b * qh * ATT_HD;
+        part += (size_t)b * qh * nchunks * (ATT_HD + 4);
     }
-    const int pos = *d_pos, len = min(pos + 1, max_ctx), p0 = c * ch;
+    const int pos = *A.d_pos, len = min(pos + 1, max_ctx), p0 = c * ch;
     float *pp = part + ((size_t)h * nchunks + c) * (ATT_HD + 4);
     if (p0 >= len) {                                   // the whole CTA leaves: no barrier below
-        if (lane == 0) { pp[0] = -INFINITY; pp[1] = 0.f; }
+        if (qw_on && lane == 0) { pp[0] = -INFINITY; pp[1] = 0.f; }
         return;
     }
     const int n = min(ch, len - p0);
@@ -124,10 +139,10 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
     float *kb = reinterpret_cast<float *>(vs + ch * ATT_HD);        // [128] scratch for the new k
 
     // q of head h
-    {
+    if (qw_on) {
         float q[4];
         const float4 r = reinterpret_cast<const float4 *>(qg + (size_t)h * 2 * ATT_HD)[lane];
-        att_norm_rope(r, qn_w, eps, n_rot, theta, pos, qs + warp * ATT_HD, lane, q);
+        att_norm_rope(r, A.qn_w, eps, n_rot, theta, pos, qs + warp * ATT_HD, lane, q);
 #pragma unroll
         for (int i = 0; i < 4; i++) qs[warp * ATT_HD + 4 * lane + i] = q[i];
         if (c == 0 && q_seam)
@@ -135,7 +150,7 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
     }
     // the chunk's cached k and v rows (16-byte pieces; the current position's
     // row is replaced below)
-    for (int i = threadIdx.x; i < n * 32; i += blockDim.x) {
+    for (int i = tid; i < n * 32; i += nthr) {
         const int r = i >> 5, piece = i & 15;
         const size_t off = ((size_t)(p0 + r) * kvh + g) * ATT_HD + 8 * piece;
         if (i & 16) *reinterpret_cast<uint4 *>(vs + r * ATT_HD + 8 * piece) = *reinterpret_cast<const uint4 *>(vcache + off);
@@ -146,7 +161,7 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
     if (warp == 0 && pos >= p0 && pos < p0 + n) {
         float k[4];
         const float4 r = reinterpret_cast<const float4 *>(kv + (size_t)g * ATT_HD)[lane];
-        att_norm_rope(r, kn_w, eps, n_rot, theta, pos, kb, lane, k);
+        att_norm_rope(r, A.kn_w, eps, n_rot, theta, pos, kb, lane, k);
         const float4 vr = reinterpret_cast<const float4 *>(kv + (size_t)(kvh + g) * ATT_HD)[lane];
         const __half2 k01 = __floats2half2_rn(k[0], k[1]), k23 = __floats2half2_rn(k[2], k[3]);
         const __half2 v01 = __floats2half2_rn(vr.x, vr.y), v23 = __floats2half2_rn(vr.z, vr.w);
@@ -161,6 +176,7 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
         *reinterpret_cast<uint2 *>(vcache + off) = vw;
     }
     __syncthreads();
+    if (!qw_on) return;                                // no barrier below
     // scores: lanes over positions, q broadcast from shared memory
     const float scale = rsqrtf((float)ATT_HD);
     const float *qw = qs + warp * ATT_HD;
@@ -210,25 +226,30 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const float *qg, const f
     reinterpret_cast<float4 *>(pp + 4)[lane] = make_float4(a0, a1, a2, a3);
 }
 
+__global__ void __launch_bounds__(1024) dec_attn_kernel(const dec_attn_args A)
+{
+    extern __shared__ __align__(16) uint8_t att_sm[];
+    PDL_ENTER();
+    dec_attn_cta(A, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, blockDim.x, att_sm);
+}
+
 // Flash-decoding, part 2: combine the chunks of each q head, apply the
 // sigmoid output gate (the raw projection, ref/run9b.c:871-872), to fp16.
 // One CTA of 128 threads per q head: chunk weights exp(m_c - M) in shared
 // memory, then thread d sums dimension d over the chunks.
-__global__ void __launch_bounds__(128) dec_attn_combine_kernel(const float *part, const float *gate, int gate_stride,
-                                                               int hd, int nchunks, const int32_t *d_pos, int ch,
-                                                               uint16_t *y)
+// Piece (q head h, sequence b) of the combine by 128 threads (t < 128), with
+// its own wc[1024] / red[32] scratch; every thread reaches the same barriers.
+__device__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc, float *red)
 {
-    __shared__ float wc[1024];
-    __shared__ float red[32];
-    PDL_ENTER();
-    const int h = blockIdx.x, t = threadIdx.x;
-    if (blockIdx.y) {                                    // sequence blockIdx.y of a batch
-        const size_t b = blockIdx.y, qh = gridDim.x;
-        part += b * qh * nchunks * (hd + 4);
-        gate += b * qh * gate_stride;
-        y += b * qh * hd;
+    const int hd = ATT_HD, nchunks = A.nchunks, ch = A.ch, qh = A.qh, gate_stride = 2 * ATT_HD;
+    const float *part = A.part, *gate = A.qg + ATT_HD;           // the gate: second half of each q|gate row
+    uint16_t *y = A.y;
+    if (b) {
+        part += (size_t)b * qh * nchunks * (hd + 4);
+        gate += (size_t)b * qh * gate_stride;
+        y += (size_t)b * qh * hd;
     }
-    const int used = min(nchunks, (*d_pos + 1 + ch - 1) / ch);
+    const int used = min(nchunks, (*A.d_pos + 1 + ch - 1) / ch);
     const float *ph = part + (size_t)h * nchunks * (hd + 4);
     float M = -INFINITY;
     for (int c = t; c < used; c += 128) M = fmaxf(M, ph[(size_t)c * (hd + 4)]);
@@ -256,6 +277,14 @@ __global__ void __launch_bounds__(128) dec_attn_combine_kernel(const float *part
     y[(size_t)h * hd + t] = __half_as_ushort(__float2half_rn(a / L * sigm_f(gv)));
 }
 
+__global__ void __launch_bounds__(128) dec_attn_combine_kernel(const dec_attn_args A)
+{
+    __shared__ float wc[1024];
+    __shared__ float red[32];
+    PDL_ENTER();
+    dec_attn_combine_cta(A, blockIdx.x, blockIdx.y, threadIdx.x, wc, red);
+}
+
 __global__ void dec_add_kernel(float *x, const float *t, int n)
 {
     PDL_ENTER();
@@ -268,21 +297,30 @@ __global__ void dec_add_kernel(float *x, const float *t, int n)
 // token is the prompt's while the prompt lasts (prompt[0] holds its length
 // len, prompt[1 + b * len + i] sequence b's tokens), else the prediction.
 // Then the shared position advances.
+// by threads b < nseq of one CTA (all of its threads reach the barrier)
+__device__ __forceinline__ void dec_advance_cta(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok,
+                                                int32_t *history, int32_t *pos, int max_ctx, const int32_t *prompt,
+                                                int b, int nseq)
+{
+    const int p = *pos;
+    if (b < nseq) {
+        unsigned long long best = 0;
+        for (int i = 0; i < n; i++) best = keys[i * nseq + b] > best ? keys[i * nseq + b] : best;
+        const int32_t t = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
+        if (p < max_ctx) history[(size_t)b * max_ctx + p] = t;
+        const int plen = prompt ? prompt[0] : 0;
+        tok[b] = (p + 1 < plen) ? prompt[1 + (size_t)b * plen + p + 1] : t;
+        key[b] = 0;
+    }
+    __syncthreads();
+    if (b == 0) *pos = p + 1;
+}
+
 __global__ void dec_advance_kernel(unsigned long long *keys, int n, unsigned long long *key, int32_t *tok,
                                    int32_t *history, int32_t *pos, int max_ctx, const int32_t *prompt)
 {
     PDL_ENTER();
-    const int b = threadIdx.x, nseq = blockDim.x;
-    unsigned long long best = 0;
-    for (int i = 0; i < n; i++) best = keys[i * nseq + b] > best ? keys[i * nseq + b] : best;
-    const int32_t t = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
-    const int p = *pos;
-    if (p < max_ctx) history[(size_t)b * max_ctx + p] = t;
-    const int plen = prompt ? prompt[0] : 0;
-    tok[b] = (p + 1 < plen) ? prompt[1 + (size_t)b * plen + p + 1] : t;
-    key[b] = 0;
-    __syncthreads();
-    if (b == 0) *pos = p + 1;
+    dec_advance_cta(keys, n, key, tok, history, pos, max_ctx, prompt, threadIdx.x, blockDim.x);
 }
 
 // --------------------------------------------------- synthetic weights
@@ -367,25 +405,34 @@ size_t dec_attention_smem(int qh, int kvh, int ch)
     return (size_t)(grp * ATT_HD + grp * ch) * 4 + (size_t)ch * ATT_KS * 2 + (size_t)ch * ATT_HD * 2 + ATT_HD * 4;
 }
 
+int dec_attn_prepare(dec_attn_args *A)
+{
+    if (A->kvh <= 0 || A->qh % A->kvh || A->qh / A->kvh > 32 || A->ch <= 0 || A->ch > 64 || (A->n_rot & 1)
+        || A->n_rot > ATT_HD || A->nseq < 1 || A->nseq > 64) return -11;
+    A->nchunks = (A->max_ctx + A->ch - 1) / A->ch;
+    if (A->nchunks > 1024) return -11;                // the combine's weight table
+    return 0;
+}
+
 int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const float *kn_w, int qh, int kvh,
                     int n_rot, float theta, float eps, const int32_t *d_pos, int max_ctx, int ch, float *part,
                     float *q_seam, uint16_t *kcache, uint16_t *vcache, uint16_t *y, int nseq, void *s, int pdl)
 {
-    if (kvh <= 0 || qh % kvh || qh / kvh > 32 || ch <= 0 || ch > 64 || (n_rot & 1) || n_rot > ATT_HD
-        || nseq < 1 || nseq > 64) return -11;
-    const int nchunks = (max_ctx + ch - 1) / ch;
-    if (nchunks > 1024) return -11;                   // the combine's weight table
+    dec_attn_args A = {qg, kv, qn_w, kn_w, qh, kvh, n_rot, theta, eps, d_pos, max_ctx, ch, 0, kcache, vcache,
+                       q_seam, part, y, nseq};
+    int rc = dec_attn_prepare(&A);
+    if (rc) return rc;
     const size_t smem = dec_attention_smem(qh, kvh, ch);
     static int attr_set[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -11;
     if (!attr_set[dev]) {
-        const int rc = dk(cudaFuncSetAttribute(dec_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        rc = dk(cudaFuncSetAttribute(dec_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
         if (rc) return rc;
         attr_set[dev] = 1;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nchunks, kvh, nseq);
+    cfg.gridDim = dim3(A.nchunks, kvh, nseq);
     cfg.blockDim = dim3(32 * (qh / kvh));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = reinterpret_cast<cudaStream_t>(s);
@@ -394,12 +441,9 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    const int rc = dk(cudaLaunchKernelEx(&cfg, dec_attn_kernel, qg, kv, qn_w, kn_w, qh, kvh, n_rot, theta, eps,
-                                         d_pos, max_ctx, ch, nchunks, kcache, vcache, q_seam, part));
+    rc = dk(cudaLaunchKernelEx(&cfg, dec_attn_kernel, A));
     if (rc) return rc;
-    // the gate is the raw projection: second half of each head's q|gate row
-    return launch(dec_attn_combine_kernel, dim3(qh, nseq), dim3(ATT_HD), s, pdl, part, qg + ATT_HD, 2 * ATT_HD, ATT_HD,
-                  nchunks, d_pos, ch, y);
+    return launch(dec_attn_combine_kernel, dim3(qh, nseq), dim3(ATT_HD), s, pdl, A);
 }
 
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl)

@@ -34,8 +34,11 @@ extern "C" int mv4i_g_cuda_err;
 #define DMV_MINB 2                 // resident CTAs per SM the registers are sized for
 #endif
 
+#ifndef DEC_PDL_HELPERS
+#define DEC_PDL_HELPERS
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#endif
 
 __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
 {
@@ -73,20 +76,6 @@ __device__ __forceinline__ int dp_us(uint32_t a, uint32_t b, int c)
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
-__device__ __forceinline__ float block_sum(float v, float *red)
-{
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    __syncthreads();
-    if (l == 0) red[w] = v;
-    __syncthreads();
-    v = l < DMV_WARPS ? red[l] : 0.f;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 // sat16(rint(f * 2^e)), round half to even; scale = 2^e exactly.  |f * 2^e| <
 // 2^15 by the choice of e, so only +32768 (from rounding) needs the clamp.
 __device__ __forceinline__ int to_i16(float f, float scale)
@@ -103,26 +92,28 @@ __device__ __forceinline__ float exp2i(int n) { return __int_as_float((127 + n) 
 //           columns; word q of a block holds columns 8q + {0,2,4,6} (+1)
 //   psum    int   [np]  sum of the staged int16 x over the pair
 //   gfac    float [ng]  2^-e of each group
+//   gs      int2  [ng]  {sum of the staged int16 x over the group, 2^-e bits}
 struct Sm {
-    uint4 *planes; int *psum; float *gfac;
+    uint4 *planes; int *psum; float *gfac; int2 *gs;
 };
 
 __host__ __device__ __forceinline__ size_t r16(size_t n) { return (n + 15) & ~(size_t)15; }
 
 __device__ __forceinline__ Sm sm_layout(uint8_t *sm, int K)
 {
-    const size_t np = K >> 6;
+    const size_t np = K >> 6, ng = K >> 7;
     Sm s;
     s.planes = reinterpret_cast<uint4 *>(sm);
     s.psum = reinterpret_cast<int *>(sm + 128 * np);
     s.gfac = reinterpret_cast<float *>(sm + 128 * np + r16(4 * np));
+    s.gs = reinterpret_cast<int2 *>(sm + 128 * np + r16(4 * np) + r16(4 * ng));
     return s;
 }
 
 __host__ __device__ __forceinline__ size_t dmv_smem_x_bytes(int K)
 {
     const size_t np = K >> 6, ng = K >> 7;
-    return 128 * np + r16(4 * np) + r16(4 * ng);
+    return 128 * np + r16(4 * np) + r16(4 * ng) + r16(8 * ng);
 }
 
 // the 8 fp32 inputs of unit u (columns 8u .. 8u+7): x (fp16 / fp32
@@ -161,7 +152,7 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, const void *xv, c
 // sequences of a batch; those past P.nvec are not staged and their results
 // are dropped), vector b into the shared-memory block at sm + b * xb.
 template <int NV>
-__device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb)
+__device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb, bool seam_cta)
 {
     __shared__ float red[DMV_WARPS * 8];
     __shared__ float invs[8];
@@ -251,6 +242,7 @@ __device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb)
             for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
 #pragma unroll
             for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+            const int gsum = ssum + __shfl_xor_sync(0xffffffffu, ssum, 8);
             if (ok) {
                 uint32_t le = 0, lo = 0, he = 0, ho = 0;
 #pragma unroll
@@ -266,8 +258,11 @@ __device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb)
                 pw[4 * ((4 + par) * np + p) + q] = he;
                 pw[4 * ((6 + par) * np + p) + q] = ho;
                 if (!(u & 7)) s.psum[u >> 3] = ssum;
-                if (!(u & 15)) s.gfac[u >> 4] = exp2i(-e);
-                if (blockIdx.x == 0 && seam)
+                if (!(u & 15)) {
+                    s.gfac[u >> 4] = exp2i(-e);
+                    s.gs[u >> 4] = make_int2(gsum, __float_as_int(exp2i(-e)));
+                }
+                if (seam_cta && seam)
                     *reinterpret_cast<uint4 *>(seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             }
         }
@@ -514,246 +509,300 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
     }
 }
 
-// Several vectors (NV = 2, 4, 8): the same walk over rows and pairs, each
-// weight load and its decode shared by the NV dot products.  Per pair, the
-// x planes of one vector at a time are read from shared memory (reused by
-// the 4 row slots), so the live registers are the 4 rows' weights, 4 x NV
-// fp32 accumulators and one vector's planes.
-template <int V>
-__device__ __forceinline__ float tbfly(float (&v)[V], int lane)
+// ------------------------------------------------------- the stream on mma
+//
+// The same integer group dot products on the tensor pipe: mma.sync
+// m16n8k32 with A = 16 weight rows x 32 columns as unsigned nibble codes
+// (idx ^ 8, so cb = u - 8) and B = 32 columns x 8 input vectors as the low
+// (unsigned) and high (signed) bytes of the staged int16 x.  A warp owns a
+// tile of 16 rows (or 8 gate/up row pairs: gate in A rows 0-7, up in 8-15)
+// and walks its column slice one 128-column group at a time:
+//   lane (g, t) = (lane / 4, lane % 4) loads the 16 bytes 16t .. 16t+15 of
+//   rows g and g+8 in the group (one 128-bit load each); k-step s (0..3)
+//   takes word s of them, i.e. columns 32t + 8s + {0..7}: low nibbles are
+//   the fragment's k = 4t + i, high nibbles k = 16 + 4t + i.  The B fragment
+//   of the same columns is word s of the x planes of block 4G + t (even
+//   columns -> b0, odd -> b1), vector g.
+// Per group: lo = -8 * sum(x) + sum(u * xlo), hi = sum(u * xhi) (exact
+// int32), then acc += (lo + 256 hi) * scale * 2^-e in fp32, the contract of
+// the CUDA-core path.  Lane (g, t) ends with rows g, g+8 of vectors 2t, 2t+1
+// (accumulator fragment c0..c3); no lane reduction is needed.
+
+__device__ __forceinline__ void mma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {
-    // transposing butterfly: V values per lane in, lane L ends with the warp
-    // total of value L >> (5 - log2 V) (V - 1 shuffles, then plain ones)
-    constexpr int LV = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : 1;
-#pragma unroll
-    for (int st = 0; st < LV; st++) {
-        const int o = 16 >> st, n = V >> (st + 1);
-        const bool up = lane & o;
-#pragma unroll
-        for (int i = 0; i < n; i++) {
-            const float keep = up ? v[i + n] : v[i], send = up ? v[i] : v[i + n];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-    }
-    float r = v[0];
-#pragma unroll
-    for (int o = 16 >> LV; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-    return r;
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int NV, bool PAIRED>
-__device__ __forceinline__ void dmv_segment_b(const dmv_params &P, const dmv_job &J, uint8_t *sm, size_t xb,
-                                              float *red, int ta, int tb, int warp, int lane, int np,
-                                              size_t wpitch, unsigned long long &best)
+// 16 bytes of streamed weights (read once: no L1 allocation)
+__device__ __forceinline__ uint4 ld_w16(const uint8_t *p)
 {
-    constexpr int G = PAIRED ? DMV_G / 2 : DMV_G;
-    constexpr int NR = DMV_G;
-    constexpr int V = NR * NV;
-    constexpr int SH = V >= 32 ? 0 : V >= 16 ? 1 : 2;      // lane L holds value L >> SH
+    uint4 w;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w) : "l"(p));
+    return w;
+}
+
+// 4 consecutive fp16 scales (8-byte aligned)
+__device__ __forceinline__ uint2 ld_sc4(const uint16_t *p)
+{
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float h2f_sel(const uint2 &v, int u)
+{
+    const uint32_t w = (u >> 1) ? v.y : v.x;
+    return __half2float(__ushort_as_half((unsigned short)((u & 1) ? (w >> 16) : (w & 0xFFFF))));
+}
+
+__device__ __forceinline__ uint32_t u4w(const uint4 &v, int s)
+{
+    return s == 0 ? v.x : s == 1 ? v.y : s == 2 ? v.z : v.w;
+}
+
+#define DMV_U 4                    // groups per batch of loads
+
+template <int NV, bool PAIRED>
+__device__ __forceinline__ void dmv_segment_mma(const dmv_params &P, const dmv_job &J, uint8_t *sm, size_t xb,
+                                                float *red4, int ta, int tb, int warp, int lane, int ng,
+                                                size_t wpitch, unsigned long long (&best)[2])
+{
+    constexpr int TR = PAIRED ? 8 : 16;          // rows (pairs) per warp tile
     const int ks = P.ksplit, rt = DMV_WARPS / ks, rs = warp / ks, kq = warp % ks;
-    const int npk = np / ks, p0 = kq * npk, p1 = p0 + npk;
-    const int K = P.K;
-    for (int t = ta; t < tb; t += G) {
-        const int g = min(G, tb - t);
-        const uint8_t *wr[NR];
-        const uint16_t *sr[NR];
+    const int ngk = ng / ks, G0 = kq * ngk, G1 = G0 + ngk;
+    const int g = lane >> 2, t = lane & 3, np = P.K >> 6, nv = P.nvec;
+    // B fragments: vector g (vectors past the batch read vector 0; their
+    // columns are dropped); accumulator columns: vectors 2t, 2t+1
+    const Sm sb = sm_layout(sm + (size_t)(NV == 1 ? 0 : min(g, nv - 1)) * xb, P.K);
+    const int va = NV == 1 ? 0 : min(2 * t, nv - 1), vb = NV == 1 ? 0 : min(2 * t + 1, nv - 1);
+    const int2 *gsa = sm_layout(sm + (size_t)va * xb, P.K).gs;
+    const int2 *gsb = sm_layout(sm + (size_t)vb * xb, P.K).gs;
+    const int par = t & 1, pq = t >> 1;
+    for (int r0 = ta; r0 < tb; r0 += rt) {       // every warp the same rounds
+        const int tile = r0 + rs;
+        const bool on = tile < tb;
+        const int base = (min(tile, tb - 1) - J.tile0) * TR;
+        const int ra = min(base + g, J.rows - 1);                  // past the end: valid rows, discarded
+        const int rb = PAIRED ? ra : min(base + g + 8, J.rows - 1);
+        const uint8_t *pa = J.wq + (size_t)ra * wpitch + 16 * t;
+        const uint8_t *pb = (PAIRED ? J.wq2 : J.wq) + (size_t)rb * wpitch + 16 * t;
+        const uint16_t *qa = J.sc + (size_t)ra * J.s_pitch;
+        const uint16_t *qb = (PAIRED ? J.sc2 : J.sc) + (size_t)rb * J.s_pitch;
+        float f[4] = {0.f, 0.f, 0.f, 0.f};
+        if (on) {
+            // batches of 4 aligned groups: one 8-byte load brings a row's 4
+            // scales (rows are 16-byte aligned, s_pitch >= ceil8(K/128))
+            for (int Gb = G0 & ~(DMV_U - 1); Gb < G1; Gb += DMV_U) {
+                uint4 wa[DMV_U], wb[DMV_U];
+                const uint2 qa4 = ld_sc4(qa + Gb), qb4 = ld_sc4(qb + Gb);
 #pragma unroll
-        for (int i = 0; i < G; i++) {
-            const int row = (t + min(i, g - 1) - J.tile0) * rt + rs;
-            const int rr = min(row, J.rows - 1);               // past the end: a valid row, discarded
-            if (PAIRED) {
-                wr[2 * i] = J.wq + (size_t)rr * wpitch;  sr[2 * i] = J.sc + (size_t)rr * J.s_pitch;
-                wr[2 * i + 1] = J.wq2 + (size_t)rr * wpitch; sr[2 * i + 1] = J.sc2 + (size_t)rr * J.s_pitch;
-            } else {
-                wr[i] = J.wq + (size_t)rr * wpitch; sr[i] = J.sc + (size_t)rr * J.s_pitch;
+                for (int u = 0; u < DMV_U; u++) {
+                    if (Gb + u >= G0 && Gb + u < G1) {
+                        wa[u] = ld_w16(pa + 64 * (size_t)(Gb + u));
+                        wb[u] = ld_w16(pb + 64 * (size_t)(Gb + u));
+                    } else {
+                        wa[u] = wb[u] = make_uint4(0, 0, 0, 0);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < DMV_U; u++) {
+                    if (Gb + u < G0) continue;
+                    if (Gb + u >= G1) break;
+                    const int G = Gb + u, p = 2 * G + pq;
+                    const float sau = h2f_sel(qa4, u), sbu = h2f_sel(qb4, u);
+                    const uint4 xle = sb.planes[(0 + par) * np + p], xlo = sb.planes[(2 + par) * np + p];
+                    const uint4 xhe = sb.planes[(4 + par) * np + p], xho = sb.planes[(6 + par) * np + p];
+                    const int2 ga = gsa[G], gb = gsb[G];
+                    int lo[4] = {-8 * ga.x, -8 * gb.x, -8 * ga.x, -8 * gb.x};
+                    int hi[4] = {0, 0, 0, 0};
+#pragma unroll
+                    for (int s = 0; s < 4; s++) {
+                        const uint32_t A = u4w(wa[u], s), B = u4w(wb[u], s);
+                        const uint32_t a[4] = {(A & 0x0F0F0F0Fu) ^ 0x08080808u, (B & 0x0F0F0F0Fu) ^ 0x08080808u,
+                                               ((A >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u,
+                                               ((B >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u};
+                        mma_u8u8(lo, a, u4w(xle, s), u4w(xlo, s));
+                        mma_u8s8(hi, a, u4w(xhe, s), u4w(xho, s));
+                    }
+                    const float fa = __int_as_float(ga.y), fb = __int_as_float(gb.y);
+                    f[0] = fmaf((float)(lo[0] + 256 * hi[0]), sau * fa, f[0]);
+                    f[1] = fmaf((float)(lo[1] + 256 * hi[1]), sau * fb, f[1]);
+                    f[2] = fmaf((float)(lo[2] + 256 * hi[2]), sbu * fa, f[2]);
+                    f[3] = fmaf((float)(lo[3] + 256 * hi[3]), sbu * fb, f[3]);
+                }
             }
         }
-        float acc[V];
+        if (ks > 1) {
 #pragma unroll
-        for (int k = 0; k < V; k++) acc[k] = 0.f;
-        for (int pb = p0; pb < p1; pb += 32) {
-            const int p = pb + lane;
-            uint32_t w[NR][8];
-            float sc[NR];
-            dmv_loads<NR>(wr, sr, p, p < p1, w, sc);
-            if (p < p1) {
-                // the weights as idx^8 nibbles (even columns) and 16*(idx^8) (odd)
-                uint32_t we[NR][8], wo[NR][8];
+            for (int i = 0; i < 4; i++) red4[(warp * 4 + i) * 32 + lane] = f[i];
+            __syncthreads();
+            if (kq == 0) {
 #pragma unroll
-                for (int k = 0; k < NR; k++)
+                for (int i = 0; i < 4; i++) {
+                    float a = 0.f;
+                    for (int q = 0; q < ks; q++) a += red4[((warp + q) * 4 + i) * 32 + lane];
+                    f[i] = a;
+                }
+            }
+            __syncthreads();
+        }
+        if (kq == 0 && on) {
+            if (PAIRED) {
+                if (base + g < J.rows) {
+                    if (2 * t < nv) dmv_epilogue(P, J, 2 * t, base + g, f[0], f[2], best[0]);
+                    if (2 * t + 1 < nv) dmv_epilogue(P, J, 2 * t + 1, base + g, f[1], f[3], best[1]);
+                }
+            } else {
 #pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        we[k][q] = (w[k][q] & 0x0F0F0F0Fu) ^ 0x08080808u;
-                        wo[k][q] = (w[k][q] & 0xF0F0F0F0u) ^ 0x80808080u;
-                    }
-#pragma unroll
-                for (int b = 0; b < NV; b++) {
-                    const Sm s = sm_layout(sm + b * xb, K);
-                    int a[NR][4];
-#pragma unroll
-                    for (int k = 0; k < NR; k++) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0;
-#pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        const uint4 xle = s.planes[(0 + half) * np + p], xlo = s.planes[(2 + half) * np + p];
-                        const uint4 xhe = s.planes[(4 + half) * np + p], xho = s.planes[(6 + half) * np + p];
-                        const uint32_t le[4] = {xle.x, xle.y, xle.z, xle.w}, lo[4] = {xlo.x, xlo.y, xlo.z, xlo.w};
-                        const uint32_t he[4] = {xhe.x, xhe.y, xhe.z, xhe.w}, ho[4] = {xho.x, xho.y, xho.z, xho.w};
-#pragma unroll
-                        for (int k = 0; k < NR; k++)
-#pragma unroll
-                            for (int q = 0; q < 4; q++) {
-                                a[k][0] = dp_uu(we[k][4 * half + q], le[q], a[k][0]);
-                                a[k][1] = dp_uu(wo[k][4 * half + q], lo[q], a[k][1]);
-                                a[k][2] = dp_us(we[k][4 * half + q], he[q], a[k][2]);
-                                a[k][3] = dp_us(wo[k][4 * half + q], ho[q], a[k][3]);
-                            }
-                    }
-                    const int sx = s.psum[p];
-                    const float gf = s.gfac[p >> 1];
-#pragma unroll
-                    for (int k = 0; k < NR; k++) {
-                        const int part = a[k][0] + (a[k][1] >> 4) + (a[k][2] + (a[k][3] >> 4)) * 256 - 8 * sx;
-                        acc[k * NV + b] = fmaf((float)part, sc[k] * gf, acc[k * NV + b]);
+                for (int h = 0; h < 2; h++) {
+                    const int row = base + g + 8 * h;
+                    if (row < J.rows) {
+                        if (2 * t < nv) dmv_epilogue(P, J, 2 * t, row, f[2 * h], 0.f, best[0]);
+                        if (2 * t + 1 < nv) dmv_epilogue(P, J, 2 * t + 1, row, f[2 * h + 1], 0.f, best[1]);
                     }
                 }
             }
         }
-        float v0 = tbfly<V>(acc, lane);
-        const int vi = lane >> SH, k = vi / NV, b = vi % NV;
-        // the up row of a gate/up pair sits NV values (NV << SH lanes) higher
-        float v1 = PAIRED ? __shfl_down_sync(0xffffffffu, v0, NV << SH) : 0.f;
-        const bool holder = (lane & ((1 << SH) - 1)) == 0 && (!PAIRED || !(k & 1));
-        if (ks > 1) {
-            red[warp * 64 + lane] = v0;
-            red[warp * 64 + 32 + lane] = v1;
-            __syncthreads();
-            if (kq == 0) {
-                float a = 0.f, c = 0.f;
-                for (int q = 0; q < ks; q++) { a += red[(warp + q) * 64 + lane]; c += red[(warp + q) * 64 + 32 + lane]; }
-                v0 = a; v1 = c;
-            }
-            __syncthreads();
-        }
-        const int i = PAIRED ? k >> 1 : k;
-        if (kq == 0 && holder && i < g && b < P.nvec) {
-            const int row = (t + i - J.tile0) * rt + rs;
-            if (row < J.rows) dmv_epilogue(P, J, b, row, v0, v1, best);
-        }
     }
 }
 
-template <int NV>
-__global__ void __launch_bounds__(DMV_THREADS, NV == 1 ? DMV_MINB : 1) dmv_kernel(const __grid_constant__ dmv_params P)
+// L2 prefetch of up to `budget` weight bytes of tiles [t0, t1) (the CTA's
+// range of a launch), by one thread; `mma` selects the tile height
+__device__ __forceinline__ void dmv_prefetch(const dmv_params &P, const dmv_job *JS, int t0, int t1, int64_t budget,
+                                             bool mma)
 {
-    extern __shared__ __align__(128) uint8_t dmv_sm[];
+    const size_t wpitch = (size_t)P.K >> 1;
+    for (int t = t0; t < t1 && budget > 0;) {
+        const dmv_job &J = JS[dmv_job_of(P, JS, t)];
+        const int te = min(t1, J.tile0 + J.ntiles);
+        const int TR = mma ? (J.wq2 ? 8 : 16) : DMV_WARPS / P.ksplit;
+        const int r0 = (t - J.tile0) * TR;
+        const int r1 = min(J.rows, (te - J.tile0) * TR);
+        int64_t bytes = (int64_t)(r1 - r0) * (int64_t)wpitch;
+        if (bytes > budget) bytes = budget & ~(int64_t)15;
+        for (int m = 0; m < (J.wq2 ? 2 : 1); m++) {
+            const uint8_t *base = (m ? J.wq2 : J.wq) + (size_t)r0 * wpitch;
+            for (int64_t off = 0; off < bytes; off += 65536)
+                prefetch_l2(base + off, (uint32_t)min((int64_t)65536, bytes - off));
+        }
+        budget -= bytes * (J.wq2 ? 2 : 1);
+        t = te;
+    }
+}
+
+// One CTA's share (CTA bid of nb) of a matvec launch.  NV = 1 streams on the
+// CUDA cores (dp4a), NV = 2..8 on the tensor pipe (mma.sync, the same integer
+// contract): one vector is cheapest as dp4a, several share each mma.
+// Standalone launches (pdl) prefetch their own first weights and synchronise
+// with the previous kernel; the persistent decode kernel prefetches for the
+// next stage itself.  Every thread of the CTA calls it (barriers inside).
+template <int NV>
+__device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, int bid, int nb, bool standalone)
+{
+    constexpr bool MMA = NV > 1;
     __shared__ dmv_job JS[DMV_MAXJ];
-    __shared__ float red[DMV_WARPS * 4 * 2 * DMV_WARPS];
+    __shared__ float red[DMV_WARPS * 4 * 32];
     if (threadIdx.x < P.njobs) JS[threadIdx.x] = P.jobs[threadIdx.x];
     __syncthreads();
     const int T = P.total_tiles;
-    const int t0 = (int)((int64_t)blockIdx.x * T / gridDim.x);
-    const int t1 = (int)((int64_t)(blockIdx.x + 1) * T / gridDim.x);
-    const int K = P.K, np = K >> 6;
+    const int t0 = (int)((int64_t)bid * T / nb);
+    const int t1 = (int)((int64_t)(bid + 1) * T / nb);
+    const int K = P.K, np = K >> 6, ng = K >> 7;
     const size_t wpitch = (size_t)K >> 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int j0 = dmv_job_of(P, JS, min(t0, T - 1));
-    // weights do not depend on the previous kernel: ask L2 for the first
-    // ones now
-    if (threadIdx.x == 0 && P.pf_bytes > 0) {
-        int64_t budget = P.pf_bytes;
-        for (int t = t0; t < t1 && budget > 0;) {
-            const dmv_job &J = JS[dmv_job_of(P, JS, t)];
-            const int te = min(t1, J.tile0 + J.ntiles);
-            const int r0 = (t - J.tile0) * (DMV_WARPS / P.ksplit);
-            const int r1 = min(J.rows, (te - J.tile0) * (DMV_WARPS / P.ksplit));
-            int64_t bytes = (int64_t)(r1 - r0) * (int64_t)wpitch;
-            if (bytes > budget) bytes = budget & ~(int64_t)15;
-            for (int m = 0; m < (J.wq2 ? 2 : 1); m++) {
-                const uint8_t *base = (m ? J.wq2 : J.wq) + (size_t)r0 * wpitch;
-                for (int64_t off = 0; off < bytes; off += 65536)
-                    prefetch_l2(base + off, (uint32_t)min((int64_t)65536, bytes - off));
-            }
-            budget -= bytes * (J.wq2 ? 2 : 1);
-            t = te;
-        }
+    if (standalone) {
+        // weights do not depend on the previous kernel: ask L2 for the first
+        // ones now
+        if (threadIdx.x == 0 && P.pf_bytes > 0) dmv_prefetch(P, JS, t0, t1, P.pf_bytes, MMA);
+        pdl_trigger();
+        pdl_wait();
     }
-    pdl_trigger();
-    pdl_wait();
+    if (t0 >= t1) return;                               // uniform over the CTA
 
     const size_t xb = dmv_smem_x_bytes(K);
-    dmv_stage<NV>(P, dmv_sm, xb);
+    dmv_stage<NV>(P, dmv_sm, xb, t0 == 0);               // the first CTA with tiles writes the seam
 
-    unsigned long long best = 0;
-    for (int j = j0; j < P.njobs && t0 < t1; j++) {
+    unsigned long long best[2] = {0, 0};
+    for (int j = j0; j < P.njobs; j++) {
         const dmv_job &J = JS[j];
         const int ta = max(t0, J.tile0), tb = min(t1, J.tile0 + J.ntiles);
         if (ta >= tb) continue;
-        if (NV == 1) {
-            const Sm s = sm_layout(dmv_sm, K);
-            if (J.wq2) dmv_segment<true>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
-            else dmv_segment<false>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best);
+        if (MMA) {
+            if (J.wq2) dmv_segment_mma<NV, true>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, ng, wpitch, best);
+            else dmv_segment_mma<NV, false>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, ng, wpitch, best);
         } else {
-            if (J.wq2) dmv_segment_b<NV, true>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, np, wpitch, best);
-            else dmv_segment_b<NV, false>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, np, wpitch, best);
+            const Sm s = sm_layout(dmv_sm, K);
+            if (J.wq2) dmv_segment<true>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best[0]);
+            else dmv_segment<false>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best[0]);
         }
     }
-    // the argmax keys: every holder lane keeps one vector's best
-    if (best) {
-        constexpr int SH = NV >= 8 ? 0 : NV >= 4 ? 1 : NV >= 2 ? 2 : 3;
-        atomicMax(P.key + (NV == 1 ? 0 : ((lane >> SH) % NV)), best);
+    if (MMA) {
+        // the argmax keys: lanes (g, t) hold vectors 2t and 2t+1; the warp's
+        // maximum per vector, then one atomic per vector
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            unsigned long long b = best[h];
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                const unsigned long long c = __shfl_xor_sync(0xffffffffu, b, o);
+                b = c > b ? c : b;
+            }
+            if (b && lane < 4 && 2 * lane + h < P.nvec) atomicMax(P.key + 2 * lane + h, b);
+        }
+    } else if (best[0]) {
+        atomicMax(P.key, best[0]);
     }
 }
 
-extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
+template <int NV>
+__global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid_constant__ dmv_params P)
 {
-    if (!p || p->njobs < 1 || p->njobs > DMV_MAXJ || p->K < 128 || (p->K & 127) || p->K > 32768 || !p->x)
-        return -11;
-    if (p->op == DMV_OP_RMSNORM && !p->nw) return -11;
-    if (p->op == DMV_OP_GATED && (!p->nw || !p->x2)) return -11;
-    if (p->op < DMV_OP_F16 || p->op > DMV_OP_GATED) return -11;
-    dmv_params P = *p;
+    extern __shared__ __align__(128) uint8_t dmv_sm[];
+    dmv_body<NV>(P, dmv_sm, blockIdx.x, gridDim.x, true);
+}
+
+// Validates a parameter block and sets its launch-dependent fields (tiles
+// and the column split) for `slots` CTAs; returns the dynamic shared memory
+// the kernel needs, or a negative status.
+static long long dmv_prepare(dmv_params &P, int slots)
+{
+    if (P.njobs < 1 || P.njobs > DMV_MAXJ || P.K < 128 || (P.K & 127) || P.K > 32768 || !P.x) return -11;
+    if (P.op == DMV_OP_RMSNORM && !P.nw) return -11;
+    if (P.op == DMV_OP_GATED && (!P.nw || !P.x2)) return -11;
+    if (P.op < DMV_OP_F16 || P.op > DMV_OP_GATED) return -11;
     if (P.nvec <= 0) P.nvec = 1;
     if (P.nvec > 8 || (P.nvec > 1 && P.xs < P.K) || (P.xs & 7)) return -11;
+    const bool mma = P.nvec > 1;
     const int NV = P.nvec == 1 ? 1 : P.nvec == 2 ? 2 : P.nvec <= 4 ? 4 : 8;
-    const void *fn = NV == 1 ? (const void *)dmv_kernel<1> : NV == 2 ? (const void *)dmv_kernel<2>
-                   : NV == 4 ? (const void *)dmv_kernel<4> : (const void *)dmv_kernel<8>;
-    const int fi = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : 3;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-    if (dev < 0 || dev >= 64) return -11;
-    // per device and kernel instance: the SM count, and the occupancy of up
-    // to 8 shared-memory sizes (the decode step uses 3 or 4)
-    static int s_sms[64], s_occ[64][4][8], s_attr[64][4];
-    static size_t s_occ_smem[64][4][8];
     const size_t smem = (size_t)NV * dmv_smem_x_bytes(P.K);
     if (smem > 200 * 1024) return -11;
-    if (!s_attr[dev][fi]) {
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-        s_attr[dev][fi] = 1;
+    // Rows are short of warps when a CTA would get fewer than 16 (one per
+    // warp on the CUDA-core path; 8 warp tiles of 16 rows on the mma path):
+    // then split each row's columns over up to all 8 warps of the CTA.
+    long long all_rows = 0, wtiles = 0;
+    for (int j = 0; j < P.njobs; j++) {
+        const int r = P.jobs[j].rows > 0 ? P.jobs[j].rows : 0;
+        all_rows += r;
+        wtiles += (r + (P.jobs[j].wq2 ? 7 : 15)) / (P.jobs[j].wq2 ? 8 : 16);
     }
-    int occ = 0;
-    for (int i = 0; i < 8; i++) if (s_occ[dev][fi][i] && s_occ_smem[dev][fi][i] == smem) occ = s_occ[dev][fi][i];
-    if (!occ) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DMV_THREADS, smem);
-        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
-        if (occ < 1) occ = 1;
-        for (int i = 0; i < 8; i++)
-            if (!s_occ[dev][fi][i]) { s_occ[dev][fi][i] = occ; s_occ_smem[dev][fi][i] = smem; break; }
-    }
-    const int slots = s_sms[dev] * occ;
-    // Rows are short of warps when a CTA would get fewer than 16: then split
-    // each row's columns over up to all 8 warps of the CTA (at most 32 pairs,
-    // one batch, per warp where the pair count allows).
-    long long all_rows = 0;
-    for (int j = 0; j < P.njobs; j++) all_rows += P.jobs[j].rows > 0 ? P.jobs[j].rows : 0;
-    const int np = P.K / 64;
+    const int np = P.K / 64, ng = P.K / 128;
     int ks = 1;
-    if (all_rows < 16LL * slots)
+    if (mma) {
+        while (ks < DMV_WARPS && wtiles * ks < (long long)DMV_WARPS * slots && (ng % (2 * ks)) == 0) ks *= 2;
+    } else if (all_rows < 16LL * slots) {
         while (ks < DMV_WARPS && np / ks > 32 && (np % (2 * ks)) == 0) ks *= 2;
+    }
     P.ksplit = ks;
     const int rt = DMV_WARPS / ks;
     int tiles = 0;
@@ -778,16 +827,56 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
         if (P.nvec > 1 && J.epi == DMV_EPI_GATES && (J.ostride < J.n1 || J.ostride < J.rows - J.n1)) return -11;
         if (J.epi != DMV_EPI_SWIGLU && J.wq2) return -11;
         J.tile0 = tiles;
-        J.ntiles = (J.rows + rt - 1) / rt;
+        J.ntiles = mma ? (J.rows + (J.wq2 ? 7 : 15)) / (J.wq2 ? 8 : 16) : (J.rows + rt - 1) / rt;
         tiles += J.ntiles;
     }
     P.total_tiles = tiles;
+    return (long long)smem;
+}
+
+extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
+{
+    if (!p) return -11;
+    dmv_params P = *p;
+    const int nvec = P.nvec <= 0 ? 1 : P.nvec;
+    if (nvec > 8) return -11;
+    const int NV = nvec == 1 ? 1 : nvec == 2 ? 2 : nvec <= 4 ? 4 : 8;
+    const void *fn = NV == 1 ? (const void *)dmv_kernel<1> : NV == 2 ? (const void *)dmv_kernel<2>
+                   : NV == 4 ? (const void *)dmv_kernel<4> : (const void *)dmv_kernel<8>;
+    const int fi = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : 3;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+    if (dev < 0 || dev >= 64) return -11;
+    // per device and kernel instance: the SM count, and the occupancy of up
+    // to 8 shared-memory sizes (the decode step uses 3 or 4)
+    static int s_sms[64], s_occ[64][4][8], s_attr[64][4];
+    static size_t s_occ_smem[64][4][8];
+    if (!s_attr[dev][fi]) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+        s_attr[dev][fi] = 1;
+    }
+    const size_t smem = (size_t)NV * dmv_smem_x_bytes(P.K > 0 ? P.K : 128);
+    int occ = 0;
+    for (int i = 0; i < 8; i++) if (s_occ[dev][fi][i] && s_occ_smem[dev][fi][i] == smem) occ = s_occ[dev][fi][i];
+    if (!occ) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DMV_THREADS, smem);
+        if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+        if (occ < 1) occ = 1;
+        for (int i = 0; i < 8; i++)
+            if (!s_occ[dev][fi][i]) { s_occ[dev][fi][i] = occ; s_occ_smem[dev][fi][i] = smem; break; }
+    }
+    const int slots = s_sms[dev] * occ;
+    const long long rc = dmv_prepare(P, slots);
+    if (rc < 0) return (int)rc;
     int grid = slots;
-    if (grid > tiles) grid = tiles;
+    if (grid > P.total_tiles) grid = P.total_tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(DMV_THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = (size_t)rc;
     cfg.stream = reinterpret_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -96,6 +96,10 @@ struct dec_model {
     uint32_t *ar_epoch, *ar_done, *ak_epoch;
     int      *err;
     int64_t   weight_bytes;
+    /* the persistent kernel's program (single GPU) */
+    mg_prog   mg;
+    int       persistent, mega_ok;
+    int32_t  *layer_clock;               /* [n_layers + 1]: clock index at each layer's end */
     void     *allocs[MAX_ALLOCS];
     int       nalloc;
 };
@@ -147,6 +151,8 @@ static int make_vec(dec_model *m, float **p, uint64_t key, const int32_t *h_idx,
     if (h_idx) CK(to_device_i32(m, &d_idx, h_idx, (size_t)n));
     return dec_k_synth_vec(key, d_idx, idx0, n, mean, std, *p, NULL, NULL);
 }
+
+static int mega_build(dec_model *m);
 
 static int is_attn(const dec_config *c, int il) { return ((il + 1) % c->attn_every) == 0; }
 
@@ -279,6 +285,13 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->prompt, 4 * ((size_t)c->max_ctx * B + 1)));
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { rc = fail(e); goto bad; }
+    m->layer_clock = (int32_t *)calloc((size_t)c->n_layers + 1, sizeof(int32_t));
+    if (!m->layer_clock) { rc = -11; goto bad; }
+    if (W == 1) {
+        const char *pe = getenv("DEC_PERSISTENT");
+        m->persistent = pe && pe[0] == '1';
+        if (m->persistent) TRY(mega_build(m));
+    }
     free(rows); free(cidx);
     *out = m;
     return 0;
@@ -296,6 +309,9 @@ int dec_destroy(dec_model *m)
     if (m->comm_ok) ncclCommDestroy(m->comm);
     for (int r = 0; r < 8; r++) if (m->p2p_open[r]) cudaIpcCloseMemHandle(m->p2p_peer[r]);
     for (int i = 0; i < m->nalloc; i++) cudaFree(m->allocs[i]);
+    if (m->mg.d_prog) cudaFree(m->mg.d_prog);
+    if (m->mg.ctl) cudaFree(m->mg.ctl);
+    free(m->layer_clock);
     free(m->chan);
     free(m->L);
     free(m);
@@ -364,6 +380,14 @@ int dec_status(dec_model *m, int32_t *flags)
     cudaError_t e = cudaSetDevice(m->device);
     if (e == cudaSuccess) e = cudaMemcpy(&v, m->err, 4, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess) e = cudaMemset(m->err, 0, 4);
+    if (e == cudaSuccess && m->mg.ctl) {
+        mg_ctl ctl;
+        e = cudaMemcpy(&ctl, m->mg.ctl, sizeof ctl, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && ctl.abort) {
+            v |= 4;
+            e = cudaMemset(m->mg.ctl, 0, sizeof ctl);
+        }
+    }
     if (e != cudaSuccess) return fail(e);
     *flags = v;
     return 0;
@@ -472,12 +496,53 @@ int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream)
 
 #define PF_BYTES (48 * 1024)
 
-/* outputs [batch][rows] */
-static void mvjob(dmv_job *J, const linear_t *l, int epi)
+/* The step as a program.  dec_program walks the layers once and hands each
+ * piece of work to an emitter: in launch mode (rec == NULL) every piece is a
+ * kernel launch on the stream (programmatic dependents of one another); in
+ * record mode it becomes a stage of the persistent kernel's program, with a
+ * grid barrier after every stage whose output a later one reads. */
+typedef struct {
+    dec_model *m;
+    void      *s;
+    int        pdl;
+    mg_stage  *rec;
+    int        n, cap, nbar;
+} emit_t;
+
+static mg_stage *em_new(emit_t *E, int op, int sync)
 {
-    memset(J, 0, sizeof *J);
-    J->wq = l->wq; J->sc = l->sc; J->rows = l->rows; J->epi = epi; J->s_pitch = l->s_pitch;
-    J->ostride = l->rows;
+    if (E->n == E->cap) {
+        const int cap = E->cap ? 2 * E->cap : 256;
+        mg_stage *r = (mg_stage *)realloc(E->rec, sizeof(mg_stage) * (size_t)cap);
+        if (!r) return NULL;
+        E->rec = r; E->cap = cap;
+    }
+    mg_stage *st = &E->rec[E->n++];
+    memset(st, 0, sizeof *st);
+    st->op = op; st->sync = sync; st->pf = -1;
+    E->nbar += sync ? 1 : 0;
+    return st;
+}
+
+static int em_matvec(emit_t *E, const dmv_params *P)
+{
+    if (!E->rec) return dec_k_matvec(P, E->s, E->pdl);
+    mg_stage *st = em_new(E, MG_MATVEC, 1);
+    if (!st) return -11;
+    st->u.mv = *P;
+    return 0;
+}
+
+static int em_copy(emit_t *E, float *dst, const float *src, int64_t n)
+{
+    if (!E->rec)
+        return cudaMemcpyAsync(dst, src, sizeof(float) * (size_t)n, cudaMemcpyDeviceToDevice, (cudaStream_t)E->s)
+               == cudaSuccess ? 0 : -20;
+    /* no barrier: the stage after it reads the residual but does not write it */
+    mg_stage *st = em_new(E, MG_COPY, 0);
+    if (!st) return -11;
+    st->u.cp.dst = dst; st->u.cp.src = src; st->u.cp.n = n;
+    return 0;
 }
 
 /* inputs [batch][K] */
@@ -489,40 +554,54 @@ static void mvparams(dec_model *m, dmv_params *P, int K, int op, const void *x, 
     P->nvec = m->B; P->xs = K;
 }
 
+/* outputs [batch][rows] */
+static void mvjob(dmv_job *J, const linear_t *l, int epi)
+{
+    memset(J, 0, sizeof *J);
+    J->wq = l->wq; J->sc = l->sc; J->rows = l->rows; J->epi = epi; J->s_pitch = l->s_pitch;
+    J->ostride = l->rows;
+}
+
 /* row-parallel block: a single GPU adds into the residual in the matvec
  * epilogue; tensor parallel sums the partials with one NCCL all-reduce */
-static int row_parallel(dec_model *m, dmv_params *P, const linear_t *l, void *s)
+static int row_parallel(emit_t *E, dmv_params *P, const linear_t *l)
 {
+    dec_model *m = E->m;
+    void *s = E->s;
     mvjob(&P->jobs[0], l, m->world == 1 ? DMV_EPI_ACC : DMV_EPI_F32);
     P->jobs[0].out_f32 = m->world == 1 ? m->x : m->t;
     P->jobs[0].ostride = m->c.hidden;
     P->njobs = 1;
-    CK(dec_k_matvec(P, s, m->pdl));
+    CK(em_matvec(E, P));
     if (m->world == 1) return 0;
+    if (E->rec) return -11;                       /* tensor parallel runs in launch mode */
     if (m->p2p_ok)
         return dec_k_allreduce_p2p(m->p2p_peer, m->rank, m->world, m->c.hidden, m->t, m->x, m->ar_epoch,
-                                   m->ar_done, m->err, m->spin_limit, s, m->pdl && s != NULL);
+                                   m->ar_done, m->err, m->spin_limit, s, E->pdl);
     if (ncclAllReduce(m->t, m->t, (size_t)m->c.hidden, ncclFloat32, ncclSum, m->comm, (cudaStream_t)s)
         != ncclSuccess) return -20;
-    return dec_k_add(m->x, m->t, m->c.hidden, s, m->pdl && s != NULL);
+    return dec_k_add(m->x, m->t, m->c.hidden, s, E->pdl);
 }
 
-int dec_step(dec_model *m, void *s)
+static int dec_program(dec_model *m, emit_t *E)
 {
-    if (!m) return -11;
-    if (m->world > 1 && !m->comm_ok && !m->p2p_ok) return -11;
-    if (m->hpos >= m->c.max_ctx) return -11;   /* the KV cache is full */
-    m->hpos++;
     const dec_config *c = &m->c;
-    const int H = c->hidden, pdl = m->pdl && s != NULL;   /* not on the legacy default stream */
+    const int H = c->hidden;
+    void *s = E->s;
+    const int pdl = E->pdl;
     dmv_params P;
-    CK(dec_k_embed(m->embed, H, m->tok, m->x, m->B, s, pdl));
-    const size_t xbytes = sizeof(float) * (size_t)H * m->B;
+    if (E->rec) {
+        mg_stage *st = em_new(E, MG_EMBED, 1);
+        if (!st) return -11;
+        st->u.emb.emb = m->embed; st->u.emb.tok = m->tok; st->u.emb.x = m->x;
+        st->u.emb.hidden = H; st->u.emb.nseq = m->B;
+    } else {
+        CK(dec_k_embed(m->embed, H, m->tok, m->x, m->B, s, pdl));
+    }
+    const size_t xn = (size_t)H * m->B;
     for (int il = 0; il < c->n_layers; il++) {
         layer_t *l = &m->L[il];
-        if (m->rseam && il < m->nrseam
-            && cudaMemcpyAsync(m->rseam + il * (xbytes / 4), m->x, xbytes, cudaMemcpyDeviceToDevice,
-                               (cudaStream_t)s) != cudaSuccess) return -20;
+        if (m->rseam && il < m->nrseam) CK(em_copy(E, m->rseam + il * xn, m->x, (int64_t)xn));
         mvparams(m, &P, H, DMV_OP_RMSNORM, m->x, l->attn_norm, c->rms_eps, m->h16);
         if (!l->attn) {
             /* q|k|v with the conv + SiLU epilogue, z, and a|b with the gates */
@@ -535,7 +614,7 @@ int dec_step(dec_model *m, void *s)
             P.jobs[2].out_f32 = m->eg; P.jobs[2].out2_f32 = m->beta;
             P.jobs[2].p0 = l->ssm_a; P.jobs[2].p1 = l->dt_bias; P.jobs[2].n1 = m->vh; P.jobs[2].ostride = m->vh;
             P.njobs = 3;
-            CK(dec_k_matvec(&P, s, pdl));
+            CK(em_matvec(E, &P));
             gdn_f32_args g;
             memset(&g, 0, sizeof g);
             g.T = 1; g.H = m->vh; g.KH = m->kh; g.D = HD; g.S = l->rec_state;
@@ -543,45 +622,72 @@ int dec_step(dec_model *m, void *s)
             g.g = NULL; g.eg = m->eg; g.beta = m->beta; g.l2norm = 1; g.q_scale = 1.0f / sqrtf((float)HD);
             g.out_f32 = m->o_f; g.pdl = pdl;
             g.nseq = m->B; g.seq_in = m->conv_dim;
-            CK(gdn_run_f32(&g, s));
+            if (E->rec) {
+                mg_stage *st = em_new(E, MG_GDN, 1);
+                if (!st) return -11;
+                st->u.gdn = g;
+            } else {
+                CK(gdn_run_f32(&g, s));
+            }
             /* output norm and z gate folded into the out projection */
             mvparams(m, &P, m->vh * HD, DMV_OP_GATED, m->o_f, l->ssm_norm, c->rms_eps, m->y16);
             P.x2 = m->z_f;
-            CK(row_parallel(m, &P, &l->out, s));
+            CK(row_parallel(E, &P, &l->out));
         } else {
             mvjob(&P.jobs[0], &l->qg, DMV_EPI_F32);
             P.jobs[0].out_f32 = m->qg_f;
             mvjob(&P.jobs[1], &l->kv, DMV_EPI_F32);
             P.jobs[1].out_f32 = m->kv_f;
             P.njobs = 2;
-            CK(dec_k_matvec(&P, s, pdl));
+            CK(em_matvec(E, &P));
             /* q/k norm, RoPE and the cache write folded into flash decoding */
-            CK(dec_k_attention(m->qg_f, m->kv_f, l->q_norm, l->k_norm, m->qh, m->kvh, c->n_rot, c->rope_theta,
-                               c->rms_eps, m->pos, c->max_ctx, m->att_ch, m->part, m->q_f, l->kcache, l->vcache,
-                               m->ya16, m->B, s, pdl));
+            if (E->rec) {
+                dec_attn_args A = {m->qg_f, m->kv_f, l->q_norm, l->k_norm, m->qh, m->kvh, c->n_rot, c->rope_theta,
+                                   c->rms_eps, m->pos, c->max_ctx, m->att_ch, 0, l->kcache, l->vcache, m->q_f,
+                                   m->part, m->ya16, m->B};
+                mg_stage *st = em_new(E, MG_ATTN, 1);
+                if (!st) return -11;
+                st->u.att = A;
+                st = em_new(E, MG_COMBINE, 1);
+                if (!st) return -11;
+                st->u.att = A;
+            } else {
+                CK(dec_k_attention(m->qg_f, m->kv_f, l->q_norm, l->k_norm, m->qh, m->kvh, c->n_rot, c->rope_theta,
+                                   c->rms_eps, m->pos, c->max_ctx, m->att_ch, m->part, m->q_f, l->kcache,
+                                   l->vcache, m->ya16, m->B, s, pdl));
+            }
             mvparams(m, &P, m->qh * HD, DMV_OP_F16, m->ya16, NULL, 0.f, NULL);
-            CK(row_parallel(m, &P, &l->o, s));
+            CK(row_parallel(E, &P, &l->o));
         }
         /* SwiGLU: gate and up rows paired in one warp, silu(g)*u in the epilogue */
         mvparams(m, &P, H, DMV_OP_RMSNORM, m->x, l->post_norm, c->rms_eps, m->h16);
         mvjob(&P.jobs[0], &l->gate, DMV_EPI_SWIGLU);
         P.jobs[0].wq2 = l->up.wq; P.jobs[0].sc2 = l->up.sc; P.jobs[0].out_f16 = m->hf16;
         P.njobs = 1;
-        CK(dec_k_matvec(&P, s, pdl));
+        CK(em_matvec(E, &P));
         mvparams(m, &P, m->ffn, DMV_OP_F16, m->hf16, NULL, 0.f, NULL);
-        CK(row_parallel(m, &P, &l->down, s));
-        if (m->lev && il < m->nlev && cudaEventRecord((cudaEvent_t)m->lev[il], (cudaStream_t)s) != cudaSuccess)
+        CK(row_parallel(E, &P, &l->down));
+        if (E->rec) m->layer_clock[il] = E->nbar;
+        else if (m->lev && il < m->nlev && cudaEventRecord((cudaEvent_t)m->lev[il], (cudaStream_t)s) != cudaSuccess)
             return -20;
     }
-    if (m->rseam && c->n_layers < m->nrseam
-        && cudaMemcpyAsync(m->rseam + c->n_layers * (xbytes / 4), m->x, xbytes, cudaMemcpyDeviceToDevice,
-                           (cudaStream_t)s) != cudaSuccess) return -20;
+    if (m->rseam && c->n_layers < m->nrseam) CK(em_copy(E, m->rseam + c->n_layers * xn, m->x, (int64_t)xn));
     /* LM head with the first-max argmax key in its epilogue */
     mvparams(m, &P, H, DMV_OP_RMSNORM, m->x, m->final_norm, c->rms_eps, m->h16);
     mvjob(&P.jobs[0], &m->lm, DMV_EPI_ARGMAX);
     P.jobs[0].out_f32 = m->logits;
     P.key = m->key; P.idx0 = m->voc0; P.njobs = 1;
-    CK(dec_k_matvec(&P, s, pdl));
+    CK(em_matvec(E, &P));
+    if (E->rec) {
+        if (m->world > 1) return -11;
+        m->layer_clock[c->n_layers] = E->nbar;
+        mg_stage *st = em_new(E, MG_ADVANCE, 0);
+        if (!st) return -11;
+        st->u.adv.keys = m->key; st->u.adv.key = m->key; st->u.adv.tok = m->tok; st->u.adv.hist = m->hist;
+        st->u.adv.pos = m->pos; st->u.adv.prompt = m->prompt; st->u.adv.n = 1; st->u.adv.nseq = m->B;
+        st->u.adv.max_ctx = c->max_ctx;
+        return 0;
+    }
     if (m->world > 1 && m->p2p_ok)
         return dec_k_advance_p2p(m->p2p_peer, m->rank, m->world, H, m->key, m->tok, m->hist, m->pos, c->max_ctx,
                                  m->prompt, m->ak_epoch, m->err, m->spin_limit, s, pdl);
@@ -590,6 +696,84 @@ int dec_step(dec_model *m, void *s)
         return dec_k_advance(m->keys, m->world, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, 1, s, pdl);
     }
     return dec_k_advance(m->key, 1, m->key, m->tok, m->hist, m->pos, c->max_ctx, m->prompt, m->B, s, pdl);
+}
+
+/* records the step and uploads it for the persistent kernel (single GPU) */
+static int mega_build(dec_model *m)
+{
+    if (m->world != 1) return 0;
+    emit_t E;
+    memset(&E, 0, sizeof E);
+    E.m = m;
+    E.rec = (mg_stage *)malloc(sizeof(mg_stage) * 256);      /* rec != NULL: record mode */
+    if (!E.rec) return -11;
+    E.cap = 256;
+    int rc = dec_program(m, &E);
+    if (!rc) {
+        if (m->mg.d_prog && m->mg.n != E.n) {
+            cudaFree(m->mg.d_prog);
+            m->mg.d_prog = NULL;
+        }
+        rc = dec_mega_upload(E.rec, E.n, m->B, &m->mg);
+    }
+    free(E.rec);
+    m->mega_ok = rc == 0;
+    return rc;
+}
+
+int dec_step(dec_model *m, void *s)
+{
+    if (!m) return -11;
+    if (m->world > 1 && !m->comm_ok && !m->p2p_ok) return -11;
+    if (m->hpos >= m->c.max_ctx) return -11;   /* the KV cache is full */
+    m->hpos++;
+    if (m->persistent && m->mega_ok) return dec_k_mega(&m->mg, s);
+    emit_t E;
+    memset(&E, 0, sizeof E);
+    E.m = m; E.s = s; E.pdl = m->pdl && s != NULL;   /* not on the legacy default stream */
+    return dec_program(m, &E);
+}
+
+int dec_set_persistent(dec_model *m, int on)
+{
+    if (!m) return -11;
+    if (on && m->world != 1) return -11;
+    m->persistent = on != 0;
+    if (m->persistent && !m->mega_ok) CK(mega_build(m));
+    return 0;
+}
+
+int dec_persistent(dec_model *m)
+{
+    return m ? (m->persistent && m->mega_ok) : -11;
+}
+
+int dec_set_wait_limit(dec_model *m, int64_t ns)
+{
+    if (!m || ns < 0) return -11;
+    m->mg.timeout_ns = ns > 0 ? ns : 1000000000LL;
+    return 0;
+}
+
+int dec_set_clock(dec_model *m, uint64_t *d_clock)
+{
+    if (!m) return -11;
+    m->mg.clock = (unsigned long long *)d_clock;
+    return 0;
+}
+
+int dec_clock_slots(dec_model *m)
+{
+    if (!m) return -11;
+    if (!m->mega_ok) return 0;
+    return m->mg.nbar + 1;
+}
+
+int dec_layer_clock(dec_model *m, int layer)
+{
+    if (!m || !m->mega_ok || layer < -1 || layer > m->c.n_layers) return -11;
+    if (layer == -1) return 1;                  /* after the embedding */
+    return m->layer_clock[layer];
 }
 
 int dec_set_layer_events(dec_model *m, void **events, int n)
@@ -605,6 +789,7 @@ int dec_set_residual_seams(dec_model *m, float *buf, int n)
     if (!m || n < 0 || n > m->c.n_layers + 1 || (n && !buf)) return -11;
     m->rseam = n ? buf : NULL;
     m->nrseam = n;
+    if (m->mega_ok || m->persistent) CK(mega_build(m));
     return 0;
 }
 

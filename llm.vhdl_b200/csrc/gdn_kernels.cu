@@ -22,6 +22,7 @@
 #include <stdint.h>
 #include <math.h>
 #include "../../include/gdn_b200.h"
+#include "gdn_f32_step.cuh"
 
 extern "C" int mv4i_g_cuda_err;
 static int gdn_fail(cudaError_t e) { mv4i_g_cuda_err = (int)e; return -20; }
@@ -44,12 +45,6 @@ __device__ __forceinline__ uint64_t max8_u64(uint64_t v)
 {
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) { const uint64_t w = __shfl_xor_sync(0xffffffffu, v, o); v = w > v ? w : v; }
-    return v;
-}
-__device__ __forceinline__ float sum8_f32(float v)
-{
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
 
@@ -338,117 +333,16 @@ extern "C" int gdn_scalar_dev(int H, const int32_t *d_sc, int32_t *d_eg, int32_t
 
 // --------------------------------------------------------- binary32 steps
 
-struct StepIn {
-    uint32_t k[8], q[8];        // 16 fp16 keys of this lane's slice (packed pairs)
-    uint16_t v, g;              // this column's v and gate
-    float a, b;                 // the head's decay and beta inputs
-};
-
-__device__ __forceinline__ void load_step(const gdn_f32_args &A, int t, int h, int hk, int j, int i0, StepIn &s)
-{
-    const size_t kq = ((size_t)t * A.KH + hk) * 128 + i0;
-    const uint4 *kp = reinterpret_cast<const uint4 *>(A.k + kq), *qp = reinterpret_cast<const uint4 *>(A.q + kq);
-    const uint4 k0 = __ldg(kp), k1 = __ldg(kp + 1), q0 = __ldg(qp), q1 = __ldg(qp + 1);
-    s.k[0] = k0.x; s.k[1] = k0.y; s.k[2] = k0.z; s.k[3] = k0.w; s.k[4] = k1.x; s.k[5] = k1.y; s.k[6] = k1.z; s.k[7] = k1.w;
-    s.q[0] = q0.x; s.q[1] = q0.y; s.q[2] = q0.z; s.q[3] = q0.w; s.q[4] = q1.x; s.q[5] = q1.y; s.q[6] = q1.z; s.q[7] = q1.w;
-    const size_t vj = ((size_t)t * A.H + h) * 128 + j;
-    s.v = __ldg(A.v + vj);
-    s.g = A.g ? __ldg(A.g + vj) : (uint16_t)0;
-    s.a = A.eg ? __ldg(A.eg + (size_t)t * A.H + h) : __ldg(A.a + (size_t)t * A.H + h);
-    s.b = A.beta ? __ldg(A.beta + (size_t)t * A.H + h) : __ldg(A.b + (size_t)t * A.H + h);
-}
-
-// grid: H x 8 CTAs of 4 warps; CTA (h, c) owns columns 16c .. 16c+15 of head h.
+// grid: H x 8 CTAs of 4 warps; CTA (h, c) owns columns 16c .. 16c+15 of head h
+// (the body is gdn_f32_step.cuh, shared with the persistent decode kernel).
 __global__ void __launch_bounds__(128)
 gdn_f32_kernel(const gdn_f32_args A0)
 {
-    // sequence blockIdx.y of a batched step: its inputs, outputs and state
-    gdn_f32_args A = A0;
-    if (blockIdx.y) {
-        const size_t n = blockIdx.y, hd = (size_t)A.H * 128;
-        A.q += n * A.seq_in; A.k += n * A.seq_in; A.v += n * A.seq_in;
-        if (A.g) A.g += n * hd;
-        if (A.a) A.a += n * A.H;
-        if (A.b) A.b += n * A.H;
-        if (A.eg) A.eg += n * A.H;
-        if (A.beta) A.beta += n * A.H;
-        if (A.out_f32) A.out_f32 += n * hd;
-        if (A.out_f16) A.out_f16 += n * hd;
-        A.S += n * hd * 128;
-    }
-    const int h = blockIdx.x >> 3;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = (blockIdx.x & 7) * 16 + warp * 4 + (lane >> 3);
-    const int sl = lane & 7, i0 = 16 * sl;
-    const int hk = h % A.KH;
     // a programmatic dependent of the previous kernel: let the next one
     // launch, then wait for this one's inputs (no-ops otherwise)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    float *scol = A.S + ((size_t)h * 128 + j) * 128 + i0;
-    float s[16];
-#pragma unroll
-    for (int t4 = 0; t4 < 4; t4++) {
-        const float4 v = reinterpret_cast<const float4 *>(scol)[t4];
-        s[4 * t4] = v.x; s[4 * t4 + 1] = v.y; s[4 * t4 + 2] = v.z; s[4 * t4 + 3] = v.w;
-    }
-    StepIn cur, nxt;
-    load_step(A, 0, h, hk, j, i0, cur);
-    for (int t = 0; t < A.T; t++) {
-        if (t + 1 < A.T) load_step(A, t + 1, h, hk, j, i0, nxt);
-        float kf[16], qf[16];
-#pragma unroll
-        for (int p = 0; p < 8; p++) {
-            const float2 kk = __half22float2(*reinterpret_cast<const __half2 *>(&cur.k[p]));
-            const float2 qq = __half22float2(*reinterpret_cast<const __half2 *>(&cur.q[p]));
-            kf[2 * p] = kk.x; kf[2 * p + 1] = kk.y; qf[2 * p] = qq.x; qf[2 * p + 1] = qq.y;
-        }
-        if (A.l2norm) {
-            float nk = 0.f, nq = 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; i++) { nk = fmaf(kf[i], kf[i], nk); nq = fmaf(qf[i], qf[i], nq); }
-            nk = sum8_f32(nk);
-            nq = sum8_f32(nq);
-            const float rk = 1.0f / fmaxf(sqrtf(nk), 1e-12f), rq = A.q_scale / fmaxf(sqrtf(nq), 1e-12f);
-#pragma unroll
-            for (int i = 0; i < 16; i++) { kf[i] *= rk; qf[i] *= rq; }
-        } else if (A.q_scale != 1.0f) {
-#pragma unroll
-            for (int i = 0; i < 16; i++) qf[i] *= A.q_scale;
-        }
-        float alpha, beta;
-        if (A.eg) { alpha = cur.a; beta = cur.b; }
-        else {
-            const float sp = cur.a > 30.f ? cur.a : log1pf(expf(cur.a));
-            alpha = expf(-sp);
-            beta = 1.0f / (1.0f + expf(-cur.b));
-        }
-        float sk0 = 0.f, sk1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-            s[i] *= alpha; s[i + 1] *= alpha;
-            sk0 = fmaf(s[i], kf[i], sk0); sk1 = fmaf(s[i + 1], kf[i + 1], sk1);
-        }
-        const float sk = sum8_f32(sk0 + sk1);
-        const float d = (__half2float(__ushort_as_half(cur.v)) - sk) * beta;
-        float o0 = 0.f, o1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-            s[i] = fmaf(kf[i], d, s[i]); s[i + 1] = fmaf(kf[i + 1], d, s[i + 1]);
-            o0 = fmaf(s[i], qf[i], o0); o1 = fmaf(s[i + 1], qf[i + 1], o1);
-        }
-        float o = sum8_f32(o0 + o1);
-        if (A.g) o = o / (1.0f + expf(-__half2float(__ushort_as_half(cur.g))));
-        if (sl == 0) {
-            const size_t oj = ((size_t)t * A.H + h) * 128 + j;
-            if (A.out_f32) A.out_f32[oj] = o;
-            if (A.out_f16) A.out_f16[oj] = __half_as_ushort(__float2half_rn(o));
-        }
-        cur = nxt;
-    }
-#pragma unroll
-    for (int t4 = 0; t4 < 4; t4++)
-        reinterpret_cast<float4 *>(scol)[t4] = make_float4(s[4 * t4], s[4 * t4 + 1], s[4 * t4 + 2], s[4 * t4 + 3]);
+    gdn_f32_cta<false>(A0, blockIdx.x, blockIdx.y, threadIdx.x);
 }
 
 extern "C" int gdn_run_f32(const gdn_f32_args *a, void *stream)

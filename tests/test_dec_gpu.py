@@ -279,7 +279,13 @@ def test_batched_sequences_match_oracle(pkg, cuda, O):
         assert not np.array_equal(lg[0], lg[1]) and not np.array_equal(lg[1], lg[2])
     finally:
         d.close()
-    # sequence 0 of a batch is the unbatched model's sequence (same draws)
+    # sequence 0 of a batch is the unbatched model's sequence (same draws).
+    # A batch streams the projections on the tensor pipe (the exact integer
+    # dot of each 128-column group, then one fp32 multiply-add), one sequence
+    # on the CUDA cores (one fp32 multiply-add per 64-column half): the fp32
+    # sums round differently, an fp16 activation can land on the other side
+    # of a rounding boundary, and that grows through the layers -- so the
+    # step's tolerance, not bit equality.
     d1, d3 = Dec(pkg), Dec(pkg, cfg)
     try:
         for x in (d1, d3):
@@ -287,7 +293,7 @@ def test_batched_sequences_match_oracle(pkg, cuda, O):
             x.step(torch)
         a = device_read(torch, d1.pointers()["logits"], (cfg["vocab"],), np.float32).astype(np.float64)
         b = device_read(torch, d3.pointers()["logits"], (3, cfg["vocab"]), np.float32)[0].astype(np.float64)
-        assert rel(b, a) <= 1e-5
+        assert rel(b, a) <= TOL
     finally:
         d1.close()
         d3.close()
