@@ -298,3 +298,47 @@ def test_g128_cross_check_golden(cuda, pkg, synth):
     assert rc == 0
     yg = r["y_data"].astype(np.float64) * 2.0 ** (-r["y_exp"])
     assert np.max(np.abs(yg - y32[0])) <= 2e-4 * np.max(np.abs(y32[0]))
+
+
+@pytest.mark.parametrize("M,K,n_rows,n_cols,accum", [(37, 1024, 37, 1024, 0), (1000, 2176, 1000, 2176, 0),
+                                                    (333, 2048, 300, 1000, 0), (4096, 8192, 4096, 8192, 1),
+                                                    (17, 128, 17, 100, 1)])
+def test_g128_layouts(cuda, pkg, M, K, n_rows, n_cols, accum):
+    """Padded scale rows (a pitch beyond K/128), ragged row counts, a group
+    count that is not a power of two, a column window that ends inside a
+    group, the accumulate flag, and several jobs sharing CTAs.  Same
+    tolerances as test_g128_vs_double_oracle."""
+    torch = cuda
+    L = pkg.lib()
+    ng = (K + 127) // 128
+    sp = (ng + 7) & ~7
+    G = 3
+    wq, sc0, x = _g128_operands(torch, pkg, 5, M, K, G)
+    sc = torch.zeros((G, M, sp), dtype=torch.float16, device="cuda")
+    sc[:, :, :ng] = sc0
+    y16 = torch.zeros((G, M), dtype=torch.float16, device="cuda")
+    base = torch.randn((G, M), device="cuda") if accum else torch.zeros((G, M), device="cuda")
+    y32 = base.clone()
+    mats, jobs = [], []
+    for i in range(G):
+        dm = pkg.DMat()
+        assert L.mv4i_dmat_wrap_g128(_dptr(wq[i]), K // 2, _dptr(sc[i]), sp, M, K, 0, C.byref(dm)) == 0
+        mats.append(dm)
+        j = pkg.Job()
+        j.w = C.pointer(dm); j.x = x[i].data_ptr(); j.n_rows = n_rows; j.n_cols = n_cols; j.nvec = 1
+        j.y_f16 = y16[i].data_ptr(); j.y_f32 = y32[i].data_ptr(); j.accum = accum
+        jobs.append(j)
+    arr = (pkg.Job * G)(*jobs)
+    assert L.mv4i_launch(arr, G, None, None) == 0
+    torch.cuda.synchronize()
+    for i in range(G):
+        xc = x[i].cpu().numpy().copy()
+        xc[n_cols:] = 0
+        ref = O.matvec_g128_f64(wq[i].cpu().numpy(), sc0[i].cpu().numpy(), xc, K)[:n_rows]
+        got32 = (y32[i] - base[i]).cpu().numpy()[:n_rows].astype(np.float64)
+        amax = np.max(np.abs(ref))
+        assert np.max(np.abs(got32 - ref)) <= 1e-4 * amax + (1e-6 * np.max(np.abs(base[i].cpu().numpy())) if accum else 0)
+        assert np.all(y32[i].cpu().numpy()[n_rows:] == base[i].cpu().numpy()[n_rows:])
+        if not accum:
+            e16 = np.abs(y16[i].cpu().numpy()[:n_rows].astype(np.float64) - ref)
+            assert np.all(e16 <= 2.0 ** -11 * np.abs(ref) + 1e-4 * amax)
