@@ -106,7 +106,7 @@ __device__ __forceinline__ void att_norm_rope(const float4 r, const float *w, fl
 // Piece (chunk c, kv head g, sequence b) of the attention step, by `nthr`
 // threads (tid < nthr; at least 32 * qh/kvh; warps past the GQA group only help
 // load the chunk).  Every thread reaches the same barriers.
-__device__ void dec_attn_cta(const dec_attn_args &A, int c, int g, int b, int tid, int nthr, uint8_t *att_sm)
+__device__ __forceinline__ void dec_attn_cta(const dec_attn_args &A, int c, int g, int b, int tid, int nthr, uint8_t *att_sm)
 {
     const int qh = A.qh, kvh = A.kvh, max_ctx = A.max_ctx, ch = A.ch, nchunks = A.nchunks, n_rot = A.n_rot;
     const float theta = A.theta, eps = A.eps;
@@ -226,7 +226,7 @@ __device__ void dec_attn_cta(const dec_attn_args &A, int c, int g, int b, int ti
     reinterpret_cast<float4 *>(pp + 4)[lane] = make_float4(a0, a1, a2, a3);
 }
 
-__global__ void __launch_bounds__(1024) dec_attn_kernel(const dec_attn_args A)
+__global__ void __launch_bounds__(1024, 1) dec_attn_kernel(const dec_attn_args A)
 {
     extern __shared__ __align__(16) uint8_t att_sm[];
     PDL_ENTER();
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(1024) dec_attn_kernel(const dec_attn_args A)
 // memory, then thread d sums dimension d over the chunks.
 // Piece (q head h, sequence b) of the combine by 128 threads (t < 128), with
 // its own wc[1024] / red[32] scratch; every thread reaches the same barriers.
-__device__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc, float *red)
+__device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc, float *red)
 {
     const int hd = ATT_HD, nchunks = A.nchunks, ch = A.ch, qh = A.qh, gate_stride = 2 * ATT_HD;
     const float *part = A.part, *gate = A.qg + ATT_HD;           // the gate: second half of each q|gate row

@@ -83,6 +83,13 @@ __device__ __forceinline__ int to_i16(float f, float scale)
     return min(__float2int_rn(f * scale), 32767);
 }
 
+__device__ __forceinline__ uint32_t prmt_b(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
 // 2^n for n in [-126, 127]
 __device__ __forceinline__ float exp2i(int n) { return __int_as_float((127 + n) << 23); }
 
@@ -244,14 +251,12 @@ __device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb, bool seam
             for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
             const int gsum = ssum + __shfl_xor_sync(0xffffffffu, ssum, 8);
             if (ok) {
-                uint32_t le = 0, lo = 0, he = 0, ho = 0;
-#pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    le |= (uint32_t)(xi[2 * t] & 0xFF) << (8 * t);
-                    he |= (uint32_t)((xi[2 * t] >> 8) & 0xFF) << (8 * t);
-                    lo |= (uint32_t)(xi[2 * t + 1] & 0xFF) << (8 * t);
-                    ho |= (uint32_t)((xi[2 * t + 1] >> 8) & 0xFF) << (8 * t);
-                }
+                // byte planes by permutes: t = {x0.b0, x2.b0, x0.b1, x2.b1} and
+                // {x4.b0, x6.b0, x4.b1, x6.b1}, then their low / high halves
+                const uint32_t te0 = prmt_b(xi[0], xi[2], 0x5140u), te1 = prmt_b(xi[4], xi[6], 0x5140u);
+                const uint32_t to0 = prmt_b(xi[1], xi[3], 0x5140u), to1 = prmt_b(xi[5], xi[7], 0x5140u);
+                const uint32_t le = prmt_b(te0, te1, 0x5410u), he = prmt_b(te0, te1, 0x7632u);
+                const uint32_t lo = prmt_b(to0, to1, 0x5410u), ho = prmt_b(to0, to1, 0x7632u);
                 const int c = u >> 2, q = u & 3, p = c >> 1, par = c & 1;
                 pw[4 * ((0 + par) * np + p) + q] = le;
                 pw[4 * ((2 + par) * np + p) + q] = lo;
