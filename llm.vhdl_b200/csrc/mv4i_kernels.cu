@@ -692,13 +692,23 @@ __device__ __forceinline__ int32_t combine_v3(const int (&a)[4], int32_t sx)
     return a[0] + (a[1] >> 4) + (a[2] + (a[3] >> 4)) * 256 - 8 * sx;   // a[1], a[3]: multiples of 16
 }
 
+// Resident CTAs per SM the registers are sized for (RW = 2): more warps keep
+// more loads in flight while others compute.
+#ifndef V3_MINB_G128
+#define V3_MINB_G128 4
+#endif
+#ifndef V3_MINB_GOLD
+#define V3_MINB_GOLD 3
+#endif
+#define V3_MINB(KIND) ((KIND) == KIND_G128 ? V3_MINB_G128 : V3_MINB_GOLD)
+
 // Work split: a job's rows are processed LPR lanes per row (LPR = largest
 // power of two <= 32 dividing the job's group count), so 32/LPR rows share a
 // warp and every lane owns whole 128-column groups (GPL of them); RW rows per
 // lane segment share each x-plane load.  Tiles of 8 warps x (32/LPR) x RW
 // rows are flattened over the job list and cut into contiguous per-CTA ranges.
 template <int KIND, int RW>
-__global__ void __launch_bounds__(MV_THREADS, RW == 4 ? 2 : 3)
+__global__ void __launch_bounds__(MV_THREADS, RW == 4 ? 2 : V3_MINB(KIND))
 mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
 {
     extern __shared__ __align__(128) uint8_t smem[];
