@@ -660,6 +660,43 @@ def profile_decode(args):
     D.dec_destroy(h)
 
 
+def profile_matvec(args):
+    """`--only matvec`: a short run for profilers -- the config-0 stack of
+    `--stack` 4096x4096 g128 matrices (seeded), `--warmup` then `--steps`
+    launches of the whole job list on one stream."""
+    import torch
+    pkg = load_pkg()
+    L = pkg.lib()
+    G = args.stack
+    wq = torch.empty((G, M, K // 2), dtype=torch.uint8, device="cuda")
+    sc = torch.empty((G, M, K // 128), dtype=torch.float16, device="cuda")
+    x = torch.empty((G, K), dtype=torch.float16, device="cuda")
+    assert L.mv4i_synth_g128(0, G, M, K, C.c_void_p(wq.data_ptr()), C.c_void_p(sc.data_ptr()),
+                             C.c_void_p(x.data_ptr()), None) == 0
+    y = torch.zeros((G, M), dtype=torch.float16, device="cuda")
+    mats = (pkg.DMat * G)()
+    jobs = (pkg.Job * G)()
+    for i in range(G):
+        assert L.mv4i_dmat_wrap_g128(C.c_void_p(wq[i].data_ptr()), K // 2, C.c_void_p(sc[i].data_ptr()), K // 128,
+                                     M, K, 0, C.byref(mats[i])) == 0
+        j = jobs[i]
+        j.w = C.pointer(mats[i]); j.x = x[i].data_ptr(); j.n_rows = M; j.n_cols = K; j.nvec = 1
+        j.y_f16 = y[i].data_ptr()
+    s = torch.cuda.Stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            assert L.mv4i_launch(jobs, G, None, C.c_void_p(s.cuda_stream)) == 0
+        e0.record(s)
+        for _ in range(args.steps):
+            assert L.mv4i_launch(jobs, G, None, C.c_void_p(s.cuda_stream)) == 0
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"only": "matvec", "stack": G, "steps": args.steps, "ms_per_step": ms,
+                      "GBps": round(G * G128_BYTES / (ms * 1e-3) / 1e9, 1)}))
+
+
 def gdn_cpu_baseline(budget_s=3.0):
     """The reference's binary32 recurrence (restated in oracle/gdn_oracle.c,
     heads over pthreads as ref/gdn_err.c:447-449 does with OpenMP)."""
@@ -689,8 +726,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--stack", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["decode3", "decode4"], default=None,
-                    help="profiling aid: build one decode model, run --steps direct steps, print ms/step")
+    ap.add_argument("--only", choices=["decode3", "decode4", "matvec"], default=None,
+                    help="profiling aid: build one decode model (or the config-0 stack of --stack "
+                         "matrices), run --steps direct steps, print ms/step")
     ap.add_argument("--batch", type=int, default=1, help="sequences of the --only decode model")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -720,6 +758,9 @@ def main():
                     "d2h_bytes_per_step": 0}}))
         return
 
+    if args.only == "matvec":
+        profile_matvec(args)
+        return
     if args.only:
         profile_decode(args)
         return

@@ -342,3 +342,27 @@ def test_g128_layouts(cuda, pkg, M, K, n_rows, n_cols, accum):
         if not accum:
             e16 = np.abs(y16[i].cpu().numpy()[:n_rows].astype(np.float64) - ref)
             assert np.all(e16 <= 2.0 ** -11 * np.abs(ref) + 1e-4 * amax)
+
+
+@pytest.mark.parametrize("count", [1, 3, 5, 64])
+def test_g128_host_buffer_call_equals_device_launch(cuda, pkg, count):
+    """mv4i_g128_matvec_host (pinned host x in, host y out, the end-to-end
+    call of the benchmark) gives the device launch's fp16 results bit for bit,
+    twice in a row, for one job and for job lists of several sizes."""
+    torch = cuda
+    L = pkg.lib()
+    M, K = 512, 2048
+    wq, sc, x = _g128_operands(torch, pkg, 9, M, K, count)
+    y16, _ = _g128_run(torch, pkg, wq, sc, x, M, K)
+    mats = (pkg.DMat * count)()
+    for i in range(count):
+        assert L.mv4i_dmat_wrap_g128(_dptr(wq[i]), K // 2, _dptr(sc[i]), K // 128, M, K, 0, C.byref(mats[i])) == 0
+    hx = torch.empty((count, K), dtype=torch.float16).pin_memory()
+    hx.copy_(x.cpu())
+    hy = torch.zeros((count, M), dtype=torch.float16).pin_memory()
+    s = torch.cuda.Stream()
+    for _ in range(2):
+        hy.zero_()
+        assert L.mv4i_g128_matvec_host(mats, count, C.c_void_p(hx.data_ptr()), C.c_void_p(hy.data_ptr()),
+                                       C.c_void_p(s.cuda_stream)) == 0
+        assert np.array_equal(hy.numpy().view(np.uint16), y16.view(np.uint16))
