@@ -707,7 +707,11 @@ __device__ __forceinline__ int32_t combine_v3(const int (&a)[4], int32_t sx)
 // warp and every lane owns whole 128-column groups (GPL of them); RW rows per
 // lane segment share each x-plane load.  Tiles of 8 warps x (32/LPR) x RW
 // rows are flattened over the job list and cut into contiguous per-CTA ranges.
-template <int KIND, int RW>
+// NGPC != 0: every job of the list covers exactly NGPC = 32 groups (4096
+// columns): the plane stride, the lanes per row (32, one group each) and the
+// group loop are compile-time (shared-memory offsets become load immediates,
+// the loop and the row reduction unroll)
+template <int KIND, int RW, int NGPC = 0>
 __global__ void __launch_bounds__(MV_THREADS, RW == 4 ? 2 : V3_MINB(KIND))
 mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
 {
@@ -729,12 +733,13 @@ mv4i_v3_kernel(const __grid_constant__ LaunchParams P)
         const uint8_t *const wq = J.wq;
         const uint16_t *const scp = reinterpret_cast<const uint16_t *>(J.sc);
         const int64_t w_pitch = J.w_pitch, s_pitch = J.s_pitch;
-        const int n_rows = J.n_rows, nb = J.nb, lpr = J.lpr, mode = J.mode, out_shift = J.out_shift;
+        const int n_rows = J.n_rows, nb = NGPC ? 4 * NGPC : J.nb, lpr = NGPC ? 32 : J.lpr, mode = J.mode,
+                  out_shift = J.out_shift;
         const bool sc_vec = J.sc_vec;
         const int tile0 = J.tile0;
         const int tj_end = min(t_end, tile0 + J.ntiles);
         const int ngr = (nb + 3) >> 2;             // groups covering the job
-        const int ngp = (ngr + 3) & ~3;
+        const int ngp = NGPC ? NGPC : ((ngr + 3) & ~3);
         const int rpw = (32 / lpr) * RW;           // rows per warp per tile
         const int rpt = MV_WARPS * rpw;            // rows per tile
         uint4 *planes = reinterpret_cast<uint4 *>(smem);
@@ -1009,7 +1014,7 @@ static cudaError_t launch_one(const LaunchParams &P, int tiles, size_t smem, cud
     return cudaGetLastError();
 }
 
-template <int KIND, int RW>
+template <int KIND, int RW, int NGPC = 0>
 static cudaError_t launch_v3(const LaunchParams &P, int tiles, size_t smem, cudaStream_t st)
 {
     int dev = 0;
@@ -1018,7 +1023,7 @@ static cudaError_t launch_v3(const LaunchParams &P, int tiles, size_t smem, cuda
     if (dev >= 64) return cudaErrorInvalidDevice;
     static unsigned long long attr_set = 0;
     if (!(attr_set >> dev & 1ull)) {
-        e = cudaFuncSetAttribute(mv4i_v3_kernel<KIND, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(mv4i_v3_kernel<KIND, RW, NGPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  200 * 1024);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
@@ -1029,17 +1034,17 @@ static cudaError_t launch_v3(const LaunchParams &P, int tiles, size_t smem, cuda
     }
     int ctas = 0;
     for (int i = 0; i < g_nocc; i++)
-        if (g_occ[i].dev == dev && g_occ[i].kind == 16 + KIND && g_occ[i].rw == RW && g_occ[i].smem == smem)
+        if (g_occ[i].dev == dev && g_occ[i].kind == 16 + KIND + 8 * (NGPC != 0) && g_occ[i].rw == RW && g_occ[i].smem == smem)
             ctas = g_occ[i].ctas;
     if (!ctas) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, mv4i_v3_kernel<KIND, RW>, MV_THREADS, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, mv4i_v3_kernel<KIND, RW, NGPC>, MV_THREADS, smem);
         if (e != cudaSuccess) return e;
         if (ctas < 1) ctas = 1;
-        if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{dev, 16 + KIND, RW, smem, ctas};
+        if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{dev, 16 + KIND + 8 * (NGPC != 0), RW, smem, ctas};
     }
     int grid = g_sms[dev] * ctas;
     if (grid > tiles) grid = tiles;
-    mv4i_v3_kernel<KIND, RW><<<grid, MV_THREADS, smem, st>>>(P);
+    mv4i_v3_kernel<KIND, RW, NGPC><<<grid, MV_THREADS, smem, st>>>(P);
     return cudaGetLastError();
 }
 
@@ -1150,13 +1155,22 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
     cudaError_t e;
     if (v3) {
         const size_t ngp = (size_t)((((max_nb + 3) / 4) + 3) & ~3);
+        // every job covers exactly 32 groups with 32 lanes per row (the
+        // config-0 shape): the compile-time instance
+        int ngp_all = -1;
+        for (int i = 0; i < njobs; i++) {
+            const int gr = (P.jobs[i].nb + 3) / 4;
+            ngp_all = (ngp_all < 0 || ngp_all == gr) && gr == 32 && P.jobs[i].lpr == 32 ? gr : 0;
+        }
         const size_t smem = ngp * (256 + 16 + 4 + 16);
         switch (kind * 4 + rw) {
         case KIND_LIN * 4 + 2:  e = launch_v3<KIND_LIN, 2>(P, tiles, smem, st); break;
         case KIND_LIN * 4 + 4:  e = launch_v3<KIND_LIN, 4>(P, tiles, smem, st); break;
         case KIND_TAB * 4 + 2:  e = launch_v3<KIND_TAB, 2>(P, tiles, smem, st); break;
         case KIND_TAB * 4 + 4:  e = launch_v3<KIND_TAB, 4>(P, tiles, smem, st); break;
-        case KIND_G128 * 4 + 2: e = launch_v3<KIND_G128, 2>(P, tiles, smem, st); break;
+        case KIND_G128 * 4 + 2:
+            e = ngp_all == 32 ? launch_v3<KIND_G128, 2, 32>(P, tiles, smem, st) : launch_v3<KIND_G128, 2>(P, tiles, smem, st);
+            break;
         case KIND_G128 * 4 + 4: e = launch_v3<KIND_G128, 4>(P, tiles, smem, st); break;
         default: return -11;
         }
