@@ -1164,7 +1164,9 @@ extern "C" int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, voi
         }
         const size_t smem = ngp * (256 + 16 + 4 + 16);
         switch (kind * 4 + rw) {
-        case KIND_LIN * 4 + 2:  e = launch_v3<KIND_LIN, 2>(P, tiles, smem, st); break;
+        case KIND_LIN * 4 + 2:
+            e = ngp_all == 32 ? launch_v3<KIND_LIN, 2, 32>(P, tiles, smem, st) : launch_v3<KIND_LIN, 2>(P, tiles, smem, st);
+            break;
         case KIND_LIN * 4 + 4:  e = launch_v3<KIND_LIN, 4>(P, tiles, smem, st); break;
         case KIND_TAB * 4 + 2:  e = launch_v3<KIND_TAB, 2>(P, tiles, smem, st); break;
         case KIND_TAB * 4 + 4:  e = launch_v3<KIND_TAB, 4>(P, tiles, smem, st); break;
