@@ -159,6 +159,16 @@ int dec_set_layer_events(dec_model *m, void **events, int n);
  * synchronises the device), dec_persistent(m) tells which mode dec_step uses. */
 int dec_set_persistent(dec_model *m, int on);
 int dec_persistent(dec_model *m);
+/* Input staging in launch mode.  Every CTA of a matvec needs the whole input
+ * vector of each sequence as int16 byte planes; for a batch, building them
+ * in every CTA costs more than the weight stream.  mode 1 (the default)
+ * stages a batch's inputs once per matvec in a launch of its own that the
+ * matvec's CTAs copy from; 2 does so for single sequences too; 0 never.  The
+ * staged values are the same in every mode (bit-identical results);
+ * DEC_PRESTAGE=0|1|2 in the environment sets the mode at creation.  No
+ * counterpart in the reference (its CPU matvec stages each input once). */
+int dec_set_prestage(dec_model *m, int mode);
+
 /* Bound of each grid-barrier wait of the persistent step, in ns (0: the
  * default, one second). */
 int dec_set_wait_limit(dec_model *m, int64_t ns);

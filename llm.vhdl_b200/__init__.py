@@ -198,6 +198,7 @@ DEC_EXPORTS = {
     "dec_set_layer_events": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "dec_set_residual_seams": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "dec_set_persistent": (C.c_int, [C.c_void_p, C.c_int]),
+    "dec_set_prestage": (C.c_int, [C.c_void_p, C.c_int]),
     "dec_persistent": (C.c_int, [C.c_void_p]),
     "dec_set_clock": (C.c_int, [C.c_void_p, C.c_void_p]),
     "dec_set_wait_limit": (C.c_int, [C.c_void_p, C.c_int64]),

@@ -60,6 +60,11 @@ typedef struct {
                                       argmax key at key[b] (0 means 1)      */
     int32_t      xs;
     int32_t      pad_;
+    uint8_t     *xst;              /* optional: the inputs already staged by
+                                      dec_k_stage ([nvec] blocks of the
+                                      shared-memory layout); the matvec copies
+                                      them instead of staging (and leaves the
+                                      seam to dec_k_stage)                    */
 } dmv_params;
 
 /* the gated-attention step (dec_kernels.cu): flash decoding over chunks of
@@ -146,6 +151,11 @@ int dec_k_mega(const mg_prog *P, void *stream);
 /* Launches the decode matvec on `stream`; pdl != 0 launches it as a
  * programmatic dependent of the previous kernel in the stream. */
 int dec_k_matvec(const dmv_params *p, void *stream, int pdl);
+/* Stages the input vectors of a matvec (prologue, fp16 rounding, int16 byte
+ * planes; the seam) into p->xst once for all CTAs of the matvec that follows;
+ * dec_k_stage_bytes(K, nvec) is the size p->xst needs. */
+int dec_k_stage(const dmv_params *p, void *stream, int pdl);
+long long dec_k_stage_bytes(int K, int nvec);
 #ifdef __cplusplus
 }
 #endif

@@ -153,125 +153,152 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, const void *xv, c
     }
 }
 
-// Stage x: unit u = 8 columns per thread, so a 128-column group is 16
-// consecutive lanes (a half warp) and a 64-column pair 8 lanes: group max,
-// pair sums and per-head norms are shuffle reductions.  NV vectors (the
-// sequences of a batch; those past P.nvec are not staged and their results
-// are dropped), vector b into the shared-memory block at sm + b * xb.
+// 1 / rms of vectors b0 .. b0+NB-1 (those below P.nvec) into invs[0..NB-1]
+// (RMSNorm prologue only); every thread of the CTA calls it
+template <int NB>
+__device__ __forceinline__ void dmv_norms(const dmv_params &P, int b0, float *invs)
+{
+    __shared__ float red[DMV_WARPS * 8];
+    const int K = P.K, tid = threadIdx.x, nv = P.nvec;
+    float a[NB];
+#pragma unroll
+    for (int i = 0; i < NB; i++) {
+        const int b = b0 + i;
+        a[i] = 0.f;
+        if (b < nv) {
+            const float *x = static_cast<const float *>(P.x) + (size_t)b * P.xs;
+            for (int c = 4 * tid; c < K; c += 4 * DMV_THREADS) {
+                const float4 v = *reinterpret_cast<const float4 *>(x + c);
+                a[i] = fmaf(v.x, v.x, a[i]); a[i] = fmaf(v.y, v.y, a[i]);
+                a[i] = fmaf(v.z, v.z, a[i]); a[i] = fmaf(v.w, v.w, a[i]);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) a[i] += __shfl_xor_sync(0xffffffffu, a[i], o);
+        if ((tid & 31) == 0) red[i * DMV_WARPS + (tid >> 5)] = a[i];
+    }
+    __syncthreads();
+    if (tid < NB) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < DMV_WARPS; w++) t += red[tid * DMV_WARPS + w];
+        invs[tid] = rsqrtf(t / (float)K + P.eps);
+    }
+    __syncthreads();
+}
+
+// Stage units [u_lo, u_hi) of vector b into the block at dst (shared memory,
+// or global memory for dec_k_stage: the same layout): unit u = 8 columns per
+// thread, so a 128-column group is 16 consecutive lanes (a half warp) and a
+// 64-column pair 8 lanes: group max, pair sums and per-head norms are
+// shuffle reductions.  u_lo and u_hi are multiples of 16; every thread of
+// the CTA calls it.
+__device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float inv, uint8_t *dst, int u_lo,
+                                              int u_hi, bool seam_cta)
+{
+    const int K = P.K, np = K >> 6, tid = threadIdx.x;
+    const Sm s = sm_layout(dst, K);
+    const void *xv = P.op == DMV_OP_F16 ? static_cast<const void *>(static_cast<const uint16_t *>(P.x) + (size_t)b * P.xs)
+                                        : static_cast<const void *>(static_cast<const float *>(P.x) + (size_t)b * P.xs);
+    const float *x2v = P.x2 ? P.x2 + (size_t)b * P.xs : nullptr;
+    uint16_t *seam = P.seam ? P.seam + (size_t)b * K : nullptr;
+    uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
+    for (int u0 = u_lo; u0 < u_hi; u0 += DMV_THREADS) {    // uniform trip count: shuffles below
+        const int u = u0 + tid;
+        const bool ok = u < u_hi;                           // whole half warps
+        float v[8], z[8];
+        unit_load(P, xv, x2v, u, ok, v, z);
+        if (P.op == DMV_OP_RMSNORM) {
+            if (ok) {
+                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + 8 * u);
+                const float4 a = wp[0], c = wp[1];
+                const float w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[k] = v[k] * inv * w[k];
+            }
+        } else if (P.op == DMV_OP_GATED) {
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float ginv = rsqrtf(ss / 128.f + P.eps);
+            if (ok) {
+                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + ((8 * u) & 127));
+                const float4 a = wp[0], c = wp[1];
+                const float w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[k] = v[k] * ginv * w[k] * silu_f(z[k]);
+            }
+        }
+        // fp16 rounding (the storage contract), then the group exponent
+        uint32_t hw[4];
+        float m = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+            hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
+            const float2 f = __half22float2(h2);
+            v[2 * k] = f.x; v[2 * k + 1] = f.y;
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        int e = 0;
+        // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
+        if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
+        const float scale = exp2i(e);
+        int xi[8], ssum = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+        const int gsum = ssum + __shfl_xor_sync(0xffffffffu, ssum, 8);
+        if (ok) {
+            // byte planes by permutes: t = {x0.b0, x2.b0, x0.b1, x2.b1} and
+            // {x4.b0, x6.b0, x4.b1, x6.b1}, then their low / high halves
+            const uint32_t te0 = prmt_b(xi[0], xi[2], 0x5140u), te1 = prmt_b(xi[4], xi[6], 0x5140u);
+            const uint32_t to0 = prmt_b(xi[1], xi[3], 0x5140u), to1 = prmt_b(xi[5], xi[7], 0x5140u);
+            const uint32_t le = prmt_b(te0, te1, 0x5410u), he = prmt_b(te0, te1, 0x7632u);
+            const uint32_t lo = prmt_b(to0, to1, 0x5410u), ho = prmt_b(to0, to1, 0x7632u);
+            const int c = u >> 2, q = u & 3, p = c >> 1, par = c & 1;
+            pw[4 * ((0 + par) * np + p) + q] = le;
+            pw[4 * ((2 + par) * np + p) + q] = lo;
+            pw[4 * ((4 + par) * np + p) + q] = he;
+            pw[4 * ((6 + par) * np + p) + q] = ho;
+            if (!(u & 7)) s.psum[u >> 3] = ssum;
+            if (!(u & 15)) {
+                s.gfac[u >> 4] = exp2i(-e);
+                s.gs[u >> 4] = make_int2(gsum, __float_as_int(exp2i(-e)));
+            }
+            if (seam_cta && seam)
+                *reinterpret_cast<uint4 *>(seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+    }
+}
+
+// Stage x: NV vectors (the sequences of a batch; those past P.nvec are not
+// staged and their results are dropped), vector b into the shared-memory
+// block at sm + b * xb.
 template <int NV>
 __device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb, bool seam_cta)
 {
-    __shared__ float red[DMV_WARPS * 8];
     __shared__ float invs[8];
-    const int K = P.K, np = K >> 6, nu = K >> 3, tid = threadIdx.x, nv = P.nvec;
-    if (P.op == DMV_OP_RMSNORM) {
-        float a[NV];
-#pragma unroll
-        for (int b = 0; b < NV; b++) {
-            a[b] = 0.f;
-            if (b < nv) {
-                const float *x = static_cast<const float *>(P.x) + (size_t)b * P.xs;
-                for (int i = 4 * tid; i < K; i += 4 * DMV_THREADS) {
-                    const float4 v = *reinterpret_cast<const float4 *>(x + i);
-                    a[b] = fmaf(v.x, v.x, a[b]); a[b] = fmaf(v.y, v.y, a[b]);
-                    a[b] = fmaf(v.z, v.z, a[b]); a[b] = fmaf(v.w, v.w, a[b]);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) a[b] += __shfl_xor_sync(0xffffffffu, a[b], o);
-            if ((tid & 31) == 0) red[b * DMV_WARPS + (tid >> 5)] = a[b];
-        }
-        __syncthreads();
-        if (tid < NV) {
-            float t = 0.f;
-#pragma unroll
-            for (int w = 0; w < DMV_WARPS; w++) t += red[tid * DMV_WARPS + w];
-            invs[tid] = rsqrtf(t / (float)K + P.eps);
-        }
-        __syncthreads();
-    }
+    if (P.op == DMV_OP_RMSNORM) dmv_norms<NV>(P, 0, invs);
 #pragma unroll 1
-    for (int b = 0; b < NV && b < nv; b++) {
-        const Sm s = sm_layout(sm + b * xb, K);
-        const float inv = P.op == DMV_OP_RMSNORM ? invs[b] : 0.f;
-        const void *xv = P.op == DMV_OP_F16 ? static_cast<const void *>(static_cast<const uint16_t *>(P.x) + (size_t)b * P.xs)
-                                            : static_cast<const void *>(static_cast<const float *>(P.x) + (size_t)b * P.xs);
-        const float *x2v = P.x2 ? P.x2 + (size_t)b * P.xs : nullptr;
-        uint16_t *seam = P.seam ? P.seam + (size_t)b * K : nullptr;
-        uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
-        for (int u0 = 0; u0 < nu; u0 += DMV_THREADS) {        // uniform trip count: shuffles below
-            const int u = u0 + tid;
-            const bool ok = u < nu;                             // whole half warps (nu % 16 == 0)
-            float v[8], z[8];
-            unit_load(P, xv, x2v, u, ok, v, z);
-            if (P.op == DMV_OP_RMSNORM) {
-                if (ok) {
-                    const float4 *wp = reinterpret_cast<const float4 *>(P.nw + 8 * u);
-                    const float4 a = wp[0], c = wp[1];
-                    const float w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-                    for (int k = 0; k < 8; k++) v[k] = v[k] * inv * w[k];
-                }
-            } else if (P.op == DMV_OP_GATED) {
-                float ss = 0.f;
-#pragma unroll
-                for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
-#pragma unroll
-                for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                const float ginv = rsqrtf(ss / 128.f + P.eps);
-                if (ok) {
-                    const float4 *wp = reinterpret_cast<const float4 *>(P.nw + ((8 * u) & 127));
-                    const float4 a = wp[0], c = wp[1];
-                    const float w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-                    for (int k = 0; k < 8; k++) v[k] = v[k] * ginv * w[k] * silu_f(z[k]);
-                }
-            }
-            // fp16 rounding (the storage contract), then the group exponent
-            uint32_t hw[4];
-            float m = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-                hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
-                const float2 f = __half22float2(h2);
-                v[2 * k] = f.x; v[2 * k + 1] = f.y;
-                m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-            }
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            int e = 0;
-            // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
-            if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
-            const float scale = exp2i(e);
-            int xi[8], ssum = 0;
-#pragma unroll
-            for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-            const int gsum = ssum + __shfl_xor_sync(0xffffffffu, ssum, 8);
-            if (ok) {
-                // byte planes by permutes: t = {x0.b0, x2.b0, x0.b1, x2.b1} and
-                // {x4.b0, x6.b0, x4.b1, x6.b1}, then their low / high halves
-                const uint32_t te0 = prmt_b(xi[0], xi[2], 0x5140u), te1 = prmt_b(xi[4], xi[6], 0x5140u);
-                const uint32_t to0 = prmt_b(xi[1], xi[3], 0x5140u), to1 = prmt_b(xi[5], xi[7], 0x5140u);
-                const uint32_t le = prmt_b(te0, te1, 0x5410u), he = prmt_b(te0, te1, 0x7632u);
-                const uint32_t lo = prmt_b(to0, to1, 0x5410u), ho = prmt_b(to0, to1, 0x7632u);
-                const int c = u >> 2, q = u & 3, p = c >> 1, par = c & 1;
-                pw[4 * ((0 + par) * np + p) + q] = le;
-                pw[4 * ((2 + par) * np + p) + q] = lo;
-                pw[4 * ((4 + par) * np + p) + q] = he;
-                pw[4 * ((6 + par) * np + p) + q] = ho;
-                if (!(u & 7)) s.psum[u >> 3] = ssum;
-                if (!(u & 15)) {
-                    s.gfac[u >> 4] = exp2i(-e);
-                    s.gs[u >> 4] = make_int2(gsum, __float_as_int(exp2i(-e)));
-                }
-                if (seam_cta && seam)
-                    *reinterpret_cast<uint4 *>(seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            }
-        }
-    }
+    for (int b = 0; b < NV && b < P.nvec; b++)
+        dmv_stage_vec(P, b, P.op == DMV_OP_RMSNORM ? invs[b] : 0.f, sm + b * xb, 0, P.K >> 3, seam_cta);
+    __syncthreads();
+}
+
+// The blocks dec_k_stage wrote (vectors 0 .. nvs-1, contiguous) into shared
+// memory: 16-byte asynchronous copies, all in flight at once.
+__device__ __forceinline__ void dmv_load_staged(const uint8_t *src, uint8_t *sm, size_t bytes)
+{
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(sm);
+    for (size_t i = 16 * (size_t)threadIdx.x; i < bytes; i += 16 * DMV_THREADS)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(base + (uint32_t)i), "l"(src + i) : "memory");
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 }
 
@@ -736,7 +763,8 @@ __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, i
     if (t0 >= t1) return;                               // uniform over the CTA
 
     const size_t xb = dmv_smem_x_bytes(K);
-    dmv_stage<NV>(P, dmv_sm, xb, t0 == 0);               // the first CTA with tiles writes the seam
+    if (P.xst) dmv_load_staged(P.xst, dmv_sm, xb * (size_t)min(NV, P.nvec));
+    else dmv_stage<NV>(P, dmv_sm, xb, t0 == 0);        // the first CTA with tiles writes the seam
 
     unsigned long long best[2] = {0, 0};
     for (int j = j0; j < P.njobs; j++) {
@@ -770,6 +798,23 @@ __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, i
     }
 }
 
+// The input staging of a matvec as a launch of its own (dec_k_stage): CTA
+// (cx, b) stages units [256 cx, 256 cx + 256) of vector b into the global
+// block P.xst + b * xb, and every CTA of the matvec that follows copies the
+// blocks (dmv_load_staged) instead of staging all vectors itself.  Same
+// arithmetic as the in-CTA staging (bit-identical blocks).
+__global__ void __launch_bounds__(DMV_THREADS) dmv_stage_kernel(const __grid_constant__ dmv_params P)
+{
+    __shared__ float invs[1];
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.y;
+    if (P.op == DMV_OP_RMSNORM) dmv_norms<1>(P, b, invs);
+    const int nu = P.K >> 3, u_lo = blockIdx.x * DMV_THREADS;
+    dmv_stage_vec(P, b, P.op == DMV_OP_RMSNORM ? invs[0] : 0.f, P.xst + (size_t)b * dmv_smem_x_bytes(P.K), u_lo,
+                  min(nu, u_lo + DMV_THREADS), true);
+}
+
 template <int NV>
 __global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid_constant__ dmv_params P)
 {
@@ -780,14 +825,22 @@ __global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid
 // Validates a parameter block and sets its launch-dependent fields (tiles
 // and the column split) for `slots` CTAs; returns the dynamic shared memory
 // the kernel needs, or a negative status.
-static long long dmv_prepare(dmv_params &P, int slots)
+// the input side of a parameter block (prologue, vectors, staged blocks)
+static int dmv_check_input(dmv_params &P)
 {
-    if (P.njobs < 1 || P.njobs > DMV_MAXJ || P.K < 128 || (P.K & 127) || P.K > 32768 || !P.x) return -11;
+    if (P.K < 128 || (P.K & 127) || P.K > 32768 || !P.x) return -11;
     if (P.op == DMV_OP_RMSNORM && !P.nw) return -11;
     if (P.op == DMV_OP_GATED && (!P.nw || !P.x2)) return -11;
     if (P.op < DMV_OP_F16 || P.op > DMV_OP_GATED) return -11;
     if (P.nvec <= 0) P.nvec = 1;
     if (P.nvec > 8 || (P.nvec > 1 && P.xs < P.K) || (P.xs & 7)) return -11;
+    if (((uintptr_t)P.xst) & 15) return -11;
+    return 0;
+}
+
+static long long dmv_prepare(dmv_params &P, int slots)
+{
+    if (P.njobs < 1 || P.njobs > DMV_MAXJ || dmv_check_input(P)) return -11;
     const bool mma = P.nvec > 1;
     const int NV = P.nvec == 1 ? 1 : P.nvec == 2 ? 2 : P.nvec <= 4 ? 4 : 8;
     const size_t smem = (size_t)NV * dmv_smem_x_bytes(P.K);
@@ -890,6 +943,33 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
     cfg.numAttrs = pdl ? 1 : 0;
     void *args[] = {&P};
     e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
+    return 0;
+}
+
+extern "C" long long dec_k_stage_bytes(int K, int nvec)
+{
+    if (K < 128 || (K & 127) || K > 32768 || nvec < 1 || nvec > 8) return -11;
+    return (long long)nvec * (long long)dmv_smem_x_bytes(K);
+}
+
+extern "C" int dec_k_stage(const dmv_params *p, void *stream, int pdl)
+{
+    if (!p || !p->xst) return -11;
+    dmv_params P = *p;
+    if (dmv_check_input(P)) return -11;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(((P.K >> 3) + DMV_THREADS - 1) / DMV_THREADS), (unsigned)P.nvec);
+    cfg.blockDim = dim3(DMV_THREADS);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void *args[] = {&P};
+    const cudaError_t e = cudaLaunchKernelExC(&cfg, (const void *)dmv_stage_kernel, args);
     if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
     return 0;
 }

@@ -99,6 +99,10 @@ struct dec_model {
     /* the persistent kernel's program (single GPU) */
     mg_prog   mg;
     int       persistent, mega_ok;
+    /* launch mode: inputs staged once per matvec by a launch of their own
+     * (0 never, 1 batches of 2+ sequences, 2 always) into xst */
+    int       prestage;
+    uint8_t  *xst;
     int32_t  *layer_clock;               /* [n_layers + 1]: clock index at each layer's end */
     void     *allocs[MAX_ALLOCS];
     int       nalloc;
@@ -283,6 +287,17 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     TRY(dalloc(m, (void **)&m->ak_epoch, 16));
     TRY(dalloc(m, (void **)&m->err, 16));
     TRY(dalloc(m, (void **)&m->prompt, 4 * ((size_t)c->max_ctx * B + 1)));
+    {
+        /* the staged inputs of the widest matvec input */
+        int kx = mx;
+        if (m->vh * HD > kx) kx = m->vh * HD;
+        if (m->qh * HD > kx) kx = m->qh * HD;
+        const long long xb = dec_k_stage_bytes(kx, m->B);
+        if (xb < 0) { rc = -11; goto bad; }
+        TRY(dalloc(m, (void **)&m->xst, (size_t)xb));
+        const char *ps = getenv("DEC_PRESTAGE");
+        m->prestage = ps && ps[0] >= '0' && ps[0] <= '2' ? ps[0] - '0' : 1;
+    }
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { rc = fail(e); goto bad; }
     m->layer_clock = (int32_t *)calloc((size_t)c->n_layers + 1, sizeof(int32_t));
@@ -526,6 +541,15 @@ static mg_stage *em_new(emit_t *E, int op, int sync)
 
 static int em_matvec(emit_t *E, const dmv_params *P)
 {
+    dec_model *m = E->m;
+    if (!E->rec && m->xst && (m->prestage == 2 || (m->prestage == 1 && m->B > 1))) {
+        /* every CTA of the matvec would stage all the batch's vectors: stage
+         * them once, the matvec's CTAs copy the blocks */
+        dmv_params Q = *P;
+        Q.xst = m->xst;
+        CK(dec_k_stage(&Q, E->s, E->pdl));
+        return dec_k_matvec(&Q, E->s, E->pdl);
+    }
     if (!E->rec) return dec_k_matvec(P, E->s, E->pdl);
     mg_stage *st = em_new(E, MG_MATVEC, 1);
     if (!st) return -11;
@@ -740,6 +764,13 @@ int dec_set_persistent(dec_model *m, int on)
     if (on && m->world != 1) return -11;
     m->persistent = on != 0;
     if (m->persistent && !m->mega_ok) CK(mega_build(m));
+    return 0;
+}
+
+int dec_set_prestage(dec_model *m, int mode)
+{
+    if (!m || mode < 0 || mode > 2) return -11;
+    m->prestage = mode;
     return 0;
 }
 

@@ -41,7 +41,8 @@ class Params(C.Structure):
     _fields_ = [("jobs", Job * 4), ("njobs", C.c_int32), ("total_tiles", C.c_int32), ("K", C.c_int32),
                 ("op", C.c_int32), ("x", P_), ("x2", P_), ("nw", P_), ("eps", C.c_float), ("seam", P_),
                 ("key", P_), ("idx0", C.c_int32), ("pf_bytes", C.c_int32), ("ksplit", C.c_int32),
-                ("nvec", C.c_int32), ("xs", C.c_int32), ("pad_", C.c_int32)]
+                ("nvec", C.c_int32), ("xs", C.c_int32), ("pad_", C.c_int32),
+                ("xst", C.c_void_p)]
 
 
 @pytest.fixture(scope="module")
@@ -490,3 +491,71 @@ def test_batch_argmax_keys(cuda, L, O):
         want = int(np.flatnonzero(lg[b] == lg[b].max())[0])
         assert 0xFFFFFFFF - (int(key[b].item()) & 0xFFFFFFFF) == 100 + want, b
     assert 0xFFFFFFFF - (int(key[1].item()) & 0xFFFFFFFF) == 100 + min(e, top1)
+
+
+@pytest.mark.parametrize("op", ["F16", "RMSNORM", "GATED"])
+@pytest.mark.parametrize("nv,K", [(1, 2048), (3, 2048), (8, 2048), (8, 6144), (2, 17408)])
+def test_prestaged_inputs_equal_in_cta_staging(cuda, L, O, op, nv, K):
+    """dec_k_stage stages the inputs once into a global block and the matvec
+    copies it: the same arithmetic as staging in every CTA, so outputs and
+    seams are bit-identical; chained as programmatic dependents too."""
+    torch = cuda
+    L.dec_k_stage.argtypes = [C.POINTER(Params), P_, C.c_int]
+    L.dec_k_stage.restype = C.c_int
+    L.dec_k_stage_bytes.argtypes = [C.c_int, C.c_int]
+    L.dec_k_stage_bytes.restype = C.c_longlong
+    rows = 1000
+    wq, sc = weights(torch, rows, K, 7 * K + nv)
+    g = torch.Generator().manual_seed(K + 13 * nv)
+    xs_ = K + 64
+    if op == "F16":
+        x = (torch.randn(nv, xs_, generator=g) * torch.exp2(torch.randint(-8, 3, (nv, xs_), generator=g).float())).half().cuda()
+    else:
+        x = (torch.randn(nv, xs_, generator=g) * (1 + torch.arange(nv).float()[:, None])).cuda()
+    z = (2 * torch.randn(nv, xs_, generator=g)).cuda()
+    w = (1 + 0.1 * torch.randn(K, generator=g)).cuda()
+    nbytes = L.dec_k_stage_bytes(K, nv)
+    assert nbytes > 0
+    xst = torch.zeros(nbytes // 4 + 4, dtype=torch.int32, device="cuda")
+    outs = []
+    for mode in range(3):
+        y = torch.zeros(nv, rows, device="cuda")
+        acc = torch.ones(nv, rows, device="cuda")
+        seam = torch.zeros(nv, K, dtype=torch.int16, device="cuda")
+        p = Params(K=K, op=OP[op], x=dp(x), x2=dp(z) if op == "GATED" else None, nw=dp(w), eps=1e-6,
+                   seam=dp(seam), njobs=2, nvec=nv, xs=xs_, pf_bytes=65536)
+        p.jobs[0] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["F32"], out_f32=dp(y), ostride=rows)
+        p.jobs[1] = Job(s_pitch=spitch(K), wq=dp(wq), sc=dp(sc), rows=rows, epi=EPI["ACC"], out_f32=dp(acc),
+                        ostride=rows)
+        if mode:
+            xst.zero_()
+            p.xst = dp(xst)
+            assert L.dec_k_stage(C.byref(p), None, mode - 1) == 0
+            assert L.dec_k_matvec(C.byref(p), None, mode - 1) == 0
+        else:
+            assert L.dec_k_matvec(C.byref(p), None, 0) == 0
+        torch.cuda.synchronize()
+        outs.append((y.cpu().numpy(), acc.cpu().numpy(), seam.cpu().numpy()))
+    for mode in (1, 2):
+        for a, b in zip(outs[0], outs[mode]):
+            assert np.array_equal(a, b), mode
+    # and the staged product itself against the oracle (vector nv - 1)
+    W = deq(O, wq, sc)
+    s16 = outs[0][2][nv - 1].view(np.float16)
+    assert rel(outs[1][0][nv - 1].astype(np.float64), staged_ref(O, W, s16)) <= 2e-6
+
+
+def test_stage_refusals(cuda, L):
+    torch = cuda
+    L.dec_k_stage.argtypes = [C.POINTER(Params), P_, C.c_int]
+    L.dec_k_stage.restype = C.c_int
+    L.dec_k_stage_bytes.argtypes = [C.c_int, C.c_int]
+    L.dec_k_stage_bytes.restype = C.c_longlong
+    x = torch.zeros(2048, dtype=torch.float16, device="cuda")
+    buf = torch.zeros(8192, dtype=torch.int32, device="cuda")
+    assert L.dec_k_stage(C.byref(Params(K=2048, op=OP["F16"], x=dp(x))), None, 0) == -11          # no block
+    assert L.dec_k_stage(C.byref(Params(K=2000, op=OP["F16"], x=dp(x), xst=dp(buf))), None, 0) == -11
+    assert L.dec_k_stage(C.byref(Params(K=2048, op=OP["F16"], x=dp(x), xst=dp(buf) + 4)), None, 0) == -11
+    assert L.dec_k_stage(C.byref(Params(K=2048, op=OP["RMSNORM"], x=dp(x), xst=dp(buf))), None, 0) == -11
+    assert L.dec_k_stage_bytes(2048, 9) < 0 and L.dec_k_stage_bytes(100, 1) < 0
+    torch.cuda.synchronize()
