@@ -100,3 +100,25 @@ def test_decode_bad_configs_are_refused_before_any_cuda_call(pkg):
     assert L.dec_create(C.byref(pkg.DecConfig(**cfg0)), 1, 0, 0, 8, C.byref(h)) == -11   # 4 kv heads
     # batches are single-GPU
     assert L.dec_create(C.byref(pkg.DecConfig(**dict(cfg0, batch=2))), 1, 0, 0, 2, C.byref(h)) == -11
+
+
+def test_batch_input_staging_host_checks(pkg):
+    """The batch input-staging pieces refuse bad arguments on the host: the
+    mode setter (no model, mode out of range) and the staged-block size
+    (K a multiple of 128 up to 32768, 1-8 vectors), whose value is the
+    per-vector shared-memory block of the decode matvec times the vectors."""
+    L = pkg.declib()
+    assert L.dec_set_prestage(None, 1) == -11
+    L.dec_k_stage_bytes.argtypes = [C.c_int, C.c_int]
+    L.dec_k_stage_bytes.restype = C.c_longlong
+    L.dec_k_stage.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    L.dec_k_stage.restype = C.c_int
+    r16 = lambda n: (n + 15) & ~15
+    for K in (128, 2048, 6144, 17408, 32768):
+        npair, ng = K // 64, K // 128
+        block = 128 * npair + r16(4 * npair) + r16(4 * ng) + r16(8 * ng)
+        for nv in (1, 3, 8):
+            assert L.dec_k_stage_bytes(K, nv) == nv * block, (K, nv)
+    for K, nv in [(100, 1), (2000, 1), (32896, 1), (2048, 0), (2048, 9)]:
+        assert L.dec_k_stage_bytes(K, nv) < 0, (K, nv)
+    assert L.dec_k_stage(None, None, 0) == -11
