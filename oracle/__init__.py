@@ -17,7 +17,8 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_TREE = os.environ.get("LLMVHDL_REF", "/root/reference")
+# the llm.vhdl tree: $LLMVHDL_REF, else the directory `reference` beside this repository
+REF_TREE = os.environ.get("LLMVHDL_REF") or os.path.normpath(os.path.join(HERE, "..", "..", "reference"))
 LIB = os.path.join(HERE, "liboracle.so")
 REFLIB = os.path.join(HERE, "_ref", "libref_mv4i.so")
 REFBIN = os.path.join(HERE, "_ref", "matvec_int4")
@@ -312,3 +313,209 @@ def argmax_first(v):
     """ref/run9b.c:399-405: the first maximum wins."""
     v = np.asarray(v)
     return int(np.flatnonzero(v == v.max())[0])
+
+
+# ---------------------------------------------- DeltaNet block (fixed point)
+
+class Blk(C.Structure):
+    """Field for field the caller-owned block record of ref/gdn_block_vec.c:183-202
+    (also oracle/gdn_block_oracle.c's orc_blk and the library's gdn_blk_t)."""
+    _fields_ = [("xtap", C.c_void_p), ("wtap", C.c_void_p), ("e_t", C.c_void_p),
+                ("tvalid", C.c_void_p), ("cw_exp", C.c_void_p), ("sc", C.c_void_p),
+                ("zm", C.c_void_p), ("wm", C.c_void_p), ("w_e", C.c_int), ("z_e", C.c_int),
+                ("tk0", C.c_int), ("smem", C.c_void_p), ("semem", C.c_void_p), ("y", C.c_void_p),
+                ("y_exp", C.c_int), ("err_conv", C.c_int), ("err_g", C.c_int), ("err_se", C.c_int),
+                ("y_sat", C.c_int)]
+
+
+def _blk_sig():
+    L = _gdn_sig()
+    if getattr(L, "_blk_bound", False):
+        return L
+    sig = {
+        "orc_rsqrt_rom": (None, [C.c_void_p]),
+        "orc_to_q12": (C.c_int32, [C.c_int64, C.c_int]),
+        "orc_sigma_q15": (C.c_int32, [C.c_int32]),
+        "orc_silu": (C.c_int32, [C.c_int32, C.c_int]),
+        "orc_conv_seg": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "orc_l2norm_rs": (None, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+        "orc_rmsnorm_bf": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_double,
+                                     C.c_void_p, C.POINTER(C.c_int)]),
+        "orc_y_emit": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.POINTER(C.c_int)]),
+        "orc_emit_chain": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
+        "orc_gdn_block_token": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(Blk)]),
+    }
+    for n, (res, args) in sig.items():
+        f = getattr(L, n)
+        f.restype, f.argtypes = res, args
+    L._blk_bound = True
+    return L
+
+
+def _ref_blk():
+    R = ref_gdn()
+    if not getattr(R, "_blk_bound", False):
+        R.ref_gdn_block_token.restype = None
+        R.ref_gdn_block_token.argtypes = [C.c_int, C.c_int, C.c_int, C.POINTER(Blk)]
+        R.ref_l2norm_rs.restype = None
+        R.ref_rsqrt_rom.argtypes = [C.c_void_p]
+        R.ref_l2norm_rs.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        R.ref_rmsnorm_bf.restype = C.c_int
+        R.ref_rmsnorm_bf.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                     C.POINTER(C.c_int)]
+        R.ref_silu.restype = C.c_int
+        R.ref_silu.argtypes = [C.c_int, C.c_int]
+        R._blk_bound = True
+    return R
+
+
+def conv_seg(x, w, e_t, tv, cw_exp):
+    """x, w [nch][4] int16 -> (sm[nch] int16, e_seg, sh_seg, err)."""
+    L = _blk_sig()
+    x = np.ascontiguousarray(x, np.int16)
+    w = np.ascontiguousarray(w, np.int16)
+    sm = np.zeros(x.shape[0], np.int16)
+    es, ss = C.c_int(0), C.c_int(0)
+    err = L.orc_conv_seg(x.shape[0], _p(x), _p(w), _p(np.ascontiguousarray(e_t, np.int32)),
+                         _p(np.ascontiguousarray(tv, np.int32)), int(cw_exp), _p(sm), C.byref(es),
+                         C.byref(ss))
+    return sm, es.value, ss.value, err
+
+
+def l2norm_rs(x, log2n, use_ref=False):
+    x = np.ascontiguousarray(x, np.int32)
+    k = np.zeros(x.size, np.int32)
+    q = np.zeros(x.size, np.int32)
+    (_ref_blk().ref_l2norm_rs if use_ref else _blk_sig().orc_l2norm_rs)(_p(x), x.size, log2n, _p(k), _p(q))
+    return k, q
+
+
+def rmsnorm_bf(xm, xe, wm, we, use_ref=False):
+    xm = np.ascontiguousarray(xm, np.int16)
+    wm = np.ascontiguousarray(wm, np.int16)
+    o = np.zeros(xm.size, np.int16)
+    oe = C.c_int(0)
+    if use_ref:
+        _ref_blk().ref_rmsnorm_bf(_p(xm), int(xe), _p(wm), int(we), xm.size, _p(o), C.byref(oe))
+    else:
+        _blk_sig().orc_rmsnorm_bf(_p(xm), int(xe), _p(wm), int(we), xm.size, 1.0e-6, _p(o), C.byref(oe))
+    return o, oe.value
+
+
+def y_emit(ep, po, pz):
+    """ep [H]; po, pz [H][D] int16 -> (y [H*D], y_exp, sat)."""
+    L = _blk_sig()
+    po = np.ascontiguousarray(po, np.int16)
+    pz = np.ascontiguousarray(pz, np.int16)
+    H, D = po.shape
+    y = np.zeros(H * D, np.int16)
+    ye = C.c_int(0)
+    sat = L.orc_y_emit(H, D, _p(np.ascontiguousarray(ep, np.int32)), _p(po), _p(pz), _p(y), C.byref(ye))
+    return y, ye.value, sat
+
+
+def emit_chain(o_acc, e_o, zm, wm, we, z_e):
+    """o_acc int64 / e_o / zm [H][D] -> (y [H*D], y_exp, sat)."""
+    L = _blk_sig()
+    o_acc = np.ascontiguousarray(o_acc, np.int64)
+    H, D = o_acc.shape
+    y = np.zeros(H * D, np.int16)
+    ye = C.c_int(0)
+    sat = L.orc_emit_chain(H, D, _p(o_acc), _p(np.ascontiguousarray(e_o, np.int32)),
+                           _p(np.ascontiguousarray(zm, np.int16)), _p(np.ascontiguousarray(wm, np.int16)),
+                           int(we), int(z_e), _p(y), C.byref(ye))
+    return y, ye.value, sat
+
+
+def blk_taps(t, caps):
+    """Tap exponents and validity of token t (ref/gdn_block_vec.c:657-669):
+    tap 3 is the current token, tap k refers to token t-(3-k); a tap before
+    the sequence start is invalid and carries the exponent -47.
+    caps [T][3] are the per-token captured segment exponents."""
+    n = min(t + 1, 4)
+    e_t = np.zeros((3, 4), np.int32)
+    tv = np.zeros((3, 4), np.int32)
+    for s in range(3):
+        for k in range(4):
+            src = t - (3 - k)
+            ok = k >= 4 - n
+            tv[s, k] = ok
+            e_t[s, k] = caps[src][s] if ok else -47
+    return e_t, tv
+
+
+def gdn_block_run(KH, VH, D, stim, smem, semem, use_ref=False):
+    """Run len(stim['xtap']) tokens through the oracle (or the reference's own
+    gdn_block_token).  smem [VH][D][D] int16 and semem [VH][D] int32 are
+    updated in place.  Returns y [T][VH*D], y_exp [T], flags [T][4]."""
+    fn = _ref_blk().ref_gdn_block_token if use_ref else _blk_sig().orc_gdn_block_token
+    T = stim["xtap"].shape[0]
+    ys = np.zeros((T, VH * D), np.int16)
+    yexp = np.zeros(T, np.int32)
+    flags = np.zeros((T, 4), np.int32)
+    wtap = np.ascontiguousarray(stim["wtap"], np.int16)
+    cw = np.ascontiguousarray(stim["cw_exp"], np.int32)
+    wm = np.ascontiguousarray(stim["wm"], np.int16)
+    assert smem.dtype == np.int16 and semem.dtype == np.int32
+    assert smem.flags.c_contiguous and semem.flags.c_contiguous
+    for t in range(T):
+        keep = [np.ascontiguousarray(stim[k][t], dt) for k, dt in
+                (("xtap", np.int16), ("e_t", np.int32), ("tvalid", np.int32), ("sc", np.int32),
+                 ("zm", np.int16))]
+        b = Blk()
+        b.xtap, b.wtap, b.e_t, b.tvalid = keep[0].ctypes.data, wtap.ctypes.data, keep[1].ctypes.data, \
+            keep[2].ctypes.data
+        b.cw_exp, b.sc, b.zm, b.wm = cw.ctypes.data, keep[3].ctypes.data, keep[4].ctypes.data, wm.ctypes.data
+        b.w_e, b.z_e, b.tk0 = int(stim["w_e"]), int(stim["z_e"]), int(stim["tk0"][t])
+        b.smem, b.semem, b.y = smem.ctypes.data, semem.ctypes.data, ys[t].ctypes.data
+        rc = fn(KH, VH, D, C.byref(b))
+        assert rc in (None, 0), rc
+        yexp[t] = b.y_exp
+        flags[t] = (b.err_conv, b.err_g, b.err_se, b.y_sat)
+    return ys, yexp, flags
+
+
+def gdn_block_stimulus(KH, VH, D, T, seed):
+    """Seeded block stimulus in the reference generator's ranges
+    (ref/gdn_block_vec.c:570-618): conv weights and history in +-2047, segment
+    exponents 11..13, capture exponents 8..12, norm weights 2000..6000 on 12,
+    the scalar-path inputs in the physical band, z in +-8192 on 12, masked taps
+    filled with garbage.  Returns (stim, smem, semem)."""
+    rng = np.random.default_rng(seed)
+    CH = 2 * KH * D + VH * D
+    hist = rng.integers(-2047, 2048, (T, CH), dtype=np.int64).astype(np.int16)
+    caps = [[8 + (t + s) % 5 for s in range(3)] for t in range(T)]
+    stim = dict(wtap=rng.integers(-2047, 2048, (CH, 4)).astype(np.int16),
+                cw_exp=np.array([11, 12, 13], np.int32),
+                wm=rng.integers(2000, 6001, D).astype(np.int16), w_e=12, z_e=12,
+                tk0=np.array([1] + [0] * (T - 1), np.int32))
+    xt = np.zeros((T, CH, 4), np.int16)
+    et = np.zeros((T, 3, 4), np.int32)
+    tv = np.zeros((T, 3, 4), np.int32)
+    for t in range(T):
+        et[t], tv[t] = blk_taps(t, caps)
+        for k in range(4):
+            src = t - (3 - k)
+            if src >= 0:
+                xt[t, :, k] = hist[src]
+            else:
+                xt[t, :, k] = (-30000 + ((np.arange(CH) * 7 + k * 13) % 60000)).astype(np.int16)
+    sc = np.zeros((T, VH, 8), np.int32)
+    sc[:, :, 0] = rng.integers(-1000, 1001, (T, VH)); sc[:, :, 1] = 14
+    sc[:, :, 2] = -rng.integers(2000, 32001, (T, VH)); sc[:, :, 3] = 12
+    sc[:, :, 4] = -rng.integers(1, 3001, (T, VH)); sc[:, :, 5] = 16
+    sc[:, :, 6] = rng.integers(-30000, 30001, (T, VH)); sc[:, :, 7] = 12
+    stim.update(xtap=xt, e_t=et, tvalid=tv, sc=sc,
+                zm=rng.integers(-8192, 8193, (T, VH, D)).astype(np.int16))
+    smem = np.zeros((VH, D, D), np.int16)
+    semem = np.zeros((VH, D), np.int32)
+    for h in range(VH):
+        for j in range(D):
+            top = int(rng.integers(16384, 32768))
+            smem[h, j] = rng.integers(-top, top + 1, D)
+            smem[h, j, rng.integers(0, D)] = top
+            semem[h, j] = 9 + (h + j) % 4
+    return stim, smem, semem

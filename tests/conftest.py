@@ -9,7 +9,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 GOLDEN = os.path.join(ROOT, "tests", "golden")
-REF_TREE = os.environ.get("LLMVHDL_REF", "/root/reference")
+# the llm.vhdl tree: $LLMVHDL_REF, else the directory `reference` beside this repository
+REF_TREE = os.environ.get("LLMVHDL_REF") or os.path.normpath(os.path.join(ROOT, "..", "reference"))
 
 
 def pytest_configure(config):

@@ -11,7 +11,7 @@ import pytest
 
 import oracle as O
 
-REF_TREE = os.environ.get("LLMVHDL_REF", "/root/reference")
+from conftest import REF_TREE  # noqa: E402
 
 
 def _img_for(golden, key):
