@@ -15,6 +15,7 @@
 #ifndef GDN_B200_H
 #define GDN_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -88,6 +89,110 @@ typedef struct {
 } gdn_f32_args;
 
 int gdn_run_f32(const gdn_f32_args *a, void *stream);
+
+/* ------------------------------------------------ the fixed-point block */
+
+/* Field for field the caller-owned block record of the reference,
+ * blk_t (ref/gdn_block_vec.c:183-202), in HOST memory:
+ *   xtap, wtap [2*KH*D + VH*D][4]  conv taps (tap 3 = this token) and weights,
+ *                                  channels [q | k | v], head-major
+ *   e_t, tvalid [3][4]             per segment: tap exponents, tap validity
+ *   cw_exp [3]                     conv weight exponent per segment
+ *   sc [VH][8]                     {al_m, al_e, dt_m, dt_e, a_m, a_e, b_m, b_e}
+ *   zm [VH][D] on z_e              the z gate input
+ *   wm [D] on w_e                  the output rmsnorm weights
+ *   tk0                            first token (state taken as zero)
+ *   smem [VH][D][D], semem [VH][D] state mantissas / column exponents, in place
+ *   y [VH*D], y_exp                output mantissas and the token exponent
+ *   err_conv, err_g, err_se, y_sat range flags: set to 1, never cleared       */
+typedef struct {
+    const int16_t *xtap;
+    const int16_t *wtap;
+    const int     *e_t;
+    const int     *tvalid;
+    const int     *cw_exp;
+    const int32_t *sc;
+    const int16_t *zm;
+    const int16_t *wm;
+    int            w_e, z_e;
+    int            tk0;
+    int16_t       *smem;
+    int           *semem;
+    int16_t       *y;
+    int            y_exp;
+    int            err_conv, err_g, err_se, y_sat;
+} gdn_blk_t;
+
+/* Replaces gdn_block_token (ref/gdn_block_vec.c:208-423), whose shape comes
+ * from the file globals KH, VH, D (:138) -- here arguments.  One token of the
+ * fixed-point Gated DeltaNet block, bit-exact: conv + segment requantiser,
+ * silu, per-key-head L2 norms, scalar path, recurrence, site-12 head emit,
+ * output rmsnorm_bf (eps 1e-6), z gate, site-13 whole-token renorm.  Value
+ * head h reads key head h % KH.  D is 32, 64 or 128; VH a multiple of KH.
+ * Host buffers: the record is staged through device memory on every call
+ * (the drop-in form; deltanet_step keeps everything resident).  Returns 0,
+ * -11 (bad shape, no valid tap in a segment) or -20 (CUDA error). */
+int gdn_block_token_host(int KH, int VH, int D, gdn_blk_t *b);
+
+/* The same token on DEVICE buffers, state resident.  Three launches on
+ * `stream` (front: conv/silu/L2 norms/scalar path; one CTA per value head:
+ * recurrence, head emit, rmsnorm, gate; site-13 tail), each a programmatic
+ * dependent of the previous one; with pdl set the first is also a dependent
+ * of the kernel before it in the stream.  The small per-token control words
+ * (tap exponents, validity, segment weight exponents) are passed by value.
+ * status (device, 5 ints) receives {y_exp, err_conv, err_g, err_se, y_sat}
+ * for this token.  work: deltanet_work_bytes(KH, VH, D) bytes of device
+ * memory, 256-byte aligned, owned by the caller (scratch between the
+ * launches; two calls in flight at once need two workspaces). */
+typedef struct {
+    int32_t        KH, VH, D;
+    const int16_t *xtap, *wtap;     /* [2*KH*D + VH*D][4], 8-byte aligned       */
+    int32_t        e_t[3][4];
+    int32_t        tvalid[3][4];
+    int32_t        cw_exp[3];
+    const int32_t *sc;              /* [VH][8]                                  */
+    const int16_t *zm;              /* [VH][D]                                  */
+    const int16_t *wm;              /* [D]                                      */
+    int32_t        w_e, z_e, tk0;
+    int16_t       *smem;            /* [VH][D][D], 32-byte aligned, in place    */
+    int32_t       *semem;           /* [VH][D], in place                        */
+    int16_t       *y;               /* [VH*D]                                   */
+    int32_t       *status;          /* [5]                                      */
+    void          *work;
+    int32_t        pdl;
+} deltanet_args;
+
+size_t deltanet_work_bytes(int KH, int VH, int D);
+int deltanet_step(const deltanet_args *a, void *stream);
+
+/* The block's stages one at a time, on device buffers: the unit cores the
+ * reference keeps for its vector generators.
+ *   gdn_conv_seg_dev   conv + segment requantiser (ref/gdn_conv_vec.c:80-103):
+ *                      ncase segments of nch channels x 4 taps; cfg [ncase][9]
+ *                      = {tvalid[4], e_t[4], cw_exp}; sm [ncase][nch] the
+ *                      requantised mantissas; info [ncase][3] = {e_seg, sh_seg, err}
+ *   gdn_silu_dev       silu with the exponent preserved (ref/gdn_silu_vec.c):
+ *                      ncase rows of n int16, row r on exponent e_row[r]
+ *   gdn_l2norm_dev     l2norm_rs (ref/l2norm_rs_vec.c:118): nvec vectors of N
+ *                      (32/64/128) -> k (exponent 15) and q (exponent 18)
+ *   gdn_rmsnorm_bf_dev rmsnorm_bf_int (ref/rmsnorm_bf_vec.c:199), eps 1e-6:
+ *                      nvec vectors of N with their own xe, weights, we
+ *   gdn_y_emit_dev     site 13 (ref/gdn_y_emit_vec.c:124-143); status[0] =
+ *                      y_exp, status[4] = saturation
+ *   gdn_emit_chain_dev site 12 -> rmsnorm -> z gate -> site 13
+ *                      (ref/gdn_emit_chain_vec.c); work as for deltanet_step
+ *                      with KH = 1, VH = H */
+int gdn_conv_seg_dev(int ncase, int nch, const int16_t *x, const int16_t *w, const int32_t *cfg,
+                     int16_t *sm, int32_t *info, void *stream);
+int gdn_silu_dev(int ncase, int n, const int16_t *sm, const int32_t *e_row, int32_t *y, void *stream);
+int gdn_l2norm_dev(int nvec, int N, const int32_t *x, int16_t *k, int16_t *q, void *stream);
+int gdn_rmsnorm_bf_dev(int nvec, int N, const int16_t *xm, const int32_t *xe, const int16_t *wm,
+                       const int32_t *we, int16_t *o, int32_t *o_exp, void *stream);
+int gdn_y_emit_dev(int H, int D, const int32_t *ep, const int16_t *po, const int16_t *pz,
+                   int16_t *y, int32_t *status, void *stream);
+int gdn_emit_chain_dev(int H, int D, const int64_t *o_acc, const int32_t *e_o, const int16_t *zm,
+                       const int16_t *wm, int we, int z_e, int16_t *y, int32_t *status, void *work,
+                       void *stream);
 
 #ifdef __cplusplus
 }

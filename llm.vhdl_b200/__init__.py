@@ -21,7 +21,7 @@ LIBDIR = os.path.join(HERE, "lib")
 LIBPATH = os.path.join(LIBDIR, "libmv4i_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]
+SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]   # gdn_kernels.cu includes gdn_block.cuh
 DEC_LIBPATH = os.path.join(LIBDIR, "libdec_b200.so")
 DEC_SOURCES = ["csrc/dec_step.cu", "csrc/dec_model.c"]   # dec_step.cu includes dec_kernels.cu, dec_matvec.cu
 
@@ -102,6 +102,16 @@ class GdnF32(C.Structure):
                 ("seq_in", C.c_int32), ("pad_", C.c_int32)]
 
 
+class DeltanetArgs(C.Structure):
+    """deltanet_args of include/gdn_b200.h (device buffers)."""
+    _fields_ = [("KH", C.c_int32), ("VH", C.c_int32), ("D", C.c_int32), ("xtap", C.c_void_p),
+                ("wtap", C.c_void_p), ("e_t", (C.c_int32 * 4) * 3), ("tvalid", (C.c_int32 * 4) * 3),
+                ("cw_exp", C.c_int32 * 3), ("sc", C.c_void_p), ("zm", C.c_void_p), ("wm", C.c_void_p),
+                ("w_e", C.c_int32), ("z_e", C.c_int32), ("tk0", C.c_int32), ("smem", C.c_void_p),
+                ("semem", C.c_void_p), ("y", C.c_void_p), ("status", C.c_void_p), ("work", C.c_void_p),
+                ("pdl", C.c_int32)]
+
+
 class Job(C.Structure):
     _fields_ = [("w", C.POINTER(DMat)), ("x", C.c_void_p), ("d_x_exp", C.c_void_p),
                 ("x_exp", C.c_int32), ("n_rows", C.c_int32), ("n_cols", C.c_int32),
@@ -141,6 +151,19 @@ EXPORTS = {
     "gdn_scalar_dev": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "gdn_step_fixed": (C.c_int, [C.POINTER(GdnFixed), C.c_void_p]),
     "gdn_run_f32": (C.c_int, [C.POINTER(GdnF32), C.c_void_p]),
+    "deltanet_work_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "deltanet_step": (C.c_int, [C.POINTER(DeltanetArgs), C.c_void_p]),
+    "gdn_block_token_host": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "gdn_conv_seg_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_void_p]),
+    "gdn_silu_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "gdn_l2norm_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "gdn_rmsnorm_bf_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p]),
+    "gdn_y_emit_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_void_p]),
+    "gdn_emit_chain_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mv4i_last_cuda_error": (C.c_int, []),
     "mv4i_version": (C.c_char_p, []),
 }

@@ -1,0 +1,921 @@
+// llm.vhdl_b200/csrc/gdn_block.cuh -- the fixed-point Gated DeltaNet block
+// (llm.vhdl subsystem B, one token end to end, bit-exact with the reference's
+// gdn_block_token, ref/gdn_block_vec.c:208-423).  Included by gdn_kernels.cu,
+// whose integer helpers (g_floor_shr, g_round_shift, g_msb, ...), scalar path
+// (d_to_q_wide, ...) and LUT upload it shares.
+//
+// Three launches per token, each a programmatic dependent of the one before:
+//
+//   gdn_blk_front_kernel   grid 4 x 1024 threads.  CTA s < 3 is conv segment s
+//                          (q, k, v: spec B 2.1.3): the 4-tap conv with masked
+//                          taps and the segment requantiser (a CTA-wide maximum),
+//                          silu with the exponent preserved, and for q / k the
+//                          per-key-head L2 norm (a warp per head, the Newton
+//                          rsqrt on the shared Q30 seed table).  CTA 3 runs the
+//                          scalar path (eg, beta) for every value head.
+//   gdn_blk_rec_kernel<D>  one CTA per value head, D*D/16 threads: the
+//                          recurrence (stages 1-5, state column j owned by D/16
+//                          lanes of 16 keys each; the state slice is loaded
+//                          before the wait on the front kernel), then warp 0
+//                          runs the head tail: site-12 head emit, the output
+//                          rmsnorm_bf, the z gate.
+//   gdn_blk_tail_kernel    one CTA: site 13, the gated product over all heads
+//                          aligned to the minimum head exponent and renormalised
+//                          to one token exponent; writes the status word.
+//
+// Scratch between the launches lives in the caller's workspace
+// (deltanet_work_bytes); nothing is allocated here.  Roofline: HBM for the
+// state (2*VH*D*D bytes read and written per token, 2 MiB at KH 16 / VH 32 /
+// D 128); every other operand is under 200 KB and the launches are latency-
+// bound at that size.
+
+#define BLK_FULL 0xffffffffu
+#define BLK_EPS_E 50                    /* e_eps = 30 - floor(log2(1e-6))   */
+#define BLK_EPS_M 1125899907LL          /* llround(1e-6 * 2^50)             */
+#define BLK_INV_SQRT2 759250125LL       /* round(2^30 / sqrt 2)             */
+
+__device__ int64_t d_sig_tab[513];      // the Q30 sigmoid table, global copy for divergent reads
+__device__ int64_t d_rsqrt_rom[64];     // round(2^30 / sqrt(1 + k/64))
+
+static unsigned long long g_blk_tab_ready = 0;
+
+static cudaError_t upload_blk_tables()
+{
+    int dev = 0;
+    cudaError_t e = upload_luts();
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && (g_blk_tab_ready >> dev & 1ull)) return cudaSuccess;
+    static int64_t ts[513], rom[64];
+    for (int k = 0; k <= 512; k++) {
+        const double z = -16.0 + (double)k * (32.0 / 512.0);
+        ts[k] = llround((1.0 / (1.0 + exp(-z))) * 1073741824.0);
+    }
+    for (int k = 0; k < 64; k++) rom[k] = llround(1073741824.0 / sqrt(1.0 + (double)k / 64.0));
+    e = cudaMemcpyToSymbol(d_sig_tab, ts, sizeof ts);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(d_rsqrt_rom, rom, sizeof rom);
+    if (e == cudaSuccess && dev < 64) g_blk_tab_ready |= 1ull << dev;
+    return e;
+}
+
+// ------------------------------------------------------------ fixed-point units
+
+// site-3 Q12 conversion of a mantissa on exponent e (ref/gdn_silu_vec.c:42-57)
+__device__ __forceinline__ int32_t fx_to_q12(int64_t x, int e)
+{
+    const int sh = e - 12;
+    if (sh >= 0) return sh > 62 ? 0 : (int32_t)g_round_shift(x, sh);
+    const int k = -sh;
+    if (k > 40) return x > 0 ? INT32_MAX : (x < 0 ? INT32_MIN : 0);
+    const int64_t v = x * ((int64_t)1 << k);
+    return v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : (int32_t)v);
+}
+
+// sigma, Q12 in / Q15 out, interpolated on the Q30 table (ref/gdn_silu_vec.c:59-80)
+__device__ __forceinline__ int32_t fx_sigma_q15(int32_t z)
+{
+    const int64_t lim = (int64_t)16 << 12;
+    if ((int64_t)z <= -lim) return 0;
+    if ((int64_t)z >= lim) return 1 << 15;
+    const int64_t pos = ((int64_t)z + lim) * 16;
+    int64_t k = pos >> 12;
+    if (k > 511) k = 511;
+    const int64_t frac = pos - (k << 12);
+    const int64_t lo = __ldg(d_sig_tab + k), hi = __ldg(d_sig_tab + k + 1);
+    const int64_t r = g_round_shift(lo + (((hi - lo) * frac) >> 12), 15);
+    return (int32_t)(r < 0 ? 0 : (r > 32768 ? 32768 : r));
+}
+
+// silu with the exponent preserved (ref/gdn_block_vec.c:250-253)
+__device__ __forceinline__ int32_t fx_silu(int32_t sm, int e)
+{
+    return (int32_t)g_round_shift((int64_t)sm * fx_sigma_q15(fx_to_q12(sm, e)), 15);
+}
+
+// numeric_std forms used by rmsnorm_bf (ref/rmsnorm_bf_vec.c:108-157)
+__device__ __forceinline__ int64_t fx_sll(int64_t v, int sh)
+{ return sh <= 0 ? v : (sh >= 64 ? 0 : (int64_t)((uint64_t)v << sh)); }
+__device__ __forceinline__ int64_t fx_narrow(int64_t v, int w)
+{
+    const int64_t r = (int64_t)((uint64_t)v & (((uint64_t)1 << (w - 1)) - 1));
+    return v < 0 ? r - ((int64_t)1 << (w - 1)) : r;
+}
+__device__ __forceinline__ int fx_msb63(int64_t v)
+{
+    const uint64_t u = (uint64_t)v & 0x7FFFFFFFFFFFFFFFull;
+    return u ? 63 - __clzll((long long)u) : 0;
+}
+
+// one L2-norm rsqrt pass (ref/l2norm_rs_vec.c:93-115): Q30 mantissa, exponent he
+__device__ __forceinline__ int64_t fx_l2_rsqrt(int64_t arg, int &he)
+{
+    const int m = fx_msb63(arg);
+    const uint64_t mant = m <= 30 ? (uint64_t)arg << (30 - m) : (uint64_t)arg >> (m - 30);
+    const int64_t sm = (int64_t)(uint32_t)mant;
+    int64_t y = d_rsqrt_rom[(mant >> 24) & 63];
+#pragma unroll
+    for (int it = 0; it < 2; it++) {
+        const int64_t y2 = (int64_t)(int32_t)((y * y) >> 30);
+        const int64_t d = (3LL << 30) - ((sm * y2) >> 30);
+        y = (int64_t)(int32_t)((d * y) >> 31);
+    }
+    if (m & 1) { he = (m - 1) / 2; y = (y * BLK_INV_SQRT2) >> 30; }
+    else he = m / 2;
+    return y;
+}
+
+// the rmsnorm_bf reciprocal (ref/rmsnorm_bf_vec.c:230-331) of a sum of squares
+// S of N = 2^lg mantissas on exponent xe: the clamped u31 inv32, Q = 12
+__device__ int64_t fx_rms_inv(int64_t S, int xe, int lg)
+{
+    const int shs = 30 - fx_msb63(S);
+    const int e_mean = lg + 2 * xe + shs;
+    const int64_t m_mean = S == 0 ? 0 : (shs >= 0 ? fx_sll(S, shs) : g_floor_shr(S, -shs));
+    int d, mean_smaller, e_out;
+    if (S == 0) { d = 0; mean_smaller = 1; e_out = BLK_EPS_E; }
+    else if (e_mean > BLK_EPS_E) { d = e_mean - BLK_EPS_E; mean_smaller = 1; e_out = BLK_EPS_E; }
+    else { d = BLK_EPS_E - e_mean; mean_smaller = 0; e_out = e_mean; }
+    if (d > 63) d = 63;
+    const int64_t align = S == 0 ? 0 : (mean_smaller ? g_floor_shr(m_mean, d) : g_floor_shr(BLK_EPS_M, d));
+    const int64_t msq = mean_smaller ? align + BLK_EPS_M : m_mean + align;
+    const int p = fx_msb63(msq);
+    const uint64_t mant = p <= 30 ? (uint64_t)msq << (30 - p) : (uint64_t)msq >> (p - 30);
+    const int64_t sm = (int64_t)(uint32_t)mant;
+    int64_t y = d_rsqrt_rom[(mant >> 24) & 63];
+#pragma unroll
+    for (int it = 0; it < 2; it++) {
+        const int64_t y2 = fx_narrow(g_floor_shr(y * y, 30), 32);
+        const int64_t df = fx_narrow((3LL << 30) - fx_narrow(g_floor_shr(sm * y2, 30), 34), 34);
+        y = fx_narrow(g_floor_shr(df * y, 31), 32);
+    }
+    const int rq_d = p - e_out;
+    int64_t yf;
+    int he;
+    if (rq_d % 2 != 0) { yf = fx_narrow(g_floor_shr(y * BLK_INV_SQRT2, 30), 32); he = (rq_d - 1) / 2; }
+    else { yf = y; he = rq_d / 2; }
+    const int E = 12 - 30 - he;
+    int64_t inv;
+    if (E > 32) inv = 2147483647LL;
+    else if (E >= 0) inv = fx_sll(yf, E);
+    else inv = g_floor_shr(yf + fx_sll(1, -E - 1), -E);
+    return inv > 2147483647LL ? 2147483647LL : (inv < 0 ? 0 : inv);
+}
+
+__device__ __forceinline__ int64_t warp_sum_i64(int64_t v)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(BLK_FULL, v, o);
+    return v;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) { const uint64_t w = __shfl_xor_sync(BLK_FULL, v, o); v = w > v ? w : v; }
+    return v;
+}
+__device__ __forceinline__ int warp_min_i32(int v)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(BLK_FULL, v, o));
+    return v;
+}
+// CTA-wide maximum (every thread gets it); red holds one word per warp
+__device__ uint64_t cta_max_u64(uint64_t v, uint64_t *red)
+{
+    v = warp_max_u64(v);
+    const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    uint64_t m = 0;
+    for (int i = 0; i < nw; i++) m = red[i] > m ? red[i] : m;
+    return m;
+}
+
+// L2 norm of one head of R*32 silu mantissas held R per lane (element lane + 32 r):
+// the k output (exponent 15) or the q output (exponent 18), zeros when the
+// sum of squares is 0 (ref/l2norm_rs_vec.c:118-140)
+template <int R>
+__device__ void fx_l2norm_warp(const int32_t (&x)[R], int log2n, bool q_path, int16_t *out)
+{
+    int64_t ssq = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) ssq += (int64_t)x[r] * x[r];
+    ssq = warp_sum_i64(ssq);
+    const int lane = threadIdx.x & 31;
+    if (ssq == 0) {
+#pragma unroll
+        for (int r = 0; r < R; r++) out[lane + 32 * r] = 0;
+        return;
+    }
+    int he;
+    const int64_t y = fx_l2_rsqrt(q_path ? ssq << log2n : ssq, he);
+    const int sh = (q_path ? 12 : 15) + he;
+#pragma unroll
+    for (int r = 0; r < R; r++)
+        out[lane + 32 * r] = g_sat16(((int64_t)x[r] * y + ((int64_t)1 << (sh - 1))) >> sh);
+}
+
+// rmsnorm_bf of one head of R*32 int16 mantissas on exponent xe, R per lane,
+// weights wm on we (ref/rmsnorm_bf_vec.c:199-389); returns the output exponent
+template <int R>
+__device__ int fx_rmsnorm_warp(const int32_t (&xm)[R], int xe, const int16_t *wm, int we, int lg,
+                               int32_t (&o)[R], int &nsat)
+{
+    const int lane = threadIdx.x & 31;
+    int64_t S = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) S += (int64_t)xm[r] * xm[r];
+    S = warp_sum_i64(S);
+    const int64_t inv = fx_rms_inv(S, xe, lg);
+    int64_t raw[R];
+    uint64_t mx = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        raw[r] = fx_narrow(xm[r] * inv, 48) * (int64_t)wm[lane + 32 * r];
+        const uint64_t a = (uint64_t)(raw[r] < 0 ? -raw[r] : raw[r]);
+        mx = a > mx ? a : mx;
+    }
+    mx = warp_max_u64(mx);
+    int st = fx_msb63((int64_t)mx) - 14;
+    if (st < 0) st = 0;
+    const int64_t bias = st == 0 ? 0 : fx_sll(1, st - 1);
+    nsat = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const int64_t v = g_floor_shr(raw[r] + bias, st);
+        nsat += (v > 32767 || v < -32768);
+        o[r] = g_sat16(v);
+    }
+    return xe + we + 12 - st;
+}
+
+// ------------------------------------------------------------- block kernels
+
+struct BlkWork {                       // device scratch between the three launches
+    int16_t *kn, *qs;                  // [KH][D] Q15 / Q18 (1/sqrt(D) folded)
+    int32_t *v;                        // [VH][D] silu(v) mantissas on e_v
+    int32_t *eg, *beta;                // [VH]
+    int16_t *po, *pz;                  // [VH][D] normed output / gated z
+    int32_t *ep;                       // [VH] product exponents
+    int32_t *err_se;                   // [VH]
+    int32_t *misc;                     // [0] e_v, [1..3] err_conv per segment, [4] err_g
+};
+
+static size_t blk_al(size_t n) { return (n + 255) & ~(size_t)255; }
+
+static BlkWork blk_work_layout(void *base, int KH, int VH, int D, size_t *bytes)
+{
+    BlkWork w;
+    char *p = (char *)base;
+    size_t off = 0;
+#define BLK_TAKE(field, T, n) w.field = (T *)(p + off); off += blk_al((size_t)(n) * sizeof(T));
+    BLK_TAKE(kn, int16_t, KH * D)
+    BLK_TAKE(qs, int16_t, KH * D)
+    BLK_TAKE(v, int32_t, VH * D)
+    BLK_TAKE(eg, int32_t, VH)
+    BLK_TAKE(beta, int32_t, VH)
+    BLK_TAKE(po, int16_t, VH * D)
+    BLK_TAKE(pz, int16_t, VH * D)
+    BLK_TAKE(ep, int32_t, VH)
+    BLK_TAKE(err_se, int32_t, VH)
+    BLK_TAKE(misc, int32_t, 8)
+#undef BLK_TAKE
+    if (bytes) *bytes = off;
+    return w;
+}
+
+struct BlkFrontArgs {
+    const int16_t *xtap, *wtap;        // [2*KH*D + VH*D][4]
+    int32_t KH, VH, D, lg;
+    int32_t e_t[3][4], tvalid[3][4], cw_exp[3];
+    const int32_t *sc;                 // [VH][8]
+    BlkWork w;
+};
+
+// conv of one channel over its valid taps, aligned to the smallest valid tap
+// exponent by floor (ref/gdn_block_vec.c:231-239)
+__device__ __forceinline__ int64_t blk_conv_ch(const int16_t *x, const int16_t *w, int vmask, const int (&tsh)[4])
+{
+    const uint2 xv = *reinterpret_cast<const uint2 *>(x), wv = *reinterpret_cast<const uint2 *>(w);
+    const int32_t xs[4] = {lo16(xv.x), hi16(xv.x), lo16(xv.y), hi16(xv.y)};
+    const int32_t ws[4] = {lo16(wv.x), hi16(wv.x), lo16(wv.y), hi16(wv.y)};
+    int64_t a = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+        if (vmask >> t & 1) a += g_floor_shr((int64_t)(xs[t] * ws[t]), tsh[t]);
+    return a;
+}
+
+// e_ref = smallest exponent among the valid taps; per-tap alignment shifts
+__device__ __forceinline__ int blk_taps(const int32_t (&e_t)[4], const int32_t (&tv)[4], int (&tsh)[4], int &vmask)
+{
+    int e_ref = 0, have = 0;
+    vmask = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+        if (tv[t]) { vmask |= 1 << t; if (!have || e_t[t] < e_ref) { e_ref = e_t[t]; have = 1; } }
+#pragma unroll
+    for (int t = 0; t < 4; t++) { const int s = e_t[t] - e_ref; tsh[t] = s > 63 ? 63 : s; }
+    return e_ref;
+}
+
+template <int R>
+__device__ void blk_front_segment(const BlkFrontArgs &A, int s, uint64_t *red)
+{
+    const int D = R * 32, QCH = A.KH * D;
+    const int base = s == 0 ? 0 : (s == 1 ? QCH : 2 * QCH), nch = s == 2 ? A.VH * D : QCH;
+    int tsh[4], vmask;
+    const int e_ref = blk_taps(A.e_t[s], A.tvalid[s], tsh, vmask);
+    const int16_t *xs = A.xtap + (size_t)base * 4, *ws = A.wtap + (size_t)base * 4;
+    uint64_t am = 0;
+    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+        const int64_t a = blk_conv_ch(xs + 4 * c, ws + 4 * c, vmask, tsh);
+        const uint64_t m = g_abs64(a);
+        am = m > am ? m : am;
+    }
+    am = cta_max_u64(am, red);
+    int sh = g_msb(am) - 14;
+    if (sh < 0) sh = 0;
+    const int e_seg = e_ref + A.cw_exp[s] - sh;
+    if (threadIdx.x == 0) {
+        A.w.misc[1 + s] = (e_seg > 127 || e_seg < -128);
+        if (s == 2) A.w.misc[0] = e_seg;
+    }
+    if (s == 2) {
+        for (int c = threadIdx.x; c < nch; c += blockDim.x)
+            A.w.v[c] = fx_silu(g_sat16(g_round_shift(blk_conv_ch(xs + 4 * c, ws + 4 * c, vmask, tsh), sh)), e_seg);
+        return;
+    }
+    // q / k: one warp per key head, the head's silu outputs then its L2 norm
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int hk = warp; hk < A.KH; hk += nw) {
+        int32_t x[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int c = hk * D + lane + 32 * r;
+            x[r] = fx_silu(g_sat16(g_round_shift(blk_conv_ch(xs + 4 * c, ws + 4 * c, vmask, tsh), sh)), e_seg);
+        }
+        fx_l2norm_warp<R>(x, A.lg, s == 0, (s == 0 ? A.w.qs : A.w.kn) + hk * D);
+    }
+}
+
+__global__ void __launch_bounds__(1024)
+gdn_blk_front_kernel(const BlkFrontArgs A)
+{
+    __shared__ uint64_t red[32];
+    // wait for the previous kernel in the stream before touching anything:
+    // the next launch may start its state prefetch only once this point is
+    // passed (then every earlier token's state write-back has completed)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int s = blockIdx.x;
+    if (s < 3) {
+        if (A.D == 32) blk_front_segment<1>(A, s, red);
+        else if (A.D == 64) blk_front_segment<2>(A, s, red);
+        else blk_front_segment<4>(A, s, red);
+        return;
+    }
+    // the scalar path for every value head (gdn_scalar_kernel's body)
+    int err = 0;
+    for (int h = threadIdx.x; h < A.VH; h += blockDim.x) {
+        const int32_t *p = A.sc + (size_t)h * 8;
+        const int64_t arg = d_to_q_wide(p[0], p[1]) + d_to_q_wide(p[2], p[3]);
+        const int64_t one = (int64_t)1 << SPQ, lim = 16 * one;
+        int64_t sp;
+        if (arg <= -lim) sp = 0;
+        else if (arg >= lim) sp = arg;
+        else {
+            const int64_t ax = arg < 0 ? -arg : arg, pos = arg > 0 ? arg : 0;
+            sp = pos + (ax >= lim ? 0 : d_lut_interp(c_sp_lut, 256, lim - ax, SPQ));
+            if (sp < 0) sp = 0;
+            if (sp > 0x7FFFFFFF) sp = 0x7FFFFFFF;
+        }
+        int64_t g = d_rshift_r(sp * (int64_t)p[4], p[5]);
+        if (g > 0) g = 0;
+        err |= g < -lim;
+        if (g < -lim) g = -lim;
+        int64_t ex = d_lut_interp(c_exp_lut, 256, g + lim, SPQ);
+        if (ex < 0) ex = 0;
+        if (ex > 0x7FFFFFFF) ex = 0x7FFFFFFF;
+        int64_t egv = d_rshift_r(ex, SPQ - 15);
+        egv = egv > 32768 ? 32768 : (egv < 0 ? 0 : egv);
+        int64_t bq = d_to_q_wide(p[6], p[7]);
+        bq = bq > lim ? lim : (bq < -lim ? -lim : bq);
+        int64_t sg;
+        if (bq <= -lim) sg = 0;
+        else if (bq >= lim) sg = one;
+        else {
+            sg = d_lut_interp(c_sig_lut, 512, bq + lim, SPQ);
+            sg = sg < 0 ? 0 : (sg > one ? one : sg);
+        }
+        int64_t bv = d_rshift_r(sg, SPQ - 16);
+        bv = bv > 65535 ? 65535 : (bv < 0 ? 0 : bv);
+        A.w.eg[h] = (int32_t)egv;
+        A.w.beta[h] = (int32_t)bv;
+    }
+    err = __syncthreads_or(err);
+    if (threadIdx.x == 0) A.w.misc[4] = err;
+}
+
+struct BlkRecArgs {
+    int32_t KH, VH, tk0, w_e, z_e;
+    int16_t *smem;                     // [VH][D][D]
+    int32_t *semem;                    // [VH][D]
+    const int16_t *zm, *wm;            // [VH][D], [D]
+    BlkWork w;
+    // head-tail input override (emit-chain unit entry): o_acc / e_o from memory
+    const int64_t *o_acc_in;
+    const int32_t *e_o_in;
+};
+
+// warp 0 of a head's CTA: site-12 head emit of the head's D column outputs,
+// the output rmsnorm, the z gate; po / pz / ep for the site-13 launch
+template <int D>
+__device__ void blk_head_tail(const BlkRecArgs &A, int h, const int64_t *s_oacc, const int32_t *s_eo)
+{
+    constexpr int R = D / 32, LG = D == 32 ? 5 : (D == 64 ? 6 : 7);
+    const int lane = threadIdx.x & 31;
+    int emin = 1 << 30;
+#pragma unroll
+    for (int r = 0; r < R; r++) emin = min(emin, s_eo[lane + 32 * r]);
+    emin = warp_min_i32(emin);
+    int64_t al[R];
+    uint64_t am = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        int shj = s_eo[lane + 32 * r] - emin;
+        if (shj > 63) shj = 63;
+        al[r] = g_floor_shr(s_oacc[lane + 32 * r], shj);
+        const uint64_t a = g_abs64(al[r]);
+        am = a > am ? a : am;
+    }
+    am = warp_max_u64(am);
+    int shh = g_msb(am) - 14;
+    if (shh < 0) shh = 0;
+    int32_t oh[R], po[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) oh[r] = g_sat16(g_round_shift(al[r], shh));
+    int nsat;
+    const int o_exp = fx_rmsnorm_warp<R>(oh, emin - shh, A.wm, A.w_e, LG, po, nsat);
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const int j = lane + 32 * r;
+        A.w.po[h * D + j] = (int16_t)po[r];
+        A.w.pz[h * D + j] = g_sat16(fx_silu(A.zm[h * D + j], A.z_e));
+    }
+    if (lane == 0) A.w.ep[h] = o_exp + A.z_e;
+}
+
+template <int D>
+__global__ void __launch_bounds__(D * D / 16)
+gdn_blk_rec_kernel(const BlkRecArgs A)
+{
+    constexpr int LPC = D / 16, CPW = 32 / LPC;
+    __shared__ int64_t s_oacc[D];
+    __shared__ int32_t s_eo[D];
+    const int h = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j = warp * CPW + lane / LPC;          // value column
+    const int i0 = 16 * (lane % LPC);               // key slice
+    const int hk = h % A.KH;
+
+    // the state slice, its exponent and the gate inputs do not depend on the
+    // front kernel: load them before waiting for it
+    int16_t *scol = A.smem + ((size_t)h * D + j) * D + i0;
+    uint32_t sm[8], kn[8], qs[8];
+    ld16_i16(scol, sm);
+    const int se_j = A.semem[h * D + j];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    ld16_i16(A.w.kn + (size_t)hk * D + i0, kn);
+    ld16_i16(A.w.qs + (size_t)hk * D + i0, qs);
+    const int32_t v_j = A.w.v[h * D + j];
+    const int egh = A.w.eg[h], bth = A.w.beta[h], tk0 = A.tk0, e_v = A.w.misc[0];
+
+    // stages 1-2: decay, sk dot
+    int32_t w18[16];
+    int64_t sk = 0;
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const int32_t a = tk0 ? 0 : lo16(sm[p]) * egh, b = tk0 ? 0 : hi16(sm[p]) * egh;
+        w18[2 * p] = (a + 4096) >> 13;
+        w18[2 * p + 1] = (b + 4096) >> 13;
+        sk += (int64_t)w18[2 * p] * lo16(kn[p]) + (int64_t)w18[2 * p + 1] * hi16(kn[p]);
+    }
+#pragma unroll
+    for (int o = 1; o < LPC; o <<= 1) sk += __shfl_xor_sync(BLK_FULL, sk, o);
+    int sh_sk = g_msb(g_abs64(sk)) - 14;
+    if (sh_sk < 0) sh_sk = 0;
+    const int64_t skm = g_round_shift(sk, sh_sk);
+    const int ske = se_j + 17 - sh_sk;
+
+    // stage 3: delta
+    const bool masked = tk0 || egh == 0;
+    const int e_d = masked ? e_v : (e_v < ske ? e_v : ske);
+    int s1 = e_v - e_d, s2 = ske - e_d;
+    if (s1 > 63) s1 = 63;
+    if (s2 > 63) s2 = 63;
+    const int64_t draw = (g_floor_shr(v_j, s1) - g_floor_shr(skm, s2)) * (int64_t)bth;
+    int shd = g_msb(g_abs64(draw)) - 14;
+    if (shd < 0) shd = 0;
+    const int64_t d_m = g_round_shift(draw, shd);
+    const int e_dm = e_d + 16 - shd;
+
+    // stage 4: update, write-back quantiser
+    const int e_kd = 15 + e_dm;
+    const int e_u = masked ? e_kd : (se_j + 2 < e_kd ? se_j + 2 : e_kd);
+    int su = se_j + 2 - e_u, sk2 = e_kd - e_u;
+    if (su > 63) su = 63;
+    if (sk2 > 63) sk2 = 63;
+    uint64_t amax = 0;
+#pragma unroll
+    for (int p = 0; p < 16; p++) {
+        const int32_t k = (p & 1) ? hi16(kn[p >> 1]) : lo16(kn[p >> 1]);
+        const int64_t u = (tk0 ? 0 : g_floor_shr(w18[p], su)) + g_floor_shr((int64_t)k * d_m, sk2);
+        const uint64_t a = g_abs64(u);
+        amax = a > amax ? a : amax;
+    }
+#pragma unroll
+    for (int o = 1; o < LPC; o <<= 1) { const uint64_t w = __shfl_xor_sync(BLK_FULL, amax, o); amax = w > amax ? w : amax; }
+    int sh = g_msb(amax) - 14;
+    if (sh < 0) sh = 0;
+    uint32_t sn[8];
+    int64_t od = 0;
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        int32_t r2[2];
+#pragma unroll
+        for (int hlf = 0; hlf < 2; hlf++) {
+            const int32_t k = hlf ? hi16(kn[p]) : lo16(kn[p]);
+            const int64_t u = (tk0 ? 0 : g_floor_shr(w18[2 * p + hlf], su)) + g_floor_shr((int64_t)k * d_m, sk2);
+            r2[hlf] = g_sat16(g_round_shift(u, sh));
+        }
+        sn[p] = ((uint32_t)(uint16_t)r2[0]) | ((uint32_t)(uint16_t)r2[1] << 16);
+        od += (int64_t)r2[0] * lo16(qs[p]) + (int64_t)r2[1] * hi16(qs[p]);     // stage 5
+    }
+    reinterpret_cast<uint4 *>(scol)[0] = make_uint4(sn[0], sn[1], sn[2], sn[3]);
+    reinterpret_cast<uint4 *>(scol)[1] = make_uint4(sn[4], sn[5], sn[6], sn[7]);
+#pragma unroll
+    for (int o = 1; o < LPC; o <<= 1) od += __shfl_xor_sync(BLK_FULL, od, o);
+    const int se_new = e_u - sh, e_o = se_new + 18;
+    int err = 0;
+    if (lane % LPC == 0) {
+        A.semem[h * D + j] = se_new;
+        s_oacc[j] = od;
+        s_eo[j] = e_o;
+        err = se_new > 127 || se_new < -128 || e_o > 127 || e_o < -128;
+    }
+    err = __syncthreads_or(err);
+    if (warp == 0) {
+        blk_head_tail<D>(A, h, s_oacc, s_eo);
+        if (lane == 0) A.w.err_se[h] = err;
+    }
+}
+
+// the emit chain alone (site 12 -> rmsnorm -> z gate) on o_acc / e_o from
+// memory, one warp per head: the unit entry point of the block's tail
+template <int D>
+__global__ void __launch_bounds__(32)
+gdn_blk_chain_kernel(const BlkRecArgs A)
+{
+    __shared__ int64_t s_oacc[D];
+    __shared__ int32_t s_eo[D];
+    const int h = blockIdx.x, lane = threadIdx.x;
+    for (int j = lane; j < D; j += 32) { s_oacc[j] = A.o_acc_in[h * D + j]; s_eo[j] = A.e_o_in[h * D + j]; }
+    __syncwarp();
+    blk_head_tail<D>(A, h, s_oacc, s_eo);
+}
+
+struct BlkTailArgs {
+    int32_t VH, D;
+    const int16_t *po, *pz;
+    const int32_t *ep;
+    int16_t *y;
+    int32_t *status;                   // [5] y_exp, err_conv, err_g, err_se, y_sat
+    const int32_t *misc, *err_se;      // NULL for the site-13 unit entry
+};
+
+// site 13 (ref/gdn_block_vec.c:396-418): one CTA over all VH*D products
+__global__ void __launch_bounds__(1024)
+gdn_blk_tail_kernel(const BlkTailArgs A)
+{
+    __shared__ uint64_t red[32];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    int e_y = A.ep[0];
+    for (int h = 1; h < A.VH; h++) e_y = min(e_y, A.ep[h]);
+    const int n = A.VH * A.D;
+    uint64_t am = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        int s = A.ep[i / A.D] - e_y;
+        const uint64_t a = g_abs64(g_floor_shr((int64_t)A.po[i] * A.pz[i], s > 63 ? 63 : s));
+        am = a > am ? a : am;
+    }
+    am = cta_max_u64(am, red);
+    int sh = g_msb(am) - 14;
+    if (sh < 0) sh = 0;
+    int sat = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        int s = A.ep[i / A.D] - e_y;
+        const int64_t v = g_round_shift(g_floor_shr((int64_t)A.po[i] * A.pz[i], s > 63 ? 63 : s), sh);
+        sat |= v > 32767 || v < -32768;
+        A.y[i] = g_sat16(v);
+    }
+    sat = __syncthreads_or(sat);
+    if (threadIdx.x == 0) {
+        A.status[0] = e_y - sh;
+        A.status[4] = sat;
+        if (A.misc) {
+            int es = 0;
+            for (int h = 0; h < A.VH; h++) es |= A.err_se[h];
+            A.status[1] = A.misc[1] | A.misc[2] | A.misc[3];
+            A.status[2] = A.misc[4];
+            A.status[3] = es;
+        }
+    }
+}
+
+// the conv + segment requantiser unit: one CTA per case (no silu)
+__global__ void __launch_bounds__(256)
+gdn_conv_unit_kernel(int nch, const int16_t *x, const int16_t *w, const int32_t *cfg, int16_t *sm,
+                     int32_t *info)
+{
+    __shared__ uint64_t red[32];
+    const int c = blockIdx.x;
+    const int32_t *p = cfg + 9 * c;              // tv[4], e_t[4], cw_exp
+    const int32_t tv[4] = {p[0], p[1], p[2], p[3]}, et[4] = {p[4], p[5], p[6], p[7]};
+    int tsh[4], vmask;
+    const int e_ref = blk_taps(et, tv, tsh, vmask);
+    const int16_t *xs = x + (size_t)c * nch * 4, *ws = w + (size_t)c * nch * 4;
+    uint64_t am = 0;
+    for (int i = threadIdx.x; i < nch; i += blockDim.x) {
+        const uint64_t a = g_abs64(blk_conv_ch(xs + 4 * i, ws + 4 * i, vmask, tsh));
+        am = a > am ? a : am;
+    }
+    am = cta_max_u64(am, red);
+    int sh = g_msb(am) - 14;
+    if (sh < 0) sh = 0;
+    for (int i = threadIdx.x; i < nch; i += blockDim.x)
+        sm[(size_t)c * nch + i] = g_sat16(g_round_shift(blk_conv_ch(xs + 4 * i, ws + 4 * i, vmask, tsh), sh));
+    if (threadIdx.x == 0) {
+        const int e_seg = e_ref + p[8] - sh;
+        info[3 * c] = e_seg;
+        info[3 * c + 1] = sh;
+        info[3 * c + 2] = e_seg > 127 || e_seg < -128;
+    }
+}
+
+// silu unit: element-wise over ncase rows of n, row r on exponent e[r]
+__global__ void gdn_silu_unit_kernel(int n, int total, const int16_t *sm, const int32_t *e, int32_t *y)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < total) y[i] = fx_silu(sm[i], e[i / n]);
+}
+
+// L2-norm unit: one warp per vector of N = 32 R
+template <int R>
+__global__ void __launch_bounds__(32)
+gdn_l2norm_unit_kernel(const int32_t *x, int log2n, int16_t *k, int16_t *q)
+{
+    const int v = blockIdx.x, lane = threadIdx.x;
+    int32_t xr[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) xr[r] = x[(size_t)v * 32 * R + lane + 32 * r];
+    fx_l2norm_warp<R>(xr, log2n, false, k + (size_t)v * 32 * R);
+    fx_l2norm_warp<R>(xr, log2n, true, q + (size_t)v * 32 * R);
+}
+
+// rmsnorm_bf unit: one warp per vector of N = 32 R
+template <int R>
+__global__ void __launch_bounds__(32)
+gdn_rmsnorm_unit_kernel(const int16_t *xm, const int32_t *xe, const int16_t *wm, const int32_t *we,
+                        int16_t *o, int32_t *o_exp)
+{
+    constexpr int LG = R == 1 ? 5 : (R == 2 ? 6 : 7);
+    const int v = blockIdx.x, lane = threadIdx.x;
+    int32_t x[R], out[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) x[r] = xm[(size_t)v * 32 * R + lane + 32 * r];
+    int nsat;
+    const int e = fx_rmsnorm_warp<R>(x, xe[v], wm + (size_t)v * 32 * R, we[v], LG, out, nsat);
+#pragma unroll
+    for (int r = 0; r < R; r++) o[(size_t)v * 32 * R + lane + 32 * r] = (int16_t)out[r];
+    if (lane == 0) o_exp[v] = e;
+}
+
+// ------------------------------------------------------------- host entries
+
+static cudaError_t blk_launch(const void *fn, dim3 grid, dim3 block, cudaStream_t st, bool pdl, void **args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+static bool blk_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
+
+extern "C" size_t deltanet_work_bytes(int KH, int VH, int D)
+{
+    if (KH <= 0 || VH <= 0 || !blk_dim_ok(D)) return 0;
+    size_t n = 0;
+    blk_work_layout(nullptr, KH, VH, D, &n);
+    return n;
+}
+
+extern "C" int deltanet_step(const deltanet_args *a, void *stream)
+{
+    if (!a || a->KH <= 0 || a->VH < a->KH || a->VH % a->KH || !blk_dim_ok(a->D) || !a->xtap || !a->wtap
+        || !a->sc || !a->zm || !a->wm || !a->smem || !a->semem || !a->y || !a->status || !a->work)
+        return -11;
+    if ((((uintptr_t)a->smem) & 31) || (((uintptr_t)a->xtap) & 7) || (((uintptr_t)a->wtap) & 7)
+        || (((uintptr_t)a->work) & 255))
+        return -11;
+    for (int s = 0; s < 3; s++) {
+        int any = 0;
+        for (int t = 0; t < 4; t++) any |= a->tvalid[s][t] != 0;
+        if (!any) return -11;                    // a segment with no valid tap
+    }
+    cudaError_t e = upload_blk_tables();
+    if (e != cudaSuccess) return gdn_fail(e);
+    const int KH = a->KH, VH = a->VH, D = a->D;
+    const BlkWork w = blk_work_layout(a->work, KH, VH, D, nullptr);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+    BlkFrontArgs F;
+    F.xtap = a->xtap; F.wtap = a->wtap; F.KH = KH; F.VH = VH; F.D = D;
+    F.lg = D == 32 ? 5 : (D == 64 ? 6 : 7);
+    for (int s = 0; s < 3; s++) {
+        F.cw_exp[s] = a->cw_exp[s];
+        for (int t = 0; t < 4; t++) { F.e_t[s][t] = a->e_t[s][t]; F.tvalid[s][t] = a->tvalid[s][t] != 0; }
+    }
+    F.sc = a->sc; F.w = w;
+    void *fa[] = {&F};
+    e = blk_launch((const void *)gdn_blk_front_kernel, dim3(4), dim3(1024), st, a->pdl != 0, fa);
+    if (e != cudaSuccess) return gdn_fail(e);
+
+    BlkRecArgs R;
+    R.KH = KH; R.VH = VH; R.tk0 = a->tk0 != 0; R.w_e = a->w_e; R.z_e = a->z_e;
+    R.smem = a->smem; R.semem = a->semem; R.zm = a->zm; R.wm = a->wm; R.w = w;
+    R.o_acc_in = nullptr; R.e_o_in = nullptr;
+    void *ra[] = {&R};
+    const void *rk = D == 32 ? (const void *)gdn_blk_rec_kernel<32>
+                   : (D == 64 ? (const void *)gdn_blk_rec_kernel<64> : (const void *)gdn_blk_rec_kernel<128>);
+    e = blk_launch(rk, dim3(VH), dim3(D * D / 16), st, true, ra);
+    if (e != cudaSuccess) return gdn_fail(e);
+
+    BlkTailArgs T;
+    T.VH = VH; T.D = D; T.po = w.po; T.pz = w.pz; T.ep = w.ep; T.y = a->y; T.status = a->status;
+    T.misc = w.misc; T.err_se = w.err_se;
+    void *ta[] = {&T};
+    e = blk_launch((const void *)gdn_blk_tail_kernel, dim3(1), dim3(1024), st, true, ta);
+    return e == cudaSuccess ? 0 : gdn_fail(e);
+}
+
+// The reference's gdn_block_token on host buffers (same record, same in-place
+// state, same sticky flags): stages the record through device memory, runs
+// deltanet_step on a private stream and copies the state and outputs back.
+extern "C" int gdn_block_token_host(int KH, int VH, int D, gdn_blk_t *b)
+{
+    if (!b || KH <= 0 || VH < KH || VH % KH || !blk_dim_ok(D) || !b->xtap || !b->wtap || !b->e_t
+        || !b->tvalid || !b->cw_exp || !b->sc || !b->zm || !b->wm || !b->smem || !b->semem || !b->y)
+        return -11;
+    const size_t CH = (size_t)(2 * KH + VH) * D, HD = (size_t)VH * D, wb = deltanet_work_bytes(KH, VH, D);
+    const size_t off_x = 0, off_w = off_x + blk_al(CH * 8), off_sc = off_w + blk_al(CH * 8),
+                 off_z = off_sc + blk_al((size_t)VH * 32), off_wm = off_z + blk_al(HD * 2),
+                 off_s = off_wm + blk_al((size_t)D * 2), off_se = off_s + blk_al(HD * D * 2),
+                 off_y = off_se + blk_al(HD * 4), off_st = off_y + blk_al(HD * 2),
+                 off_wk = off_st + 256, total = off_wk + wb;
+    char *dv = nullptr;
+    cudaStream_t st = nullptr;
+    cudaError_t e = cudaMalloc(&dv, total);
+    if (e != cudaSuccess) return gdn_fail(e);
+    e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    int rc = 0;
+    int32_t status[5] = {0, 0, 0, 0, 0};
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_x, b->xtap, CH * 8, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_w, b->wtap, CH * 8, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_sc, b->sc, (size_t)VH * 32, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_z, b->zm, HD * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_wm, b->wm, (size_t)D * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_s, b->smem, HD * D * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv + off_se, b->semem, HD * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) {
+        deltanet_args a = {};
+        a.KH = KH; a.VH = VH; a.D = D;
+        a.xtap = (const int16_t *)(dv + off_x); a.wtap = (const int16_t *)(dv + off_w);
+        for (int s = 0; s < 3; s++) {
+            a.cw_exp[s] = b->cw_exp[s];
+            for (int t = 0; t < 4; t++) { a.e_t[s][t] = b->e_t[4 * s + t]; a.tvalid[s][t] = b->tvalid[4 * s + t]; }
+        }
+        a.sc = (const int32_t *)(dv + off_sc); a.zm = (const int16_t *)(dv + off_z);
+        a.wm = (const int16_t *)(dv + off_wm); a.w_e = b->w_e; a.z_e = b->z_e; a.tk0 = b->tk0;
+        a.smem = (int16_t *)(dv + off_s); a.semem = (int32_t *)(dv + off_se);
+        a.y = (int16_t *)(dv + off_y); a.status = (int32_t *)(dv + off_st); a.work = dv + off_wk;
+        rc = deltanet_step(&a, st);
+    }
+    if (e == cudaSuccess && rc == 0) e = cudaMemcpyAsync(b->smem, dv + off_s, HD * D * 2, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && rc == 0) e = cudaMemcpyAsync(b->semem, dv + off_se, HD * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && rc == 0) e = cudaMemcpyAsync(b->y, dv + off_y, HD * 2, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && rc == 0) e = cudaMemcpyAsync(status, dv + off_st, sizeof status, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && st) e = cudaStreamSynchronize(st);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dv);
+    if (e != cudaSuccess) return gdn_fail(e);
+    if (rc) return rc;
+    b->y_exp = status[0];
+    if (status[1]) b->err_conv = 1;
+    if (status[2]) b->err_g = 1;
+    if (status[3]) b->err_se = 1;
+    if (status[4]) b->y_sat = 1;
+    return 0;
+}
+
+extern "C" int gdn_conv_seg_dev(int ncase, int nch, const int16_t *x, const int16_t *w, const int32_t *cfg,
+                                int16_t *sm, int32_t *info, void *stream)
+{
+    if (ncase <= 0 || nch <= 0 || !x || !w || !cfg || !sm || !info || (((uintptr_t)x | (uintptr_t)w) & 7))
+        return -11;
+    gdn_conv_unit_kernel<<<ncase, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(nch, x, w, cfg, sm, info);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : gdn_fail(e);
+}
+
+extern "C" int gdn_silu_dev(int ncase, int n, const int16_t *sm, const int32_t *e_row, int32_t *y, void *stream)
+{
+    if (ncase <= 0 || n <= 0 || !sm || !e_row || !y) return -11;
+    cudaError_t e = upload_blk_tables();
+    if (e != cudaSuccess) return gdn_fail(e);
+    const int total = ncase * n;
+    gdn_silu_unit_kernel<<<(total + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(n, total, sm, e_row, y);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : gdn_fail(e);
+}
+
+extern "C" int gdn_l2norm_dev(int nvec, int N, const int32_t *x, int16_t *k, int16_t *q, void *stream)
+{
+    if (nvec <= 0 || !blk_dim_ok(N) || !x || !k || !q) return -11;
+    cudaError_t e = upload_blk_tables();
+    if (e != cudaSuccess) return gdn_fail(e);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (N == 32) gdn_l2norm_unit_kernel<1><<<nvec, 32, 0, st>>>(x, 5, k, q);
+    else if (N == 64) gdn_l2norm_unit_kernel<2><<<nvec, 32, 0, st>>>(x, 6, k, q);
+    else gdn_l2norm_unit_kernel<4><<<nvec, 32, 0, st>>>(x, 7, k, q);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : gdn_fail(e);
+}
+
+extern "C" int gdn_rmsnorm_bf_dev(int nvec, int N, const int16_t *xm, const int32_t *xe, const int16_t *wm,
+                                  const int32_t *we, int16_t *o, int32_t *o_exp, void *stream)
+{
+    if (nvec <= 0 || !blk_dim_ok(N) || !xm || !xe || !wm || !we || !o || !o_exp) return -11;
+    cudaError_t e = upload_blk_tables();
+    if (e != cudaSuccess) return gdn_fail(e);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (N == 32) gdn_rmsnorm_unit_kernel<1><<<nvec, 32, 0, st>>>(xm, xe, wm, we, o, o_exp);
+    else if (N == 64) gdn_rmsnorm_unit_kernel<2><<<nvec, 32, 0, st>>>(xm, xe, wm, we, o, o_exp);
+    else gdn_rmsnorm_unit_kernel<4><<<nvec, 32, 0, st>>>(xm, xe, wm, we, o, o_exp);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : gdn_fail(e);
+}
+
+extern "C" int gdn_y_emit_dev(int H, int D, const int32_t *ep, const int16_t *po, const int16_t *pz,
+                              int16_t *y, int32_t *status, void *stream)
+{
+    if (H <= 0 || D <= 0 || !ep || !po || !pz || !y || !status) return -11;
+    BlkTailArgs T = {};
+    T.VH = H; T.D = D; T.po = po; T.pz = pz; T.ep = ep; T.y = y; T.status = status;
+    void *ta[] = {&T};
+    cudaError_t e = blk_launch((const void *)gdn_blk_tail_kernel, dim3(1), dim3(1024),
+                               reinterpret_cast<cudaStream_t>(stream), false, ta);
+    return e == cudaSuccess ? 0 : gdn_fail(e);
+}
+
+extern "C" int gdn_emit_chain_dev(int H, int D, const int64_t *o_acc, const int32_t *e_o, const int16_t *zm,
+                                  const int16_t *wm, int we, int z_e, int16_t *y, int32_t *status, void *work,
+                                  void *stream)
+{
+    if (H <= 0 || !blk_dim_ok(D) || !o_acc || !e_o || !zm || !wm || !y || !status || !work
+        || (((uintptr_t)work) & 255))
+        return -11;
+    cudaError_t e = upload_blk_tables();
+    if (e != cudaSuccess) return gdn_fail(e);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    BlkRecArgs R = {};
+    R.KH = 1; R.VH = H; R.w_e = we; R.z_e = z_e; R.zm = zm; R.wm = wm;
+    R.w = blk_work_layout(work, 1, H, D, nullptr);
+    R.o_acc_in = o_acc; R.e_o_in = e_o;
+    if (D == 32) gdn_blk_chain_kernel<32><<<H, 32, 0, st>>>(R);
+    else if (D == 64) gdn_blk_chain_kernel<64><<<H, 32, 0, st>>>(R);
+    else gdn_blk_chain_kernel<128><<<H, 32, 0, st>>>(R);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return gdn_fail(e);
+    return gdn_y_emit_dev(H, D, R.w.ep, R.w.po, R.w.pz, y, status, stream);
+}

@@ -364,3 +364,7 @@ extern "C" int gdn_run_f32(const gdn_f32_args *a, void *stream)
     cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_f32_kernel, *a);
     return e == cudaSuccess ? 0 : gdn_fail(e);
 }
+
+// ------------------------------------------------ the fixed-point block
+
+#include "gdn_block.cuh"

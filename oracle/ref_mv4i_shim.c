@@ -48,3 +48,18 @@ uint8_t *ref_pack_geom(int M, int K, int rows_if, int axi_dw, int w_exp, int out
 void ref_free(void *p) { free(p); }
 
 const int8_t *ref_iq4_nl(void) { return IQ4_NL; }
+
+/* The reference's static byte accessors (ref/matvec_int4.c:267-307) over a
+ * whole image: every weight index [M][K] and every 32-block scale [M][nb]. */
+int ref_dump_layout(const uint8_t *img, size_t len, uint8_t *widx, uint16_t *scale)
+{
+    mv4i_file f;
+    int rc = mv4i_parse(&f, img, len);
+    if (rc) return rc;
+    const int M = (int)f.h.M, K = (int)f.h.K, nb = (K + 31) / 32;
+    for (int r = 0; r < M; r++) {
+        for (int k = 0; k < K; k++) widx[(size_t)r * K + k] = (uint8_t)get_widx(&f, r, k);
+        for (int b = 0; b < nb; b++) scale[(size_t)r * nb + b] = get_scale(&f, r, b);
+    }
+    return 0;
+}

@@ -2,6 +2,8 @@
 and its host-only entry points (parse, byte accessors) match the reference.
 No compute call here needs a GPU."""
 import ctypes as C
+import os
+import subprocess
 
 import numpy as np
 import pytest
@@ -34,19 +36,69 @@ def test_struct_sizes_match_reference_layout(pkg):
     assert C.sizeof(pkg.Result) == 8 * 3 + 4 * 2 + 8 + 8
 
 
-def test_parse_matches_reference(pkg, golden):
-    for g in range(6):
-        img = golden["img%d" % g].tobytes()
+GOLDEN_IMAGES = ["img%d" % g for g in range(6)] + ["lin0_img", "sat0_img"]
+
+
+@pytest.mark.skipif(not O.have_ref(), reason="oracle/_ref not built")
+def test_accessors_match_reference(pkg, golden):
+    """mv4i_parse's header fields and, element by element, mv4i_get_widx /
+    mv4i_get_scale against the reference's own parse and static accessors
+    (ref/matvec_int4.c:161-307, through oracle/_ref) on every golden image:
+    AXI widths 64-256, ROWS_IF 4 and 8, the IQ4_NL and linear codebooks."""
+    L, R = pkg.lib(), O.ref()
+    R.ref_dump_layout.restype = C.c_int
+    R.ref_dump_layout.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
+    for key in GOLDEN_IMAGES:
+        img = golden[key].tobytes()
         pi = pkg.ParsedImage(img)
-        assert pi.rc == 0
-        rc = O.orc().orc_parse  # noqa: F841  (symbol exists)
-        # byte accessors against the oracle's restatement
+        assert pi.rc == 0, key
         h = pi.f.h
-        rng = np.random.default_rng(g)
-        for _ in range(200):
-            r = int(rng.integers(0, h.M))
-            k = int(rng.integers(0, h.K))
-            assert pkg.lib().mv4i_get_widx(C.byref(pi.f), r, k) >= 0
+        M, K, nb = h.M, h.K, (h.K + 31) // 32
+        vals = [C.c_int(0) for _ in range(4)]
+        buf = np.frombuffer(img, np.uint8).copy()
+        assert R.ref_parse(O._p(buf), buf.size, *[C.byref(v) for v in vals]) == 0
+        assert (M, K, h.w_exp, h.out_shift) == tuple(v.value for v in vals), key
+        widx = np.zeros((M, K), np.uint8)
+        scl = np.zeros((M, nb), np.uint16)
+        assert R.ref_dump_layout(O._p(buf), buf.size, O._p(widx), O._p(scl)) == 0
+        got_w = np.array([[L.mv4i_get_widx(C.byref(pi.f), r, k) for k in range(K)] for r in range(M)])
+        got_s = np.array([[L.mv4i_get_scale(C.byref(pi.f), r, b) for b in range(nb)] for r in range(M)])
+        assert np.array_equal(got_w, widx), key
+        assert np.array_equal(got_s, scl), key
+
+
+CONSUMER = os.path.join(os.path.dirname(__file__), "c_consumer", "mv4i_consumer.c")
+
+
+def build_consumer(pkg, out_dir):
+    """gcc a plain C program against include/mv4i_b200.h and -lmv4i_b200."""
+    exe = os.path.join(out_dir, "mv4i_consumer")
+    libdir = os.path.dirname(pkg.LIBPATH)
+    cmd = ["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-O2", "-I" + os.path.join(pkg.ROOT, "include"),
+           "-o", exe, CONSUMER, "-L" + libdir, "-lmv4i_b200", "-Wl,-rpath," + libdir]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return exe
+
+
+def test_c_consumer_builds_and_parses(pkg, golden, tmp_path):
+    """The boundary as a C caller sees it: the header compiles as C11 with
+    warnings as errors, the program links against the shared library, and its
+    mv4i_parse reads every golden image's header as the reference does (no
+    GPU needed for parse)."""
+    exe = build_consumer(pkg, str(tmp_path))
+    for key in GOLDEN_IMAGES:
+        img = golden[key].tobytes()
+        path = tmp_path / (key + ".mv4i")
+        path.write_bytes(img)
+        out = subprocess.run([exe, "parse", str(path)], capture_output=True, text=True, check=True).stdout.split()
+        rc, M, K, w_exp, out_shift = [int(v) for v in out[:5]]
+        pi = pkg.ParsedImage(img)
+        assert (rc, M, K, w_exp, out_shift) == (0, pi.f.h.M, pi.f.h.K, pi.f.h.w_exp, pi.f.h.out_shift)
+    bad = tmp_path / "bad.mv4i"
+    bad.write_bytes(b"\0" * 100)
+    out = subprocess.run([exe, "parse", str(bad)], capture_output=True, text=True, check=True).stdout.split()
+    assert int(out[0]) < 0
 
 
 def _refusal_cases():
