@@ -405,6 +405,8 @@ def run_gdn(args, pkg, L, torch, dev, stream, sp, timed):
 
 DEC_C3 = dict(hidden=2048, n_layers=24, attn_every=4, vocab=151936, ffn=6144, gdn_kh=16, gdn_vh=16, gdn_hd=128,
               att_qh=16, att_kvh=2, att_hd=128, n_rot=32, rope_theta=1.0e6, rms_eps=1e-6, max_ctx=1024)
+DEC_C2 = dict(hidden=2048, n_layers=2, attn_every=2, vocab=2048, ffn=6144, gdn_kh=16, gdn_vh=16, gdn_hd=128,
+              att_qh=16, att_kvh=2, att_hd=128, n_rot=32, rope_theta=1.0e6, rms_eps=1e-6, max_ctx=4096 + 512)
 DEC_C4 = dict(hidden=5120, n_layers=48, attn_every=4, vocab=151936, ffn=17408, gdn_kh=32, gdn_vh=32, gdn_hd=128,
               att_qh=40, att_kvh=8, att_hd=128, n_rot=32, rope_theta=1.0e6, rms_eps=1e-6, max_ctx=8192 + 512)
 
@@ -439,7 +441,7 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
                 raise RuntimeError("dec_step failed %d" % rc)
         return f
 
-    def layer_profile(h, cfg):
+    def layer_profile(h, cfg, reps=1):
         """One step timed layer by layer: per-layer time and the fraction of
         the HBM peak its bytes reach (DeltaNet / attention layers and the LM
         head, averaged by kind).  The persistent step stamps the GPU global
@@ -463,19 +465,22 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
             idx = [D.dec_layer_clock(h, il) for il in range(-1, nl + 1)]
             bounds = [(t[idx[il + 1]] - t[idx[il]]) / 1e3 for il in range(nl + 1)]
         else:
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(nl + 2)]
-            for e in evs:                       # torch creates the CUDA event on first record
-                e.record(stream)
-            torch.cuda.synchronize(dev)
-            arr = (C.c_void_p * nl)(*[C.c_void_p(e.cuda_event) for e in evs[1:nl + 1]])
-            assert D.dec_set_layer_events(h, arr, nl) == 0
-            with torch.cuda.stream(stream):
-                evs[0].record(stream)
-                step_fn(h)()
-                evs[nl + 1].record(stream)
-            torch.cuda.synchronize(dev)
-            assert D.dec_set_layer_events(h, None, 0) == 0
-            bounds = [evs[il].elapsed_time(evs[il + 1]) * 1e3 for il in range(nl + 1)]
+            acc = np.zeros(nl + 1)
+            for _ in range(reps):
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(nl + 2)]
+                for e in evs:                       # torch creates the CUDA event on first record
+                    e.record(stream)
+                torch.cuda.synchronize(dev)
+                arr = (C.c_void_p * nl)(*[C.c_void_p(e.cuda_event) for e in evs[1:nl + 1]])
+                assert D.dec_set_layer_events(h, arr, nl) == 0
+                with torch.cuda.stream(stream):
+                    evs[0].record(stream)
+                    step_fn(h)()
+                    evs[nl + 1].record(stream)
+                torch.cuda.synchronize(dev)
+                assert D.dec_set_layer_events(h, None, 0) == 0
+                acc += [evs[il].elapsed_time(evs[il + 1]) * 1e3 for il in range(nl + 1)]
+            bounds = list(acc / reps)
         kinds = {"deltanet": [], "attention": [], "lm_head": []}
         for il in range(nl + 1):
             us = float(bounds[il])
@@ -566,7 +571,46 @@ def run_decode(args, pkg, torch, dev, stream, sp, timed, rank, world, local_rank
                     "h2d_bytes": nb * 512 * 4, "d2h_bytes_per_step": nb * 4},
         }
 
+    def run_c2():
+        """Config 2: one DeltaNet block and one gated-attention block at hidden
+        2048 (the config-3 layer shapes), KV cache pre-filled to 4096
+        positions with N(0,1), batch 1.  Each block timed with CUDA events
+        around it, averaged over 64 steps; the pair (plus a 2048-entry LM head,
+        2 MB) also as one CUDA-graph replay per step."""
+        cfg = DEC_C2
+        h = create(cfg, 2, 0, 1)
+        assert D.dec_prefill_random(h, 4096, 5) == 0
+        assert D.dec_set(h, 4096, 1) == 0
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step_fn(h)()
+        torch.cuda.synchronize(dev)
+        per_block = layer_profile(h, cfg, reps=64)
+        assert D.dec_set(h, 4096, 1) == 0
+        g = capture(h)
+        for _ in range(args.warmup):
+            g.replay()
+        n = 64
+        ms = timed(g.replay, n)
+        sbytes = D.dec_step_bytes(h)
+        del g
+        D.dec_destroy(h)
+        peak, _ = peaks()
+        us = ms * 1e3 / n
+        res = {"workload": "config 2: 1 DeltaNet block (16/16 heads x 128, conv, gates, out 2048x2048) + SwiGLU "
+                           "6144, then 1 gated-attention block (16 q / 2 KV heads x 128, RoPE 1e6, sigmoid gate) "
+                           "+ SwiGLU 6144; hidden 2048, INT4 g128, KV pre-filled to 4096 with N(0,1), batch 1",
+               "deltanet_block": per_block.get("deltanet"), "attention_block": per_block.get("attention"),
+               "timing": per_block.get("timing") + ", mean of 64 steps",
+               "pair_step_us": round(us, 2), "pair_step_bytes": sbytes,
+               "pair_step_frac_hbm": round(sbytes / (us * 1e-6) / 1e9 / peak, 4),
+               "pair_step_how": "both blocks + final norm + 2048-entry LM head + argmax, one CUDA-graph replay"}
+        if rank == 0:
+            res["cpu_baseline"] = c2_cpu_baseline()
+        return res
+
     if world == 1:
+        out["config2"] = run_c2()
         out["config3"] = run_c3(1)
         out["config3"]["batch8"] = run_c3(8)
 
@@ -695,6 +739,65 @@ def profile_matvec(args):
     ms = e0.elapsed_time(e1) / args.steps
     print(json.dumps({"only": "matvec", "stack": G, "steps": args.steps, "ms_per_step": ms,
                       "GBps": round(G * G128_BYTES / (ms * 1e-3) / 1e9, 1)}))
+
+
+def c2_cpu_baseline(budget_s=4.0):
+    """Config 2 on the host cores: the float64 restatement of the reference's
+    layer_gdn / layer_attn (oracle/dec_oracle.py, pinned to ref/run9b.c) on
+    synthetic weights of the config-2 shapes, KV pre-filled to 4096; mean
+    seconds per block over as many steps as fit the budget.  A port (numpy,
+    the BLAS threads it is given), not the reference's own C, which is
+    compiled for its 9B shapes."""
+    import os as _os
+    import numpy as np
+    from oracle import dec_oracle as DO
+    c = DEC_C2
+    rng = np.random.default_rng(2)
+    H, HD, KH, VH, QH, KVH, F = c["hidden"], 128, c["gdn_kh"], c["gdn_vh"], c["att_qh"], c["att_kvh"], c["ffn"]
+    cd = 2 * KH * HD + VH * HD
+
+    def w(r, k):
+        return rng.standard_normal((r, k)) * 0.02
+    W = {(0, "qkv"): w(cd, H), (0, "z"): w(VH * HD, H), (0, "ab"): w(2 * VH, H), (0, "out"): w(H, VH * HD),
+         (1, "qg"): w(2 * QH * HD, H), (1, "kv"): w(2 * KVH * HD, H), (1, "o"): w(H, QH * HD)}
+    for il in (0, 1):
+        W[il, "gate"], W[il, "up"], W[il, "down"] = w(F, H), w(F, H), w(H, F)
+    P = {}
+    for il in (0, 1):
+        P[il, "attn_norm"] = np.ones(H)
+        P[il, "post_norm"] = np.ones(H)
+    P[0, "conv_w"] = rng.standard_normal(cd * 4) * 0.3
+    P[0, "ssm_a"] = -np.abs(rng.standard_normal(VH))
+    P[0, "dt_bias"] = rng.standard_normal(VH)
+    P[0, "ssm_norm"] = np.ones(HD)
+    P[1, "q_norm"] = np.ones(HD)
+    P[1, "k_norm"] = np.ones(HD)
+    S = {(0, "conv_state"): np.zeros((3, cd)), (0, "rec_state"): np.zeros((VH, HD, HD)),
+         (1, "kcache"): np.zeros((c["max_ctx"], KVH, HD)), (1, "vcache"): np.zeros((c["max_ctx"], KVH, HD))}
+    S[1, "kcache"][:4096] = rng.standard_normal((4096, KVH, HD))
+    S[1, "vcache"][:4096] = rng.standard_normal((4096, KVH, HD))
+    M = DO.Model(c, W, P, S, fp16=False)
+    x = rng.standard_normal(H)
+    tg = ta = 0.0
+    n = 0
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or n == 0:
+        t0 = time.perf_counter()
+        y = M.gdn(0, x)
+        y = M.ffn(0, y)
+        t1 = time.perf_counter()
+        y = M.attn(1, y, 4096 + n)
+        y = M.ffn(1, y)
+        t2 = time.perf_counter()
+        tg += t1 - t0
+        ta += t2 - t1
+        n += 1
+        if 4096 + n >= c["max_ctx"]:
+            break
+    thr = _os.environ.get("OMP_NUM_THREADS") or str(_os.cpu_count())
+    return {"deltanet_block_us": round(tg / n * 1e6, 1), "attention_block_us": round(ta / n * 1e6, 1),
+            "unit": "us per block", "cores": int(thr), "kind": "port",
+            "sample": "%d steps of both config-2 blocks, float64 numpy (oracle/dec_oracle.py)" % n}
 
 
 def gdn_cpu_baseline(budget_s=3.0):

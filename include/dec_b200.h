@@ -16,6 +16,7 @@
 #ifndef DEC_B200_H
 #define DEC_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -188,6 +189,46 @@ int dec_layer_clock(dec_model *m, int layer);
  * slot il as layer il starts, and into slot n_layers after the last layer
  * (the LM head's input).  Copies on the step's stream. */
 int dec_set_residual_seams(dec_model *m, float *buf, int n);
+
+/* ------------------------------------------------ one attention token */
+
+/* One token of gated attention on device buffers, the counterpart of the
+ * reference's attn_token (ref/attn_block_vec.c:533-541) in the decoder's
+ * floating-point mode (ref/run9b.c:786-872, layer_attn without its
+ * projections).  For every KV head: k = NeoX-RoPE(RMSNorm(k_in, k_norm)) and
+ * the raw v go to the fp16 caches at row pos (the append); for every query
+ * head: q = RoPE(RMSNorm(q_in, q_norm)), softmax(q . K[0..pos] / sqrt(128))
+ * over its KV head (GQA, contiguous groups: query head h reads KV head
+ * h / (n_qh / n_kvh)), times V, times sigmoid(gate), fp16 out.  Past
+ * capacity (pos >= max_ctx) the cache is attended as it stands.
+ *   qg       [n_qh][2][128] fp32: q then gate, per head (the reference's qg)
+ *   kv       [2][n_kvh][128] fp32: k rows, then v rows
+ *   q_norm, k_norm [128] fp32; eps the RMSNorm epsilon
+ *   d_pos    device int32: the position this token writes and attends up to
+ *   kcache, vcache fp16 [max_ctx][n_kvh][128]
+ *   y        fp16 [n_qh][128]; q_out (optional) fp32 [n_qh][128] the
+ *            normalised, rotated q
+ *   work     gated_attn_work_bytes(n_qh, max_ctx) bytes of device memory
+ * Two launches (flash decoding over chunks of 32 or 64 positions, then the
+ * combine with the gate); pdl makes the first a programmatic dependent of the
+ * kernel before it in the stream.  Head dim 128, n_qh / n_kvh <= 32, n_rot
+ * even and <= 128, max_ctx <= 65536.  Returns 0, -11 or -20. */
+typedef struct {
+    int32_t         n_qh, n_kvh, head_dim, n_rot;
+    float           rope_theta, eps;
+    const float    *qg, *kv;
+    const float    *q_norm, *k_norm;
+    const int32_t  *d_pos;
+    int32_t         max_ctx;
+    uint16_t       *kcache, *vcache;
+    uint16_t       *y;
+    float          *q_out;
+    void           *work;
+    int32_t         pdl;
+} gated_attn_args;
+
+size_t gated_attn_work_bytes(int n_qh, int max_ctx);
+int gated_attn(const gated_attn_args *a, void *stream);
 
 #ifdef __cplusplus
 }

@@ -222,7 +222,10 @@ int mv4i_launch(const mv4i_job *jobs, int njobs, void *d_scratch, void *stream);
  *
  * The first call on a device looks up the array's device address with that
  * device current (cudaGetSymbolAddress), so make that first call before any
- * stream capture.  Each call clears the counters it uses on `stream`
+ * stream capture.  The looked-up address is kept for the life of the
+ * process: it does not survive cudaDeviceReset (or any other teardown of the
+ * device's primary context), after which this entry point must not be called
+ * in that process.  Each call clears the counters it uses on `stream`
  * (cudaMemsetAsync) before its kernel.  All calls on one device share the
  * array and it keeps the last call's contents, so calls that overlap on the
  * GPU (other streams, other host threads) race.  More than

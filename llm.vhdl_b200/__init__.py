@@ -195,7 +195,18 @@ class DecConfig(C.Structure):
                 ("batch", C.c_int32)]
 
 
+class GatedAttnArgs(C.Structure):
+    """gated_attn_args of include/dec_b200.h (device buffers)."""
+    _fields_ = [("n_qh", C.c_int32), ("n_kvh", C.c_int32), ("head_dim", C.c_int32), ("n_rot", C.c_int32),
+                ("rope_theta", C.c_float), ("eps", C.c_float), ("qg", C.c_void_p), ("kv", C.c_void_p),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("d_pos", C.c_void_p), ("max_ctx", C.c_int32),
+                ("kcache", C.c_void_p), ("vcache", C.c_void_p), ("y", C.c_void_p), ("q_out", C.c_void_p),
+                ("work", C.c_void_p), ("pdl", C.c_int32)]
+
+
 DEC_EXPORTS = {
+    "gated_attn_work_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "gated_attn": (C.c_int, [C.POINTER(GatedAttnArgs), C.c_void_p]),
     "dec_create": (C.c_int, [C.POINTER(DecConfig), C.c_uint64, C.c_int, C.c_int, C.c_int,
                              C.POINTER(C.c_void_p)]),
     "dec_destroy": (C.c_int, [C.c_void_p]),

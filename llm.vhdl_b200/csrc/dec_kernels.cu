@@ -12,6 +12,7 @@
 #include <stdint.h>
 #include <math.h>
 #include "dec_internal.h"
+#include "../../include/dec_b200.h"
 
 extern "C" int mv4i_g_cuda_err;
 
@@ -634,3 +635,28 @@ int dec_k_advance_p2p(void *const *regions, int rank, int world, int hidden, uns
 }
 
 }  // extern "C"
+
+// the public one-token entry (include/dec_b200.h): chunks of 32 positions up
+// to a 4096-position cache, 64 beyond (the decode step's choice)
+static int gated_attn_chunk(int max_ctx) { return max_ctx <= 4096 ? 32 : 64; }
+
+extern "C" size_t gated_attn_work_bytes(int n_qh, int max_ctx)
+{
+    if (n_qh <= 0 || max_ctx <= 0 || max_ctx > 65536) return 0;
+    const int ch = gated_attn_chunk(max_ctx);
+    return (size_t)4 * n_qh * ((max_ctx + ch - 1) / ch) * (ATT_HD + 4);
+}
+
+extern "C" int gated_attn(const gated_attn_args *a, void *stream)
+{
+    if (!a || a->head_dim != ATT_HD || a->n_qh <= 0 || a->n_kvh <= 0 || !a->qg || !a->kv || !a->q_norm
+        || !a->k_norm || !a->d_pos || !a->kcache || !a->vcache || !a->y || !a->work || a->max_ctx <= 0
+        || a->max_ctx > 65536)
+        return -11;
+    if ((((uintptr_t)a->qg) | ((uintptr_t)a->kv) | ((uintptr_t)a->q_norm) | ((uintptr_t)a->k_norm)
+         | ((uintptr_t)a->kcache) | ((uintptr_t)a->vcache) | ((uintptr_t)a->work)) & 15)
+        return -11;
+    return dec_k_attention(a->qg, a->kv, a->q_norm, a->k_norm, a->n_qh, a->n_kvh, a->n_rot, a->rope_theta, a->eps,
+                           a->d_pos, a->max_ctx, gated_attn_chunk(a->max_ctx), (float *)a->work, a->q_out,
+                           a->kcache, a->vcache, a->y, 1, stream, a->pdl);
+}

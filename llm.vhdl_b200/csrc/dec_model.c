@@ -103,6 +103,7 @@ struct dec_model {
      * (0 never, 1 batches of 2+ sequences, 2 always) into xst */
     int       prestage;
     uint8_t  *xst;
+    long long xst_bytes;                 /* its capacity: every staging is checked against it */
     int32_t  *layer_clock;               /* [n_layers + 1]: clock index at each layer's end */
     void     *allocs[MAX_ALLOCS];
     int       nalloc;
@@ -295,6 +296,7 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
         const long long xb = dec_k_stage_bytes(kx, m->B);
         if (xb < 0) { rc = -11; goto bad; }
         TRY(dalloc(m, (void **)&m->xst, (size_t)xb));
+        m->xst_bytes = xb;
         const char *ps = getenv("DEC_PRESTAGE");
         m->prestage = ps && ps[0] >= '0' && ps[0] <= '2' ? ps[0] - '0' : 1;
     }
@@ -546,6 +548,8 @@ static int em_matvec(emit_t *E, const dmv_params *P)
         /* every CTA of the matvec would stage all the batch's vectors: stage
          * them once, the matvec's CTAs copy the blocks */
         dmv_params Q = *P;
+        const long long need = dec_k_stage_bytes(P->K, P->nvec > 0 ? P->nvec : 1);
+        if (need < 0 || need > m->xst_bytes) return -11;     /* an input wider than the staging block */
         Q.xst = m->xst;
         CK(dec_k_stage(&Q, E->s, E->pdl));
         return dec_k_matvec(&Q, E->s, E->pdl);

@@ -73,6 +73,8 @@ def test_noalloc_matches_launch_twice(cuda, pkg, golden):
         mode = int(golden[k + "_meta"][7])
         got = want[i][2] if mode == 2 else (want[i][1] if mode == 0 else want[i][0])
         assert np.array_equal(got.astype(np.int64), golden[k + "_y"]), k
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
     for call in range(2):
         for o in outs:
             for t in o[1:]:
@@ -84,6 +86,11 @@ def test_noalloc_matches_launch_twice(cuda, pkg, golden):
             for a, b in zip(want[i], got[i]):
                 assert np.array_equal(a, b), (call, KEYS[i])
         assert np.array_equal(want_st, got_st), call
+    # the entry point allocated nothing: the device's free memory is unchanged
+    # across both calls (torch's own caching allocator is not involved: every
+    # test buffer above existed before the first call)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] >= free0
     for _, dm in mats:
         L.mv4i_dmat_free(C.byref(dm))
 
