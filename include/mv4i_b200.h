@@ -29,6 +29,7 @@
  *   -12      tensor-parallel reduction refused: y_exp spread > 17
  *   -13      tensor-parallel reduction refused: out_shift differs between shards
  *   -14      mv4i_launch_noalloc: more jobs than its fixed counter array holds
+ *   -15      tensor-parallel message from another collective (sequence number)
  *   -20      CUDA runtime error (mv4i_last_cuda_error() has the code)
  *
  * Streams are passed as void* (a cudaStream_t; NULL = legacy default stream)
@@ -256,6 +257,60 @@ int mv4i_g128_matvec_host(const mv4i_dmat *w, int count, const uint16_t *h_x, ui
 int mv4i_tp_reduce(int N, int n_rows, const int64_t *d_parts, const int32_t *d_y_exps,
                    const int32_t *d_out_shifts, int16_t *d_out_mant, int32_t *d_y32,
                    mv4i_status *d_status, void *stream);
+
+/* ------------------------------------------- tensor-parallel collective */
+
+/* The transport of E (tp-collective-design.md:153-180): the message one rank
+ * sends every peer for one row-parallel block -- its n_rows unrounded s48
+ * partials in 64-bit slots, then a trailer of its y_exp, its out_shift and
+ * the collective's SEQUENCE number, the sequence word stored last.  The
+ * receiver accepts a message only when its sequence number is the one it
+ * expects for this collective: a message left from collective k read as
+ * collective k+1 is refused (-15), not summed.  Refusals (all ranks alike):
+ *   -15  a message carries another collective's sequence number
+ *   -12  y_exp spread > 17          -13  out_shift differs between ranks */
+typedef struct {
+    int32_t  y_exp;
+    int32_t  out_shift;
+    uint32_t seq;
+    uint32_t pad_;
+} mv4i_tp_trailer;
+
+/* bytes of one message: 8 * n_rows, padded to 16, plus the 16-byte trailer */
+size_t mv4i_tp_msg_bytes(int n_rows);
+
+/* Host memory: write one message (payload, then trailer, sequence last), and
+ * check N received messages for collective `seq` (their trailers into
+ * y_exps / out_shifts, either may be NULL).  Returns 0, -11, -15, -12, -13. */
+int mv4i_tp_msg_pack(const int64_t *y_acc, int n_rows, int y_exp, int out_shift, uint32_t seq, void *msg);
+int mv4i_tp_msgs_check(int N, int n_rows, const void *const *msgs, uint32_t seq, int32_t *y_exps,
+                       int32_t *out_shifts);
+
+/* Device memory: the same message written by a kernel (y_exp read from the
+ * PARTIAL job's device status when d_part_status is non-NULL, else y_exp),
+ * and the E 2.1 reduction of N messages stored msg_bytes apart in d_msgs,
+ * with the sequence / spread / out_shift checks done on the device
+ * (d_status->err = -15 / -12 / -13, outputs untouched). */
+int mv4i_tp_msg_pack_dev(const int64_t *d_y_acc, int n_rows, const mv4i_status *d_part_status, int y_exp,
+                         int out_shift, uint32_t seq, void *d_msg, void *stream);
+int mv4i_tp_reduce_msgs(int N, int n_rows, const void *d_msgs, uint32_t seq, int16_t *d_out_mant, int32_t *d_y32,
+                        mv4i_status *d_status, void *stream);
+
+/* One row-parallel golden block between the ranks of an NCCL communicator
+ * (one process per GPU): pack this rank's message, all-gather the messages
+ * (ncclAllGather), reduce them identically on every rank.  d_work holds
+ * (world + 1) * mv4i_tp_msg_bytes(n_rows) bytes.  seq must advance by one per
+ * collective and be the same on every rank.  The communicator comes from
+ * mv4i_tp_comm_create with the 128 bytes rank 0 got from mv4i_tp_unique_id
+ * (shipped to the other ranks by any transport).  Row-parallel g128 blocks
+ * sum their fp32 partials with mv4i_tp_allreduce_f32. */
+int mv4i_tp_unique_id(uint8_t id[128]);
+int mv4i_tp_comm_create(const uint8_t id[128], int rank, int world, int device, void **comm);
+int mv4i_tp_comm_destroy(void *comm);
+int mv4i_tp_row_parallel(void *comm, const int64_t *d_y_acc, int n_rows, const mv4i_status *d_part_status,
+                         int out_shift, uint32_t seq, void *d_work, int16_t *d_out_mant, int32_t *d_y32,
+                         mv4i_status *d_status, void *stream);
+int mv4i_tp_allreduce_f32(void *comm, float *d_y, int n, void *stream);
 
 /* ------------------------------------------------- activation BFP pack */
 

@@ -37,7 +37,7 @@ def build(verbose=False):
     os.makedirs(LIBDIR, exist_ok=True)
     cmds = [
         [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
-         "-shared", "-o", LIBPATH, *[os.path.join(HERE, s) for s in SOURCES], "-lpthread"],
+         "-shared", "-o", LIBPATH, *[os.path.join(HERE, s) for s in SOURCES], "-lpthread", "-lnccl"],
         [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
          "-shared", "-o", DEC_LIBPATH, *[os.path.join(HERE, s) for s in DEC_SOURCES],
          "-L" + LIBDIR, "-lmv4i_b200", "-lnccl", "-Xlinker", "-rpath=$ORIGIN"],
@@ -164,6 +164,19 @@ EXPORTS = {
                                  C.c_void_p, C.c_void_p]),
     "gdn_emit_chain_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                      C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mv4i_tp_msg_bytes": (C.c_size_t, [C.c_int]),
+    "mv4i_tp_msg_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_void_p]),
+    "mv4i_tp_msgs_check": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p]),
+    "mv4i_tp_msg_pack_dev": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint32, C.c_void_p,
+                                       C.c_void_p]),
+    "mv4i_tp_reduce_msgs": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p]),
+    "mv4i_tp_unique_id": (C.c_int, [C.c_void_p]),
+    "mv4i_tp_comm_create": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "mv4i_tp_comm_destroy": (C.c_int, [C.c_void_p]),
+    "mv4i_tp_row_parallel": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_uint32, C.c_void_p,
+                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mv4i_tp_allreduce_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "mv4i_last_cuda_error": (C.c_int, []),
     "mv4i_version": (C.c_char_p, []),
 }

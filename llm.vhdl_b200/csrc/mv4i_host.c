@@ -474,3 +474,50 @@ out:
 }
 
 const char *mv4i_version(void) { return "llm.vhdl_b200 mv4i 0.1 (sm_100a)"; }
+
+/* ------------------------------------------- tensor-parallel messages */
+
+size_t mv4i_tp_msg_bytes(int n_rows)
+{
+    if (n_rows <= 0) return 0;
+    return (((size_t)n_rows * 8 + 15) & ~(size_t)15) + sizeof(mv4i_tp_trailer);
+}
+
+int mv4i_tp_msg_pack(const int64_t *y_acc, int n_rows, int y_exp, int out_shift, uint32_t seq, void *msg)
+{
+    if (!y_acc || !msg || n_rows <= 0) return -11;
+    uint8_t *m = (uint8_t *)msg;
+    memcpy(m, y_acc, (size_t)n_rows * 8);
+    volatile mv4i_tp_trailer *t = (volatile mv4i_tp_trailer *)(m + mv4i_tp_msg_bytes(n_rows) - sizeof(mv4i_tp_trailer));
+    t->y_exp = y_exp;
+    t->out_shift = out_shift;
+    t->pad_ = 0;
+    __atomic_thread_fence(__ATOMIC_RELEASE);   /* the sequence word is stored last */
+    t->seq = seq;
+    return 0;
+}
+
+int mv4i_tp_msgs_check(int N, int n_rows, const void *const *msgs, uint32_t seq, int32_t *y_exps,
+                       int32_t *out_shifts)
+{
+    if (N <= 0 || N > 64 || n_rows <= 0 || !msgs) return -11;
+    const size_t off = mv4i_tp_msg_bytes(n_rows) - sizeof(mv4i_tp_trailer);
+    int ymin = 0, ymax = 0, osh0 = 0, rc = 0;
+    for (int c = 0; c < N; c++) {
+        if (!msgs[c]) return -11;
+        const mv4i_tp_trailer *t = (const mv4i_tp_trailer *)((const uint8_t *)msgs[c] + off);
+        const uint32_t sq = __atomic_load_n(&t->seq, __ATOMIC_ACQUIRE);
+        if (sq != seq) return -15;
+        if (y_exps) y_exps[c] = t->y_exp;
+        if (out_shifts) out_shifts[c] = t->out_shift;
+        if (c == 0) { ymin = ymax = t->y_exp; osh0 = t->out_shift; }
+        else {
+            ymin = t->y_exp < ymin ? t->y_exp : ymin;
+            ymax = t->y_exp > ymax ? t->y_exp : ymax;
+            if (t->out_shift != osh0) rc = -13;
+        }
+    }
+    if (!rc && ymax - ymin > 17) rc = -12;
+    return rc;
+}
+

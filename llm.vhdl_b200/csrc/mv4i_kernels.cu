@@ -27,6 +27,8 @@
 // matter; the g128 fp32 reduction uses a fixed shuffle tree.
 
 #include <cuda_runtime.h>
+#include <nccl.h>
+#include <string.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -1225,34 +1227,47 @@ extern "C" int mv4i_launch_noalloc(const mv4i_job *jobs, int njobs, void *stream
 
 // ------------------------------------------------ tensor-parallel reduction
 
+// the shards' partials as one [N][n_rows] array, or as N messages (payload
+// then trailer) msg_bytes apart
+struct TpFlat {
+    const int64_t *p; int n;
+    __device__ int64_t at(int c, int r) const { return p[(int64_t)c * n + r]; }
+};
+struct TpMsgs {
+    const uint8_t *m; size_t mb;
+    __device__ int64_t at(int c, int r) const { return reinterpret_cast<const int64_t *>(m + (size_t)c * mb)[r]; }
+};
+
 // One CTA: n_rows is a hidden size (<= a few 10^4), so a single pass with a
 // block-level maximum is cheaper than a multi-CTA completion protocol.
-__global__ void __launch_bounds__(1024)
-tp_reduce_kernel(int N, int n_rows, const int64_t *parts, const int32_t *y_exps,
-                 const int32_t *out_shifts, int16_t *out, int32_t *y32, mv4i_status *status)
+// s_ye / s_os hold the N shards' y_exp and out_shift; err0 is a refusal found
+// before (the message sequence check), reported instead of reducing.
+template <typename SRC>
+__device__ void tp_reduce_body(int N, int n_rows, const SRC src, const int32_t *s_ye, const int32_t *s_os, int err0,
+                               int16_t *out, int32_t *y32, mv4i_status *status)
 {
     __shared__ uint32_t s_amax, s_sat;
     __shared__ int s_ymin, s_err;
     if (threadIdx.x == 0) {
-        int ymin = y_exps[0], ymax = y_exps[0], err = 0;
+        int ymin = s_ye[0], ymax = s_ye[0], err = 0;
         for (int c = 1; c < N; c++) {
-            ymin = min(ymin, y_exps[c]); ymax = max(ymax, y_exps[c]);
-            if (out_shifts[c] != out_shifts[0]) err = -13;
+            ymin = min(ymin, s_ye[c]); ymax = max(ymax, s_ye[c]);
+            if (s_os[c] != s_os[0]) err = -13;
         }
         if (!err && ymax - ymin > 17) err = -12;
-        s_ymin = ymin; s_err = err; s_amax = 0; s_sat = 0;
+        s_ymin = ymin; s_err = err0 ? err0 : err; s_amax = 0; s_sat = 0;
     }
     __syncthreads();
     if (s_err) {
         if (threadIdx.x == 0) { mv4i_status st = {}; st.err = s_err; *status = st; }
         return;
     }
-    const int ymin = s_ymin, osh = out_shifts[0];
+    const int ymin = s_ymin, osh = s_os[0];
     uint32_t amax = 0, nsat = 0;
     for (int r = threadIdx.x; r < n_rows; r += blockDim.x) {
-        int64_t s = 0;
-        for (int c = 0; c < N; c++) s += floor_shr(parts[(int64_t)c * n_rows + r], y_exps[c] - ymin);
-        const int64_t rs = round_shift(s, osh);
+        int64_t acc = 0;
+        for (int c = 0; c < N; c++) acc += floor_shr(src.at(c, r), s_ye[c] - ymin);
+        const int64_t rs = round_shift(acc, osh);
         int32_t y;
         if (rs > 2147483647LL) { y = 2147483647; nsat++; }
         else if (rs < -2147483648LL) { y = (int32_t)0x80000000u; nsat++; }
@@ -1270,9 +1285,9 @@ tp_reduce_kernel(int N, int n_rows, const int64_t *parts, const int32_t *y_exps,
     int ns = msb_pos(s_amax) - 14;
     if (ns < 0) ns = 0;
     for (int r = threadIdx.x; r < n_rows; r += blockDim.x) {
-        int64_t s = 0;
-        for (int c = 0; c < N; c++) s += floor_shr(parts[(int64_t)c * n_rows + r], y_exps[c] - ymin);
-        const int64_t rs = round_shift(s, osh);
+        int64_t acc = 0;
+        for (int c = 0; c < N; c++) acc += floor_shr(src.at(c, r), s_ye[c] - ymin);
+        const int64_t rs = round_shift(acc, osh);
         const int64_t y = rs > 2147483647LL ? 2147483647LL : (rs < -2147483648LL ? -2147483648LL : rs);
         out[r] = sat16(round_shift(y, ns));
     }
@@ -1282,6 +1297,155 @@ tp_reduce_kernel(int N, int n_rows, const int64_t *parts, const int32_t *y_exps,
         st.sat_event = s_sat ? 1 : 0; st.sat_count = s_sat; st.err = 0;
         *status = st;
     }
+}
+
+__global__ void __launch_bounds__(1024)
+tp_reduce_kernel(int N, int n_rows, const int64_t *parts, const int32_t *y_exps,
+                 const int32_t *out_shifts, int16_t *out, int32_t *y32, mv4i_status *status)
+{
+    __shared__ int32_t s_ye[64], s_os[64];
+    if (threadIdx.x < N) { s_ye[threadIdx.x] = y_exps[threadIdx.x]; s_os[threadIdx.x] = out_shifts[threadIdx.x]; }
+    __syncthreads();
+    TpFlat src{parts, n_rows};
+    tp_reduce_body(N, n_rows, src, s_ye, s_os, 0, out, y32, status);
+}
+
+// E 2.1 over N messages: each message's sequence word must be `seq` (a
+// message of another collective is refused with -15 before anything is read
+// from its payload), then the trailers give the shards' y_exp / out_shift.
+__global__ void __launch_bounds__(1024)
+tp_reduce_msgs_kernel(int N, int n_rows, const uint8_t *msgs, size_t mb, uint32_t seq, int16_t *out, int32_t *y32,
+                      mv4i_status *status)
+{
+    __shared__ int32_t s_ye[64], s_os[64];
+    __shared__ int s_bad;
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+    if (threadIdx.x < N) {
+        const mv4i_tp_trailer *t = reinterpret_cast<const mv4i_tp_trailer *>(msgs + (size_t)threadIdx.x * mb + mb
+                                                                              - sizeof(mv4i_tp_trailer));
+        uint32_t sq;
+        asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(sq) : "l"(&t->seq) : "memory");
+        if (sq != seq) atomicOr(&s_bad, 1);
+        s_ye[threadIdx.x] = t->y_exp;
+        s_os[threadIdx.x] = t->out_shift;
+    }
+    __syncthreads();
+    TpMsgs src{msgs, mb};
+    tp_reduce_body(N, n_rows, src, s_ye, s_os, s_bad ? -15 : 0, out, y32, status);
+}
+
+// this rank's message: payload, trailer, then (after a fence) the sequence word
+__global__ void tp_msg_pack_kernel(const int64_t *y_acc, int n_rows, const mv4i_status *pst, int y_exp, int out_shift,
+                                   uint32_t seq, uint8_t *msg, size_t mb)
+{
+    int64_t *pay = reinterpret_cast<int64_t *>(msg);
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n_rows; r += gridDim.x * blockDim.x) pay[r] = y_acc[r];
+    __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        mv4i_tp_trailer *t = reinterpret_cast<mv4i_tp_trailer *>(msg + mb - sizeof(mv4i_tp_trailer));
+        t->y_exp = pst ? pst->y_exp : y_exp;
+        t->out_shift = out_shift;
+        t->pad_ = 0;
+    }
+}
+
+__global__ void tp_msg_seq_kernel(uint8_t *msg, size_t mb, uint32_t seq)
+{
+    mv4i_tp_trailer *t = reinterpret_cast<mv4i_tp_trailer *>(msg + mb - sizeof(mv4i_tp_trailer));
+    __threadfence();
+    asm volatile("st.release.gpu.u32 [%0], %1;" :: "l"(&t->seq), "r"(seq) : "memory");
+}
+
+extern "C" int mv4i_tp_msg_pack_dev(const int64_t *d_y_acc, int n_rows, const mv4i_status *d_part_status, int y_exp,
+                                    int out_shift, uint32_t seq, void *d_msg, void *stream)
+{
+    if (!d_y_acc || !d_msg || n_rows <= 0 || (((uintptr_t)d_msg) & 15)) return -11;
+    const size_t mb = mv4i_tp_msg_bytes(n_rows);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    tp_msg_pack_kernel<<<(n_rows + 255) / 256 < 64 ? (n_rows + 255) / 256 : 64, 256, 0, st>>>(
+        d_y_acc, n_rows, d_part_status, y_exp, out_shift, seq, static_cast<uint8_t *>(d_msg), mb);
+    // the sequence word in a launch of its own: stream order puts it after
+    // every block's payload stores
+    tp_msg_seq_kernel<<<1, 1, 0, st>>>(static_cast<uint8_t *>(d_msg), mb, seq);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}
+
+extern "C" int mv4i_tp_reduce_msgs(int N, int n_rows, const void *d_msgs, uint32_t seq, int16_t *d_out_mant,
+                                   int32_t *d_y32, mv4i_status *d_status, void *stream)
+{
+    if (N <= 0 || N > 64 || n_rows <= 0 || !d_msgs || !d_out_mant || !d_status || (((uintptr_t)d_msgs) & 15))
+        return -11;
+    tp_reduce_msgs_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        N, n_rows, static_cast<const uint8_t *>(d_msgs), mv4i_tp_msg_bytes(n_rows), seq, d_out_mant, d_y32, d_status);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e);
+}
+
+// ---------------------------------------------------- NCCL communicator
+
+struct Mv4iTpComm { ncclComm_t comm; int rank, world, device; };
+
+static int nccl_fail(ncclResult_t r) { mv4i_g_cuda_err = 1000 + (int)r; return -20; }
+
+extern "C" int mv4i_tp_unique_id(uint8_t id[128])
+{
+    if (!id) return -11;
+    ncclUniqueId u;
+    const ncclResult_t r = ncclGetUniqueId(&u);
+    if (r != ncclSuccess) return nccl_fail(r);
+    memcpy(id, &u, sizeof u < 128 ? sizeof u : 128);
+    return 0;
+}
+
+extern "C" int mv4i_tp_comm_create(const uint8_t id[128], int rank, int world, int device, void **comm)
+{
+    if (!id || !comm || world < 1 || world > 64 || rank < 0 || rank >= world) return -11;
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e);
+    Mv4iTpComm *c = static_cast<Mv4iTpComm *>(calloc(1, sizeof(Mv4iTpComm)));
+    if (!c) return -11;
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof u < 128 ? sizeof u : 128);
+    const ncclResult_t r = ncclCommInitRank(&c->comm, world, u, rank);
+    if (r != ncclSuccess) { free(c); return nccl_fail(r); }
+    c->rank = rank; c->world = world; c->device = device;
+    *comm = c;
+    return 0;
+}
+
+extern "C" int mv4i_tp_comm_destroy(void *comm)
+{
+    if (!comm) return -11;
+    Mv4iTpComm *c = static_cast<Mv4iTpComm *>(comm);
+    const ncclResult_t r = ncclCommDestroy(c->comm);
+    free(c);
+    return r == ncclSuccess ? 0 : nccl_fail(r);
+}
+
+extern "C" int mv4i_tp_row_parallel(void *comm, const int64_t *d_y_acc, int n_rows, const mv4i_status *d_part_status,
+                                    int out_shift, uint32_t seq, void *d_work, int16_t *d_out_mant, int32_t *d_y32,
+                                    mv4i_status *d_status, void *stream)
+{
+    if (!comm || !d_y_acc || !d_work || !d_out_mant || !d_status || !d_part_status || n_rows <= 0) return -11;
+    Mv4iTpComm *c = static_cast<Mv4iTpComm *>(comm);
+    const size_t mb = mv4i_tp_msg_bytes(n_rows);
+    uint8_t *recv = static_cast<uint8_t *>(d_work), *send = recv + (size_t)c->world * mb;
+    int rc = mv4i_tp_msg_pack_dev(d_y_acc, n_rows, d_part_status, 0, out_shift, seq, send, stream);
+    if (rc) return rc;
+    const ncclResult_t r = ncclAllGather(send, recv, mb, ncclUint8, c->comm, reinterpret_cast<cudaStream_t>(stream));
+    if (r != ncclSuccess) return nccl_fail(r);
+    return mv4i_tp_reduce_msgs(c->world, n_rows, recv, seq, d_out_mant, d_y32, d_status, stream);
+}
+
+extern "C" int mv4i_tp_allreduce_f32(void *comm, float *d_y, int n, void *stream)
+{
+    if (!comm || !d_y || n <= 0) return -11;
+    Mv4iTpComm *c = static_cast<Mv4iTpComm *>(comm);
+    const ncclResult_t r = ncclAllReduce(d_y, d_y, (size_t)n, ncclFloat32, ncclSum, c->comm,
+                                         reinterpret_cast<cudaStream_t>(stream));
+    return r == ncclSuccess ? 0 : nccl_fail(r);
 }
 
 extern "C" int mv4i_tp_reduce(int N, int n_rows, const int64_t *d_parts, const int32_t *d_y_exps,

@@ -85,3 +85,15 @@ def device_read(torch, ptr, shape, dtype):
     """Copy device memory at ptr into a new numpy array of `dtype`."""
     torch.cuda.synchronize()
     return device_view(torch, ptr, shape, dtype).cpu().numpy().view(np.dtype(dtype)).copy()
+
+
+def split(n, world, rank, align=1):
+    """Contiguous [start, start+count) of n items for `rank`, in units of
+    `align` (the last ranks take the remainder): a row-parallel K-slice."""
+    units = (n + align - 1) // align
+    per, extra = units // world, units % world
+    u0 = rank * per + min(rank, extra)
+    u1 = u0 + per + (1 if rank < extra else 0)
+    s, e = u0 * align, min(n, u1 * align)
+    return s, max(0, e - s)
+

@@ -3,16 +3,23 @@
 Each rank packs its own K-slice of a matrix (the reference's row-parallel
 split, ref/matvec_int4.c:1124-1197 emulates the same in one process),
 BFP-packs its own x slice, runs PARTIAL mode (the CPU oracle stands in for
-the GPU matvec here), and the partials are all-gathered through
-llm.vhdl_b200.tp; the E 2.1 reduction (the oracle's, standing in for
-mv4i_tp_reduce) must give the same answer on every rank, stay within the
-reference's stated bound of the exact sum, and refuse a y_exp spread above 17
-or an out_shift mismatch on every rank alike.  Failure paths are made on the
-host: a rank that leaves before the collective, and a mismatched shard.
+the GPU matvec here), and writes its E message -- payload, then the trailer
+{y_exp, out_shift, sequence number}, sequence last -- with the library's
+mv4i_tp_msg_pack.  The messages travel by a gloo all-gather (the transport a
+host-side caller might use; GPUs use mv4i_tp_row_parallel's NCCL
+all-gather), every rank checks them with the library's mv4i_tp_msgs_check,
+and the E 2.1 reduction (the oracle's, standing in for the device's) must
+give the same answer on every rank and stay within the reference's stated
+bound of the exact sum.  Refusals on every rank alike: a y_exp spread above
+17, an out_shift mismatch, and a message carrying the previous collective's
+sequence number (E 2.3).  Failure paths are made on the host: a rank that
+leaves before the collective.
 """
 import os
 import socket
 import sys
+
+import ctypes as C
 
 import numpy as np
 import pytest
@@ -37,9 +44,9 @@ def _worker(rank, world, port, mode, q):
         import torch
         import torch.distributed as dist
         sys.path.insert(0, os.path.join(ROOT, "tests"))
-        from conftest import load_package
-        load_package()
-        import llmvhdl_b200.tp as TP
+        from conftest import load_package, split
+        pkg = load_package()
+        L = pkg.lib()
 
         import oracle as O
         dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank,
@@ -49,7 +56,7 @@ def _worker(rank, world, port, mode, q):
         idx = rng.integers(0, 16, (M, K), dtype=np.uint8)
         scl = rng.integers(8000, 32000, (M, K // 32), dtype=np.uint16)
         u = rng.integers(-(1 << 24), 1 << 24, K)              # the producer's s32-grid activation
-        k0, kn = TP.split(K, world, rank, align=128)
+        k0, kn = split(K, world, rank, align=128)
         out_shift = 8 if mode != "oshift" or rank == 0 else 9
         img = O.pack(M, kn, 4, 128, 1, out_shift, O.IQ4_NL, idx[:, k0:k0 + kn],
                      scl[:, k0 // 32:(k0 + kn) // 32])
@@ -67,14 +74,23 @@ def _worker(rank, world, port, mode, q):
             q.put((rank, "left"))
             return                                            # never joins the collective
 
-        def reduce_fn(parts, ye, osh):
-            prc, out, oe, y32, sat = O.tp_reduce(list(parts.numpy()), list(ye.numpy()), list(osh.numpy()))
-            return prc, out, oe, y32
-
+        seq = 41                                              # this collective's sequence number
         try:
-            prc, out, oe, y32 = TP.row_parallel_golden(torch.from_numpy(r["y_acc"]), r["y_exp"],
-                                                       out_shift, reduce_fn)
-            q.put((rank, (prc, out.tolist(), oe, y32.tolist(), r["y_exp"])))
+            mb = L.mv4i_tp_msg_bytes(M)
+            msg = np.zeros(mb, np.uint8)
+            my_seq = seq - 1 if (mode == "stale" and rank == world - 1) else seq
+            assert L.mv4i_tp_msg_pack(r["y_acc"].ctypes.data, M, r["y_exp"], out_shift, my_seq, msg.ctypes.data) == 0
+            bufs = [torch.empty(mb, dtype=torch.uint8) for _ in range(world)]
+            dist.all_gather(bufs, torch.from_numpy(msg))
+            arrs = [b.numpy() for b in bufs]
+            ptrs = (C.c_void_p * world)(*[a.ctypes.data for a in arrs])
+            ye = np.zeros(world, np.int32)
+            osh = np.zeros(world, np.int32)
+            lrc = L.mv4i_tp_msgs_check(world, M, ptrs, seq, ye.ctypes.data, osh.ctypes.data)
+            parts = [a[:8 * M].view(np.int64).copy() for a in arrs]
+            prc, out, oe, y32, sat = O.tp_reduce(parts, list(ye), list(osh)) if lrc != -15 else (None,) * 5
+            q.put((rank, (lrc, prc, None if out is None else out.tolist(), oe,
+                          None if y32 is None else y32.tolist(), r["y_exp"])))
         except Exception as e:  # noqa: BLE001
             q.put((rank, "error: " + type(e).__name__))
         dist.destroy_process_group()
@@ -104,12 +120,10 @@ def _run(world, mode):
 def test_row_parallel_golden_identical_on_ranks(world):
     res = _run(world, "ok")
     assert all(isinstance(v, tuple) for v in res.values()), res
-    rc0, out0, oe0, y320, _ = res[0]
-    assert rc0 == 0
+    lrc0, prc0, out0, oe0, y320, _ = res[0]
+    assert lrc0 == 0 and prc0 == 0
     for r in range(1, world):
-        assert res[r][:4] == (rc0, out0, oe0, y320), r
-    exps = [res[r][4] for r in range(world)]
-    assert len(set(exps)) >= 1
+        assert res[r][:5] == (lrc0, prc0, out0, oe0, y320), r
     # the reduced value is close to the unsharded product (15.4b: bounded loss)
     import oracle as O
     M, K = 64, 1024
@@ -125,15 +139,55 @@ def test_row_parallel_golden_identical_on_ranks(world):
 
 def test_out_shift_mismatch_refused_everywhere():
     res = _run(2, "oshift")
-    assert [res[r][0] for r in range(2)] == [-2, -2], res     # oracle code for -13
+    assert [res[r][0] for r in range(2)] == [-13, -13], res   # the library's check
+    assert [res[r][1] for r in range(2)] == [-2, -2], res     # the oracle's code for the same refusal
 
 
 def test_spread_over_17_refused_everywhere():
     res = _run(2, "spread")
-    assert [res[r][0] for r in range(2)] == [-1, -1], res     # oracle code for -12
+    assert [res[r][0] for r in range(2)] == [-12, -12], res
+    assert [res[r][1] for r in range(2)] == [-1, -1], res
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_stale_sequence_refused_everywhere(world):
+    """One rank's message carries the previous collective's sequence number
+    (E 2.3: a stale flag read as completion): every rank refuses it (-15)."""
+    res = _run(world, "stale")
+    assert [res[r][0] for r in range(world)] == [-15] * world, res
 
 
 def test_rank_that_leaves_fails_the_collective_not_the_host():
     res = _run(2, "leave")
     assert res[1] == "left"
     assert isinstance(res[0], str) and res[0].startswith("error"), res
+
+
+def test_msg_pack_and_check_on_the_host(pkg):
+    """The message format on one host: payload, trailer, sequence word last;
+    a message of another collective, and each refusal, detected."""
+    L = pkg.lib()
+    M = 37
+    mb = L.mv4i_tp_msg_bytes(M)
+    assert mb == ((8 * M + 15) // 16) * 16 + 16 and L.mv4i_tp_msg_bytes(0) == 0
+    rng = np.random.default_rng(3)
+    msgs = []
+    for c in range(3):
+        y = rng.integers(-(1 << 40), 1 << 40, M)
+        m = np.zeros(mb, np.uint8)
+        assert L.mv4i_tp_msg_pack(y.ctypes.data, M, 20 + c, 7, 5, m.ctypes.data) == 0
+        assert np.array_equal(m[:8 * M].view(np.int64), y)
+        assert list(m[mb - 16:].view(np.int32)[:3].astype(np.int64)) == [20 + c, 7, 5]
+        msgs.append(m)
+
+    def check(seq):
+        ye, osh = np.zeros(3, np.int32), np.zeros(3, np.int32)
+        ptrs = (C.c_void_p * 3)(*[m.ctypes.data for m in msgs])
+        return L.mv4i_tp_msgs_check(3, M, ptrs, seq, ye.ctypes.data, osh.ctypes.data), list(ye), list(osh)
+    assert check(5) == (0, [20, 21, 22], [7, 7, 7])
+    assert check(6)[0] == -15 and check(4)[0] == -15
+    msgs[1][mb - 12:mb - 8] = np.array([8], np.int32).view(np.uint8)       # out_shift of rank 1
+    assert check(5)[0] == -13
+    msgs[1][mb - 12:mb - 8] = np.array([7], np.int32).view(np.uint8)
+    msgs[2][mb - 16:mb - 12] = np.array([20 + 18], np.int32).view(np.uint8)  # y_exp spread 18
+    assert check(5)[0] == -12

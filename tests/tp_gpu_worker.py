@@ -1,12 +1,15 @@
 """Rank process for tests/test_tp_gpu.py (launched by torchrun, one per GPU).
 
 Row-parallel golden block: every rank uploads its own K-slice of the same
-matrix, BFP-packs its own x slice, runs the PARTIAL-mode kernel, the partials
-travel over NCCL (all-gather), and every rank reduces with mv4i_tp_reduce; the
-result must equal the CPU oracle's reduction of the same partials bit for bit
-and be identical on all ranks.  Then a g128 row-parallel block: fp32 partials,
-NCCL all-reduce, against the double-precision product of the whole matrix.
-Exits 0 on success.
+matrix, BFP-packs its own x slice, runs the PARTIAL-mode kernel, and
+mv4i_tp_row_parallel (the library's NCCL communicator) all-gathers the E
+messages (partials + {y_exp, out_shift, sequence}) and reduces them on every
+rank; the result must equal the CPU oracle's reduction of the same partials
+bit for bit and be identical on all ranks.  A second collective whose
+sequence number one rank gets wrong is refused (-15) on every rank.  Then a
+g128 row-parallel block: fp32 partials, mv4i_tp_allreduce_f32, against the
+double-precision product of the whole matrix.  torch.distributed only ships
+the communicator's id and compares the ranks' results.  Exits 0 on success.
 """
 import ctypes as C
 import datetime
@@ -23,10 +26,8 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 def main():
     import torch
     import torch.distributed as dist
-    from conftest import load_package
+    from conftest import load_package, split
     pkg = load_package()
-    import llmvhdl_b200.tp as TP
-    import llmvhdl_b200.synth as S
 
     import oracle as O
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -42,7 +43,7 @@ def main():
     idx = rng.integers(0, 16, (M, K), dtype=np.uint8)
     scl = rng.integers(4000, 32000, (M, K // 32), dtype=np.uint16)
     u = rng.integers(-(1 << 22), 1 << 22, K)
-    k0, kn = TP.split(K, world, rank, align=128)
+    k0, kn = split(K, world, rank, align=128)
     img = O.pack(M, kn, 4, 128, 2, 9, O.IQ4_NL, idx[:, k0:k0 + kn], scl[:, k0 // 32:(k0 + kn) // 32])
     xs = np.zeros(kn, np.int16)
     x_exp = O.orc().orc_bfp_pack_s64(u[k0:k0 + kn].astype(np.int64).ctypes.data_as(C.c_void_p), kn, 16,
@@ -62,17 +63,46 @@ def main():
     y_exp = int(st[0].item())
     rc, r = O.matvec(img, xs, x_exp, M, kn, 2)
     assert rc == 0 and np.array_equal(ya.cpu().numpy(), r["y_acc"]) and y_exp == r["y_exp"]
-    out, y32, status = TP.row_parallel_golden(ya, y_exp, 9, lambda p, e, o: TP.reduce_partials_device(L, p, e, o))
+    # the library's communicator: rank 0's id shipped over torch.distributed
+    uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        h = (C.c_uint8 * 128)()
+        assert L.mv4i_tp_unique_id(h) == 0
+        uid = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=dev)
+    dist.broadcast(uid, 0)
+    comm = C.c_void_p()
+    assert L.mv4i_tp_comm_create((C.c_uint8 * 128)(*uid.cpu().tolist()), rank, world, rank, C.byref(comm)) == 0
+    mb = L.mv4i_tp_msg_bytes(M)
+    work = torch.zeros((world + 1) * mb, dtype=torch.uint8, device=dev)
+    out = torch.zeros(M, dtype=torch.int16, device=dev)
+    y32 = torch.zeros(M, dtype=torch.int32, device=dev)
+    status = torch.zeros(8, dtype=torch.int32, device=dev)
+    assert L.mv4i_tp_row_parallel(comm, C.c_void_p(ya.data_ptr()), M, C.c_void_p(st.data_ptr()), 9, 1,
+                                  C.c_void_p(work.data_ptr()), C.c_void_p(out.data_ptr()),
+                                  C.c_void_p(y32.data_ptr()), C.c_void_p(status.data_ptr()), None) == 0
     torch.cuda.synchronize()
-    parts, ye, osh = TP.gather_partials(ya, y_exp, 9)
-    prc, oout, oexp, oy32, osat = O.tp_reduce(list(parts.cpu().numpy()), list(ye.cpu().numpy()),
-                                            list(osh.cpu().numpy()))
+    recv = work[:world * mb].cpu().numpy().reshape(world, mb)
+    parts = [recv[c, :8 * M].view(np.int64) for c in range(world)]
+    ye = [int(recv[c, mb - 16:mb - 12].view(np.int32)[0]) for c in range(world)]
+    osh = [int(recv[c, mb - 12:mb - 8].view(np.int32)[0]) for c in range(world)]
+    assert ye[rank] == y_exp and osh == [9] * world
+    prc, oout, oexp, oy32, osat = O.tp_reduce(parts, ye, osh)
     assert prc == 0 and int(status[4].item()) == 0
     assert np.array_equal(out.cpu().numpy(), oout) and int(status[0].item()) == oexp
+    assert np.array_equal(y32.cpu().numpy(), oy32)
     out32 = out.to(torch.int32)                     # NCCL has no int16
     allo = [torch.empty_like(out32) for _ in range(world)]
     dist.all_gather(allo, out32)
     assert all(torch.equal(allo[0], a) for a in allo)
+    # the next collective with the last rank one sequence number behind: refused everywhere
+    out.zero_()
+    assert L.mv4i_tp_row_parallel(comm, C.c_void_p(ya.data_ptr()), M, C.c_void_p(st.data_ptr()), 9,
+                                  2 if rank < world - 1 else 1, C.c_void_p(work.data_ptr()),
+                                  C.c_void_p(out.data_ptr()), C.c_void_p(y32.data_ptr()),
+                                  C.c_void_p(status.data_ptr()), None) == 0
+    torch.cuda.synchronize()
+    want = -15
+    assert int(status[4].item()) == want and not out.any().item(), int(status[4].item())
 
     # ---- g128 row-parallel: fp32 partials + all-reduce
     M2, K2 = 2048, 6144
@@ -81,7 +111,7 @@ def main():
     x = torch.empty(K2, dtype=torch.float16, device=dev)
     assert L.mv4i_synth_g128(5, 1, M2, K2, C.c_void_p(wq.data_ptr()), C.c_void_p(sc.data_ptr()),
                              C.c_void_p(x.data_ptr()), None) == 0
-    c0, cn = TP.split(K2, world, rank, align=128)
+    c0, cn = split(K2, world, rank, align=128)
     wsl = wq[:, c0 // 2:(c0 + cn) // 2].contiguous()
     ssl = sc[:, c0 // 128:(c0 + cn) // 128].contiguous()
     xsl = x[c0:c0 + cn].contiguous()
@@ -93,12 +123,13 @@ def main():
     j2.w = C.pointer(dm2); j2.x = xsl.data_ptr(); j2.n_rows = M2; j2.n_cols = cn; j2.nvec = 1
     j2.y_f32 = y.data_ptr()
     assert L.mv4i_launch(C.byref(j2), 1, None, None) == 0
-    TP.row_parallel_fp32(y)
+    assert L.mv4i_tp_allreduce_f32(comm, C.c_void_p(y.data_ptr()), M2, None) == 0
     torch.cuda.synchronize()
     ref = O.matvec_g128_f64(wq.cpu().numpy(), sc.cpu().numpy(), x.cpu().numpy(), K2)
     err = np.abs(y.cpu().numpy() - ref).max() / np.abs(ref).max()
     assert err <= 1e-4, err
     L.mv4i_dmat_free(C.byref(dm))
+    assert L.mv4i_tp_comm_destroy(comm) == 0
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
