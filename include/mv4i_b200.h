@@ -258,6 +258,38 @@ int mv4i_tp_reduce(int N, int n_rows, const int64_t *d_parts, const int32_t *d_y
                    const int32_t *d_out_shifts, int16_t *d_out_mant, int32_t *d_y32,
                    mv4i_status *d_status, void *stream);
 
+/* --------------------------------------------------------- weight packing */
+
+/* The offline weight path of tools/pack_int4.py, as library calls (host
+ * memory, no device needed):
+ *   mv4i_quantize            quantize() (:280-359, spec 6.1): float W [M][K]
+ *                            -> idx [M][NB][32] codebook indices, scale
+ *                            [M][NB] uint15 (Q15), w_exp; the per-block scale
+ *                            is the least-squares best of 8 candidates around
+ *                            the amax-anchored one.  The codebook must be
+ *                            ascending (IQ4_NL is); -11 otherwise.  Same bytes
+ *                            as the reference's quantiser.
+ *   mv4i_calibrate_out_shift calibrate_out_shift() (:434-446, spec 7.4): the
+ *                            out_shift for which sat32 cannot fire
+ *   mv4i_pack_size           the image size (packed_layout(), :451-486), 0
+ *                            for a geometry the reference refuses
+ *   mv4i_pack                pack() (:488-559, spec 6.4 / 6.5a): the .mv4i
+ *                            image, byte-identical to the reference's
+ *   mv4i_image_to_g128       an image the g128 format holds exactly (linear
+ *                            codebook {0..7,-8..-1}, K % 128 == 0, equal
+ *                            scales in each 128-column group, scales exact
+ *                            in fp16) -> INT4 nibbles [M][K/2] and fp16
+ *                            scales [M][sc_pitch]; -11 when not exact.  No
+ *                            counterpart in the reference (the decode
+ *                            engine's layout, see dec_load_linear). */
+int    mv4i_quantize(const float *W, int M, int K, const int8_t cb[16], uint8_t *idx, uint16_t *scale,
+                     int *w_exp);
+int    mv4i_calibrate_out_shift(int K);
+size_t mv4i_pack_size(int M, int K, int rows_if, int axi_dw);
+int    mv4i_pack(const uint8_t *idx, const uint16_t *scale, int w_exp, int M, int K, int rows_if, int out_shift,
+                 const int8_t cb[16], int axi_dw, uint8_t *out);
+int    mv4i_image_to_g128(const mv4i_file *f, uint8_t *wq, uint16_t *sc, int sc_pitch);
+
 /* ------------------------------------------- tensor-parallel collective */
 
 /* The transport of E (tp-collective-design.md:153-180): the message one rank

@@ -21,7 +21,7 @@ LIBDIR = os.path.join(HERE, "lib")
 LIBPATH = os.path.join(LIBDIR, "libmv4i_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c"]   # gdn_kernels.cu includes gdn_block.cuh
+SOURCES = ["csrc/mv4i_kernels.cu", "csrc/gdn_kernels.cu", "csrc/mv4i_host.c", "csrc/mv4i_pack.c"]   # gdn_kernels.cu includes gdn_block.cuh
 DEC_LIBPATH = os.path.join(LIBDIR, "libdec_b200.so")
 DEC_SOURCES = ["csrc/dec_step.cu", "csrc/dec_model.c"]   # dec_step.cu includes dec_kernels.cu, dec_matvec.cu
 
@@ -164,6 +164,13 @@ EXPORTS = {
                                  C.c_void_p, C.c_void_p]),
     "gdn_emit_chain_dev": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                      C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mv4i_quantize": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                C.POINTER(C.c_int)]),
+    "mv4i_calibrate_out_shift": (C.c_int, [C.c_int]),
+    "mv4i_pack_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "mv4i_pack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                            C.c_int, C.c_void_p]),
+    "mv4i_image_to_g128": (C.c_int, [C.POINTER(File), C.c_void_p, C.c_void_p, C.c_int]),
     "mv4i_tp_msg_bytes": (C.c_size_t, [C.c_int]),
     "mv4i_tp_msg_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_void_p]),
     "mv4i_tp_msgs_check": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p]),
