@@ -117,6 +117,17 @@ int dec_pointers(dec_model *m, float **logits, int32_t **history, float **residu
 int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, const uint16_t **d_sc,
                int32_t *rows, int32_t *cols, int32_t *s_pitch);
 
+/* Real weights into a model: copies a g128 tensor from host memory -- INT4
+ * two's-complement nibbles [rows][cols/2] (column k even in the low nibble)
+ * and fp16 scales [rows][sc_pitch], one per 128 columns -- over the linear
+ * `name` of `layer` (names as dec_linear).  rows x cols must be the shard
+ * this rank holds (dec_linear reports it).  An .mv4i image converts to this
+ * form with mv4i_image_to_g128 when its values allow it, a float matrix with
+ * mv4i_quantize_g128.  No counterpart in the reference, whose weights come
+ * to the card as packed images. */
+int dec_load_linear(dec_model *m, int layer, const char *name, const uint8_t *h_wq, const uint16_t *h_sc,
+                    int rows, int cols, int sc_pitch);
+
 /* Parameter and state vectors: "attn_norm", "post_norm", "conv_w"
  * ([conv_dim][4]), "ssm_a", "dt_bias", "ssm_norm", "q_norm", "k_norm",
  * "conv_state", "rec_state", "kcache", "vcache" (per layer; the states and

@@ -290,6 +290,13 @@ int    mv4i_pack(const uint8_t *idx, const uint16_t *scale, int w_exp, int M, in
                  const int8_t cb[16], int axi_dw, uint8_t *out);
 int    mv4i_image_to_g128(const mv4i_file *f, uint8_t *wq, uint16_t *sc, int sc_pitch);
 
+/* A float matrix W [M][K] (K % 128 == 0) straight to the g128 layout: per row
+ * and 128-column group, scale = fp16(max|w| / 7) (round to nearest even),
+ * q = clamp(rint(w / scale), -8, 7) as two's-complement nibbles (column k even
+ * in the low nibble).  -11 when a scale overflows fp16.  No counterpart in the
+ * reference (the benchmark's format, not the .mv4i one). */
+int    mv4i_quantize_g128(const float *W, int M, int K, uint8_t *wq, uint16_t *sc, int sc_pitch);
+
 /* ------------------------------------------- tensor-parallel collective */
 
 /* The transport of E (tp-collective-design.md:153-180): the message one rank

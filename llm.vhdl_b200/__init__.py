@@ -171,6 +171,7 @@ EXPORTS = {
     "mv4i_pack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                             C.c_int, C.c_void_p]),
     "mv4i_image_to_g128": (C.c_int, [C.POINTER(File), C.c_void_p, C.c_void_p, C.c_int]),
+    "mv4i_quantize_g128": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
     "mv4i_tp_msg_bytes": (C.c_size_t, [C.c_int]),
     "mv4i_tp_msg_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_void_p]),
     "mv4i_tp_msgs_check": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p]),
@@ -227,6 +228,8 @@ class GatedAttnArgs(C.Structure):
 DEC_EXPORTS = {
     "gated_attn_work_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "gated_attn": (C.c_int, [C.POINTER(GatedAttnArgs), C.c_void_p]),
+    "dec_load_linear": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                  C.c_int]),
     "dec_create": (C.c_int, [C.POINTER(DecConfig), C.c_uint64, C.c_int, C.c_int, C.c_int,
                              C.POINTER(C.c_void_p)]),
     "dec_destroy": (C.c_int, [C.c_void_p]),

@@ -889,6 +889,23 @@ int dec_linear(dec_model *m, int layer, const char *name, const uint8_t **d_wq, 
     return 0;
 }
 
+int dec_load_linear(dec_model *m, int layer, const char *name, const uint8_t *h_wq, const uint16_t *h_sc,
+                    int rows, int cols, int sc_pitch)
+{
+    const uint8_t *d_wq;
+    const uint16_t *d_sc;
+    int32_t r, k, sp;
+    if (!h_wq || !h_sc || sc_pitch < cols / 128) return -11;
+    CK(dec_linear(m, layer, name, &d_wq, &d_sc, &r, &k, &sp));
+    if (rows != r || cols != k) return -11;          /* the shard this rank holds */
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e == cudaSuccess) e = cudaMemcpy((void *)d_wq, h_wq, (size_t)r * k / 2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2D((void *)d_sc, (size_t)sp * 2, h_sc, (size_t)sc_pitch * 2, (size_t)(k / 128) * 2, (size_t)r,
+                         cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? 0 : fail(e);
+}
+
 int dec_param(dec_model *m, int layer, const char *name, const void **d_ptr, int32_t *count)
 {
     if (!m || !name) return -11;

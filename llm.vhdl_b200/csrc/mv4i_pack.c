@@ -246,3 +246,48 @@ int mv4i_image_to_g128(const mv4i_file *f, uint8_t *wq, uint16_t *sc, int sc_pit
     }
     return 0;
 }
+
+/* fp16 bits of a finite non-negative float, round to nearest even; 0xFFFF when
+ * it overflows fp16 */
+static uint16_t f32_to_f16_pos(float f)
+{
+    if (!(f >= 0.f)) return 0xFFFF;
+    if (f == 0.f) return 0;
+    int e;
+    const double m = frexp((double)f, &e);           /* f = m * 2^e, m in [0.5, 1) */
+    if (e > 16) return 0xFFFF;
+    if (e >= -13) {                                  /* normal: 11 significant bits */
+        double q = rint(ldexp(m, 11));
+        if (q == 2048.0) { q = 1024.0; e++; }
+        if (e > 16) return 0xFFFF;
+        const uint16_t h = (uint16_t)(((e - 1 + 15) << 10) | ((uint32_t)q & 0x3FF));
+        return h >= 0x7C00 ? 0xFFFF : h;
+    }
+    return (uint16_t)rint(ldexp((double)f, 24));     /* subnormal: units of 2^-24 */
+}
+
+int mv4i_quantize_g128(const float *W, int M, int K, uint8_t *wq, uint16_t *sc, int sc_pitch)
+{
+    if (!W || !wq || !sc || M <= 0 || K <= 0 || K % 128 || sc_pitch < K / 128) return -11;
+    for (int r = 0; r < M; r++)
+        for (int g = 0; g < K / 128; g++) {
+            const float *w = W + (size_t)r * K + 128 * g;
+            float amax = 0.f;
+            for (int j = 0; j < 128; j++) amax = fmaxf(amax, fabsf(w[j]));
+            const uint16_t h = f32_to_f16_pos(amax / 7.0f);
+            if (h == 0xFFFF) return -11;
+            sc[(size_t)r * sc_pitch + g] = h;
+            /* the scale as fp16 stores it */
+            const float s = (h >> 10) ? ldexpf((float)(1024 | (h & 0x3FF)), (h >> 10) - 25)
+                                      : ldexpf((float)h, -24);
+            for (int j = 0; j < 128; j += 2) {
+                int q[2];
+                for (int t = 0; t < 2; t++) {
+                    const float v = s > 0.f ? rintf(w[j + t] / s) : 0.f;
+                    q[t] = v < -8.f ? -8 : (v > 7.f ? 7 : (int)v);
+                }
+                wq[(size_t)r * (K / 2) + 64 * g + j / 2] = (uint8_t)((q[0] & 15) | ((q[1] & 15) << 4));
+            }
+        }
+    return 0;
+}

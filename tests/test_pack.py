@@ -115,3 +115,26 @@ def test_image_to_g128_exact_or_refused(pkg):
     assert L.mv4i_image_to_g128(C.byref(pi2.f), wq.ctypes.data, sc.ctypes.data, 8) == -11
     pi3 = pkg.ParsedImage(O.pack(M, K, 4, 128, 5, 3, O.IQ4_NL, idx, scl))  # not the linear codebook
     assert L.mv4i_image_to_g128(C.byref(pi3.f), wq.ctypes.data, sc.ctypes.data, 8) == -11
+
+
+def test_quantize_g128_matches_numpy(pkg):
+    """The float -> g128 quantiser: scale = fp16(max|w| / 7) per 128 columns,
+    q = clamp(rint(w / scale), -8, 7), restated in numpy."""
+    L = pkg.lib()
+    rng = np.random.default_rng(9)
+    M, K = 12, 640
+    W = (rng.standard_normal((M, K)) * rng.uniform(1e-4, 3.0, (M, 1))).astype(np.float32)
+    W[3, 128:256] = 0.0                                        # an all-zero group
+    wq = np.zeros((M, K // 2), np.uint8)
+    sc = np.zeros((M, 8), np.uint16)
+    assert L.mv4i_quantize_g128(W.ctypes.data, M, K, wq.ctypes.data, sc.ctypes.data, 8) == 0
+    g = W.reshape(M, K // 128, 128)
+    s16 = (np.abs(g).max(axis=2) / np.float32(7.0)).astype(np.float16)
+    s32 = s16.astype(np.float32)[:, :, None]
+    q = np.where(s32 > 0, np.clip(np.rint(g / np.where(s32 > 0, s32, 1)), -8, 7), 0).astype(np.int64)
+    q = q.reshape(M, K)
+    want = ((q[:, 0::2] & 15) | ((q[:, 1::2] & 15) << 4)).astype(np.uint8)
+    assert np.array_equal(sc[:, :K // 128], s16.view(np.uint16))
+    assert np.array_equal(wq, want)
+    big = np.full((1, 128), 1e6, np.float32)
+    assert L.mv4i_quantize_g128(big.ctypes.data, 1, 128, wq.ctypes.data, sc.ctypes.data, 8) == -11
