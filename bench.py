@@ -140,10 +140,39 @@ def cpu_baseline(budget_s=3.0):
     from oracle import cpu_baseline as CB
     steps, kind, P = CB.run(budget_s=budget_s)
     t = steps[0]
+    one, _, _ = CB.run(P=1, budget_s=2.0)
     return {"value": round(CB.GOLDEN_BYTES / t / 1e9, 4), "unit": "GB/s", "cores": P,
             "kind": kind, "ms_per_matvec": round(t * 1e3, 3),
             "sample": "config-0 golden-mode mv4i_matvec (BFP out), %d processes x row shards, "
-                      "~%.0f s each" % (P, budget_s)}
+                      "~%.0f s each" % (P, budget_s),
+            "single_thread": {"ms_per_matvec": round(one[0] * 1e3, 3),
+                              "GBps": round(CB.GOLDEN_BYTES / one[0] / 1e9, 4), "cores": 1, "kind": kind,
+                              "sample": "the whole 4096 x 4096 matvec in one process, ~2 s"}}
+
+
+def block_cpu_baseline(budget_s=2.0):
+    """The reference's own fixed-point gdn_block_token (ref/gdn_block_vec.c:208,
+    compiled from source into oracle/_ref/libref_gdn.so) on the bench's block
+    stimulus, one thread; the restatement when the reference was not built."""
+    import numpy as np
+    import oracle as O
+    b = block_inputs(1)
+    use_ref = O.have_gdn_ref()
+    T = 0
+    smem, semem = b["smem"].copy(), b["semem"].copy()
+    e_t = np.array([[8 + (s + k) % 5 for k in range(4)] for s in range(3)], np.int32)
+    stim = dict(wtap=b["wtap"], cw_exp=np.array([11, 12, 13], np.int32), wm=b["wm"], w_e=12, z_e=12)
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or T == 0:
+        n = 4
+        stim.update(xtap=np.repeat(b["xtap"][None], n, 0), e_t=np.repeat(e_t[None], n, 0),
+                    tvalid=np.ones((n, 3, 4), np.int32), sc=np.repeat(b["sc"][None], n, 0),
+                    zm=np.repeat(b["zm"][None], n, 0), tk0=np.zeros(n, np.int32))
+        O.gdn_block_run(BLK_KH, BLK_VH, BLK_D, stim, smem, semem, use_ref=use_ref)
+        T += n
+    us = (time.perf_counter() - t0) / T * 1e6
+    return {"us_per_token": round(us, 1), "cores": 1, "kind": "reference" if use_ref else "port",
+            "sample": "%d block tokens at 16/32 heads x 128, one thread" % T}
 
 
 # --------------------------------------------------------------------- ours
@@ -389,6 +418,7 @@ def run_gdn(args, pkg, L, torch, dev, stream, sp, timed):
     ms_steps = timed(graph.replay, nrep) / nrep
     del graph
     us_step = ms_steps * 1e3 / GDN_T
+    blk = run_block(pkg, L, torch, dev, stream, sp, timed, nrep)
     return {
         "workload": "config 1: 16 heads x 128 x 128 fp32 state, 256 sequential steps, seed 1",
         "persistent_us_per_step": round(ms_all * 1e3 / GDN_T, 3),
@@ -398,7 +428,86 @@ def run_gdn(args, pkg, L, torch, dev, stream, sp, timed):
         "per_step_bytes": GDN_STEP_BYTES,
         "per_step_how": "one launch per step, state through HBM, 256 launches in a CUDA graph",
         "kernel": "gdn_f32_kernel",
+        "fixed_block": blk,
     }
+
+
+BLK_KH, BLK_VH, BLK_D = 16, 32, 128
+
+
+def block_inputs(seed=1):
+    """Fixed-point DeltaNet block stimulus at the model shape (16 key heads, 32
+    value heads, D 128), in the ranges of the reference's generator
+    (ref/gdn_block_vec.c:570-618): conv taps/weights +-2047, norm weights
+    2000..6000, the scalar path in its physical band, z +-8192, state mantissas
+    up to full scale with column exponents 9..12."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    KH, VH, D = BLK_KH, BLK_VH, BLK_D
+    CH = 2 * KH * D + VH * D
+    sc = np.zeros((VH, 8), np.int32)
+    sc[:, 0] = rng.integers(-1000, 1001, VH); sc[:, 1] = 14
+    sc[:, 2] = -rng.integers(2000, 32001, VH); sc[:, 3] = 12
+    sc[:, 4] = -rng.integers(1, 3001, VH); sc[:, 5] = 16
+    sc[:, 6] = rng.integers(-30000, 30001, VH); sc[:, 7] = 12
+    return dict(xtap=rng.integers(-2047, 2048, (CH, 4)).astype(np.int16),
+                wtap=rng.integers(-2047, 2048, (CH, 4)).astype(np.int16), sc=sc,
+                zm=rng.integers(-8192, 8193, (VH, D)).astype(np.int16),
+                wm=rng.integers(2000, 6001, D).astype(np.int16),
+                smem=rng.integers(-30000, 30001, (VH, D, D)).astype(np.int16),
+                semem=(9 + (np.arange(VH)[:, None] + np.arange(D)[None]) % 4).astype(np.int32))
+
+
+BLK_BYTES = 2 * BLK_VH * BLK_D * BLK_D * 2 + 2 * BLK_VH * BLK_D * 4 + (2 * BLK_KH + BLK_VH) * BLK_D * 4 * 2 * 2
+
+
+def run_block(pkg, L, torch, dev, stream, sp, timed, nrep):
+    """The fixed-point block (deltanet_step) per token at the model shape:
+    64 tokens per CUDA graph, each a programmatic dependent of the one before,
+    the state resident in HBM (read and written every token)."""
+    b = block_inputs(1)
+    t = {n: torch.from_numpy(x.copy()).to(dev) for n, x in b.items()}
+    y = torch.empty(BLK_VH * BLK_D, dtype=torch.int16, device=dev)
+    status = torch.zeros(8, dtype=torch.int32, device=dev)
+    nb = L.deltanet_work_bytes(BLK_KH, BLK_VH, BLK_D)
+    work = torch.empty(nb + 256, dtype=torch.uint8, device=dev)
+    a = pkg.DeltanetArgs()
+    a.KH, a.VH, a.D = BLK_KH, BLK_VH, BLK_D
+    a.xtap, a.wtap, a.sc, a.zm, a.wm = (t[k].data_ptr() for k in ("xtap", "wtap", "sc", "zm", "wm"))
+    for s in range(3):
+        a.cw_exp[s] = 11 + s
+        for k in range(4):
+            a.e_t[s][k] = 8 + (s + k) % 5
+            a.tvalid[s][k] = 1
+    a.w_e, a.z_e, a.tk0 = 12, 12, 0
+    a.smem, a.semem, a.y, a.status = t["smem"].data_ptr(), t["semem"].data_ptr(), y.data_ptr(), status.data_ptr()
+    a.work = (work.data_ptr() + 255) & ~255
+    a.pdl = 1
+    T = 64
+
+    def tokens():
+        for _ in range(T):
+            if L.deltanet_step(C.byref(a), sp):
+                raise RuntimeError("deltanet_step failed")
+    tokens()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        tokens()
+    for _ in range(3):
+        g.replay()
+    ms = timed(g.replay, nrep) / nrep
+    del g
+    us = ms * 1e3 / T
+    peak, _ = peaks()
+    return {"workload": "fixed-point DeltaNet block token (bit-exact with gdn_block_token): 16 key / 32 value "
+                        "heads, D 128, int16 state 1 MiB read + written per token",
+            "us_per_token": round(us, 3), "bytes_per_token": BLK_BYTES,
+            "GBps": round(BLK_BYTES / (us * 1e-6) / 1e9, 1),
+            "frac_hbm": round(BLK_BYTES / (us * 1e-6) / 1e9 / peak, 4),
+            "how": "3 launches per token (front, per-head recurrence + emit, site-13 tail), 64 tokens per "
+                   "CUDA graph", "kernels": ["gdn_blk_front_kernel", "gdn_blk_rec_kernel<128>",
+                                            "gdn_blk_tail_kernel"]}
 
 
 # ------------------------------------------------------------ decode (configs 3, 4)
@@ -880,10 +989,13 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()          # spawn-started workers, before any CUDA work
         gcpu = gdn_cpu_baseline()
+        bcpu = block_cpu_baseline()
     out = run_ours(args, rank, world, local_rank)
     out["cpu_baseline"] = cpu
     if gcpu:
         out["gdn"]["cpu_baseline"] = gcpu
+        if isinstance(out["gdn"].get("fixed_block"), dict):
+            out["gdn"]["fixed_block"]["cpu_baseline"] = bcpu
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

@@ -192,3 +192,25 @@ def test_f32_single_steps_equal_one_run(cuda, pkg):
         o, _ = _run_f32(torch, pkg, S2, q[t:t + 1], k[t:t + 1], v[t:t + 1], g[t:t + 1], a[t:t + 1], b[t:t + 1])
         assert np.array_equal(o[0], run[t]), t
     assert torch.equal(S1, S2)
+
+
+def test_f32_config1_bench_inputs_elementwise(cuda, pkg):
+    """The benchmark's own config-1 inputs (bench.gdn_inputs: the splitmix64
+    stream of seed 1 that bench.py times) through all 256 steps, compared
+    element by element with the double oracle: |out - ref| <= 1e-3 * |ref| +
+    1e-4 * max|ref| per step (north_star's 1e-3 relative error; the absolute
+    floor covers outputs that cancel to near zero), fp16 output likewise."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    torch = cuda
+    S0, q, k, v, g, a, b = bench.gdn_inputs(1)
+    T, H = q.shape[0], q.shape[1]
+    S = torch.from_numpy(S0.copy()).cuda()
+    out, out16 = _run_f32(torch, pkg, S, q, k, v, g, a, b)
+    ref = O.gdn_cfg1_f64(S0.astype(np.float64), q.astype(np.float64), k.astype(np.float64), v.astype(np.float64),
+                         a.astype(np.float64), b.astype(np.float64), g.astype(np.float64))
+    for t in range(T):
+        bound = 1e-3 * np.abs(ref[t]) + 1e-4 * np.abs(ref[t]).max()
+        assert np.all(np.abs(out[t] - ref[t]) <= bound), t
+        assert np.all(np.abs(out16[t].astype(np.float64) - ref[t]) <= bound), t
