@@ -4,21 +4,19 @@
 // whose integer helpers (g_floor_shr, g_round_shift, g_msb, ...), scalar path
 // (d_to_q_wide, ...) and LUT upload it shares.
 //
-// Three launches per token, each a programmatic dependent of the one before:
+// Two launches per token, each a programmatic dependent of the one before:
 //
-//   gdn_blk_front_kernel   grid 4 x 1024 threads.  CTA s < 3 is conv segment s
-//                          (q, k, v: spec B 2.1.3): the 4-tap conv with masked
-//                          taps and the segment requantiser (a CTA-wide maximum),
-//                          silu with the exponent preserved, and for q / k the
-//                          per-key-head L2 norm (a warp per head, the Newton
-//                          rsqrt on the shared Q30 seed table).  CTA 3 runs the
-//                          scalar path (eg, beta) for every value head.
-//   gdn_blk_rec_kernel<D>  one CTA per value head, D*D/16 threads: the
-//                          recurrence (stages 1-5, state column j owned by D/16
-//                          lanes of 16 keys each; the state slice is loaded
-//                          before the wait on the front kernel), then warp 0
-//                          runs the head tail: site-12 head emit, the output
-//                          rmsnorm_bf, the z gate.
+//   gdn_blk_head_kernel<D> one CTA per value head, D*D/16 threads: the three
+//                          conv segments' requantiser maxima (every CTA reduces
+//                          whole segments from L2), then one warp each for the
+//                          head's q / k (silu, L2 norm with the Newton rsqrt on
+//                          the Q30 seed table), v (silu) and scalar path (eg,
+//                          beta); the recurrence (stages 1-5, state column j
+//                          owned by D/16 lanes of 16 keys each; the state slice
+//                          is loaded before the wait on the launch before); then
+//                          warp 0 runs the head tail: site-12 head emit, the
+//                          output rmsnorm_bf, the z gate.  Tables live in shared
+//                          memory, copied before the wait.
 //   gdn_blk_tail_kernel    one CTA: site 13, the gated product over all heads
 //                          aligned to the minimum head exponent and renormalised
 //                          to one token exponent; writes the status word.
@@ -72,7 +70,7 @@ __device__ __forceinline__ int32_t fx_to_q12(int64_t x, int e)
 }
 
 // sigma, Q12 in / Q15 out, interpolated on the Q30 table (ref/gdn_silu_vec.c:59-80)
-__device__ __forceinline__ int32_t fx_sigma_q15(int32_t z)
+__device__ __forceinline__ int32_t fx_sigma_q15(int32_t z, const int64_t *tab)
 {
     const int64_t lim = (int64_t)16 << 12;
     if ((int64_t)z <= -lim) return 0;
@@ -81,15 +79,16 @@ __device__ __forceinline__ int32_t fx_sigma_q15(int32_t z)
     int64_t k = pos >> 12;
     if (k > 511) k = 511;
     const int64_t frac = pos - (k << 12);
-    const int64_t lo = __ldg(d_sig_tab + k), hi = __ldg(d_sig_tab + k + 1);
+    const int64_t lo = tab[k], hi = tab[k + 1];
     const int64_t r = g_round_shift(lo + (((hi - lo) * frac) >> 12), 15);
     return (int32_t)(r < 0 ? 0 : (r > 32768 ? 32768 : r));
 }
 
-// silu with the exponent preserved (ref/gdn_block_vec.c:250-253)
-__device__ __forceinline__ int32_t fx_silu(int32_t sm, int e)
+// silu with the exponent preserved (ref/gdn_block_vec.c:250-253); tab is the
+// Q30 sigmoid table (d_sig_tab or a shared-memory copy of it)
+__device__ __forceinline__ int32_t fx_silu(int32_t sm, int e, const int64_t *tab)
 {
-    return (int32_t)g_round_shift((int64_t)sm * fx_sigma_q15(fx_to_q12(sm, e)), 15);
+    return (int32_t)g_round_shift((int64_t)sm * fx_sigma_q15(fx_to_q12(sm, e), tab), 15);
 }
 
 // numeric_std forms used by rmsnorm_bf (ref/rmsnorm_bf_vec.c:108-157)
@@ -106,13 +105,14 @@ __device__ __forceinline__ int fx_msb63(int64_t v)
     return u ? 63 - __clzll((long long)u) : 0;
 }
 
-// one L2-norm rsqrt pass (ref/l2norm_rs_vec.c:93-115): Q30 mantissa, exponent he
-__device__ __forceinline__ int64_t fx_l2_rsqrt(int64_t arg, int &he)
+// one L2-norm rsqrt pass (ref/l2norm_rs_vec.c:93-115): Q30 mantissa, exponent he;
+// rom is the seed table (d_rsqrt_rom or a shared-memory copy of it)
+__device__ __forceinline__ int64_t fx_l2_rsqrt(int64_t arg, int &he, const int64_t *rom)
 {
     const int m = fx_msb63(arg);
     const uint64_t mant = m <= 30 ? (uint64_t)arg << (30 - m) : (uint64_t)arg >> (m - 30);
     const int64_t sm = (int64_t)(uint32_t)mant;
-    int64_t y = d_rsqrt_rom[(mant >> 24) & 63];
+    int64_t y = rom[(mant >> 24) & 63];
 #pragma unroll
     for (int it = 0; it < 2; it++) {
         const int64_t y2 = (int64_t)(int32_t)((y * y) >> 30);
@@ -126,7 +126,7 @@ __device__ __forceinline__ int64_t fx_l2_rsqrt(int64_t arg, int &he)
 
 // the rmsnorm_bf reciprocal (ref/rmsnorm_bf_vec.c:230-331) of a sum of squares
 // S of N = 2^lg mantissas on exponent xe: the clamped u31 inv32, Q = 12
-__device__ int64_t fx_rms_inv(int64_t S, int xe, int lg)
+__device__ int64_t fx_rms_inv(int64_t S, int xe, int lg, const int64_t *rom)
 {
     const int shs = 30 - fx_msb63(S);
     const int e_mean = lg + 2 * xe + shs;
@@ -141,7 +141,7 @@ __device__ int64_t fx_rms_inv(int64_t S, int xe, int lg)
     const int p = fx_msb63(msq);
     const uint64_t mant = p <= 30 ? (uint64_t)msq << (30 - p) : (uint64_t)msq >> (p - 30);
     const int64_t sm = (int64_t)(uint32_t)mant;
-    int64_t y = d_rsqrt_rom[(mant >> 24) & 63];
+    int64_t y = rom[(mant >> 24) & 63];
 #pragma unroll
     for (int it = 0; it < 2; it++) {
         const int64_t y2 = fx_narrow(g_floor_shr(y * y, 30), 32);
@@ -196,7 +196,7 @@ __device__ uint64_t cta_max_u64(uint64_t v, uint64_t *red)
 // the k output (exponent 15) or the q output (exponent 18), zeros when the
 // sum of squares is 0 (ref/l2norm_rs_vec.c:118-140)
 template <int R>
-__device__ void fx_l2norm_warp(const int32_t (&x)[R], int log2n, bool q_path, int16_t *out)
+__device__ void fx_l2norm_warp(const int32_t (&x)[R], int log2n, bool q_path, int16_t *out, const int64_t *rom)
 {
     int64_t ssq = 0;
 #pragma unroll
@@ -209,7 +209,7 @@ __device__ void fx_l2norm_warp(const int32_t (&x)[R], int log2n, bool q_path, in
         return;
     }
     int he;
-    const int64_t y = fx_l2_rsqrt(q_path ? ssq << log2n : ssq, he);
+    const int64_t y = fx_l2_rsqrt(q_path ? ssq << log2n : ssq, he, rom);
     const int sh = (q_path ? 12 : 15) + he;
 #pragma unroll
     for (int r = 0; r < R; r++)
@@ -220,14 +220,14 @@ __device__ void fx_l2norm_warp(const int32_t (&x)[R], int log2n, bool q_path, in
 // weights wm on we (ref/rmsnorm_bf_vec.c:199-389); returns the output exponent
 template <int R>
 __device__ int fx_rmsnorm_warp(const int32_t (&xm)[R], int xe, const int16_t *wm, int we, int lg,
-                               int32_t (&o)[R], int &nsat)
+                               int32_t (&o)[R], int &nsat, const int64_t *rom)
 {
     const int lane = threadIdx.x & 31;
     int64_t S = 0;
 #pragma unroll
     for (int r = 0; r < R; r++) S += (int64_t)xm[r] * xm[r];
     S = warp_sum_i64(S);
-    const int64_t inv = fx_rms_inv(S, xe, lg);
+    const int64_t inv = fx_rms_inv(S, xe, lg, rom);
     int64_t raw[R];
     uint64_t mx = 0;
 #pragma unroll
@@ -252,46 +252,32 @@ __device__ int fx_rmsnorm_warp(const int32_t (&xm)[R], int xe, const int16_t *wm
 
 // ------------------------------------------------------------- block kernels
 
-struct BlkWork {                       // device scratch between the three launches
-    int16_t *kn, *qs;                  // [KH][D] Q15 / Q18 (1/sqrt(D) folded)
-    int32_t *v;                        // [VH][D] silu(v) mantissas on e_v
-    int32_t *eg, *beta;                // [VH]
+struct BlkWork {                       // device scratch between the two launches of a token
     int16_t *po, *pz;                  // [VH][D] normed output / gated z
     int32_t *ep;                       // [VH] product exponents
-    int32_t *err_se;                   // [VH]
-    int32_t *misc;                     // [0] e_v, [1..3] err_conv per segment, [4] err_g
+    int32_t *err;                      // [VH] bit 0 conv segment exponent, bit 1 g, bit 2 state exponent
 };
 
 static size_t blk_al(size_t n) { return (n + 255) & ~(size_t)255; }
 
-static BlkWork blk_work_layout(void *base, int KH, int VH, int D, size_t *bytes)
+static BlkWork blk_work_layout(void *base, int VH, int D, size_t *bytes)
 {
     BlkWork w;
     char *p = (char *)base;
     size_t off = 0;
 #define BLK_TAKE(field, T, n) w.field = (T *)(p + off); off += blk_al((size_t)(n) * sizeof(T));
-    BLK_TAKE(kn, int16_t, KH * D)
-    BLK_TAKE(qs, int16_t, KH * D)
-    BLK_TAKE(v, int32_t, VH * D)
-    BLK_TAKE(eg, int32_t, VH)
-    BLK_TAKE(beta, int32_t, VH)
     BLK_TAKE(po, int16_t, VH * D)
     BLK_TAKE(pz, int16_t, VH * D)
     BLK_TAKE(ep, int32_t, VH)
-    BLK_TAKE(err_se, int32_t, VH)
-    BLK_TAKE(misc, int32_t, 8)
+    BLK_TAKE(err, int32_t, VH)
 #undef BLK_TAKE
     if (bytes) *bytes = off;
     return w;
 }
 
-struct BlkFrontArgs {
-    const int16_t *xtap, *wtap;        // [2*KH*D + VH*D][4]
-    int32_t KH, VH, D, lg;
-    int32_t e_t[3][4], tvalid[3][4], cw_exp[3];
-    const int32_t *sc;                 // [VH][8]
-    BlkWork w;
-};
+// floor(v / 2^sh) for a 32-bit v, sh <= 63 (g_floor_shr on int32 values)
+__device__ __forceinline__ int32_t blk_floor_shr32(int32_t v, int sh)
+{ return sh <= 0 ? v : (sh >= 31 ? (v < 0 ? -1 : 0) : (v >> sh)); }
 
 // conv of one channel over its valid taps, aligned to the smallest valid tap
 // exponent by floor (ref/gdn_block_vec.c:231-239)
@@ -303,7 +289,7 @@ __device__ __forceinline__ int64_t blk_conv_ch(const int16_t *x, const int16_t *
     int64_t a = 0;
 #pragma unroll
     for (int t = 0; t < 4; t++)
-        if (vmask >> t & 1) a += g_floor_shr((int64_t)(xs[t] * ws[t]), tsh[t]);
+        if (vmask >> t & 1) a += blk_floor_shr32(xs[t] * ws[t], tsh[t]);
     return a;
 }
 
@@ -320,119 +306,54 @@ __device__ __forceinline__ int blk_taps(const int32_t (&e_t)[4], const int32_t (
     return e_ref;
 }
 
-template <int R>
-__device__ void blk_front_segment(const BlkFrontArgs &A, int s, uint64_t *red)
+// the scalar path of one value head (ref/gdn_block_vec.c:282-290 calling
+// gdn_scalar_int, ref/gdn_scalar_vec.c:100-156; the same arithmetic as
+// gdn_scalar_kernel): eg (Q15 decay) and beta (Q16) from the head's eight
+// inputs; returns 1 when g was clamped at -16
+__device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta)
 {
-    const int D = R * 32, QCH = A.KH * D;
-    const int base = s == 0 ? 0 : (s == 1 ? QCH : 2 * QCH), nch = s == 2 ? A.VH * D : QCH;
-    int tsh[4], vmask;
-    const int e_ref = blk_taps(A.e_t[s], A.tvalid[s], tsh, vmask);
-    const int16_t *xs = A.xtap + (size_t)base * 4, *ws = A.wtap + (size_t)base * 4;
-    uint64_t am = 0;
-    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
-        const int64_t a = blk_conv_ch(xs + 4 * c, ws + 4 * c, vmask, tsh);
-        const uint64_t m = g_abs64(a);
-        am = m > am ? m : am;
+    const int64_t arg = d_to_q_wide(p[0], p[1]) + d_to_q_wide(p[2], p[3]);
+    const int64_t one = (int64_t)1 << SPQ, lim = 16 * one;
+    int64_t sp;
+    if (arg <= -lim) sp = 0;
+    else if (arg >= lim) sp = arg;
+    else {
+        const int64_t ax = arg < 0 ? -arg : arg, pos = arg > 0 ? arg : 0;
+        sp = pos + (ax >= lim ? 0 : d_lut_interp(c_sp_lut, 256, lim - ax, SPQ));
+        if (sp < 0) sp = 0;
+        if (sp > 0x7FFFFFFF) sp = 0x7FFFFFFF;
     }
-    am = cta_max_u64(am, red);
-    int sh = g_msb(am) - 14;
-    if (sh < 0) sh = 0;
-    const int e_seg = e_ref + A.cw_exp[s] - sh;
-    if (threadIdx.x == 0) {
-        A.w.misc[1 + s] = (e_seg > 127 || e_seg < -128);
-        if (s == 2) A.w.misc[0] = e_seg;
+    int64_t g = d_rshift_r(sp * (int64_t)p[4], p[5]);
+    if (g > 0) g = 0;
+    const int err = g < -lim;
+    if (g < -lim) g = -lim;
+    int64_t ex = d_lut_interp(c_exp_lut, 256, g + lim, SPQ);
+    if (ex < 0) ex = 0;
+    if (ex > 0x7FFFFFFF) ex = 0x7FFFFFFF;
+    int64_t egv = d_rshift_r(ex, SPQ - 15);
+    egv = egv > 32768 ? 32768 : (egv < 0 ? 0 : egv);
+    int64_t bq = d_to_q_wide(p[6], p[7]);
+    bq = bq > lim ? lim : (bq < -lim ? -lim : bq);
+    int64_t sg;
+    if (bq <= -lim) sg = 0;
+    else if (bq >= lim) sg = one;
+    else {
+        sg = d_lut_interp(c_sig_lut, 512, bq + lim, SPQ);
+        sg = sg < 0 ? 0 : (sg > one ? one : sg);
     }
-    if (s == 2) {
-        for (int c = threadIdx.x; c < nch; c += blockDim.x)
-            A.w.v[c] = fx_silu(g_sat16(g_round_shift(blk_conv_ch(xs + 4 * c, ws + 4 * c, vmask, tsh), sh)), e_seg);
-        return;
-    }
-    // q / k: one warp per key head, the head's silu outputs then its L2 norm
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int hk = warp; hk < A.KH; hk += nw) {
-        int32_t x[R];
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            const int c = hk * D + lane + 32 * r;
-            x[r] = fx_silu(g_sat16(g_round_shift(blk_conv_ch(xs + 4 * c, ws + 4 * c, vmask, tsh), sh)), e_seg);
-        }
-        fx_l2norm_warp<R>(x, A.lg, s == 0, (s == 0 ? A.w.qs : A.w.kn) + hk * D);
-    }
+    int64_t bv = d_rshift_r(sg, SPQ - 16);
+    bv = bv > 65535 ? 65535 : (bv < 0 ? 0 : bv);
+    eg = (int32_t)egv;
+    beta = (int32_t)bv;
+    return err;
 }
 
-__global__ void __launch_bounds__(1024)
-gdn_blk_front_kernel(const BlkFrontArgs A)
-{
-    __shared__ uint64_t red[32];
-    // wait for the previous kernel in the stream before touching anything:
-    // the next launch may start its state prefetch only once this point is
-    // passed (then every earlier token's state write-back has completed)
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int s = blockIdx.x;
-    if (s < 3) {
-        if (A.D == 32) blk_front_segment<1>(A, s, red);
-        else if (A.D == 64) blk_front_segment<2>(A, s, red);
-        else blk_front_segment<4>(A, s, red);
-        return;
-    }
-    // the scalar path for every value head (gdn_scalar_kernel's body)
-    int err = 0;
-    for (int h = threadIdx.x; h < A.VH; h += blockDim.x) {
-        const int32_t *p = A.sc + (size_t)h * 8;
-        const int64_t arg = d_to_q_wide(p[0], p[1]) + d_to_q_wide(p[2], p[3]);
-        const int64_t one = (int64_t)1 << SPQ, lim = 16 * one;
-        int64_t sp;
-        if (arg <= -lim) sp = 0;
-        else if (arg >= lim) sp = arg;
-        else {
-            const int64_t ax = arg < 0 ? -arg : arg, pos = arg > 0 ? arg : 0;
-            sp = pos + (ax >= lim ? 0 : d_lut_interp(c_sp_lut, 256, lim - ax, SPQ));
-            if (sp < 0) sp = 0;
-            if (sp > 0x7FFFFFFF) sp = 0x7FFFFFFF;
-        }
-        int64_t g = d_rshift_r(sp * (int64_t)p[4], p[5]);
-        if (g > 0) g = 0;
-        err |= g < -lim;
-        if (g < -lim) g = -lim;
-        int64_t ex = d_lut_interp(c_exp_lut, 256, g + lim, SPQ);
-        if (ex < 0) ex = 0;
-        if (ex > 0x7FFFFFFF) ex = 0x7FFFFFFF;
-        int64_t egv = d_rshift_r(ex, SPQ - 15);
-        egv = egv > 32768 ? 32768 : (egv < 0 ? 0 : egv);
-        int64_t bq = d_to_q_wide(p[6], p[7]);
-        bq = bq > lim ? lim : (bq < -lim ? -lim : bq);
-        int64_t sg;
-        if (bq <= -lim) sg = 0;
-        else if (bq >= lim) sg = one;
-        else {
-            sg = d_lut_interp(c_sig_lut, 512, bq + lim, SPQ);
-            sg = sg < 0 ? 0 : (sg > one ? one : sg);
-        }
-        int64_t bv = d_rshift_r(sg, SPQ - 16);
-        bv = bv > 65535 ? 65535 : (bv < 0 ? 0 : bv);
-        A.w.eg[h] = (int32_t)egv;
-        A.w.beta[h] = (int32_t)bv;
-    }
-    err = __syncthreads_or(err);
-    if (threadIdx.x == 0) A.w.misc[4] = err;
-}
-
-struct BlkRecArgs {
-    int32_t KH, VH, tk0, w_e, z_e;
-    int16_t *smem;                     // [VH][D][D]
-    int32_t *semem;                    // [VH][D]
-    const int16_t *zm, *wm;            // [VH][D], [D]
-    BlkWork w;
-    // head-tail input override (emit-chain unit entry): o_acc / e_o from memory
-    const int64_t *o_acc_in;
-    const int32_t *e_o_in;
-};
-
-// warp 0 of a head's CTA: site-12 head emit of the head's D column outputs,
-// the output rmsnorm, the z gate; po / pz / ep for the site-13 launch
+// one warp: site-12 head emit of a value head's D column outputs (o_acc on
+// per-column exponents e_o), the output rmsnorm, the z gate; writes the head's
+// po / pz / ep for site 13 (ref/gdn_emit_chain_vec.c)
 template <int D>
-__device__ void blk_head_tail(const BlkRecArgs &A, int h, const int64_t *s_oacc, const int32_t *s_eo)
+__device__ void blk_head_tail(int h, const int64_t *s_oacc, const int32_t *s_eo, const int16_t *zm, int z_e,
+                              const int16_t *wm, int w_e, const BlkWork &w, const int64_t *sig, const int64_t *rom)
 {
     constexpr int R = D / 32, LG = D == 32 ? 5 : (D == 64 ? 6 : 7);
     const int lane = threadIdx.x & 31;
@@ -457,43 +378,191 @@ __device__ void blk_head_tail(const BlkRecArgs &A, int h, const int64_t *s_oacc,
 #pragma unroll
     for (int r = 0; r < R; r++) oh[r] = g_sat16(g_round_shift(al[r], shh));
     int nsat;
-    const int o_exp = fx_rmsnorm_warp<R>(oh, emin - shh, A.wm, A.w_e, LG, po, nsat);
+    const int o_exp = fx_rmsnorm_warp<R>(oh, emin - shh, wm, w_e, LG, po, nsat, rom);
 #pragma unroll
     for (int r = 0; r < R; r++) {
         const int j = lane + 32 * r;
-        A.w.po[h * D + j] = (int16_t)po[r];
-        A.w.pz[h * D + j] = g_sat16(fx_silu(A.zm[h * D + j], A.z_e));
+        w.po[h * D + j] = (int16_t)po[r];
+        w.pz[h * D + j] = g_sat16(fx_silu(zm[h * D + j], z_e, sig));
     }
-    if (lane == 0) A.w.ep[h] = o_exp + A.z_e;
+    if (lane == 0) w.ep[h] = o_exp + z_e;
+}
+
+struct BlkHeadArgs {
+    const int16_t *xtap, *wtap;        // [2*KH*D + VH*D][4]
+    const int32_t *sc;                 // [VH][8]
+    int32_t KH, VH, tk0, w_e, z_e;
+    int32_t e_t[3][4], tvalid[3][4], cw_exp[3];
+    int16_t *smem;                     // [VH][D][D]
+    int32_t *semem;                    // [VH][D]
+    const int16_t *zm, *wm;            // [VH][D], [D]
+    BlkWork w;
+};
+
+// One CTA per value head h, D*D/16 threads: the whole token for that head.
+//  1. The three conv segments' maxima (q, k, v; spec B 2.1.3).  One segment
+//     shares one requantiser shift, so every cluster reduces whole segments
+//     (at KH 16 / VH 32 / D 128, 8192 channels, 128 KB of taps from L2),
+//     each of its CTAs a slice, the partial maxima exchanged through
+//     distributed shared memory.
+//  2. One warp per task: q and k of key head h % KH (silu, L2 norm), v of head
+//     h (silu), the scalar path of head h; results in shared memory.
+//  3. The recurrence, stages 1-5 (state column j owned by D/16 lanes of 16
+//     keys each, ref/gdn_block_vec.c:304-380).
+//  4. Warp 0: the head tail (site-12 emit, rmsnorm_bf, z gate).
+// thread-block cluster helpers: the CTA's rank, the cluster's size, a 64-bit
+// load from the same shared-memory variable of CTA `rank`, and the split
+// cluster barrier.  A launch without a cluster attribute is a cluster of one.
+__device__ __forceinline__ unsigned blk_cl_rank()
+{ unsigned r; asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r)); return r; }
+__device__ __forceinline__ unsigned blk_cl_size()
+{ unsigned r; asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r)); return r; }
+__device__ __forceinline__ uint64_t blk_ld_cluster_u64(const void *p, unsigned rank)
+{
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    unsigned ra;
+    uint64_t v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(ra) : "memory");
+    return v;
+}
+__device__ __forceinline__ void blk_cl_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void blk_cl_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// conv + requantiser + silu of one head's D channels of segment s, R per lane
+// (element lane + 32 r), the channels starting at c0
+template <int R>
+__device__ __forceinline__ void blk_seg_head(const BlkHeadArgs &A, int s, size_t c0, int shs, int es,
+                                             const int64_t *sig, int32_t (&x)[R])
+{
+    int tsh[4], vm;
+    blk_taps(A.e_t[s], A.tvalid[s], tsh, vm);
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const size_t c = c0 + lane + 32 * r;
+        x[r] = fx_silu(g_sat16(g_round_shift(blk_conv_ch(A.xtap + 4 * c, A.wtap + 4 * c, vm, tsh), shs)), es, sig);
+    }
 }
 
 template <int D>
 __global__ void __launch_bounds__(D * D / 16)
-gdn_blk_rec_kernel(const BlkRecArgs A)
+gdn_blk_head_kernel(const BlkHeadArgs A)
 {
-    constexpr int LPC = D / 16, CPW = 32 / LPC;
-    __shared__ int64_t s_oacc[D];
-    __shared__ int32_t s_eo[D];
-    const int h = blockIdx.x;
+    constexpr int NT = D * D / 16, NW = NT / 32, LPC = D / 16, CPW = 32 / LPC, R = D / 32;
+    constexpr int LG = D == 32 ? 5 : (D == 64 ? 6 : 7);
+    __shared__ int64_t s_sig[513], s_rom[64], s_oacc[D];
+    __shared__ __align__(16) uint4 s_st[2 * NT];    // the state slices, [half][thread]
+    __shared__ __align__(16) int16_t s_kn[D], s_qs[D];
+    __shared__ int32_t s_v[D], s_eo[D], s_sc[3], s_sh[3], s_es[3], s_errc;
+    __shared__ uint64_t s_red[3][NW], s_part[3];
+    const int h = blockIdx.x, hk = h % A.KH;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j = warp * CPW + lane / LPC;          // value column
     const int i0 = 16 * (lane % LPC);               // key slice
-    const int hk = h % A.KH;
 
-    // the state slice, its exponent and the gate inputs do not depend on the
-    // front kernel: load them before waiting for it
+    // Before the wait: the constant tables and this head's state slice (an
+    // asynchronous copy into shared memory).  A grid of this kernel starts only
+    // once the launch before it has passed its own wait (the site-13 launch of
+    // the previous token, or a later kernel), so the previous token's state
+    // write-back has completed by then.
     int16_t *scol = A.smem + ((size_t)h * D + j) * D + i0;
-    uint32_t sm[8], kn[8], qs[8];
-    ld16_i16(scol, sm);
+    {
+        const unsigned d0 = (unsigned)__cvta_generic_to_shared(s_st + threadIdx.x);
+        const unsigned d1 = (unsigned)__cvta_generic_to_shared(s_st + NT + threadIdx.x);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(d0), "l"(scol) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(d1), "l"(scol + 8) : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < 513; i += NT) s_sig[i] = d_sig_tab[i];
+    for (int i = threadIdx.x; i < 64; i += NT) s_rom[i] = d_rsqrt_rom[i];
     const int se_j = A.semem[h * D + j];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    ld16_i16(A.w.kn + (size_t)hk * D + i0, kn);
-    ld16_i16(A.w.qs + (size_t)hk * D + i0, qs);
-    const int32_t v_j = A.w.v[h * D + j];
-    const int egh = A.w.eg[h], bth = A.w.beta[h], tk0 = A.tk0, e_v = A.w.misc[0];
 
-    // stages 1-2: decay, sk dot
+    // 1. segment maxima: the CTAs of a cluster split each segment's channels,
+    //    then every CTA reads the cluster's partial maxima from the others'
+    //    shared memory
+    const int QCH = A.KH * D;
+    const int crank = (int)blk_cl_rank(), csize = (int)blk_cl_size();
+#pragma unroll
+    for (int s = 0; s < 3; s++) {
+        int tsh[4], vm;
+        blk_taps(A.e_t[s], A.tvalid[s], tsh, vm);
+        const int nch = s == 2 ? A.VH * D : QCH;
+        const int16_t *xs = A.xtap + (size_t)s * QCH * 4, *ws = A.wtap + (size_t)s * QCH * 4;
+        uint64_t m = 0;
+#pragma unroll 2
+        for (int c = crank * NT + threadIdx.x; c < nch; c += csize * NT) {
+            const uint64_t a = g_abs64(blk_conv_ch(xs + 4 * c, ws + 4 * c, vm, tsh));
+            m = a > m ? a : m;
+        }
+        m = warp_max_u64(m);
+        if (lane == 0) s_red[s][warp] = m;
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int s = 0; s < 3; s++) {
+            const uint64_t m = warp_max_u64(lane < NW ? s_red[s][lane] : 0);
+            if (lane == 0) s_part[s] = m;
+        }
+    }
+    blk_cl_arrive();
+    blk_cl_wait();
+    if (warp == 0) {
+        int errc = 0;
+#pragma unroll
+        for (int s = 0; s < 3; s++) {
+            uint64_t m = lane < csize ? blk_ld_cluster_u64(&s_part[s], (unsigned)lane) : 0;
+            m = warp_max_u64(m);
+            int tsh[4], vm;
+            int x = g_msb(m) - 14;
+            x = x < 0 ? 0 : x;
+            const int e = blk_taps(A.e_t[s], A.tvalid[s], tsh, vm) + A.cw_exp[s] - x;
+            errc |= e > 127 || e < -128;
+            if (lane == 0) { s_sh[s] = x; s_es[s] = e; }
+        }
+        if (lane == 0) s_errc = errc;
+    }
+    // this CTA is done reading the others' partials; the matching wait is the
+    // kernel's last statement, so no CTA leaves while another may still read it
+    blk_cl_arrive();
+    __syncthreads();
+
+    // 2. this head's inputs, one warp per task
+    for (int t = warp; t < 4; t += NW) {
+        int32_t x[R];
+        if (t == 0) {
+            blk_seg_head<R>(A, 0, (size_t)hk * D, s_sh[0], s_es[0], s_sig, x);
+            fx_l2norm_warp<R>(x, LG, true, s_qs, s_rom);
+        } else if (t == 1) {
+            blk_seg_head<R>(A, 1, (size_t)QCH + (size_t)hk * D, s_sh[1], s_es[1], s_sig, x);
+            fx_l2norm_warp<R>(x, LG, false, s_kn, s_rom);
+        } else if (t == 2) {
+            blk_seg_head<R>(A, 2, 2 * (size_t)QCH + (size_t)h * D, s_sh[2], s_es[2], s_sig, x);
+#pragma unroll
+            for (int r = 0; r < R; r++) s_v[lane + 32 * r] = x[r];
+        } else if (lane == 0) {
+            int32_t eg, bt;
+            s_sc[2] = blk_scalar(A.sc + (size_t)h * 8, eg, bt);
+            s_sc[0] = eg;
+            s_sc[1] = bt;
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+
+    // 3. the recurrence; stages 1-2: decay, sk dot
+    uint32_t sm[8], kn[8], qs[8];
+    {
+        const uint4 a0 = s_st[threadIdx.x], a1 = s_st[NT + threadIdx.x];
+        sm[0] = a0.x; sm[1] = a0.y; sm[2] = a0.z; sm[3] = a0.w; sm[4] = a1.x; sm[5] = a1.y; sm[6] = a1.z; sm[7] = a1.w;
+    }
+    ld16_i16(s_kn + i0, kn);
+    ld16_i16(s_qs + i0, qs);
+    const int32_t v_j = s_v[j];
+    const int egh = s_sc[0], bth = s_sc[1], tk0 = A.tk0, e_v = s_es[2];
     int32_t w18[16];
     int64_t sk = 0;
 #pragma unroll
@@ -522,24 +591,27 @@ gdn_blk_rec_kernel(const BlkRecArgs A)
     const int64_t d_m = g_round_shift(draw, shd);
     const int e_dm = e_d + 16 - shd;
 
-    // stage 4: update, write-back quantiser
+    // stage 4: update, write-back quantiser.  In 32 bits: |w18| <= 2^17 + 1,
+    // |d_m| <= 2^15 and |k| <= 2^15, so |u| < 2^30 + 2^18 and shq <= 16.
     const int e_kd = 15 + e_dm;
     const int e_u = masked ? e_kd : (se_j + 2 < e_kd ? se_j + 2 : e_kd);
     int su = se_j + 2 - e_u, sk2 = e_kd - e_u;
     if (su > 63) su = 63;
     if (sk2 > 63) sk2 = 63;
-    uint64_t amax = 0;
+    const int32_t d32 = (int32_t)d_m;
+    uint32_t amax = 0;
 #pragma unroll
     for (int p = 0; p < 16; p++) {
         const int32_t k = (p & 1) ? hi16(kn[p >> 1]) : lo16(kn[p >> 1]);
-        const int64_t u = (tk0 ? 0 : g_floor_shr(w18[p], su)) + g_floor_shr((int64_t)k * d_m, sk2);
-        const uint64_t a = g_abs64(u);
+        const int32_t u = (tk0 ? 0 : blk_floor_shr32(w18[p], su)) + blk_floor_shr32(k * d32, sk2);
+        const uint32_t a = u < 0 ? 0u - (uint32_t)u : (uint32_t)u;
         amax = a > amax ? a : amax;
     }
 #pragma unroll
-    for (int o = 1; o < LPC; o <<= 1) { const uint64_t w = __shfl_xor_sync(BLK_FULL, amax, o); amax = w > amax ? w : amax; }
-    int sh = g_msb(amax) - 14;
-    if (sh < 0) sh = 0;
+    for (int o = 1; o < LPC; o <<= 1) amax = max(amax, __shfl_xor_sync(BLK_FULL, amax, o));
+    int shq = (amax ? 31 - __clz((int)amax) : 0) - 14;
+    if (shq < 0) shq = 0;
+    const int32_t rq = shq ? 1 << (shq - 1) : 0;
     uint32_t sn[8];
     int64_t od = 0;
 #pragma unroll
@@ -548,8 +620,9 @@ gdn_blk_rec_kernel(const BlkRecArgs A)
 #pragma unroll
         for (int hlf = 0; hlf < 2; hlf++) {
             const int32_t k = hlf ? hi16(kn[p]) : lo16(kn[p]);
-            const int64_t u = (tk0 ? 0 : g_floor_shr(w18[2 * p + hlf], su)) + g_floor_shr((int64_t)k * d_m, sk2);
-            r2[hlf] = g_sat16(g_round_shift(u, sh));
+            const int32_t u = (tk0 ? 0 : blk_floor_shr32(w18[2 * p + hlf], su)) + blk_floor_shr32(k * d32, sk2);
+            const int32_t v = (u + rq) >> shq;
+            r2[hlf] = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
         }
         sn[p] = ((uint32_t)(uint16_t)r2[0]) | ((uint32_t)(uint16_t)r2[1] << 16);
         od += (int64_t)r2[0] * lo16(qs[p]) + (int64_t)r2[1] * hi16(qs[p]);     // stage 5
@@ -558,7 +631,7 @@ gdn_blk_rec_kernel(const BlkRecArgs A)
     reinterpret_cast<uint4 *>(scol)[1] = make_uint4(sn[4], sn[5], sn[6], sn[7]);
 #pragma unroll
     for (int o = 1; o < LPC; o <<= 1) od += __shfl_xor_sync(BLK_FULL, od, o);
-    const int se_new = e_u - sh, e_o = se_new + 18;
+    const int se_new = e_u - shq, e_o = se_new + 18;
     int err = 0;
     if (lane % LPC == 0) {
         A.semem[h * D + j] = se_new;
@@ -567,24 +640,35 @@ gdn_blk_rec_kernel(const BlkRecArgs A)
         err = se_new > 127 || se_new < -128 || e_o > 127 || e_o < -128;
     }
     err = __syncthreads_or(err);
+
+    // 4. the head tail
     if (warp == 0) {
-        blk_head_tail<D>(A, h, s_oacc, s_eo);
-        if (lane == 0) A.w.err_se[h] = err;
+        blk_head_tail<D>(h, s_oacc, s_eo, A.zm, A.z_e, A.wm, A.w_e, A.w, s_sig, s_rom);
+        if (lane == 0) A.w.err[h] = (s_errc ? 1 : 0) | (s_sc[2] ? 2 : 0) | (err ? 4 : 0);
     }
+    blk_cl_wait();
 }
 
 // the emit chain alone (site 12 -> rmsnorm -> z gate) on o_acc / e_o from
 // memory, one warp per head: the unit entry point of the block's tail
+struct BlkChainArgs {
+    const int64_t *o_acc;              // [H][D]
+    const int32_t *e_o;                // [H][D]
+    const int16_t *zm, *wm;
+    int32_t w_e, z_e;
+    BlkWork w;
+};
+
 template <int D>
 __global__ void __launch_bounds__(32)
-gdn_blk_chain_kernel(const BlkRecArgs A)
+gdn_blk_chain_kernel(const BlkChainArgs A)
 {
     __shared__ int64_t s_oacc[D];
     __shared__ int32_t s_eo[D];
     const int h = blockIdx.x, lane = threadIdx.x;
-    for (int j = lane; j < D; j += 32) { s_oacc[j] = A.o_acc_in[h * D + j]; s_eo[j] = A.e_o_in[h * D + j]; }
+    for (int j = lane; j < D; j += 32) { s_oacc[j] = A.o_acc[h * D + j]; s_eo[j] = A.e_o[h * D + j]; }
     __syncwarp();
-    blk_head_tail<D>(A, h, s_oacc, s_eo);
+    blk_head_tail<D>(h, s_oacc, s_eo, A.zm, A.z_e, A.wm, A.w_e, A.w, d_sig_tab, d_rsqrt_rom);
 }
 
 struct BlkTailArgs {
@@ -593,45 +677,78 @@ struct BlkTailArgs {
     const int32_t *ep;
     int16_t *y;
     int32_t *status;                   // [5] y_exp, err_conv, err_g, err_se, y_sat
-    const int32_t *misc, *err_se;      // NULL for the site-13 unit entry
+    const int32_t *err;                // [VH] the heads' flag words; NULL for the site-13 unit entry
 };
 
-// site 13 (ref/gdn_block_vec.c:396-418): one CTA over all VH*D products
+// one site-13 product aligned to the token's minimum head exponent e_y:
+// |po * pz| <= 2^30, so 32 bits hold it
+__device__ __forceinline__ int32_t blk_site13_term(const BlkTailArgs &A, int i, int e_y)
+{
+    const int s = A.ep[i / A.D] - e_y;
+    return blk_floor_shr32((int32_t)A.po[i] * A.pz[i], s > 63 ? 63 : s);
+}
+
+// site 13 (ref/gdn_block_vec.c:396-418): one CTA over all VH*D products, the
+// first 8192 of them kept in registers between the two passes
 __global__ void __launch_bounds__(1024)
 gdn_blk_tail_kernel(const BlkTailArgs A)
 {
+    constexpr int KR = 8;
     __shared__ uint64_t red[32];
+    __shared__ int32_t s_ey, s_err;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    int e_y = A.ep[0];
-    for (int h = 1; h < A.VH; h++) e_y = min(e_y, A.ep[h]);
-    const int n = A.VH * A.D;
-    uint64_t am = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        int s = A.ep[i / A.D] - e_y;
-        const uint64_t a = g_abs64(g_floor_shr((int64_t)A.po[i] * A.pz[i], s > 63 ? 63 : s));
-        am = a > am ? a : am;
+    if (threadIdx.x < 32) {
+        int m = 0x7FFFFFFF, er = 0;
+        for (int h = threadIdx.x; h < A.VH; h += 32) {
+            m = min(m, A.ep[h]);
+            if (A.err) er |= A.err[h];
+        }
+        m = warp_min_i32(m);
+        er = (int)__reduce_or_sync(BLK_FULL, (unsigned)er);
+        if (threadIdx.x == 0) { s_ey = m; s_err = er; }
     }
-    am = cta_max_u64(am, red);
+    __syncthreads();
+    const int e_y = s_ey, n = A.VH * A.D, nt = blockDim.x;
+    int32_t pv[KR];
+    uint32_t am = 0;
+#pragma unroll
+    for (int k = 0; k < KR; k++) {
+        const int i = threadIdx.x + nt * k;
+        pv[k] = i < n ? blk_site13_term(A, i, e_y) : 0;
+        am = max(am, pv[k] < 0 ? 0u - (uint32_t)pv[k] : (uint32_t)pv[k]);
+    }
+    for (int i = threadIdx.x + nt * KR; i < n; i += nt) {
+        const int32_t v = blk_site13_term(A, i, e_y);
+        am = max(am, v < 0 ? 0u - (uint32_t)v : (uint32_t)v);
+    }
+    am = (uint32_t)cta_max_u64(am, red);
     int sh = g_msb(am) - 14;
     if (sh < 0) sh = 0;
+    const int32_t rq = sh ? 1 << (sh - 1) : 0;
     int sat = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        int s = A.ep[i / A.D] - e_y;
-        const int64_t v = g_round_shift(g_floor_shr((int64_t)A.po[i] * A.pz[i], s > 63 ? 63 : s), sh);
+#pragma unroll
+    for (int k = 0; k < KR; k++) {
+        const int i = threadIdx.x + nt * k;
+        if (i < n) {
+            const int32_t v = (pv[k] + rq) >> sh;
+            sat |= v > 32767 || v < -32768;
+            A.y[i] = g_sat16(v);
+        }
+    }
+    for (int i = threadIdx.x + nt * KR; i < n; i += nt) {
+        const int32_t v = (blk_site13_term(A, i, e_y) + rq) >> sh;
         sat |= v > 32767 || v < -32768;
         A.y[i] = g_sat16(v);
     }
     sat = __syncthreads_or(sat);
     if (threadIdx.x == 0) {
         A.status[0] = e_y - sh;
-        A.status[4] = sat;
-        if (A.misc) {
-            int es = 0;
-            for (int h = 0; h < A.VH; h++) es |= A.err_se[h];
-            A.status[1] = A.misc[1] | A.misc[2] | A.misc[3];
-            A.status[2] = A.misc[4];
-            A.status[3] = es;
+        A.status[4] = sat != 0;
+        if (A.err) {
+            A.status[1] = s_err & 1;
+            A.status[2] = s_err >> 1 & 1;
+            A.status[3] = s_err >> 2 & 1;
         }
     }
 }
@@ -670,7 +787,7 @@ gdn_conv_unit_kernel(int nch, const int16_t *x, const int16_t *w, const int32_t 
 __global__ void gdn_silu_unit_kernel(int n, int total, const int16_t *sm, const int32_t *e, int32_t *y)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < total) y[i] = fx_silu(sm[i], e[i / n]);
+    if (i < total) y[i] = fx_silu(sm[i], e[i / n], d_sig_tab);
 }
 
 // L2-norm unit: one warp per vector of N = 32 R
@@ -682,8 +799,8 @@ gdn_l2norm_unit_kernel(const int32_t *x, int log2n, int16_t *k, int16_t *q)
     int32_t xr[R];
 #pragma unroll
     for (int r = 0; r < R; r++) xr[r] = x[(size_t)v * 32 * R + lane + 32 * r];
-    fx_l2norm_warp<R>(xr, log2n, false, k + (size_t)v * 32 * R);
-    fx_l2norm_warp<R>(xr, log2n, true, q + (size_t)v * 32 * R);
+    fx_l2norm_warp<R>(xr, log2n, false, k + (size_t)v * 32 * R, d_rsqrt_rom);
+    fx_l2norm_warp<R>(xr, log2n, true, q + (size_t)v * 32 * R, d_rsqrt_rom);
 }
 
 // rmsnorm_bf unit: one warp per vector of N = 32 R
@@ -698,7 +815,7 @@ gdn_rmsnorm_unit_kernel(const int16_t *xm, const int32_t *xe, const int16_t *wm,
 #pragma unroll
     for (int r = 0; r < R; r++) x[r] = xm[(size_t)v * 32 * R + lane + 32 * r];
     int nsat;
-    const int e = fx_rmsnorm_warp<R>(x, xe[v], wm + (size_t)v * 32 * R, we[v], LG, out, nsat);
+    const int e = fx_rmsnorm_warp<R>(x, xe[v], wm + (size_t)v * 32 * R, we[v], LG, out, nsat, d_rsqrt_rom);
 #pragma unroll
     for (int r = 0; r < R; r++) o[(size_t)v * 32 * R + lane + 32 * r] = (int16_t)out[r];
     if (lane == 0) o_exp[v] = e;
@@ -706,18 +823,62 @@ gdn_rmsnorm_unit_kernel(const int16_t *xm, const int32_t *xe, const int16_t *wm,
 
 // ------------------------------------------------------------- host entries
 
-static cudaError_t blk_launch(const void *fn, dim3 grid, dim3 block, cudaStream_t st, bool pdl, void **args)
+static cudaError_t blk_launch(const void *fn, dim3 grid, dim3 block, cudaStream_t st, bool pdl, void **args,
+                              int cluster = 1)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na++].val.programmaticStreamSerializationAllowed = 1;
+    }
+    if (cluster > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)cluster;
+        attr[na].val.clusterDim.y = 1;
+        attr[na++].val.clusterDim.z = 1;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// cluster size of the head kernel: the largest of 8, 4, 2 that divides VH and
+// that the device can co-schedule for this kernel (asked once per kernel)
+static int blk_head_cluster(const void *fn, int VH, int nt)
+{
+    static const void *seen[3] = {nullptr, nullptr, nullptr};
+    static int best[3] = {1, 1, 1};
+    int slot = 0;
+    while (slot < 3 && seen[slot] && seen[slot] != fn) slot++;
+    if (slot == 3) slot = 0;
+    if (seen[slot] != fn) {
+        int c = 8;
+        for (; c > 1; c >>= 1) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(c);
+            cfg.blockDim = dim3(nt);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)c;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n >= 1) break;
+            cudaGetLastError();
+        }
+        best[slot] = c;
+        seen[slot] = fn;
+    }
+    int c = best[slot];
+    while (c > 1 && VH % c) c >>= 1;
+    return c;
 }
 
 static bool blk_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
@@ -726,7 +887,7 @@ extern "C" size_t deltanet_work_bytes(int KH, int VH, int D)
 {
     if (KH <= 0 || VH <= 0 || !blk_dim_ok(D)) return 0;
     size_t n = 0;
-    blk_work_layout(nullptr, KH, VH, D, &n);
+    blk_work_layout(nullptr, VH, D, &n);
     return n;
 }
 
@@ -746,34 +907,25 @@ extern "C" int deltanet_step(const deltanet_args *a, void *stream)
     cudaError_t e = upload_blk_tables();
     if (e != cudaSuccess) return gdn_fail(e);
     const int KH = a->KH, VH = a->VH, D = a->D;
-    const BlkWork w = blk_work_layout(a->work, KH, VH, D, nullptr);
+    const BlkWork w = blk_work_layout(a->work, VH, D, nullptr);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
-    BlkFrontArgs F;
-    F.xtap = a->xtap; F.wtap = a->wtap; F.KH = KH; F.VH = VH; F.D = D;
-    F.lg = D == 32 ? 5 : (D == 64 ? 6 : 7);
+    BlkHeadArgs H;
+    H.xtap = a->xtap; H.wtap = a->wtap; H.sc = a->sc; H.KH = KH; H.VH = VH; H.tk0 = a->tk0 != 0;
+    H.w_e = a->w_e; H.z_e = a->z_e;
     for (int s = 0; s < 3; s++) {
-        F.cw_exp[s] = a->cw_exp[s];
-        for (int t = 0; t < 4; t++) { F.e_t[s][t] = a->e_t[s][t]; F.tvalid[s][t] = a->tvalid[s][t] != 0; }
+        H.cw_exp[s] = a->cw_exp[s];
+        for (int t = 0; t < 4; t++) { H.e_t[s][t] = a->e_t[s][t]; H.tvalid[s][t] = a->tvalid[s][t] != 0; }
     }
-    F.sc = a->sc; F.w = w;
-    void *fa[] = {&F};
-    e = blk_launch((const void *)gdn_blk_front_kernel, dim3(4), dim3(1024), st, a->pdl != 0, fa);
-    if (e != cudaSuccess) return gdn_fail(e);
-
-    BlkRecArgs R;
-    R.KH = KH; R.VH = VH; R.tk0 = a->tk0 != 0; R.w_e = a->w_e; R.z_e = a->z_e;
-    R.smem = a->smem; R.semem = a->semem; R.zm = a->zm; R.wm = a->wm; R.w = w;
-    R.o_acc_in = nullptr; R.e_o_in = nullptr;
-    void *ra[] = {&R};
-    const void *rk = D == 32 ? (const void *)gdn_blk_rec_kernel<32>
-                   : (D == 64 ? (const void *)gdn_blk_rec_kernel<64> : (const void *)gdn_blk_rec_kernel<128>);
-    e = blk_launch(rk, dim3(VH), dim3(D * D / 16), st, true, ra);
+    H.smem = a->smem; H.semem = a->semem; H.zm = a->zm; H.wm = a->wm; H.w = w;
+    void *ha[] = {&H};
+    const void *hk = D == 32 ? (const void *)gdn_blk_head_kernel<32>
+                   : (D == 64 ? (const void *)gdn_blk_head_kernel<64> : (const void *)gdn_blk_head_kernel<128>);
+    e = blk_launch(hk, dim3(VH), dim3(D * D / 16), st, a->pdl != 0, ha, blk_head_cluster(hk, VH, D * D / 16));
     if (e != cudaSuccess) return gdn_fail(e);
 
     BlkTailArgs T;
-    T.VH = VH; T.D = D; T.po = w.po; T.pz = w.pz; T.ep = w.ep; T.y = a->y; T.status = a->status;
-    T.misc = w.misc; T.err_se = w.err_se;
+    T.VH = VH; T.D = D; T.po = w.po; T.pz = w.pz; T.ep = w.ep; T.y = a->y; T.status = a->status; T.err = w.err;
     void *ta[] = {&T};
     e = blk_launch((const void *)gdn_blk_tail_kernel, dim3(1), dim3(1024), st, true, ta);
     return e == cudaSuccess ? 0 : gdn_fail(e);
@@ -908,10 +1060,9 @@ extern "C" int gdn_emit_chain_dev(int H, int D, const int64_t *o_acc, const int3
     cudaError_t e = upload_blk_tables();
     if (e != cudaSuccess) return gdn_fail(e);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    BlkRecArgs R = {};
-    R.KH = 1; R.VH = H; R.w_e = we; R.z_e = z_e; R.zm = zm; R.wm = wm;
-    R.w = blk_work_layout(work, 1, H, D, nullptr);
-    R.o_acc_in = o_acc; R.e_o_in = e_o;
+    BlkChainArgs R = {};
+    R.o_acc = o_acc; R.e_o = e_o; R.zm = zm; R.wm = wm; R.w_e = we; R.z_e = z_e;
+    R.w = blk_work_layout(work, H, D, nullptr);
     if (D == 32) gdn_blk_chain_kernel<32><<<H, 32, 0, st>>>(R);
     else if (D == 64) gdn_blk_chain_kernel<64><<<H, 32, 0, st>>>(R);
     else gdn_blk_chain_kernel<128><<<H, 32, 0, st>>>(R);
