@@ -134,11 +134,12 @@ typedef struct {
  * -11 (bad shape, no valid tap in a segment) or -20 (CUDA error). */
 int gdn_block_token_host(int KH, int VH, int D, gdn_blk_t *b);
 
-/* The same token on DEVICE buffers, state resident.  Three launches on
- * `stream` (front: conv/silu/L2 norms/scalar path; one CTA per value head:
- * recurrence, head emit, rmsnorm, gate; site-13 tail), each a programmatic
- * dependent of the previous one; with pdl set the first is also a dependent
- * of the kernel before it in the stream.  The small per-token control words
+/* The same token on DEVICE buffers, state resident.  Two launches on
+ * `stream` (one CTA per value head, in clusters of up to 8: conv segment
+ * maxima, silu, L2 norms, scalar path, recurrence, head emit, rmsnorm, gate;
+ * then the site-13 tail), the second a programmatic dependent of the first;
+ * with pdl set the first is also a dependent of the kernel before it in the
+ * stream.  The small per-token control words
  * (tap exponents, validity, segment weight exponents) are passed by value.
  * status (device, 5 ints) receives {y_exp, err_conv, err_g, err_se, y_sat}
  * for this token.  work: deltanet_work_bytes(KH, VH, D) bytes of device
