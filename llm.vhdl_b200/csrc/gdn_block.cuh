@@ -34,6 +34,9 @@
 
 __device__ int64_t d_sig_tab[513];      // the Q30 sigmoid table, global copy for divergent reads
 __device__ int64_t d_rsqrt_rom[64];     // round(2^30 / sqrt(1 + k/64))
+// global copies of the scalar path's Q30 tables (the constant-bank ones serve
+// uniform reads; these are copied into shared memory by every thread)
+__device__ int64_t d_sp_tab[257], d_exp_tab[257], d_sg_tab[513];
 
 static unsigned long long g_blk_tab_ready = 0;
 
@@ -52,6 +55,13 @@ static cudaError_t upload_blk_tables()
     for (int k = 0; k < 64; k++) rom[k] = llround(1073741824.0 / sqrt(1.0 + (double)k / 64.0));
     e = cudaMemcpyToSymbol(d_sig_tab, ts, sizeof ts);
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(d_rsqrt_rom, rom, sizeof rom);
+    static int64_t sp[257], ex[257], sg[513];
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(sp, c_sp_lut, sizeof sp);
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(ex, c_exp_lut, sizeof ex);
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(sg, c_sig_lut, sizeof sg);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(d_sp_tab, sp, sizeof sp);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(d_exp_tab, ex, sizeof ex);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(d_sg_tab, sg, sizeof sg);
     if (e == cudaSuccess && dev < 64) g_blk_tab_ready |= 1ull << dev;
     return e;
 }
@@ -161,11 +171,16 @@ __device__ int64_t fx_rms_inv(int64_t S, int xe, int lg, const int64_t *rom)
     return inv > 2147483647LL ? 2147483647LL : (inv < 0 ? 0 : inv);
 }
 
-__device__ __forceinline__ int64_t warp_sum_i64(int64_t v)
+// warp sum of non-negative 64-bit values (sums of squares) as three 21-bit
+// slices, each summed exactly in 32 bits by one reduction; equal to the
+// 64-bit sum modulo 2^64
+__device__ __forceinline__ int64_t warp_sum_sq(int64_t v)
 {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(BLK_FULL, v, o);
-    return v;
+    const uint64_t u = (uint64_t)v;
+    const uint64_t lo = __reduce_add_sync(BLK_FULL, (unsigned)(u & 0x1FFFFF));
+    const uint64_t mi = __reduce_add_sync(BLK_FULL, (unsigned)((u >> 21) & 0x1FFFFF));
+    const uint64_t hi = __reduce_add_sync(BLK_FULL, (unsigned)(u >> 42));
+    return (int64_t)((hi << 42) + (mi << 21) + lo);
 }
 __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v)
 {
@@ -201,7 +216,7 @@ __device__ void fx_l2norm_warp(const int32_t (&x)[R], int log2n, bool q_path, in
     int64_t ssq = 0;
 #pragma unroll
     for (int r = 0; r < R; r++) ssq += (int64_t)x[r] * x[r];
-    ssq = warp_sum_i64(ssq);
+    ssq = warp_sum_sq(ssq);
     const int lane = threadIdx.x & 31;
     if (ssq == 0) {
 #pragma unroll
@@ -226,18 +241,17 @@ __device__ int fx_rmsnorm_warp(const int32_t (&xm)[R], int xe, const int16_t *wm
     int64_t S = 0;
 #pragma unroll
     for (int r = 0; r < R; r++) S += (int64_t)xm[r] * xm[r];
-    S = warp_sum_i64(S);
+    S = warp_sum_sq(S);
     const int64_t inv = fx_rms_inv(S, xe, lg, rom);
     int64_t raw[R];
-    uint64_t mx = 0;
+    int mb = 0;
 #pragma unroll
     for (int r = 0; r < R; r++) {
         raw[r] = fx_narrow(xm[r] * inv, 48) * (int64_t)wm[lane + 32 * r];
-        const uint64_t a = (uint64_t)(raw[r] < 0 ? -raw[r] : raw[r]);
-        mx = a > mx ? a : mx;
+        mb = max(mb, fx_msb63((int64_t)(uint64_t)(raw[r] < 0 ? -raw[r] : raw[r])));
     }
-    mx = warp_max_u64(mx);
-    int st = fx_msb63((int64_t)mx) - 14;
+    mb = __reduce_max_sync(BLK_FULL, mb);            // |raw| < 2^62: the msb of the maximum
+    int st = mb - 14;
     if (st < 0) st = 0;
     const int64_t bias = st == 0 ? 0 : fx_sll(1, st - 1);
     nsat = 0;
@@ -256,6 +270,7 @@ struct BlkWork {                       // device scratch between the two launche
     int16_t *po, *pz;                  // [VH][D] normed output / gated z
     int32_t *ep;                       // [VH] product exponents
     int32_t *err;                      // [VH] bit 0 conv segment exponent, bit 1 g, bit 2 state exponent
+    int32_t *pmax, *pmin;              // [VH] largest / smallest product po * pz of each head
 };
 
 static size_t blk_al(size_t n) { return (n + 255) & ~(size_t)255; }
@@ -270,6 +285,8 @@ static BlkWork blk_work_layout(void *base, int VH, int D, size_t *bytes)
     BLK_TAKE(pz, int16_t, VH * D)
     BLK_TAKE(ep, int32_t, VH)
     BLK_TAKE(err, int32_t, VH)
+    BLK_TAKE(pmax, int32_t, VH)
+    BLK_TAKE(pmin, int32_t, VH)
 #undef BLK_TAKE
     if (bytes) *bytes = off;
     return w;
@@ -310,7 +327,8 @@ __device__ __forceinline__ int blk_taps(const int32_t (&e_t)[4], const int32_t (
 // gdn_scalar_int, ref/gdn_scalar_vec.c:100-156; the same arithmetic as
 // gdn_scalar_kernel): eg (Q15 decay) and beta (Q16) from the head's eight
 // inputs; returns 1 when g was clamped at -16
-__device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta)
+__device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta, const int64_t *tsp, const int64_t *tex,
+                           const int64_t *tsg)
 {
     const int64_t arg = d_to_q_wide(p[0], p[1]) + d_to_q_wide(p[2], p[3]);
     const int64_t one = (int64_t)1 << SPQ, lim = 16 * one;
@@ -319,7 +337,7 @@ __device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta)
     else if (arg >= lim) sp = arg;
     else {
         const int64_t ax = arg < 0 ? -arg : arg, pos = arg > 0 ? arg : 0;
-        sp = pos + (ax >= lim ? 0 : d_lut_interp(c_sp_lut, 256, lim - ax, SPQ));
+        sp = pos + (ax >= lim ? 0 : d_lut_interp(tsp, 256, lim - ax, SPQ));
         if (sp < 0) sp = 0;
         if (sp > 0x7FFFFFFF) sp = 0x7FFFFFFF;
     }
@@ -327,7 +345,7 @@ __device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta)
     if (g > 0) g = 0;
     const int err = g < -lim;
     if (g < -lim) g = -lim;
-    int64_t ex = d_lut_interp(c_exp_lut, 256, g + lim, SPQ);
+    int64_t ex = d_lut_interp(tex, 256, g + lim, SPQ);
     if (ex < 0) ex = 0;
     if (ex > 0x7FFFFFFF) ex = 0x7FFFFFFF;
     int64_t egv = d_rshift_r(ex, SPQ - 15);
@@ -338,7 +356,7 @@ __device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta)
     if (bq <= -lim) sg = 0;
     else if (bq >= lim) sg = one;
     else {
-        sg = d_lut_interp(c_sig_lut, 512, bq + lim, SPQ);
+        sg = d_lut_interp(tsg, 512, bq + lim, SPQ);
         sg = sg < 0 ? 0 : (sg > one ? one : sg);
     }
     int64_t bv = d_rshift_r(sg, SPQ - 16);
@@ -350,40 +368,54 @@ __device__ int blk_scalar(const int32_t *p, int32_t &eg, int32_t &beta)
 
 // one warp: site-12 head emit of a value head's D column outputs (o_acc on
 // per-column exponents e_o), the output rmsnorm, the z gate; writes the head's
-// po / pz / ep for site 13 (ref/gdn_emit_chain_vec.c)
+// po / pz / ep for site 13 (ref/gdn_emit_chain_vec.c).  pz_in, when given,
+// holds the head's gated z already (silu(zm) does not depend on the rest);
+// w.pmax / w.pmin, when set, receive the head's extreme products po * pz.
+// Only the msb of a maximum feeds a shift, so maxima are reduced as msb
+// positions (the msb of the largest value is the largest msb).
 template <int D>
 __device__ void blk_head_tail(int h, const int64_t *s_oacc, const int32_t *s_eo, const int16_t *zm, int z_e,
-                              const int16_t *wm, int w_e, const BlkWork &w, const int64_t *sig, const int64_t *rom)
+                              const int16_t *pz_in, const int16_t *wm, int w_e, const BlkWork &w,
+                              const int64_t *sig, const int64_t *rom)
 {
     constexpr int R = D / 32, LG = D == 32 ? 5 : (D == 64 ? 6 : 7);
     const int lane = threadIdx.x & 31;
     int emin = 1 << 30;
 #pragma unroll
     for (int r = 0; r < R; r++) emin = min(emin, s_eo[lane + 32 * r]);
-    emin = warp_min_i32(emin);
+    emin = __reduce_min_sync(BLK_FULL, emin);
     int64_t al[R];
-    uint64_t am = 0;
+    int mb = 0;
 #pragma unroll
     for (int r = 0; r < R; r++) {
         int shj = s_eo[lane + 32 * r] - emin;
         if (shj > 63) shj = 63;
         al[r] = g_floor_shr(s_oacc[lane + 32 * r], shj);
-        const uint64_t a = g_abs64(al[r]);
-        am = a > am ? a : am;
+        mb = max(mb, g_msb(g_abs64(al[r])));
     }
-    am = warp_max_u64(am);
-    int shh = g_msb(am) - 14;
+    mb = __reduce_max_sync(BLK_FULL, mb);
+    int shh = mb - 14;
     if (shh < 0) shh = 0;
     int32_t oh[R], po[R];
 #pragma unroll
     for (int r = 0; r < R; r++) oh[r] = g_sat16(g_round_shift(al[r], shh));
     int nsat;
     const int o_exp = fx_rmsnorm_warp<R>(oh, emin - shh, wm, w_e, LG, po, nsat, rom);
+    int pmx = INT32_MIN, pmn = INT32_MAX;
 #pragma unroll
     for (int r = 0; r < R; r++) {
         const int j = lane + 32 * r;
+        const int16_t pz = pz_in ? pz_in[j] : g_sat16(fx_silu(zm[h * D + j], z_e, sig));
         w.po[h * D + j] = (int16_t)po[r];
-        w.pz[h * D + j] = g_sat16(fx_silu(zm[h * D + j], z_e, sig));
+        w.pz[h * D + j] = pz;
+        const int32_t pr = po[r] * (int32_t)pz;
+        pmx = max(pmx, pr);
+        pmn = min(pmn, pr);
+    }
+    if (w.pmax) {
+        pmx = __reduce_max_sync(BLK_FULL, pmx);
+        pmn = __reduce_min_sync(BLK_FULL, pmn);
+        if (lane == 0) { w.pmax[h] = pmx; w.pmin[h] = pmn; }
     }
     if (lane == 0) w.ep[h] = o_exp + z_e;
 }
@@ -399,69 +431,92 @@ struct BlkHeadArgs {
     BlkWork w;
 };
 
-// One CTA per value head h, D*D/16 threads: the whole token for that head.
-//  1. The three conv segments' maxima (q, k, v; spec B 2.1.3).  One segment
-//     shares one requantiser shift, so every cluster reduces whole segments
-//     (at KH 16 / VH 32 / D 128, 8192 channels, 128 KB of taps from L2),
-//     each of its CTAs a slice, the partial maxima exchanged through
-//     distributed shared memory.
-//  2. One warp per task: q and k of key head h % KH (silu, L2 norm), v of head
-//     h (silu), the scalar path of head h; results in shared memory.
-//  3. The recurrence, stages 1-5 (state column j owned by D/16 lanes of 16
-//     keys each, ref/gdn_block_vec.c:304-380).
-//  4. Warp 0: the head tail (site-12 emit, rmsnorm_bf, z gate).
-// thread-block cluster helpers: the CTA's rank, the cluster's size, a 64-bit
-// load from the same shared-memory variable of CTA `rank`, and the split
-// cluster barrier.  A launch without a cluster attribute is a cluster of one.
+// thread-block cluster helpers: the CTA's rank, the cluster's size, loads from
+// the same shared-memory variable of CTA `rank`, and the split cluster
+// barrier.  A launch without a cluster attribute is a cluster of one.
 __device__ __forceinline__ unsigned blk_cl_rank()
 { unsigned r; asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r)); return r; }
 __device__ __forceinline__ unsigned blk_cl_size()
 { unsigned r; asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r)); return r; }
-__device__ __forceinline__ uint64_t blk_ld_cluster_u64(const void *p, unsigned rank)
+__device__ __forceinline__ unsigned blk_cl_addr(const void *p, unsigned rank)
 {
     const unsigned a = (unsigned)__cvta_generic_to_shared(p);
     unsigned ra;
-    uint64_t v;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
-    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(ra) : "memory");
+    return ra;
+}
+__device__ __forceinline__ int64_t blk_ld_cl_i64(const void *p, unsigned rank)
+{
+    int64_t v;
+    asm volatile("ld.shared::cluster.s64 %0, [%1];" : "=l"(v) : "r"(blk_cl_addr(p, rank)) : "memory");
+    return v;
+}
+__device__ __forceinline__ int blk_ld_cl_i32(const void *p, unsigned rank)
+{
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(blk_cl_addr(p, rank)) : "memory");
     return v;
 }
 __device__ __forceinline__ void blk_cl_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void blk_cl_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
-// conv + requantiser + silu of one head's D channels of segment s, R per lane
-// (element lane + 32 r), the channels starting at c0
-template <int R>
-__device__ __forceinline__ void blk_seg_head(const BlkHeadArgs &A, int s, size_t c0, int shs, int es,
-                                             const int64_t *sig, int32_t (&x)[R])
+// msb position of |x|, 0 for 0 and 1 (g_msb(g_abs64(x)) for 64-bit values)
+__device__ __forceinline__ int blk_msb_abs(int64_t x) { return g_msb(g_abs64(x)); }
+
+// the head kernel's shape for head dimension D: 32 value columns per CTA,
+// D/16 lanes per column (16 keys each), D/32 CTAs per value head
+template <int D>
+struct BlkShape {
+    static constexpr int LPC = D / 16, COLS = 32, SPH = D / COLS, NT = COLS * LPC, NW = NT / 32;
+    static constexpr int CPW = 32 / LPC, R = D / 32, LG = D == 32 ? 5 : (D == 64 ? 6 : 7);
+};
+
+// conv of channel c of the flattened [q | k | v] taps with segment s's tap
+// shifts (s selects among the three sets held in registers)
+__device__ __forceinline__ int64_t blk_conv_sel(const BlkHeadArgs &A, size_t c, int s, const int (&t0)[4],
+                                                const int (&t1)[4], const int (&t2)[4], int v0, int v1, int v2)
 {
-    int tsh[4], vm;
-    blk_taps(A.e_t[s], A.tvalid[s], tsh, vm);
-    const int lane = threadIdx.x & 31;
+    int ts[4];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        const size_t c = c0 + lane + 32 * r;
-        x[r] = fx_silu(g_sat16(g_round_shift(blk_conv_ch(A.xtap + 4 * c, A.wtap + 4 * c, vm, tsh), shs)), es, sig);
-    }
+    for (int k = 0; k < 4; k++) ts[k] = s == 0 ? t0[k] : (s == 1 ? t1[k] : t2[k]);
+    return blk_conv_ch(A.xtap + 4 * c, A.wtap + 4 * c, s == 0 ? v0 : (s == 1 ? v1 : v2), ts);
 }
 
+// D/32 CTAs per value head h (CTA part p holds columns 32p .. 32p+31), in
+// thread-block clusters of 2-8 CTAs that hold whole heads:
+//  1. The three conv segments' requantiser shifts (q, k, v; spec B 2.1.3).
+//     One segment shares one shift, so each cluster reduces whole segments
+//     (at KH 16 / VH 32 / D 128, 8192 channels, 128 KB of taps from L2), every
+//     CTA a slice; only the msb position of the largest |conv| matters, so
+//     that is what the CTAs reduce and exchange through distributed shared
+//     memory.  The raw conv of the channels this CTA needs itself (q and k of
+//     key head h % KH, v of its 32 columns) is kept in shared memory.
+//  2. One warp per task: q and k (silu, L2 norm), v (silu), the scalar path.
+//  3. The recurrence, stages 1-5, for the CTA's 32 columns (column j owned by
+//     D/16 lanes of 16 keys each, ref/gdn_block_vec.c:304-380).
+//  4. The head's first CTA gathers the D column results from the others and
+//     its warp 0 runs the head tail (site-12 emit, rmsnorm_bf, z gate).
 template <int D>
-__global__ void __launch_bounds__(D * D / 16)
+__global__ void __launch_bounds__(2 * D)
 gdn_blk_head_kernel(const BlkHeadArgs A)
 {
-    constexpr int NT = D * D / 16, NW = NT / 32, LPC = D / 16, CPW = 32 / LPC, R = D / 32;
-    constexpr int LG = D == 32 ? 5 : (D == 64 ? 6 : 7);
-    __shared__ int64_t s_sig[513], s_rom[64], s_oacc[D];
-    __shared__ __align__(16) uint4 s_st[2 * NT];    // the state slices, [half][thread]
+    using S = BlkShape<D>;
+    constexpr int NT = S::NT, NW = S::NW, LPC = S::LPC, SPH = S::SPH, CPW = S::CPW, R = S::R, LG = S::LG;
+    __shared__ int64_t s_sig[513], s_rom[64], s_raw[2 * D + 32], s_oacc[D], s_loacc[32];
+    __shared__ __align__(16) uint4 s_st[2 * NT];        // the state slices, [half][thread]
     __shared__ __align__(16) int16_t s_kn[D], s_qs[D];
-    __shared__ int32_t s_v[D], s_eo[D], s_sc[3], s_sh[3], s_es[3], s_errc;
-    __shared__ uint64_t s_red[3][NW], s_part[3];
-    const int h = blockIdx.x, hk = h % A.KH;
+    __shared__ int32_t s_eo[D], s_leo[32], s_v[32], s_red[3][NW], s_part[3];
+    __shared__ int32_t s_sc[3], s_sh[3], s_es[3], s_errc, s_lerr, s_gerr;
+    __shared__ int64_t s_lsp[257], s_lex[257], s_lsg[513];   // the scalar path's Q30 tables
+    __shared__ int16_t s_pz[D], s_zmv[D], s_wm[D];
+    __shared__ int32_t s_scv[8];
+    const int h = blockIdx.x / SPH, part = blockIdx.x % SPH, hk = h % A.KH;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = warp * CPW + lane / LPC;          // value column
-    const int i0 = 16 * (lane % LPC);               // key slice
+    const int jl = warp * CPW + lane / LPC;             // local value column
+    const int j = 32 * part + jl;                       // value column of the head
+    const int i0 = 16 * (lane % LPC);                   // key slice
 
-    // Before the wait: the constant tables and this head's state slice (an
+    // Before the wait: the constant tables and this CTA's state slice (an
     // asynchronous copy into shared memory).  A grid of this kernel starts only
     // once the launch before it has passed its own wait (the site-13 launch of
     // the previous token, or a later kernel), so the previous token's state
@@ -476,78 +531,130 @@ gdn_blk_head_kernel(const BlkHeadArgs A)
     }
     for (int i = threadIdx.x; i < 513; i += NT) s_sig[i] = d_sig_tab[i];
     for (int i = threadIdx.x; i < 64; i += NT) s_rom[i] = d_rsqrt_rom[i];
+    for (int i = threadIdx.x; i < 257; i += NT) { s_lsp[i] = d_sp_tab[i]; s_lex[i] = d_exp_tab[i]; }
+    for (int i = threadIdx.x; i < 513; i += NT) s_lsg[i] = d_sg_tab[i];
     const int se_j = A.semem[h * D + j];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // 1. segment maxima: the CTAs of a cluster split each segment's channels,
-    //    then every CTA reads the cluster's partial maxima from the others'
-    //    shared memory
-    const int QCH = A.KH * D;
+    // 1. segment shifts
+    const int QCH = A.KH * D, NCH = 2 * QCH + A.VH * D;
     const int crank = (int)blk_cl_rank(), csize = (int)blk_cl_size();
+    int t0[4], t1[4], t2[4], v0, v1, v2;
+    const int er0 = blk_taps(A.e_t[0], A.tvalid[0], t0, v0);
+    const int er1 = blk_taps(A.e_t[1], A.tvalid[1], t1, v1);
+    const int er2 = blk_taps(A.e_t[2], A.tvalid[2], t2, v2);
+    // the taps of this CTA's own channels (q / k of key head hk, v of its 32
+    // columns: 2D + 32 <= 2 NT of them) are loaded first, so their latency
+    // overlaps the segment loop's
+    auto own_ch = [&](int t, int &s) -> size_t {
+        s = t < D ? 0 : (t < 2 * D ? 1 : 2);
+        return s == 0 ? (size_t)hk * D + t
+             : (s == 1 ? (size_t)QCH + (size_t)hk * D + (t - D)
+                       : 2 * (size_t)QCH + (size_t)h * D + 32 * part + (t - 2 * D));
+    };
+    uint2 ox[2], ow[2];
 #pragma unroll
-    for (int s = 0; s < 3; s++) {
-        int tsh[4], vm;
-        blk_taps(A.e_t[s], A.tvalid[s], tsh, vm);
-        const int nch = s == 2 ? A.VH * D : QCH;
-        const int16_t *xs = A.xtap + (size_t)s * QCH * 4, *ws = A.wtap + (size_t)s * QCH * 4;
-        uint64_t m = 0;
-#pragma unroll 2
-        for (int c = crank * NT + threadIdx.x; c < nch; c += csize * NT) {
-            const uint64_t a = g_abs64(blk_conv_ch(xs + 4 * c, ws + 4 * c, vm, tsh));
-            m = a > m ? a : m;
+    for (int q = 0; q < 2; q++) {
+        const int t = threadIdx.x + q * NT;
+        int s;
+        if (t < 2 * D + 32) {
+            const size_t c = own_ch(t, s);
+            ox[q] = *reinterpret_cast<const uint2 *>(A.xtap + 4 * c);
+            ow[q] = *reinterpret_cast<const uint2 *>(A.wtap + 4 * c);
         }
-        m = warp_max_u64(m);
-        if (lane == 0) s_red[s][warp] = m;
     }
-    __syncthreads();
-    if (warp == 0) {
+    // this head's scalar inputs, z row and norm weights: loaded now, kept in
+    // shared memory by the end of the phase
+    int32_t pre = 0;
+    if (part == 0) pre = threadIdx.x < D ? A.zm[(size_t)h * D + threadIdx.x] : A.wm[threadIdx.x - D];
+    int32_t scp = threadIdx.x < 8 ? A.sc[(size_t)h * 8 + threadIdx.x] : 0;
+    int mb0 = 0, mb1 = 0, mb2 = 0;
+#pragma unroll 4
+    for (int c = crank * NT + threadIdx.x; c < NCH; c += csize * NT) {
+        const int s = c < QCH ? 0 : (c < 2 * QCH ? 1 : 2);
+        const int m = blk_msb_abs(blk_conv_sel(A, (size_t)c, s, t0, t1, t2, v0, v1, v2));
+        if (s == 0) mb0 = max(mb0, m);
+        else if (s == 1) mb1 = max(mb1, m);
+        else mb2 = max(mb2, m);
+    }
 #pragma unroll
-        for (int s = 0; s < 3; s++) {
-            const uint64_t m = warp_max_u64(lane < NW ? s_red[s][lane] : 0);
-            if (lane == 0) s_part[s] = m;
+    for (int q = 0; q < 2; q++) {
+        const int t = threadIdx.x + q * NT;
+        if (t < 2 * D + 32) {
+            int s;
+            own_ch(t, s);
+            int ts[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) ts[k] = s == 0 ? t0[k] : (s == 1 ? t1[k] : t2[k]);
+            s_raw[t] = blk_conv_ch(reinterpret_cast<const int16_t *>(&ox[q]), reinterpret_cast<const int16_t *>(&ow[q]),
+                                   s == 0 ? v0 : (s == 1 ? v1 : v2), ts);
         }
+    }
+    mb0 = __reduce_max_sync(BLK_FULL, mb0);
+    mb1 = __reduce_max_sync(BLK_FULL, mb1);
+    mb2 = __reduce_max_sync(BLK_FULL, mb2);
+    if (lane == 0) { s_red[0][warp] = mb0; s_red[1][warp] = mb1; s_red[2][warp] = mb2; }
+    if (part == 0) {
+        if (threadIdx.x < D) s_zmv[threadIdx.x] = (int16_t)pre;
+        else s_wm[threadIdx.x - D] = (int16_t)pre;
+    }
+    if (threadIdx.x < 8) s_scv[threadIdx.x] = scp;
+    __syncthreads();
+    if (threadIdx.x < 3) {
+        int m = 0;
+#pragma unroll
+        for (int w = 0; w < NW; w++) m = max(m, s_red[threadIdx.x][w]);
+        s_part[threadIdx.x] = m;
     }
     blk_cl_arrive();
     blk_cl_wait();
     if (warp == 0) {
-        int errc = 0;
-#pragma unroll
-        for (int s = 0; s < 3; s++) {
-            uint64_t m = lane < csize ? blk_ld_cluster_u64(&s_part[s], (unsigned)lane) : 0;
-            m = warp_max_u64(m);
-            int tsh[4], vm;
-            int x = g_msb(m) - 14;
-            x = x < 0 ? 0 : x;
-            const int e = blk_taps(A.e_t[s], A.tvalid[s], tsh, vm) + A.cw_exp[s] - x;
-            errc |= e > 127 || e < -128;
-            if (lane == 0) { s_sh[s] = x; s_es[s] = e; }
+        int m0 = 0, m1 = 0, m2 = 0;
+        if (lane < csize) {
+            m0 = blk_ld_cl_i32(&s_part[0], (unsigned)lane);
+            m1 = blk_ld_cl_i32(&s_part[1], (unsigned)lane);
+            m2 = blk_ld_cl_i32(&s_part[2], (unsigned)lane);
         }
-        if (lane == 0) s_errc = errc;
+        m0 = __reduce_max_sync(BLK_FULL, m0);
+        m1 = __reduce_max_sync(BLK_FULL, m1);
+        m2 = __reduce_max_sync(BLK_FULL, m2);
+        if (lane == 0) {
+            const int ms[3] = {m0, m1, m2}, er[3] = {er0, er1, er2};
+            int errc = 0;
+#pragma unroll
+            for (int s = 0; s < 3; s++) {
+                const int x = ms[s] - 14 < 0 ? 0 : ms[s] - 14;
+                const int e = er[s] + A.cw_exp[s] - x;
+                errc |= e > 127 || e < -128;
+                s_sh[s] = x;
+                s_es[s] = e;
+            }
+            s_errc = errc;
+        }
     }
-    // this CTA is done reading the others' partials; the matching wait is the
-    // kernel's last statement, so no CTA leaves while another may still read it
-    blk_cl_arrive();
     __syncthreads();
 
-    // 2. this head's inputs, one warp per task
-    for (int t = warp; t < 4; t += NW) {
-        int32_t x[R];
-        if (t == 0) {
-            blk_seg_head<R>(A, 0, (size_t)hk * D, s_sh[0], s_es[0], s_sig, x);
-            fx_l2norm_warp<R>(x, LG, true, s_qs, s_rom);
-        } else if (t == 1) {
-            blk_seg_head<R>(A, 1, (size_t)QCH + (size_t)hk * D, s_sh[1], s_es[1], s_sig, x);
-            fx_l2norm_warp<R>(x, LG, false, s_kn, s_rom);
-        } else if (t == 2) {
-            blk_seg_head<R>(A, 2, 2 * (size_t)QCH + (size_t)h * D, s_sh[2], s_es[2], s_sig, x);
+    // 2. this CTA's inputs, one warp per task: q, k, v, the scalar path, and
+    //    in the head's first CTA the z gate for the head tail
+    for (int t = warp; t < 5; t += NW) {
+        if (t < 2) {
+            int32_t x[R];
 #pragma unroll
-            for (int r = 0; r < R; r++) s_v[lane + 32 * r] = x[r];
-        } else if (lane == 0) {
-            int32_t eg, bt;
-            s_sc[2] = blk_scalar(A.sc + (size_t)h * 8, eg, bt);
-            s_sc[0] = eg;
-            s_sc[1] = bt;
+            for (int r = 0; r < R; r++)
+                x[r] = fx_silu(g_sat16(g_round_shift(s_raw[t * D + lane + 32 * r], s_sh[t])), s_es[t], s_sig);
+            fx_l2norm_warp<R>(x, LG, t == 0, t == 0 ? s_qs : s_kn, s_rom);
+        } else if (t == 2) {
+            s_v[lane] = fx_silu(g_sat16(g_round_shift(s_raw[2 * D + lane], s_sh[2])), s_es[2], s_sig);
+        } else if (t == 3) {
+            if (lane == 0) {
+                int32_t eg, bt;
+                s_sc[2] = blk_scalar(s_scv, eg, bt, s_lsp, s_lex, s_lsg);
+                s_sc[0] = eg;
+                s_sc[1] = bt;
+            }
+        } else if (part == 0) {
+            for (int i = lane; i < D; i += 32) s_pz[i] = g_sat16(fx_silu(s_zmv[i], A.z_e, s_sig));
         }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -561,7 +668,7 @@ gdn_blk_head_kernel(const BlkHeadArgs A)
     }
     ld16_i16(s_kn + i0, kn);
     ld16_i16(s_qs + i0, qs);
-    const int32_t v_j = s_v[j];
+    const int32_t v_j = s_v[jl];
     const int egh = s_sc[0], bth = s_sc[1], tk0 = A.tk0, e_v = s_es[2];
     int32_t w18[16];
     int64_t sk = 0;
@@ -635,16 +742,37 @@ gdn_blk_head_kernel(const BlkHeadArgs A)
     int err = 0;
     if (lane % LPC == 0) {
         A.semem[h * D + j] = se_new;
-        s_oacc[j] = od;
-        s_eo[j] = e_o;
+        s_loacc[jl] = od;
+        s_leo[jl] = e_o;
         err = se_new > 127 || se_new < -128 || e_o > 127 || e_o < -128;
     }
     err = __syncthreads_or(err);
+    if (threadIdx.x == 0) s_lerr = err;
 
-    // 4. the head tail
-    if (warp == 0) {
-        blk_head_tail<D>(h, s_oacc, s_eo, A.zm, A.z_e, A.wm, A.w_e, A.w, s_sig, s_rom);
-        if (lane == 0) A.w.err[h] = (s_errc ? 1 : 0) | (s_sc[2] ? 2 : 0) | (err ? 4 : 0);
+    // 4. the head's first CTA gathers its D columns (CTA part p of the head is
+    //    cluster rank crank + p), then runs the head tail; the others wait at
+    //    the end until it has read their shared memory
+    blk_cl_arrive();
+    blk_cl_wait();
+    if (part == 0) {
+        for (int t = threadIdx.x; t < D; t += NT) {
+            s_oacc[t] = blk_ld_cl_i64(&s_loacc[t & 31], (unsigned)(crank + (t >> 5)));
+            s_eo[t] = blk_ld_cl_i32(&s_leo[t & 31], (unsigned)(crank + (t >> 5)));
+        }
+        if (threadIdx.x == 0) {
+            int e = 0;
+#pragma unroll
+            for (int p = 0; p < SPH; p++) e |= blk_ld_cl_i32(&s_lerr, (unsigned)(crank + p));
+            s_gerr = e;
+        }
+    }
+    blk_cl_arrive();
+    if (part == 0) {
+        __syncthreads();
+        if (warp == 0) {
+            blk_head_tail<D>(h, s_oacc, s_eo, A.zm, A.z_e, s_pz, s_wm, A.w_e, A.w, s_sig, s_rom);
+            if (lane == 0) A.w.err[h] = (s_errc ? 1 : 0) | (s_sc[2] ? 2 : 0) | (s_gerr ? 4 : 0);
+        }
     }
     blk_cl_wait();
 }
@@ -668,7 +796,7 @@ gdn_blk_chain_kernel(const BlkChainArgs A)
     const int h = blockIdx.x, lane = threadIdx.x;
     for (int j = lane; j < D; j += 32) { s_oacc[j] = A.o_acc[h * D + j]; s_eo[j] = A.e_o[h * D + j]; }
     __syncwarp();
-    blk_head_tail<D>(h, s_oacc, s_eo, A.zm, A.z_e, A.wm, A.w_e, A.w, d_sig_tab, d_rsqrt_rom);
+    blk_head_tail<D>(h, s_oacc, s_eo, A.zm, A.z_e, nullptr, A.wm, A.w_e, A.w, d_sig_tab, d_rsqrt_rom);
 }
 
 struct BlkTailArgs {
@@ -688,68 +816,196 @@ __device__ __forceinline__ int32_t blk_site13_term(const BlkTailArgs &A, int i, 
     return blk_floor_shr32((int32_t)A.po[i] * A.pz[i], s > 63 ? 63 : s);
 }
 
-// site 13 (ref/gdn_block_vec.c:396-418): one CTA over all VH*D products, the
-// first 8192 of them kept in registers between the two passes
-__global__ void __launch_bounds__(1024)
+__device__ __forceinline__ int blk_msb_abs32(int32_t v)
+{
+    const uint32_t a = v < 0 ? 0u - (uint32_t)v : (uint32_t)v;
+    return a ? 31 - __clz((int)a) : 0;
+}
+
+// site 13 (ref/gdn_block_vec.c:396-418) over all VH*D products on their own
+// (the unit entry gdn_y_emit_dev, no head records), split over the CTAs of
+// one cluster (BLK_TAIL_NT threads each; a launch without a
+// cluster is one CTA): each CTA takes a contiguous slice, the msb of the
+// largest aligned product is exchanged through distributed shared memory,
+// and cluster rank 0 writes the status word.
+#define BLK_TAIL_NT 256
+__global__ void __launch_bounds__(BLK_TAIL_NT)
 gdn_blk_tail_kernel(const BlkTailArgs A)
 {
-    constexpr int KR = 8;
-    __shared__ uint64_t red[32];
-    __shared__ int32_t s_ey, s_err;
+    constexpr int KR = 8, NW = BLK_TAIL_NT / 32;
+    __shared__ int32_t s_red[NW], s_ey, s_err, s_part, s_sat;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (threadIdx.x < 32) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int crank = (int)blk_cl_rank(), csize = (int)blk_cl_size();
+    if (warp == 0) {
         int m = 0x7FFFFFFF, er = 0;
-        for (int h = threadIdx.x; h < A.VH; h += 32) {
+        for (int h = lane; h < A.VH; h += 32) {
             m = min(m, A.ep[h]);
             if (A.err) er |= A.err[h];
         }
-        m = warp_min_i32(m);
+        m = __reduce_min_sync(BLK_FULL, m);
         er = (int)__reduce_or_sync(BLK_FULL, (unsigned)er);
-        if (threadIdx.x == 0) { s_ey = m; s_err = er; }
+        if (lane == 0) { s_ey = m; s_err = er; }
     }
     __syncthreads();
-    const int e_y = s_ey, n = A.VH * A.D, nt = blockDim.x;
+    const int e_y = s_ey, n = A.VH * A.D;
+    const int chunk = (n + csize - 1) / csize, lo = crank * chunk, hi = min(n, lo + chunk);
     int32_t pv[KR];
-    uint32_t am = 0;
+    int mb = 0;
 #pragma unroll
     for (int k = 0; k < KR; k++) {
-        const int i = threadIdx.x + nt * k;
-        pv[k] = i < n ? blk_site13_term(A, i, e_y) : 0;
-        am = max(am, pv[k] < 0 ? 0u - (uint32_t)pv[k] : (uint32_t)pv[k]);
+        const int i = lo + threadIdx.x + BLK_TAIL_NT * k;
+        pv[k] = i < hi ? blk_site13_term(A, i, e_y) : 0;
+        mb = max(mb, blk_msb_abs32(pv[k]));
     }
-    for (int i = threadIdx.x + nt * KR; i < n; i += nt) {
-        const int32_t v = blk_site13_term(A, i, e_y);
-        am = max(am, v < 0 ? 0u - (uint32_t)v : (uint32_t)v);
+    for (int i = lo + threadIdx.x + BLK_TAIL_NT * KR; i < hi; i += BLK_TAIL_NT)
+        mb = max(mb, blk_msb_abs32(blk_site13_term(A, i, e_y)));
+    mb = __reduce_max_sync(BLK_FULL, mb);
+    if (lane == 0) s_red[warp] = mb;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int m = 0;
+#pragma unroll
+        for (int w = 0; w < NW; w++) m = max(m, s_red[w]);
+        s_part = m;
     }
-    am = (uint32_t)cta_max_u64(am, red);
-    int sh = g_msb(am) - 14;
+    blk_cl_arrive();
+    blk_cl_wait();
+    if (warp == 0) {
+        int m = lane < csize ? blk_ld_cl_i32(&s_part, (unsigned)lane) : 0;
+        m = __reduce_max_sync(BLK_FULL, m);
+        if (lane == 0) s_red[0] = m;                  // the cluster-wide msb, for this CTA's threads
+    }
+    __syncthreads();
+    int sh = s_red[0] - 14;
     if (sh < 0) sh = 0;
     const int32_t rq = sh ? 1 << (sh - 1) : 0;
     int sat = 0;
 #pragma unroll
     for (int k = 0; k < KR; k++) {
-        const int i = threadIdx.x + nt * k;
-        if (i < n) {
+        const int i = lo + threadIdx.x + BLK_TAIL_NT * k;
+        if (i < hi) {
             const int32_t v = (pv[k] + rq) >> sh;
             sat |= v > 32767 || v < -32768;
             A.y[i] = g_sat16(v);
         }
     }
-    for (int i = threadIdx.x + nt * KR; i < n; i += nt) {
+    for (int i = lo + threadIdx.x + BLK_TAIL_NT * KR; i < hi; i += BLK_TAIL_NT) {
         const int32_t v = (blk_site13_term(A, i, e_y) + rq) >> sh;
         sat |= v > 32767 || v < -32768;
         A.y[i] = g_sat16(v);
     }
     sat = __syncthreads_or(sat);
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0) s_sat = sat != 0;
+    blk_cl_arrive();
+    blk_cl_wait();
+    if (crank == 0 && threadIdx.x == 0) {
+        int st = 0;
+        for (int r = 0; r < csize; r++) st |= blk_ld_cl_i32(&s_sat, (unsigned)r);
         A.status[0] = e_y - sh;
-        A.status[4] = sat != 0;
+        A.status[4] = st;
         if (A.err) {
             A.status[1] = s_err & 1;
             A.status[2] = s_err >> 1 & 1;
             A.status[3] = s_err >> 2 & 1;
         }
+    }
+    blk_cl_arrive();
+    blk_cl_wait();
+}
+
+// site 13 of deltanet_step (ref/gdn_block_vec.c:396-418) from the heads'
+// records: the token exponent e_y (the smallest head exponent), the shift
+// (the msb of the largest aligned product) and the saturation flag all follow
+// from each head's exponent and extreme products, because the floor shift and
+// the rounding shift are monotone: the extremes of the aligned products are
+// the aligned extremes.  So no CTA waits for another: each of the
+// ceil(VH*D / 1024) CTAs reduces the VH records itself (one warp) while its
+// threads load their four products.
+#define BLK_S13_NT 256
+#define BLK_S13_PER 4
+struct BlkSite13Args {
+    int32_t VH, D;
+    const int16_t *po, *pz;
+    const int32_t *ep, *pmax, *pmin, *err;
+    int16_t *y;
+    int32_t *status;                   // [5] y_exp, err_conv, err_g, err_se, y_sat
+};
+
+__global__ void __launch_bounds__(BLK_S13_NT)
+gdn_blk_site13_kernel(const BlkSite13Args A)
+{
+    __shared__ int32_t s_ey, s_sh, s_sat, s_err;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n = A.VH * A.D;
+    const int base = blockIdx.x * BLK_S13_NT * BLK_S13_PER + threadIdx.x;
+    int32_t p[BLK_S13_PER], eh[BLK_S13_PER];
+#pragma unroll
+    for (int k = 0; k < BLK_S13_PER; k++) {
+        const int i = base + BLK_S13_NT * k;
+        p[k] = i < n ? (int32_t)A.po[i] * A.pz[i] : 0;
+        eh[k] = i < n ? A.ep[i / A.D] : 0;
+    }
+    if (warp == 0) {
+        // the first 128 head records in one round of loads, the rest (if any)
+        // read again after the minimum
+        constexpr int HP = 4;
+        int eh_[HP], mx_[HP], mn_[HP], m = 0x7FFFFFFF, er = 0;
+#pragma unroll
+        for (int k = 0; k < HP; k++) {
+            const int h = lane + 32 * k;
+            const bool ok = h < A.VH;
+            eh_[k] = ok ? A.ep[h] : 0x7FFFFFFF;
+            mx_[k] = ok ? A.pmax[h] : INT32_MIN;
+            mn_[k] = ok ? A.pmin[h] : INT32_MAX;
+            er |= ok ? A.err[h] : 0;
+            m = min(m, eh_[k]);
+        }
+        for (int h = lane + 32 * HP; h < A.VH; h += 32) { m = min(m, A.ep[h]); er |= A.err[h]; }
+        m = __reduce_min_sync(BLK_FULL, m);
+        er = (int)__reduce_or_sync(BLK_FULL, (unsigned)er);
+        int hi = INT32_MIN, lo = INT32_MAX;
+#pragma unroll
+        for (int k = 0; k < HP; k++) {
+            if (lane + 32 * k < A.VH) {
+                const int s = min(eh_[k] - m, 63);
+                hi = max(hi, blk_floor_shr32(mx_[k], s));
+                lo = min(lo, blk_floor_shr32(mn_[k], s));
+            }
+        }
+        for (int h = lane + 32 * HP; h < A.VH; h += 32) {
+            const int s = min(A.ep[h] - m, 63);
+            hi = max(hi, blk_floor_shr32(A.pmax[h], s));
+            lo = min(lo, blk_floor_shr32(A.pmin[h], s));
+        }
+        hi = __reduce_max_sync(BLK_FULL, hi);
+        lo = __reduce_min_sync(BLK_FULL, lo);
+        int sh = max(blk_msb_abs32(hi), blk_msb_abs32(lo)) - 14;
+        if (sh < 0) sh = 0;
+        const int32_t rq = sh ? 1 << (sh - 1) : 0;
+        if (lane == 0) {
+            s_ey = m;
+            s_sh = sh;
+            s_sat = ((hi + rq) >> sh) > 32767 || ((lo + rq) >> sh) < -32768;
+            s_err = er;
+        }
+    }
+    __syncthreads();
+    const int e_y = s_ey, sh = s_sh;
+    const int32_t rq = sh ? 1 << (sh - 1) : 0;
+#pragma unroll
+    for (int k = 0; k < BLK_S13_PER; k++) {
+        const int i = base + BLK_S13_NT * k;
+        if (i < n) A.y[i] = g_sat16((blk_floor_shr32(p[k], min(eh[k] - e_y, 63)) + rq) >> sh);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        A.status[0] = e_y - sh;
+        A.status[1] = s_err & 1;
+        A.status[2] = s_err >> 1 & 1;
+        A.status[3] = s_err >> 2 & 1;
+        A.status[4] = s_sat;
     }
 }
 
@@ -847,38 +1103,42 @@ static cudaError_t blk_launch(const void *fn, dim3 grid, dim3 block, cudaStream_
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-// cluster size of the head kernel: the largest of 8, 4, 2 that divides VH and
-// that the device can co-schedule for this kernel (asked once per kernel)
-static int blk_head_cluster(const void *fn, int VH, int nt)
+// the largest cluster of 8, 4 or 2 CTAs (else 1) of `nt` threads that the
+// device can co-schedule for kernel fn, asked once per kernel
+static int blk_cluster_max(const void *fn, int nt)
 {
-    static const void *seen[3] = {nullptr, nullptr, nullptr};
-    static int best[3] = {1, 1, 1};
+    static const void *seen[8] = {};
+    static int best[8] = {};
     int slot = 0;
-    while (slot < 3 && seen[slot] && seen[slot] != fn) slot++;
-    if (slot == 3) slot = 0;
-    if (seen[slot] != fn) {
-        int c = 8;
-        for (; c > 1; c >>= 1) {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(c);
-            cfg.blockDim = dim3(nt);
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = (unsigned)c;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n >= 1) break;
-            cudaGetLastError();
-        }
-        best[slot] = c;
-        seen[slot] = fn;
+    while (slot < 8 && seen[slot] && seen[slot] != fn) slot++;
+    if (slot < 8 && seen[slot] == fn) return best[slot];
+    int c = 8;
+    for (; c > 1; c >>= 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c);
+        cfg.blockDim = dim3(nt);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)c;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n >= 1) break;
+        cudaGetLastError();
     }
-    int c = best[slot];
-    while (c > 1 && VH % c) c >>= 1;
+    if (slot < 8) { best[slot] = c; seen[slot] = fn; }
     return c;
+}
+
+// the head kernel's cluster: whole heads (a multiple of the CTAs per head
+// sph), dividing the grid; 0 when the device cannot co-schedule one head
+static int blk_head_cluster(const void *fn, int nt, int grid, int sph)
+{
+    int c = blk_cluster_max(fn, nt);
+    while (c > sph && grid % c) c >>= 1;
+    return c >= sph && grid % c == 0 ? c : 0;
 }
 
 static bool blk_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
@@ -921,13 +1181,17 @@ extern "C" int deltanet_step(const deltanet_args *a, void *stream)
     void *ha[] = {&H};
     const void *hk = D == 32 ? (const void *)gdn_blk_head_kernel<32>
                    : (D == 64 ? (const void *)gdn_blk_head_kernel<64> : (const void *)gdn_blk_head_kernel<128>);
-    e = blk_launch(hk, dim3(VH), dim3(D * D / 16), st, a->pdl != 0, ha, blk_head_cluster(hk, VH, D * D / 16));
+    const int sph = D / 32, grid = VH * sph, hcl = blk_head_cluster(hk, 2 * D, grid, sph);
+    if (!hcl) return gdn_fail(cudaErrorInvalidClusterSize);
+    e = blk_launch(hk, dim3(grid), dim3(2 * D), st, a->pdl != 0, ha, hcl);
     if (e != cudaSuccess) return gdn_fail(e);
 
-    BlkTailArgs T;
-    T.VH = VH; T.D = D; T.po = w.po; T.pz = w.pz; T.ep = w.ep; T.y = a->y; T.status = a->status; T.err = w.err;
+    BlkSite13Args T;
+    T.VH = VH; T.D = D; T.po = w.po; T.pz = w.pz; T.ep = w.ep; T.pmax = w.pmax; T.pmin = w.pmin; T.err = w.err;
+    T.y = a->y; T.status = a->status;
     void *ta[] = {&T};
-    e = blk_launch((const void *)gdn_blk_tail_kernel, dim3(1), dim3(1024), st, true, ta);
+    const int n13 = (VH * D + BLK_S13_NT * BLK_S13_PER - 1) / (BLK_S13_NT * BLK_S13_PER);
+    e = blk_launch((const void *)gdn_blk_site13_kernel, dim3(n13), dim3(BLK_S13_NT), st, true, ta);
     return e == cudaSuccess ? 0 : gdn_fail(e);
 }
 
@@ -1045,8 +1309,9 @@ extern "C" int gdn_y_emit_dev(int H, int D, const int32_t *ep, const int16_t *po
     BlkTailArgs T = {};
     T.VH = H; T.D = D; T.po = po; T.pz = pz; T.ep = ep; T.y = y; T.status = status;
     void *ta[] = {&T};
-    cudaError_t e = blk_launch((const void *)gdn_blk_tail_kernel, dim3(1), dim3(1024),
-                               reinterpret_cast<cudaStream_t>(stream), false, ta);
+    const int tcl = blk_cluster_max((const void *)gdn_blk_tail_kernel, BLK_TAIL_NT);
+    cudaError_t e = blk_launch((const void *)gdn_blk_tail_kernel, dim3(tcl), dim3(BLK_TAIL_NT),
+                               reinterpret_cast<cudaStream_t>(stream), false, ta, tcl);
     return e == cudaSuccess ? 0 : gdn_fail(e);
 }
 
