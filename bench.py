@@ -505,9 +505,9 @@ def run_block(pkg, L, torch, dev, stream, sp, timed, nrep):
             "us_per_token": round(us, 3), "bytes_per_token": BLK_BYTES,
             "GBps": round(BLK_BYTES / (us * 1e-6) / 1e9, 1),
             "frac_hbm": round(BLK_BYTES / (us * 1e-6) / 1e9 / peak, 4),
-            "how": "3 launches per token (front, per-head recurrence + emit, site-13 tail), 64 tokens per "
-                   "CUDA graph", "kernels": ["gdn_blk_front_kernel", "gdn_blk_rec_kernel<128>",
-                                            "gdn_blk_tail_kernel"]}
+            "how": "2 launches per token (head kernel: D/32 CTAs per value head in clusters; site-13 kernel "
+                   "from the head records), 64 tokens per CUDA graph",
+            "kernels": ["gdn_blk_head_kernel<128>", "gdn_blk_site13_kernel"]}
 
 
 # ------------------------------------------------------------ decode (configs 3, 4)
