@@ -139,6 +139,21 @@ __device__ __forceinline__ void dec_attn_cta(const dec_attn_args &A, int c, int 
     __half *vs = ks + ch * ATT_KS;                                  // [ch][128]
     float *kb = reinterpret_cast<float *>(vs + ch * ATT_HD);        // [128] scratch for the new k
 
+    // the chunk's cached k and v rows: 16-byte asynchronous copies, all in
+    // flight while q is built (the current position's row is replaced below)
+    {
+        const uint32_t kb0 = (uint32_t)__cvta_generic_to_shared(ks), vb0 = (uint32_t)__cvta_generic_to_shared(vs);
+        for (int i = tid; i < n * 32; i += nthr) {
+            const int r = i >> 5, piece = i & 15;
+            const size_t off = ((size_t)(p0 + r) * kvh + g) * ATT_HD + 8 * piece;
+            if (i & 16)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                             :: "r"(vb0 + (uint32_t)(2 * (r * ATT_HD + 8 * piece))), "l"(vcache + off) : "memory");
+            else
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                             :: "r"(kb0 + (uint32_t)(2 * (r * ATT_KS + 8 * piece))), "l"(kcache + off) : "memory");
+        }
+    }
     // q of head h
     if (qw_on) {
         float q[4];
@@ -149,14 +164,7 @@ __device__ __forceinline__ void dec_attn_cta(const dec_attn_args &A, int c, int 
         if (c == 0 && q_seam)
             reinterpret_cast<float4 *>(q_seam + (size_t)h * ATT_HD)[lane] = make_float4(q[0], q[1], q[2], q[3]);
     }
-    // the chunk's cached k and v rows (16-byte pieces; the current position's
-    // row is replaced below)
-    for (int i = tid; i < n * 32; i += nthr) {
-        const int r = i >> 5, piece = i & 15;
-        const size_t off = ((size_t)(p0 + r) * kvh + g) * ATT_HD + 8 * piece;
-        if (i & 16) *reinterpret_cast<uint4 *>(vs + r * ATT_HD + 8 * piece) = *reinterpret_cast<const uint4 *>(vcache + off);
-        else *reinterpret_cast<uint4 *>(ks + r * ATT_KS + 8 * piece) = *reinterpret_cast<const uint4 *>(kcache + off);
-    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     // the current position: new k and v of kv head g
     if (warp == 0 && pos >= p0 && pos < p0 + n) {
@@ -236,11 +244,12 @@ __global__ void __launch_bounds__(1024, 1) dec_attn_kernel(const dec_attn_args A
 
 // Flash-decoding, part 2: combine the chunks of each q head, apply the
 // sigmoid output gate (the raw projection, ref/run9b.c:871-872), to fp16.
-// One CTA of 128 threads per q head: chunk weights exp(m_c - M) in shared
-// memory, then thread d sums dimension d over the chunks.
-// Piece (q head h, sequence b) of the combine by 128 threads (t < 128), with
-// its own wc[1024] / red[32] scratch; every thread reaches the same barriers.
-__device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc, float *red)
+// Piece (q head h, sequence b) by 128 threads (t < 128) with its own scratch
+// wc (at least 8 + 4 * 128 floats): warp w takes chunks w, w + 4, ..., eight
+// records' loads in flight at a time (lane l holds dims 4l..4l+3), with its
+// own running maximum (the online-softmax rescale); then the four warps meet
+// in shared memory.  Every thread reaches the same barriers.
+__device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc)
 {
     const int hd = ATT_HD, nchunks = A.nchunks, ch = A.ch, qh = A.qh, gate_stride = 2 * ATT_HD;
     const float *part = A.part, *gate = A.qg + ATT_HD;           // the gate: second half of each q|gate row
@@ -252,38 +261,58 @@ __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int
     }
     const int used = min(nchunks, (*A.d_pos + 1 + ch - 1) / ch);
     const float *ph = part + (size_t)h * nchunks * (hd + 4);
-    float M = -INFINITY;
-    for (int c = t; c < used; c += 128) M = fmaxf(M, ph[(size_t)c * (hd + 4)]);
+    const int w = t >> 5, lane = t & 31;
+    float M = -INFINITY, L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int c0 = w; c0 < used; c0 += 32) {
+        float2 ml[8];
+        float4 o[8];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if ((t & 31) == 0) red[t >> 5] = M;
-    __syncthreads();
-    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    float L = 0.f;
-    for (int c = t; c < used; c += 128) {
-        const float w = expf(ph[(size_t)c * (hd + 4)] - M);
-        wc[c] = w;
-        L += ph[(size_t)c * (hd + 4) + 1] * w;
+        for (int k = 0; k < 8; k++) {
+            const int c = c0 + 4 * k;
+            if (c < used) {
+                const float *rec = ph + (size_t)c * (hd + 4);
+                ml[k] = *reinterpret_cast<const float2 *>(rec);
+                o[k] = reinterpret_cast<const float4 *>(rec + 4)[lane];
+            } else {
+                ml[k] = make_float2(-INFINITY, 0.f);
+                o[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        float Mn = M;
+#pragma unroll
+        for (int k = 0; k < 8; k++) Mn = fmaxf(Mn, ml[k].x);
+        const float ro = M == -INFINITY ? 0.f : expf(M - Mn);
+        L *= ro; a0 *= ro; a1 *= ro; a2 *= ro; a3 *= ro;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float f = ml[k].x == -INFINITY ? 0.f : expf(ml[k].x - Mn);
+            L = fmaf(ml[k].y, f, L);
+            a0 = fmaf(o[k].x, f, a0); a1 = fmaf(o[k].y, f, a1); a2 = fmaf(o[k].z, f, a2); a3 = fmaf(o[k].w, f, a3);
+        }
+        M = Mn;
     }
+    float *mw = wc, *lw = wc + 4, *aw = wc + 8;                // [4], [4], [4][128]
+    if (lane == 0) { mw[w] = M; lw[w] = L; }
+    reinterpret_cast<float4 *>(aw + w * hd)[lane] = make_float4(a0, a1, a2, a3);
+    __syncthreads();
+    const float Mx = fmaxf(fmaxf(mw[0], mw[1]), fmaxf(mw[2], mw[3]));   // finite: chunk 0 is in use
+    float tot = 0.f, a = 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    __syncthreads();
-    if ((t & 31) == 0) red[8 + (t >> 5)] = L;
-    __syncthreads();
-    L = red[8] + red[9] + red[10] + red[11];
-    float a = 0.f;
-#pragma unroll 8
-    for (int c = 0; c < used; c++) a = fmaf(wc[c], ph[(size_t)c * (hd + 4) + 4 + t], a);
+    for (int i = 0; i < 4; i++) {
+        const float f = mw[i] == -INFINITY ? 0.f : expf(mw[i] - Mx);
+        tot = fmaf(lw[i], f, tot);
+        a = fmaf(aw[i * hd + t], f, a);
+    }
     const float gv = gate[(size_t)h * gate_stride + t];
-    y[(size_t)h * hd + t] = __half_as_ushort(__float2half_rn(a / L * sigm_f(gv)));
+    y[(size_t)h * hd + t] = __half_as_ushort(__float2half_rn(a / tot * sigm_f(gv)));
+    __syncthreads();                                       // the scratch may be reused
 }
 
 __global__ void __launch_bounds__(128) dec_attn_combine_kernel(const dec_attn_args A)
 {
-    __shared__ float wc[1024];
-    __shared__ float red[32];
+    __shared__ float wc[8 + 4 * ATT_HD];
     PDL_ENTER();
-    dec_attn_combine_cta(A, blockIdx.x, blockIdx.y, threadIdx.x, wc, red);
+    dec_attn_combine_cta(A, blockIdx.x, blockIdx.y, threadIdx.x, wc);
 }
 
 __global__ void dec_add_kernel(float *x, const float *t, int n)
@@ -411,7 +440,7 @@ int dec_attn_prepare(dec_attn_args *A)
     if (A->kvh <= 0 || A->qh % A->kvh || A->qh / A->kvh > 32 || A->ch <= 0 || A->ch > 64 || (A->n_rot & 1)
         || A->n_rot > ATT_HD || A->nseq < 1 || A->nseq > 64) return -11;
     A->nchunks = (A->max_ctx + A->ch - 1) / A->ch;
-    if (A->nchunks > 1024) return -11;                // the combine's weight table
+    if (A->nchunks > 1024) return -11;                // at most 65536 positions of 64
     return 0;
 }
 
