@@ -336,7 +336,9 @@ __device__ __forceinline__ void dec_advance_cta(unsigned long long *keys, int n,
     if (b < nseq) {
         unsigned long long best = 0;
         for (int i = 0; i < n; i++) best = keys[i * nseq + b] > best ? keys[i * nseq + b] : best;
-        const int32_t t = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
+        // a step whose LM head left no key (0) continues from token 0: the
+        // next embedding gather never indexes outside the table
+        const int32_t t = best ? (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull)) : 0;
         if (p < max_ctx) history[(size_t)b * max_ctx + p] = t;
         const int plen = prompt ? prompt[0] : 0;
         tok[b] = (p + 1 < plen) ? prompt[1 + (size_t)b * plen + p + 1] : t;
@@ -597,7 +599,7 @@ __global__ void dec_advance_p2p_kernel(const __grid_constant__ PeerRegion R, int
         best = k > best ? k : best;
     }
     *epoch = E;
-    const int32_t tk = (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull));
+    const int32_t tk = best ? (int32_t)(0xFFFFFFFFull - (best & 0xFFFFFFFFull)) : 0;   // no key: token 0
     const int p = *pos;
     if (p < max_ctx) history[p] = tk;
     const int plen = prompt ? prompt[0] : 0;

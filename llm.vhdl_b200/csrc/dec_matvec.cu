@@ -27,8 +27,11 @@
 
 extern "C" int mv4i_g_cuda_err;
 
-#define DMV_THREADS 256
+#define DMV_THREADS 256            // CTA of the persistent decode kernel and the staging launch
 #define DMV_WARPS 8
+#define DMV_WIDE_K 4096            // a single-sequence launch with K at least this runs one CTA
+                                   // of 16 warps per SM (the staging split over twice the
+                                   // threads), shorter ones two CTAs of 8 warps
 #define DMV_G 4                    // rows a warp streams together (2 gate/up pairs)
 #ifndef DMV_MINB
 #define DMV_MINB 2                 // resident CTAs per SM the registers are sized for
@@ -154,18 +157,21 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, const void *xv, c
 }
 
 // 1 / rms of vectors b0 .. b0+NB-1 (those below P.nvec) into invs[0..NB-1]
-// (RMSNorm prologue only); every thread of the CTA calls it
-template <int NB>
+// (RMSNorm prologue only); every thread of the CTA calls it.  The sums of
+// squares run over the first 256 threads whatever the CTA's size, so the
+// statistic (and every result after it) is the same bit for bit in 8- and
+// 16-warp CTAs and in the staging launch.
+template <int NB, int NW>
 __device__ __forceinline__ void dmv_norms(const dmv_params &P, int b0, float *invs)
 {
-    __shared__ float red[DMV_WARPS * 8];
+    __shared__ float red[NW * 8];
     const int K = P.K, tid = threadIdx.x, nv = P.nvec;
     float a[NB];
 #pragma unroll
     for (int i = 0; i < NB; i++) {
         const int b = b0 + i;
         a[i] = 0.f;
-        if (b < nv) {
+        if (b < nv && tid < DMV_THREADS) {
             const float *x = static_cast<const float *>(P.x) + (size_t)b * P.xs;
             for (int c = 4 * tid; c < K; c += 4 * DMV_THREADS) {
                 const float4 v = *reinterpret_cast<const float4 *>(x + c);
@@ -175,13 +181,13 @@ __device__ __forceinline__ void dmv_norms(const dmv_params &P, int b0, float *in
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) a[i] += __shfl_xor_sync(0xffffffffu, a[i], o);
-        if ((tid & 31) == 0) red[i * DMV_WARPS + (tid >> 5)] = a[i];
+        if ((tid & 31) == 0) red[i * NW + (tid >> 5)] = a[i];
     }
     __syncthreads();
     if (tid < NB) {
         float t = 0.f;
 #pragma unroll
-        for (int w = 0; w < DMV_WARPS; w++) t += red[tid * DMV_WARPS + w];
+        for (int w = 0; w < NW; w++) t += red[tid * NW + w];
         invs[tid] = rsqrtf(t / (float)K + P.eps);
     }
     __syncthreads();
@@ -193,6 +199,7 @@ __device__ __forceinline__ void dmv_norms(const dmv_params &P, int b0, float *in
 // 64-column pair 8 lanes: group max, pair sums and per-head norms are
 // shuffle reductions.  u_lo and u_hi are multiples of 16; every thread of
 // the CTA calls it.
+template <int NW>
 __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float inv, uint8_t *dst, int u_lo,
                                               int u_hi, bool seam_cta)
 {
@@ -203,7 +210,7 @@ __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float 
     const float *x2v = P.x2 ? P.x2 + (size_t)b * P.xs : nullptr;
     uint16_t *seam = P.seam ? P.seam + (size_t)b * K : nullptr;
     uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
-    for (int u0 = u_lo; u0 < u_hi; u0 += DMV_THREADS) {    // uniform trip count: shuffles below
+    for (int u0 = u_lo; u0 < u_hi; u0 += 32 * NW) {       // uniform trip count: shuffles below
         const int u = u0 + tid;
         const bool ok = u < u_hi;                           // whole half warps
         float v[8], z[8];
@@ -280,23 +287,24 @@ __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float 
 // Stage x: NV vectors (the sequences of a batch; those past P.nvec are not
 // staged and their results are dropped), vector b into the shared-memory
 // block at sm + b * xb.
-template <int NV>
+template <int NV, int NW>
 __device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb, bool seam_cta)
 {
     __shared__ float invs[8];
-    if (P.op == DMV_OP_RMSNORM) dmv_norms<NV>(P, 0, invs);
+    if (P.op == DMV_OP_RMSNORM) dmv_norms<NV, NW>(P, 0, invs);
 #pragma unroll 1
     for (int b = 0; b < NV && b < P.nvec; b++)
-        dmv_stage_vec(P, b, P.op == DMV_OP_RMSNORM ? invs[b] : 0.f, sm + b * xb, 0, P.K >> 3, seam_cta);
+        dmv_stage_vec<NW>(P, b, P.op == DMV_OP_RMSNORM ? invs[b] : 0.f, sm + b * xb, 0, P.K >> 3, seam_cta);
     __syncthreads();
 }
 
 // The blocks dec_k_stage wrote (vectors 0 .. nvs-1, contiguous) into shared
 // memory: 16-byte asynchronous copies, all in flight at once.
+template <int NW>
 __device__ __forceinline__ void dmv_load_staged(const uint8_t *src, uint8_t *sm, size_t bytes)
 {
     const uint32_t base = (uint32_t)__cvta_generic_to_shared(sm);
-    for (size_t i = 16 * (size_t)threadIdx.x; i < bytes; i += 16 * DMV_THREADS)
+    for (size_t i = 16 * (size_t)threadIdx.x; i < bytes; i += 16 * 32 * NW)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(base + (uint32_t)i), "l"(src + i) : "memory");
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
@@ -458,14 +466,14 @@ __device__ __forceinline__ void dmv_dots(const Sm &s, int np, int p, const uint3
 // row slot w / ks over column slice w % ks, and the ks partial sums of a row
 // meet in shared memory (uniform control flow: every warp walks the same
 // groups and the same number of batches).
-template <bool PAIRED>
+template <bool PAIRED, int NW>
 __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &J, const Sm &s, float *red,
                                             int ta, int tb, int warp, int lane, int np, size_t wpitch,
                                             unsigned long long &best)
 {
     constexpr int G = PAIRED ? DMV_G / 2 : DMV_G;
     constexpr int NR = DMV_G;
-    const int ks = P.ksplit, rt = DMV_WARPS / ks, rs = warp / ks, kq = warp % ks;
+    const int ks = P.ksplit, rt = NW / ks, rs = warp / ks, kq = warp % ks;
     const int npk = np / ks, p0 = kq * npk, p1 = p0 + npk;
     for (int t = ta; t < tb; t += G) {
         const int g = min(G, tb - t);
@@ -520,15 +528,15 @@ __device__ __forceinline__ void dmv_segment(const dmv_params &P, const dmv_job &
         }
         if (ks > 1) {
             if (holder) {
-                red[((rs * 4 + vi) * 2 + 0) * DMV_WARPS + kq] = v0;
-                red[((rs * 4 + vi) * 2 + 1) * DMV_WARPS + kq] = v1;
+                red[((rs * 4 + vi) * 2 + 0) * NW + kq] = v0;
+                red[((rs * 4 + vi) * 2 + 1) * NW + kq] = v1;
             }
             __syncthreads();
             if (kq == 0 && holder) {
                 float a = 0.f, b2 = 0.f;
                 for (int q = 0; q < ks; q++) {
-                    a += red[((rs * 4 + vi) * 2 + 0) * DMV_WARPS + q];
-                    b2 += red[((rs * 4 + vi) * 2 + 1) * DMV_WARPS + q];
+                    a += red[((rs * 4 + vi) * 2 + 0) * NW + q];
+                    b2 += red[((rs * 4 + vi) * 2 + 1) * NW + q];
                 }
                 v0 = a; v1 = b2;
             }
@@ -603,13 +611,13 @@ __device__ __forceinline__ uint32_t u4w(const uint4 &v, int s)
 
 #define DMV_U 4                    // groups per batch of loads
 
-template <int NV, bool PAIRED>
+template <int NV, bool PAIRED, int NW>
 __device__ __forceinline__ void dmv_segment_mma(const dmv_params &P, const dmv_job &J, uint8_t *sm, size_t xb,
                                                 float *red4, int ta, int tb, int warp, int lane, int ng,
                                                 size_t wpitch, unsigned long long (&best)[2])
 {
     constexpr int TR = PAIRED ? 8 : 16;          // rows (pairs) per warp tile
-    const int ks = P.ksplit, rt = DMV_WARPS / ks, rs = warp / ks, kq = warp % ks;
+    const int ks = P.ksplit, rt = NW / ks, rs = warp / ks, kq = warp % ks;
     const int ngk = ng / ks, G0 = kq * ngk, G1 = G0 + ngk;
     const int g = lane >> 2, t = lane & 3, np = P.K >> 6, nv = P.nvec;
     // B fragments: vector g (vectors past the batch read vector 0; their
@@ -710,13 +718,13 @@ __device__ __forceinline__ void dmv_segment_mma(const dmv_params &P, const dmv_j
 // L2 prefetch of up to `budget` weight bytes of tiles [t0, t1) (the CTA's
 // range of a launch), by one thread; `mma` selects the tile height
 __device__ __forceinline__ void dmv_prefetch(const dmv_params &P, const dmv_job *JS, int t0, int t1, int64_t budget,
-                                             bool mma)
+                                             bool mma, int nw)
 {
     const size_t wpitch = (size_t)P.K >> 1;
     for (int t = t0; t < t1 && budget > 0;) {
         const dmv_job &J = JS[dmv_job_of(P, JS, t)];
         const int te = min(t1, J.tile0 + J.ntiles);
-        const int TR = mma ? (J.wq2 ? 8 : 16) : DMV_WARPS / P.ksplit;
+        const int TR = mma ? (J.wq2 ? 8 : 16) : nw / P.ksplit;
         const int r0 = (t - J.tile0) * TR;
         const int r1 = min(J.rows, (te - J.tile0) * TR);
         int64_t bytes = (int64_t)(r1 - r0) * (int64_t)wpitch;
@@ -737,12 +745,12 @@ __device__ __forceinline__ void dmv_prefetch(const dmv_params &P, const dmv_job 
 // Standalone launches (pdl) prefetch their own first weights and synchronise
 // with the previous kernel; the persistent decode kernel prefetches for the
 // next stage itself.  Every thread of the CTA calls it (barriers inside).
-template <int NV>
+template <int NV, int NW>
 __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, int bid, int nb, bool standalone)
 {
     constexpr bool MMA = NV > 1;
     __shared__ dmv_job JS[DMV_MAXJ];
-    __shared__ float red[DMV_WARPS * 4 * 32];
+    __shared__ float red[NW * 4 * 32];
     if (threadIdx.x < P.njobs) JS[threadIdx.x] = P.jobs[threadIdx.x];
     __syncthreads();
     const int T = P.total_tiles;
@@ -756,15 +764,15 @@ __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, i
     if (standalone) {
         // weights do not depend on the previous kernel: ask L2 for the first
         // ones now
-        if (threadIdx.x == 0 && P.pf_bytes > 0) dmv_prefetch(P, JS, t0, t1, P.pf_bytes, MMA);
+        if (threadIdx.x == 0 && P.pf_bytes > 0) dmv_prefetch(P, JS, t0, t1, (int64_t)P.pf_bytes * NW / 8, MMA, NW);
         pdl_trigger();
         pdl_wait();
     }
     if (t0 >= t1) return;                               // uniform over the CTA
 
     const size_t xb = dmv_smem_x_bytes(K);
-    if (P.xst) dmv_load_staged(P.xst, dmv_sm, xb * (size_t)min(NV, P.nvec));
-    else dmv_stage<NV>(P, dmv_sm, xb, t0 == 0);        // the first CTA with tiles writes the seam
+    if (P.xst) dmv_load_staged<NW>(P.xst, dmv_sm, xb * (size_t)min(NV, P.nvec));
+    else dmv_stage<NV, NW>(P, dmv_sm, xb, t0 == 0);    // the first CTA with tiles writes the seam
 
     unsigned long long best[2] = {0, 0};
     for (int j = j0; j < P.njobs; j++) {
@@ -772,12 +780,12 @@ __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, i
         const int ta = max(t0, J.tile0), tb = min(t1, J.tile0 + J.ntiles);
         if (ta >= tb) continue;
         if (MMA) {
-            if (J.wq2) dmv_segment_mma<NV, true>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, ng, wpitch, best);
-            else dmv_segment_mma<NV, false>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, ng, wpitch, best);
+            if (J.wq2) dmv_segment_mma<NV, true, NW>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, ng, wpitch, best);
+            else dmv_segment_mma<NV, false, NW>(P, J, dmv_sm, xb, red, ta, tb, warp, lane, ng, wpitch, best);
         } else {
             const Sm s = sm_layout(dmv_sm, K);
-            if (J.wq2) dmv_segment<true>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best[0]);
-            else dmv_segment<false>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best[0]);
+            if (J.wq2) dmv_segment<true, NW>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best[0]);
+            else dmv_segment<false, NW>(P, J, s, red, ta, tb, warp, lane, np, wpitch, best[0]);
         }
     }
     if (MMA) {
@@ -809,17 +817,17 @@ __global__ void __launch_bounds__(DMV_THREADS) dmv_stage_kernel(const __grid_con
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.y;
-    if (P.op == DMV_OP_RMSNORM) dmv_norms<1>(P, b, invs);
+    if (P.op == DMV_OP_RMSNORM) dmv_norms<1, DMV_WARPS>(P, b, invs);
     const int nu = P.K >> 3, u_lo = blockIdx.x * DMV_THREADS;
-    dmv_stage_vec(P, b, P.op == DMV_OP_RMSNORM ? invs[0] : 0.f, P.xst + (size_t)b * dmv_smem_x_bytes(P.K), u_lo,
+    dmv_stage_vec<DMV_WARPS>(P, b, P.op == DMV_OP_RMSNORM ? invs[0] : 0.f, P.xst + (size_t)b * dmv_smem_x_bytes(P.K), u_lo,
                   min(nu, u_lo + DMV_THREADS), true);
 }
 
-template <int NV>
-__global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dmv_kernel(const __grid_constant__ dmv_params P)
+template <int NV, int NW>
+__global__ void __launch_bounds__(32 * NW, 16 / NW) dmv_kernel(const __grid_constant__ dmv_params P)
 {
     extern __shared__ __align__(128) uint8_t dmv_sm[];
-    dmv_body<NV>(P, dmv_sm, blockIdx.x, gridDim.x, true);
+    dmv_body<NV, NW>(P, dmv_sm, blockIdx.x, gridDim.x, true);
 }
 
 // Validates a parameter block and sets its launch-dependent fields (tiles
@@ -838,16 +846,16 @@ static int dmv_check_input(dmv_params &P)
     return 0;
 }
 
-static long long dmv_prepare(dmv_params &P, int slots)
+static long long dmv_prepare(dmv_params &P, int slots, int nw)
 {
     if (P.njobs < 1 || P.njobs > DMV_MAXJ || dmv_check_input(P)) return -11;
     const bool mma = P.nvec > 1;
     const int NV = P.nvec == 1 ? 1 : P.nvec == 2 ? 2 : P.nvec <= 4 ? 4 : 8;
     const size_t smem = (size_t)NV * dmv_smem_x_bytes(P.K);
     if (smem > 200 * 1024) return -11;
-    // Rows are short of warps when a CTA would get fewer than 16 (one per
-    // warp on the CUDA-core path; 8 warp tiles of 16 rows on the mma path):
-    // then split each row's columns over up to all 8 warps of the CTA.
+    // Rows are short of warps when a CTA of nw warps would get fewer than 2 nw
+    // (CUDA-core path; nw warp tiles of 16 rows on the mma path): then split
+    // each row's columns over up to all nw warps of the CTA.
     long long all_rows = 0, wtiles = 0;
     for (int j = 0; j < P.njobs; j++) {
         const int r = P.jobs[j].rows > 0 ? P.jobs[j].rows : 0;
@@ -857,12 +865,12 @@ static long long dmv_prepare(dmv_params &P, int slots)
     const int np = P.K / 64, ng = P.K / 128;
     int ks = 1;
     if (mma) {
-        while (ks < DMV_WARPS && wtiles * ks < (long long)DMV_WARPS * slots && (ng % (2 * ks)) == 0) ks *= 2;
-    } else if (all_rows < 16LL * slots) {
-        while (ks < DMV_WARPS && np / ks > 32 && (np % (2 * ks)) == 0) ks *= 2;
+        while (ks < nw && wtiles * ks < (long long)nw * slots && (ng % (2 * ks)) == 0) ks *= 2;
+    } else if (all_rows < 2LL * nw * slots) {
+        while (ks < nw && np / ks > 32 && (np % (2 * ks)) == 0) ks *= 2;
     }
     P.ksplit = ks;
-    const int rt = DMV_WARPS / ks;
+    const int rt = nw / ks;
     int tiles = 0;
     for (int j = 0; j < P.njobs; j++) {
         dmv_job &J = P.jobs[j];
@@ -899,17 +907,20 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
     const int nvec = P.nvec <= 0 ? 1 : P.nvec;
     if (nvec > 8) return -11;
     const int NV = nvec == 1 ? 1 : nvec == 2 ? 2 : nvec <= 4 ? 4 : 8;
-    const void *fn = NV == 1 ? (const void *)dmv_kernel<1> : NV == 2 ? (const void *)dmv_kernel<2>
-                   : NV == 4 ? (const void *)dmv_kernel<4> : (const void *)dmv_kernel<8>;
-    const int fi = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : 3;
+    const bool wide = NV == 1 && P.K >= DMV_WIDE_K;
+    const int nw = wide ? 16 : 8;
+    const void *fn = wide ? (const void *)dmv_kernel<1, 16> : NV == 1 ? (const void *)dmv_kernel<1, 8>
+                   : NV == 2 ? (const void *)dmv_kernel<2, 8> : NV == 4 ? (const void *)dmv_kernel<4, 8>
+                   : (const void *)dmv_kernel<8, 8>;
+    const int fi = wide ? 4 : NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : 3;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
     if (dev < 0 || dev >= 64) return -11;
     // per device and kernel instance: the SM count, and the occupancy of up
     // to 8 shared-memory sizes (the decode step uses 3 or 4)
-    static int s_sms[64], s_occ[64][4][8], s_attr[64][4];
-    static size_t s_occ_smem[64][4][8];
+    static int s_sms[64], s_occ[64][5][8], s_attr[64][5];
+    static size_t s_occ_smem[64][5][8];
     if (!s_attr[dev][fi]) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -920,20 +931,20 @@ extern "C" int dec_k_matvec(const dmv_params *p, void *stream, int pdl)
     int occ = 0;
     for (int i = 0; i < 8; i++) if (s_occ[dev][fi][i] && s_occ_smem[dev][fi][i] == smem) occ = s_occ[dev][fi][i];
     if (!occ) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DMV_THREADS, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, 32 * nw, smem);
         if (e != cudaSuccess) { mv4i_g_cuda_err = (int)e; return -20; }
         if (occ < 1) occ = 1;
         for (int i = 0; i < 8; i++)
             if (!s_occ[dev][fi][i]) { s_occ[dev][fi][i] = occ; s_occ_smem[dev][fi][i] = smem; break; }
     }
     const int slots = s_sms[dev] * occ;
-    const long long rc = dmv_prepare(P, slots);
+    const long long rc = dmv_prepare(P, slots, nw);
     if (rc < 0) return (int)rc;
     int grid = slots;
     if (grid > P.total_tiles) grid = P.total_tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(DMV_THREADS);
+    cfg.blockDim = dim3(32 * nw);
     cfg.dynamicSmemBytes = (size_t)rc;
     cfg.stream = reinterpret_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];

@@ -511,7 +511,7 @@ int dec_set_prompt(dec_model *m, const int32_t *tokens, int n, void *stream)
     return 0;
 }
 
-#define PF_BYTES (48 * 1024)
+#define PF_BYTES (48 * 1024)       /* weight bytes a matvec CTA asks L2 for early, per 8 warps */
 
 /* The step as a program.  dec_program walks the layers once and hands each
  * piece of work to an emitter: in launch mode (rec == NULL) every piece is a

@@ -131,11 +131,11 @@ __global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dec_mega_kernel(const _
             const int T = N.total_tiles;
             const int t0 = (int)((int64_t)blockIdx.x * T / gridDim.x);
             const int t1 = (int)((int64_t)(blockIdx.x + 1) * T / gridDim.x);
-            dmv_prefetch(N, N.jobs, t0, t1, P.pf_bytes, NV > 1);
+            dmv_prefetch(N, N.jobs, t0, t1, P.pf_bytes, NV > 1, DMV_WARPS);
         }
         switch (st.op) {
         case MG_MATVEC:
-            dmv_body<NV>(st.u.mv, mg_sm, blockIdx.x, gridDim.x, false);
+            dmv_body<NV, DMV_WARPS>(st.u.mv, mg_sm, blockIdx.x, gridDim.x, false);
             break;
         case MG_GDN: {
             // pieces of 128 threads (16 value columns of a head), two per CTA
@@ -245,7 +245,7 @@ extern "C" int dec_mega_upload(mg_stage *S, int n, int nvec, mg_prog *P)
     int nbar = 0, done = -1;
     for (int i = 0; i < n; i++) {
         if (S[i].op == MG_MATVEC) {
-            const long long rc = dmv_prepare(S[i].u.mv, grid);
+            const long long rc = dmv_prepare(S[i].u.mv, grid, DMV_WARPS);
             if (rc < 0) return (int)rc;
         }
         nbar += S[i].sync ? 1 : 0;

@@ -494,7 +494,7 @@ def test_batch_argmax_keys(cuda, L, O):
 
 
 @pytest.mark.parametrize("op", ["F16", "RMSNORM", "GATED"])
-@pytest.mark.parametrize("nv,K", [(1, 2048), (3, 2048), (8, 2048), (8, 6144), (2, 17408)])
+@pytest.mark.parametrize("nv,K", [(1, 2048), (1, 6144), (3, 2048), (8, 2048), (8, 6144), (2, 17408)])
 def test_prestaged_inputs_equal_in_cta_staging(cuda, L, O, op, nv, K):
     """dec_k_stage stages the inputs once into a global block and the matvec
     copies it: the same arithmetic as staging in every CTA, so outputs and
