@@ -87,16 +87,21 @@ __device__ __forceinline__ void att_norm_rope(const float4 r, const float *w, fl
     for (int i = 0; i < 4; i++) buf[4 * lane + i] = v[i];
     __syncwarp();
     const int half = n_rot / 2;
+    // the angle pos * theta^(-2k/n_rot) in double (8192 rad needs more than
+    // float's 24 bits), reduced to [-pi, pi] in double, then single-precision
+    // sine and cosine of the reduced angle (error ~1e-7)
+    const double lt = 4 * lane < n_rot ? log2((double)theta) : 0.0;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int d = 4 * lane + i;
         if (d < n_rot) {
             const int k = d < half ? d : d - half;
-            const double th = (double)pos * exp2(-2.0 * (double)k / (double)n_rot * log2((double)theta));
-            double sn, cs;
-            sincos(th, &sn, &cs);
+            const double th = (double)pos * exp2(-2.0 * (double)k / (double)n_rot * lt);
+            const double r = th - 6.283185307179586 * rint(th * 0.15915494309189535);
+            float sn, cs;
+            sincosf((float)r, &sn, &cs);
             const float a = buf[k], b = buf[k + half];
-            out[i] = d < half ? (float)(a * cs - b * sn) : (float)(a * sn + b * cs);
+            out[i] = d < half ? a * cs - b * sn : a * sn + b * cs;
         } else {
             out[i] = v[i];
         }
