@@ -249,11 +249,13 @@ __global__ void __launch_bounds__(1024, 1) dec_attn_kernel(const dec_attn_args A
 
 // Flash-decoding, part 2: combine the chunks of each q head, apply the
 // sigmoid output gate (the raw projection, ref/run9b.c:871-872), to fp16.
-// Piece (q head h, sequence b) by 128 threads (t < 128) with its own scratch
-// wc (at least 8 + 4 * 128 floats): warp w takes chunks w, w + 4, ..., eight
-// records' loads in flight at a time (lane l holds dims 4l..4l+3), with its
-// own running maximum (the online-softmax rescale); then the four warps meet
-// in shared memory.  Every thread reaches the same barriers.
+// Piece (q head h, sequence b) by NW warps (t < 32 NW) with its own scratch
+// wc (at least 2 NW + NW * 128 floats): warp w takes chunks w, w + NW, ...,
+// eight records' loads in flight at a time (lane l holds dims 4l..4l+3), with
+// its own running maximum (the online-softmax rescale); then the warps meet in
+// shared memory and threads t < 128 write dimension t.  Every thread reaches
+// the same barriers.
+template <int NW>
 __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc)
 {
     const int hd = ATT_HD, nchunks = A.nchunks, ch = A.ch, qh = A.qh, gate_stride = 2 * ATT_HD;
@@ -268,12 +270,12 @@ __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int
     const float *ph = part + (size_t)h * nchunks * (hd + 4);
     const int w = t >> 5, lane = t & 31;
     float M = -INFINITY, L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int c0 = w; c0 < used; c0 += 32) {
+    for (int c0 = w; c0 < used; c0 += 8 * NW) {
         float2 ml[8];
         float4 o[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const int c = c0 + 4 * k;
+            const int c = c0 + NW * k;
             if (c < used) {
                 const float *rec = ph + (size_t)c * (hd + 4);
                 ml[k] = *reinterpret_cast<const float2 *>(rec);
@@ -296,28 +298,33 @@ __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int
         }
         M = Mn;
     }
-    float *mw = wc, *lw = wc + 4, *aw = wc + 8;                // [4], [4], [4][128]
+    float *mw = wc, *lw = wc + NW, *aw = wc + 2 * NW;          // [NW], [NW], [NW][128]
     if (lane == 0) { mw[w] = M; lw[w] = L; }
     reinterpret_cast<float4 *>(aw + w * hd)[lane] = make_float4(a0, a1, a2, a3);
     __syncthreads();
-    const float Mx = fmaxf(fmaxf(mw[0], mw[1]), fmaxf(mw[2], mw[3]));   // finite: chunk 0 is in use
-    float tot = 0.f, a = 0.f;
+    if (t < hd) {
+        float Mx = mw[0];
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float f = mw[i] == -INFINITY ? 0.f : expf(mw[i] - Mx);
-        tot = fmaf(lw[i], f, tot);
-        a = fmaf(aw[i * hd + t], f, a);
+        for (int i = 1; i < NW; i++) Mx = fmaxf(Mx, mw[i]);    // finite: chunk 0 is in use
+        float tot = 0.f, a = 0.f;
+#pragma unroll
+        for (int i = 0; i < NW; i++) {
+            const float f = mw[i] == -INFINITY ? 0.f : expf(mw[i] - Mx);
+            tot = fmaf(lw[i], f, tot);
+            a = fmaf(aw[i * hd + t], f, a);
+        }
+        const float gv = gate[(size_t)h * gate_stride + t];
+        y[(size_t)h * hd + t] = __half_as_ushort(__float2half_rn(a / tot * sigm_f(gv)));
     }
-    const float gv = gate[(size_t)h * gate_stride + t];
-    y[(size_t)h * hd + t] = __half_as_ushort(__float2half_rn(a / tot * sigm_f(gv)));
     __syncthreads();                                       // the scratch may be reused
 }
 
-__global__ void __launch_bounds__(128) dec_attn_combine_kernel(const dec_attn_args A)
+#define ATT_COMB_WARPS 8
+__global__ void __launch_bounds__(32 * ATT_COMB_WARPS) dec_attn_combine_kernel(const dec_attn_args A)
 {
-    __shared__ float wc[8 + 4 * ATT_HD];
+    __shared__ float wc[2 * ATT_COMB_WARPS + ATT_COMB_WARPS * ATT_HD];
     PDL_ENTER();
-    dec_attn_combine_cta(A, blockIdx.x, blockIdx.y, threadIdx.x, wc);
+    dec_attn_combine_cta<ATT_COMB_WARPS>(A, blockIdx.x, blockIdx.y, threadIdx.x, wc);
 }
 
 __global__ void dec_add_kernel(float *x, const float *t, int n)
@@ -480,7 +487,7 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
     cfg.numAttrs = pdl ? 1 : 0;
     rc = dk(cudaLaunchKernelEx(&cfg, dec_attn_kernel, A));
     if (rc) return rc;
-    return launch(dec_attn_combine_kernel, dim3(qh, nseq), dim3(ATT_HD), s, pdl, A);
+    return launch(dec_attn_combine_kernel, dim3(qh, nseq), dim3(32 * ATT_COMB_WARPS), s, pdl, A);
 }
 
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl)

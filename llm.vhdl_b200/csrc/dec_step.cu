@@ -97,7 +97,7 @@ __device__ __noinline__ void mg_attn_piece(const dec_attn_args &A, int c, int g,
 }
 __device__ __noinline__ void mg_combine_piece(const dec_attn_args &A, int h, int b, float *wc)
 {
-    dec_attn_combine_cta(A, h, b, threadIdx.x & 127, wc);
+    dec_attn_combine_cta<4>(A, h, b, threadIdx.x & 127, wc);
 }
 
 template <int NV>
