@@ -220,7 +220,7 @@ int dec_set_residual_seams(dec_model *m, float *buf, int n);
  *   y        fp16 [n_qh][128]; q_out (optional) fp32 [n_qh][128] the
  *            normalised, rotated q
  *   work     gated_attn_work_bytes(n_qh, max_ctx) bytes of device memory
- * Two launches (flash decoding over chunks of 32 or 64 positions, then the
+ * Two launches (flash decoding over chunks of 16, 32 or 64 positions, then the
  * combine with the gate); pdl makes the first a programmatic dependent of the
  * kernel before it in the stream.  Head dim 128, n_qh / n_kvh <= 32, n_rot
  * even and <= 128, max_ctx <= 65536.  Returns 0, -11 or -20. */

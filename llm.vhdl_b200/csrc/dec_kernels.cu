@@ -679,9 +679,10 @@ int dec_k_advance_p2p(void *const *regions, int rank, int world, int hidden, uns
 
 }  // extern "C"
 
-// the public one-token entry (include/dec_b200.h): chunks of 32 positions up
-// to a 4096-position cache, 64 beyond (the decode step's choice)
-static int gated_attn_chunk(int max_ctx) { return max_ctx <= 4096 ? 32 : 64; }
+// the public one-token entry (include/dec_b200.h): chunks of 16 positions up
+// to a 2048-position cache, 32 up to 6144, 64 beyond (the decode step's choice
+// for one sequence)
+static int gated_attn_chunk(int max_ctx) { return max_ctx <= 2048 ? 16 : (max_ctx <= 6144 ? 32 : 64); }
 
 extern "C" size_t gated_attn_work_bytes(int n_qh, int max_ctx)
 {

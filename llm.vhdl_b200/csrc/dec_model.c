@@ -188,7 +188,9 @@ int dec_create(const dec_config *cfg, uint64_t seed, int device, int tp_rank, in
     m->vocab = c->vocab / W + (R < c->vocab % W ? 1 : 0);
     m->voc0 = R * (c->vocab / W) + (R < c->vocab % W ? R : c->vocab % W);
     m->conv_dim = 2 * m->kh * HD + m->vh * HD;
-    m->att_ch = c->max_ctx <= 4096 ? 32 : 64;       /* positions per attention CTA */
+    /* positions per attention CTA: short caches of one sequence in chunks of
+     * 16 (more CTAs on a step that is a latency chain), then 32, then 64 */
+    m->att_ch = (c->max_ctx <= 2048 && m->B == 1) ? 16 : (c->max_ctx <= 6144 ? 32 : 64);
     m->nchunks = (c->max_ctx + m->att_ch - 1) / m->att_ch;
     m->L = (layer_t *)calloc((size_t)c->n_layers, sizeof(layer_t));
     const int H = c->hidden, KHg = c->gdn_kh, VHg = c->gdn_vh;
