@@ -33,6 +33,8 @@ extern "C" int mv4i_g_cuda_err;
                                    // of 16 warps per SM (the staging split over twice the
                                    // threads), shorter ones two CTAs of 8 warps
 #define DMV_G 4                    // rows a warp streams together (2 gate/up pairs)
+#define DMV_MAXG 256               // 128-column groups of the widest input (K <= 32768)
+#define DMV_HOLD 2                 // units per thread an RMSNorm prologue keeps in registers
 #ifndef DMV_MINB
 #define DMV_MINB 2                 // resident CTAs per SM the registers are sized for
 #endif
@@ -156,41 +158,115 @@ __device__ __forceinline__ void unit_load(const dmv_params &P, const void *xv, c
     }
 }
 
-// 1 / rms of vectors b0 .. b0+NB-1 (those below P.nvec) into invs[0..NB-1]
-// (RMSNorm prologue only); every thread of the CTA calls it.  The sums of
-// squares run over the first 256 threads whatever the CTA's size, so the
-// statistic (and every result after it) is the same bit for bit in 8- and
-// 16-warp CTAs and in the staging launch.
-template <int NB, int NW>
-__device__ __forceinline__ void dmv_norms(const dmv_params &P, int b0, float *invs)
+// sum of squares of a unit's 8 values, then over its half warp: the
+// 128-column group's sum (every lane of the half warp gets the same bits)
+__device__ __forceinline__ float grp_ssq(const float (&v)[8])
 {
-    __shared__ float red[NW * 8];
-    const int K = P.K, tid = threadIdx.x, nv = P.nvec;
-    float a[NB];
+    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < NB; i++) {
-        const int b = b0 + i;
-        a[i] = 0.f;
-        if (b < nv && tid < DMV_THREADS) {
-            const float *x = static_cast<const float *>(P.x) + (size_t)b * P.xs;
-            for (int c = 4 * tid; c < K; c += 4 * DMV_THREADS) {
-                const float4 v = *reinterpret_cast<const float4 *>(x + c);
-                a[i] = fmaf(v.x, v.x, a[i]); a[i] = fmaf(v.y, v.y, a[i]);
-                a[i] = fmaf(v.z, v.z, a[i]); a[i] = fmaf(v.w, v.w, a[i]);
+    for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    return ss;
+}
+
+// The RMSNorm statistic of a K-column vector from its 128-column group sums
+// gss[0 .. K/128): four interleaved partial sums in group order, then
+// (s0 + s1) + (s2 + s3).  Every path (8- and 16-warp CTAs, the staging
+// launch, batches) forms the group sums the same way (grp_ssq), so the
+// statistic and every result after it are the same bit for bit.
+__device__ __forceinline__ float dmv_inv_rms(const float *gss, int K, float eps)
+{
+    const int ng = K >> 7;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g = 0; g < ng; g += 4) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) if (g + j < ng) s[j] += gss[g + j];
+    }
+    return rsqrtf(((s[0] + s[1]) + (s[2] + s[3])) / (float)K + eps);
+}
+
+// The group sums of squares of vectors b0 .. b0+NB-1 (those below P.nvec)
+// into gss + i * DMV_MAXG (RMSNorm prologue, fp32 residual input); every
+// thread of the CTA calls it (shuffles inside), a barrier must follow.
+template <int NB, int NW>
+__device__ __forceinline__ void dmv_group_ssq(const dmv_params &P, int b0, float *gss)
+{
+    const int nu = P.K >> 3, tid = threadIdx.x;
+    for (int u0 = 0; u0 < nu; u0 += 32 * NW) {           // uniform trip count: shuffles below
+        const int u = u0 + tid;
+        const bool ok = u < nu;                           // whole half warps
+        float v[NB][8];
+#pragma unroll
+        for (int i = 0; i < NB; i++) {
+            const bool oki = ok && b0 + i < P.nvec;
+            if (oki) {
+                const float4 *x = reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) +
+                                                                   (size_t)(b0 + i) * P.xs + 8 * u);
+                const float4 a = x[0], c = x[1];
+                v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+                v[i][4] = c.x; v[i][5] = c.y; v[i][6] = c.z; v[i][7] = c.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[i][k] = 0.f;
             }
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) a[i] += __shfl_xor_sync(0xffffffffu, a[i], o);
-        if ((tid & 31) == 0) red[i * NW + (tid >> 5)] = a[i];
+        for (int i = 0; i < NB; i++) {
+            const float ss = grp_ssq(v[i]);
+            if (ok && !(u & 15)) gss[i * DMV_MAXG + (u >> 4)] = ss;
+        }
     }
-    __syncthreads();
-    if (tid < NB) {
-        float t = 0.f;
+}
+
+// fp16 rounding (the storage contract), the group exponent, and unit u's
+// int16 x into the byte planes, pair sums and group records of the block s;
+// v holds the unit's 8 inputs after the prologue's arithmetic.  Whole half
+// warps call it together (shuffles inside); ok is false for padding units.
+__device__ __forceinline__ void stage_unit(const Sm &s, int np, int u, bool ok, float (&v)[8], uint16_t *seam)
+{
+    uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
+    uint32_t hw[4];
+    float m = 0.f;
 #pragma unroll
-        for (int w = 0; w < NW; w++) t += red[tid * NW + w];
-        invs[tid] = rsqrtf(t / (float)K + P.eps);
+    for (int k = 0; k < 4; k++) {
+        const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+        hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
+        const float2 f = __half22float2(h2);
+        v[2 * k] = f.x; v[2 * k + 1] = f.y;
+        m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
     }
-    __syncthreads();
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int e = 0;
+    // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
+    if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
+    const float scale = exp2i(e);
+    int xi[8], ssum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    const int gsum = ssum + __shfl_xor_sync(0xffffffffu, ssum, 8);
+    if (ok) {
+        // byte planes by permutes: t = {x0.b0, x2.b0, x0.b1, x2.b1} and
+        // {x4.b0, x6.b0, x4.b1, x6.b1}, then their low / high halves
+        const uint32_t te0 = prmt_b(xi[0], xi[2], 0x5140u), te1 = prmt_b(xi[4], xi[6], 0x5140u);
+        const uint32_t to0 = prmt_b(xi[1], xi[3], 0x5140u), to1 = prmt_b(xi[5], xi[7], 0x5140u);
+        const uint32_t le = prmt_b(te0, te1, 0x5410u), he = prmt_b(te0, te1, 0x7632u);
+        const uint32_t lo = prmt_b(to0, to1, 0x5410u), ho = prmt_b(to0, to1, 0x7632u);
+        const int c = u >> 2, q = u & 3, p = c >> 1, par = c & 1;
+        pw[4 * ((0 + par) * np + p) + q] = le;
+        pw[4 * ((2 + par) * np + p) + q] = lo;
+        pw[4 * ((4 + par) * np + p) + q] = he;
+        pw[4 * ((6 + par) * np + p) + q] = ho;
+        if (!(u & 7)) s.psum[u >> 3] = ssum;
+        if (!(u & 15)) {
+            s.gfac[u >> 4] = exp2i(-e);
+            s.gs[u >> 4] = make_int2(gsum, __float_as_int(exp2i(-e)));
+        }
+        if (seam) *reinterpret_cast<uint4 *>(seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    }
 }
 
 // Stage units [u_lo, u_hi) of vector b into the block at dst (shared memory,
@@ -198,7 +274,7 @@ __device__ __forceinline__ void dmv_norms(const dmv_params &P, int b0, float *in
 // thread, so a 128-column group is 16 consecutive lanes (a half warp) and a
 // 64-column pair 8 lanes: group max, pair sums and per-head norms are
 // shuffle reductions.  u_lo and u_hi are multiples of 16; every thread of
-// the CTA calls it.
+// the CTA calls it.  inv: 1 / rms of the vector (RMSNorm prologue).
 template <int NW>
 __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float inv, uint8_t *dst, int u_lo,
                                               int u_hi, bool seam_cta)
@@ -208,8 +284,7 @@ __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float 
     const void *xv = P.op == DMV_OP_F16 ? static_cast<const void *>(static_cast<const uint16_t *>(P.x) + (size_t)b * P.xs)
                                         : static_cast<const void *>(static_cast<const float *>(P.x) + (size_t)b * P.xs);
     const float *x2v = P.x2 ? P.x2 + (size_t)b * P.xs : nullptr;
-    uint16_t *seam = P.seam ? P.seam + (size_t)b * K : nullptr;
-    uint32_t *pw = reinterpret_cast<uint32_t *>(s.planes);
+    uint16_t *seam = P.seam && seam_cta ? P.seam + (size_t)b * K : nullptr;
     for (int u0 = u_lo; u0 < u_hi; u0 += 32 * NW) {       // uniform trip count: shuffles below
         const int u = u0 + tid;
         const bool ok = u < u_hi;                           // whole half warps
@@ -224,12 +299,7 @@ __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float 
                 for (int k = 0; k < 8; k++) v[k] = v[k] * inv * w[k];
             }
         } else if (P.op == DMV_OP_GATED) {
-            float ss = 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; k++) ss = fmaf(v[k], v[k], ss);
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float ginv = rsqrtf(ss / 128.f + P.eps);
+            const float ginv = rsqrtf(grp_ssq(v) / 128.f + P.eps);
             if (ok) {
                 const float4 *wp = reinterpret_cast<const float4 *>(P.nw + ((8 * u) & 127));
                 const float4 a = wp[0], c = wp[1];
@@ -238,63 +308,84 @@ __device__ __forceinline__ void dmv_stage_vec(const dmv_params &P, int b, float 
                 for (int k = 0; k < 8; k++) v[k] = v[k] * ginv * w[k] * silu_f(z[k]);
             }
         }
-        // fp16 rounding (the storage contract), then the group exponent
-        uint32_t hw[4];
-        float m = 0.f;
+        stage_unit(s, np, u, ok, v, seam);
+    }
+}
+
+// One sequence's RMSNorm prologue in one read of the residual: each thread
+// keeps its units (at most DMV_HOLD per thread) and their norm weights in
+// registers while the group sums of squares meet in shared memory, then
+// scales and stages them.  The same arithmetic as dmv_group_ssq +
+// dmv_stage_vec (bit-identical blocks).
+template <int NW>
+__device__ __forceinline__ void dmv_stage_rms1(const dmv_params &P, uint8_t *dst, float *gss, bool seam_cta)
+{
+    const int K = P.K, np = K >> 6, nu = K >> 3, tid = threadIdx.x;
+    const int nit = (nu + 32 * NW - 1) / (32 * NW);
+    const float *x = static_cast<const float *>(P.x);
+    float v[DMV_HOLD][8], w[DMV_HOLD][8];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-            hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
-            const float2 f = __half22float2(h2);
-            v[2 * k] = f.x; v[2 * k + 1] = f.y;
-            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
+    for (int it = 0; it < DMV_HOLD; it++) {
+        if (it < nit) {                                     // uniform over the CTA
+            const int u = it * 32 * NW + tid;
+            if (u < nu) {
+                const float4 *xp = reinterpret_cast<const float4 *>(x + 8 * u);
+                const float4 *wp = reinterpret_cast<const float4 *>(P.nw + 8 * u);
+                const float4 a = xp[0], c = xp[1], d = wp[0], f = wp[1];
+                v[it][0] = a.x; v[it][1] = a.y; v[it][2] = a.z; v[it][3] = a.w;
+                v[it][4] = c.x; v[it][5] = c.y; v[it][6] = c.z; v[it][7] = c.w;
+                w[it][0] = d.x; w[it][1] = d.y; w[it][2] = d.z; w[it][3] = d.w;
+                w[it][4] = f.x; w[it][5] = f.y; w[it][6] = f.z; w[it][7] = f.w;
+            } else {
 #pragma unroll
-        for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        int e = 0;
-        // m in [2^(ex-1), 2^ex) (frexp's ex; m is an fp16 value, a normal fp32)
-        if (m > 0.f) e = 15 - ((int)((__float_as_uint(m) >> 23) & 0xFF) - 126);
-        const float scale = exp2i(e);
-        int xi[8], ssum = 0;
-#pragma unroll
-        for (int k = 0; k < 8; k++) { xi[k] = to_i16(v[k], scale); ssum += xi[k]; }
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-        const int gsum = ssum + __shfl_xor_sync(0xffffffffu, ssum, 8);
-        if (ok) {
-            // byte planes by permutes: t = {x0.b0, x2.b0, x0.b1, x2.b1} and
-            // {x4.b0, x6.b0, x4.b1, x6.b1}, then their low / high halves
-            const uint32_t te0 = prmt_b(xi[0], xi[2], 0x5140u), te1 = prmt_b(xi[4], xi[6], 0x5140u);
-            const uint32_t to0 = prmt_b(xi[1], xi[3], 0x5140u), to1 = prmt_b(xi[5], xi[7], 0x5140u);
-            const uint32_t le = prmt_b(te0, te1, 0x5410u), he = prmt_b(te0, te1, 0x7632u);
-            const uint32_t lo = prmt_b(to0, to1, 0x5410u), ho = prmt_b(to0, to1, 0x7632u);
-            const int c = u >> 2, q = u & 3, p = c >> 1, par = c & 1;
-            pw[4 * ((0 + par) * np + p) + q] = le;
-            pw[4 * ((2 + par) * np + p) + q] = lo;
-            pw[4 * ((4 + par) * np + p) + q] = he;
-            pw[4 * ((6 + par) * np + p) + q] = ho;
-            if (!(u & 7)) s.psum[u >> 3] = ssum;
-            if (!(u & 15)) {
-                s.gfac[u >> 4] = exp2i(-e);
-                s.gs[u >> 4] = make_int2(gsum, __float_as_int(exp2i(-e)));
+                for (int k = 0; k < 8; k++) { v[it][k] = 0.f; w[it][k] = 0.f; }
             }
-            if (seam_cta && seam)
-                *reinterpret_cast<uint4 *>(seam + 8 * u) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < DMV_HOLD; it++) {
+        if (it < nit) {
+            const int u = it * 32 * NW + tid;
+            const float ss = grp_ssq(v[it]);
+            if (u < nu && !(u & 15)) gss[u >> 4] = ss;
+        }
+    }
+    __syncthreads();
+    const float inv = dmv_inv_rms(gss, K, P.eps);
+    const Sm s = sm_layout(dst, K);
+    uint16_t *seam = P.seam && seam_cta ? P.seam : nullptr;
+#pragma unroll
+    for (int it = 0; it < DMV_HOLD; it++) {
+        if (it < nit) {
+            const int u = it * 32 * NW + tid;
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[it][k] = v[it][k] * inv * w[it][k];
+            stage_unit(s, np, u, u < nu, v[it], seam);
         }
     }
 }
 
 // Stage x: NV vectors (the sequences of a batch; those past P.nvec are not
 // staged and their results are dropped), vector b into the shared-memory
-// block at sm + b * xb.
-template <int NV, int NW>
+// block at sm + b * xb.  HOLD: a single sequence's RMSNorm prologue keeps its
+// units in registers (one read of the residual) where they fit.
+template <int NV, int NW, bool HOLD>
 __device__ void dmv_stage(const dmv_params &P, uint8_t *sm, size_t xb, bool seam_cta)
 {
-    __shared__ float invs[8];
-    if (P.op == DMV_OP_RMSNORM) dmv_norms<NV, NW>(P, 0, invs);
+    __shared__ float gss[NV * DMV_MAXG];
+    if (HOLD && P.op == DMV_OP_RMSNORM && NV == 1 && (P.K >> 3) <= DMV_HOLD * 32 * NW) {
+        dmv_stage_rms1<NW>(P, sm, gss, seam_cta);
+        __syncthreads();
+        return;
+    }
+    if (P.op == DMV_OP_RMSNORM) {
+        dmv_group_ssq<NV, NW>(P, 0, gss);
+        __syncthreads();
+    }
 #pragma unroll 1
     for (int b = 0; b < NV && b < P.nvec; b++)
-        dmv_stage_vec<NW>(P, b, P.op == DMV_OP_RMSNORM ? invs[b] : 0.f, sm + b * xb, 0, P.K >> 3, seam_cta);
+        dmv_stage_vec<NW>(P, b, P.op == DMV_OP_RMSNORM ? dmv_inv_rms(gss + b * DMV_MAXG, P.K, P.eps) : 0.f,
+                          sm + b * xb, 0, P.K >> 3, seam_cta);
     __syncthreads();
 }
 
@@ -745,7 +836,7 @@ __device__ __forceinline__ void dmv_prefetch(const dmv_params &P, const dmv_job 
 // Standalone launches (pdl) prefetch their own first weights and synchronise
 // with the previous kernel; the persistent decode kernel prefetches for the
 // next stage itself.  Every thread of the CTA calls it (barriers inside).
-template <int NV, int NW>
+template <int NV, int NW, bool HOLD = true>
 __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, int bid, int nb, bool standalone)
 {
     constexpr bool MMA = NV > 1;
@@ -772,7 +863,7 @@ __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, i
 
     const size_t xb = dmv_smem_x_bytes(K);
     if (P.xst) dmv_load_staged<NW>(P.xst, dmv_sm, xb * (size_t)min(NV, P.nvec));
-    else dmv_stage<NV, NW>(P, dmv_sm, xb, t0 == 0);    // the first CTA with tiles writes the seam
+    else dmv_stage<NV, NW, HOLD>(P, dmv_sm, xb, t0 == 0);    // the first CTA with tiles writes the seam
 
     unsigned long long best[2] = {0, 0};
     for (int j = j0; j < P.njobs; j++) {
@@ -813,14 +904,17 @@ __device__ __forceinline__ void dmv_body(const dmv_params &P, uint8_t *dmv_sm, i
 // arithmetic as the in-CTA staging (bit-identical blocks).
 __global__ void __launch_bounds__(DMV_THREADS) dmv_stage_kernel(const __grid_constant__ dmv_params P)
 {
-    __shared__ float invs[1];
+    __shared__ float gss[DMV_MAXG];
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.y;
-    if (P.op == DMV_OP_RMSNORM) dmv_norms<1, DMV_WARPS>(P, b, invs);
+    if (P.op == DMV_OP_RMSNORM) {
+        dmv_group_ssq<1, DMV_WARPS>(P, b, gss);
+        __syncthreads();
+    }
     const int nu = P.K >> 3, u_lo = blockIdx.x * DMV_THREADS;
-    dmv_stage_vec<DMV_WARPS>(P, b, P.op == DMV_OP_RMSNORM ? invs[0] : 0.f, P.xst + (size_t)b * dmv_smem_x_bytes(P.K), u_lo,
-                  min(nu, u_lo + DMV_THREADS), true);
+    dmv_stage_vec<DMV_WARPS>(P, b, P.op == DMV_OP_RMSNORM ? dmv_inv_rms(gss, P.K, P.eps) : 0.f,
+                             P.xst + (size_t)b * dmv_smem_x_bytes(P.K), u_lo, min(nu, u_lo + DMV_THREADS), true);
 }
 
 template <int NV, int NW>

@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(DMV_THREADS, DMV_MINB) dec_mega_kernel(const _
         }
         switch (st.op) {
         case MG_MATVEC:
-            dmv_body<NV, DMV_WARPS>(st.u.mv, mg_sm, blockIdx.x, gridDim.x, false);
+            dmv_body<NV, DMV_WARPS, false>(st.u.mv, mg_sm, blockIdx.x, gridDim.x, false);
             break;
         case MG_GDN: {
             // pieces of 128 threads (16 value columns of a head), two per CTA
