@@ -240,9 +240,27 @@ __device__ __forceinline__ void dec_attn_cta(const dec_attn_args &A, int c, int 
     reinterpret_cast<float4 *>(pp + 4)[lane] = make_float4(a0, a1, a2, a3);
 }
 
+__device__ __forceinline__ void prefetch_line(const void *p) { asm volatile("prefetch.global.L2 [%0];" :: "l"(p)); }
+
+// The cached k and v rows of chunk c of kv head g (sequence b) up to the
+// position pos_hint + 1, into L2: called before the wait for the previous
+// kernel, which does not write them (pos_hint only bounds the request: a
+// stale value costs a few useless lines, never a wrong result).
+__device__ __forceinline__ void dec_attn_prefetch(const dec_attn_args &A, int c, int g, int b, int tid, int nthr)
+{
+    const int hint = *(volatile const int *)A.d_pos;
+    const int p0 = c * A.ch, p1 = min(min(p0 + A.ch, hint + 2), A.max_ctx);
+    const size_t base = (size_t)b * A.max_ctx * A.kvh * ATT_HD;
+    for (int i = tid; i < 4 * (p1 - p0); i += nthr) {         // 4 lines a row: k and v, 256 bytes each
+        const size_t off = base + ((size_t)(p0 + (i >> 2)) * A.kvh + g) * ATT_HD + 64 * (i & 1);
+        prefetch_line((i & 2) ? (const void *)(A.vcache + off) : (const void *)(A.kcache + off));
+    }
+}
+
 __global__ void __launch_bounds__(1024, 1) dec_attn_kernel(const dec_attn_args A)
 {
     extern __shared__ __align__(16) uint8_t att_sm[];
+    dec_attn_prefetch(A, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, blockDim.x);
     PDL_ENTER();
     dec_attn_cta(A, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, blockDim.x, att_sm);
 }

@@ -338,6 +338,12 @@ extern "C" int gdn_scalar_dev(int H, const int32_t *d_sc, int32_t *d_eg, int32_t
 __global__ void __launch_bounds__(128)
 gdn_f32_kernel(const gdn_f32_args A0)
 {
+    // the CTA's 16 state columns (8 KB, contiguous) do not depend on the
+    // previous kernel: ask L2 for them first
+    if (threadIdx.x == 0) {
+        const float *S = A0.S + ((size_t)blockIdx.y * A0.H * 128 + (size_t)(blockIdx.x >> 3) * 128 + (blockIdx.x & 7) * 16) * 128;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(S), "r"(8192u) : "memory");
+    }
     // a programmatic dependent of the previous kernel: let the next one
     // launch, then wait for this one's inputs (no-ops otherwise)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
