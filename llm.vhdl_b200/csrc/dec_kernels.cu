@@ -269,11 +269,11 @@ __global__ void __launch_bounds__(1024, 1) dec_attn_kernel(const dec_attn_args A
 // sigmoid output gate (the raw projection, ref/run9b.c:871-872), to fp16.
 // Piece (q head h, sequence b) by NW warps (t < 32 NW) with its own scratch
 // wc (at least 2 NW + NW * 128 floats): warp w takes chunks w, w + NW, ...,
-// eight records' loads in flight at a time (lane l holds dims 4l..4l+3), with
+// R records' loads in flight at a time (lane l holds dims 4l..4l+3), with
 // its own running maximum (the online-softmax rescale); then the warps meet in
 // shared memory and threads t < 128 write dimension t.  Every thread reaches
 // the same barriers.
-template <int NW>
+template <int NW, int R = 8>
 __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int h, int b, int t, float *wc)
 {
     const int hd = ATT_HD, nchunks = A.nchunks, ch = A.ch, qh = A.qh, gate_stride = 2 * ATT_HD;
@@ -288,11 +288,11 @@ __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int
     const float *ph = part + (size_t)h * nchunks * (hd + 4);
     const int w = t >> 5, lane = t & 31;
     float M = -INFINITY, L = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int c0 = w; c0 < used; c0 += 8 * NW) {
-        float2 ml[8];
-        float4 o[8];
+    for (int c0 = w; c0 < used; c0 += R * NW) {
+        float2 ml[R];
+        float4 o[R];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
+        for (int k = 0; k < R; k++) {
             const int c = c0 + NW * k;
             if (c < used) {
                 const float *rec = ph + (size_t)c * (hd + 4);
@@ -305,11 +305,11 @@ __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int
         }
         float Mn = M;
 #pragma unroll
-        for (int k = 0; k < 8; k++) Mn = fmaxf(Mn, ml[k].x);
+        for (int k = 0; k < R; k++) Mn = fmaxf(Mn, ml[k].x);
         const float ro = M == -INFINITY ? 0.f : expf(M - Mn);
         L *= ro; a0 *= ro; a1 *= ro; a2 *= ro; a3 *= ro;
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
+        for (int k = 0; k < R; k++) {
             const float f = ml[k].x == -INFINITY ? 0.f : expf(ml[k].x - Mn);
             L = fmaf(ml[k].y, f, L);
             a0 = fmaf(o[k].x, f, a0); a1 = fmaf(o[k].y, f, a1); a2 = fmaf(o[k].z, f, a2); a3 = fmaf(o[k].w, f, a3);
@@ -337,12 +337,15 @@ __device__ __forceinline__ void dec_attn_combine_cta(const dec_attn_args &A, int
     __syncthreads();                                       // the scratch may be reused
 }
 
-#define ATT_COMB_WARPS 8
-__global__ void __launch_bounds__(32 * ATT_COMB_WARPS) dec_attn_combine_kernel(const dec_attn_args A)
+// NW warps x R records in flight: 8 x 8 (one round of loads) up to 64 chunks,
+// 16 x 9 up to 144 (more warps for few chunks only lengthen the merge)
+#define ATT_COMB_SPLIT 64
+template <int NW, int R>
+__global__ void __launch_bounds__(32 * NW) dec_attn_combine_kernel(const dec_attn_args A)
 {
-    __shared__ float wc[2 * ATT_COMB_WARPS + ATT_COMB_WARPS * ATT_HD];
+    __shared__ float wc[2 * NW + NW * ATT_HD];
     PDL_ENTER();
-    dec_attn_combine_cta<ATT_COMB_WARPS>(A, blockIdx.x, blockIdx.y, threadIdx.x, wc);
+    dec_attn_combine_cta<NW, R>(A, blockIdx.x, blockIdx.y, threadIdx.x, wc);
 }
 
 __global__ void dec_add_kernel(float *x, const float *t, int n)
@@ -505,7 +508,8 @@ int dec_k_attention(const float *qg, const float *kv, const float *qn_w, const f
     cfg.numAttrs = pdl ? 1 : 0;
     rc = dk(cudaLaunchKernelEx(&cfg, dec_attn_kernel, A));
     if (rc) return rc;
-    return launch(dec_attn_combine_kernel, dim3(qh, nseq), dim3(32 * ATT_COMB_WARPS), s, pdl, A);
+    if (A.nchunks <= ATT_COMB_SPLIT) return launch(dec_attn_combine_kernel<8, 8>, dim3(qh, nseq), dim3(256), s, pdl, A);
+    return launch(dec_attn_combine_kernel<16, 9>, dim3(qh, nseq), dim3(512), s, pdl, A);
 }
 
 int dec_k_add(float *x, const float *t, int n, void *s, int pdl)
